@@ -1,0 +1,367 @@
+"""Benchmark: Qwen3-30B-A3B Q4_K MoE decode tok/s on B200 (% of HBM roofline).
+
+Workload: the 48-layer MoE-FFN stack, Qwen3-30B-A3B
+shapes (hidden 2048, 128 experts, top-8, intermediate 768, Q4_K gate/up, Q6_K
+down), batch-1 decode, every expert resident.  One step = one decode of 256
+tokens, strictly one token after another (one persistent-kernel launch); the
+token inputs are AR(1) hidden states (rho 0.9, RMS-normed); attention is the
+identity and the residual adds the MoE output.  Synthetic data: seeded
+N(0, 0.02) weights generated and quantised on the device, N(0, 0.02) fp32
+routers.  Every token streams 1.23 GB of expert and router weights, far more
+than the 126 MB L2, so no step reuses another's weights from L2.
+
+    python bench.py [--gpus N --steps K --warmup W]          # this repo's kernels
+    python bench.py --impl reference [...]                    # CPU reference path
+
+With N > 1 (torchrun), each rank decodes its own 256-token stream on its own
+GPU (batch-1 decode does not shard: replicas, weak scaling); the time is the
+max over ranks.  Rank 0 prints one JSON line.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N_LAYERS, N_EXPERT, TOP_K, N_EMBD, N_FF = 48, 128, 8, 2048, 768
+GATE_BYTES = N_FF * (N_EMBD // 256) * 144            # 884,736
+DOWN_BYTES = N_EMBD * (N_FF // 256) * 210            # 1,290,240
+EXPERT_BYTES = 2 * GATE_BYTES + DOWN_BYTES           # 3,059,712
+ROUTER_BYTES = N_EXPERT * N_EMBD * 4                 # 1,048,576
+XY_BYTES = 2 * N_EMBD * 4                            # layer input + output
+LAYER_TOKEN_BYTES = ROUTER_BYTES + TOP_K * EXPERT_BYTES + XY_BYTES   # 25,542,656
+METRIC = "Qwen3-30B-A3B Q4_K MoE decode tok/s at 1/2/4/8 B200; % of HBM roofline"
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def ar1_states(n_tok, n_embd, seed, rho=0.9):
+    rng = np.random.default_rng(seed)
+    h = np.empty((n_tok, n_embd), np.float32)
+    prev = rng.standard_normal(n_embd)
+    for t in range(n_tok):
+        prev = rho * prev + np.sqrt(1 - rho * rho) * rng.standard_normal(n_embd)
+        h[t] = prev
+    return (h / np.sqrt((h.astype(np.float64) ** 2).mean(-1, keepdims=True))).astype(np.float32)
+
+
+def config_block(tokens):
+    return {
+        "workload": "config1: 48-layer Qwen3-30B-A3B MoE-FFN stack, batch-1 decode, "
+                    f"{tokens} tokens per step, all 128 experts resident",
+        "n_layers": N_LAYERS, "n_expert": N_EXPERT, "top_k": TOP_K, "n_embd": N_EMBD,
+        "n_ff": N_FF, "quant": "Q4_K gate/up, Q6_K down, Q8_1 activations",
+        "tokens_per_step": tokens,
+        "l2": "inputs larger than L2: 1.23 GB of expert+router weights per token",
+        "parallelism": "replicas (batch-1 decode does not shard)",
+    }
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, bus_id=None):
+        self.bus_id = (bus_id or "").lower()
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        rows = []
+        if self.path and os.path.exists(self.path):
+            with open(self.path) as f:
+                for line in f:
+                    parts = [p.strip() for p in line.split(",")]
+                    if len(parts) < 9:
+                        continue
+                    if self.bus_id and self.bus_id[-12:] not in parts[0].lower():
+                        continue
+                    rows.append(parts)
+            os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle's restatement of the ggml CPU rows path
+# ---------------------------------------------------------------------------
+def cpu_baseline(host_layers, seconds, threads):
+    """Times the integer-dot CPU rows path (Q8_K activations, ggml op order,
+    OpenMP) on a bounded sample: the given layers' weights, tokens cycled
+    through them until `seconds` of CPU work; returns tok/s of the 48-layer
+    stack (layer-token rate / 48)."""
+    import oracle
+    oracle.build()
+    rng = np.random.default_rng(5)
+    x = ar1_states(64, N_EMBD, 77)
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        L = host_layers[n % len(host_layers)]
+        oracle.moe_layer_cpu_fast(x[n % 64], L["router"], L["gate"], L["up"], L["down"], 14,
+                                  N_FF, TOP_K, n_threads=threads)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds and n >= 8:
+            break
+    del rng
+    return n / el / N_LAYERS, n, el
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# ---------------------------------------------------------------------------
+# reference arm
+# ---------------------------------------------------------------------------
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import oracle
+    oracle.build()
+    threads = host_threads()
+    # two layers of weights generated on the host (numpy N(0, 0.02), the
+    # oracle's quantiser); the reference's own CPU path cannot be built here
+    layers = []
+    for il in range(2):
+        rng = np.random.default_rng(1000 * il)
+        layers.append({
+            "gate": oracle.quantize((rng.standard_normal((N_EXPERT * N_FF, N_EMBD)) * 0.02)
+                                    .astype(np.float32), 12).reshape(N_EXPERT, -1),
+            "up": oracle.quantize((rng.standard_normal((N_EXPERT * N_FF, N_EMBD)) * 0.02)
+                                  .astype(np.float32), 12).reshape(N_EXPERT, -1),
+            "down": oracle.quantize((rng.standard_normal((N_EXPERT * N_EMBD, N_FF)) * 0.02)
+                                    .astype(np.float32), 14).reshape(N_EXPERT, -1),
+            "router": (rng.standard_normal((N_EXPERT, N_EMBD)) * 0.02).astype(np.float32),
+        })
+    per_step = max(1.0, float(args.ref_seconds))
+    for _ in range(args.warmup):
+        cpu_baseline(layers, min(per_step, 1.0), threads)
+    vals, tot_n, tot_t = [], 0, 0.0
+    for _ in range(args.steps):
+        v, n, el = cpu_baseline(layers, per_step, threads)
+        vals.append(v)
+        tot_n += n
+        tot_t += el
+    value = tot_n / tot_t / N_LAYERS
+    sample = (f"{tot_n} layer-tokens over 2 host-resident layers (2 x 392 MB), "
+              f"{per_step:.0f} s per step; tok/s = layer-tokens/s / 48")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * tot_t / max(args.steps, 1), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": config_block(args.tokens),
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "the reference's CPU MoE path (ggml mul_mat_id / GGML_OP_MOE_ROWS in patches "
+                "against llama.cpp) cannot be built here; this is the oracle's restatement of "
+                "it (Q4_K/Q6_K x Q8_K integer dots, ggml op order, OpenMP)",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--tokens", type=int, default=256)
+    ap.add_argument("--layers", type=int, default=N_LAYERS)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--ref-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+    from moe_prefetch_b200 import MoeStack
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    n_layers, tokens = args.layers, args.tokens
+    st = MoeStack(n_layers=n_layers)
+    st.synth_resident(seed=7919 * rank + 11)
+    h = torch.from_numpy(ar1_states(tokens, N_EMBD, seed=12345 + rank)).cuda()
+    out = torch.empty_like(h)
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        st.decode(h, out)
+    st.sync()
+
+    props = torch.cuda.get_device_properties(local)
+    bus = getattr(props, "pci_bus_id", None)
+    bus = f"{getattr(props, 'pci_domain_id', 0):08x}:{bus:02x}" if isinstance(bus, int) else None
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(bus).start()
+    time.sleep(0.3)
+    t_all0 = torch.cuda.Event(enable_timing=True)
+    t_all1 = torch.cuda.Event(enable_timing=True)
+    t_all0.record(stream)
+    for i in range(args.steps):
+        starts[i].record(stream)
+        st.decode(h, out)
+        ends[i].record(stream)
+    t_all1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    barrier()
+    st.sync()
+    total_ms = t_all0.elapsed_time(t_all1)
+    launch_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    avg_launch_ms = sum(launch_ms) / len(launch_ms)
+    t = torch.tensor([total_ms, avg_launch_ms], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, avg_launch_ms = float(t[0]), float(t[1])
+    value = world * args.steps * tokens / (total_ms / 1000.0)
+
+    # end to end through the public API: pinned host in -> decode -> host out
+    e2e = None
+    if not args.no_e2e:
+        hp = h.cpu().pin_memory()
+        op = torch.empty_like(hp).pin_memory()
+        for _ in range(max(1, args.warmup)):
+            st.decode_host(hp, op)
+        n_e2e = max(3, args.steps // 2)
+        barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n_e2e):
+            st.decode_host(hp, op)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        te = torch.tensor([e0.elapsed_time(e1)], device="cuda", dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e = {"value": world * n_e2e * tokens / (float(te[0]) / 1000.0), "unit": "tok/s",
+               "h2d_bytes_per_step": tokens * N_EMBD * 4, "d2h_bytes_per_step": tokens * N_EMBD * 4,
+               "steps": n_e2e}
+
+    peak, peak_kind = measured_peaks()
+    layer_token = LAYER_TOKEN_BYTES
+    bytes_per_launch = layer_token * n_layers * tokens
+    achieved = bytes_per_launch / (avg_launch_ms / 1000.0) / 1e9
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "decode_traffic.json")
+    if os.path.exists(tp):
+        with open(tp) as f:
+            tr = json.load(f)
+        if tr.get("dram_bytes_per_layer_token"):
+            traffic = float(tr["dram_bytes_per_layer_token"]) * n_layers * tokens
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "traffic": traffic,
+                "kernel": "moe::k_decode", "peak_kind": peak_kind,
+                "algorithmic_bytes_per_launch": bytes_per_launch,
+                "algorithmic_bytes_per_layer_token": layer_token}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        host_layers = []
+        for il in range(2):
+            g, u, d = st.slot_views(il)
+            host_layers.append({"gate": g[:N_EXPERT].cpu().numpy(), "up": u[:N_EXPERT].cpu().numpy(),
+                                "down": d[:N_EXPERT].cpu().numpy(),
+                                "router": np.ascontiguousarray(
+                                    np.random.default_rng(il).standard_normal((N_EXPERT, N_EMBD))
+                                    .astype(np.float32) * np.float32(0.02))})
+        threads = host_threads()
+        v, n, el = cpu_baseline(host_layers, args.cpu_seconds, threads)
+        cpu = {"value": v, "unit": "tok/s", "cores": threads, "kind": "port",
+               "sample": f"{n} layer-tokens over 2 host-resident layers in {el:.1f} s "
+                         "(oracle's integer-dot CPU rows path, Q8_K activations, OpenMP); "
+                         "tok/s = layer-tokens/s / 48"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (seeded N(0,0.02) weights quantised on device; AR(1) inputs)",
+            "config": config_block(tokens), "roofline": roofline, "cpu_baseline": cpu,
+            "e2e": e2e, "gpu_launches": args.steps, "clocks": clocks,
+            "decode_geometry": st.decode_info(),
+        }
+        print(json.dumps(line), flush=True)
+    st.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

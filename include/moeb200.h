@@ -1,0 +1,284 @@
+/*
+ * moeb200.h -- C ABI of libmoeb200.so, the B200-native MoE layer with a GPU
+ * expert slot cache.
+ *
+ * Plain pointers and sizes only; `stream` is a cudaStream_t passed as void*
+ * (NULL = the legacy default stream).  Every entry point returns an int status
+ * (MOE_OK = 0, negative = error) unless stated; the message of the last error
+ * is available from moe_last_error().  Nothing aborts the process.
+ *
+ * Each declaration names the reference interface it replaces, as
+ * file:line in everett6/moe-prefetch (patches are cited by line of the patch
+ * file).  The reference's interface takes llama/ggml types; here the same
+ * operations take plain buffers.
+ */
+#ifndef MOEB200_H
+#define MOEB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------- */
+#define MOE_OK               0
+#define MOE_ERR_ARG         -1   /* bad argument / shape                         */
+#define MOE_ERR_CUDA        -2   /* a CUDA runtime call failed                   */
+#define MOE_ERR_OOM         -3   /* device or pinned allocation failed           */
+#define MOE_ERR_UNSUPPORTED -4   /* shape or mode this build does not implement  */
+#define MOE_ERR_TIMEOUT     -5   /* a device-side bounded wait gave up           */
+#define MOE_ERR_STATE       -6   /* call out of order (e.g. weights missing)     */
+#define MOE_ERR_DEVICE      -7   /* a kernel reported a bad index                */
+
+/* ggml type ids of the weight blocks (same numbers as ggml's enum) */
+#define MOE_QTYPE_Q4_K 12
+#define MOE_QTYPE_Q6_K 14
+
+/* admission gate (LLAMA_MOE_ADMIT, patches/0007:182-188) */
+#define MOE_ADMIT_OFF    0
+#define MOE_ADMIT_HEAT   1
+#define MOE_ADMIT_WINDOW 2
+
+typedef struct moe_ctx moe_ctx;
+
+/* Cache + layer configuration.  Replaces the arguments of
+ * llama_moe_cache_init(model, n_slots, max_inserts) (patches/0006:482) and the
+ * LLAMA_MOE_* environment switches it parses (patches/0006:501-520,
+ * 0007:492-506, 0008:536-573). */
+typedef struct moe_cfg {
+    int32_t n_layers;          /* MoE layers in the stack                          */
+    int32_t n_expert;          /* routed experts per layer (multiple of 32, <=256) */
+    int32_t n_used;            /* experts per token (top-k, <= 8)                  */
+    int32_t n_embd;            /* hidden size (2048 in this build)                 */
+    int32_t n_ff;              /* expert intermediate size (multiple of 256)       */
+    int32_t down_type;         /* MOE_QTYPE_Q6_K or MOE_QTYPE_Q4_K                 */
+    int32_t n_slots;           /* --moe-expert-cache N, default slots per layer    */
+    const int32_t *slot_profile; /* per-layer slots (LLAMA_MOE_SLOT_PROFILE) or NULL */
+    int32_t max_inserts;       /* --moe-expert-cache-inserts (0 -> 2)              */
+    int32_t admit_mode;        /* MOE_ADMIT_*                                      */
+    int32_t admit_window;      /* LLAMA_MOE_ADMIT_WINDOW (0 -> 8)                  */
+    int32_t admit_half;        /* LLAMA_MOE_ADMIT_HALF (0 -> 64)                   */
+    float   admit_floor;       /* LLAMA_MOE_ADMIT_FLOOR                            */
+    int32_t spec_probation;    /* LLAMA_MOE_SPEC_PROBATION                         */
+    int32_t batch_tables;      /* LLAMA_MOE_BATCH_TABLES (tables always move in one
+                                  device step here; kept for the stats counter)   */
+    float   cache_prior;       /* LLAMA_MOE_CACHE_PRIOR, delta (0 = off)           */
+    int32_t early_issue;       /* LLAMA_MOE_EARLY_ISSUE (must be 0 on device)      */
+    int32_t freeze;            /* LLAMA_MOE_CACHE_FREEZE                           */
+    int32_t use_heat_counts;   /* a heat file is configured (LLAMA_MOE_HEAT_FILE)  */
+    int32_t device;            /* CUDA device ordinal                              */
+} moe_cfg;
+
+/* What llama_moe_cache_lookup(up_exps) returns for one layer
+ * (struct llama_moe_cache_layer, patches/0007:774-790): slot slabs
+ * [n_slots + 1][...] (slot n_slots is the dummy), the device table
+ * (expert -> slot, n_slots when not resident) and the slot count. */
+typedef struct moe_layer_info {
+    void    *gate_c;           /* device: [n_slots+1][n_ff rows of n_embd]  Q4_K  */
+    void    *up_c;             /* device: same                                     */
+    void    *down_c;           /* device: [n_slots+1][n_embd rows of n_ff]  down   */
+    int32_t *dev_table;        /* device: [n_expert]                               */
+    int64_t  gate_bytes;       /* bytes of one expert's gate (= up) matrix         */
+    int64_t  down_bytes;       /* bytes of one expert's down matrix                */
+    int32_t  n_slots;
+    int32_t  il;
+} moe_layer_info;
+
+/* Counters (the reference's every-512-steps stderr line, patches/0006:928-953,
+ * 0007:762-770), read with moe_get_stats in this order. */
+enum moe_stat {
+    MOE_STAT_STEPS = 0, MOE_STAT_CLOCK, MOE_STAT_HITS, MOE_STAT_MISSES,
+    MOE_STAT_UPLOADS, MOE_STAT_SCHEDULED, MOE_STAT_COPIED, MOE_STAT_PUBLISHED,
+    MOE_STAT_ADMIT_OK, MOE_STAT_ADMIT_DENIED, MOE_STAT_TABLE_FLUSHES,
+    MOE_STAT_UPLOAD_BYTES, MOE_STAT_COUNT
+};
+
+/* ---- lifetime ---------------------------------------------------------------- */
+
+/* Create the cache + layer context on cfg->device: allocates the slot slabs,
+ * tables and slot state on the device, all slots empty, all tables -> dummy.
+ * Replaces llama_moe_cache_init (patches/0006:482-763, 0007:519-655,
+ * 0008:825-573 env handling, 0009:620-658 ownership by the context). */
+int moe_create(const moe_cfg *cfg, moe_ctx **out);
+
+/* Free everything; waits for in-flight uploads.  Replaces
+ * llama_moe_cache_shutdown/_claim (patches/0009:1019-1056). */
+void moe_destroy(moe_ctx *ctx);
+
+/* Text of the last error on this context ("" if none). */
+const char *moe_last_error(const moe_ctx *ctx);
+
+/* Per-layer slabs / table.  Replaces llama_moe_cache_lookup
+ * (patches/0009:1184-1218, struct at 0007:774-790). */
+int moe_get_layer(moe_ctx *ctx, int layer, moe_layer_info *out);
+
+/* ---- weights ------------------------------------------------------------------- */
+
+/* Router weight ffn_gate_inp of one layer, fp32 [n_expert][n_embd], host or
+ * device memory (copied into the context).  The reference keeps it in the
+ * model (build_moe_ffn, context of patches/0007:101-128). */
+int moe_set_router(moe_ctx *ctx, int layer, const float *w);
+
+/* Register the caller-owned host copies of one layer's experts, ggml layout
+ * [n_expert][rows][blocks] for gate, up and down.  They are pinned and mapped
+ * (cudaHostRegister) unless already pinned, and are the source of every
+ * upload and of zero-copy reads for missed experts.  Replaces the host-resident
+ * up_src/gate_src/down_src tensors of layer_state (patches/0006:585-590) and
+ * the -ot CUDA_Host placement (patches/0006:1-17). */
+int moe_set_expert_weights(moe_ctx *ctx, int layer, const void *gate, const void *up,
+                           const void *down);
+
+/* Place experts into slots without going through admission: slot_expert[ns]
+ * gives the expert for each slot (-1 = empty).  With copy != 0 the bytes are
+ * copied from the registered host weights, else the caller has already written
+ * the slots (moe_get_layer).  Replaces the map replay frame (patches/0008:435-475)
+ * and the heat warm start placement (0007:567-618). Synchronous. */
+int moe_place(moe_ctx *ctx, int layer, const int32_t *slot_expert, int copy);
+
+/* ---- the hot path -------------------------------------------------------------- */
+
+/* One MoE layer for n_tok tokens, device buffers x [n_tok][n_embd] (the
+ * ffn_norm output) -> y [n_tok][n_embd] (the weighted sum of the k expert
+ * rows; the caller adds the residual).  Fused router (+cache prior when
+ * n_tok == 1), slot lookup, observation (n_tok == 1 only, as the reference's
+ * callback), gate/up GEMV with SiLU*mul, down GEMV with the weighted combine.
+ * Missed experts are read zero-copy from the registered host weights.
+ * ids/w [n_tok][n_used] are optional outputs.  Replaces build_moe_ffn's expert
+ * path with the cache chain (patches/0009:659-705, 0008:372-390) and
+ * ggml_cpu_moe_rows (patches/0008:186-251). */
+int moe_layer_forward(moe_ctx *ctx, int layer, const float *x, float *y, int n_tok,
+                      int32_t *ids, float *w, void *stream);
+
+/* Optional per-(token, layer) dumps of the decode stack, device pointers or NULL:
+ * x [n_tok][n_layers][n_embd] (router input), ids/w [n_tok][n_layers][n_used],
+ * y [n_tok][n_layers][n_embd] (the layer's MoE output). */
+typedef struct moe_decode_dbg {
+    float   *x;
+    int32_t *ids;
+    float   *w;
+    float   *y;
+} moe_decode_dbg;
+
+/* Batch-1 decode of n_tok tokens, strictly one after another, through all
+ * n_layers: for each token t the residual starts at h[t]; every layer applies
+ * RMSNorm (eps 1e-6, unit weight), the MoE layer and the residual add;
+ * out[t] is the final residual.  One persistent kernel per call (one CTA per
+ * SM).  Device buffers.  Replaces the per-layer decode graph of
+ * llama_context::decode for the MoE part (patches/0009:620-705). */
+int moe_decode(moe_ctx *ctx, const float *h, float *out, int n_tok,
+               const moe_decode_dbg *dbg, void *stream);
+
+/* The same with host buffers: h_host -> device, decode, device -> out_host,
+ * all on `stream`, synchronised before returning. */
+int moe_decode_host(moe_ctx *ctx, const float *h_host, float *out_host, int n_tok,
+                    void *stream);
+
+/* Synchronise `stream` and report what the kernels flagged since the last
+ * call (MOE_ERR_TIMEOUT: a bounded device wait gave up; MOE_ERR_DEVICE: an
+ * id out of range).  The hot-path launches are asynchronous; this is where
+ * their device-side errors surface.  Replaces the error return of
+ * llama_context::decode when the sidecar times out (patches/0009:652-655). */
+int moe_sync(moe_ctx *ctx, void *stream);
+
+/* Decode-kernel geometry: grid (CTAs), shared bytes per CTA, gate/up rows and
+ * down rows per CTA (max), threads per CTA; n = how many to copy. */
+int moe_decode_info(const moe_ctx *ctx, int32_t *out, int n);
+
+/* ---- the slot cache step ------------------------------------------------------- */
+
+/* Observe one layer's routed ids (device [n_tok][n_ids]) outside
+ * moe_layer_forward: hits refresh recency, misses feed the second-miss window
+ * and the pending list.  Only n_tok == 1 is observed.  Replaces moe_obs_cb
+ * (patches/0006:295-400, 0007:247-321). */
+int moe_observe(moe_ctx *ctx, int layer, const int32_t *ids, int n_tok, int n_ids,
+                void *stream);
+
+/* Between tokens: publish every upload scheduled at the previous step in
+ * (layer, slot) order, advance the step, schedule this step's admissions and
+ * evictions on the device, then issue their copies on the dedicated copy
+ * stream.  Deterministic publication.  Synchronises `stream` once.  Replaces
+ * llama_moe_cache_step (patches/0006:765-953, 0007:655-773, 0008:607-660). */
+int moe_step(moe_ctx *ctx, void *stream);
+
+/* 1: moe_step needs the previous forward complete (always, here).  Replaces
+ * llama_moe_cache_requires_sync (patches/0008:603-605). */
+int moe_requires_sync(const moe_ctx *ctx);
+
+/* Host copies of one layer's slot state (any pointer may be NULL):
+ * expert_slot [n_expert] (slot or -1), slot_expert / last_use / in_flight /
+ * protect [n_slots].  Synchronous. */
+int moe_get_tables(moe_ctx *ctx, int layer, int32_t *expert_slot, int32_t *slot_expert,
+                   uint64_t *last_use, uint8_t *in_flight, uint64_t *protect);
+
+/* Admission-gate state of one layer (heat f32, miss_last / miss_prev u64,
+ * use_count u32, each [n_expert]; NULL to skip).  Synchronous. */
+int moe_get_gate_state(moe_ctx *ctx, int layer, float *heat, uint64_t *miss_last,
+                       uint64_t *miss_prev, uint32_t *use_count);
+
+/* Counters in enum moe_stat order; n = how many to copy.  Synchronous. */
+int moe_get_stats(moe_ctx *ctx, uint64_t *out, int n);
+
+/* Load use counts from a host array [n_layers][n_expert] (e.g. a parsed
+ * "moe-heat 1" file, patches/0007:431-466, already halved) and place the
+ * hottest experts before the first token (0007:567-618).  Returns the number
+ * placed (>= 0) or an error. */
+int moe_warm_start(moe_ctx *ctx, const uint32_t *use_count);
+
+/* ---- stateless kernels (device pointers) ------------------------------------------ */
+
+/* Fused router for n_tok tokens: logits = W x in the canonical fp32 order,
+ * softmax, + delta on experts with table[e] != n_slots (only when table is
+ * non-NULL, delta > 0 and n_tok == 1), top-k (ties to the lower id),
+ * renormalised weights from the unbiased probabilities.  logits optional.
+ * Replaces the router nodes of build_moe_ffn (context of patches/0007:101-128). */
+int moe_router_run(const float *W, const float *x, int n_tok, int n_expert, int n_embd,
+                   const int32_t *table, int n_slots, float delta, int k,
+                   int32_t *ids, float *w, float *logits, void *stream);
+
+/* Quantise fp32 rows (n % 256 == 0) into Q4_K or Q6_K blocks on the device,
+ * bit-identical to the oracle's quantiser (a synthetic-weight tool; ggml's
+ * quantize_row_q4_K is not in the reference tree). */
+int moe_quantize(const float *x, void *y, int64_t n, int qtype, void *stream);
+
+/* Synthetic N(0, sigma^2) weights generated and quantised on the device in
+ * one pass (element i of block b from a counter hash of (seed, b*256 + i)),
+ * for the benchmark's 18.8 GB expert set; and synthetic fp32 N(0, sigma^2)
+ * values.  No reference counterpart (the reference loads a GGUF). */
+int moe_synth_weights(void *y, int64_t n_blocks, int qtype, uint64_t seed, float sigma,
+                      void *stream);
+int moe_synth_f32(float *y, int64_t n, uint64_t seed, float sigma, void *stream);
+
+/* ---- ExpertCache (src/prefetch_engine.py:45-168) ----------------------------------- */
+
+typedef struct moe_xc moe_xc;
+
+/* Per-layer LRU cache of byte slabs [capacity][bytes_per_expert] in device
+ * memory, refilled from a pinned host staging buffer [n_experts][bytes] on a
+ * dedicated copy stream with one event per copy.  Replaces
+ * ExpertCache.__init__ (src/prefetch_engine.py:48-70). */
+int moe_xc_create(int n_layers, int n_experts, int capacity, int64_t bytes_per_expert,
+                  const void *host_staging, int device, moe_xc **out);
+void moe_xc_destroy(moe_xc *xc);
+/* prefetch (src/prefetch_engine.py:89-106): start copies for the ids not yet
+ * cached; returns how many started (>= 0) or an error. */
+int moe_xc_prefetch(moe_xc *xc, int layer, const int32_t *ids, int n);
+/* query (:108-132): status[i] = 0 hit, 1 late (copy still in flight), 2 miss. */
+int moe_xc_query(moe_xc *xc, int layer, const int32_t *ids, int n, int32_t *status);
+/* admit (:134-154): bring missed experts in (copies move the bytes). */
+int moe_xc_admit(moe_xc *xc, int layer, const int32_t *ids, int n);
+/* sync (:156-157) */
+int moe_xc_sync(moe_xc *xc);
+/* vram_bytes (:159-160) */
+int64_t moe_xc_vram_bytes(const moe_xc *xc);
+/* stats: hits, misses, late, fetches, bytes, evictions (:69-70) */
+int moe_xc_stats(const moe_xc *xc, uint64_t *out6);
+/* device slab of a layer and the slot an expert sits in (-1 if not cached) */
+void *moe_xc_slab(moe_xc *xc, int layer);
+int moe_xc_slot_of(const moe_xc *xc, int layer, int expert);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MOEB200_H */

@@ -1,0 +1,947 @@
+// moe_api.cu -- the C ABI of libmoeb200.so (include/moeb200.h): context,
+// device allocation, weight registration, the hot-path launches, the cache
+// step with its copy-stream uploader, and the ExpertCache prototype API.
+#include "moeb200.h"
+#include "moe_kernels.h"
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <list>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+using namespace moe;
+
+namespace {
+
+struct LayerMem {
+    uint8_t *slab = nullptr;          // gate | up | down for (ns + 1) slots
+    uint8_t *gate = nullptr, *up = nullptr, *down = nullptr;
+    const uint8_t *hgate = nullptr, *hup = nullptr, *hdown = nullptr;   // device aliases
+    const void *hgate_user = nullptr, *hup_user = nullptr, *hdown_user = nullptr;
+    bool registered[3] = {false, false, false};
+    int32_t ns = 0;
+};
+
+}  // namespace
+
+struct moe_ctx {
+    moe_cfg cfg{};
+    std::vector<int32_t> ns;           // per layer
+    std::vector<int32_t> slot_off;
+    int32_t sum_ns = 0;
+    int64_t gate_bytes = 0, down_bytes = 0;
+    std::vector<LayerMem> L;
+    float *router = nullptr;           // [L][E][H]
+    // slot state (device)
+    void *state_mem = nullptr;
+    SlotState st{};
+    int32_t *d_ns = nullptr, *d_slot_off = nullptr;
+    // decode
+    LayerDesc *d_layers = nullptr;
+    int32_t *d_part = nullptr;         // gu_r0 | gu_r1 | dn_h0 | dn_h1
+    int grid = 0;
+    DecodeParams dp{};
+    float *resid = nullptr, *logits = nullptr, *act = nullptr;
+    unsigned *bar = nullptr;
+    int *abort_flag = nullptr, *err = nullptr;
+    // scratch for moe_layer_forward / moe_decode_host
+    int32_t *s_ids = nullptr;
+    float *s_w = nullptr, *s_act = nullptr, *s_io = nullptr;
+    int s_cap_tok = 0, s_io_cap = 0;
+    // uploader
+    cudaStream_t copy_stream = nullptr;
+    cudaEvent_t ev_step = nullptr, ev_copy = nullptr;
+    bool copies_pending = false;
+    int32_t *h_jobs = nullptr;         // mapped pinned [L*MI*4 + 4]
+    int32_t *d_jobs_alias = nullptr;
+    uint64_t upload_bytes = 0;
+    std::string err_msg;
+};
+
+static int fail(moe_ctx *c, int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    if (c) c->err_msg = buf;
+    else fprintf(stderr, "moeb200: %s\n", buf);
+    return code;
+}
+
+#define CK(call)                                                                               \
+    do {                                                                                       \
+        cudaError_t e_ = (call);                                                               \
+        if (e_ != cudaSuccess)                                                                 \
+            return fail(c, MOE_ERR_CUDA, "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                        __FILE__, __LINE__);                                                   \
+    } while (0)
+
+static int64_t row_bytes(int type, int n) {
+    return (int64_t)(n / MOE_QK) * (type == MOE_QTYPE_Q6_K ? MOE_Q6K_BYTES : MOE_Q4K_BYTES);
+}
+
+static size_t al256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// ---------------------------------------------------------------------------
+// lifetime
+// ---------------------------------------------------------------------------
+
+extern "C" int moe_create(const moe_cfg *cfg, moe_ctx **out) {
+    if (!cfg || !out) return fail(nullptr, MOE_ERR_ARG, "moe_create: null argument");
+    *out = nullptr;
+    moe_ctx *c = new moe_ctx();
+    c->cfg = *cfg;
+    moe_cfg &g = c->cfg;
+    g.slot_profile = nullptr;
+    if (g.max_inserts <= 0) g.max_inserts = 2;
+    if (g.freeze) g.max_inserts = 0;
+    if (g.admit_window <= 0) g.admit_window = 8;
+    if (g.admit_half <= 0) g.admit_half = 64;
+    auto bad = [&](int code, const char *m) {
+        fprintf(stderr, "moeb200: moe_create: %s\n", m);
+        delete c;
+        return code;
+    };
+    if (g.n_layers <= 0 || g.n_expert <= 0 || g.n_used <= 0 || g.n_embd <= 0 || g.n_ff <= 0)
+        return bad(MOE_ERR_ARG, "non-positive shape");
+    if (g.n_expert % 32 || g.n_expert > 256) return bad(MOE_ERR_UNSUPPORTED, "n_expert must be a multiple of 32, <= 256");
+    if (g.n_used > 8 || g.n_used > g.n_expert) return bad(MOE_ERR_UNSUPPORTED, "n_used must be <= 8");
+    if (g.n_embd != 2048) return bad(MOE_ERR_UNSUPPORTED, "n_embd must be 2048 in this build");
+    if (g.n_ff % 256 || g.n_ff > 1024) return bad(MOE_ERR_UNSUPPORTED, "n_ff must be a multiple of 256, <= 1024");
+    if (g.down_type != MOE_QTYPE_Q6_K && g.down_type != MOE_QTYPE_Q4_K)
+        return bad(MOE_ERR_UNSUPPORTED, "down_type must be Q6_K or Q4_K");
+    if (g.early_issue) return bad(MOE_ERR_UNSUPPORTED, "early issue is not implemented on the device");
+    if (g.admit_mode < 0 || g.admit_mode > 2) return bad(MOE_ERR_ARG, "admit_mode");
+    if (g.n_slots <= 0 && !cfg->slot_profile) return bad(MOE_ERR_ARG, "n_slots must be > 0");
+    c->ns.resize(g.n_layers);
+    c->slot_off.resize(g.n_layers);
+    for (int l = 0; l < g.n_layers; ++l) {
+        const int ns = cfg->slot_profile && cfg->slot_profile[l] > 0 ? cfg->slot_profile[l] : g.n_slots;
+        if (ns <= 0 || ns > 4096) return bad(MOE_ERR_ARG, "slots per layer out of range");
+        c->ns[l] = ns;
+        c->slot_off[l] = c->sum_ns;
+        c->sum_ns += ns;
+    }
+    *out = c;
+    if (cudaSetDevice(g.device) != cudaSuccess) {
+        delete c;
+        *out = nullptr;
+        return fail(nullptr, MOE_ERR_CUDA, "cudaSetDevice(%d) failed", g.device);
+    }
+    const int L = g.n_layers, E = g.n_expert, H = g.n_embd, I = g.n_ff, K = g.n_used;
+    c->gate_bytes = row_bytes(MOE_QTYPE_Q4_K, H) * I;
+    c->down_bytes = row_bytes(g.down_type, I) * H;
+    c->L.resize(L);
+    auto cleanup_fail = [&](int code) {
+        moe_destroy(c);
+        *out = nullptr;
+        return code;
+    };
+    // slabs
+    for (int l = 0; l < L; ++l) {
+        LayerMem &m = c->L[l];
+        m.ns = c->ns[l];
+        const size_t gsz = al256((size_t)(m.ns + 1) * c->gate_bytes);
+        const size_t dsz = al256((size_t)(m.ns + 1) * c->down_bytes + 64);
+        if (cudaMalloc(&m.slab, 2 * gsz + dsz) != cudaSuccess) {
+            fail(c, MOE_ERR_OOM, "slab allocation of layer %d (%zu bytes) failed", l, 2 * gsz + dsz);
+            fprintf(stderr, "moeb200: %s\n", c->err_msg.c_str());
+            return cleanup_fail(MOE_ERR_OOM);
+        }
+        m.gate = m.slab;
+        m.up = m.slab + gsz;
+        m.down = m.slab + 2 * gsz;
+        cudaMemsetAsync(m.slab + 2 * gsz + (size_t)m.ns * c->down_bytes, 0,
+                        (size_t)c->down_bytes + 64);   // dummy slot + pad
+    }
+    if (cudaMalloc(&c->router, sizeof(float) * (size_t)L * E * H) != cudaSuccess) return cleanup_fail(MOE_ERR_OOM);
+    cudaMemset(c->router, 0, sizeof(float) * (size_t)L * E * H);
+    // slot state
+    {
+        const size_t LE = (size_t)L * E, S = (size_t)c->sum_ns, MI = (size_t)g.max_inserts > 0 ? g.max_inserts : 1;
+        std::vector<size_t> sz = {
+            LE * 4,            // table
+            S * 4,             // slot_expert
+            S * 8,             // last_use
+            S * 8,             // protect
+            S,                 // in_flight
+            LE * 4,            // pending
+            (size_t)L * 4,     // n_pending
+            g.admit_mode == 1 ? LE * 4 : 0,     // heat
+            g.admit_mode == 2 ? LE * 8 : 0,     // miss_last
+            g.admit_mode == 2 ? LE * 8 : 0,     // miss_prev
+            g.use_heat_counts ? LE * 4 : 0,     // use_count
+            (size_t)L * 8, (size_t)L * 8,       // n_hit, n_miss
+            (size_t)G_COUNT * 8,                // globals
+            (size_t)L * MI * 16,                // jobs
+            (size_t)L * 4,                      // n_jobs
+            (size_t)L * 4, (size_t)L * 4        // ns, slot_off
+        };
+        size_t total = 0;
+        std::vector<size_t> off;
+        for (size_t s : sz) { off.push_back(total); total += al256(s); }
+        if (cudaMalloc(&c->state_mem, total) != cudaSuccess) return cleanup_fail(MOE_ERR_OOM);
+        cudaMemset(c->state_mem, 0, total);
+        uint8_t *b = (uint8_t *)c->state_mem;
+        SlotState &st = c->st;
+        st.n_layers = L; st.n_expert = E; st.max_inserts = g.max_inserts;
+        st.admit_mode = g.admit_mode; st.admit_window = g.admit_window; st.admit_half = g.admit_half;
+        st.admit_floor = g.admit_floor; st.cache_prior = g.cache_prior;
+        st.spec_probation = g.spec_probation; st.batch_tables = g.batch_tables; st.freeze = g.freeze;
+        st.table = (int32_t *)(b + off[0]);
+        st.slot_expert = (int32_t *)(b + off[1]);
+        st.last_use = (uint64_t *)(b + off[2]);
+        st.protect = (uint64_t *)(b + off[3]);
+        st.in_flight = (uint8_t *)(b + off[4]);
+        st.pending = (int32_t *)(b + off[5]);
+        st.n_pending = (int32_t *)(b + off[6]);
+        st.heat = g.admit_mode == 1 ? (float *)(b + off[7]) : nullptr;
+        st.miss_last = g.admit_mode == 2 ? (uint64_t *)(b + off[8]) : nullptr;
+        st.miss_prev = g.admit_mode == 2 ? (uint64_t *)(b + off[9]) : nullptr;
+        st.use_count = g.use_heat_counts ? (uint32_t *)(b + off[10]) : nullptr;
+        st.n_hit = (uint64_t *)(b + off[11]);
+        st.n_miss = (uint64_t *)(b + off[12]);
+        st.g = (uint64_t *)(b + off[13]);
+        st.jobs = (int32_t *)(b + off[14]);
+        st.n_jobs = (int32_t *)(b + off[15]);
+        c->d_ns = (int32_t *)(b + off[16]);
+        c->d_slot_off = (int32_t *)(b + off[17]);
+        st.ns = c->d_ns;
+        st.slot_off = c->d_slot_off;
+        cudaMemcpy(c->d_ns, c->ns.data(), 4 * L, cudaMemcpyHostToDevice);
+        cudaMemcpy(c->d_slot_off, c->slot_off.data(), 4 * L, cudaMemcpyHostToDevice);
+        std::vector<int32_t> tbl((size_t)L * E), se(S, -1);
+        for (int l = 0; l < L; ++l)
+            for (int e = 0; e < E; ++e) tbl[(size_t)l * E + e] = c->ns[l];
+        cudaMemcpy(st.table, tbl.data(), 4 * LE, cudaMemcpyHostToDevice);
+        cudaMemcpy(st.slot_expert, se.data(), 4 * S, cudaMemcpyHostToDevice);
+        if (st.miss_last) {
+            cudaMemset(st.miss_last, 0xFF, LE * 8);
+            cudaMemset(st.miss_prev, 0xFF, LE * 8);
+        }
+    }
+    // decode partition + buffers
+    {
+        int dev_sms = 0;
+        cudaDeviceGetAttribute(&dev_sms, cudaDevAttrMultiProcessorCount, g.device);
+        const int G = dev_sms > 0 ? dev_sms : 1;
+        std::vector<int32_t> part(4 * (size_t)G);
+        const int64_t R = (int64_t)K * I;
+        int gmax = 0, dmax = 0;
+        for (int cc = 0; cc < G; ++cc) {
+            part[cc] = (int32_t)(cc * R / G);
+            part[G + cc] = (int32_t)((cc + 1) * R / G);
+            part[2 * G + cc] = (int32_t)((int64_t)cc * H / G);
+            part[3 * G + cc] = (int32_t)((int64_t)(cc + 1) * H / G);
+            gmax = std::max(gmax, part[G + cc] - part[cc]);
+            dmax = std::max(dmax, part[3 * G + cc] - part[2 * G + cc]);
+        }
+        DecodeParams &p = c->dp;
+        p.n_layers = L; p.n_expert = E; p.k = K; p.n_embd = H; p.n_ff = I; p.down_type = g.down_type;
+        p.gate_bytes = c->gate_bytes; p.down_bytes = c->down_bytes;
+        p.gu_rows_max = gmax; p.dn_rows_max = dmax;
+        decode_smem_layout(p, G);
+        c->grid = G;
+        if (cudaMalloc(&c->d_part, sizeof(int32_t) * part.size()) != cudaSuccess) return cleanup_fail(MOE_ERR_OOM);
+        cudaMemcpy(c->d_part, part.data(), sizeof(int32_t) * part.size(), cudaMemcpyHostToDevice);
+        p.gu_r0 = c->d_part; p.gu_r1 = c->d_part + G; p.dn_h0 = c->d_part + 2 * G; p.dn_h1 = c->d_part + 3 * G;
+        if (cudaMalloc(&c->d_layers, sizeof(LayerDesc) * L) != cudaSuccess) return cleanup_fail(MOE_ERR_OOM);
+        p.layers = c->d_layers;
+        if (cudaMalloc(&c->resid, sizeof(float) * H) != cudaSuccess ||
+            cudaMalloc(&c->logits, sizeof(float) * 256) != cudaSuccess ||
+            cudaMalloc(&c->act, sizeof(float) * (size_t)MOE_KMAX * I) != cudaSuccess ||
+            cudaMalloc(&c->bar, 64) != cudaSuccess || cudaMalloc(&c->abort_flag, 64) != cudaSuccess ||
+            cudaMalloc(&c->err, 64) != cudaSuccess)
+            return cleanup_fail(MOE_ERR_OOM);
+        cudaMemset(c->err, 0, 64);
+        p.resid = c->resid; p.logits = c->logits; p.act = c->act; p.bar = c->bar;
+        p.abort_flag = c->abort_flag; p.err = c->err; p.st = c->st;
+        p.observe = 1; p.delta = g.cache_prior; p.rms_eps = 1e-6f;
+    }
+    // uploader
+    {
+        const size_t MI = (size_t)(g.max_inserts > 0 ? g.max_inserts : 1);
+        const size_t nb = ((size_t)L * MI + 4) * 4 * sizeof(int32_t);
+        if (cudaHostAlloc((void **)&c->h_jobs, nb, cudaHostAllocMapped) != cudaSuccess) return cleanup_fail(MOE_ERR_OOM);
+        memset(c->h_jobs, 0, nb);
+        if (cudaHostGetDevicePointer((void **)&c->d_jobs_alias, c->h_jobs, 0) != cudaSuccess) return cleanup_fail(MOE_ERR_CUDA);
+        if (cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaEventCreateWithFlags(&c->ev_step, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&c->ev_copy, cudaEventDisableTiming) != cudaSuccess)
+            return cleanup_fail(MOE_ERR_CUDA);
+    }
+    if (cudaDeviceSynchronize() != cudaSuccess) return cleanup_fail(MOE_ERR_CUDA);
+    return MOE_OK;
+}
+
+extern "C" void moe_destroy(moe_ctx *c) {
+    if (!c) return;
+    cudaSetDevice(c->cfg.device);
+    if (c->copy_stream) cudaStreamSynchronize(c->copy_stream);
+    cudaDeviceSynchronize();
+    for (auto &m : c->L) {
+        if (m.slab) cudaFree(m.slab);
+        for (int i = 0; i < 3; ++i) {
+            const void *p = i == 0 ? m.hgate_user : i == 1 ? m.hup_user : m.hdown_user;
+            if (m.registered[i] && p) cudaHostUnregister(const_cast<void *>(p));
+        }
+    }
+    cudaFree(c->router);
+    cudaFree(c->state_mem);
+    cudaFree(c->d_layers);
+    cudaFree(c->d_part);
+    cudaFree(c->resid);
+    cudaFree(c->logits);
+    cudaFree(c->act);
+    cudaFree(c->bar);
+    cudaFree(c->abort_flag);
+    cudaFree(c->err);
+    cudaFree(c->s_ids);
+    cudaFree(c->s_w);
+    cudaFree(c->s_act);
+    cudaFree(c->s_io);
+    if (c->h_jobs) cudaFreeHost(c->h_jobs);
+    if (c->ev_step) cudaEventDestroy(c->ev_step);
+    if (c->ev_copy) cudaEventDestroy(c->ev_copy);
+    if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
+    delete c;
+}
+
+extern "C" const char *moe_last_error(const moe_ctx *c) { return c ? c->err_msg.c_str() : ""; }
+
+extern "C" int moe_get_layer(moe_ctx *c, int layer, moe_layer_info *out) {
+    if (!c || !out || layer < 0 || layer >= c->cfg.n_layers) return fail(c, MOE_ERR_ARG, "moe_get_layer: bad layer");
+    LayerMem &m = c->L[layer];
+    out->gate_c = m.gate;
+    out->up_c = m.up;
+    out->down_c = m.down;
+    out->dev_table = c->st.table + (size_t)layer * c->cfg.n_expert;
+    out->gate_bytes = c->gate_bytes;
+    out->down_bytes = c->down_bytes;
+    out->n_slots = m.ns;
+    out->il = layer;
+    return MOE_OK;
+}
+
+// ---------------------------------------------------------------------------
+// weights
+// ---------------------------------------------------------------------------
+
+static int refresh_layer_desc(moe_ctx *c, int layer) {
+    LayerMem &m = c->L[layer];
+    LayerDesc d{};
+    d.router_w = c->router + (size_t)layer * c->cfg.n_expert * c->cfg.n_embd;
+    d.gate = m.gate; d.up = m.up; d.down = m.down;
+    d.hgate = m.hgate; d.hup = m.hup; d.hdown = m.hdown;
+    d.table = c->st.table + (size_t)layer * c->cfg.n_expert;
+    d.ns = m.ns;
+    CK(cudaMemcpy(c->d_layers + layer, &d, sizeof(d), cudaMemcpyHostToDevice));
+    return MOE_OK;
+}
+
+extern "C" int moe_set_router(moe_ctx *c, int layer, const float *w) {
+    if (!c || !w || layer < 0 || layer >= c->cfg.n_layers) return fail(c, MOE_ERR_ARG, "moe_set_router: bad argument");
+    CK(cudaSetDevice(c->cfg.device));
+    const size_t n = (size_t)c->cfg.n_expert * c->cfg.n_embd;
+    CK(cudaMemcpy(c->router + (size_t)layer * n, w, n * sizeof(float), cudaMemcpyDefault));
+    return refresh_layer_desc(c, layer);
+}
+
+static int register_host(moe_ctx *c, const void *p, size_t bytes, const uint8_t **dev, bool *registered) {
+    cudaPointerAttributes at{};
+    cudaError_t e = cudaPointerGetAttributes(&at, p);
+    if (e != cudaSuccess) { (void)cudaGetLastError(); at.type = cudaMemoryTypeUnregistered; }
+    if (at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged) {
+        *dev = (const uint8_t *)p;   // already device-visible
+        *registered = false;
+        return MOE_OK;
+    }
+    if (at.type == cudaMemoryTypeUnregistered) {
+        e = cudaHostRegister(const_cast<void *>(p), bytes, cudaHostRegisterPortable | cudaHostRegisterMapped);
+        if (e != cudaSuccess) {
+            (void)cudaGetLastError();
+            return fail(c, MOE_ERR_CUDA, "cudaHostRegister of %zu bytes failed: %s", bytes, cudaGetErrorString(e));
+        }
+        *registered = true;
+    } else {
+        *registered = false;
+    }
+    void *d = nullptr;
+    e = cudaHostGetDevicePointer(&d, const_cast<void *>(p), 0);
+    if (e != cudaSuccess) {
+        (void)cudaGetLastError();
+        return fail(c, MOE_ERR_CUDA, "cudaHostGetDevicePointer failed: %s", cudaGetErrorString(e));
+    }
+    *dev = (const uint8_t *)d;
+    return MOE_OK;
+}
+
+extern "C" int moe_set_expert_weights(moe_ctx *c, int layer, const void *gate, const void *up,
+                                      const void *down) {
+    if (!c || layer < 0 || layer >= c->cfg.n_layers || !gate || !up || !down)
+        return fail(c, MOE_ERR_ARG, "moe_set_expert_weights: bad argument");
+    if (((uintptr_t)gate | (uintptr_t)up | (uintptr_t)down) & 15)
+        return fail(c, MOE_ERR_ARG, "expert weights must be 16-byte aligned");
+    CK(cudaSetDevice(c->cfg.device));
+    LayerMem &m = c->L[layer];
+    const size_t E = (size_t)c->cfg.n_expert;
+    const void *src[3] = {gate, up, down};
+    const void **user[3] = {&m.hgate_user, &m.hup_user, &m.hdown_user};
+    const uint8_t **dev[3] = {&m.hgate, &m.hup, &m.hdown};
+    for (int i = 0; i < 3; ++i) {
+        if (m.registered[i] && *user[i]) {
+            cudaHostUnregister(const_cast<void *>(*user[i]));
+            m.registered[i] = false;
+        }
+        const size_t bytes = E * (size_t)(i == 2 ? c->down_bytes : c->gate_bytes);
+        const int r = register_host(c, src[i], bytes, dev[i], &m.registered[i]);
+        if (r != MOE_OK) return r;
+        *user[i] = src[i];
+    }
+    return refresh_layer_desc(c, layer);
+}
+
+extern "C" int moe_place(moe_ctx *c, int layer, const int32_t *slot_expert, int copy) {
+    if (!c || !slot_expert || layer < 0 || layer >= c->cfg.n_layers) return fail(c, MOE_ERR_ARG, "moe_place: bad argument");
+    CK(cudaSetDevice(c->cfg.device));
+    LayerMem &m = c->L[layer];
+    const int E = c->cfg.n_expert, ns = m.ns, so = c->slot_off[layer];
+    std::vector<int32_t> cur(ns), tbl(E, ns);
+    std::vector<uint8_t> seen(E, 0);
+    CK(cudaMemcpy(cur.data(), c->st.slot_expert + so, 4 * ns, cudaMemcpyDeviceToHost));
+    for (int s = 0; s < ns; ++s) {
+        const int e = slot_expert[s];
+        if (e < -1 || e >= E) return fail(c, MOE_ERR_ARG, "moe_place: expert %d out of range", e);
+        if (e >= 0) {
+            if (seen[e]) return fail(c, MOE_ERR_ARG, "moe_place: expert %d placed twice", e);
+            seen[e] = 1;
+            tbl[e] = s;
+        }
+    }
+    if (copy) {
+        if (!m.hgate) return fail(c, MOE_ERR_STATE, "moe_place: host weights of layer %d not registered", layer);
+        for (int s = 0; s < ns; ++s) {
+            const int e = slot_expert[s];
+            if (e < 0 || cur[s] == e) continue;
+            CK(cudaMemcpy(m.gate + (size_t)s * c->gate_bytes, m.hgate_user ? (const uint8_t *)m.hgate_user + (size_t)e * c->gate_bytes : m.hgate + (size_t)e * c->gate_bytes, c->gate_bytes, cudaMemcpyDefault));
+            CK(cudaMemcpy(m.up + (size_t)s * c->gate_bytes, (const uint8_t *)m.hup_user + (size_t)e * c->gate_bytes, c->gate_bytes, cudaMemcpyDefault));
+            CK(cudaMemcpy(m.down + (size_t)s * c->down_bytes, (const uint8_t *)m.hdown_user + (size_t)e * c->down_bytes, c->down_bytes, cudaMemcpyDefault));
+            c->upload_bytes += 2 * c->gate_bytes + c->down_bytes;
+        }
+    }
+    std::vector<uint8_t> zero(ns, 0);
+    CK(cudaMemcpy(c->st.slot_expert + so, slot_expert, 4 * ns, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(c->st.table + (size_t)layer * E, tbl.data(), 4 * E, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(c->st.in_flight + so, zero.data(), ns, cudaMemcpyHostToDevice));
+    return MOE_OK;
+}
+
+// ---------------------------------------------------------------------------
+// hot path
+// ---------------------------------------------------------------------------
+
+static int ensure_scratch(moe_ctx *c, int n_tok) {
+    if (n_tok <= c->s_cap_tok) return MOE_OK;
+    cudaFree(c->s_ids); cudaFree(c->s_w); cudaFree(c->s_act);
+    c->s_ids = nullptr; c->s_w = nullptr; c->s_act = nullptr;
+    const int K = c->cfg.n_used;
+    if (cudaMalloc(&c->s_ids, sizeof(int32_t) * (size_t)n_tok * K) != cudaSuccess ||
+        cudaMalloc(&c->s_w, sizeof(float) * (size_t)n_tok * K) != cudaSuccess ||
+        cudaMalloc(&c->s_act, sizeof(float) * (size_t)n_tok * K * c->cfg.n_ff) != cudaSuccess) {
+        c->s_cap_tok = 0;
+        return fail(c, MOE_ERR_OOM, "scratch allocation for %d tokens failed", n_tok);
+    }
+    c->s_cap_tok = n_tok;
+    return MOE_OK;
+}
+
+static ExpertSrc make_src(moe_ctx *c, int layer) {
+    LayerMem &m = c->L[layer];
+    ExpertSrc s{};
+    s.gate = m.gate; s.up = m.up; s.down = m.down;
+    s.hgate = m.hgate; s.hup = m.hup; s.hdown = m.hdown;
+    s.table = c->st.table + (size_t)layer * c->cfg.n_expert;
+    s.gate_bytes = c->gate_bytes; s.down_bytes = c->down_bytes;
+    s.ns = m.ns; s.n_expert = c->cfg.n_expert;
+    return s;
+}
+
+extern "C" int moe_layer_forward(moe_ctx *c, int layer, const float *x, float *y, int n_tok,
+                                 int32_t *ids, float *w, void *stream) {
+    if (!c || !x || !y || n_tok <= 0 || layer < 0 || layer >= c->cfg.n_layers)
+        return fail(c, MOE_ERR_ARG, "moe_layer_forward: bad argument");
+    CK(cudaSetDevice(c->cfg.device));
+    int r = ensure_scratch(c, n_tok);
+    if (r != MOE_OK) return r;
+    cudaStream_t s = (cudaStream_t)stream;
+    const moe_cfg &g = c->cfg;
+    int32_t *ids_d = ids ? ids : c->s_ids;
+    float *w_d = w ? w : c->s_w;
+    const int32_t *table = c->st.table + (size_t)layer * g.n_expert;
+    CK(launch_router(c->router + (size_t)layer * g.n_expert * g.n_embd, x, n_tok, g.n_expert, g.n_embd,
+                     table, c->L[layer].ns, g.cache_prior, n_tok == 1 && g.cache_prior > 0.0f, g.n_used,
+                     ids_d, w_d, nullptr, &c->st, n_tok == 1 ? layer : -1, s));
+    CK(launch_experts(make_src(c, layer), x, ids_d, w_d, n_tok, g.n_used, g.n_embd, g.n_ff,
+                      g.down_type, c->s_act, nullptr, y, c->err, s));
+    return MOE_OK;
+}
+
+extern "C" int moe_decode(moe_ctx *c, const float *h, float *out, int n_tok,
+                          const moe_decode_dbg *dbg, void *stream) {
+    if (!c || !h || !out || n_tok <= 0) return fail(c, MOE_ERR_ARG, "moe_decode: bad argument");
+    CK(cudaSetDevice(c->cfg.device));
+    if (c->dp.smem_bytes > 227 * 1024)
+        return fail(c, MOE_ERR_UNSUPPORTED, "decode needs %d bytes of shared memory", c->dp.smem_bytes);
+    cudaStream_t s = (cudaStream_t)stream;
+    DecodeParams p = c->dp;
+    p.h_in = h;
+    p.out = out;
+    p.n_tok = n_tok;
+    p.dbg_x = dbg ? dbg->x : nullptr;
+    p.dbg_ids = dbg ? dbg->ids : nullptr;
+    p.dbg_w = dbg ? dbg->w : nullptr;
+    p.dbg_y = dbg ? dbg->y : nullptr;
+    if (p.dbg_ids && !p.dbg_w) return fail(c, MOE_ERR_ARG, "moe_decode: dbg ids without w");
+    CK(cudaMemsetAsync(c->bar, 0, 64, s));
+    CK(cudaMemsetAsync(c->abort_flag, 0, 64, s));
+    CK(launch_decode(p, c->grid, s));
+    return MOE_OK;
+}
+
+extern "C" int moe_decode_host(moe_ctx *c, const float *h_host, float *out_host, int n_tok,
+                               void *stream) {
+    if (!c || !h_host || !out_host || n_tok <= 0) return fail(c, MOE_ERR_ARG, "moe_decode_host: bad argument");
+    CK(cudaSetDevice(c->cfg.device));
+    const size_t n = (size_t)n_tok * c->cfg.n_embd;
+    if ((int)(2 * n) > c->s_io_cap) {
+        cudaFree(c->s_io);
+        c->s_io = nullptr;
+        if (cudaMalloc(&c->s_io, sizeof(float) * 2 * n) != cudaSuccess) {
+            c->s_io_cap = 0;
+            return fail(c, MOE_ERR_OOM, "io scratch allocation failed");
+        }
+        c->s_io_cap = (int)(2 * n);
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    CK(cudaMemcpyAsync(c->s_io, h_host, sizeof(float) * n, cudaMemcpyHostToDevice, s));
+    int r = moe_decode(c, c->s_io, c->s_io + n, n_tok, nullptr, stream);
+    if (r != MOE_OK) return r;
+    CK(cudaMemcpyAsync(out_host, c->s_io + n, sizeof(float) * n, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    int e = 0;
+    CK(cudaMemcpy(&e, c->err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (e & MOE_DEV_ERR_TIMEOUT) return fail(c, MOE_ERR_TIMEOUT, "a device-side wait timed out");
+    if (e & MOE_DEV_ERR_INDEX) return fail(c, MOE_ERR_DEVICE, "a kernel saw an out-of-range index");
+    return MOE_OK;
+}
+
+extern "C" int moe_sync(moe_ctx *c, void *stream) {
+    if (!c) return MOE_ERR_ARG;
+    CK(cudaSetDevice(c->cfg.device));
+    CK(cudaStreamSynchronize((cudaStream_t)stream));
+    int e = 0;
+    CK(cudaMemcpy(&e, c->err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (e) {
+        cudaMemset(c->err, 0, sizeof(int));
+        if (e & MOE_DEV_ERR_TIMEOUT) return fail(c, MOE_ERR_TIMEOUT, "a device-side wait timed out");
+        return fail(c, MOE_ERR_DEVICE, "a kernel saw an out-of-range index");
+    }
+    return MOE_OK;
+}
+
+// ---------------------------------------------------------------------------
+// slot cache step
+// ---------------------------------------------------------------------------
+
+extern "C" int moe_observe(moe_ctx *c, int layer, const int32_t *ids, int n_tok, int n_ids,
+                           void *stream) {
+    if (!c || !ids || layer < 0 || layer >= c->cfg.n_layers || n_ids <= 0 || n_ids > 64)
+        return fail(c, MOE_ERR_ARG, "moe_observe: bad argument");
+    if (n_tok != 1) return MOE_OK;   // the reference's callback returns early for batches
+    CK(cudaSetDevice(c->cfg.device));
+    CK(launch_observe(c->st, layer, ids, n_ids, (cudaStream_t)stream));
+    return MOE_OK;
+}
+
+extern "C" int moe_step(moe_ctx *c, void *stream) {
+    if (!c) return MOE_ERR_ARG;
+    CK(cudaSetDevice(c->cfg.device));
+    cudaStream_t s = (cudaStream_t)stream;
+    if (c->copies_pending) CK(cudaStreamWaitEvent(s, c->ev_copy, 0));
+    CK(launch_step(c->st, c->d_jobs_alias, c->d_jobs_alias + (size_t)c->cfg.n_layers *
+                   (c->cfg.max_inserts > 0 ? c->cfg.max_inserts : 1) * 4, s));
+    CK(cudaEventRecord(c->ev_step, s));
+    CK(cudaEventSynchronize(c->ev_step));
+    const size_t MI = (size_t)(c->cfg.max_inserts > 0 ? c->cfg.max_inserts : 1);
+    volatile int32_t *nj_p = c->h_jobs + (size_t)c->cfg.n_layers * MI * 4;
+    const int nj = *nj_p;
+    c->copies_pending = false;
+    for (int j = 0; j < nj; ++j) {
+        const int l = c->h_jobs[4 * j], e = c->h_jobs[4 * j + 1], slot = c->h_jobs[4 * j + 2];
+        if (l < 0 || l >= c->cfg.n_layers || e < 0 || e >= c->cfg.n_expert || slot < 0 || slot >= c->L[l].ns)
+            return fail(c, MOE_ERR_DEVICE, "moe_step: bad job (%d, %d, %d)", l, e, slot);
+        LayerMem &m = c->L[l];
+        if (!m.hgate_user) return fail(c, MOE_ERR_STATE, "moe_step: layer %d has no host weights to upload from", l);
+        const uint8_t *hg = (const uint8_t *)m.hgate_user, *hu = (const uint8_t *)m.hup_user,
+                      *hd = (const uint8_t *)m.hdown_user;
+        CK(cudaMemcpyAsync(m.gate + (size_t)slot * c->gate_bytes, hg + (size_t)e * c->gate_bytes,
+                           c->gate_bytes, cudaMemcpyHostToDevice, c->copy_stream));
+        CK(cudaMemcpyAsync(m.up + (size_t)slot * c->gate_bytes, hu + (size_t)e * c->gate_bytes,
+                           c->gate_bytes, cudaMemcpyHostToDevice, c->copy_stream));
+        CK(cudaMemcpyAsync(m.down + (size_t)slot * c->down_bytes, hd + (size_t)e * c->down_bytes,
+                           c->down_bytes, cudaMemcpyHostToDevice, c->copy_stream));
+        c->upload_bytes += 2 * c->gate_bytes + c->down_bytes;
+    }
+    if (nj > 0) {
+        CK(cudaEventRecord(c->ev_copy, c->copy_stream));
+        c->copies_pending = true;
+    }
+    return MOE_OK;
+}
+
+extern "C" int moe_requires_sync(const moe_ctx *c) { return c ? 1 : 0; }
+
+extern "C" int moe_get_tables(moe_ctx *c, int layer, int32_t *expert_slot, int32_t *slot_expert,
+                              uint64_t *last_use, uint8_t *in_flight, uint64_t *protect) {
+    if (!c || layer < 0 || layer >= c->cfg.n_layers) return fail(c, MOE_ERR_ARG, "moe_get_tables: bad layer");
+    CK(cudaSetDevice(c->cfg.device));
+    CK(cudaDeviceSynchronize());
+    const int E = c->cfg.n_expert, ns = c->L[layer].ns, so = c->slot_off[layer];
+    if (expert_slot) {
+        CK(cudaMemcpy(expert_slot, c->st.table + (size_t)layer * E, 4 * E, cudaMemcpyDeviceToHost));
+        for (int e = 0; e < E; ++e) if (expert_slot[e] == ns) expert_slot[e] = -1;
+    }
+    if (slot_expert) CK(cudaMemcpy(slot_expert, c->st.slot_expert + so, 4 * ns, cudaMemcpyDeviceToHost));
+    if (last_use) CK(cudaMemcpy(last_use, c->st.last_use + so, 8 * ns, cudaMemcpyDeviceToHost));
+    if (in_flight) CK(cudaMemcpy(in_flight, c->st.in_flight + so, ns, cudaMemcpyDeviceToHost));
+    if (protect) CK(cudaMemcpy(protect, c->st.protect + so, 8 * ns, cudaMemcpyDeviceToHost));
+    return MOE_OK;
+}
+
+extern "C" int moe_get_gate_state(moe_ctx *c, int layer, float *heat, uint64_t *miss_last,
+                                  uint64_t *miss_prev, uint32_t *use_count) {
+    if (!c || layer < 0 || layer >= c->cfg.n_layers) return fail(c, MOE_ERR_ARG, "moe_get_gate_state: bad layer");
+    CK(cudaSetDevice(c->cfg.device));
+    CK(cudaDeviceSynchronize());
+    const size_t E = (size_t)c->cfg.n_expert, o = (size_t)layer * E;
+    if (heat && c->st.heat) CK(cudaMemcpy(heat, c->st.heat + o, 4 * E, cudaMemcpyDeviceToHost));
+    if (miss_last && c->st.miss_last) CK(cudaMemcpy(miss_last, c->st.miss_last + o, 8 * E, cudaMemcpyDeviceToHost));
+    if (miss_prev && c->st.miss_prev) CK(cudaMemcpy(miss_prev, c->st.miss_prev + o, 8 * E, cudaMemcpyDeviceToHost));
+    if (use_count && c->st.use_count) CK(cudaMemcpy(use_count, c->st.use_count + o, 4 * E, cudaMemcpyDeviceToHost));
+    return MOE_OK;
+}
+
+extern "C" int moe_get_stats(moe_ctx *c, uint64_t *out, int n) {
+    if (!c || !out || n <= 0) return fail(c, MOE_ERR_ARG, "moe_get_stats: bad argument");
+    CK(cudaSetDevice(c->cfg.device));
+    CK(cudaDeviceSynchronize());
+    uint64_t g[G_COUNT];
+    CK(cudaMemcpy(g, c->st.g, sizeof(g), cudaMemcpyDeviceToHost));
+    const int L = c->cfg.n_layers;
+    std::vector<uint64_t> hit(L), miss(L);
+    CK(cudaMemcpy(hit.data(), c->st.n_hit, 8 * L, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(miss.data(), c->st.n_miss, 8 * L, cudaMemcpyDeviceToHost));
+    uint64_t h = 0, m = 0;
+    for (int l = 0; l < L; ++l) { h += hit[l]; m += miss[l]; }
+    uint64_t all[MOE_STAT_COUNT] = {g[G_STEPS], g[G_CLOCK], h, m, g[G_UPLOADS], g[G_SCHEDULED],
+                                    g[G_COPIED], g[G_PUBLISHED], g[G_ADMIT_OK], g[G_ADMIT_DENIED],
+                                    g[G_FLUSHES], c->upload_bytes};
+    for (int i = 0; i < n && i < MOE_STAT_COUNT; ++i) out[i] = all[i];
+    return MOE_OK;
+}
+
+extern "C" int moe_warm_start(moe_ctx *c, const uint32_t *use_count) {
+    if (!c || !use_count) return fail(c, MOE_ERR_ARG, "moe_warm_start: bad argument");
+    CK(cudaSetDevice(c->cfg.device));
+    const int L = c->cfg.n_layers, E = c->cfg.n_expert;
+    if (c->st.use_count) CK(cudaMemcpy(c->st.use_count, use_count, 4 * (size_t)L * E, cudaMemcpyHostToDevice));
+    uint64_t clock = 0;
+    CK(cudaMemcpy(&clock, c->st.g + G_CLOCK, 8, cudaMemcpyDeviceToHost));
+    int placed = 0;
+    for (int l = 0; l < L; ++l) {
+        const uint32_t *uc = use_count + (size_t)l * E;
+        std::vector<int32_t> order(E);
+        for (int e = 0; e < E; ++e) order[e] = e;
+        std::stable_sort(order.begin(), order.end(), [&](int32_t a, int32_t b) { return uc[a] > uc[b]; });
+        const int ns = c->L[l].ns;
+        const int fill = ns;   // no reserve: early issue is off on the device
+        std::vector<int32_t> se(ns, -1);
+        std::vector<uint64_t> lu(ns, 0);
+        int slot = 0;
+        for (int k = 0; k < E && slot < fill; ++k) {
+            const int e = order[k];
+            if (uc[e] == 0) break;
+            se[slot] = e;
+            lu[slot] = (uint64_t)(fill - slot);
+            ++slot;
+            ++placed;
+        }
+        clock = std::max<uint64_t>(clock, (uint64_t)fill);
+        const int r = moe_place(c, l, se.data(), 1);
+        if (r != MOE_OK) return r;
+        CK(cudaMemcpy(c->st.last_use + c->slot_off[l], lu.data(), 8 * (size_t)ns, cudaMemcpyHostToDevice));
+    }
+    CK(cudaMemcpy(c->st.g + G_CLOCK, &clock, 8, cudaMemcpyHostToDevice));
+    return placed;
+}
+
+// ---------------------------------------------------------------------------
+// stateless kernels
+// ---------------------------------------------------------------------------
+
+extern "C" int moe_router_run(const float *W, const float *x, int n_tok, int n_expert, int n_embd,
+                              const int32_t *table, int n_slots, float delta, int k, int32_t *ids,
+                              float *w, float *logits, void *stream) {
+    if (!W || !x || !ids || !w || n_tok <= 0 || n_expert % 32 || n_expert > 256 || n_embd % 128 ||
+        k <= 0 || k > MOE_KMAX || k > n_expert)
+        return fail(nullptr, MOE_ERR_ARG, "moe_router_run: bad argument");
+    moe_ctx *c = nullptr;
+    CK(launch_router(W, x, n_tok, n_expert, n_embd, table, n_slots, delta,
+                     table != nullptr && delta > 0.0f && n_tok == 1, k, ids, w, logits, nullptr, -1,
+                     (cudaStream_t)stream));
+    return MOE_OK;
+}
+
+extern "C" int moe_quantize(const float *x, void *y, int64_t n, int qtype, void *stream) {
+    if (!x || !y || n % MOE_QK || (qtype != MOE_QTYPE_Q4_K && qtype != MOE_QTYPE_Q6_K))
+        return fail(nullptr, MOE_ERR_ARG, "moe_quantize: bad argument");
+    moe_ctx *c = nullptr;
+    CK(launch_quantize(x, y, n, qtype, (cudaStream_t)stream));
+    return MOE_OK;
+}
+
+extern "C" int moe_synth_weights(void *y, int64_t n_blocks, int qtype, uint64_t seed, float sigma,
+                                 void *stream) {
+    if (!y || n_blocks < 0 || (qtype != MOE_QTYPE_Q4_K && qtype != MOE_QTYPE_Q6_K))
+        return fail(nullptr, MOE_ERR_ARG, "moe_synth_weights: bad argument");
+    moe_ctx *c = nullptr;
+    CK(launch_synth_weights(y, n_blocks, qtype, seed, sigma, (cudaStream_t)stream));
+    return MOE_OK;
+}
+
+extern "C" int moe_synth_f32(float *y, int64_t n, uint64_t seed, float sigma, void *stream) {
+    if (!y || n < 0) return fail(nullptr, MOE_ERR_ARG, "moe_synth_f32: bad argument");
+    moe_ctx *c = nullptr;
+    CK(launch_synth_f32(y, n, seed, sigma, (cudaStream_t)stream));
+    return MOE_OK;
+}
+
+extern "C" int moe_decode_info(const moe_ctx *c, int32_t *out, int n) {
+    if (!c || !out) return MOE_ERR_ARG;
+    const int32_t v[] = {c->grid, c->dp.smem_bytes, c->dp.gu_rows_max, c->dp.dn_rows_max, 512};
+    for (int i = 0; i < n && i < 5; ++i) out[i] = v[i];
+    return MOE_OK;
+}
+
+// ---------------------------------------------------------------------------
+// ExpertCache (src/prefetch_engine.py)
+// ---------------------------------------------------------------------------
+
+struct moe_xc {
+    int n_layers = 0, n_experts = 0, capacity = 0, device = 0;
+    int64_t bytes = 0;
+    const uint8_t *staging = nullptr;
+    bool registered = false;
+    std::vector<uint8_t *> slabs;
+    // per layer: LRU list of experts (front = least recently used) + map
+    std::vector<std::list<int32_t>> lru;
+    std::vector<std::unordered_map<int32_t, std::pair<int32_t, std::list<int32_t>::iterator>>> map;
+    std::vector<std::vector<int32_t>> free_slots;
+    std::unordered_map<int64_t, cudaEvent_t> pending;   // (layer, expert) -> event
+    std::vector<cudaEvent_t> event_pool;
+    cudaStream_t copy_stream = nullptr;
+    uint64_t hits = 0, misses = 0, late = 0, fetches = 0, nbytes = 0, evictions = 0;
+};
+
+static int64_t xc_key(int layer, int e) { return (int64_t)layer << 32 | (uint32_t)e; }
+
+extern "C" int moe_xc_create(int n_layers, int n_experts, int capacity, int64_t bytes_per_expert,
+                             const void *host_staging, int device, moe_xc **out) {
+    if (!out || n_layers <= 0 || n_experts <= 0 || capacity <= 0 || bytes_per_expert <= 0 || !host_staging)
+        return fail(nullptr, MOE_ERR_ARG, "moe_xc_create: bad argument");
+    moe_ctx *c = nullptr;
+    CK(cudaSetDevice(device));
+    moe_xc *x = new moe_xc();
+    x->n_layers = n_layers; x->n_experts = n_experts; x->capacity = capacity; x->device = device;
+    x->bytes = bytes_per_expert;
+    x->staging = (const uint8_t *)host_staging;
+    cudaPointerAttributes at{};
+    if (cudaPointerGetAttributes(&at, host_staging) != cudaSuccess) { (void)cudaGetLastError(); at.type = cudaMemoryTypeUnregistered; }
+    if (at.type == cudaMemoryTypeUnregistered) {
+        if (cudaHostRegister(const_cast<void *>(host_staging), (size_t)n_experts * bytes_per_expert,
+                             cudaHostRegisterPortable) != cudaSuccess) {
+            (void)cudaGetLastError();
+            delete x;
+            return fail(nullptr, MOE_ERR_CUDA, "moe_xc_create: cudaHostRegister failed");
+        }
+        x->registered = true;
+    }
+    x->slabs.resize(n_layers, nullptr);
+    for (int l = 0; l < n_layers; ++l) {
+        if (cudaMalloc(&x->slabs[l], (size_t)capacity * bytes_per_expert) != cudaSuccess) {
+            moe_xc_destroy(x);
+            return fail(nullptr, MOE_ERR_OOM, "moe_xc_create: slab allocation failed");
+        }
+    }
+    x->lru.resize(n_layers);
+    x->map.resize(n_layers);
+    x->free_slots.resize(n_layers);
+    for (int l = 0; l < n_layers; ++l)
+        for (int s = 0; s < capacity; ++s) x->free_slots[l].push_back(s);   // pop() takes the last
+    if (cudaStreamCreateWithFlags(&x->copy_stream, cudaStreamNonBlocking) != cudaSuccess) {
+        moe_xc_destroy(x);
+        return fail(nullptr, MOE_ERR_CUDA, "moe_xc_create: stream creation failed");
+    }
+    *out = x;
+    return MOE_OK;
+}
+
+extern "C" void moe_xc_destroy(moe_xc *x) {
+    if (!x) return;
+    cudaSetDevice(x->device);
+    if (x->copy_stream) cudaStreamSynchronize(x->copy_stream);
+    for (auto &kv : x->pending) cudaEventDestroy(kv.second);
+    for (auto ev : x->event_pool) cudaEventDestroy(ev);
+    for (auto p : x->slabs) if (p) cudaFree(p);
+    if (x->registered) cudaHostUnregister(const_cast<uint8_t *>(x->staging));
+    if (x->copy_stream) cudaStreamDestroy(x->copy_stream);
+    delete x;
+}
+
+static void xc_drop_pending(moe_xc *x, int layer, int e) {
+    auto it = x->pending.find(xc_key(layer, e));
+    if (it != x->pending.end()) {
+        x->event_pool.push_back(it->second);
+        x->pending.erase(it);
+    }
+}
+
+// _slot_for (src/prefetch_engine.py:73-86)
+static int32_t xc_slot_for(moe_xc *x, int layer, int e) {
+    auto &m = x->map[layer];
+    auto &lru = x->lru[layer];
+    auto it = m.find(e);
+    if (it != m.end()) {
+        lru.splice(lru.end(), lru, it->second.second);
+        return it->second.first;
+    }
+    int32_t slot;
+    if (!x->free_slots[layer].empty()) {
+        slot = x->free_slots[layer].back();
+        x->free_slots[layer].pop_back();
+    } else {
+        const int32_t old = lru.front();
+        lru.pop_front();
+        slot = m[old].first;
+        m.erase(old);
+        xc_drop_pending(x, layer, old);
+        x->evictions++;
+    }
+    lru.push_back(e);
+    m[e] = {slot, std::prev(lru.end())};
+    return slot;
+}
+
+static int xc_fetch(moe_xc *x, int layer, const int32_t *ids, int n, bool count_started) {
+    moe_ctx *c = nullptr;
+    int started = 0;
+    for (int i = 0; i < n; ++i) {
+        const int e = ids[i];
+        if (e < 0 || e >= x->n_experts) return fail(nullptr, MOE_ERR_ARG, "expert id %d out of range", e);
+        auto it = x->map[layer].find(e);
+        if (it != x->map[layer].end()) {
+            x->lru[layer].splice(x->lru[layer].end(), x->lru[layer], it->second.second);
+            continue;
+        }
+        const int32_t slot = xc_slot_for(x, layer, e);
+        CK(cudaMemcpyAsync(x->slabs[layer] + (size_t)slot * x->bytes, x->staging + (size_t)e * x->bytes,
+                           (size_t)x->bytes, cudaMemcpyHostToDevice, x->copy_stream));
+        cudaEvent_t ev;
+        if (!x->event_pool.empty()) { ev = x->event_pool.back(); x->event_pool.pop_back(); }
+        else CK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+        CK(cudaEventRecord(ev, x->copy_stream));
+        xc_drop_pending(x, layer, e);
+        x->pending[xc_key(layer, e)] = ev;
+        started++;
+        x->fetches++;
+        x->nbytes += (uint64_t)x->bytes;
+    }
+    (void)count_started;
+    return started;
+}
+
+extern "C" int moe_xc_prefetch(moe_xc *x, int layer, const int32_t *ids, int n) {
+    if (!x || layer < 0 || layer >= x->n_layers || (n > 0 && !ids)) return MOE_ERR_ARG;
+    cudaSetDevice(x->device);
+    return xc_fetch(x, layer, ids, n, true);
+}
+
+extern "C" int moe_xc_admit(moe_xc *x, int layer, const int32_t *ids, int n) {
+    if (!x || layer < 0 || layer >= x->n_layers || (n > 0 && !ids)) return MOE_ERR_ARG;
+    cudaSetDevice(x->device);
+    const int r = xc_fetch(x, layer, ids, n, false);
+    return r < 0 ? r : MOE_OK;
+}
+
+extern "C" int moe_xc_query(moe_xc *x, int layer, const int32_t *ids, int n, int32_t *status) {
+    if (!x || layer < 0 || layer >= x->n_layers || (n > 0 && (!ids || !status))) return MOE_ERR_ARG;
+    cudaSetDevice(x->device);
+    for (int i = 0; i < n; ++i) {
+        const int e = ids[i];
+        auto it = x->map[layer].find(e);
+        if (it == x->map[layer].end()) {
+            status[i] = 2;
+            x->misses++;
+            continue;
+        }
+        auto pit = x->pending.find(xc_key(layer, e));
+        if (pit != x->pending.end()) {
+            const cudaError_t q = cudaEventQuery(pit->second);
+            if (q == cudaErrorNotReady) {
+                (void)cudaGetLastError();
+                status[i] = 1;
+                x->late++;
+                continue;
+            }
+            xc_drop_pending(x, layer, e);
+        }
+        x->lru[layer].splice(x->lru[layer].end(), x->lru[layer], it->second.second);
+        status[i] = 0;
+        x->hits++;
+    }
+    return MOE_OK;
+}
+
+extern "C" int moe_xc_sync(moe_xc *x) {
+    if (!x) return MOE_ERR_ARG;
+    cudaSetDevice(x->device);
+    moe_ctx *c = nullptr;
+    CK(cudaStreamSynchronize(x->copy_stream));
+    return MOE_OK;
+}
+
+extern "C" int64_t moe_xc_vram_bytes(const moe_xc *x) {
+    return x ? (int64_t)x->n_layers * x->capacity * x->bytes : 0;
+}
+
+extern "C" int moe_xc_stats(const moe_xc *x, uint64_t *out6) {
+    if (!x || !out6) return MOE_ERR_ARG;
+    out6[0] = x->hits; out6[1] = x->misses; out6[2] = x->late;
+    out6[3] = x->fetches; out6[4] = x->nbytes; out6[5] = x->evictions;
+    return MOE_OK;
+}
+
+extern "C" void *moe_xc_slab(moe_xc *x, int layer) {
+    return x && layer >= 0 && layer < x->n_layers ? x->slabs[layer] : nullptr;
+}
+
+extern "C" int moe_xc_slot_of(const moe_xc *x, int layer, int expert) {
+    if (!x || layer < 0 || layer >= x->n_layers) return -1;
+    auto it = x->map[layer].find(expert);
+    return it == x->map[layer].end() ? -1 : it->second.first;
+}

@@ -1,0 +1,496 @@
+// moe_dev.cuh -- device helpers shared by every kernel of libmoeb200.so:
+// exact fp32 math (exp, SiLU), the canonical router reduction, Q4_K / Q6_K x
+// Q8_1 integer dots, activation quantisation, bulk-copy / mbarrier / timer
+// wrappers, and the slot-table observation (moe_obs_cb) on the device.
+//
+// Exactness contract: every fp32 operation whose result reaches an expert id
+// (router dot, softmax, prior add, top-k, renormalisation) is written with
+// explicit round-to-nearest intrinsics (__fmaf_rn, __fadd_rn, __fmul_rn,
+// __fdiv_rn), so nvcc cannot contract or reorder them, and the CPU oracle
+// (oracle/moe_oracle.c) performs the same operations in the same order.
+#pragma once
+
+#include <cstdint>
+#include <cuda_fp16.h>
+
+#define MOE_FULL 0xffffffffu
+#define MOE_QK 256
+#define MOE_Q4K_BYTES 144
+#define MOE_Q6K_BYTES 210
+#define MOE_QT_Q4K 12
+#define MOE_QT_Q6K 14
+#define MOE_KMAX 16              // max experts per token (incl. shared)
+#define MOE_TIMEOUT_NS 2000000000ull   // 2 s: every device wait gives up after this
+
+// device error bits (moe_api maps them to MOE_ERR_*)
+#define MOE_DEV_ERR_TIMEOUT 1
+#define MOE_DEV_ERR_INDEX   2
+
+namespace moe {
+
+// ---------------------------------------------------------------------------
+// exact fp32 math
+// ---------------------------------------------------------------------------
+
+// exp(x) by Cody-Waite reduction x = n ln2 + r (ln2 split in a head with 12
+// trailing zero bits and a tail) and the degree-7 Taylor polynomial of e^r in
+// Horner form, then 2^n through the exponent field.  The same sequence of
+// correctly rounded fp32 operations as or_expf() in the oracle.
+__device__ __forceinline__ float expf_exact(float x) {
+    if (x < -80.0f) return 0.0f;
+    if (x > 80.0f) x = 80.0f;
+    const float t = __fmul_rn(x, 0x1.715476p+0f);
+    const float n = rintf(t);
+    float r = __fmaf_rn(-n, 0x1.62e000p-1f, x);
+    r = __fmaf_rn(-n, 0x1.0bfbe8p-15f, r);
+    float p = 0x1.a01a02p-13f;
+    p = __fmaf_rn(p, r, 0x1.6c16c2p-10f);
+    p = __fmaf_rn(p, r, 0x1.111112p-7f);
+    p = __fmaf_rn(p, r, 0x1.555556p-5f);
+    p = __fmaf_rn(p, r, 0x1.555556p-3f);
+    p = __fmaf_rn(p, r, 0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    const int ni = (int)n;
+    return __fmul_rn(p, __int_as_float((ni + 127) << 23));
+}
+
+// SiLU(g) * u = g / (1 + e^-g) * u
+__device__ __forceinline__ float silu_mul(float g, float u) {
+    const float e = expf_exact(-g);
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, e)), u);
+}
+
+__device__ __forceinline__ float h2f(uint32_t bits16) {
+    return __half2float(__ushort_as_half((unsigned short)(bits16 & 0xFFFFu)));
+}
+
+// ---------------------------------------------------------------------------
+// canonical router: one warp per logit
+// ---------------------------------------------------------------------------
+
+// Lane l owns columns 128*kk + 4*l + c, keeps four fma chains (c = 0..3) over
+// kk, folds them as (a0+a1)+(a2+a3), then an xor butterfly 16,8,4,2,1.
+// Every lane returns the same value.  w and x may be shared or global.
+__device__ __forceinline__ float router_dot_warp(const float *__restrict__ w,
+                                                 const float *__restrict__ x, int n_embd,
+                                                 int lane) {
+    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+    for (int kk = 0; kk < n_embd / 128; ++kk) {
+        const int j = 128 * kk + 4 * lane;
+        const float4 wv = *reinterpret_cast<const float4 *>(w + j);
+        const float4 xv = *reinterpret_cast<const float4 *>(x + j);
+        a0 = __fmaf_rn(wv.x, xv.x, a0);
+        a1 = __fmaf_rn(wv.y, xv.y, a1);
+        a2 = __fmaf_rn(wv.z, xv.z, a2);
+        a3 = __fmaf_rn(wv.w, xv.w, a3);
+    }
+    float v = __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(MOE_FULL, v, off));
+    return v;
+}
+
+// Softmax over n_expert logits, + delta on resident experts (table[e] != ns)
+// when use_prior, top-k by selection value (ties to the lower id), weights
+// from the unbiased probabilities renormalised over the k.  One warp; lane l
+// holds experts l, l+32, ...  ids/w written by lane 0 (any memory).
+__device__ __forceinline__ void router_select_warp(const float *logits, int n_expert,
+                                                   const int32_t *table, int ns, float delta,
+                                                   bool use_prior, int k, int32_t *ids_out,
+                                                   float *w_out, int lane) {
+    const int m = n_expert >> 5;   // <= 8
+    float lg[8], ex[8], p[8], sel[8];
+    bool taken[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        lg[i] = i < m ? logits[lane + 32 * i] : -INFINITY;
+        taken[i] = false;
+    }
+    float mx = lg[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i)
+        if (i < m) mx = fmaxf(mx, lg[i]);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(MOE_FULL, mx, off));
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        if (i < m) {
+            ex[i] = expf_exact(__fsub_rn(lg[i], mx));
+            s = i == 0 ? ex[0] : __fadd_rn(s, ex[i]);
+        }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) s = __fadd_rn(s, __shfl_xor_sync(MOE_FULL, s, off));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        if (i < m) {
+            p[i] = __fdiv_rn(ex[i], s);
+            const int e = lane + 32 * i;
+            const bool res = use_prior && table != nullptr && table[e] != ns;
+            sel[i] = res ? __fadd_rn(p[i], delta) : p[i];
+        } else {
+            p[i] = 0.0f;
+            sel[i] = -INFINITY;
+            taken[i] = true;
+        }
+    }
+    float psel[MOE_KMAX];
+    int isel[MOE_KMAX];
+    for (int r = 0; r < k; ++r) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        float bp = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int e = lane + 32 * i;
+            if (!taken[i] && (sel[i] > bv || (sel[i] == bv && e < bi))) {
+                bv = sel[i];
+                bi = e;
+                bp = p[i];
+            }
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+            const float ov = __shfl_xor_sync(MOE_FULL, bv, off);
+            const int oi = __shfl_xor_sync(MOE_FULL, bi, off);
+            const float op = __shfl_xor_sync(MOE_FULL, bp, off);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+                bp = op;
+            }
+        }
+        if ((bi & 31) == lane) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (i == (bi >> 5)) taken[i] = true;
+        }
+        isel[r] = bi;
+        psel[r] = bp;
+    }
+    float ws = psel[0];
+    for (int r = 1; r < k; ++r) ws = __fadd_rn(ws, psel[r]);
+    if (lane == 0) {
+        for (int r = 0; r < k; ++r) {
+            ids_out[r] = isel[r];
+            w_out[r] = __fdiv_rn(psel[r], ws);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// activation quantisation (Q8_1 blocks of 32, fp32 d and s)
+// ---------------------------------------------------------------------------
+
+// One warp quantises one block of 32 values: lane l takes element l.
+// d = amax / 127, q = roundf(x / d), s = d * sum(q); as or_quantize_q8_1().
+__device__ __forceinline__ void q8_block_warp(float v, int lane, int8_t *q, float *d,
+                                              float *s) {
+    float amax = fabsf(v);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(MOE_FULL, amax, off));
+    const float db = __fdiv_rn(amax, 127.0f);
+    const int qi = amax > 0.0f ? (int)roundf(__fdiv_rn(v, db)) : 0;
+    int sum = qi;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) sum += __shfl_xor_sync(MOE_FULL, sum, off);
+    q[lane] = (int8_t)qi;
+    if (lane == 0) {
+        *d = db;
+        *s = __fmul_rn(db, (float)sum);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Q4_K x Q8_1
+// ---------------------------------------------------------------------------
+
+// Activations of one lane's unit: super-block sb, sub-block pair p, i.e.
+// 64 int8 values (sub-blocks 2p and 2p+1) and their d / s.
+struct ActQ4 {
+    int lo[8], hi[8];
+    float d0, d1, s0, s1;
+};
+
+__device__ __forceinline__ void load_act_q4(ActQ4 &a, const int8_t *q, const float *d,
+                                            const float *s, int sb, int p) {
+    const int4 *ql = reinterpret_cast<const int4 *>(q + 256 * sb + 64 * p);
+    const int4 v0 = ql[0], v1 = ql[1], v2 = ql[2], v3 = ql[3];
+    a.lo[0] = v0.x; a.lo[1] = v0.y; a.lo[2] = v0.z; a.lo[3] = v0.w;
+    a.lo[4] = v1.x; a.lo[5] = v1.y; a.lo[6] = v1.z; a.lo[7] = v1.w;
+    a.hi[0] = v2.x; a.hi[1] = v2.y; a.hi[2] = v2.z; a.hi[3] = v2.w;
+    a.hi[4] = v3.x; a.hi[5] = v3.y; a.hi[6] = v3.z; a.hi[7] = v3.w;
+    const int b = 8 * sb + 2 * p;
+    a.d0 = d[b]; a.d1 = d[b + 1];
+    a.s0 = s[b]; a.s1 = s[b + 1];
+}
+
+__device__ __forceinline__ int byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xFF; }
+
+// 6-bit scale and min of sub-block j from the 12 scale bytes held in
+// (w0: bytes 0-3, w1: 4-7, w2: 8-11)  (upstream get_scale_min_k4).
+__device__ __forceinline__ void q4k_sm(uint32_t w0, uint32_t w1, uint32_t w2, int j, int &sc,
+                                       int &m) {
+    if (j < 4) {
+        sc = byte_of(w0, j) & 63;
+        m = byte_of(w1, j) & 63;
+    } else {
+        const int jj = j - 4;
+        const int b8 = byte_of(w2, jj);
+        sc = (b8 & 0xF) | ((byte_of(w0, jj) >> 6) << 4);
+        m = (b8 >> 4) | ((byte_of(w1, jj) >> 6) << 4);
+    }
+}
+
+// Partial dot of one unit of a Q4_K row (16-byte aligned block pointer `blk`
+// of super-block sb) with the unit's activations.  Loads are 128-bit.
+__device__ __forceinline__ float q4k_unit_dot(const uint8_t *blk, int p, const ActQ4 &a) {
+    const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);
+    const uint4 q0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * p);
+    const uint4 q1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * p);
+    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    int slo = 0, shi = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        slo = __dp4a((int)(w[i] & 0x0F0F0F0Fu), a.lo[i], slo);
+        shi = __dp4a((int)((w[i] >> 4) & 0x0F0F0F0Fu), a.hi[i], shi);
+    }
+    int sc0, m0, sc1, m1;
+    q4k_sm(hdr.y, hdr.z, hdr.w, 2 * p, sc0, m0);
+    q4k_sm(hdr.y, hdr.z, hdr.w, 2 * p + 1, sc1, m1);
+    const float d = h2f(hdr.x), dmin = h2f(hdr.x >> 16);
+    const float acc = (float)(sc0 * slo) * a.d0 + (float)(sc1 * shi) * a.d1;
+    const float mm = (float)m0 * a.s0 + (float)m1 * a.s1;
+    return d * acc - dmin * mm;
+}
+
+// ---------------------------------------------------------------------------
+// Q6_K x Q8_1
+// ---------------------------------------------------------------------------
+
+// 8 bytes at a 2-byte-aligned address, through aligned 32-bit loads and
+// funnel shifts (Q6_K blocks are 210 bytes, so rows are only 2-byte aligned).
+// Only the words that hold requested bytes are read: never past ptr + 8.
+__device__ __forceinline__ uint2 ld8_a2(const uint8_t *ptr) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(ptr);
+    const uint32_t *p = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
+    const uint32_t sh = (uint32_t)(a & 2) * 8u;
+    const uint32_t w0 = p[0], w1 = p[1];
+    const uint32_t w2 = sh ? p[2] : 0u;
+    return make_uint2(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh));
+}
+
+// Activations of one lane's Q6_K unit (super-block sb, half h, l in
+// [8j, 8j+8)): for m = 0..3 the 8 int8 values at 128h + 32m + 8j, and the d of
+// their Q8_1 block.
+struct ActQ6 {
+    int q[4][2];
+    float d[4];
+};
+
+__device__ __forceinline__ void load_act_q6(ActQ6 &a, const int8_t *q, const float *d, int sb,
+                                            int h, int j) {
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        const int e = 256 * sb + 128 * h + 32 * m + 8 * j;
+        const int2 v = *reinterpret_cast<const int2 *>(q + e);
+        a.q[m][0] = v.x;
+        a.q[m][1] = v.y;
+        a.d[m] = d[e >> 5];
+    }
+}
+
+__device__ __forceinline__ float q6k_unit_dot(const uint8_t *blk, int h, int j, const ActQ6 &a) {
+    const uint2 lo = ld8_a2(blk + 64 * h + 8 * j);
+    const uint2 hi = ld8_a2(blk + 64 * h + 32 + 8 * j);
+    const uint2 qh = ld8_a2(blk + 128 + 32 * h + 8 * j);
+    const uint2 scw = ld8_a2(blk + 192 + 8 * h);
+    const float d = h2f(*reinterpret_cast<const uint16_t *>(blk + 208));
+    const int c = j >= 2 ? 1 : 0;
+    const uint32_t L[2] = {lo.x, lo.y}, Hh[2] = {hi.x, hi.y}, Q[2] = {qh.x, qh.y};
+    int is[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int wi = 0; wi < 2; ++wi) {
+        const uint32_t v0 = (L[wi] & 0x0F0F0F0Fu) | ((Q[wi] << 4) & 0x30303030u);
+        const uint32_t v1 = (Hh[wi] & 0x0F0F0F0Fu) | ((Q[wi] << 2) & 0x30303030u);
+        const uint32_t v2 = ((L[wi] >> 4) & 0x0F0F0F0Fu) | (Q[wi] & 0x30303030u);
+        const uint32_t v3 = ((Hh[wi] >> 4) & 0x0F0F0F0Fu) | ((Q[wi] >> 2) & 0x30303030u);
+        is[0] = __dp4a((int)__vsub4(v0, 0x20202020u), a.q[0][wi], is[0]);
+        is[1] = __dp4a((int)__vsub4(v1, 0x20202020u), a.q[1][wi], is[1]);
+        is[2] = __dp4a((int)__vsub4(v2, 0x20202020u), a.q[2][wi], is[2]);
+        is[3] = __dp4a((int)__vsub4(v3, 0x20202020u), a.q[3][wi], is[3]);
+    }
+    float acc = 0.0f;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        const int pos = c + 2 * m;   // scale byte index within the 8 loaded
+        const uint32_t wsel = pos < 4 ? scw.x : scw.y;
+        const int sc = (int)(int8_t)((wsel >> (8 * (pos & 3))) & 0xFF);
+        acc += (float)(sc * is[m]) * a.d[m];
+    }
+    return d * acc;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(MOE_FULL, v, off);
+    return v;
+}
+
+// ---------------------------------------------------------------------------
+// bulk copies, mbarriers, timers
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ uint64_t gtimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: false after MOE_TIMEOUT_NS.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = gtimer();
+    while (!mbar_try_wait(bar, parity)) {
+        if (gtimer() - t0 > MOE_TIMEOUT_NS) return false;
+    }
+    return true;
+}
+
+// global -> shared bulk copy (TMA, no multicast); dst, src 16-byte aligned,
+// bytes a multiple of 16; completion is counted on `bar`.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes,
+                                         uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_u32(const unsigned *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ int ld_relaxed_i32(const int *p) {
+    int v;
+    asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// ---------------------------------------------------------------------------
+// slot-table state on the device
+// ---------------------------------------------------------------------------
+
+// Flattened per-layer arrays.  Slot-indexed arrays use slot_off[layer].
+struct SlotState {
+    int n_layers, n_expert, max_inserts, admit_mode, admit_window, admit_half;
+    float admit_floor, cache_prior;
+    int spec_probation, batch_tables, freeze;
+    const int32_t *ns;          // [L]
+    const int32_t *slot_off;    // [L]
+    int32_t *table;             // [L][E]   expert -> slot, ns = not resident
+    int32_t *slot_expert;       // [sum ns]
+    uint64_t *last_use;         // [sum ns]
+    uint64_t *protect;          // [sum ns]
+    uint8_t *in_flight;         // [sum ns]
+    int32_t *pending;           // [L][E]
+    int32_t *n_pending;         // [L]
+    float *heat;                // [L][E] or null
+    uint64_t *miss_last;        // [L][E] or null
+    uint64_t *miss_prev;        // [L][E] or null
+    uint32_t *use_count;        // [L][E] or null
+    uint64_t *n_hit;            // [L]
+    uint64_t *n_miss;           // [L]
+    uint64_t *g;                // globals: see G_* below
+    int32_t *jobs;              // [L][max_inserts][4] (expert, slot, spec, -)
+    int32_t *n_jobs;            // [L]
+};
+
+enum { G_CLOCK = 0, G_STEPS, G_UPLOADS, G_SCHEDULED, G_COPIED, G_PUBLISHED, G_ADMIT_OK,
+       G_ADMIT_DENIED, G_FLUSHES, G_UPLOAD_BYTES, G_COUNT };
+
+// moe_obs_cb for one single-token layer (patches/0006:295-400 with the
+// 0007:247-270 window/heat bookkeeping; early issue is not on the device).
+// One thread.
+__device__ __forceinline__ void observe_layer(const SlotState &st, int layer,
+                                              const int32_t *ids, int n) {
+    const int E = st.n_expert;
+    const int ns = st.ns[layer];
+    const int so = st.slot_off[layer];
+    int32_t *tbl = st.table + (size_t)layer * E;
+    int32_t *pend = st.pending + (size_t)layer * E;
+    const uint64_t n_steps = st.g[G_STEPS];
+    uint64_t clock = st.g[G_CLOCK];
+    for (int i = 0; i < n; ++i) {
+        const int id = ids[i];
+        if (id < 0 || id >= E) continue;
+        if (st.heat) st.heat[(size_t)layer * E + id] += 1.0f;
+        if (st.use_count) st.use_count[(size_t)layer * E + id] += 1u;
+        const int slot = tbl[id];
+        if (slot != ns) {
+            st.n_hit[layer] += 1;
+            st.last_use[so + slot] = ++clock;
+        } else {
+            st.n_miss[layer] += 1;
+            if (st.miss_last) {
+                uint64_t *ml = st.miss_last + (size_t)layer * E;
+                uint64_t *mp = st.miss_prev + (size_t)layer * E;
+                if (ml[id] != n_steps) {
+                    mp[id] = ml[id];
+                    ml[id] = n_steps;
+                }
+            }
+            const int np = st.n_pending[layer];
+            bool dup = false;
+            for (int q = 0; q < np; ++q)
+                if (pend[q] == id) { dup = true; break; }
+            if (!dup) {
+                pend[np] = id;
+                st.n_pending[layer] = np + 1;
+            }
+        }
+    }
+    st.g[G_CLOCK] = clock;
+}
+
+}  // namespace moe

@@ -1,0 +1,555 @@
+// moe_kernels.cu -- stand-alone kernels of libmoeb200.so:
+//   weight quantisation (Q4_K / Q6_K, bit-identical to the oracle) and the
+//   synthetic-weight generator; the fused router; the gate/up GEMV with fused
+//   SiLU*mul; the down GEMV with the fused weighted top-k combine; the device
+//   slot table (observation and the cache step).
+// The persistent multi-layer decode kernel lives in moe_decode.cu.
+#include "moe_kernels.h"
+
+namespace moe {
+
+// ===========================================================================
+// quantisation (our own quantiser; same fp32 operation sequence as
+// or_quantize_q4_K / or_quantize_q6_K in the oracle)
+// ===========================================================================
+
+__device__ __forceinline__ int clampi(int v, int lo, int hi) { return v < lo ? lo : v > hi ? hi : v; }
+
+__device__ void quantize_q4k_block(const float *xb, uint8_t *yb) {
+    float scale[8], minv[8];
+    float max_scale = 0.0f, max_min = 0.0f;
+    for (int j = 0; j < 8; ++j) {
+        float mn = xb[32 * j], mx = xb[32 * j];
+        for (int l = 1; l < 32; ++l) {
+            const float v = xb[32 * j + l];
+            if (v < mn) mn = v;
+            if (v > mx) mx = v;
+        }
+        if (mn > 0.0f) mn = 0.0f;
+        scale[j] = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
+        minv[j] = -mn;
+        if (scale[j] > max_scale) max_scale = scale[j];
+        if (minv[j] > max_min) max_min = minv[j];
+    }
+    const __half dh = __float2half_rn(__fdiv_rn(max_scale, 63.0f));
+    const __half mh = __float2half_rn(__fdiv_rn(max_min, 63.0f));
+    const float dd = __half2float(dh), dm = __half2float(mh);
+    int sc[8], m[8];
+    for (int j = 0; j < 8; ++j) {
+        sc[j] = dd > 0.0f ? clampi((int)roundf(__fdiv_rn(scale[j], dd)), 0, 63) : 0;
+        m[j] = dm > 0.0f ? clampi((int)roundf(__fdiv_rn(minv[j], dm)), 0, 63) : 0;
+    }
+    const unsigned short dbits = __half_as_ushort(dh), mbits = __half_as_ushort(mh);
+    yb[0] = (uint8_t)(dbits & 0xFF);
+    yb[1] = (uint8_t)(dbits >> 8);
+    yb[2] = (uint8_t)(mbits & 0xFF);
+    yb[3] = (uint8_t)(mbits >> 8);
+    for (int j = 0; j < 4; ++j) {
+        yb[4 + j] = (uint8_t)((sc[j] & 63) | ((sc[j + 4] >> 4) << 6));
+        yb[8 + j] = (uint8_t)((m[j] & 63) | ((m[j + 4] >> 4) << 6));
+        yb[12 + j] = (uint8_t)((sc[j + 4] & 0xF) | ((m[j + 4] & 0xF) << 4));
+    }
+    for (int p = 0; p < 4; ++p) {
+        const float es0 = __fmul_rn(dd, (float)sc[2 * p]), em0 = __fmul_rn(dm, (float)m[2 * p]);
+        const float es1 = __fmul_rn(dd, (float)sc[2 * p + 1]), em1 = __fmul_rn(dm, (float)m[2 * p + 1]);
+        for (int l = 0; l < 32; ++l) {
+            const int q0 = es0 > 0.0f
+                ? clampi((int)roundf(__fdiv_rn(__fadd_rn(xb[64 * p + l], em0), es0)), 0, 15) : 0;
+            const int q1 = es1 > 0.0f
+                ? clampi((int)roundf(__fdiv_rn(__fadd_rn(xb[64 * p + 32 + l], em1), es1)), 0, 15) : 0;
+            yb[16 + 32 * p + l] = (uint8_t)(q0 | (q1 << 4));
+        }
+    }
+}
+
+__device__ void quantize_q6k_block(const float *xb, uint8_t *yb) {
+    float gscale[16];
+    float max_scale = 0.0f;
+    for (int g = 0; g < 16; ++g) {
+        float amax = 0.0f;
+        for (int l = 0; l < 16; ++l) {
+            const float a = fabsf(xb[16 * g + l]);
+            if (a > amax) amax = a;
+        }
+        gscale[g] = __fdiv_rn(amax, 31.0f);
+        if (gscale[g] > max_scale) max_scale = gscale[g];
+    }
+    const __half dh = __float2half_rn(__fdiv_rn(max_scale, 127.0f));
+    const float dd = __half2float(dh);
+    int sc[16];
+    for (int g = 0; g < 16; ++g) {
+        sc[g] = dd > 0.0f ? clampi((int)roundf(__fdiv_rn(gscale[g], dd)), -128, 127) : 0;
+        yb[192 + g] = (uint8_t)(int8_t)sc[g];
+    }
+    for (int h = 0; h < 2; ++h) {
+        for (int l = 0; l < 32; ++l) {
+            int q[4];
+            for (int mm = 0; mm < 4; ++mm) {
+                const int e = 128 * h + 32 * mm + l;
+                const float es = __fmul_rn(dd, (float)sc[e >> 4]);
+                const int v = es != 0.0f ? clampi((int)roundf(__fdiv_rn(xb[e], es)), -32, 31) : 0;
+                q[mm] = v + 32;
+            }
+            yb[64 * h + l] = (uint8_t)((q[0] & 0xF) | ((q[2] & 0xF) << 4));
+            yb[64 * h + l + 32] = (uint8_t)((q[1] & 0xF) | ((q[3] & 0xF) << 4));
+            yb[128 + 32 * h + l] = (uint8_t)((q[0] >> 4) | ((q[1] >> 4) << 2) | ((q[2] >> 4) << 4) |
+                                             ((q[3] >> 4) << 6));
+        }
+    }
+    const unsigned short dbits = __half_as_ushort(dh);
+    yb[208] = (uint8_t)(dbits & 0xFF);
+    yb[209] = (uint8_t)(dbits >> 8);
+}
+
+__global__ void k_quantize(const float *__restrict__ x, uint8_t *__restrict__ y, int64_t nb,
+                           int qtype) {
+    const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= nb) return;
+    if (qtype == MOE_QT_Q4K) quantize_q4k_block(x + b * MOE_QK, y + b * MOE_Q4K_BYTES);
+    else quantize_q6k_block(x + b * MOE_QK, y + b * MOE_Q6K_BYTES);
+}
+
+// splitmix64 finaliser (S. Vigna's public-domain generator) as a counter hash
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+// Synthetic N(0, sigma^2) weights straight into quantised blocks: element i of
+// block b takes the Box-Muller normal of hash(seed, b*256 + i).  No fp32 copy
+// of the weights ever exists in HBM.
+__global__ void k_synth_weights(uint8_t *__restrict__ y, int64_t nb, int qtype, uint64_t seed,
+                                float sigma) {
+    const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= nb) return;
+    float xb[MOE_QK];
+    const uint64_t base = mix64(seed) ^ (uint64_t)b * 0x100000001B3ull;
+    for (int i = 0; i < MOE_QK; i += 2) {
+        const uint64_t h = mix64(base + (uint64_t)i);
+        const float u1 = ((float)(h >> 40) + 1.0f) * 0x1.0p-24f;
+        const float u2 = (float)(h & 0xFFFFFFull) * 0x1.0p-24f;
+        const float r = sqrtf(-2.0f * logf(u1)) * sigma;
+        float sn, cs;
+        sincospif(2.0f * u2, &sn, &cs);
+        xb[i] = r * cs;
+        xb[i + 1] = r * sn;
+    }
+    if (qtype == MOE_QT_Q4K) quantize_q4k_block(xb, y + b * MOE_Q4K_BYTES);
+    else quantize_q6k_block(xb, y + b * MOE_Q6K_BYTES);
+}
+
+// Synthetic fp32 N(0, sigma^2) (router weights, inputs), same hash.
+__global__ void k_synth_f32(float *__restrict__ y, int64_t n, uint64_t seed, float sigma) {
+    const int64_t i2 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 2;
+    if (i2 >= n) return;
+    const uint64_t h = mix64(mix64(seed) + (uint64_t)i2);
+    const float u1 = ((float)(h >> 40) + 1.0f) * 0x1.0p-24f;
+    const float u2 = (float)(h & 0xFFFFFFull) * 0x1.0p-24f;
+    const float r = sqrtf(-2.0f * logf(u1)) * sigma;
+    float sn, cs;
+    sincospif(2.0f * u2, &sn, &cs);
+    y[i2] = r * cs;
+    if (i2 + 1 < n) y[i2 + 1] = r * sn;
+}
+
+// ===========================================================================
+// fused router: one CTA per token, one warp per logit, warp 0 selects
+// ===========================================================================
+
+__global__ void __launch_bounds__(512) k_router(const float *__restrict__ W,
+                                                const float *__restrict__ x, int n_expert,
+                                                int n_embd, const int32_t *__restrict__ table,
+                                                int ns, float delta, int use_prior, int k,
+                                                int32_t *__restrict__ ids, float *__restrict__ w,
+                                                float *__restrict__ logits_out,
+                                                SlotState st, int observe_layer_idx) {
+    extern __shared__ __align__(16) float sm[];
+    float *xs = sm;                   // [n_embd]
+    float *lg = sm + n_embd;          // [n_expert]
+    const int t = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int i = threadIdx.x; i < n_embd; i += blockDim.x) xs[i] = x[(size_t)t * n_embd + i];
+    __syncthreads();
+    for (int e = warp; e < n_expert; e += nw) {
+        const float v = router_dot_warp(W + (size_t)e * n_embd, xs, n_embd, lane);
+        if (lane == 0) {
+            lg[e] = v;
+            if (logits_out) logits_out[(size_t)t * n_expert + e] = v;
+        }
+    }
+    __syncthreads();
+    if (warp == 0) {
+        __shared__ int32_t sids[MOE_KMAX];
+        __shared__ float sw[MOE_KMAX];
+        router_select_warp(lg, n_expert, table, ns, delta, use_prior != 0, k, sids, sw, lane);
+        __syncwarp();
+        if (lane < k) {
+            ids[(size_t)t * k + lane] = sids[lane];
+            w[(size_t)t * k + lane] = sw[lane];
+        }
+        if (observe_layer_idx >= 0 && lane == 0) observe_layer(st, observe_layer_idx, sids, k);
+    }
+}
+
+// ===========================================================================
+// gate/up GEMV with fused SiLU*mul (stand-alone; direct global loads)
+// grid: (ceil(n_ff / GU_ROWS), n_tok * k); block 256 (8 warps)
+// ===========================================================================
+
+#define GU_ROWS 32
+
+__device__ __forceinline__ const uint8_t *expert_base(const ExpertSrc &s, int which, int id,
+                                                      int32_t slot) {
+    // which: 0 gate, 1 up, 2 down
+    const uint8_t *slab = which == 0 ? s.gate : which == 1 ? s.up : s.down;
+    const uint8_t *host = which == 0 ? s.hgate : which == 1 ? s.hup : s.hdown;
+    const int64_t bytes = which == 2 ? s.down_bytes : s.gate_bytes;
+    if (slot != s.ns && slab) return slab + (int64_t)slot * bytes;
+    return host ? host + (int64_t)id * bytes : nullptr;
+}
+
+__global__ void __launch_bounds__(256) k_gate_up(ExpertSrc src, const float *__restrict__ x,
+                                                 const int32_t *__restrict__ ids, int k,
+                                                 int n_embd, int n_ff,
+                                                 float *__restrict__ act, int *err) {
+    __shared__ __align__(16) int8_t xq[4096];
+    __shared__ float xd[128], xsum[128];
+    const int tk = blockIdx.y, t = tk / k;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const float *xt = x + (size_t)t * n_embd;
+    for (int b = warp; b < n_embd / 32; b += nw)
+        q8_block_warp(xt[32 * b + lane], lane, xq + 32 * b, xd + b, xsum + b);
+    __syncthreads();
+    const int id = ids[tk];
+    if (id < 0 || id >= src.n_expert) {
+        if (threadIdx.x == 0) atomicOr(err, MOE_DEV_ERR_INDEX);
+        return;
+    }
+    const int32_t slot = src.table ? src.table[id] : src.ns;
+    const uint8_t *gbase = expert_base(src, 0, id, slot);
+    const uint8_t *ubase = expert_base(src, 1, id, slot);
+    if (!gbase || !ubase) {
+        if (threadIdx.x == 0) atomicOr(err, MOE_DEV_ERR_INDEX);
+        return;
+    }
+    const int nb = n_embd / MOE_QK;           // super-blocks per row
+    const size_t rb = (size_t)nb * MOE_Q4K_BYTES;
+    const int units = nb * 4;   // n_embd == 2048 gives exactly one unit per lane
+    const int u = lane;
+    const bool active = u < units;
+    ActQ4 a;
+    if (active) load_act_q4(a, xq, xd, xsum, u >> 2, u & 3);
+    const int i0 = blockIdx.x * GU_ROWS;
+    for (int r = warp; r < GU_ROWS; r += nw) {
+        const int i = i0 + r;
+        if (i >= n_ff) break;
+        float g = 0.0f, up = 0.0f;
+        for (int uu = u; uu < units; uu += 32) {
+            ActQ4 aa = a;
+            if (uu != u) load_act_q4(aa, xq, xd, xsum, uu >> 2, uu & 3);
+            g += q4k_unit_dot(gbase + i * rb + (uu >> 2) * MOE_Q4K_BYTES, uu & 3, aa);
+            up += q4k_unit_dot(ubase + i * rb + (uu >> 2) * MOE_Q4K_BYTES, uu & 3, aa);
+        }
+        g = warp_sum(g);
+        up = warp_sum(up);
+        if (lane == 0) act[(size_t)tk * n_ff + i] = silu_mul(g, up);
+    }
+}
+
+// ===========================================================================
+// down GEMV with fused weighted combine (stand-alone; direct global loads)
+// grid: (ceil(n_embd / DN_ROWS), n_tok); block 256
+// ===========================================================================
+
+#define DN_ROWS 16
+
+__global__ void __launch_bounds__(256) k_down(ExpertSrc src, const float *__restrict__ act,
+                                              const int32_t *__restrict__ ids,
+                                              const float *__restrict__ wts, int k, int n_embd,
+                                              int n_ff, int down_type,
+                                              const float *__restrict__ resid,
+                                              float *__restrict__ y, int *err) {
+    extern __shared__ __align__(16) uint8_t smd[];
+    int8_t *aq = reinterpret_cast<int8_t *>(smd);                       // [k][n_ff]
+    float *ad = reinterpret_cast<float *>(smd + (size_t)k * n_ff);      // [k][n_ff/32]
+    float *as = ad + (size_t)k * (n_ff / 32);                           // [k][n_ff/32]
+    float *ys = as + (size_t)k * (n_ff / 32);                           // [k][DN_ROWS]
+    const int t = blockIdx.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const float *at = act + (size_t)t * k * n_ff;
+    for (int b = warp; b < k * (n_ff / 32); b += nw)
+        q8_block_warp(at[32 * b + lane], lane, aq + 32 * b, ad + b, as + b);
+    __syncthreads();
+    const int h0 = blockIdx.x * DN_ROWS;
+    const int nb = n_ff / MOE_QK;
+    for (int kk = warp; kk < k; kk += nw) {
+        const int id = ids[(size_t)t * k + kk];
+        if (id < 0 || id >= src.n_expert) {
+            if (lane == 0) atomicOr(err, MOE_DEV_ERR_INDEX);
+            for (int r = 0; r < DN_ROWS; ++r) if (lane == 0) ys[kk * DN_ROWS + r] = 0.0f;
+            continue;
+        }
+        const int32_t slot = src.table ? src.table[id] : src.ns;
+        const uint8_t *dbase = expert_base(src, 2, id, slot);
+        const int8_t *q = aq + (size_t)kk * n_ff;
+        const float *dq = ad + (size_t)kk * (n_ff / 32);
+        const float *sq = as + (size_t)kk * (n_ff / 32);
+        if (down_type == MOE_QT_Q6K) {
+            const size_t rb = (size_t)nb * MOE_Q6K_BYTES;
+            const int units = nb * 8;
+            const int u = lane;
+            ActQ6 a;
+            const bool active = u < units;
+            if (active) load_act_q6(a, q, dq, u >> 3, (u >> 2) & 1, u & 3);
+            for (int r = 0; r < DN_ROWS; ++r) {
+                const int h = h0 + r;
+                float v = 0.0f;
+                if (active && h < n_embd && dbase)
+                    v = q6k_unit_dot(dbase + h * rb + (u >> 3) * MOE_Q6K_BYTES, (u >> 2) & 1, u & 3, a);
+                v = warp_sum(v);
+                if (lane == 0) ys[kk * DN_ROWS + r] = v;
+            }
+        } else {
+            const size_t rb = (size_t)nb * MOE_Q4K_BYTES;
+            const int units = nb * 4;
+            const int u = lane;
+            ActQ4 a;
+            const bool active = u < units;
+            if (active) load_act_q4(a, q, dq, sq, u >> 2, u & 3);
+            for (int r = 0; r < DN_ROWS; ++r) {
+                const int h = h0 + r;
+                float v = 0.0f;
+                if (active && h < n_embd && dbase)
+                    v = q4k_unit_dot(dbase + h * rb + (u >> 2) * MOE_Q4K_BYTES, u & 3, a);
+                v = warp_sum(v);
+                if (lane == 0) ys[kk * DN_ROWS + r] = v;
+            }
+        }
+    }
+    __syncthreads();
+    for (int r = threadIdx.x; r < DN_ROWS; r += blockDim.x) {
+        const int h = h0 + r;
+        if (h >= n_embd) continue;
+        float acc = 0.0f;
+        for (int kk = 0; kk < k; ++kk) acc = __fmaf_rn(wts[(size_t)t * k + kk], ys[kk * DN_ROWS + r], acc);
+        if (resid) acc = __fadd_rn(acc, resid[(size_t)t * n_embd + h]);
+        y[(size_t)t * n_embd + h] = acc;
+    }
+}
+
+// ===========================================================================
+// slot table: observation of externally computed ids, and the cache step
+// ===========================================================================
+
+__global__ void k_observe(SlotState st, int layer, const int32_t *__restrict__ ids, int n) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) observe_layer(st, layer, ids, n);
+}
+
+// llama_moe_cache_step on the device (patches/0006:765-953 non-early path,
+// 0007:655-773 admission / probation / heat decay, 0008:613-627 deterministic
+// publication).  One CTA: thread 0 publishes (the clock order is global),
+// then one thread per layer schedules.  Jobs are also written to `host_jobs`
+// (mapped pinned memory) as (layer, expert, slot, spec) for the uploader.
+__global__ void __launch_bounds__(256) k_step(SlotState st, int32_t *host_jobs,
+                                              int32_t *host_njobs) {
+    __shared__ int s_dirty;
+    const int L = st.n_layers, E = st.n_expert, MI = st.max_inserts > 0 ? st.max_inserts : 1;
+    if (threadIdx.x == 0) {
+        s_dirty = 0;
+        uint64_t clock = st.g[G_CLOCK];
+        const uint64_t n_steps = st.g[G_STEPS];
+        uint64_t published = 0;
+        for (int l = 0; l < L; ++l) {
+            const int nj = st.n_jobs[l];
+            int32_t *jb = st.jobs + (size_t)l * MI * 4;
+            // deterministic publication: (layer, slot) order
+            for (int a = 1; a < nj; ++a) {
+                int32_t tmp[4] = {jb[4 * a], jb[4 * a + 1], jb[4 * a + 2], jb[4 * a + 3]};
+                int b = a - 1;
+                while (b >= 0 && jb[4 * b + 1] > tmp[1]) {
+                    for (int c = 0; c < 4; ++c) jb[4 * (b + 1) + c] = jb[4 * b + c];
+                    --b;
+                }
+                for (int c = 0; c < 4; ++c) jb[4 * (b + 1) + c] = tmp[c];
+            }
+            const int so = st.slot_off[l];
+            for (int a = 0; a < nj; ++a) {
+                const int e = jb[4 * a], slot = jb[4 * a + 1], spec = jb[4 * a + 2];
+                st.slot_expert[so + slot] = e;
+                st.table[(size_t)l * E + e] = slot;
+                if (spec && st.spec_probation) {
+                    st.last_use[so + slot] = 1;
+                    st.protect[so + slot] = n_steps + 1;
+                } else {
+                    st.last_use[so + slot] = ++clock;
+                }
+                st.in_flight[so + slot] = 0;
+                s_dirty = 1;
+                published++;
+            }
+            st.n_jobs[l] = 0;
+        }
+        st.g[G_CLOCK] = clock;
+        st.g[G_COPIED] += published;
+        st.g[G_PUBLISHED] += published;
+        st.g[G_STEPS] = n_steps + 1;
+        *host_njobs = 0;
+    }
+    __syncthreads();
+    const uint64_t n_steps = st.g[G_STEPS];
+    for (int l = threadIdx.x; l < L; l += blockDim.x) {
+        const int np = st.n_pending[l];
+        if (np == 0) continue;
+        const int ns = st.ns[l], so = st.slot_off[l];
+        int32_t *tbl = st.table + (size_t)l * E;
+        const int32_t *pend = st.pending + (size_t)l * E;
+        int budget = st.max_inserts;
+        int nj = 0;
+        uint64_t ok_n = 0, den_n = 0;
+        bool dirty = false;
+        for (int it = np - 1; it >= 0 && budget > 0; --it) {
+            const int id = pend[it];
+            if (tbl[id] != ns) {
+                --budget;
+                continue;
+            }
+            int slot = -1;
+            uint64_t best = ~0ull;
+            for (int s = 0; s < ns; ++s) {
+                if (st.in_flight[so + s]) continue;
+                if (st.slot_expert[so + s] < 0) { slot = s; break; }
+                if (st.protect[so + s] >= n_steps) continue;
+                if (st.last_use[so + s] < best) { best = st.last_use[so + s]; slot = s; }
+            }
+            if (slot < 0) break;
+            const int victim = st.slot_expert[so + slot];
+            // admit_ok (patches/0007:414-429)
+            bool ok = true;
+            if (st.admit_mode != 0 && victim >= 0) {
+                if (st.admit_mode == 1) {
+                    const float *ht = st.heat + (size_t)l * E;
+                    ok = ht[id] > __fadd_rn(__fmul_rn(ht[victim], 1.25f), st.admit_floor);
+                } else if (st.admit_mode == 2) {
+                    const uint64_t mp = st.miss_prev[(size_t)l * E + id];
+                    const uint64_t ml = st.miss_last[(size_t)l * E + id];
+                    ok = mp != ~0ull && ml - mp < (uint64_t)st.admit_window;
+                }
+                if (ok) ok_n++; else den_n++;
+            }
+            if (!ok) continue;
+            --budget;
+            if (victim >= 0) {
+                tbl[victim] = ns;
+                st.slot_expert[so + slot] = -1;
+                dirty = true;
+            }
+            st.in_flight[so + slot] = 1;
+            int32_t *jb = st.jobs + ((size_t)l * MI + nj) * 4;
+            jb[0] = id; jb[1] = slot; jb[2] = 0; jb[3] = 0;
+            nj++;
+        }
+        st.n_jobs[l] = nj;
+        st.n_pending[l] = 0;
+        if (nj) atomicAdd((unsigned long long *)&st.g[G_SCHEDULED], (unsigned long long)nj);
+        if (ok_n) atomicAdd((unsigned long long *)&st.g[G_ADMIT_OK], (unsigned long long)ok_n);
+        if (den_n) atomicAdd((unsigned long long *)&st.g[G_ADMIT_DENIED], (unsigned long long)den_n);
+        if (dirty) s_dirty = 1;
+    }
+    __syncthreads();
+    if (st.admit_mode == 1 && st.admit_half > 0 && n_steps % (uint64_t)st.admit_half == 0) {
+        for (int i = threadIdx.x; i < L * E; i += blockDim.x) st.heat[i] = __fmul_rn(st.heat[i], 0.5f);
+    }
+    if (threadIdx.x == 0) {
+        if (s_dirty && st.batch_tables) st.g[G_FLUSHES] += 1;
+        int n = 0;
+        for (int l = 0; l < L; ++l) {
+            for (int a = 0; a < st.n_jobs[l]; ++a) {
+                const int32_t *jb = st.jobs + ((size_t)l * MI + a) * 4;
+                host_jobs[4 * n + 0] = l;
+                host_jobs[4 * n + 1] = jb[0];
+                host_jobs[4 * n + 2] = jb[1];
+                host_jobs[4 * n + 3] = jb[2];
+                n++;
+            }
+        }
+        __threadfence_system();
+        *host_njobs = n;
+    }
+}
+
+// ===========================================================================
+// host-side launchers
+// ===========================================================================
+
+cudaError_t launch_quantize(const float *x, void *y, int64_t n, int qtype, cudaStream_t s) {
+    const int64_t nb = n / MOE_QK;
+    if (nb == 0) return cudaSuccess;
+    k_quantize<<<(unsigned)((nb + 127) / 128), 128, 0, s>>>(x, (uint8_t *)y, nb, qtype);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_synth_weights(void *y, int64_t nb, int qtype, uint64_t seed, float sigma,
+                                 cudaStream_t s) {
+    if (nb == 0) return cudaSuccess;
+    k_synth_weights<<<(unsigned)((nb + 127) / 128), 128, 0, s>>>((uint8_t *)y, nb, qtype, seed, sigma);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_synth_f32(float *y, int64_t n, uint64_t seed, float sigma, cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    const int64_t nt = (n + 1) / 2;
+    k_synth_f32<<<(unsigned)((nt + 255) / 256), 256, 0, s>>>(y, n, seed, sigma);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_router(const float *W, const float *x, int n_tok, int n_expert, int n_embd,
+                          const int32_t *table, int ns, float delta, int use_prior, int k,
+                          int32_t *ids, float *w, float *logits, const SlotState *st,
+                          int observe_layer_idx, cudaStream_t s) {
+    const size_t smem = sizeof(float) * ((size_t)n_embd + n_expert);
+    SlotState dummy{};
+    const int threads = n_expert >= 512 ? 512 : (n_expert < 32 ? 32 : n_expert);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(k_router, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    k_router<<<n_tok, threads, smem, s>>>(W, x, n_expert, n_embd, table, ns, delta, use_prior, k,
+                                          ids, w, logits, st ? *st : dummy,
+                                          st ? observe_layer_idx : -1);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_experts(const ExpertSrc &src, const float *x, const int32_t *ids,
+                           const float *w, int n_tok, int k, int n_embd, int n_ff, int down_type,
+                           float *act, const float *resid, float *y, int *err, cudaStream_t s) {
+    dim3 g1((n_ff + GU_ROWS - 1) / GU_ROWS, n_tok * k);
+    k_gate_up<<<g1, 256, 0, s>>>(src, x, ids, k, n_embd, n_ff, act, err);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const size_t smem = (size_t)k * n_ff + 2 * sizeof(float) * (size_t)k * (n_ff / 32) +
+                        sizeof(float) * (size_t)k * DN_ROWS + 16;
+    if (smem > 48 * 1024) {
+        e = cudaFuncSetAttribute(k_down, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    dim3 g2((n_embd + DN_ROWS - 1) / DN_ROWS, n_tok);
+    k_down<<<g2, 256, smem, s>>>(src, act, ids, w, k, n_embd, n_ff, down_type, resid, y, err);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_observe(const SlotState &st, int layer, const int32_t *ids, int n,
+                           cudaStream_t s) {
+    k_observe<<<1, 32, 0, s>>>(st, layer, ids, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_step(const SlotState &st, int32_t *host_jobs, int32_t *host_njobs,
+                        cudaStream_t s) {
+    k_step<<<1, 256, 0, s>>>(st, host_jobs, host_njobs);
+    return cudaGetLastError();
+}
+
+}  // namespace moe

@@ -1,0 +1,85 @@
+// moe_kernels.h -- internal declarations shared by the .cu files of
+// libmoeb200.so (not part of the public C ABI in include/moeb200.h).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "moe_dev.cuh"
+
+namespace moe {
+
+// Where one layer's experts live: slot slabs on the device (slot stride =
+// per-expert bytes; table[e] == ns means not resident) and the registered
+// host copies (expert stride), read zero-copy for misses.
+struct ExpertSrc {
+    const uint8_t *gate, *up, *down;      // device slabs [ns+1][...]
+    const uint8_t *hgate, *hup, *hdown;   // mapped host [n_expert][...] or null
+    const int32_t *table;                 // [n_expert] or null (= all host)
+    int64_t gate_bytes, down_bytes;
+    int32_t ns, n_expert;
+};
+
+cudaError_t launch_quantize(const float *x, void *y, int64_t n, int qtype, cudaStream_t s);
+cudaError_t launch_synth_weights(void *y, int64_t nb, int qtype, uint64_t seed, float sigma,
+                                 cudaStream_t s);
+cudaError_t launch_synth_f32(float *y, int64_t n, uint64_t seed, float sigma, cudaStream_t s);
+cudaError_t launch_router(const float *W, const float *x, int n_tok, int n_expert, int n_embd,
+                          const int32_t *table, int ns, float delta, int use_prior, int k,
+                          int32_t *ids, float *w, float *logits, const SlotState *st,
+                          int observe_layer_idx, cudaStream_t s);
+cudaError_t launch_experts(const ExpertSrc &src, const float *x, const int32_t *ids,
+                           const float *w, int n_tok, int k, int n_embd, int n_ff, int down_type,
+                           float *act, const float *resid, float *y, int *err, cudaStream_t s);
+cudaError_t launch_observe(const SlotState &st, int layer, const int32_t *ids, int n,
+                           cudaStream_t s);
+cudaError_t launch_step(const SlotState &st, int32_t *host_jobs, int32_t *host_njobs,
+                        cudaStream_t s);
+
+// ---- persistent decode (moe_decode.cu) ------------------------------------
+
+struct LayerDesc {
+    const float *router_w;                 // [E][H] device
+    const uint8_t *gate, *up, *down;       // slot slabs
+    const uint8_t *hgate, *hup, *hdown;    // mapped host or null
+    const int32_t *table;                  // [E]
+    int32_t ns;
+    int32_t pad_;
+};
+
+struct DecodeParams {
+    int n_layers, n_expert, k, n_embd, n_ff, down_type;
+    int64_t gate_bytes, down_bytes;        // per expert
+    const LayerDesc *layers;               // device [n_layers]
+    const int32_t *gu_r0, *gu_r1;          // per CTA: flattened (k, row) range
+    const int32_t *dn_h0, *dn_h1;          // per CTA: output-row range
+    int gu_rows_max, dn_rows_max;          // staging sizes
+    const float *h_in;                     // [n_tok][H]
+    float *out;                            // [n_tok][H]
+    int n_tok;
+    float *resid;                          // [H]  residual stream
+    float *logits;                         // [E]
+    float *act;                            // [k][I]
+    unsigned *bar;                         // grid barrier counter (zeroed per launch)
+    int *abort_flag;
+    int *err;
+    SlotState st;
+    int observe;
+    float delta;
+    float rms_eps;
+    float *dbg_x;                          // [n_tok][L][H] or null
+    int32_t *dbg_ids;                      // [n_tok][L][k]
+    float *dbg_w;
+    float *dbg_y;                          // [n_tok][L][H]
+    // shared-memory layout (bytes from the start of dynamic smem)
+    int off_xf, off_xq, off_xd, off_xs, off_aq, off_ad, off_as, off_rt, off_gu, off_dn, off_ys,
+        smem_bytes;
+    int dn_stride;                         // bytes per expert chunk in the down staging
+    int rt_rows;                           // router rows per CTA (ceil(E / grid))
+};
+
+int decode_smem_layout(DecodeParams &p, int grid);
+cudaError_t launch_decode(const DecodeParams &p, int grid, cudaStream_t s);
+int decode_max_grid(int smem_bytes, int device);
+
+}  // namespace moe

@@ -1,0 +1,306 @@
+"""MoeStack: the MoE layers of a Qwen3-A3B-class model with a GPU expert slot
+cache, driven through the C ABI of libmoeb200.so.
+
+This is the host side of the reference's ``--moe-expert-cache`` path: one
+object per device that owns the slot slabs, the device slot table and the
+router weights (llama_moe_cache_init, patches/0006:482-763), runs the MoE
+layer (build_moe_ffn with the cache chain, patches/0009:659-705) or a whole
+batch-1 decode, and advances the cache between tokens (llama_moe_cache_step,
+patches/0006:765-953).  PyTorch is used only for device/pinned buffers and
+streams; every computation is a CUDA kernel of libmoeb200.so.
+"""
+import ctypes as C
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import MoeCfg, MoeDecodeDbg, MoeLayerInfo, QTYPE_Q4_K, QTYPE_Q6_K, STAT_NAMES, check
+from .config import MoeCacheConfig
+
+Q4K_BYTES, Q6K_BYTES, QK_K = 144, 210, 256
+
+
+def expert_bytes(n_embd, n_ff, down_type=QTYPE_Q6_K):
+    """(gate = up bytes, down bytes) of one expert in ggml block layout."""
+    g = n_ff * (n_embd // QK_K) * Q4K_BYTES
+    d = n_embd * (n_ff // QK_K) * (Q6K_BYTES if down_type == QTYPE_Q6_K else Q4K_BYTES)
+    return g, d
+
+
+def _ptr(t):
+    if t is None:
+        return None
+    if isinstance(t, np.ndarray):
+        return t.ctypes.data_as(C.c_void_p)
+    return C.c_void_p(t.data_ptr())
+
+
+def _stream(stream=None):
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+class _CudaView:
+    """A raw device pointer exposed through __cuda_array_interface__, so
+    torch.as_tensor can view it without a copy."""
+
+    def __init__(self, ptr, nbytes):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1",
+                                         "data": (ptr, False), "version": 3}
+
+
+class MoeStack:
+    def __init__(self, n_layers, n_expert=128, n_used=8, n_embd=2048, n_ff=768,
+                 down_type=QTYPE_Q6_K, cache=None, device=0):
+        self.lib = _lib.load()
+        self.cache = cache or MoeCacheConfig()
+        self.n_layers, self.n_expert, self.n_used = n_layers, n_expert, n_used
+        self.n_embd, self.n_ff, self.down_type = n_embd, n_ff, down_type
+        self.device = torch.device("cuda", device)
+        self.gate_bytes, self.down_bytes = expert_bytes(n_embd, n_ff, down_type)
+        self.ns = self.cache.slots_per_layer(n_layers, n_expert)
+        self._profile = np.ascontiguousarray(self.ns, np.int32)
+        cfg = MoeCfg(n_layers, n_expert, n_used, n_embd, n_ff, down_type,
+                     self.cache.n_slots if self.cache.n_slots > 0 else n_expert,
+                     self._profile.ctypes.data, self.cache.max_inserts, self.cache.admit_mode,
+                     self.cache.admit_window, self.cache.admit_half, self.cache.admit_floor,
+                     int(self.cache.spec_probation), int(self.cache.batch_tables),
+                     self.cache.cache_prior, int(self.cache.early_issue),
+                     int(self.cache.freeze), int(bool(self.cache.heat_file)), device)
+        torch.cuda.set_device(self.device)
+        ctx = C.c_void_p()
+        check(self.lib.moe_create(C.byref(cfg), C.byref(ctx)), None, "moe_create")
+        self.ctx = ctx
+        self._host = {}          # keep registered host weights alive
+
+    # -- lifetime -------------------------------------------------------------
+    def close(self):
+        if getattr(self, "ctx", None):
+            self.lib.moe_destroy(self.ctx)
+            self.ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _ck(self, rc, what):
+        return check(rc, self.ctx, what)
+
+    # -- weights --------------------------------------------------------------
+    def layer_info(self, layer):
+        info = MoeLayerInfo()
+        self._ck(self.lib.moe_get_layer(self.ctx, layer, C.byref(info)), "moe_get_layer")
+        return info
+
+    def slot_views(self, layer):
+        """torch uint8 views of the layer's gate/up/down slot slabs
+        [n_slots + 1, bytes]."""
+        info = self.layer_info(layer)
+        n = info.n_slots + 1
+        g = torch.as_tensor(_CudaView(info.gate_c, n * self.gate_bytes), device=self.device)
+        u = torch.as_tensor(_CudaView(info.up_c, n * self.gate_bytes), device=self.device)
+        d = torch.as_tensor(_CudaView(info.down_c, n * self.down_bytes), device=self.device)
+        return g.view(n, -1), u.view(n, -1), d.view(n, -1)
+
+    def set_router(self, layer, w):
+        w = w.contiguous().float()
+        self._ck(self.lib.moe_set_router(self.ctx, layer, _ptr(w)), "moe_set_router")
+
+    def set_expert_weights(self, layer, gate, up, down):
+        """Host copies of all experts of a layer (uint8, ggml layout), kept
+        alive by this object; registered (pinned, mapped) by the library."""
+        self._host[layer] = (gate, up, down)
+        self._ck(self.lib.moe_set_expert_weights(self.ctx, layer, _ptr(gate), _ptr(up), _ptr(down)),
+                 "moe_set_expert_weights")
+
+    def place(self, layer, slot_expert, copy=True):
+        se = np.ascontiguousarray(slot_expert, np.int32)
+        self._ck(self.lib.moe_place(self.ctx, layer, _ptr(se), int(copy)), "moe_place")
+
+    def synth_resident(self, seed=0, sigma=0.02, router_sigma=0.02, keep_router=False):
+        """Every layer: synthetic N(0, sigma^2) experts generated on the device
+        straight into slots 0..n_expert-1 (needs n_slots >= n_expert) and an
+        fp32 N(0, router_sigma^2) router; experts placed identity.  With
+        keep_router the router tensors stay in self.routers."""
+        self.routers = [] if keep_router else None
+        for il in range(self.n_layers):
+            if self.ns[il] < self.n_expert:
+                raise ValueError("synth_resident needs n_slots >= n_expert")
+            info = self.layer_info(il)
+            nbg = self.n_expert * self.gate_bytes // Q4K_BYTES
+            nbd = self.n_expert * self.down_bytes // (Q6K_BYTES if self.down_type == QTYPE_Q6_K
+                                                      else Q4K_BYTES)
+            s = _stream()
+            base = (seed + 1000 * il) & 0xFFFFFFFF
+            self._ck(self.lib.moe_synth_weights(info.gate_c, nbg, QTYPE_Q4_K, base + 0, sigma, s), "synth")
+            self._ck(self.lib.moe_synth_weights(info.up_c, nbg, QTYPE_Q4_K, base + 1, sigma, s), "synth")
+            self._ck(self.lib.moe_synth_weights(info.down_c, nbd, self.down_type, base + 2, sigma, s),
+                     "synth")
+            r = torch.empty(self.n_expert, self.n_embd, device=self.device)
+            self._ck(self.lib.moe_synth_f32(_ptr(r), r.numel(), base + 3, router_sigma, s), "synth")
+            torch.cuda.synchronize(self.device)
+            self.set_router(il, r)
+            if keep_router:
+                self.routers.append(r)
+            se = list(range(self.n_expert)) + [-1] * (self.ns[il] - self.n_expert)
+            self.place(il, se, copy=False)
+
+    # -- hot path -------------------------------------------------------------
+    def layer_forward(self, layer, x, stream=None):
+        """x [n_tok, n_embd] fp32 (device) -> (y, ids, w)."""
+        x = x.contiguous()
+        n_tok = x.shape[0]
+        y = torch.empty_like(x)
+        ids = torch.empty(n_tok, self.n_used, dtype=torch.int32, device=x.device)
+        w = torch.empty(n_tok, self.n_used, dtype=torch.float32, device=x.device)
+        self._ck(self.lib.moe_layer_forward(self.ctx, layer, _ptr(x), _ptr(y), n_tok, _ptr(ids),
+                                            _ptr(w), _stream(stream)), "moe_layer_forward")
+        return y, ids, w
+
+    def decode(self, h, out=None, debug=False, stream=None):
+        """Batch-1 decode of h [n_tok, n_embd] (device) through every layer,
+        one token after another; returns out (and the per-layer dumps when
+        debug)."""
+        h = h.contiguous()
+        n_tok = h.shape[0]
+        out = torch.empty_like(h) if out is None else out
+        dbg = None
+        dumps = None
+        if debug:
+            L, K, H = self.n_layers, self.n_used, self.n_embd
+            dumps = {
+                "x": torch.empty(n_tok, L, H, device=h.device),
+                "ids": torch.empty(n_tok, L, K, dtype=torch.int32, device=h.device),
+                "w": torch.empty(n_tok, L, K, device=h.device),
+                "y": torch.empty(n_tok, L, H, device=h.device),
+            }
+            dbg = MoeDecodeDbg(dumps["x"].data_ptr(), dumps["ids"].data_ptr(),
+                               dumps["w"].data_ptr(), dumps["y"].data_ptr())
+        self._ck(self.lib.moe_decode(self.ctx, _ptr(h), _ptr(out), n_tok,
+                                     C.byref(dbg) if dbg is not None else None, _stream(stream)),
+                 "moe_decode")
+        return (out, dumps) if debug else out
+
+    def decode_host(self, h_host, out_host, stream=None):
+        """End to end: pinned host h -> device -> decode -> host out."""
+        n_tok = h_host.shape[0]
+        self._ck(self.lib.moe_decode_host(self.ctx, _ptr(h_host), _ptr(out_host), n_tok,
+                                          _stream(stream)), "moe_decode_host")
+        return out_host
+
+    def sync(self, stream=None):
+        self._ck(self.lib.moe_sync(self.ctx, _stream(stream)), "moe_sync")
+
+    def decode_info(self):
+        out = np.zeros(5, np.int32)
+        self._ck(self.lib.moe_decode_info(self.ctx, _ptr(out), 5), "moe_decode_info")
+        return dict(zip(["grid", "smem_bytes", "gu_rows_max", "dn_rows_max", "threads"],
+                        (int(v) for v in out)))
+
+    # -- slot cache -----------------------------------------------------------
+    def observe(self, layer, ids, stream=None):
+        ids = ids.contiguous().to(torch.int32)
+        ids2 = ids.view(1, -1) if ids.dim() == 1 else ids
+        self._ck(self.lib.moe_observe(self.ctx, layer, _ptr(ids2), ids2.shape[0], ids2.shape[1],
+                                      _stream(stream)), "moe_observe")
+
+    def step(self, stream=None):
+        self._ck(self.lib.moe_step(self.ctx, _stream(stream)), "moe_step")
+
+    def tables(self, layer):
+        ns = self.ns[layer]
+        es = np.empty(self.n_expert, np.int32)
+        se = np.empty(ns, np.int32)
+        lu = np.empty(ns, np.uint64)
+        fl = np.empty(ns, np.uint8)
+        pr = np.empty(ns, np.uint64)
+        self._ck(self.lib.moe_get_tables(self.ctx, layer, _ptr(es), _ptr(se), _ptr(lu), _ptr(fl),
+                                         _ptr(pr)), "moe_get_tables")
+        return {"expert_slot": es, "slot_expert": se, "last_use": lu, "in_flight": fl,
+                "protect": pr}
+
+    def gate_state(self, layer):
+        E = self.n_expert
+        heat = np.zeros(E, np.float32)
+        ml = np.zeros(E, np.uint64)
+        mp = np.zeros(E, np.uint64)
+        uc = np.zeros(E, np.uint32)
+        self._ck(self.lib.moe_get_gate_state(self.ctx, layer, _ptr(heat), _ptr(ml), _ptr(mp),
+                                             _ptr(uc)), "moe_get_gate_state")
+        return {"heat": heat, "miss_last": ml, "miss_prev": mp, "use_count": uc}
+
+    def stats(self):
+        out = np.zeros(len(STAT_NAMES), np.uint64)
+        self._ck(self.lib.moe_get_stats(self.ctx, _ptr(out), len(STAT_NAMES)), "moe_get_stats")
+        return {k: int(v) for k, v in zip(STAT_NAMES, out)}
+
+    def warm_start(self, use_count):
+        uc = np.ascontiguousarray(use_count, np.uint32)
+        return self._ck(self.lib.moe_warm_start(self.ctx, _ptr(uc)), "moe_warm_start")
+
+    # -- diagnostics in the reference's text formats ----------------------------
+    def map_header(self):
+        """"moe-map 1" header (patches/0008:417-433)."""
+        lines = [f"moe-map 1 {self.n_layers}"]
+        lines += [f"layer {il} {self.ns[il]} {self.n_expert}" for il in range(self.n_layers)]
+        return "\n".join(lines) + "\n"
+
+    def map_frame(self, n_steps=None):
+        """One "step / map" frame of the published placement (patches/0008:476-488)."""
+        if n_steps is None:
+            n_steps = self.stats()["steps"]
+        lines = [f"step {n_steps}"]
+        for il in range(self.n_layers):
+            es = self.tables(il)["expert_slot"]
+            pub = [-1] * self.ns[il]
+            for e, s in enumerate(es):
+                if s >= 0:
+                    pub[s] = e
+            lines.append("map %d" % il + "".join(f" {e}" for e in pub))
+        return "\n".join(lines) + "\n"
+
+
+def load_heat(path, n_layers, n_expert):
+    """Parse a "moe-heat 1 <layers> <experts>" file (patches/0007:431-466):
+    counts halved on load; refused (None) when the dimensions differ."""
+    try:
+        with open(path) as f:
+            toks = f.read().split()
+    except OSError:
+        return None
+    if len(toks) < 4 or toks[0] != "moe-heat":
+        return None
+    try:
+        ver, nl, ne = int(toks[1]), int(toks[2]), int(toks[3])
+    except ValueError:
+        return None
+    if ver != 1 or nl != n_layers or ne != n_expert:
+        return None
+    out = np.zeros((n_layers, n_expert), np.uint32)
+    rest = toks[4:]
+    for i in range(0, len(rest) - 2, 3):
+        try:
+            il, e, c = int(rest[i]), int(rest[i + 1]), int(rest[i + 2])
+        except ValueError:
+            break
+        if 0 <= il < n_layers and 0 <= e < n_expert:
+            out[il, e] = c // 2
+    return out
+
+
+def save_heat(path, counts):
+    """Write counts [layers, experts] as "moe-heat 1" via temp + rename
+    (patches/0007:468-485)."""
+    import os
+    counts = np.asarray(counts)
+    tmp = path + ".tmp"
+    with open(tmp, "w") as f:
+        f.write(f"moe-heat 1 {counts.shape[0]} {counts.shape[1]}\n")
+        for il in range(counts.shape[0]):
+            for e in range(counts.shape[1]):
+                if counts[il, e]:
+                    f.write(f"{il} {e} {int(counts[il, e])}\n")
+    os.replace(tmp, path)

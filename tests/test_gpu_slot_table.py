@@ -1,0 +1,159 @@
+"""Device slot table vs the oracle's restatement of llama-moecache.cpp
+(patches 0006/0007/0008): tables, recency, in-flight flags, admission
+decisions and counters bit-exact after every step; uploaded slot bytes equal
+the host expert bytes the table says they hold."""
+import numpy as np
+import pytest
+
+from conftest import ar1_states
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+H = 2048
+
+
+def _needs_gpu():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+def _trace(n_tok, n_layers, n_expert, k, seed, keep=5):
+    """Routing with locality: each layer keeps most of the previous token's
+    experts and draws the rest from a skewed distribution."""
+    rng = np.random.default_rng(seed)
+    pop = rng.permutation(n_expert)
+    p = 1.0 / np.arange(1, n_expert + 1) ** 1.1
+    p /= p.sum()
+    prev = [list(rng.choice(n_expert, k, replace=False)) for _ in range(n_layers)]
+    out = np.zeros((n_tok, n_layers, k), np.int32)
+    for t in range(n_tok):
+        for L in range(n_layers):
+            cur = list(rng.permutation(prev[L])[:keep])
+            while len(cur) < k:
+                e = int(pop[rng.choice(n_expert, p=p)])
+                if e not in cur:
+                    cur.append(e)
+            rng.shuffle(cur)
+            out[t, L] = cur
+            prev[L] = cur
+    return out
+
+
+def _compare(st, oc, n_layers, ctx=""):
+    for L in range(n_layers):
+        d = st.tables(L)
+        o = oc.tables(L)
+        for key in ("expert_slot", "slot_expert", "last_use", "in_flight", "protect"):
+            assert np.array_equal(d[key], o[key]), f"{ctx} layer {L} {key}:\n{d[key]}\n{o[key]}"
+        gd, go = st.gate_state(L), oc.gate_state(L)
+        for key in ("heat", "miss_last", "miss_prev"):
+            assert np.array_equal(gd[key], go[key]), f"{ctx} layer {L} {key}"
+    sd, so = st.stats(), oc.stats()
+    for key in ("steps", "clock", "hits", "misses", "scheduled", "copied", "published",
+                "admit_ok", "admit_denied", "table_flushes"):
+        assert sd[key] == so[key], f"{ctx} stat {key}: {sd[key]} vs {so[key]}"
+
+
+def _host_weights(n_expert, gate_bytes, down_bytes, seed):
+    rng = np.random.default_rng(seed)
+    mk = lambda n: torch.from_numpy(rng.integers(0, 256, n, dtype=np.uint8)).pin_memory()
+    return mk(n_expert * gate_bytes), mk(n_expert * gate_bytes), mk(n_expert * down_bytes)
+
+
+@pytest.mark.parametrize("admit,max_inserts,batch,profile", [
+    ("off", 2, True, None),
+    ("window", 2, True, [6, 8, 12]),
+    ("heat", 3, False, None),
+    ("window", 1, False, [8, 5, 8]),
+])
+def test_slot_table_matches_oracle(oracle_lib, admit, max_inserts, batch, profile):
+    _needs_gpu()
+    from moe_prefetch_b200 import MoeCacheConfig, MoeStack, format_slot_profile
+    L, E, k, n_ff = 3, 32, 8, 256
+    cfg = MoeCacheConfig(n_slots=10, max_inserts=max_inserts, admit=admit,
+                         batch_tables=batch, admit_half=16,
+                         slot_profile=format_slot_profile(profile) if profile else "")
+    st = MoeStack(n_layers=L, n_expert=E, n_used=k, n_ff=n_ff, cache=cfg)
+    hw = [_host_weights(E, st.gate_bytes, st.down_bytes, s) for s in range(L)]
+    for il in range(L):
+        st.set_expert_weights(il, *hw[il])
+    oc = oracle_lib.OracleCache(L, E, 10, slot_profile=st.ns, max_inserts=max_inserts,
+                                admit_mode=cfg.admit_mode, admit_window=cfg.admit_window,
+                                admit_half=16, admit_floor=cfg.admit_floor,
+                                batch_tables=batch)
+    tr = _trace(40, L, E, k, seed=hash((admit, max_inserts)) & 0xFFFF)
+    for t in range(tr.shape[0]):
+        for il in range(L):
+            ids = torch.from_numpy(tr[t, il]).cuda()
+            st.observe(il, ids)
+            oc.observe(il, tr[t, il])
+        st.step()
+        oc.step()
+        _compare(st, oc, L, f"token {t}")
+    # every published slot holds the bytes of its expert
+    st.step(); oc.step()
+    torch.cuda.synchronize()
+    for il in range(L):
+        g, u, d = st.slot_views(il)
+        se = st.tables(il)["slot_expert"]
+        hg, hu, hd = (x.numpy() for x in hw[il])
+        for s, e in enumerate(se):
+            if e < 0:
+                continue
+            assert np.array_equal(g[s].cpu().numpy(), hg[e * st.gate_bytes:(e + 1) * st.gate_bytes])
+            assert np.array_equal(d[s].cpu().numpy(), hd[e * st.down_bytes:(e + 1) * st.down_bytes])
+    st.close()
+
+
+def test_decode_with_cache_end_to_end(oracle_lib):
+    """Config-2 flow at small scale: batch-1 decode token by token with
+    misses served zero-copy, second-miss admission, uploads on the copy
+    stream and deterministic publication; the device tables after every
+    step equal the oracle's, fed the same routed ids, and every layer output
+    is within tolerance of the oracle's."""
+    _needs_gpu()
+    from conftest import MAX_ABS_TOL, REL_L2_TOL, rel_l2
+    from moe_prefetch_b200 import MoeCacheConfig, MoeStack
+    L, E, k = 2, 128, 8
+    # weights: generate resident on a helper stack, then host copies
+    src = MoeStack(n_layers=L)
+    src.synth_resident(seed=33, keep_router=True)
+    host = []
+    for il in range(L):
+        g, u, d = src.slot_views(il)
+        host.append(tuple(v[:E].contiguous().cpu().pin_memory() for v in (g, u, d)))
+    routers = [r.clone() for r in src.routers]
+    src.close()
+    torch.cuda.synchronize()
+    cfg = MoeCacheConfig(n_slots=24, max_inserts=2, admit="window", batch_tables=True,
+                         cache_prior=0.01)
+    st = MoeStack(n_layers=L, cache=cfg)
+    for il in range(L):
+        st.set_router(il, routers[il])
+        st.set_expert_weights(il, *host[il])
+    oc = oracle_lib.OracleCache(L, E, 24, max_inserts=2, admit_mode=2, batch_tables=True,
+                                cache_prior=0.01)
+    h = ar1_states(24, H, seed=2)
+    for t in range(h.shape[0]):
+        # the router's prior must see the oracle's published table
+        out, dm = st.decode(torch.from_numpy(h[t:t + 1]).cuda(), debug=True)
+        st.sync()
+        xs, ids, ws, ys = (dm[q].cpu().numpy()[0] for q in ("x", "ids", "w", "y"))
+        for il in range(L):
+            tbl, prior = oc.dev_table(il)
+            W = routers[il].cpu().numpy()
+            gate, up, down = (x.numpy().reshape(E, -1) for x in host[il])
+            rids, rw, ry = oracle_lib.moe_layer(xs[il:il + 1], W, gate, up, down, 14, 768, k,
+                                                prior=prior)
+            assert np.array_equal(ids[il], rids[0]), f"token {t} layer {il}"
+            assert np.array_equal(ws[il].view(np.uint32), rw[0].view(np.uint32))
+            assert rel_l2(ys[il], ry[0]) <= REL_L2_TOL
+            assert np.abs(ys[il] - ry[0]).max() <= MAX_ABS_TOL
+            oc.observe(il, ids[il])
+        st.step()
+        oc.step()
+        _compare(st, oc, L, f"token {t}")
+    s = st.stats()
+    assert s["misses"] > 0 and s["scheduled"] > 0 and s["published"] > 0
+    st.close()
