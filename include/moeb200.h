@@ -49,7 +49,7 @@ typedef struct moe_ctx moe_ctx;
  * 0007:492-506, 0008:536-573). */
 typedef struct moe_cfg {
     int32_t n_layers;          /* MoE layers in the stack                          */
-    int32_t n_expert;          /* routed experts per layer (multiple of 32, <=256) */
+    int32_t n_expert;          /* routed experts per layer: 32, 64, 128 or 256     */
     int32_t n_used;            /* experts per token (top-k, <= 8)                  */
     int32_t n_embd;            /* hidden size (2048 in this build)                 */
     int32_t n_ff;              /* expert intermediate size (multiple of 256)       */
@@ -153,12 +153,16 @@ int moe_layer_forward(moe_ctx *ctx, int layer, const float *x, float *y, int n_t
 
 /* Optional per-(token, layer) dumps of the decode stack, device pointers or NULL:
  * x [n_tok][n_layers][n_embd] (router input), ids/w [n_tok][n_layers][n_used],
- * y [n_tok][n_layers][n_embd] (the layer's MoE output). */
+ * y [n_tok][n_layers][n_embd] (the layer's MoE output), and phase timestamps
+ * prof [n_tok][n_layers][MOE_DECODE_PHASES][grid] (%globaltimer ns, one per CTA
+ * at each phase boundary). */
+#define MOE_DECODE_PHASES 12
 typedef struct moe_decode_dbg {
-    float   *x;
-    int32_t *ids;
-    float   *w;
-    float   *y;
+    float    *x;
+    int32_t  *ids;
+    float    *w;
+    float    *y;
+    uint64_t *prof;
 } moe_decode_dbg;
 
 /* Batch-1 decode of n_tok tokens, strictly one after another, through all

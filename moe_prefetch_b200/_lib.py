@@ -46,7 +46,8 @@ class MoeLayerInfo(C.Structure):
 
 
 class MoeDecodeDbg(C.Structure):
-    _fields_ = [("x", C.c_void_p), ("ids", C.c_void_p), ("w", C.c_void_p), ("y", C.c_void_p)]
+    _fields_ = [("x", C.c_void_p), ("ids", C.c_void_p), ("w", C.c_void_p), ("y", C.c_void_p),
+                ("prof", C.c_void_p)]
 
 
 P = C.c_void_p

@@ -36,6 +36,7 @@ struct moe_ctx {
     int64_t gate_bytes = 0, down_bytes = 0;
     std::vector<LayerMem> L;
     float *router = nullptr;           // [L][E][H]
+    float *router_t = nullptr;         // [L][H][E]
     // slot state (device)
     void *state_mem = nullptr;
     SlotState st{};
@@ -46,6 +47,7 @@ struct moe_ctx {
     int grid = 0;
     DecodeParams dp{};
     float *resid = nullptr, *logits = nullptr, *act = nullptr;
+    float *part_p = nullptr, *part_s = nullptr;
     unsigned *bar = nullptr;
     int *abort_flag = nullptr, *err = nullptr;
     // scratch for moe_layer_forward / moe_decode_host
@@ -109,7 +111,8 @@ extern "C" int moe_create(const moe_cfg *cfg, moe_ctx **out) {
     };
     if (g.n_layers <= 0 || g.n_expert <= 0 || g.n_used <= 0 || g.n_embd <= 0 || g.n_ff <= 0)
         return bad(MOE_ERR_ARG, "non-positive shape");
-    if (g.n_expert % 32 || g.n_expert > 256) return bad(MOE_ERR_UNSUPPORTED, "n_expert must be a multiple of 32, <= 256");
+    if (g.n_expert != 32 && g.n_expert != 64 && g.n_expert != 128 && g.n_expert != 256)
+        return bad(MOE_ERR_UNSUPPORTED, "n_expert must be 32, 64, 128 or 256");
     if (g.n_used > 8 || g.n_used > g.n_expert) return bad(MOE_ERR_UNSUPPORTED, "n_used must be <= 8");
     if (g.n_embd != 2048) return bad(MOE_ERR_UNSUPPORTED, "n_embd must be 2048 in this build");
     if (g.n_ff % 256 || g.n_ff > 1024) return bad(MOE_ERR_UNSUPPORTED, "n_ff must be a multiple of 256, <= 1024");
@@ -161,6 +164,8 @@ extern "C" int moe_create(const moe_cfg *cfg, moe_ctx **out) {
     }
     if (cudaMalloc(&c->router, sizeof(float) * (size_t)L * E * H) != cudaSuccess) return cleanup_fail(MOE_ERR_OOM);
     cudaMemset(c->router, 0, sizeof(float) * (size_t)L * E * H);
+    if (cudaMalloc(&c->router_t, sizeof(float) * (size_t)L * E * H) != cudaSuccess) return cleanup_fail(MOE_ERR_OOM);
+    cudaMemset(c->router_t, 0, sizeof(float) * (size_t)L * E * H);
     // slot state
     {
         const size_t LE = (size_t)L * E, S = (size_t)c->sum_ns, MI = (size_t)g.max_inserts > 0 ? g.max_inserts : 1;
@@ -229,7 +234,9 @@ extern "C" int moe_create(const moe_cfg *cfg, moe_ctx **out) {
     {
         int dev_sms = 0;
         cudaDeviceGetAttribute(&dev_sms, cudaDevAttrMultiProcessorCount, g.device);
-        const int G = dev_sms > 0 ? dev_sms : 1;
+        // one CTA per SM; the partial-logit reduction reads at most 10 CTAs
+        // per warp group, so at most 160 CTAs
+        const int G = dev_sms > 0 ? std::min(dev_sms, 160) : 1;
         std::vector<int32_t> part(4 * (size_t)G);
         const int64_t R = (int64_t)K * I;
         int gmax = 0, dmax = 0;
@@ -254,12 +261,15 @@ extern "C" int moe_create(const moe_cfg *cfg, moe_ctx **out) {
         p.layers = c->d_layers;
         if (cudaMalloc(&c->resid, sizeof(float) * H) != cudaSuccess ||
             cudaMalloc(&c->logits, sizeof(float) * 256) != cudaSuccess ||
+            cudaMalloc(&c->part_p, sizeof(float) * (size_t)G * E) != cudaSuccess ||
+            cudaMalloc(&c->part_s, sizeof(float) * (size_t)G) != cudaSuccess ||
             cudaMalloc(&c->act, sizeof(float) * (size_t)MOE_KMAX * I) != cudaSuccess ||
             cudaMalloc(&c->bar, 64) != cudaSuccess || cudaMalloc(&c->abort_flag, 64) != cudaSuccess ||
             cudaMalloc(&c->err, 64) != cudaSuccess)
             return cleanup_fail(MOE_ERR_OOM);
         cudaMemset(c->err, 0, 64);
         p.resid = c->resid; p.logits = c->logits; p.act = c->act; p.bar = c->bar;
+        p.part_p = c->part_p; p.part_s = c->part_s;
         p.abort_flag = c->abort_flag; p.err = c->err; p.st = c->st;
         p.observe = 1; p.delta = g.cache_prior; p.rms_eps = 1e-6f;
     }
@@ -292,6 +302,9 @@ extern "C" void moe_destroy(moe_ctx *c) {
         }
     }
     cudaFree(c->router);
+    cudaFree(c->router_t);
+    cudaFree(c->part_p);
+    cudaFree(c->part_s);
     cudaFree(c->state_mem);
     cudaFree(c->d_layers);
     cudaFree(c->d_part);
@@ -336,6 +349,7 @@ static int refresh_layer_desc(moe_ctx *c, int layer) {
     LayerMem &m = c->L[layer];
     LayerDesc d{};
     d.router_w = c->router + (size_t)layer * c->cfg.n_expert * c->cfg.n_embd;
+    d.router_t = c->router_t + (size_t)layer * c->cfg.n_expert * c->cfg.n_embd;
     d.gate = m.gate; d.up = m.up; d.down = m.down;
     d.hgate = m.hgate; d.hup = m.hup; d.hdown = m.hdown;
     d.table = c->st.table + (size_t)layer * c->cfg.n_expert;
@@ -349,6 +363,9 @@ extern "C" int moe_set_router(moe_ctx *c, int layer, const float *w) {
     CK(cudaSetDevice(c->cfg.device));
     const size_t n = (size_t)c->cfg.n_expert * c->cfg.n_embd;
     CK(cudaMemcpy(c->router + (size_t)layer * n, w, n * sizeof(float), cudaMemcpyDefault));
+    CK(launch_transpose(c->router + (size_t)layer * n, c->router_t + (size_t)layer * n,
+                        c->cfg.n_expert, c->cfg.n_embd, 0));
+    CK(cudaDeviceSynchronize());
     return refresh_layer_desc(c, layer);
 }
 
@@ -506,6 +523,7 @@ extern "C" int moe_decode(moe_ctx *c, const float *h, float *out, int n_tok,
     p.dbg_ids = dbg ? dbg->ids : nullptr;
     p.dbg_w = dbg ? dbg->w : nullptr;
     p.dbg_y = dbg ? dbg->y : nullptr;
+    p.prof = dbg ? dbg->prof : nullptr;
     if (p.dbg_ids && !p.dbg_w) return fail(c, MOE_ERR_ARG, "moe_decode: dbg ids without w");
     CK(cudaMemsetAsync(c->bar, 0, 64, s));
     CK(cudaMemsetAsync(c->abort_flag, 0, 64, s));

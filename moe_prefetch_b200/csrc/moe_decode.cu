@@ -1,27 +1,39 @@
 // moe_decode.cu -- persistent batch-1 decode over the whole MoE stack.
 //
-// One cooperative launch, one CTA per SM, 16 warps.  For each token and
-// layer every CTA:
-//   1. reads the residual (L2), RMS-normalises it into shared memory;
-//   2. computes its share of the router logits from router rows that were
-//      bulk-copied into shared memory during the previous layer;
-//   -- grid barrier (logits complete) --
-//   3. selects top-k redundantly (canonical order -> every CTA gets the same
-//      ids), resolves slots through the device table, and issues ONE bulk
-//      copy (cp.async.bulk, TMA, no multicast) per contiguous piece of its
-//      static share of the layer's expert bytes: gate/up rows of the
-//      (expert, row) range it owns and the down rows of its output rows for
-//      all k experts, plus the next layer's router rows;
-//   4. computes gate/up GEMVs (Q4_K x Q8_1, dp4a) with SiLU*mul as each
-//      piece lands, writes the activations to L2;
-//   -- grid barrier (activations complete) --
-//   5. re-quantises the k activation vectors (Q8_1) in shared memory;
-//   6. computes the down GEMV rows (Q6_K x Q8_1) for all k experts, combines
-//      them with the routing weights, adds the residual;
-//   -- grid barrier (residual complete) at the start of the next layer --
-// Every wait (grid barrier, mbarrier) is bounded by %globaltimer; on expiry
-// the kernel raises an error bit and an abort flag, waits (bounded) for its
-// own copies in flight, and returns.
+// One cooperative launch, one CTA per SM, 16 warps; two grid barriers per
+// layer.  CTA c owns rows [h0, h1) of the residual stream for the whole
+// token and, inside every layer, the flattened (expert, row) range
+// [r0, r1) of the gate/up work.  Per token t and layer L:
+//
+//   -- grid barrier A: partial logits / partial sums of squares of (t, L)
+//      and the residual rows are complete --
+//   1. every CTA reads the full residual (L2) and the G partial logit
+//      vectors, reduces them in a fixed order (so every CTA gets the same
+//      bits) into RMSNorm-scaled logits, normalises x = r * inv_rms, and
+//      quantises x to Q8_1 in shared memory;
+//   2. softmax, + cache prior from the layer's table row (prefetched into
+//      shared memory), top-k by rank (all threads), renormalised weights;
+//      slots from the table; the routed ids are observed (moe_obs_cb) by
+//      CTA 0 with its counters cached on chip;
+//   3. warp 0 issues, lane-parallel, one bulk copy (cp.async.bulk, TMA, no
+//      multicast) per contiguous piece of this CTA's share of the layer's
+//      expert bytes -- gate/up rows of its (expert, row) range and the down
+//      rows of its residual rows for all k experts -- plus the next layer's
+//      transposed router rows for its residual rows and the next table row;
+//   4. gate/up GEMV (Q4_K x Q8_1, dp4a) with SiLU*mul as pieces land;
+//      activations to L2;
+//   -- grid barrier B: activations complete --
+//   5. the k activation vectors are re-quantised (Q8_1) in shared memory;
+//   6. down GEMV rows (Q6_K x Q8_1) of its residual rows for all k experts,
+//      weighted combine, residual add; the new rows go to L2, and the partial
+//      logits / sum of squares of the NEXT layer over these rows are
+//      computed on the spot from the prefetched router rows.
+//
+// Missed experts (table entry = n_slots) are read zero-copy from the
+// registered host weights instead of the slot slabs.  Every wait (grid
+// barrier, mbarrier) is bounded by %globaltimer; on expiry the kernel raises
+// an error bit and an abort flag, waits (bounded) for its own copies in
+// flight, and returns.
 #include "moe_kernels.h"
 
 #include <algorithm>
@@ -30,18 +42,26 @@ namespace moe {
 
 #define DEC_THREADS 512
 #define DEC_WARPS (DEC_THREADS / 32)
-#define MB_RT 0
-#define MB_GU 1    // 4 barriers: gate/up pieces
-#define MB_DN 5    // MOE_KMAX barriers: down pieces
+#define MB_WT 0
+#define MB_TBL 1
+#define MB_GU 2    // 4 barriers: gate/up pieces
+#define MB_DN 6    // MOE_KMAX barriers: down pieces
 #define N_MB (MB_DN + MOE_KMAX)
+#define DEC_PHASES 12
 
+__device__ __forceinline__ void red_release_add(unsigned *p, unsigned v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Grid barrier: every CTA adds 1 (release) and waits (acquire) until the
+// counter reaches epoch * gridDim.x.  Bounded by MOE_TIMEOUT_NS; gives up on
+// the shared abort flag.
 __device__ __forceinline__ bool grid_sync(const DecodeParams &p, unsigned &epoch, int *s_flag) {
     epoch += 1;
     const unsigned target = epoch * gridDim.x;
     __syncthreads();
     if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(p.bar, 1u);
+        red_release_add(p.bar, 1u);
         int ok = 1;
         if (ld_acquire_u32(p.bar) < target) {
             const uint64_t t0 = gtimer();
@@ -55,7 +75,6 @@ __device__ __forceinline__ bool grid_sync(const DecodeParams &p, unsigned &epoch
                 }
             }
         }
-        __threadfence();
         *s_flag = ok;
     }
     __syncthreads();
@@ -67,6 +86,143 @@ __device__ __forceinline__ void copy_host16(uint8_t *dst, const uint8_t *src, in
         *reinterpret_cast<uint4 *>(dst + off) = *reinterpret_cast<const uint4 *>(src + off);
 }
 
+__device__ __forceinline__ void red_add_u64(uint64_t *p, uint64_t v) {
+    asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// moe_obs_cb for one decode layer, one warp of CTA 0.  Hits are stamped in
+// parallel: the i-th routed id, if resident, gets clock + (hits before i) + 1,
+// which is what the reference's sequential ++clock produces (the k ids are
+// distinct).  Counters that only CTA 0 writes during the launch (the clock)
+// live in shared memory; the others are fire-and-forget reductions.  Misses
+// (window bookkeeping, the pending list) are walked in id order by lane 0.
+__device__ __forceinline__ void observe_decode(const SlotState &st, int layer,
+                                               const int32_t *ids, const int32_t *slots, int k,
+                                               int ns, uint64_t *s_clock, int lane) {
+    const int E = st.n_expert;
+    const bool in = lane < k;
+    const int id = in ? ids[lane] : 0;
+    const int slot = in ? slots[lane] : ns;
+    const bool hit = in && slot != ns;
+    const unsigned hm = __ballot_sync(MOE_FULL, hit);
+    const unsigned mm = __ballot_sync(MOE_FULL, in && !hit);
+    const uint64_t clock = *s_clock;
+    if (hit) {
+        const int rank = __popc(hm & ((1u << lane) - 1u));
+        st.last_use[st.slot_off[layer] + slot] = clock + (uint64_t)rank + 1;
+    }
+    if (in && st.heat) atomicAdd(st.heat + (size_t)layer * E + id, 1.0f);
+    if (in && st.use_count) atomicAdd(st.use_count + (size_t)layer * E + id, 1u);
+    if (lane == 0) {
+        const int nh = __popc(hm);
+        if (nh) red_add_u64(st.n_hit + layer, (uint64_t)nh);
+        *s_clock = clock + (uint64_t)nh;
+        if (mm) {
+            const uint64_t n_steps = st.g[G_STEPS];
+            int32_t *pend = st.pending + (size_t)layer * E;
+            int np = st.n_pending[layer];
+            unsigned m = mm;
+            while (m) {
+                const int i = __ffs(m) - 1;
+                m &= m - 1;
+                const int mid = ids[i];
+                st.n_miss[layer] += 1;
+                if (st.miss_last) {
+                    uint64_t *ml = st.miss_last + (size_t)layer * E;
+                    uint64_t *mp = st.miss_prev + (size_t)layer * E;
+                    if (ml[mid] != n_steps) {
+                        mp[mid] = ml[mid];
+                        ml[mid] = n_steps;
+                    }
+                }
+                bool dup = false;
+                for (int q = 0; q < np; ++q)
+                    if (pend[q] == mid) { dup = true; break; }
+                if (!dup) pend[np++] = mid;
+            }
+            st.n_pending[layer] = np;
+        }
+    }
+    __syncwarp();
+}
+
+// Cold path: missed experts read zero-copy from the registered host weights
+// into the staging buffers (out of line to keep the hot loop's code compact).
+__device__ __noinline__ void host_miss_copies(const DecodeParams &p, const LayerDesc &ld,
+                                              const int32_t *s_ids, const int32_t *s_slot,
+                                              int K, int nch, const int *ch_k, const int *ch_i0,
+                                              const int *ch_n, const int *ch_off,
+                                              uint8_t *gate_sm, uint8_t *up_sm, uint8_t *dn,
+                                              int gurow, int drow, int h0, int h1) {
+    const int tid = threadIdx.x;
+    for (int q = 0; q < nch; ++q) {
+        const int kk = ch_k[q];
+        if (s_slot[kk] == ld.ns) {
+            const size_t off = (size_t)s_ids[kk] * p.gate_bytes + (size_t)ch_i0[q] * gurow;
+            if (ld.hgate && ld.hup) {
+                copy_host16(gate_sm + (size_t)ch_off[q] * gurow, ld.hgate + off, ch_n[q] * gurow);
+                copy_host16(up_sm + (size_t)ch_off[q] * gurow, ld.hup + off, ch_n[q] * gurow);
+            } else if (tid == 0) {
+                atomicOr(p.err, MOE_DEV_ERR_INDEX);
+            }
+        }
+    }
+    for (int kk = 0; kk < K; ++kk) {
+        if (h1 > h0 && s_slot[kk] == ld.ns) {
+            if (ld.hdown) {
+                const uint8_t *base = ld.hdown + (size_t)s_ids[kk] * p.down_bytes;
+                const uintptr_t a0 = reinterpret_cast<uintptr_t>(base + (size_t)h0 * drow);
+                const uintptr_t a1 = reinterpret_cast<uintptr_t>(base + (size_t)h1 * drow);
+                const uintptr_t s0 = a0 & ~uintptr_t(15), s1 = (a1 + 15) & ~uintptr_t(15);
+                copy_host16(dn + (size_t)kk * p.dn_stride, reinterpret_cast<const uint8_t *>(s0),
+                            (int)(s1 - s0));
+            } else if (tid == 0) {
+                atomicOr(p.err, MOE_DEV_ERR_INDEX);
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void prefetch_line_l2(const void *ptr) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
+}
+
+// Speculative L2 prefetch (a hint; results never depend on it): the rows this
+// CTA would copy for layer `nl` if it routed to the experts it routed to for
+// the previous token, one 128-byte line per prefetch, spread over `nthr`
+// threads (index `tp`).
+__device__ __noinline__ void prefetch_next_layer(const DecodeParams &p, int nl, const int32_t *pred,
+                                                 const int32_t *tbl, int K, int nch, const int *ch_k,
+                                                 const int *ch_i0, const int *ch_n, int gurow,
+                                                 int drow, int h0, int h1, int tp, int nthr) {
+    const LayerDesc nd = p.layers[nl];
+    for (int q = 0; q < nch; ++q) {
+        const int pid = pred[ch_k[q]];
+        if (pid < 0) continue;
+        const int slot = tbl[pid];
+        if (slot == nd.ns) continue;
+        const size_t off = (size_t)slot * p.gate_bytes + (size_t)ch_i0[q] * gurow;
+        const int nbytes = ch_n[q] * gurow;
+        for (int o = tp * 128; o < nbytes; o += nthr * 128) {
+            prefetch_line_l2(nd.gate + off + o);
+            prefetch_line_l2(nd.up + off + o);
+        }
+    }
+    if (h1 <= h0) return;
+    for (int kk = 0; kk < K; ++kk) {
+        const int pid = pred[kk];
+        if (pid < 0) continue;
+        const int slot = tbl[pid];
+        if (slot == nd.ns) continue;
+        const uint8_t *base = nd.down + (size_t)slot * p.down_bytes;
+        const uintptr_t a0 = reinterpret_cast<uintptr_t>(base + (size_t)h0 * drow) & ~uintptr_t(127);
+        const uintptr_t a1 = reinterpret_cast<uintptr_t>(base + (size_t)h1 * drow);
+        for (uintptr_t a = a0 + (uintptr_t)tp * 128; a < a1; a += (uintptr_t)nthr * 128)
+            prefetch_line_l2(reinterpret_cast<const void *>(a));
+    }
+}
+
+template <int E_T, bool Q6_T>
 __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
     extern __shared__ __align__(128) uint8_t sm[];
     uint64_t *mb = reinterpret_cast<uint64_t *>(sm);
@@ -77,27 +233,36 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
     int8_t *aq = reinterpret_cast<int8_t *>(sm + p.off_aq);
     float *ad = reinterpret_cast<float *>(sm + p.off_ad);
     float *as_ = reinterpret_cast<float *>(sm + p.off_as);
-    float *rt = reinterpret_cast<float *>(sm + p.off_rt);
+    float *wt = reinterpret_cast<float *>(sm + p.off_rt);       // [rows][E] router^T rows
+    int32_t *tbl = reinterpret_cast<int32_t *>(sm + p.off_tbl); // [E] table row
+    float *rown = reinterpret_cast<float *>(sm + p.off_rown);   // [rows] own residual rows
+    int32_t *prev = reinterpret_cast<int32_t *>(sm + p.off_prev); // [NL][K] last token's ids
     uint8_t *gu = sm + p.off_gu;
     uint8_t *dn = sm + p.off_dn;
     float *ys = reinterpret_cast<float *>(sm + p.off_ys);
 
     __shared__ float s_lg[256];
+    __shared__ float s_p[256];
+    __shared__ float s_sel[256];
+    __shared__ uint64_t s_key[256];
+    __shared__ float s_psel[MOE_KMAX];
     __shared__ int32_t s_ids[MOE_KMAX];
     __shared__ float s_w[MOE_KMAX];
     __shared__ int32_t s_slot[MOE_KMAX];
-    __shared__ float s_red[DEC_WARPS];
+    __shared__ float s_red16[16];
     __shared__ int s_flag;
     __shared__ int s_bad;
+    __shared__ int s_any_miss;
+    __shared__ uint64_t s_clock;
 
     const int G = gridDim.x, c = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int E = p.n_expert, K = p.k, H = p.n_embd, I = p.n_ff, NL = p.n_layers;
+    constexpr int E = E_T;
+    const int K = p.k, H = p.n_embd, I = p.n_ff, NL = p.n_layers;
     const int gurow = (H / MOE_QK) * MOE_Q4K_BYTES;
-    const bool q6 = p.down_type == MOE_QT_Q6K;
-    const int drow = (I / MOE_QK) * (q6 ? MOE_Q6K_BYTES : MOE_Q4K_BYTES);
+    const int drow = (I / MOE_QK) * (Q6_T ? MOE_Q6K_BYTES : MOE_Q4K_BYTES);
     const int r0 = p.gu_r0[c], r1 = p.gu_r1[c];
     const int h0 = p.dn_h0[c], h1 = p.dn_h1[c];
-    const int rt_n = c < E ? (E - 1 - c) / G + 1 : 0;
+    const int rows = h1 - h0;
     uint8_t *gate_sm = gu;
     uint8_t *up_sm = gu + (size_t)p.gu_rows_max * gurow;
 
@@ -116,119 +281,177 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
         for (int i = 0; i < N_MB; ++i) mbar_init(&mb[i], 1);
         fence_mbar_init();
         s_bad = 0;
+        if (c == 0) s_clock = p.st.g[G_CLOCK];
     }
+    for (int i = tid; i < NL * K; i += DEC_THREADS) prev[i] = -1;
     __syncthreads();
 
     unsigned epoch = 0;
-    bool issued_rt = false;
-    int use = 0;   // (token, layer) counter: each barrier completes once per use
+    int use = 0;                      // (token, layer) index; barrier parity = use & 1
+    bool pend_wt = false, pend_tbl = false, pend_gu = false, pend_dn = false;
+    uint32_t wt_par = 0, tbl_par = 0;
 
-    // router rows for (token 0, layer 0)
-    if (tid == 0 && rt_n > 0) {
-        mbar_arrive_expect_tx(&mb[MB_RT], (uint32_t)(rt_n * H * 4));
-        for (int j = 0; j < rt_n; ++j)
-            bulk_g2s(rt + (size_t)j * H, p.layers[0].router_w + (size_t)(c + G * j) * H,
-                     (uint32_t)(H * 4), &mb[MB_RT]);
+    // ---- prologue: router rows + table of layer 0, partials of (0, 0) --------
+    if (tid == 0) {
+        mbar_arrive_expect_tx(&mb[MB_WT], (uint32_t)(rows * E * 4));
+        bulk_g2s(wt, p.layers[0].router_t + (size_t)h0 * E, (uint32_t)(rows * E * 4), &mb[MB_WT]);
+        mbar_arrive_expect_tx(&mb[MB_TBL], (uint32_t)(E * 4));
+        bulk_g2s(tbl, p.layers[0].table, (uint32_t)(E * 4), &mb[MB_TBL]);
     }
-    issued_rt = rt_n > 0;
-    bool issued_gu = false, issued_dn = false;
+    pend_wt = pend_tbl = true;
+    for (int i = tid; i < rows; i += DEC_THREADS) rown[i] = __ldg(p.h_in + h0 + i);
+    if (!mbar_wait(&mb[MB_WT], 0)) {
+        if (tid == 0) { atomicOr(p.err, MOE_DEV_ERR_TIMEOUT); atomicExch(p.abort_flag, 1); }
+    }
+    pend_wt = false;
+    wt_par = 1;
+    __syncthreads();
+    for (int e = tid; e < E; e += DEC_THREADS) {
+        float acc = 0.0f;
+        for (int i = 0; i < rows; ++i) acc = __fmaf_rn(wt[i * E + e], rown[i], acc);
+        __stcg(p.part_p + (size_t)c * E + e, acc);
+    }
+    if (tid == DEC_THREADS - 1) {
+        float s = 0.0f;
+        for (int i = 0; i < rows; ++i) s = __fmaf_rn(rown[i], rown[i], s);
+        __stcg(p.part_s + c, s);
+    }
 
     for (int t = 0; t < p.n_tok; ++t) {
         for (int L = 0; L < NL; ++L, ++use) {
             const LayerDesc ld = p.layers[L];
             const uint32_t par = (uint32_t)(use & 1);
+#define PROF(ph) \
+            if (p.prof && tid == ((ph) == 8 ? 32 : 0)) \
+                p.prof[(((size_t)t * NL + L) * DEC_PHASES + (ph)) * G + c] = gtimer();
+            PROF(0)
 
-            // ---- 1. x = RMSNorm(residual) ----------------------------------
-            if (L > 0 && !grid_sync(p, epoch, &s_flag)) goto abort;
+            // ---- A: partials and residual rows of (t, L) complete ---------------
+            if (!grid_sync(p, epoch, &s_flag)) goto abort;
+            PROF(1)
+
+            // ---- 1. residual, reduced logits, x = r * inv_rms, x -> Q8_1 ---------
+            // Every global load of the phase is issued before the first use: the
+            // residual (one float4 per thread), this warp's row group of partial
+            // logits (16 groups x float4 expert columns) and its partial sums of
+            // squares.
             {
+                float *red = reinterpret_cast<float *>(gu);   // [16][E] scratch
+                const int g = warp, cA = g * G / 16, cB = (g + 1) * G / 16;
                 const float *src = L == 0 ? p.h_in + (size_t)t * H : p.resid;
-                float ss = 0.0f;
-                for (int i = tid * 4; i < H; i += DEC_THREADS * 4) {
-                    const float4 v = L == 0 ? __ldg(reinterpret_cast<const float4 *>(src + i))
-                                            : __ldcg(reinterpret_cast<const float4 *>(src + i));
-                    *reinterpret_cast<float4 *>(xf + i) = v;
-                    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                float4 xv = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                const bool has_x = tid * 4 < H;
+                if (has_x)
+                    xv = L == 0 ? __ldg(reinterpret_cast<const float4 *>(src + tid * 4))
+                                : __ldcg(reinterpret_cast<const float4 *>(src + tid * 4));
+                for (int cbase = 0; cbase < E / 4; cbase += 32) {   // 1 pass (E=128), 2 (E=256)
+                    const int col = cbase + lane;
+                    const bool has_col = col < E / 4;
+                    const bool with_s = cbase == 0 && lane == 0;
+                    float4 v[10];
+                    float sv[10];
+#pragma unroll
+                    for (int j = 0; j < 10; ++j) {
+                        const int cc = min(cA + j, G - 1);   // clamped: always in bounds
+                        v[j] = has_col ? __ldcg(reinterpret_cast<const float4 *>(p.part_p + (size_t)cc * E) + col)
+                                       : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                        sv[j] = with_s ? __ldcg(p.part_s + cc) : 0.0f;
+                    }
+                    if (cbase == 0 && has_x) *reinterpret_cast<float4 *>(xf + tid * 4) = xv;
+                    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    float accs = 0.0f;
+#pragma unroll
+                    for (int j = 0; j < 10; ++j) {
+                        if (cA + j < cB) {
+                            acc.x = __fadd_rn(acc.x, v[j].x);
+                            acc.y = __fadd_rn(acc.y, v[j].y);
+                            acc.z = __fadd_rn(acc.z, v[j].z);
+                            acc.w = __fadd_rn(acc.w, v[j].w);
+                            accs = __fadd_rn(accs, sv[j]);
+                        }
+                    }
+                    if (has_col) *reinterpret_cast<float4 *>(red + g * E + 4 * col) = acc;
+                    if (with_s) s_red16[g] = accs;
                 }
-                ss = warp_sum(ss);
-                if (lane == 0) s_red[warp] = ss;
                 __syncthreads();
-                if (warp == 0) {
-                    float v = lane < DEC_WARPS ? s_red[lane] : 0.0f;
-                    v = warp_sum(v);
-                    if (lane == 0) s_red[0] = rsqrtf(v / (float)H + p.rms_eps);
+                PROF(2)
+                // group sums in group order; S redundantly in every thread
+                float S = s_red16[0];
+                for (int gg = 1; gg < 16; ++gg) S = __fadd_rn(S, s_red16[gg]);
+                const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(S, (float)H), p.rms_eps)));
+                for (int e = tid; e < E; e += DEC_THREADS) {
+                    float tot = red[e];
+                    for (int gg = 1; gg < 16; ++gg) tot = __fadd_rn(tot, red[gg * E + e]);
+                    s_lg[e] = __fmul_rn(tot, inv);
                 }
+                for (int i = tid; i < H; i += DEC_THREADS) xf[i] = __fmul_rn(xf[i], inv);
                 __syncthreads();
-                const float inv = s_red[0];
-                for (int i = tid; i < H; i += DEC_THREADS) xf[i] *= inv;
-                __syncthreads();
+                PROF(3)
                 if (p.dbg_x && c == 0)
                     for (int i = tid; i < H; i += DEC_THREADS)
                         p.dbg_x[((size_t)t * NL + L) * H + i] = xf[i];
             }
 
-            // ---- 2. router logits of this CTA; x -> Q8_1 ------------------
-            if (issued_rt) {
-                if (!mbar_wait(&mb[MB_RT], par)) {
-                    if (lane == 0) { atomicOr(p.err, MOE_DEV_ERR_TIMEOUT); atomicExch(p.abort_flag, 1); }
-                } else {
-                    for (int j = warp; j < rt_n; j += DEC_WARPS) {
-                        const float v = router_dot_warp(rt + (size_t)j * H, xf, H, lane);
-                        if (lane == 0) __stcg(p.logits + c + G * j, v);
-                    }
+            // ---- 2. select (warp 0 softmax; x -> Q8_1 on warps 1..) -------------
+            if (pend_tbl) {
+                if (!mbar_wait(&mb[MB_TBL], tbl_par)) {
+                    if (tid == 0) { atomicOr(p.err, MOE_DEV_ERR_TIMEOUT); atomicExch(p.abort_flag, 1); s_bad = 1; }
                 }
+                pend_tbl = false;
+                tbl_par ^= 1;
             }
-            for (int b = warp; b < H / 32; b += DEC_WARPS)
-                q8_block_warp(xf[32 * b + lane], lane, xq + 32 * b, xd + b, xs + b);
-            if (!grid_sync(p, epoch, &s_flag)) goto abort;
-            issued_rt = false;
-
-            // ---- 3. select, resolve, issue this layer's copies ------------
-            for (int e = tid; e < E; e += DEC_THREADS) s_lg[e] = __ldcg(p.logits + e);
-            __syncthreads();
             if (warp == 0)
-                router_select_warp(s_lg, E, ld.table, ld.ns, p.delta, p.delta > 0.0f, K, s_ids, s_w,
-                                   lane);
+                router_softmax_warp(s_lg, E, tbl, ld.ns, p.delta, p.delta > 0.0f, s_p, s_sel, lane,
+                                    s_key);
+            else
+                q8_quantize_cta(xf, false, H / 32, xq, xd, xs, tid - 32, DEC_THREADS - 32);
             __syncthreads();
-            if (tid < K) {
-                const int id = s_ids[tid];
-                if (id < 0 || id >= E) {
-                    atomicOr(p.err, MOE_DEV_ERR_INDEX);
-                    s_bad = 1;
-                    s_slot[tid] = ld.ns;
-                } else {
-                    s_slot[tid] = ld.table[id];
+            PROF(4)
+            if (s_bad) goto abort;
+            topk_key_block(s_key, s_p, E, K, s_ids, s_psel, tid, DEC_THREADS);
+            __syncthreads();
+            PROF(5)
+            if (warp == 0) {
+                // weights lane-parallel: each lane forms the sum in rank order
+                if (lane < K) {
+                    float ws = s_psel[0];
+                    for (int r = 1; r < K; ++r) ws = __fadd_rn(ws, s_psel[r]);
+                    s_w[lane] = __fdiv_rn(s_psel[lane], ws);
+                    const int id = s_ids[lane];
+                    const int slot = (id >= 0 && id < E) ? tbl[id] : ld.ns;
+                    s_slot[lane] = slot;
+                    if (id < 0 || id >= E) { atomicOr(p.err, MOE_DEV_ERR_INDEX); s_bad = 1; }
                 }
+                const unsigned miss = __ballot_sync(MOE_FULL, lane < K && s_slot[lane] == ld.ns);
+                if (lane == 0) s_any_miss = miss != 0;
             }
             __syncthreads();
             if (s_bad) {
                 if (tid == 0) atomicExch(p.abort_flag, 1);
                 goto abort;
             }
-            if (c == 0 && tid == 0) {
-                if (p.observe) observe_layer(p.st, L, s_ids, K);
-                if (p.dbg_ids)
-                    for (int i = 0; i < K; ++i) {
-                        p.dbg_ids[((size_t)t * NL + L) * K + i] = s_ids[i];
-                        p.dbg_w[((size_t)t * NL + L) * K + i] = s_w[i];
-                    }
+            PROF(6)
+            if (c == 0 && warp == 1) {
+                if (p.observe) observe_decode(p.st, L, s_ids, s_slot, K, ld.ns, &s_clock, lane);
+                if (p.dbg_ids && lane < K) {
+                    p.dbg_ids[((size_t)t * NL + L) * K + lane] = s_ids[lane];
+                    p.dbg_w[((size_t)t * NL + L) * K + lane] = s_w[lane];
+                }
             }
+            if (warp == 2 && lane < K) prev[L * K + lane] = s_ids[lane];
+
+            // ---- 3. warp 0 issues this layer's copies (+ next router rows / table);
+            //         the issue blocks at roughly the data rate, so the other warps
+            //         compute the gate/up rows meanwhile --------------------------------
             {
-                // next (token, layer) router rows, into the buffer read above
                 const bool has_next = L + 1 < NL || t + 1 < p.n_tok;
                 const int nl = L + 1 < NL ? L + 1 : 0;
-                if (tid == 0) {
-                    fence_proxy_async();
-                    if (has_next && rt_n > 0) {
-                        mbar_arrive_expect_tx(&mb[MB_RT], (uint32_t)(rt_n * H * 4));
-                        for (int j = 0; j < rt_n; ++j)
-                            bulk_g2s(rt + (size_t)j * H,
-                                     p.layers[nl].router_w + (size_t)(c + G * j) * H,
-                                     (uint32_t)(H * 4), &mb[MB_RT]);
-                    }
-                    for (int q = 0; q < nch; ++q) {
-                        const int kk = ch_k[q];
-                        const int slot = s_slot[kk];
+                if (warp == 0) {
+                    if (lane < nch) {
+                        const int q = lane;
+                        const int slot = s_slot[ch_k[q]];
                         const uint32_t bytes = (uint32_t)(ch_n[q] * gurow);
+                        fence_proxy_async();
                         if (slot != ld.ns) {
                             const size_t off = (size_t)slot * p.gate_bytes + (size_t)ch_i0[q] * gurow;
                             mbar_arrive_expect_tx(&mb[MB_GU + q], 2 * bytes);
@@ -238,9 +461,11 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                             mbar_arrive_expect_tx(&mb[MB_GU + q], 0);
                         }
                     }
-                    for (int kk = 0; kk < K; ++kk) {
+                    if (lane >= 8 && lane < 8 + K) {
+                        const int kk = lane - 8;
                         const int slot = s_slot[kk];
-                        if (h1 > h0 && slot != ld.ns) {
+                        fence_proxy_async();
+                        if (rows > 0 && slot != ld.ns) {
                             const uint8_t *base = ld.down + (size_t)slot * p.down_bytes;
                             const uintptr_t a0 = reinterpret_cast<uintptr_t>(base + (size_t)h0 * drow);
                             const uintptr_t a1 = reinterpret_cast<uintptr_t>(base + (size_t)h1 * drow);
@@ -252,137 +477,180 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                             mbar_arrive_expect_tx(&mb[MB_DN + kk], 0);
                         }
                     }
+                    if (lane == 30 && has_next) {
+                        fence_proxy_async();
+                        mbar_arrive_expect_tx(&mb[MB_WT], (uint32_t)(rows * E * 4));
+                        bulk_g2s(wt, p.layers[nl].router_t + (size_t)h0 * E, (uint32_t)(rows * E * 4),
+                                 &mb[MB_WT]);
+                    }
+                    if (lane == 31 && has_next) {
+                        fence_proxy_async();
+                        mbar_arrive_expect_tx(&mb[MB_TBL], (uint32_t)(E * 4));
+                        bulk_g2s(tbl, p.layers[nl].table, (uint32_t)(E * 4), &mb[MB_TBL]);
+                    }
                 }
-                issued_rt = has_next && rt_n > 0;
-                issued_gu = true;
-                issued_dn = true;
+                pend_wt = pend_tbl = has_next;
+                pend_gu = pend_dn = true;
                 // missed experts: zero-copy reads of the registered host weights
-                for (int q = 0; q < nch; ++q) {
-                    const int kk = ch_k[q];
-                    if (s_slot[kk] == ld.ns) {
-                        const int id = s_ids[kk];
-                        const size_t off = (size_t)id * p.gate_bytes + (size_t)ch_i0[q] * gurow;
-                        if (ld.hgate && ld.hup) {
-                            copy_host16(gate_sm + (size_t)ch_off[q] * gurow, ld.hgate + off, ch_n[q] * gurow);
-                            copy_host16(up_sm + (size_t)ch_off[q] * gurow, ld.hup + off, ch_n[q] * gurow);
-                        } else if (tid == 0) {
-                            atomicOr(p.err, MOE_DEV_ERR_INDEX);
-                        }
-                    }
+                if (s_any_miss) {
+                    host_miss_copies(p, ld, s_ids, s_slot, K, nch, ch_k, ch_i0, ch_n, ch_off, gate_sm,
+                                     up_sm, dn, gurow, drow, h0, h1);
+                    __syncthreads();
                 }
-                for (int kk = 0; kk < K; ++kk) {
-                    if (h1 > h0 && s_slot[kk] == ld.ns) {
-                        if (ld.hdown) {
-                            const uint8_t *base = ld.hdown + (size_t)s_ids[kk] * p.down_bytes;
-                            const uintptr_t a0 = reinterpret_cast<uintptr_t>(base + (size_t)h0 * drow);
-                            const uintptr_t a1 = reinterpret_cast<uintptr_t>(base + (size_t)h1 * drow);
-                            const uintptr_t s0 = a0 & ~uintptr_t(15), s1 = (a1 + 15) & ~uintptr_t(15);
-                            copy_host16(dn + (size_t)kk * p.dn_stride, reinterpret_cast<const uint8_t *>(s0),
-                                        (int)(s1 - s0));
-                        } else if (tid == 0) {
-                            atomicOr(p.err, MOE_DEV_ERR_INDEX);
-                        }
-                    }
-                }
-                __syncthreads();
             }
+            PROF(7)
 
-            // ---- 4. gate/up GEMV + SiLU*mul ----------------------------------
-            {
+            // ---- 4. gate/up GEMV + SiLU*mul on warps 1..15, two rows per iteration -
+            if (warp > 0) {
                 const int units = (H / MOE_QK) * 4;
+                const int W = DEC_WARPS - 1, wi = warp - 1;
                 ActQ4 a;
                 if (lane < units) load_act_q4(a, xq, xd, xs, lane >> 2, lane & 3);
-                int waited = 0;   // bit q: piece q waited by this warp
+                int waited = 0;
                 bool fail = false;
-                for (int r = r0 + warp; r < r1; r += DEC_WARPS) {
-                    const int lr = r - r0;
-                    int q = 0;
-                    while (q + 1 < nch && lr >= ch_off[q + 1]) ++q;
-                    if (!(waited & (1 << q))) {
-                        if (!mbar_wait(&mb[MB_GU + q], par)) { fail = true; break; }
-                        waited |= 1 << q;
+                for (int rA = r0 + wi; rA < r1 && !fail; rA += 2 * W) {
+                    const int rB = rA + W;
+                    const bool hasB = rB < r1;
+                    const int lA = rA - r0, lB = rB - r0;
+                    int qA = 0, qB = 0;
+                    while (qA + 1 < nch && lA >= ch_off[qA + 1]) ++qA;
+                    while (hasB && qB + 1 < nch && lB >= ch_off[qB + 1]) ++qB;
+                    if (!(waited & (1 << qA))) {
+                        if (!mbar_wait(&mb[MB_GU + qA], par)) { fail = true; break; }
+                        waited |= 1 << qA;
                     }
-                    const int kk = ch_k[q];
-                    const int i = ch_i0[q] + (lr - ch_off[q]);
-                    float g = 0.0f, u = 0.0f;
+                    if (hasB && !(waited & (1 << qB))) {
+                        if (!mbar_wait(&mb[MB_GU + qB], par)) { fail = true; break; }
+                        waited |= 1 << qB;
+                    }
+                    float gA = 0.0f, uA = 0.0f, gB = 0.0f, uB = 0.0f;
                     if (lane < units) {
-                        const int sb = lane >> 2, pp = lane & 3;
-                        g = q4k_unit_dot(gate_sm + (size_t)lr * gurow + sb * MOE_Q4K_BYTES, pp, a);
-                        u = q4k_unit_dot(up_sm + (size_t)lr * gurow + sb * MOE_Q4K_BYTES, pp, a);
+                        const int so = (lane >> 2) * MOE_Q4K_BYTES, pp = lane & 3;
+                        gA = q4k_unit_dot(gate_sm + (size_t)lA * gurow + so, pp, a);
+                        uA = q4k_unit_dot(up_sm + (size_t)lA * gurow + so, pp, a);
+                        if (hasB) {
+                            gB = q4k_unit_dot(gate_sm + (size_t)lB * gurow + so, pp, a);
+                            uB = q4k_unit_dot(up_sm + (size_t)lB * gurow + so, pp, a);
+                        }
                     }
-                    g = warp_sum(g);
-                    u = warp_sum(u);
-                    if (lane == 0) __stcg(p.act + (size_t)kk * I + i, silu_mul(g, u));
+#pragma unroll
+                    for (int off = 16; off >= 1; off >>= 1) {
+                        gA += __shfl_xor_sync(MOE_FULL, gA, off);
+                        uA += __shfl_xor_sync(MOE_FULL, uA, off);
+                        gB += __shfl_xor_sync(MOE_FULL, gB, off);
+                        uB += __shfl_xor_sync(MOE_FULL, uB, off);
+                    }
+                    if (lane == 0) {
+                        __stcg(p.act + (size_t)ch_k[qA] * I + ch_i0[qA] + (lA - ch_off[qA]), silu_mul(gA, uA));
+                        if (hasB)
+                            __stcg(p.act + (size_t)ch_k[qB] * I + ch_i0[qB] + (lB - ch_off[qB]), silu_mul(gB, uB));
+                    }
                 }
                 if (fail && lane == 0) { atomicOr(p.err, MOE_DEV_ERR_TIMEOUT); atomicExch(p.abort_flag, 1); }
+                // the gate/up rows are done: warm L2 for the next layer while the
+                // other CTAs finish (the next table row was issued with this
+                // layer's copies)
+                const bool has_next = L + 1 < NL || t + 1 < p.n_tok;
+                const int nl = L + 1 < NL ? L + 1 : 0;
+                if (has_next && !fail && (!pend_tbl || mbar_wait(&mb[MB_TBL], tbl_par)))
+                    prefetch_next_layer(p, nl, prev + nl * K, tbl, K, nch, ch_k, ch_i0, ch_n, gurow, drow,
+                                        h0, h1, tid - 32, DEC_THREADS - 32);
             }
+            PROF(8)
+
+            // ---- B: activations complete ----------------------------------------------
             if (!grid_sync(p, epoch, &s_flag)) goto abort;
-            issued_gu = false;
+            PROF(9)
+            pend_gu = false;
 
-            // ---- 5. activations -> Q8_1 -----------------------------------
-            for (int b = warp; b < K * I / 32; b += DEC_WARPS)
-                q8_block_warp(__ldcg(p.act + 32 * b + lane), lane, aq + 32 * b, ad + b, as_ + b);
+            // ---- 5. activations -> Q8_1 ---------------------------------------------
+            q8_quantize_cta(p.act, true, K * I / 32, aq, ad, as_, tid, DEC_THREADS);
             __syncthreads();
+            PROF(10)
 
-            // ---- 6. down GEMV, weighted combine, residual ------------------
-            if (h1 > h0) {
+            // ---- 6. down GEMV: one lane per half super-block, 8-lane row groups ------
+            if (rows > 0) {
                 const int wpk = DEC_WARPS / K;   // warps per expert (>= 1)
                 if (warp < K * wpk) {
                     const int kk = warp / wpk, sub = warp % wpk;
-                    const uint8_t *base = ld.down + (size_t)s_slot[kk] * p.down_bytes;
-                    if (s_slot[kk] == ld.ns) base = ld.hdown + (size_t)s_ids[kk] * p.down_bytes;
+                    const int grp = lane >> 3, u = lane & 7;   // row group, unit in group
+                    const uint8_t *base = s_slot[kk] != ld.ns
+                        ? ld.down + (size_t)s_slot[kk] * p.down_bytes
+                        : ld.hdown + (size_t)s_ids[kk] * p.down_bytes;
                     const uintptr_t a0 = reinterpret_cast<uintptr_t>(base + (size_t)h0 * drow);
-                    const int lead = (int)(a0 & 15);
-                    const uint8_t *rows = dn + (size_t)kk * p.dn_stride + lead;
+                    const uint8_t *rws = dn + (size_t)kk * p.dn_stride + (int)(a0 & 15);
                     if (!mbar_wait(&mb[MB_DN + kk], par)) {
                         if (lane == 0) { atomicOr(p.err, MOE_DEV_ERR_TIMEOUT); atomicExch(p.abort_flag, 1); }
-                    } else if (q6) {
-                        const int units = (I / MOE_QK) * 8;
-                        ActQ6 a;
-                        const bool act_on = lane < units;
-                        if (act_on)
-                            load_act_q6(a, aq + (size_t)kk * I, ad + (size_t)kk * (I / 32), lane >> 3,
-                                        (lane >> 2) & 1, lane & 3);
-                        for (int h = h0 + sub; h < h1; h += wpk) {
+                    } else if constexpr (Q6_T) {
+                        const int nunits = (I / MOE_QK) * 2;           // half blocks per row
+                        const bool on = u < nunits;
+                        const int sb = u >> 1, hh = u & 1;
+                        ActHalf a;
+                        if (on) load_act_half(a, aq + (size_t)kk * I, ad + (size_t)kk * (I / 32), sb, hh);
+                        for (int i0 = sub * 4; i0 < rows; i0 += 4 * wpk) {
+                            const int i = i0 + grp;
                             float v = 0.0f;
-                            if (act_on)
-                                v = q6k_unit_dot(rows + (size_t)(h - h0) * drow + (lane >> 3) * MOE_Q6K_BYTES,
-                                                 (lane >> 2) & 1, lane & 3, a);
-                            v = warp_sum(v);
-                            if (lane == 0) ys[kk * p.dn_rows_max + (h - h0)] = v;
+                            if (on && i < rows) v = q6k_half_dot(rws + (size_t)i * drow + sb * MOE_Q6K_BYTES, hh, a);
+                            v = group8_sum(v);
+                            if (u == 0 && i < rows) ys[kk * p.dn_rows_max + i] = v;
                         }
                     } else {
                         const int units = (I / MOE_QK) * 4;
                         ActQ4 a;
-                        const bool act_on = lane < units;
-                        if (act_on)
+                        const bool on = lane < units;
+                        if (on)
                             load_act_q4(a, aq + (size_t)kk * I, ad + (size_t)kk * (I / 32),
                                         as_ + (size_t)kk * (I / 32), lane >> 2, lane & 3);
-                        for (int h = h0 + sub; h < h1; h += wpk) {
+                        for (int i = sub; i < rows; i += wpk) {
                             float v = 0.0f;
-                            if (act_on)
-                                v = q4k_unit_dot(rows + (size_t)(h - h0) * drow + (lane >> 2) * MOE_Q4K_BYTES,
-                                                 lane & 3, a);
+                            if (on) v = q4k_unit_dot(rws + (size_t)i * drow + (lane >> 2) * MOE_Q4K_BYTES, lane & 3, a);
                             v = warp_sum(v);
-                            if (lane == 0) ys[kk * p.dn_rows_max + (h - h0)] = v;
+                            if (lane == 0) ys[kk * p.dn_rows_max + i] = v;
                         }
                     }
                 }
             }
             __syncthreads();
-            issued_dn = false;
-            for (int h = h0 + tid; h < h1; h += DEC_THREADS) {
+            pend_dn = false;
+            const bool last = L == NL - 1;
+            for (int i = tid; i < rows; i += DEC_THREADS) {
                 float y = 0.0f;
-                for (int kk = 0; kk < K; ++kk) y = __fmaf_rn(s_w[kk], ys[kk * p.dn_rows_max + (h - h0)], y);
-                const float rin = L == 0 ? __ldg(p.h_in + (size_t)t * H + h) : p.resid[h];
-                const float rn = __fadd_rn(rin, y);
-                __stcg(p.resid + h, rn);
-                if (L == NL - 1) p.out[(size_t)t * H + h] = rn;
-                if (p.dbg_y) p.dbg_y[((size_t)t * NL + L) * H + h] = y;
+                for (int kk = 0; kk < K; ++kk) y = __fmaf_rn(s_w[kk], ys[kk * p.dn_rows_max + i], y);
+                const float rn = __fadd_rn(rown[i], y);
+                if (last) {
+                    p.out[(size_t)t * H + h0 + i] = rn;
+                    if (t + 1 < p.n_tok) rown[i] = __ldg(p.h_in + (size_t)(t + 1) * H + h0 + i);
+                } else {
+                    rown[i] = rn;
+                    __stcg(p.resid + h0 + i, rn);
+                }
+                if (p.dbg_y) p.dbg_y[((size_t)t * NL + L) * H + h0 + i] = y;
             }
+            PROF(11)
+            // partials of the next (token, layer) over this CTA's rows
+            if (pend_wt) {
+                if (!mbar_wait(&mb[MB_WT], wt_par)) {
+                    if (tid == 0) { atomicOr(p.err, MOE_DEV_ERR_TIMEOUT); atomicExch(p.abort_flag, 1); }
+                }
+                __syncthreads();
+                pend_wt = false;
+                wt_par ^= 1;
+                for (int e = tid; e < E; e += DEC_THREADS) {
+                    float acc = 0.0f;
+                    for (int i = 0; i < rows; ++i) acc = __fmaf_rn(wt[i * E + e], rown[i], acc);
+                    __stcg(p.part_p + (size_t)c * E + e, acc);
+                }
+                if (tid == DEC_THREADS - 1) {
+                    float s = 0.0f;
+                    for (int i = 0; i < rows; ++i) s = __fmaf_rn(rown[i], rown[i], s);
+                    __stcg(p.part_s + c, s);
+                }
+            }
+#undef PROF
             if (ld_relaxed_i32(p.abort_flag)) goto abort;
         }
     }
+    if (c == 0 && tid == 0) p.st.g[G_CLOCK] = s_clock;
     return;
 
 abort:
@@ -390,11 +658,13 @@ abort:
     {
         const uint32_t par = (uint32_t)(use & 1);
         if (tid == 0) {
-            if (issued_rt) mbar_wait(&mb[MB_RT], par);
-            if (issued_gu)
+            if (pend_wt) mbar_wait(&mb[MB_WT], wt_par);
+            if (pend_tbl) mbar_wait(&mb[MB_TBL], tbl_par);
+            if (pend_gu)
                 for (int q = 0; q < nch; ++q) mbar_wait(&mb[MB_GU + q], par);
-            if (issued_dn)
+            if (pend_dn)
                 for (int kk = 0; kk < K; ++kk) mbar_wait(&mb[MB_DN + kk], par);
+            if (c == 0) p.st.g[G_CLOCK] = s_clock;
         }
         __syncthreads();
     }
@@ -406,6 +676,7 @@ int decode_smem_layout(DecodeParams &p, int grid) {
     const int H = p.n_embd, I = p.n_ff, K = p.k, E = p.n_expert;
     const int gurow = (H / MOE_QK) * MOE_Q4K_BYTES;
     const int drow = (I / MOE_QK) * (p.down_type == MOE_QT_Q6K ? MOE_Q6K_BYTES : MOE_Q4K_BYTES);
+    (void)grid;
     int off = align16(N_MB * 8);
     p.off_xf = off; off = align16(off + H * 4);
     p.off_xq = off; off = align16(off + H);
@@ -414,8 +685,10 @@ int decode_smem_layout(DecodeParams &p, int grid) {
     p.off_aq = off; off = align16(off + K * I);
     p.off_ad = off; off = align16(off + K * (I / 32) * 4);
     p.off_as = off; off = align16(off + K * (I / 32) * 4);
-    p.rt_rows = (E + grid - 1) / grid;
-    p.off_rt = off; off = align16(off + p.rt_rows * H * 4);
+    p.off_rt = off; off = align16(off + p.dn_rows_max * E * 4);
+    p.off_tbl = off; off = align16(off + E * 4);
+    p.off_rown = off; off = align16(off + p.dn_rows_max * 4);
+    p.off_prev = off; off = align16(off + p.n_layers * K * 4);
     p.off_gu = off; off = align16(off + 2 * p.gu_rows_max * gurow + 16);
     p.dn_stride = align16(p.dn_rows_max * drow + 32) + 16;
     p.off_dn = off; off = align16(off + K * p.dn_stride);
@@ -424,23 +697,36 @@ int decode_smem_layout(DecodeParams &p, int grid) {
     return off;
 }
 
+// the template instance for (n_expert, down type), or null
+static const void *decode_kernel(int n_expert, int down_type) {
+    const bool q6 = down_type == MOE_QT_Q6K;
+    switch (n_expert) {
+        case 32:  return q6 ? (const void *)k_decode<32, true> : (const void *)k_decode<32, false>;
+        case 64:  return q6 ? (const void *)k_decode<64, true> : (const void *)k_decode<64, false>;
+        case 128: return q6 ? (const void *)k_decode<128, true> : (const void *)k_decode<128, false>;
+        case 256: return q6 ? (const void *)k_decode<256, true> : (const void *)k_decode<256, false>;
+        default:  return nullptr;
+    }
+}
+
 cudaError_t launch_decode(const DecodeParams &p, int grid, cudaStream_t s) {
-    cudaError_t e = cudaFuncSetAttribute(k_decode, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         p.smem_bytes);
+    const void *fn = decode_kernel(p.n_expert, p.down_type);
+    if (!fn) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem_bytes);
     if (e != cudaSuccess) return e;
     DecodeParams pp = p;
     void *args[] = {&pp};
-    return cudaLaunchCooperativeKernel((const void *)k_decode, dim3(grid), dim3(DEC_THREADS), args,
-                                       (size_t)p.smem_bytes, s);
+    return cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(DEC_THREADS), args, (size_t)p.smem_bytes, s);
 }
 
-int decode_max_grid(int smem_bytes, int device) {
-    if (cudaFuncSetAttribute(k_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) !=
-        cudaSuccess)
+int decode_max_grid(int smem_bytes, int device, int n_expert, int down_type) {
+    const void *fn = decode_kernel(n_expert, down_type);
+    if (!fn) return 0;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) != cudaSuccess)
         return 0;
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode, DEC_THREADS,
-                                                      (size_t)smem_bytes) != cudaSuccess)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, DEC_THREADS, (size_t)smem_bytes) !=
+        cudaSuccess)
         return 0;
     int sms = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);

@@ -180,19 +180,142 @@ __device__ __forceinline__ void router_select_warp(const float *logits, int n_ex
     }
 }
 
+// The softmax half of router_select_warp, run by one warp: probabilities and
+// selection values (p + delta on resident experts) into shared memory, in the
+// same canonical order.
+__device__ __forceinline__ void router_softmax_warp(const float *logits, int n_expert,
+                                                    const int32_t *table, int ns, float delta,
+                                                    bool use_prior, float *s_p, float *s_sel,
+                                                    int lane, uint64_t *s_key = nullptr) {
+    const int m = n_expert >> 5;
+    float lg[8], ex[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) lg[i] = i < m ? logits[lane + 32 * i] : -INFINITY;
+    float mx = lg[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i)
+        if (i < m) mx = fmaxf(mx, lg[i]);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(MOE_FULL, mx, off));
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        if (i < m) {
+            ex[i] = expf_exact(__fsub_rn(lg[i], mx));
+            s = i == 0 ? ex[0] : __fadd_rn(s, ex[i]);
+        }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) s = __fadd_rn(s, __shfl_xor_sync(MOE_FULL, s, off));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        if (i < m) {
+            const int e = lane + 32 * i;
+            const float p = __fdiv_rn(ex[i], s);
+            const bool res = use_prior && table != nullptr && table[e] != ns;
+            const float sv = res ? __fadd_rn(p, delta) : p;
+            s_p[e] = p;
+            s_sel[e] = sv;
+            if (s_key) s_key[e] = ((uint64_t)__float_as_uint(sv) << 32) | (uint64_t)(~(uint32_t)e);
+        }
+    }
+}
+
+// Top-k by rank, all threads of the CTA: rank(e) = #experts before e in the
+// order (selection value descending, id ascending); the k experts with rank < k
+// land at position rank.  The same total order as k rounds of arg-max with
+// ties to the lower id, so the same ids in the same order.  Needs a
+// __syncthreads() before (s_sel / s_p complete) and after (outputs).
+__device__ __forceinline__ void topk_rank_block(const float *s_sel, const float *s_p,
+                                                int n_expert, int k, int32_t *ids_out,
+                                                float *psel_out, int tid, int nthreads) {
+    const int parts = nthreads / n_expert;   // 2 (256 experts) or 4 (128): a power of 2
+    const int e = tid / parts, part = tid % parts;
+    const int span = n_expert / parts;
+    int cnt = 0;
+    float v = 0.0f;
+    if (e < n_expert) {
+        v = s_sel[e];
+        for (int j = part * span; j < (part + 1) * span; ++j) {
+            const float u = s_sel[j];
+            cnt += (u > v || (u == v && j < e)) ? 1 : 0;
+        }
+    }
+    for (int off = 1; off < parts; off <<= 1) cnt += __shfl_xor_sync(MOE_FULL, cnt, off);
+    if (e < n_expert && part == 0 && cnt < k) {
+        ids_out[cnt] = e;
+        psel_out[cnt] = s_p[e];
+    }
+}
+
 // ---------------------------------------------------------------------------
 // activation quantisation (Q8_1 blocks of 32, fp32 d and s)
 // ---------------------------------------------------------------------------
 
+// All threads of the CTA quantise n_blocks blocks of 32 values, 4 threads per
+// block (8 values each): same d, q and s as q8_block_warp / the oracle (amax
+// and the integer sum do not depend on the order).  src is read with
+// ld.global.cg when from_global (data written by other CTAs), else from
+// shared memory.  n_blocks * 4 must be a multiple of 32.
+__device__ __forceinline__ void q8_quantize_cta(const float *src, bool from_global, int n_blocks,
+                                                int8_t *q, float *d, float *s, int tid,
+                                                int nthreads) {
+    const int lane = tid & 31;
+    for (int base = tid - lane; base < n_blocks * 4; base += nthreads) {
+        const int b4 = base + lane;
+        const int blk = b4 >> 2, part = b4 & 3;
+        const bool valid = b4 < n_blocks * 4;
+        float v[8];
+        if (valid) {
+            const float4 *p = reinterpret_cast<const float4 *>(src + 32 * blk + 8 * part);
+            const float4 a = from_global ? __ldcg(p) : p[0];
+            const float4 c = from_global ? __ldcg(p + 1) : p[1];
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+            v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+        }
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+        amax = fmaxf(amax, __shfl_xor_sync(MOE_FULL, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(MOE_FULL, amax, 2));
+        const float db = __fdiv_rn(amax, 127.0f);
+        const float id = amax > 0.0f ? __fdiv_rn(1.0f, db) : 0.0f;
+        int qi[8];
+        int sum = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            qi[i] = (int)roundf(__fmul_rn(v[i], id));
+            sum += qi[i];
+        }
+        sum += __shfl_xor_sync(MOE_FULL, sum, 1);
+        sum += __shfl_xor_sync(MOE_FULL, sum, 2);
+        if (valid) {
+            const uint32_t lo = (uint32_t)(qi[0] & 0xFF) | ((uint32_t)(qi[1] & 0xFF) << 8) |
+                                ((uint32_t)(qi[2] & 0xFF) << 16) | ((uint32_t)(qi[3] & 0xFF) << 24);
+            const uint32_t hi = (uint32_t)(qi[4] & 0xFF) | ((uint32_t)(qi[5] & 0xFF) << 8) |
+                                ((uint32_t)(qi[6] & 0xFF) << 16) | ((uint32_t)(qi[7] & 0xFF) << 24);
+            *reinterpret_cast<uint2 *>(q + 32 * blk + 8 * part) = make_uint2(lo, hi);
+            if (part == 0) {
+                d[blk] = db;
+                s[blk] = __fmul_rn(db, (float)sum);
+            }
+        }
+    }
+}
+
 // One warp quantises one block of 32 values: lane l takes element l.
-// d = amax / 127, q = roundf(x / d), s = d * sum(q); as or_quantize_q8_1().
+// d = amax / 127, q = roundf(x * (1/d)), s = d * sum(q); as or_quantize_q8_1().
 __device__ __forceinline__ void q8_block_warp(float v, int lane, int8_t *q, float *d,
                                               float *s) {
     float amax = fabsf(v);
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(MOE_FULL, amax, off));
     const float db = __fdiv_rn(amax, 127.0f);
-    const int qi = amax > 0.0f ? (int)roundf(__fdiv_rn(v, db)) : 0;
+    const float id = amax > 0.0f ? __fdiv_rn(1.0f, db) : 0.0f;
+    const int qi = (int)roundf(__fmul_rn(v, id));
     int sum = qi;
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) sum += __shfl_xor_sync(MOE_FULL, sum, off);
@@ -333,6 +456,107 @@ __device__ __forceinline__ float q6k_unit_dot(const uint8_t *blk, int h, int j, 
     return d * acc;
 }
 
+// ---------------------------------------------------------------------------
+// Q6_K x Q8_1, one lane per half super-block (128 elements)
+// ---------------------------------------------------------------------------
+
+// n consecutive 32-bit words starting at a 2-byte-aligned address, read as
+// aligned words and realigned with funnel shifts; reads only words that hold
+// requested bytes.
+template <int N>
+__device__ __forceinline__ void ldw_a2(const uint8_t *ptr, uint32_t (&w)[N]) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(ptr);
+    const uint32_t *p = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
+    const uint32_t sh = (uint32_t)(a & 2) * 8u;
+    uint32_t raw[N + 1];
+#pragma unroll
+    for (int i = 0; i < N; ++i) raw[i] = p[i];
+    raw[N] = sh ? p[N] : 0u;
+#pragma unroll
+    for (int i = 0; i < N; ++i) w[i] = __funnelshift_r(raw[i], raw[i + 1], sh);
+}
+
+// Activations of a half super-block: 128 int8 (l = 0..31 for m = 0..3, as
+// q[m][l/4]) and the d of the four Q8_1 blocks.
+struct ActHalf {
+    int q[4][8];
+    float d[4];
+};
+
+__device__ __forceinline__ void load_act_half(ActHalf &a, const int8_t *q, const float *d, int sb,
+                                              int h) {
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        const int e = 256 * sb + 128 * h + 32 * m;
+        const int4 *qp = reinterpret_cast<const int4 *>(q + e);
+        const int4 v0 = qp[0], v1 = qp[1];
+        a.q[m][0] = v0.x; a.q[m][1] = v0.y; a.q[m][2] = v0.z; a.q[m][3] = v0.w;
+        a.q[m][4] = v1.x; a.q[m][5] = v1.y; a.q[m][6] = v1.z; a.q[m][7] = v1.w;
+        a.d[m] = d[e >> 5];
+    }
+}
+
+// Partial dot of half h of the Q6_K block at `blk` (2-byte aligned): for each
+// of its 8 scale groups (m, lower/upper 16 of l) an integer sum, scaled by the
+// group scale and the Q8_1 d, accumulated in (m, group) order; times the
+// block's d.
+__device__ __forceinline__ float q6k_half_dot(const uint8_t *blk, int h, const ActHalf &a) {
+    uint32_t lo[8], hi[8], qh[8], sc[2];
+    ldw_a2<8>(blk + 64 * h, lo);          // ql[64h + l],      l = 0..31
+    ldw_a2<8>(blk + 64 * h + 32, hi);     // ql[64h + 32 + l]
+    ldw_a2<8>(blk + 128 + 32 * h, qh);    // qh[32h + l]
+    ldw_a2<2>(blk + 192 + 8 * h, sc);     // scales[8h .. 8h+7]
+    const float d = h2f(*reinterpret_cast<const uint16_t *>(blk + 208));
+    float acc = 0.0f;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        int is0 = 0, is1 = 0;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+            const uint32_t src = (m & 1) ? hi[w] : lo[w];
+            const uint32_t nib = (m >> 1) ? ((src >> 4) & 0x0F0F0F0Fu) : (src & 0x0F0F0F0Fu);
+            const uint32_t hb = ((qh[w] >> (2 * m)) & 0x03030303u) << 4;
+            const int v = (int)__vsub4(nib | hb, 0x20202020u);
+            if (w < 4) is0 = __dp4a(v, a.q[m][w], is0);
+            else is1 = __dp4a(v, a.q[m][w], is1);
+        }
+        const int g0 = 2 * m, g1 = 2 * m + 1;   // scale bytes within the 8 loaded
+        const int s0 = (int)(int8_t)((sc[g0 >> 2] >> (8 * (g0 & 3))) & 0xFF);
+        const int s1 = (int)(int8_t)((sc[g1 >> 2] >> (8 * (g1 & 3))) & 0xFF);
+        acc += (float)(s0 * is0) * a.d[m];
+        acc += (float)(s1 * is1) * a.d[m];
+    }
+    return d * acc;
+}
+
+// Sum over the 8 lanes of an aligned 8-lane group, butterfly 1, 2, 4 (fixed
+// order; every lane of the group gets the same value).
+__device__ __forceinline__ float group8_sum(float v) {
+    v += __shfl_xor_sync(MOE_FULL, v, 1);
+    v += __shfl_xor_sync(MOE_FULL, v, 2);
+    v += __shfl_xor_sync(MOE_FULL, v, 4);
+    return v;
+}
+
+// Top-k by rank over 64-bit keys (selection bits << 32 | ~id: larger is
+// better, ties to the lower id), thread (e, part) comparing against experts
+// part, part + parts, ...; the same total order as topk_rank_block.
+__device__ __forceinline__ void topk_key_block(const uint64_t *s_key, const float *s_p,
+                                               int n_expert, int k, int32_t *ids_out,
+                                               float *psel_out, int tid, int nthreads) {
+    const int parts = nthreads / n_expert;
+    const int e = tid / parts, part = tid - e * parts;
+    int cnt = 0;
+    const uint64_t ke = e < n_expert ? s_key[e] : 0ull;
+    if (e < n_expert)
+        for (int j = part; j < n_expert; j += parts) cnt += s_key[j] > ke ? 1 : 0;
+    for (int off = 1; off < parts; off <<= 1) cnt += __shfl_xor_sync(MOE_FULL, cnt, off);
+    if (e < n_expert && part == 0 && cnt < k) {
+        ids_out[cnt] = e;
+        psel_out[cnt] = s_p[e];
+    }
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(MOE_FULL, v, off);
@@ -403,6 +627,12 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
             "r"(smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
+}
+
+// Hint: bring [src, src + bytes) into L2 (no completion, no destination);
+// src 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
 __device__ __forceinline__ uint32_t ld_acquire_u32(const unsigned *p) {

@@ -297,19 +297,21 @@ __global__ void __launch_bounds__(256) k_down(ExpertSrc src, const float *__rest
         const float *dq = ad + (size_t)kk * (n_ff / 32);
         const float *sq = as + (size_t)kk * (n_ff / 32);
         if (down_type == MOE_QT_Q6K) {
+            // one lane per half super-block, 8-lane row groups: the same unit
+            // mapping and reduction order as the persistent decode kernel
             const size_t rb = (size_t)nb * MOE_Q6K_BYTES;
-            const int units = nb * 8;
-            const int u = lane;
-            ActQ6 a;
-            const bool active = u < units;
-            if (active) load_act_q6(a, q, dq, u >> 3, (u >> 2) & 1, u & 3);
-            for (int r = 0; r < DN_ROWS; ++r) {
-                const int h = h0 + r;
+            const int grp = lane >> 3, u = lane & 7;
+            const bool on = u < nb * 2;
+            const int sb = u >> 1, hh = u & 1;
+            ActHalf a;
+            if (on) load_act_half(a, q, dq, sb, hh);
+            for (int r0w = 0; r0w < DN_ROWS; r0w += 4) {
+                const int r = r0w + grp, h = h0 + r;
                 float v = 0.0f;
-                if (active && h < n_embd && dbase)
-                    v = q6k_unit_dot(dbase + h * rb + (u >> 3) * MOE_Q6K_BYTES, (u >> 2) & 1, u & 3, a);
-                v = warp_sum(v);
-                if (lane == 0) ys[kk * DN_ROWS + r] = v;
+                if (on && h < n_embd && dbase)
+                    v = q6k_half_dot(dbase + h * rb + sb * MOE_Q6K_BYTES, hh, a);
+                v = group8_sum(v);
+                if (u == 0) ys[kk * DN_ROWS + r] = v;
             }
         } else {
             const size_t rb = (size_t)nb * MOE_Q4K_BYTES;
@@ -342,6 +344,21 @@ __global__ void __launch_bounds__(256) k_down(ExpertSrc src, const float *__rest
 // ===========================================================================
 // slot table: observation of externally computed ids, and the cache step
 // ===========================================================================
+
+__global__ void k_transpose(const float *__restrict__ in, float *__restrict__ out, int rows,
+                            int cols) {
+    __shared__ float tile[32][33];
+    const int bx = blockIdx.x * 32, by = blockIdx.y * 32;
+    for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+        const int r = by + j, cc = bx + threadIdx.x;
+        if (r < rows && cc < cols) tile[j][threadIdx.x] = in[(size_t)r * cols + cc];
+    }
+    __syncthreads();
+    for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+        const int r = bx + j, cc = by + threadIdx.x;   // out is [cols][rows]
+        if (r < cols && cc < rows) out[(size_t)r * rows + cc] = tile[threadIdx.x][j];
+    }
+}
 
 __global__ void k_observe(SlotState st, int layer, const int32_t *__restrict__ ids, int n) {
     if (threadIdx.x == 0 && blockIdx.x == 0) observe_layer(st, layer, ids, n);
@@ -537,6 +554,12 @@ cudaError_t launch_experts(const ExpertSrc &src, const float *x, const int32_t *
     }
     dim3 g2((n_embd + DN_ROWS - 1) / DN_ROWS, n_tok);
     k_down<<<g2, 256, smem, s>>>(src, act, ids, w, k, n_embd, n_ff, down_type, resid, y, err);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_transpose(const float *in, float *out, int rows, int cols, cudaStream_t s) {
+    dim3 grid((cols + 31) / 32, (rows + 31) / 32);
+    k_transpose<<<grid, dim3(32, 8), 0, s>>>(in, out, rows, cols);
     return cudaGetLastError();
 }
 

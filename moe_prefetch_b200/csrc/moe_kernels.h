@@ -31,6 +31,7 @@ cudaError_t launch_router(const float *W, const float *x, int n_tok, int n_exper
 cudaError_t launch_experts(const ExpertSrc &src, const float *x, const int32_t *ids,
                            const float *w, int n_tok, int k, int n_embd, int n_ff, int down_type,
                            float *act, const float *resid, float *y, int *err, cudaStream_t s);
+cudaError_t launch_transpose(const float *in, float *out, int rows, int cols, cudaStream_t s);
 cudaError_t launch_observe(const SlotState &st, int layer, const int32_t *ids, int n,
                            cudaStream_t s);
 cudaError_t launch_step(const SlotState &st, int32_t *host_jobs, int32_t *host_njobs,
@@ -40,6 +41,7 @@ cudaError_t launch_step(const SlotState &st, int32_t *host_jobs, int32_t *host_n
 
 struct LayerDesc {
     const float *router_w;                 // [E][H] device
+    const float *router_t;                 // [H][E] device (transposed)
     const uint8_t *gate, *up, *down;       // slot slabs
     const uint8_t *hgate, *hup, *hdown;    // mapped host or null
     const int32_t *table;                  // [E]
@@ -58,7 +60,9 @@ struct DecodeParams {
     float *out;                            // [n_tok][H]
     int n_tok;
     float *resid;                          // [H]  residual stream
-    float *logits;                         // [E]
+    float *logits;                         // [E] (unused by the 2-barrier kernel)
+    float *part_p;                         // [grid][E] partial logits
+    float *part_s;                         // [grid] partial sums of squares
     float *act;                            // [k][I]
     unsigned *bar;                         // grid barrier counter (zeroed per launch)
     int *abort_flag;
@@ -71,15 +75,16 @@ struct DecodeParams {
     int32_t *dbg_ids;                      // [n_tok][L][k]
     float *dbg_w;
     float *dbg_y;                          // [n_tok][L][H]
+    uint64_t *prof;                        // [n_tok][L][DEC_PHASES][grid] or null
     // shared-memory layout (bytes from the start of dynamic smem)
-    int off_xf, off_xq, off_xd, off_xs, off_aq, off_ad, off_as, off_rt, off_gu, off_dn, off_ys,
-        smem_bytes;
+    int off_xf, off_xq, off_xd, off_xs, off_aq, off_ad, off_as, off_rt, off_tbl, off_rown, off_prev,
+        off_gu, off_dn, off_ys, smem_bytes;
     int dn_stride;                         // bytes per expert chunk in the down staging
     int rt_rows;                           // router rows per CTA (ceil(E / grid))
 };
 
 int decode_smem_layout(DecodeParams &p, int grid);
 cudaError_t launch_decode(const DecodeParams &p, int grid, cudaStream_t s);
-int decode_max_grid(int smem_bytes, int device);
+int decode_max_grid(int smem_bytes, int device, int n_expert, int down_type);
 
 }  // namespace moe

@@ -160,10 +160,11 @@ class MoeStack:
                                             _ptr(w), _stream(stream)), "moe_layer_forward")
         return y, ids, w
 
-    def decode(self, h, out=None, debug=False, stream=None):
+    def decode(self, h, out=None, debug=False, stream=None, profile=False):
         """Batch-1 decode of h [n_tok, n_embd] (device) through every layer,
         one token after another; returns out (and the per-layer dumps when
-        debug)."""
+        debug; with profile, dumps["prof"] holds the per-CTA phase timestamps
+        [n_tok, n_layers, 12, grid] in ns)."""
         h = h.contiguous()
         n_tok = h.shape[0]
         out = torch.empty_like(h) if out is None else out
@@ -177,8 +178,13 @@ class MoeStack:
                 "w": torch.empty(n_tok, L, K, device=h.device),
                 "y": torch.empty(n_tok, L, H, device=h.device),
             }
+            prof_ptr = None
+            if profile:
+                grid = self.decode_info()["grid"]
+                dumps["prof"] = torch.zeros(n_tok, L, 12, grid, dtype=torch.int64, device=h.device)
+                prof_ptr = dumps["prof"].data_ptr()
             dbg = MoeDecodeDbg(dumps["x"].data_ptr(), dumps["ids"].data_ptr(),
-                               dumps["w"].data_ptr(), dumps["y"].data_ptr())
+                               dumps["w"].data_ptr(), dumps["y"].data_ptr(), prof_ptr)
         self._ck(self.lib.moe_decode(self.ctx, _ptr(h), _ptr(out), n_tok,
                                      C.byref(dbg) if dbg is not None else None, _stream(stream)),
                  "moe_decode")

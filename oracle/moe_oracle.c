@@ -287,9 +287,10 @@ void or_quantize_q8_1(const float *x, int8_t *q, float *d, float *s, int64_t n) 
             if (a > amax) amax = a;
         }
         const float db = amax / 127.0f;
+        const float id = amax > 0.0f ? 1.0f / db : 0.0f;
         int sum = 0;
         for (int l = 0; l < 32; ++l) {
-            const int v = amax > 0.0f ? (int)roundf(x[32 * b + l] / db) : 0;
+            const int v = (int)roundf(x[32 * b + l] * id);
             q[32 * b + l] = (int8_t)v;
             sum += v;
         }
@@ -399,10 +400,60 @@ float or_router_dot(const float *w, const float *x, int n_embd) {
 void or_router(const float *W, const float *x, int n_expert, int n_embd,
                const float *prior, int k, int32_t *ids, float *w,
                float *probs_out, float *logits_out) {
-    float logits[256], ex[256], p[256], sel[256];
+    float logits[256];
     for (int e = 0; e < n_expert; ++e) {
         logits[e] = or_router_dot(W + (size_t)e * n_embd, x, n_embd);
     }
+    if (logits_out) memcpy(logits_out, logits, sizeof(float) * (size_t)n_expert);
+    or_router_select(logits, n_expert, prior, k, ids, w, probs_out);
+}
+
+void or_router_fused(const float *Wt, const float *r, int n_expert, int n_embd,
+                     const int32_t *h0, const int32_t *h1, int G, float eps,
+                     const float *prior, int k, int32_t *ids, float *w, float *x_out,
+                     float *logits_out) {
+    float *P = (float *)malloc(sizeof(float) * (size_t)G * n_expert);
+    float *S = (float *)malloc(sizeof(float) * (size_t)G);
+    for (int c = 0; c < G; ++c) {
+        for (int e = 0; e < n_expert; ++e) {
+            float acc = 0.0f;
+            for (int h = h0[c]; h < h1[c]; ++h) acc = fmaf(Wt[(size_t)h * n_expert + e], r[h], acc);
+            P[(size_t)c * n_expert + e] = acc;
+        }
+        float s = 0.0f;
+        for (int h = h0[c]; h < h1[c]; ++h) s = fmaf(r[h], r[h], s);
+        S[c] = s;
+    }
+    /* 16 contiguous groups of c, each summed sequentially from 0; the group
+     * sums added in group order */
+    float logits[256];
+    for (int e = 0; e < n_expert; ++e) {
+        float tot = 0.0f;
+        for (int g = 0; g < 16; ++g) {
+            float acc = 0.0f;
+            for (int c = g * G / 16; c < (g + 1) * G / 16; ++c) acc = acc + P[(size_t)c * n_expert + e];
+            tot = g == 0 ? acc : tot + acc;
+        }
+        logits[e] = tot;
+    }
+    float st = 0.0f;
+    for (int g = 0; g < 16; ++g) {
+        float acc = 0.0f;
+        for (int c = g * G / 16; c < (g + 1) * G / 16; ++c) acc = acc + S[c];
+        st = g == 0 ? acc : st + acc;
+    }
+    const float inv = 1.0f / sqrtf(st / (float)n_embd + eps);
+    for (int e = 0; e < n_expert; ++e) logits[e] = logits[e] * inv;
+    if (x_out) for (int h = 0; h < n_embd; ++h) x_out[h] = r[h] * inv;
+    if (logits_out) memcpy(logits_out, logits, sizeof(float) * (size_t)n_expert);
+    or_router_select(logits, n_expert, prior, k, ids, w, NULL);
+    free(P);
+    free(S);
+}
+
+void or_router_select(const float *logits, int n_expert, const float *prior, int k,
+                      int32_t *ids, float *w, float *probs_out) {
+    float ex[256], p[256], sel[256];
     float mx = logits[0];
     for (int e = 1; e < n_expert; ++e) {
         if (logits[e] > mx) mx = logits[e];
@@ -445,7 +496,6 @@ void or_router(const float *W, const float *x, int n_expert, int n_embd,
     for (int i = 1; i < k; ++i) ws = ws + p[ids[i]];
     for (int i = 0; i < k; ++i) w[i] = p[ids[i]] / ws;
     if (probs_out) memcpy(probs_out, p, sizeof(float) * (size_t)n_expert);
-    if (logits_out) memcpy(logits_out, logits, sizeof(float) * (size_t)n_expert);
 }
 
 /* ------------------------------------------------------------------------ */
@@ -554,6 +604,33 @@ static void or_layer_impl(or_row_fn fn, const float *x, int n_tok, int n_embd, i
             for (int i = 0; i < k; ++i) {
                 acc += (double)w_out[t * k + i] * rows[((size_t)t * k + i) * n_embd + h];
             }
+            y_out[(size_t)t * n_embd + h] = (float)acc;
+        }
+    }
+    free(rows);
+}
+
+void or_moe_experts(const float *x, int n_tok, int n_embd, int n_ff, int k,
+                    const int32_t *ids, const float *w, const uint8_t *gate,
+                    const uint8_t *up, const uint8_t *down, int down_type, float *y_out,
+                    int n_threads) {
+    const size_t gexp = row_bytes(OR_QTYPE_Q4_K, n_embd) * (size_t)n_ff;
+    const size_t dexp = row_bytes(down_type, n_ff) * (size_t)n_embd;
+    float *rows = (float *)malloc(sizeof(float) * (size_t)n_tok * k * n_embd);
+#ifdef _OPENMP
+#pragma omp parallel for num_threads(n_threads > 0 ? n_threads : 1) schedule(dynamic, 1)
+#endif
+    for (int tk = 0; tk < n_tok * k; ++tk) {
+        const int t = tk / k;
+        const int32_t e = ids[tk];
+        or_expert_row(gate + e * gexp, up + e * gexp, down + e * dexp, down_type, n_embd, n_ff,
+                      x + (size_t)t * n_embd, rows + (size_t)tk * n_embd, NULL);
+    }
+    (void)n_threads;
+    for (int t = 0; t < n_tok; ++t) {
+        for (int h = 0; h < n_embd; ++h) {
+            double acc = 0.0;
+            for (int i = 0; i < k; ++i) acc += (double)w[t * k + i] * rows[((size_t)t * k + i) * n_embd + h];
             y_out[(size_t)t * n_embd + h] = (float)acc;
         }
     }

@@ -57,7 +57,8 @@ void or_quantize_q4_K(const float *x, uint8_t *y, int64_t n);
 void or_quantize_q6_K(const float *x, uint8_t *y, int64_t n);
 void or_dequantize_q4_K(const uint8_t *y, float *x, int64_t n);
 void or_dequantize_q6_K(const uint8_t *y, float *x, int64_t n);
-/* Q8_1-style activation blocks of 32: d = amax/127, q = roundf(x/d),
+/* Q8_1-style activation blocks of 32: d = amax/127, q = roundf(x * (1/d))
+ * (the reciprocal rounded once, as ggml's CPU quantize_row_q8_1_ref),
  * s = d * sum(q), d and s kept in fp32.  n % 32 == 0. */
 void or_quantize_q8_1(const float *x, int8_t *q, float *d, float *s, int64_t n);
 /* Q8_K as ggml's CPU path uses it (vec_dot_type of Q4_K/Q6_K): blocks of 256,
@@ -80,6 +81,23 @@ void or_router(const float *W, const float *x, int n_expert, int n_embd,
                float *probs_out, float *logits_out);
 /* the canonical dot alone (exposed for tests) */
 float or_router_dot(const float *w_row, const float *x, int n_embd);
+/* Select top-k from given logits (softmax, + prior, ties to the lower id,
+ * renormalised unbiased weights), the order of or_router after the logits. */
+void or_router_select(const float *logits, int n_expert, const float *prior, int k,
+                      int32_t *ids, float *w, float *probs_out);
+/* The decode kernel's fused RMSNorm + router (canonical order of the
+ * persistent kernel): the residual r [n_embd] is split in G row ranges
+ * [h0[c], h1[c]); per range, partial logits P[c][e] = sum_h Wt[h][e] r[h]
+ * (fma chain in h order) and S[c] = sum_h r[h]^2 (fma chain); partials are
+ * summed in 16 contiguous groups of c ([g*G/16, (g+1)*G/16), sequential adds
+ * from 0), the group sums added in group order; inv = 1 / sqrtf(S / n_embd +
+ * eps); logits = sum * inv;
+ * x = r * inv.  Wt is the router transposed, [n_embd][n_expert].  x_out and
+ * logits_out optional. */
+void or_router_fused(const float *Wt, const float *r, int n_expert, int n_embd,
+                     const int32_t *h0, const int32_t *h1, int G, float eps,
+                     const float *prior, int k, int32_t *ids, float *w, float *x_out,
+                     float *logits_out);
 
 /* ---- expert rows / layer ---------------------------------------------------------- */
 /* One expert: act = silu(gate x) * (up x) with x, act quantised to Q8_1;
@@ -102,6 +120,11 @@ void or_moe_layer(const float *x, int n_tok, int n_embd, int n_ff, int n_expert,
                   const uint8_t *gate, const uint8_t *up, const uint8_t *down,
                   int down_type, int32_t *ids_out, float *w_out, float *y_out,
                   int n_threads);
+/* The expert half alone: given ids / w [n_tok][k], y = sum_i w_i row(ids_i, x). */
+void or_moe_experts(const float *x, int n_tok, int n_embd, int n_ff, int k,
+                    const int32_t *ids, const float *w, const uint8_t *gate,
+                    const uint8_t *up, const uint8_t *down, int down_type, float *y_out,
+                    int n_threads);
 /* ggml CPU path (Q8_K activations), same outputs; the timed CPU baseline. */
 void or_moe_layer_q8K(const float *x, int n_tok, int n_embd, int n_ff, int n_expert,
                       int k, const float *router_w, const float *prior,

@@ -65,6 +65,9 @@ def _declare(L):
     L.or_dot_q6_K_q8_1.argtypes = [P, P, P, P, I64]
     L.or_dot_q6_K_q8_1.restype = C.c_double
     L.or_router.argtypes = [P, P, C.c_int, C.c_int, P, C.c_int, P, P, P, P]
+    L.or_router_select.argtypes = [P, C.c_int, P, C.c_int, P, P, P]
+    L.or_router_fused.argtypes = [P, P, C.c_int, C.c_int, P, P, C.c_int, F32, P, C.c_int, P, P,
+                                  P, P]
     L.or_router_dot.argtypes = [P, P, C.c_int]
     L.or_router_dot.restype = F32
     L.or_expert_row.argtypes = [P, P, P, C.c_int, C.c_int, C.c_int, P, P, P]
@@ -72,6 +75,8 @@ def _declare(L):
     layer_args = [P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, P, P, P, P, P,
                   C.c_int, P, P, P, C.c_int]
     L.or_moe_layer.argtypes = layer_args
+    L.or_moe_experts.argtypes = [P, C.c_int, C.c_int, C.c_int, C.c_int, P, P, P, P, P, C.c_int,
+                                 P, C.c_int]
     L.or_moe_layer_q8K.argtypes = layer_args
     L.or_moe_layer_cpu_fast.argtypes = [P, C.c_int, C.c_int, C.c_int, C.c_int, P, P, P, P,
                                         P, C.c_int, P, P, P, C.c_int]
@@ -188,6 +193,25 @@ def router(W, x, k, prior=None):
     return ids, w, probs, logits
 
 
+def router_fused(Wt, r, k, h0, h1, eps=1e-6, prior=None):
+    """The decode kernel's fused RMSNorm + router.  Wt [n_embd, n_expert];
+    h0/h1 the per-CTA row ranges.  Returns ids, w, x (normalised r), logits."""
+    Wt = _c(Wt, np.float32)
+    r = _c(r, np.float32)
+    H, E = Wt.shape
+    h0 = _c(h0, np.int32)
+    h1 = _c(h1, np.int32)
+    ids = np.empty(k, np.int32)
+    w = np.empty(k, np.float32)
+    x = np.empty(H, np.float32)
+    logits = np.empty(E, np.float32)
+    pr = _c(prior, np.float32) if prior is not None else None
+    lib().or_router_fused(_p(Wt), _p(r), E, H, _p(h0), _p(h1), len(h0), eps,
+                          _p(pr) if pr is not None else None, k, _p(ids), _p(w), _p(x),
+                          _p(logits))
+    return ids, w, x, logits
+
+
 def expert_row(gate, up, down, down_type, n_embd, n_ff, x, q8K=False):
     """One expert's unweighted output row f32[n_embd] (and act f32[n_ff])."""
     gate, up, down = (_c(a, np.uint8) for a in (gate, up, down))
@@ -221,6 +245,20 @@ def moe_layer(x, router_w, gate, up, down, down_type, n_ff, k, prior=None,
        _p(pr) if pr is not None else None, _p(gate), _p(up), _p(down), down_type,
        _p(ids), _p(w), _p(y), nt)
     return ids, w, y
+
+
+def moe_experts(x, ids, w, gate, up, down, down_type, n_ff, n_threads=None):
+    """y [n_tok, n_embd] = sum_i w[t, i] * expert_row(ids[t, i], x[t])."""
+    x = _c(np.atleast_2d(x), np.float32)
+    n_tok, n_embd = x.shape
+    ids = _c(np.atleast_2d(ids), np.int32)
+    w = _c(np.atleast_2d(w), np.float32)
+    k = ids.shape[1]
+    gate, up, down = (_c(a, np.uint8) for a in (gate, up, down))
+    y = np.empty((n_tok, n_embd), np.float32)
+    lib().or_moe_experts(_p(x), n_tok, n_embd, n_ff, k, _p(ids), _p(w), _p(gate), _p(up),
+                         _p(down), down_type, _p(y), n_threads or os.cpu_count())
+    return y
 
 
 def moe_layer_cpu_fast(x, router_w, gate, up, down, down_type, n_ff, k, prior=None,
@@ -443,7 +481,7 @@ class RefPredictor:
         self._lib().refpred_score(self.h, il, *args, _p(out))
         return out
 
-    def top_k(self, scores, k):
+    def top_k_ids(self, scores, k):
         scores = _c(scores, np.float32)
         out = np.empty(k, np.int32)
         n = self._lib().refpred_top_k(self.h, _p(scores), k, _p(out))

@@ -37,6 +37,34 @@ def rms_norm(h, eps=0.0):
     return (h / np.sqrt((h.astype(np.float64) ** 2).mean(-1, keepdims=True) + eps)).astype(np.float32)
 
 
+def decode_partition(n_embd, grid):
+    """Residual-row ranges [h0, h1) of the persistent decode kernel's CTAs."""
+    h0 = np.array([c * n_embd // grid for c in range(grid)], np.int32)
+    h1 = np.array([(c + 1) * n_embd // grid for c in range(grid)], np.int32)
+    return h0, h1
+
+
+def check_decode_layer(oracle_lib, h_tok, dumps, t, L, W, gate, up, down, grid, n_ff=768,
+                       down_type=14, prior=None):
+    """One (token, layer) of a decode against the oracle: the residual before
+    the layer is h + y_0 + ... + y_{L-1} in fp32 (the kernel's order); the
+    fused router must give the same ids, weights and normalised x bit for bit;
+    the layer output must be within the output tolerance."""
+    r = np.asarray(h_tok, np.float32).copy()
+    ys = dumps["y"]
+    for Lp in range(L):
+        r = (r + ys[t, Lp]).astype(np.float32)
+    h0, h1 = decode_partition(r.size, grid)
+    k = dumps["ids"].shape[-1]
+    rid, rw, rx, _ = oracle_lib.router_fused(np.ascontiguousarray(W.T), r, k, h0, h1, 1e-6, prior)
+    assert np.array_equal(dumps["ids"][t, L], rid), f"ids (t={t}, L={L})"
+    assert np.array_equal(dumps["w"][t, L].view(np.uint32), rw.view(np.uint32)), f"w (t={t}, L={L})"
+    assert np.array_equal(dumps["x"][t, L].view(np.uint32), rx.view(np.uint32)), f"x (t={t}, L={L})"
+    ry = oracle_lib.moe_experts(rx[None], rid[None], rw[None], gate, up, down, down_type, n_ff)[0]
+    assert rel_l2(ys[t, L], ry) <= REL_L2_TOL, (t, L, rel_l2(ys[t, L], ry))
+    assert np.abs(ys[t, L] - ry).max() <= MAX_ABS_TOL
+
+
 def ar1_states(n_tok, n_embd, rho=0.9, seed=12345):
     """AR(1) hidden states h_t = rho h_{t-1} + sqrt(1-rho^2) eps_t, RMS-normed."""
     rng = np.random.default_rng(seed)

@@ -5,7 +5,7 @@ the host expert bytes the table says they hold."""
 import numpy as np
 import pytest
 
-from conftest import ar1_states
+from conftest import ar1_states, check_decode_layer
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
@@ -113,7 +113,6 @@ def test_decode_with_cache_end_to_end(oracle_lib):
     step equal the oracle's, fed the same routed ids, and every layer output
     is within tolerance of the oracle's."""
     _needs_gpu()
-    from conftest import MAX_ABS_TOL, REL_L2_TOL, rel_l2
     from moe_prefetch_b200 import MoeCacheConfig, MoeStack
     L, E, k = 2, 128, 8
     # weights: generate resident on a helper stack, then host copies
@@ -135,22 +134,19 @@ def test_decode_with_cache_end_to_end(oracle_lib):
     oc = oracle_lib.OracleCache(L, E, 24, max_inserts=2, admit_mode=2, batch_tables=True,
                                 cache_prior=0.01)
     h = ar1_states(24, H, seed=2)
+    grid = st.decode_info()["grid"]
     for t in range(h.shape[0]):
         # the router's prior must see the oracle's published table
         out, dm = st.decode(torch.from_numpy(h[t:t + 1]).cuda(), debug=True)
         st.sync()
-        xs, ids, ws, ys = (dm[q].cpu().numpy()[0] for q in ("x", "ids", "w", "y"))
+        dumps = {q: v.cpu().numpy() for q, v in dm.items()}
         for il in range(L):
             tbl, prior = oc.dev_table(il)
             W = routers[il].cpu().numpy()
             gate, up, down = (x.numpy().reshape(E, -1) for x in host[il])
-            rids, rw, ry = oracle_lib.moe_layer(xs[il:il + 1], W, gate, up, down, 14, 768, k,
-                                                prior=prior)
-            assert np.array_equal(ids[il], rids[0]), f"token {t} layer {il}"
-            assert np.array_equal(ws[il].view(np.uint32), rw[0].view(np.uint32))
-            assert rel_l2(ys[il], ry[0]) <= REL_L2_TOL
-            assert np.abs(ys[il] - ry[0]).max() <= MAX_ABS_TOL
-            oc.observe(il, ids[il])
+            check_decode_layer(oracle_lib, h[t], dumps, 0, il, W, gate, up, down, grid,
+                               prior=prior)
+            oc.observe(il, dumps["ids"][0, il])
         st.step()
         oc.step()
         _compare(st, oc, L, f"token {t}")
