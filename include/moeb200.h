@@ -151,6 +151,42 @@ int moe_place(moe_ctx *ctx, int layer, const int32_t *slot_expert, int copy);
 int moe_layer_forward(moe_ctx *ctx, int layer, const float *x, float *y, int n_tok,
                       int32_t *ids, float *w, void *stream);
 
+/* moe_layer_forward that allocates no device memory.  This entry point has no
+ * counterpart in the reference, whose CPU expert path allocates nothing on
+ * the GPU.
+ *
+ * Who needs it: callers that cannot allocate device memory while they run.
+ * For example, a serving process that commits all of its device memory at
+ * start-up (weights, KV cache, compute buffers), or a ggml-style scheduler
+ * that sizes every buffer before it runs the graph.  moe_layer_forward grows
+ * its scratch with cudaMalloc the first time it sees a larger n_tok.  Growing
+ * also frees the old scratch, and cudaFree waits for the whole device.  This
+ * variant never does either.
+ *
+ * Arguments, results and error behaviour are those of moe_layer_forward.  The
+ * only difference is where the scratch lives: the router ids/weights and the
+ * gate/up activations go to one static device array of
+ * MOE_NOALLOC_SCRATCH_BYTES per device, built into the library.
+ *
+ * Limit: a call needs 2 * round_up(4 * n_tok * n_used, 256) +
+ * 4 * n_tok * n_used * n_ff bytes of that array.  For n_used 8 and n_ff 768
+ * that is at most 170 tokens.  A larger n_tok returns MOE_ERR_ARG, with the
+ * limit in the message, before anything is launched.
+ *
+ * Set-up: the first call on each device looks up the array's address (with
+ * that device current) and keeps it.  Make that first call before any stream
+ * capture starts.
+ *
+ * Races: every context on a device shares the one array.  Calls whose work
+ * overlaps in time race on it: other streams, other contexts, other host
+ * threads.  Calls issued one after another on a single stream are safe.
+ *
+ * Nothing in the array has to start at zero: every entry a call reads, the
+ * same call writes first. */
+#define MOE_NOALLOC_SCRATCH_BYTES (4u << 20)
+int moe_layer_forward_noalloc(moe_ctx *ctx, int layer, const float *x, float *y, int n_tok,
+                              int32_t *ids, float *w, void *stream);
+
 /* Optional per-(token, layer) dumps of the decode stack, device pointers or NULL:
  * x [n_tok][n_layers][n_embd] (router input), ids/w [n_tok][n_layers][n_used],
  * y [n_tok][n_layers][n_embd] (the layer's MoE output), and phase timestamps

@@ -9,6 +9,7 @@
 #include <cstdio>
 #include <cstring>
 #include <list>
+#include <mutex>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -505,6 +506,84 @@ extern "C" int moe_layer_forward(moe_ctx *c, int layer, const float *x, float *y
                      ids_d, w_d, nullptr, &c->st, n_tok == 1 ? layer : -1, s));
     CK(launch_experts(make_src(c, layer), x, ids_d, w_d, n_tok, g.n_used, g.n_embd, g.n_ff,
                       g.down_type, c->s_act, nullptr, y, c->err, s));
+    return MOE_OK;
+}
+
+// ---- moe_layer_forward_noalloc ----------------------------------------------
+// Some callers cannot allocate device memory while they run: their device
+// memory is committed up front, and a cudaFree on growth would also wait for
+// the whole device.  This variant therefore keeps the router ids/weights and
+// the gate/up activations in a static array that is part of the library
+// image.  Each device has its own copy of the array.  Every context on that
+// device shares it, so calls that overlap in time race on it.
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[MOE_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kNoallocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+uint8_t *g_noalloc_ptr[kNoallocMaxDevices] = {};   // device ordinal -> scratch address
+
+constexpr size_t round256(size_t b) { return (b + 255) & ~(size_t)255; }
+
+// Bytes of scratch one call needs: ids and weights, each rounded to 256
+// bytes, then the [n_tok][n_used][n_ff] fp32 activations.
+size_t noalloc_need(size_t n_tok, size_t k, size_t n_ff) {
+    return 2 * round256(4 * n_tok * k) + 4 * n_tok * k * n_ff;
+}
+}  // namespace
+
+// The first call on a device (with that device current) looks the array's
+// address up; later calls reuse it.  The lookup may make the runtime load the
+// library's device image, so the first call must come before any stream
+// capture.
+static int noalloc_scratch(moe_ctx *c, uint8_t **out) {
+    const int dev = c->cfg.device;
+    if (dev < 0 || dev >= kNoallocMaxDevices)
+        return fail(c, MOE_ERR_UNSUPPORTED, "moe_layer_forward_noalloc: device %d is out of range", dev);
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void *p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            return fail(c, MOE_ERR_CUDA, "moe_layer_forward_noalloc: cudaGetSymbolAddress: %s",
+                        cudaGetErrorString(e));
+        g_noalloc_ptr[dev] = static_cast<uint8_t *>(p);
+    }
+    *out = g_noalloc_ptr[dev];
+    return MOE_OK;
+}
+
+extern "C" int moe_layer_forward_noalloc(moe_ctx *c, int layer, const float *x, float *y,
+                                         int n_tok, int32_t *ids, float *w, void *stream) {
+    if (!c || !x || !y || n_tok <= 0 || layer < 0 || layer >= c->cfg.n_layers)
+        return fail(c, MOE_ERR_ARG, "moe_layer_forward_noalloc: bad argument");
+    const moe_cfg &g = c->cfg;
+    const size_t K = (size_t)g.n_used, I = (size_t)g.n_ff;
+    if (noalloc_need((size_t)n_tok, K, I) > MOE_NOALLOC_SCRATCH_BYTES) {
+        size_t max_tok = MOE_NOALLOC_SCRATCH_BYTES / (4 * K * I);
+        while (max_tok > 0 && noalloc_need(max_tok, K, I) > MOE_NOALLOC_SCRATCH_BYTES) --max_tok;
+        return fail(c, MOE_ERR_ARG,
+                    "moe_layer_forward_noalloc: %d tokens need %zu bytes of scratch; the static "
+                    "scratch holds %u bytes, enough for at most %zu tokens with n_used %d, n_ff %d",
+                    n_tok, noalloc_need((size_t)n_tok, K, I), MOE_NOALLOC_SCRATCH_BYTES, max_tok,
+                    g.n_used, g.n_ff);
+    }
+    CK(cudaSetDevice(g.device));
+    uint8_t *scr = nullptr;
+    const int r = noalloc_scratch(c, &scr);
+    if (r != MOE_OK) return r;
+    const size_t sel = round256(4 * (size_t)n_tok * K);
+    int32_t *ids_d = ids ? ids : reinterpret_cast<int32_t *>(scr);
+    float *w_d = w ? w : reinterpret_cast<float *>(scr + sel);
+    float *act = reinterpret_cast<float *>(scr + 2 * sel);
+    cudaStream_t s = (cudaStream_t)stream;
+    const int32_t *table = c->st.table + (size_t)layer * g.n_expert;
+    CK(launch_router(c->router + (size_t)layer * g.n_expert * g.n_embd, x, n_tok, g.n_expert, g.n_embd,
+                     table, c->L[layer].ns, g.cache_prior, n_tok == 1 && g.cache_prior > 0.0f, g.n_used,
+                     ids_d, w_d, nullptr, &c->st, n_tok == 1 ? layer : -1, s));
+    CK(launch_experts(make_src(c, layer), x, ids_d, w_d, n_tok, g.n_used, g.n_embd, g.n_ff,
+                      g.down_type, act, nullptr, y, c->err, s));
     return MOE_OK;
 }
 

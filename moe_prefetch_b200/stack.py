@@ -160,6 +160,23 @@ class MoeStack:
                                             _ptr(w), _stream(stream)), "moe_layer_forward")
         return y, ids, w
 
+    def layer_forward_noalloc(self, layer, x, y, ids=None, w=None, stream=None):
+        """layer_forward for callers that cannot allocate device memory while
+        they run (their device memory is committed up front).  Neither the
+        library nor this method allocates.  The caller owns y
+        [n_tok, n_embd], and ids/w [n_tok, n_used] when it wants them.  The
+        scratch is one static array per device, shared by every stack on that
+        device: calls that overlap in time race on it.  n_tok is limited by
+        its size (MOE_NOALLOC_SCRATCH_BYTES); a larger batch raises
+        MoeError.  Returns y."""
+        for t in (x, y, ids, w):
+            if t is not None and not t.is_contiguous():
+                raise ValueError("layer_forward_noalloc needs contiguous tensors (a copy would allocate)")
+        self._ck(self.lib.moe_layer_forward_noalloc(self.ctx, layer, _ptr(x), _ptr(y), x.shape[0],
+                                                    _ptr(ids), _ptr(w), _stream(stream)),
+                 "moe_layer_forward_noalloc")
+        return y
+
     def decode(self, h, out=None, debug=False, stream=None, profile=False):
         """Batch-1 decode of h [n_tok, n_embd] (device) through every layer,
         one token after another; returns out (and the per-layer dumps when
