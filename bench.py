@@ -317,7 +317,7 @@ def main():
     bytes_per_launch = layer_token * n_layers * tokens
     achieved = bytes_per_launch / (avg_launch_ms / 1000.0) / 1e9
     traffic = None
-    tp = os.path.join(ROOT, "profiles", "decode_traffic.json")
+    tp = os.path.join(ROOT, "profiles", "k_decode_config1_traffic.json")
     if os.path.exists(tp):
         with open(tp) as f:
             tr = json.load(f)

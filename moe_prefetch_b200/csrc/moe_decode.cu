@@ -183,45 +183,6 @@ __device__ __noinline__ void host_miss_copies(const DecodeParams &p, const Layer
     }
 }
 
-__device__ __forceinline__ void prefetch_line_l2(const void *ptr) {
-    asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
-}
-
-// Speculative L2 prefetch (a hint; results never depend on it): the rows this
-// CTA would copy for layer `nl` if it routed to the experts it routed to for
-// the previous token, one 128-byte line per prefetch, spread over `nthr`
-// threads (index `tp`).
-__device__ __noinline__ void prefetch_next_layer(const DecodeParams &p, int nl, const int32_t *pred,
-                                                 const int32_t *tbl, int K, int nch, const int *ch_k,
-                                                 const int *ch_i0, const int *ch_n, int gurow,
-                                                 int drow, int h0, int h1, int tp, int nthr) {
-    const LayerDesc nd = p.layers[nl];
-    for (int q = 0; q < nch; ++q) {
-        const int pid = pred[ch_k[q]];
-        if (pid < 0) continue;
-        const int slot = tbl[pid];
-        if (slot == nd.ns) continue;
-        const size_t off = (size_t)slot * p.gate_bytes + (size_t)ch_i0[q] * gurow;
-        const int nbytes = ch_n[q] * gurow;
-        for (int o = tp * 128; o < nbytes; o += nthr * 128) {
-            prefetch_line_l2(nd.gate + off + o);
-            prefetch_line_l2(nd.up + off + o);
-        }
-    }
-    if (h1 <= h0) return;
-    for (int kk = 0; kk < K; ++kk) {
-        const int pid = pred[kk];
-        if (pid < 0) continue;
-        const int slot = tbl[pid];
-        if (slot == nd.ns) continue;
-        const uint8_t *base = nd.down + (size_t)slot * p.down_bytes;
-        const uintptr_t a0 = reinterpret_cast<uintptr_t>(base + (size_t)h0 * drow) & ~uintptr_t(127);
-        const uintptr_t a1 = reinterpret_cast<uintptr_t>(base + (size_t)h1 * drow);
-        for (uintptr_t a = a0 + (uintptr_t)tp * 128; a < a1; a += (uintptr_t)nthr * 128)
-            prefetch_line_l2(reinterpret_cast<const void *>(a));
-    }
-}
-
 template <int E_T, bool Q6_T>
 __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
     extern __shared__ __align__(128) uint8_t sm[];
@@ -236,7 +197,6 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
     float *wt = reinterpret_cast<float *>(sm + p.off_rt);       // [rows][E] router^T rows
     int32_t *tbl = reinterpret_cast<int32_t *>(sm + p.off_tbl); // [E] table row
     float *rown = reinterpret_cast<float *>(sm + p.off_rown);   // [rows] own residual rows
-    int32_t *prev = reinterpret_cast<int32_t *>(sm + p.off_prev); // [NL][K] last token's ids
     uint8_t *gu = sm + p.off_gu;
     uint8_t *dn = sm + p.off_dn;
     float *ys = reinterpret_cast<float *>(sm + p.off_ys);
@@ -283,7 +243,6 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
         s_bad = 0;
         if (c == 0) s_clock = p.st.g[G_CLOCK];
     }
-    for (int i = tid; i < NL * K; i += DEC_THREADS) prev[i] = -1;
     __syncthreads();
 
     unsigned epoch = 0;
@@ -438,7 +397,6 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                     p.dbg_w[((size_t)t * NL + L) * K + lane] = s_w[lane];
                 }
             }
-            if (warp == 2 && lane < K) prev[L * K + lane] = s_ids[lane];
 
             // ---- 3. warp 0 issues this layer's copies (+ next router rows / table);
             //         the issue blocks at roughly the data rate, so the other warps
@@ -547,14 +505,6 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                     }
                 }
                 if (fail && lane == 0) { atomicOr(p.err, MOE_DEV_ERR_TIMEOUT); atomicExch(p.abort_flag, 1); }
-                // the gate/up rows are done: warm L2 for the next layer while the
-                // other CTAs finish (the next table row was issued with this
-                // layer's copies)
-                const bool has_next = L + 1 < NL || t + 1 < p.n_tok;
-                const int nl = L + 1 < NL ? L + 1 : 0;
-                if (has_next && !fail && (!pend_tbl || mbar_wait(&mb[MB_TBL], tbl_par)))
-                    prefetch_next_layer(p, nl, prev + nl * K, tbl, K, nch, ch_k, ch_i0, ch_n, gurow, drow,
-                                        h0, h1, tid - 32, DEC_THREADS - 32);
             }
             PROF(8)
 
@@ -688,7 +638,6 @@ int decode_smem_layout(DecodeParams &p, int grid) {
     p.off_rt = off; off = align16(off + p.dn_rows_max * E * 4);
     p.off_tbl = off; off = align16(off + E * 4);
     p.off_rown = off; off = align16(off + p.dn_rows_max * 4);
-    p.off_prev = off; off = align16(off + p.n_layers * K * 4);
     p.off_gu = off; off = align16(off + 2 * p.gu_rows_max * gurow + 16);
     p.dn_stride = align16(p.dn_rows_max * drow + 32) + 16;
     p.off_dn = off; off = align16(off + K * p.dn_stride);
