@@ -213,6 +213,132 @@ def run_reference(args):
 
 
 # ---------------------------------------------------------------------------
+# config 2: the constrained slot cache, swept over slot budgets and delta
+# ---------------------------------------------------------------------------
+SWEEP_SLOTS = (16, 32, 56, 96)
+SWEEP_DELTA = (0.0, 0.01)
+MISS_GRID = (8, 16, 24, 32, 40, 48, 56, 64, 80, 96, 112, 128)
+
+
+def lru_miss_rates(ids, grid):
+    """Per-layer miss rate of an all-admit LRU cache of each size in `grid`
+    over a route trace ids [T][L][k]: {size: [rate per layer]}.  Used only to
+    rank layers for the byte-priced profile."""
+    T, L, K = ids.shape
+    out = {g: [0.0] * L for g in grid}
+    for il in range(L):
+        seq = ids[:, il, :]
+        for g in grid:
+            last, clock, miss = {}, 0, 0
+            for t in range(T):
+                for e in seq[t]:
+                    clock += 1
+                    if e in last:
+                        last[e] = clock
+                        continue
+                    miss += 1
+                    if len(last) >= g:
+                        del last[min(last, key=last.get)]
+                    last[e] = clock
+            out[g][il] = miss / float(T * K)
+    return out
+
+
+def run_config2(args):
+    """Config 2: the 48-layer stack with every expert in pinned host memory
+    and a slot cache of n_slots per layer (byte-priced per-layer profile from
+    a route trace of a separate token stream), second-miss admission (window
+    8), batched table writes, delta in {0, 0.01}.  Batch-1 decode token by
+    token with the cache step between tokens; misses are read zero-copy and
+    admitted experts uploaded on the copy stream.  One JSON line per point."""
+    import torch
+    from moe_prefetch_b200 import MoeCacheConfig, MoeStack
+    from moe_prefetch_b200.config import format_slot_profile, greedy_allocate_bytes
+
+    torch.cuda.set_device(0)
+    n_layers = args.layers
+    warm, timed = args.c2_warm, args.c2_tokens
+    res = MoeStack(n_layers=n_layers)
+    res.synth_resident(seed=11, keep_router=True)
+    host = []
+    for il in range(n_layers):
+        g, u, d = res.slot_views(il)
+        hl = []
+        for v in (g, u, d):
+            t = torch.empty(N_EXPERT * v.shape[1], dtype=torch.uint8, pin_memory=True)
+            t.view(N_EXPERT, -1).copy_(v[:N_EXPERT])
+            hl.append(t)
+        host.append(tuple(hl))
+    routers = [r.clone() for r in res.routers]
+    # route trace on a separate stream of tokens (delta 0: routing does not
+    # depend on the cache) -> per-layer miss curves -> byte-priced profiles
+    h_trace = torch.from_numpy(ar1_states(256, N_EMBD, seed=4242)).cuda()
+    _, dm = res.decode(h_trace, debug=True)
+    res.sync()
+    trace = dm["ids"].cpu().numpy()
+    del dm
+    res.close()
+    torch.cuda.synchronize()
+    miss8 = lru_miss_rates(trace, MISS_GRID)
+    h = torch.from_numpy(ar1_states(warm + timed, N_EMBD, seed=12345)).cuda()
+    out = torch.empty_like(h)
+    stream = torch.cuda.current_stream()
+    for ns in SWEEP_SLOTS:
+        grid = [g for g in MISS_GRID if g <= N_EXPERT]
+        caps, used, budget = greedy_allocate_bytes(miss8, grid, n_layers, ns, [],
+                                                   [EXPERT_BYTES] * n_layers)
+        for delta in SWEEP_DELTA:
+            cfg = MoeCacheConfig(n_slots=ns, max_inserts=2, admit="window", admit_window=8,
+                                 batch_tables=True, cache_prior=delta,
+                                 slot_profile=format_slot_profile(caps))
+            st = MoeStack(n_layers=n_layers, cache=cfg)
+            for il in range(n_layers):
+                st.set_router(il, routers[il])
+                st.set_expert_weights(il, *host[il])
+            for t in range(warm):
+                st.decode(h[t:t + 1], out[t:t + 1])
+                st.step()
+            st.sync()
+            s0 = st.stats()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for t in range(warm, warm + timed):
+                st.decode(h[t:t + 1], out[t:t + 1])
+                st.step()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            st.sync()
+            s1 = st.stats()
+            ms = e0.elapsed_time(e1)
+            d = {k: s1[k] - s0[k] for k in s1}
+            routed = d["hits"] + d["misses"]
+            line = {
+                "metric": "config2 slot-cache decode", "value": timed / (ms / 1000.0),
+                "unit": "tok/s", "n_gpus": 1, "higher_is_better": True,
+                "config": {"workload": "config2: 48-layer stack, experts in pinned host memory, "
+                                       "slot cache, window admission (W=8), batched tables",
+                           "n_slots": ns, "delta": delta, "max_inserts": 2,
+                           "profile": "byte-priced greedy from a 256-token route trace "
+                                      "(separate seed)",
+                           "slots_total": int(sum(caps)), "slots_uniform_total": ns * n_layers,
+                           "warm_tokens": warm, "timed_tokens": timed},
+                "hit_rate": d["hits"] / routed if routed else None,
+                "misses_per_token": d["misses"] / timed,
+                # step-scheduled uploads; "uploads" counts only the early-issue path
+                "uploads_per_token": d["scheduled"] / timed,
+                "published_per_token": d["published"] / timed,
+                "upload_gbs": d["upload_bytes"] / (ms / 1000.0) / 1e9,
+                "zero_copy_miss_gbs": d["misses"] * EXPERT_BYTES / (ms / 1000.0) / 1e9,
+                "ms_per_token": ms / timed,
+            }
+            print(json.dumps(line), flush=True)
+            st.close()
+            torch.cuda.synchronize()
+    return 0
+
+
+# ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
 def main():
@@ -227,9 +353,14 @@ def main():
     ap.add_argument("--ref-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--workload", default="config1", choices=["config1", "config2"])
+    ap.add_argument("--c2-warm", type=int, default=64)
+    ap.add_argument("--c2-tokens", type=int, default=128)
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "config2":
+        return run_config2(args)
 
     import torch
     import torch.distributed as dist

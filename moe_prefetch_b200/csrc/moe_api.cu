@@ -55,6 +55,11 @@ struct moe_ctx {
     int32_t *s_ids = nullptr;
     float *s_w = nullptr, *s_act = nullptr, *s_io = nullptr;
     int s_cap_tok = 0, s_io_cap = 0;
+    // grouping of the routed pairs by expert (n_tok > 1) and the unweighted
+    // per-pair down rows [P][n_embd]
+    int32_t *s_group = nullptr;
+    GroupBufs grp{};
+    float *s_ypair = nullptr;
     // uploader
     cudaStream_t copy_stream = nullptr;
     cudaEvent_t ev_step = nullptr, ev_copy = nullptr;
@@ -319,6 +324,8 @@ extern "C" void moe_destroy(moe_ctx *c) {
     cudaFree(c->s_w);
     cudaFree(c->s_act);
     cudaFree(c->s_io);
+    cudaFree(c->s_group);
+    cudaFree(c->s_ypair);
     if (c->h_jobs) cudaFreeHost(c->h_jobs);
     if (c->ev_step) cudaEventDestroy(c->ev_step);
     if (c->ev_copy) cudaEventDestroy(c->ev_copy);
@@ -466,14 +473,28 @@ extern "C" int moe_place(moe_ctx *c, int layer, const int32_t *slot_expert, int 
 static int ensure_scratch(moe_ctx *c, int n_tok) {
     if (n_tok <= c->s_cap_tok) return MOE_OK;
     cudaFree(c->s_ids); cudaFree(c->s_w); cudaFree(c->s_act);
+    cudaFree(c->s_group); cudaFree(c->s_ypair);
     c->s_ids = nullptr; c->s_w = nullptr; c->s_act = nullptr;
-    const int K = c->cfg.n_used;
-    if (cudaMalloc(&c->s_ids, sizeof(int32_t) * (size_t)n_tok * K) != cudaSuccess ||
-        cudaMalloc(&c->s_w, sizeof(float) * (size_t)n_tok * K) != cudaSuccess ||
-        cudaMalloc(&c->s_act, sizeof(float) * (size_t)n_tok * K * c->cfg.n_ff) != cudaSuccess) {
+    c->s_group = nullptr; c->s_ypair = nullptr;
+    const int K = c->cfg.n_used, E = c->cfg.n_expert;
+    const size_t P = (size_t)n_tok * K;
+    // cnt [E] | off [E + 1] | pair_pos [P] | pos_pair [P] | tiles [E + P] | n_tiles [1]
+    const size_t gints = (size_t)E + (E + 1) + P + P + (E + P) + 1;
+    if (cudaMalloc(&c->s_ids, sizeof(int32_t) * P) != cudaSuccess ||
+        cudaMalloc(&c->s_w, sizeof(float) * P) != cudaSuccess ||
+        cudaMalloc(&c->s_act, sizeof(float) * P * c->cfg.n_ff) != cudaSuccess ||
+        cudaMalloc(&c->s_group, sizeof(int32_t) * gints) != cudaSuccess ||
+        cudaMalloc(&c->s_ypair, sizeof(float) * P * c->cfg.n_embd) != cudaSuccess) {
         c->s_cap_tok = 0;
         return fail(c, MOE_ERR_OOM, "scratch allocation for %d tokens failed", n_tok);
     }
+    int32_t *g = c->s_group;
+    c->grp.cnt = g; g += E;
+    c->grp.off = g; g += E + 1;
+    c->grp.pair_pos = g; g += P;
+    c->grp.pos_pair = g; g += P;
+    c->grp.tiles = g; g += E + P;
+    c->grp.n_tiles = g;
     c->s_cap_tok = n_tok;
     return MOE_OK;
 }
@@ -504,8 +525,16 @@ extern "C" int moe_layer_forward(moe_ctx *c, int layer, const float *x, float *y
     CK(launch_router(c->router + (size_t)layer * g.n_expert * g.n_embd, x, n_tok, g.n_expert, g.n_embd,
                      table, c->L[layer].ns, g.cache_prior, n_tok == 1 && g.cache_prior > 0.0f, g.n_used,
                      ids_d, w_d, nullptr, &c->st, n_tok == 1 ? layer : -1, s));
-    CK(launch_experts(make_src(c, layer), x, ids_d, w_d, n_tok, g.n_used, g.n_embd, g.n_ff,
-                      g.down_type, c->s_act, nullptr, y, c->err, s));
+    if (n_tok == 1) {
+        CK(launch_experts(make_src(c, layer), x, ids_d, w_d, n_tok, g.n_used, g.n_embd, g.n_ff,
+                          g.down_type, c->s_act, nullptr, y, c->err, s));
+    } else {
+        // a batch: group the pairs by expert so that each expert's rows are
+        // read once per tile of its tokens (bit-identical results)
+        CK(launch_group(ids_d, n_tok * g.n_used, g.n_expert, GROUP_TILE, c->grp, c->err, s));
+        CK(launch_experts_grouped(make_src(c, layer), x, c->grp, n_tok, g.n_used, g.n_embd, g.n_ff,
+                                  g.down_type, w_d, c->s_act, c->s_ypair, nullptr, y, c->err, s));
+    }
     return MOE_OK;
 }
 

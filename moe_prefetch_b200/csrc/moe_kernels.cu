@@ -198,18 +198,6 @@ __global__ void __launch_bounds__(512) k_router(const float *__restrict__ W,
 // grid: (ceil(n_ff / GU_ROWS), n_tok * k); block 256 (8 warps)
 // ===========================================================================
 
-#define GU_ROWS 32
-
-__device__ __forceinline__ const uint8_t *expert_base(const ExpertSrc &s, int which, int id,
-                                                      int32_t slot) {
-    // which: 0 gate, 1 up, 2 down
-    const uint8_t *slab = which == 0 ? s.gate : which == 1 ? s.up : s.down;
-    const uint8_t *host = which == 0 ? s.hgate : which == 1 ? s.hup : s.hdown;
-    const int64_t bytes = which == 2 ? s.down_bytes : s.gate_bytes;
-    if (slot != s.ns && slab) return slab + (int64_t)slot * bytes;
-    return host ? host + (int64_t)id * bytes : nullptr;
-}
-
 __global__ void __launch_bounds__(256) k_gate_up(ExpertSrc src, const float *__restrict__ x,
                                                  const int32_t *__restrict__ ids, int k,
                                                  int n_embd, int n_ff,
@@ -262,8 +250,6 @@ __global__ void __launch_bounds__(256) k_gate_up(ExpertSrc src, const float *__r
 // down GEMV with fused weighted combine (stand-alone; direct global loads)
 // grid: (ceil(n_embd / DN_ROWS), n_tok); block 256
 // ===========================================================================
-
-#define DN_ROWS 16
 
 __global__ void __launch_bounds__(256) k_down(ExpertSrc src, const float *__restrict__ act,
                                               const int32_t *__restrict__ ids,

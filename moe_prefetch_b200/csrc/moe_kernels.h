@@ -20,6 +20,21 @@ struct ExpertSrc {
     int32_t ns, n_expert;
 };
 
+// Row bytes of expert `id` (which: 0 gate, 1 up, 2 down) in its slot, or in
+// the registered host copy when the slot is the dummy (a miss); null when
+// neither exists.
+__device__ __forceinline__ const uint8_t *expert_base(const ExpertSrc &s, int which, int id,
+                                                      int32_t slot) {
+    const uint8_t *slab = which == 0 ? s.gate : which == 1 ? s.up : s.down;
+    const uint8_t *host = which == 0 ? s.hgate : which == 1 ? s.hup : s.hdown;
+    const int64_t bytes = which == 2 ? s.down_bytes : s.gate_bytes;
+    if (slot != s.ns && slab) return slab + (int64_t)slot * bytes;
+    return host ? host + (int64_t)id * bytes : nullptr;
+}
+
+#define GU_ROWS 32   // gate/up rows per CTA of the stand-alone GEMVs
+#define DN_ROWS 16   // down rows per CTA of the stand-alone GEMVs
+
 cudaError_t launch_quantize(const float *x, void *y, int64_t n, int qtype, cudaStream_t s);
 cudaError_t launch_synth_weights(void *y, int64_t nb, int qtype, uint64_t seed, float sigma,
                                  cudaStream_t s);
@@ -36,6 +51,29 @@ cudaError_t launch_observe(const SlotState &st, int layer, const int32_t *ids, i
                            cudaStream_t s);
 cudaError_t launch_step(const SlotState &st, int32_t *host_jobs, int32_t *host_njobs,
                         cudaStream_t s);
+
+// ---- batched layer, tokens grouped by expert (moe_batched.cu) -------------
+
+#define GROUP_TILE 8   // pairs per CTA tile of the grouped GEMVs
+
+// Device buffers of one grouping: cnt [E], off [E + 1], pair_pos [P] (pair
+// t * k + r -> position in expert order), pos_pair [P], tiles
+// [group_max_tiles] ((expert << 16) | token tile), n_tiles [1].
+struct GroupBufs {
+    int32_t *cnt, *off, *pair_pos, *pos_pair, *tiles, *n_tiles;
+};
+
+int group_max_tiles(int n_expert, int P, int tile);
+cudaError_t launch_group(const int32_t *ids, int P, int n_expert, int tile, const GroupBufs &g,
+                         int *err, cudaStream_t s);
+// gate/up + down over the grouped pairs (act [P][n_ff], ypair [P][n_embd]
+// scratch), then the combine into y.
+cudaError_t launch_experts_grouped(const ExpertSrc &src, const float *x, const GroupBufs &g,
+                                   int n_tok, int k, int n_embd, int n_ff, int down_type,
+                                   const float *w, float *act, float *ypair, const float *resid,
+                                   float *y, int *err, cudaStream_t s);
+cudaError_t launch_combine(const float *ypair, const int32_t *pair_pos, const float *w, int n_tok,
+                           int k, int n_embd, const float *resid, float *y, cudaStream_t s);
 
 // ---- persistent decode (moe_decode.cu) ------------------------------------
 

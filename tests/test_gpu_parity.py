@@ -163,6 +163,45 @@ def test_layer_forward_batched(layer0, oracle_lib):
     _check_layer(y.cpu().numpy(), ids.cpu().numpy(), w.cpu().numpy(), ry, rids, rw)
 
 
+def _per_pair(st, x):
+    """The per-pair kernels (one read of an expert's rows per routed pair),
+    reached through the allocation-free entry point, which keeps them."""
+    y = torch.empty_like(x)
+    ids = torch.empty(x.shape[0], K, dtype=torch.int32, device=x.device)
+    w = torch.empty(x.shape[0], K, device=x.device)
+    st.layer_forward_noalloc(0, x, y, ids, w)
+    return y, ids, w
+
+
+@pytest.mark.parametrize("n_tok", [2, 9, 33, 170])
+def test_grouped_batch_bit_identical_to_per_pair(layer0, n_tok):
+    """n_tok > 1 groups the pairs by expert (one weight read per expert tile);
+    the result must equal the per-pair kernels bit for bit, including past
+    the grouping kernel's 1024-pair chunk (170 tokens = 1360 pairs)."""
+    st = layer0[0]
+    X = torch.from_numpy(rms_norm(np.random.default_rng(500 + n_tok).standard_normal((n_tok, H)))).cuda()
+    y, ids, w = st.layer_forward(0, X)
+    y1, ids1, w1 = _per_pair(st, X)
+    st.sync()
+    assert torch.equal(ids, ids1) and torch.equal(w.view(torch.int32), w1.view(torch.int32))
+    assert torch.equal(y.view(torch.int32), y1.view(torch.int32))
+
+
+def test_grouped_batch_skewed_routing(layer0, oracle_lib):
+    """Every token identical: all pairs land on the same 8 experts, 64 pairs
+    each, i.e. 8 tiles per expert and 120 idle experts."""
+    st, W, gate, up, down = layer0
+    x1 = rms_norm(np.random.default_rng(77).standard_normal((1, H)))
+    X = np.repeat(x1, 64, axis=0)
+    y, ids, w = st.layer_forward(0, torch.from_numpy(X).cuda())
+    y1, _, _ = _per_pair(st, torch.from_numpy(X).cuda())
+    st.sync()
+    assert torch.equal(y.view(torch.int32), y1.view(torch.int32))
+    rids, rw, ry = oracle_lib.moe_layer(X[:1], W, gate, up, down, Q6K, I, K)
+    _check_layer(y.cpu().numpy()[:1], ids.cpu().numpy()[:1], w.cpu().numpy()[:1], ry, rids, rw)
+    assert (y.cpu().numpy() == y.cpu().numpy()[:1]).all()
+
+
 def test_layer_forward_vs_fp32_and_q8K_informational(layer0, oracle_lib):
     """How far the Q8_1 kernel is from a plain fp32 reference and from the
     ggml CPU path's Q8_K activations (informational bounds, not the bar)."""
