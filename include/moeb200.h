@@ -151,6 +151,24 @@ int moe_place(moe_ctx *ctx, int layer, const int32_t *slot_expert, int copy);
 int moe_layer_forward(moe_ctx *ctx, int layer, const float *x, float *y, int n_tok,
                       int32_t *ids, float *w, void *stream);
 
+/* Expert paths of moe_layer_forward_path. */
+#define MOE_PATH_AUTO 0   /* GEMM when n_tok * n_used >= 4 * n_expert and it applies, else GEMV */
+#define MOE_PATH_GEMV 1   /* Q8_1 activations, int8 dot products: moe_layer_forward */
+#define MOE_PATH_GEMM 2   /* tcgen05 grouped GEMM: fp16 weights and activations, fp32 sums */
+
+/* moe_layer_forward with the expert arithmetic chosen by `path`.
+ * MOE_PATH_GEMM is the batched / prefill path.  It groups the routed pairs
+ * by expert in tiles of up to 64 tokens and dequantises each expert's
+ * Q4_K/Q6_K rows to fp16 in shared memory.  The products run on the tensor
+ * cores (tcgen05.mma, fp32 accumulators in tensor memory), then the same
+ * combine follows.  Its outputs match exact weights times unquantised
+ * activations within the layer tolerance; the GEMV path's Q8_1 activations
+ * are a different rounding.  It needs Q6_K down weights.  The router,
+ * prior and observation are moe_layer_forward's.  Replaces the batched
+ * mul_mat_id of build_moe_ffn (patches/0009:684-695) for prefill ubatches. */
+int moe_layer_forward_path(moe_ctx *ctx, int layer, const float *x, float *y, int n_tok,
+                           int32_t *ids, float *w, int path, void *stream);
+
 /* moe_layer_forward that allocates no device memory.  This entry point has no
  * counterpart in the reference, whose CPU expert path allocates nothing on
  * the GPU.

@@ -66,6 +66,7 @@ SIGNATURES = {
     "moe_place": (I, [P, I, P, I]),
     "moe_layer_forward": (I, [P, I, P, P, I, P, P, P]),
     "moe_layer_forward_noalloc": (I, [P, I, P, P, I, P, P, P]),
+    "moe_layer_forward_path": (I, [P, I, P, P, I, P, P, I, P]),
     "moe_decode": (I, [P, P, P, I, P, P]),
     "moe_decode_host": (I, [P, P, P, I, P]),
     "moe_sync": (I, [P, P]),

@@ -60,6 +60,9 @@ struct moe_ctx {
     int32_t *s_group = nullptr;
     GroupBufs grp{};
     float *s_ypair = nullptr;
+    // tensor-core GEMM operand tiles (fp16)
+    void *s_gemm = nullptr;
+    int s_gemm_cap_tok = 0;
     // uploader
     cudaStream_t copy_stream = nullptr;
     cudaEvent_t ev_step = nullptr, ev_copy = nullptr;
@@ -326,6 +329,7 @@ extern "C" void moe_destroy(moe_ctx *c) {
     cudaFree(c->s_io);
     cudaFree(c->s_group);
     cudaFree(c->s_ypair);
+    cudaFree(c->s_gemm);
     if (c->h_jobs) cudaFreeHost(c->h_jobs);
     if (c->ev_step) cudaEventDestroy(c->ev_step);
     if (c->ev_copy) cudaEventDestroy(c->ev_copy);
@@ -535,6 +539,49 @@ extern "C" int moe_layer_forward(moe_ctx *c, int layer, const float *x, float *y
         CK(launch_experts_grouped(make_src(c, layer), x, c->grp, n_tok, g.n_used, g.n_embd, g.n_ff,
                                   g.down_type, w_d, c->s_act, c->s_ypair, nullptr, y, c->err, s));
     }
+    return MOE_OK;
+}
+
+static int ensure_gemm_scratch(moe_ctx *c, int n_tok) {
+    if (n_tok <= c->s_gemm_cap_tok) return MOE_OK;
+    cudaFree(c->s_gemm);
+    c->s_gemm = nullptr;
+    const moe_cfg &g = c->cfg;
+    const size_t halves = gemm_scratch_halves(g.n_expert, n_tok * g.n_used, g.n_embd, g.n_ff);
+    if (cudaMalloc(&c->s_gemm, 2 * halves) != cudaSuccess) {
+        c->s_gemm_cap_tok = 0;
+        return fail(c, MOE_ERR_OOM, "GEMM scratch allocation for %d tokens failed", n_tok);
+    }
+    c->s_gemm_cap_tok = n_tok;
+    return MOE_OK;
+}
+
+extern "C" int moe_layer_forward_path(moe_ctx *c, int layer, const float *x, float *y, int n_tok,
+                                      int32_t *ids, float *w, int path, void *stream) {
+    if (!c || !x || !y || n_tok <= 0 || layer < 0 || layer >= c->cfg.n_layers)
+        return fail(c, MOE_ERR_ARG, "moe_layer_forward_path: bad argument");
+    const moe_cfg &g = c->cfg;
+    const bool gemm_ok = g.down_type == MOE_QTYPE_Q6_K && g.n_ff % 128 == 0 && g.n_embd % 128 == 0;
+    if (path == MOE_PATH_AUTO)
+        path = gemm_ok && n_tok * g.n_used >= 4 * g.n_expert ? MOE_PATH_GEMM : MOE_PATH_GEMV;
+    if (path == MOE_PATH_GEMV) return moe_layer_forward(c, layer, x, y, n_tok, ids, w, stream);
+    if (path != MOE_PATH_GEMM) return fail(c, MOE_ERR_ARG, "moe_layer_forward_path: unknown path %d", path);
+    if (!gemm_ok)
+        return fail(c, MOE_ERR_UNSUPPORTED, "the GEMM path needs Q6_K down weights and n_ff, n_embd multiples of 128");
+    CK(cudaSetDevice(g.device));
+    int r = ensure_scratch(c, n_tok);
+    if (r != MOE_OK) return r;
+    if ((r = ensure_gemm_scratch(c, n_tok)) != MOE_OK) return r;
+    cudaStream_t s = (cudaStream_t)stream;
+    int32_t *ids_d = ids ? ids : c->s_ids;
+    float *w_d = w ? w : c->s_w;
+    const int32_t *table = c->st.table + (size_t)layer * g.n_expert;
+    CK(launch_router(c->router + (size_t)layer * g.n_expert * g.n_embd, x, n_tok, g.n_expert, g.n_embd,
+                     table, c->L[layer].ns, g.cache_prior, n_tok == 1 && g.cache_prior > 0.0f, g.n_used,
+                     ids_d, w_d, nullptr, &c->st, n_tok == 1 ? layer : -1, s));
+    CK(launch_group(ids_d, n_tok * g.n_used, g.n_expert, GM_NT, c->grp, c->err, s));
+    CK(launch_experts_gemm(make_src(c, layer), x, c->grp, n_tok, g.n_used, g.n_embd, g.n_ff,
+                           g.down_type, w_d, c->s_gemm, c->s_ypair, nullptr, y, c->err, s));
     return MOE_OK;
 }
 

@@ -1,0 +1,499 @@
+// moe_gemm.cu -- grouped expert GEMM on the 5th-generation tensor cores, for
+// batches whose per-expert token counts make the expert FFN a dense
+// contraction (prefill chunks, large decode batches).
+//
+// The routed pairs are grouped by expert (k_group, tiles of GM_NT pairs).
+// Then:
+//   k_gather_x16    the tile's token rows -> fp16, written in the canonical
+//                   K-major no-swizzle tcgen05 operand layout, one contiguous
+//                   block per 64-wide K stage;
+//   k_gemm_gate_up  CTA = (128 rows of gate and up, one token tile):
+//                   - Q4_K rows are loaded (vector loads, one stage ahead in
+//                     registers), dequantised to fp16 in shared memory;
+//                   - the token tile arrives by bulk copy (TMA, no
+//                     multicast);
+//                   - one thread issues tcgen05.mma (M = 128, N = pairs
+//                     rounded to 16, K = 16, fp32 accumulators in TMEM);
+//                   - the epilogue reads TMEM (tcgen05.ld) and forms
+//                     SiLU(g)*u.  It writes the activations as fp16,
+//                     directly in the down GEMM's operand layout;
+//   k_gemm_down     CTA = (128 rows of down, one token tile): Q6_K rows
+//                   dequantised the same way, activations by bulk copy,
+//                   tcgen05.mma, unweighted rows to ypair[pos][h];
+//   k_combine       the weighted sum over ranks, in rank order.
+//
+// Numerics: weights and activations are rounded to fp16 once, and products
+// accumulate in fp32.  The reference for this path is exact weights times
+// unquantised activations with fp64 accumulation.  The GEMV kernels'
+// Q8_1 activations are a different rounding, so the two paths agree only
+// within tolerance.
+#include "moe_kernels.h"
+
+#include <cuda_fp16.h>
+
+namespace moe {
+
+#define GM_ROWS 128        // weight rows per CTA (MMA M)
+#define GM_THREADS 256
+#define GM_KS_GU 64        // K per gate/up stage (one Q4_K 64-element group)
+#define GM_KS_DN 128       // K per down stage (one Q6_K half block)
+
+// ---- tcgen05 / TMEM wrappers ------------------------------------------------
+
+__device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(slot)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16, one CTA.
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive (once) on `bar` when every tcgen05.mma issued so far by this thread
+// has completed.
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+            smem_u32(bar))
+        : "memory");
+}
+
+// 16 consecutive fp32 columns of the calling warp's 32 TMEM lanes (lane =
+// thread), waited for.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor, K-major, no swizzle: core matrices of 8
+// rows x 16 bytes stored contiguously; `lbo` = bytes between adjacent core
+// matrices along K, `sbo` = bytes between adjacent 8-row groups; version 1.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+
+// Instruction descriptor of kind::f16: fp16 A and B (K-major), fp32 D, M x N.
+__device__ __forceinline__ uint32_t idesc_f16(int M, int N) {
+    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+__device__ __forceinline__ void st_shared_v4(void *p, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(p)), "r"(a), "r"(b),
+                 "r"(c), "r"(d)
+                 : "memory");
+}
+
+// Exact small integer -> float (0 <= q < 2^23).
+__device__ __forceinline__ float u2f(uint32_t q) {
+    return __int_as_float(0x4B000000 | q) - 8388608.0f;
+}
+
+// ---- operand tiles --------------------------------------------------------
+// Canonical no-swizzle K-major tile of R rows x KS columns (fp16): element
+// (r, k) at byte ((k / 8) * R + r) * 16 + (k % 8) * 2, i.e. LBO = 16 R,
+// SBO = 128.  A token tile has R = GM_NT rows.
+
+// x [n_tok][n_embd] fp32 -> xt[tile][stage][k / 8][n][8] fp16 for every
+// tile of the grouping (rows past the tile's pairs are zero).
+__global__ void __launch_bounds__(256) k_gather_x16(const float *__restrict__ x,
+                                                    const int32_t *__restrict__ off,
+                                                    const int32_t *__restrict__ cnt,
+                                                    const int32_t *__restrict__ pos_pair,
+                                                    const int32_t *__restrict__ tiles,
+                                                    const int32_t *__restrict__ n_tiles, int k,
+                                                    int n_embd, __half *__restrict__ xt) {
+    const int i = blockIdx.x;
+    if (i >= *n_tiles) return;
+    const int tl = tiles[i], e = tl >> 16, tt = tl & 0xFFFF;
+    const int pos0 = off[e] + tt * GM_NT;
+    const int np = min(GM_NT, cnt[e] - tt * GM_NT);
+    __half *dst = xt + (size_t)i * n_embd * GM_NT;
+    const int chunks = (n_embd / 8) * GM_NT;      // (stage, k/8, n) in that order
+    for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
+        const int n = c % GM_NT, kc = c / GM_NT;  // kc over the whole row: stage = kc / 8
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (n < np) {
+            const int t = pos_pair[pos0 + n] / k;
+            const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)t * n_embd + 8 * kc);
+            const float4 a = src[0], b = src[1];
+            v = make_uint4(pack_h2(a.x, a.y), pack_h2(a.z, a.w), pack_h2(b.x, b.y),
+                           pack_h2(b.z, b.w));
+        }
+        *reinterpret_cast<uint4 *>(dst + (size_t)c * 8) = v;
+    }
+}
+
+// Dequantise one 64-element group g of a Q4_K super-block (header `hdr`,
+// quants q0/q1 = the group's 32 bytes) into row m of a canonical 128-row
+// tile at `A` (LBO 2048): w = d*sc*q - dmin*m in fp32, rounded to fp16 once.
+__device__ __forceinline__ void deq_q4k_group(const uint4 &hdr, const uint4 &q0, const uint4 &q1,
+                                              int g, uint8_t *A, int m) {
+    int sc0, mn0, sc1, mn1;
+    q4k_sm(hdr.y, hdr.z, hdr.w, 2 * g, sc0, mn0);
+    q4k_sm(hdr.y, hdr.z, hdr.w, 2 * g + 1, sc1, mn1);
+    const float d = h2f(hdr.x & 0xFFFFu), dmin = h2f(hdr.x >> 16);
+    const float d1 = d * (float)sc0, m1 = dmin * (float)mn0;
+    const float d2 = d * (float)sc1, m2 = dmin * (float)mn1;
+    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    uint8_t *row = A + (m >> 3) * 128 + (m & 7) * 16;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {   // bytes 8c .. 8c+7 -> elements 8c.. (low), 32+8c.. (high)
+        uint32_t lo[4], hi[4];
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+            const uint32_t v = w[2 * c + b];
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const uint32_t b0 = (v >> (16 * j)) & 0xFFu, b1 = (v >> (16 * j + 8)) & 0xFFu;
+                lo[2 * b + j] = pack_h2(fmaf(d1, u2f(b0 & 15u), -m1), fmaf(d1, u2f(b1 & 15u), -m1));
+                hi[2 * b + j] = pack_h2(fmaf(d2, u2f(b0 >> 4), -m2), fmaf(d2, u2f(b1 >> 4), -m2));
+            }
+        }
+        st_shared_v4(row + c * 2048, lo[0], lo[1], lo[2], lo[3]);
+        st_shared_v4(row + (4 + c) * 2048, hi[0], hi[1], hi[2], hi[3]);
+    }
+}
+
+struct GuRaw {
+    uint4 hdr, q0, q1;
+};
+
+__device__ __forceinline__ GuRaw load_gu_raw(const uint8_t *row, int s) {
+    const uint8_t *blk = row + (s >> 2) * MOE_Q4K_BYTES;
+    GuRaw r;
+    r.hdr = __ldg(reinterpret_cast<const uint4 *>(blk));
+    r.q0 = __ldg(reinterpret_cast<const uint4 *>(blk + 16 + 32 * (s & 3)));
+    r.q1 = __ldg(reinterpret_cast<const uint4 *>(blk + 32 + 32 * (s & 3)));
+    return r;
+}
+
+// Shared memory of k_gemm_gate_up: A[2 stages][gate, up][128 x 64 fp16]
+// (16 KB each), B[3][64 x 64 fp16] (8 KB each), barriers, TMEM address.
+#define GU_A_BYTES (GM_ROWS * GM_KS_GU * 2)
+#define GU_B_BYTES (GM_NT * GM_KS_GU * 2)
+#define GU_SMEM (4 * GU_A_BYTES + 3 * GU_B_BYTES + 128)
+
+__global__ void __launch_bounds__(GM_THREADS, 2) k_gemm_gate_up(
+    ExpertSrc src, const __half *__restrict__ xt, const int32_t *__restrict__ off,
+    const int32_t *__restrict__ cnt, const int32_t *__restrict__ tiles,
+    const int32_t *__restrict__ n_tiles, int n_embd, int n_ff, __half *__restrict__ at, int *err) {
+    extern __shared__ __align__(1024) uint8_t sm[];
+    const int i = blockIdx.y;
+    if (i >= *n_tiles) return;
+    uint8_t *sA = sm;                                   // [stage][mat] 16 KB
+    uint8_t *sB = sm + 4 * GU_A_BYTES;                  // [3] 8 KB
+    uint64_t *mma_done = reinterpret_cast<uint64_t *>(sB + 3 * GU_B_BYTES);   // [2]
+    uint64_t *b_full = mma_done + 2;                                           // [3]
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(b_full + 3);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tl = tiles[i], e = tl >> 16, tt = tl & 0xFFFF;
+    const int np = min(GM_NT, cnt[e] - tt * GM_NT);
+    const int N = (np + 15) & ~15;
+    const int r0 = blockIdx.x * GM_ROWS;
+    const int S = n_embd / GM_KS_GU;
+    const int32_t slot = src.table ? src.table[e] : src.ns;
+    const uint8_t *gbase = expert_base(src, 0, e, slot);
+    const uint8_t *ubase = expert_base(src, 1, e, slot);
+    if (!gbase || !ubase) {
+        if (tid == 0) atomicOr(err, MOE_DEV_ERR_INDEX);
+        return;
+    }
+    if (tid == 0) {
+        for (int q = 0; q < 2; ++q) mbar_init(&mma_done[q], 1);
+        for (int q = 0; q < 3; ++q) mbar_init(&b_full[q], 1);
+        fence_mbar_init();
+    }
+    if (warp == 0) tmem_alloc(tslot, 128);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;               // gate accumulator: columns 0..63, up: 64..127
+    const __half *xtile = xt + (size_t)i * n_embd * GM_NT;
+    if (tid == 0) {
+        mbar_arrive_expect_tx(&b_full[0], GU_B_BYTES);
+        bulk_g2s(sB, xtile, GU_B_BYTES, &b_full[0]);
+    }
+    const int mat = tid >> 7, m = tid & 127;
+    const size_t rb = (size_t)(n_embd / MOE_QK) * MOE_Q4K_BYTES;
+    const uint8_t *row = (mat ? ubase : gbase) + (size_t)(r0 + m) * rb;
+    const uint32_t idesc = idesc_f16(GM_ROWS, N);
+    bool ok = true;
+    GuRaw nxt = load_gu_raw(row, 0);
+    for (int s = 0; s < S; ++s) {
+        const GuRaw cur = nxt;
+        if (s + 1 < S) nxt = load_gu_raw(row, s + 1);
+        const int b = s & 1;
+        if (s >= 2 && !mbar_wait(&mma_done[b], ((s - 2) >> 1) & 1)) ok = false;
+        if (tid == 0 && s + 1 < S) {
+            // B buffer (s+1) % 3 was last read by the MMAs of stage s-2
+            const int nb = (s + 1) % 3;
+            mbar_arrive_expect_tx(&b_full[nb], GU_B_BYTES);
+            bulk_g2s(sB + nb * GU_B_BYTES, xtile + (size_t)(s + 1) * GM_NT * GM_KS_GU, GU_B_BYTES,
+                     &b_full[nb]);
+        }
+        deq_q4k_group(cur.hdr, cur.q0, cur.q1, s & 3, sA + (2 * b + mat) * GU_A_BYTES, m);
+        fence_proxy_async();
+        __syncthreads();
+        if (tid == 0) {
+            tc_fence_after();
+            if (mbar_wait(&b_full[s % 3], (s / 3) & 1)) {
+                const uint32_t aG = smem_u32(sA + (2 * b) * GU_A_BYTES);
+                const uint32_t aU = smem_u32(sA + (2 * b + 1) * GU_A_BYTES);
+                const uint32_t bB = smem_u32(sB + (s % 3) * GU_B_BYTES);
+#pragma unroll
+                for (int j = 0; j < GM_KS_GU / 16; ++j) {
+                    const uint64_t db = smem_desc(bB + j * 2 * (GM_NT * 16), GM_NT * 16, 128);
+                    tc_mma(tmem, smem_desc(aG + j * 2 * (GM_ROWS * 16), GM_ROWS * 16, 128), db,
+                           idesc, (s | j) != 0);
+                    tc_mma(tmem + 64, smem_desc(aU + j * 2 * (GM_ROWS * 16), GM_ROWS * 16, 128), db,
+                           idesc, (s | j) != 0);
+                }
+            } else {
+                ok = false;
+            }
+            tc_commit(&mma_done[b]);
+        }
+    }
+    if (!mbar_wait(&mma_done[(S - 1) & 1], ((S - 1) >> 1) & 1)) ok = false;
+    tc_fence_after();
+    if (warp < 4) {
+        // epilogue: row m = 32 warp + lane; act = silu(g) * u -> the down GEMM's
+        // operand tile: at[tile][stage r0/128][k/8 = m/8][n][m % 8]
+        const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16);
+        const int mm = warp * 32 + lane;
+        __half *dst = at + ((size_t)i * n_ff + r0) * GM_NT + (size_t)(mm >> 3) * GM_NT * 8 + (mm & 7);
+        for (int c0 = 0; c0 < N; c0 += 16) {
+            float g[16], u[16];
+            tmem_ld16(ta + c0, g);
+            tmem_ld16(ta + 64 + c0, u);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int n = c0 + j;
+                if (n < np) dst[(size_t)n * 8] = __float2half_rn(silu_mul(g[j], u[j]));
+            }
+        }
+    }
+    if (!ok && tid == 0) atomicOr(err, MOE_DEV_ERR_TIMEOUT);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) tmem_dealloc(tmem, 128);
+}
+
+// Q6_K half block h of super-block `blk` (2-byte aligned) -> quarters
+// q = 2p, 2p+1 (64 elements) of row m of a canonical 128-row tile at `A`
+// (LBO 2048): w = d * sc * q6 in fp32, rounded to fp16 once.
+__device__ __forceinline__ void deq_q6k_part(const uint32_t (&lo)[8], const uint32_t (&hi)[8],
+                                             const uint32_t (&qh)[8], const uint32_t (&sc)[2],
+                                             float d, int p, uint8_t *A, int m) {
+    uint8_t *row = A + (m >> 3) * 128 + (m & 7) * 16;
+#pragma unroll
+    for (int qq = 0; qq < 2; ++qq) {
+        const int q = 2 * p + qq;                      // quarter: elements 32q + l
+        const uint32_t(&src)[8] = qq ? hi : lo;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {                  // l = 8c .. 8c+7
+            const int g = (c >> 1) + 2 * q;            // scale byte (l / 16) + 2q
+            const float ws = d * (float)(int8_t)((sc[g >> 2] >> (8 * (g & 3))) & 0xFFu);
+            uint32_t o[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                float v2[2];
+#pragma unroll
+                for (int t = 0; t < 2; ++t) {
+                    const int l = 8 * c + 2 * j + t;
+                    const uint32_t nib = (src[l >> 2] >> (8 * (l & 3) + 4 * p)) & 15u;
+                    const uint32_t hb = (qh[l >> 2] >> (8 * (l & 3) + 2 * q)) & 3u;
+                    v2[t] = ws * (u2f(nib | (hb << 4)) - 32.0f);
+                }
+                o[j] = pack_h2(v2[0], v2[1]);
+            }
+            st_shared_v4(row + (4 * q + c) * 2048, o[0], o[1], o[2], o[3]);
+        }
+    }
+}
+
+// Shared memory of k_gemm_down: A[2][128 x 128 fp16] (32 KB each),
+// B[3][64 x 128 fp16] (16 KB each), barriers, TMEM address.
+#define DN_A_BYTES (GM_ROWS * GM_KS_DN * 2)
+#define DN_B_BYTES (GM_NT * GM_KS_DN * 2)
+#define DN_SMEM (2 * DN_A_BYTES + 3 * DN_B_BYTES + 128)
+
+__global__ void __launch_bounds__(GM_THREADS, 2) k_gemm_down(
+    ExpertSrc src, const __half *__restrict__ at, const int32_t *__restrict__ off,
+    const int32_t *__restrict__ cnt, const int32_t *__restrict__ tiles,
+    const int32_t *__restrict__ n_tiles, int n_embd, int n_ff, float *__restrict__ ypair,
+    int *err) {
+    extern __shared__ __align__(1024) uint8_t sm[];
+    const int i = blockIdx.y;
+    if (i >= *n_tiles) return;
+    uint8_t *sA = sm;                                   // [2] 32 KB
+    uint8_t *sB = sm + 2 * DN_A_BYTES;                  // [3] 16 KB
+    uint64_t *mma_done = reinterpret_cast<uint64_t *>(sB + 3 * DN_B_BYTES);   // [2]
+    uint64_t *b_full = mma_done + 2;                                           // [3]
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(b_full + 3);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tl = tiles[i], e = tl >> 16, tt = tl & 0xFFFF;
+    const int pos0 = off[e] + tt * GM_NT;
+    const int np = min(GM_NT, cnt[e] - tt * GM_NT);
+    const int N = (np + 15) & ~15;
+    const int r0 = blockIdx.x * GM_ROWS;
+    const int S = n_ff / GM_KS_DN;
+    const int32_t slot = src.table ? src.table[e] : src.ns;
+    const uint8_t *dbase = expert_base(src, 2, e, slot);
+    if (!dbase) {
+        if (tid == 0) atomicOr(err, MOE_DEV_ERR_INDEX);
+        return;
+    }
+    if (tid == 0) {
+        for (int q = 0; q < 2; ++q) mbar_init(&mma_done[q], 1);
+        for (int q = 0; q < 3; ++q) mbar_init(&b_full[q], 1);
+        fence_mbar_init();
+    }
+    if (warp == 0) tmem_alloc(tslot, 64);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    const __half *atile = at + (size_t)i * n_ff * GM_NT;
+    if (tid == 0) {
+        mbar_arrive_expect_tx(&b_full[0], DN_B_BYTES);
+        bulk_g2s(sB, atile, DN_B_BYTES, &b_full[0]);
+    }
+    const int p = tid >> 7, m = tid & 127;
+    const size_t rb = (size_t)(n_ff / MOE_QK) * MOE_Q6K_BYTES;
+    const uint8_t *row = dbase + (size_t)(r0 + m) * rb;
+    const uint32_t idesc = idesc_f16(GM_ROWS, N);
+    bool ok = true;
+    for (int s = 0; s < S; ++s) {
+        const uint8_t *blk = row + (s >> 1) * MOE_Q6K_BYTES;
+        const int h = s & 1;
+        uint32_t lo[8], hi[8], qh[8], sc[2];
+        ldw_a2<8>(blk + 64 * h, lo);
+        ldw_a2<8>(blk + 64 * h + 32, hi);
+        ldw_a2<8>(blk + 128 + 32 * h, qh);
+        ldw_a2<2>(blk + 192 + 8 * h, sc);
+        const float d = h2f(*reinterpret_cast<const uint16_t *>(blk + 208));
+        const int b = s & 1;
+        if (s >= 2 && !mbar_wait(&mma_done[b], ((s - 2) >> 1) & 1)) ok = false;
+        if (tid == 0 && s + 1 < S) {
+            const int nb = (s + 1) % 3;
+            mbar_arrive_expect_tx(&b_full[nb], DN_B_BYTES);
+            bulk_g2s(sB + nb * DN_B_BYTES, atile + (size_t)(s + 1) * GM_NT * GM_KS_DN, DN_B_BYTES,
+                     &b_full[nb]);
+        }
+        deq_q6k_part(lo, hi, qh, sc, d, p, sA + b * DN_A_BYTES, m);
+        fence_proxy_async();
+        __syncthreads();
+        if (tid == 0) {
+            tc_fence_after();
+            if (mbar_wait(&b_full[s % 3], (s / 3) & 1)) {
+                const uint32_t aA = smem_u32(sA + b * DN_A_BYTES);
+                const uint32_t bB = smem_u32(sB + (s % 3) * DN_B_BYTES);
+#pragma unroll
+                for (int j = 0; j < GM_KS_DN / 16; ++j)
+                    tc_mma(tmem, smem_desc(aA + j * 2 * (GM_ROWS * 16), GM_ROWS * 16, 128),
+                           smem_desc(bB + j * 2 * (GM_NT * 16), GM_NT * 16, 128), idesc,
+                           (s | j) != 0);
+            } else {
+                ok = false;
+            }
+            tc_commit(&mma_done[b]);
+        }
+    }
+    if (!mbar_wait(&mma_done[(S - 1) & 1], ((S - 1) >> 1) & 1)) ok = false;
+    tc_fence_after();
+    if (warp < 4) {
+        const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16);
+        const int hrow = r0 + warp * 32 + lane;
+        for (int c0 = 0; c0 < N; c0 += 16) {
+            float v[16];
+            tmem_ld16(ta + c0, v);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int n = c0 + j;
+                if (n < np) ypair[(size_t)(pos0 + n) * n_embd + hrow] = v[j];
+            }
+        }
+    }
+    if (!ok && tid == 0) atomicOr(err, MOE_DEV_ERR_TIMEOUT);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) tmem_dealloc(tmem, 64);
+}
+
+size_t gemm_scratch_halves(int n_expert, int P, int n_embd, int n_ff) {
+    const size_t tiles = (size_t)group_max_tiles(n_expert, P, GM_NT);
+    return tiles * GM_NT * ((size_t)n_embd + n_ff);
+}
+
+cudaError_t launch_experts_gemm(const ExpertSrc &src, const float *x, const GroupBufs &g,
+                                int n_tok, int k, int n_embd, int n_ff, int down_type,
+                                const float *w, void *scratch_v, float *ypair, const float *resid,
+                                float *y, int *err, cudaStream_t s) {
+    __half *scratch = static_cast<__half *>(scratch_v);
+    if (down_type != MOE_QT_Q6K || n_ff % GM_KS_DN || n_embd % GM_ROWS || n_ff % GM_ROWS)
+        return cudaErrorInvalidValue;
+    const int P = n_tok * k;
+    const int maxt = group_max_tiles(src.n_expert, P, GM_NT);
+    __half *xt = scratch;
+    __half *at = scratch + (size_t)maxt * GM_NT * n_embd;
+    cudaError_t e;
+    k_gather_x16<<<maxt, 256, 0, s>>>(x, g.off, g.cnt, g.pos_pair, g.tiles, g.n_tiles, k, n_embd, xt);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    if ((e = cudaFuncSetAttribute(k_gemm_gate_up, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  GU_SMEM)) != cudaSuccess)
+        return e;
+    if ((e = cudaFuncSetAttribute(k_gemm_down, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  DN_SMEM)) != cudaSuccess)
+        return e;
+    k_gemm_gate_up<<<dim3(n_ff / GM_ROWS, maxt), GM_THREADS, GU_SMEM, s>>>(
+        src, xt, g.off, g.cnt, g.tiles, g.n_tiles, n_embd, n_ff, at, err);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    k_gemm_down<<<dim3(n_embd / GM_ROWS, maxt), GM_THREADS, DN_SMEM, s>>>(
+        src, at, g.off, g.cnt, g.tiles, g.n_tiles, n_embd, n_ff, ypair, err);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    return launch_combine(ypair, g.pair_pos, w, n_tok, k, n_embd, resid, y, s);
+}
+
+}  // namespace moe

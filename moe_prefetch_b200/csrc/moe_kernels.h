@@ -75,6 +75,19 @@ cudaError_t launch_experts_grouped(const ExpertSrc &src, const float *x, const G
 cudaError_t launch_combine(const float *ypair, const int32_t *pair_pos, const float *w, int n_tok,
                            int k, int n_embd, const float *resid, float *y, cudaStream_t s);
 
+// ---- tensor-core grouped GEMM (moe_gemm.cu) --------------------------------
+
+#define GM_NT 64       // pairs per token tile of the GEMM (MMA N <= 64)
+
+// fp16 elements of scratch the GEMM needs for P pairs (token tiles + activation tiles)
+size_t gemm_scratch_halves(int n_expert, int P, int n_embd, int n_ff);
+// gate/up + down on tcgen05 over pairs grouped with tile GM_NT, then the
+// combine.  Q6_K down only; n_embd and n_ff multiples of 128.
+cudaError_t launch_experts_gemm(const ExpertSrc &src, const float *x, const GroupBufs &g,
+                                int n_tok, int k, int n_embd, int n_ff, int down_type,
+                                const float *w, void *scratch, float *ypair, const float *resid,
+                                float *y, int *err, cudaStream_t s);
+
 // ---- persistent decode (moe_decode.cu) ------------------------------------
 
 struct LayerDesc {

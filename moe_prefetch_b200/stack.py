@@ -160,6 +160,20 @@ class MoeStack:
                                             _ptr(w), _stream(stream)), "moe_layer_forward")
         return y, ids, w
 
+    def layer_forward_path(self, layer, x, path="auto", stream=None):
+        """layer_forward with the expert arithmetic chosen: "gemv" (Q8_1
+        activations, int8 dots), "gemm" (tcgen05 grouped GEMM, fp16 operands,
+        fp32 sums) or "auto" (GEMM when the batch gives >= 4 pairs per expert)."""
+        x = x.contiguous()
+        n_tok = x.shape[0]
+        y = torch.empty_like(x)
+        ids = torch.empty(n_tok, self.n_used, dtype=torch.int32, device=x.device)
+        w = torch.empty(n_tok, self.n_used, dtype=torch.float32, device=x.device)
+        code = {"auto": 0, "gemv": 1, "gemm": 2}[path]
+        self._ck(self.lib.moe_layer_forward_path(self.ctx, layer, _ptr(x), _ptr(y), n_tok, _ptr(ids),
+                                                 _ptr(w), code, _stream(stream)), "moe_layer_forward_path")
+        return y, ids, w
+
     def layer_forward_noalloc(self, layer, x, y, ids=None, w=None, stream=None):
         """layer_forward for callers that cannot allocate device memory while
         they run (their device memory is committed up front).  Neither the

@@ -637,6 +637,68 @@ void or_moe_experts(const float *x, int n_tok, int n_embd, int n_ff, int k,
     free(rows);
 }
 
+/* The expert half with unquantised activations: the fp32-accumulated
+ * reference of a GEMM path.  Weights are dequantised exactly (ggml block
+ * layout, as or_dequantize_*), x is used as given, every dot accumulates in
+ * double, act = silu(g) * u in double, and y = sum_i w_i * row_i in double.
+ * Follows the op order of ggml_cpu_moe_rows (patches/0008:186-251: up, gate,
+ * swiglu(gate, up), down) without its Q8_K activation rounding.  Each expert
+ * that is routed to is dequantised once. */
+void or_moe_experts_f32(const float *x, int n_tok, int n_embd, int n_ff, int n_expert, int k,
+                        const int32_t *ids, const float *w, const uint8_t *gate,
+                        const uint8_t *up, const uint8_t *down, int down_type, float *y_out,
+                        int n_threads) {
+    const size_t grb = row_bytes(OR_QTYPE_Q4_K, n_embd), drb = row_bytes(down_type, n_ff);
+    const size_t gexp = grb * (size_t)n_ff, dexp = drb * (size_t)n_embd;
+    double *rows = (double *)calloc((size_t)n_tok * k * n_embd, sizeof(double));
+#ifdef _OPENMP
+#pragma omp parallel for num_threads(n_threads > 0 ? n_threads : 1) schedule(dynamic, 1)
+#endif
+    for (int e = 0; e < n_expert; ++e) {
+        int used = 0;
+        for (int tk = 0; tk < n_tok * k && !used; ++tk) used = ids[tk] == e;
+        if (!used) continue;
+        float *wg = (float *)malloc(sizeof(float) * (size_t)n_ff * n_embd);
+        float *wu = (float *)malloc(sizeof(float) * (size_t)n_ff * n_embd);
+        float *wd = (float *)malloc(sizeof(float) * (size_t)n_embd * n_ff);
+        double *act = (double *)malloc(sizeof(double) * (size_t)n_ff);
+        for (int i = 0; i < n_ff; ++i) {
+            or_dequantize_q4_K(gate + e * gexp + i * grb, wg + (size_t)i * n_embd, n_embd);
+            or_dequantize_q4_K(up + e * gexp + i * grb, wu + (size_t)i * n_embd, n_embd);
+        }
+        for (int h = 0; h < n_embd; ++h) deq_row(down_type, down + e * dexp + h * drb,
+                                                 wd + (size_t)h * n_ff, n_ff);
+        for (int tk = 0; tk < n_tok * k; ++tk) {
+            if (ids[tk] != e) continue;
+            const float *xt = x + (size_t)(tk / k) * n_embd;
+            for (int i = 0; i < n_ff; ++i) {
+                double g = 0.0, u = 0.0;
+                const float *rg = wg + (size_t)i * n_embd, *ru = wu + (size_t)i * n_embd;
+                for (int j = 0; j < n_embd; ++j) {
+                    g += (double)rg[j] * xt[j];
+                    u += (double)ru[j] * xt[j];
+                }
+                act[i] = g / (1.0 + exp(-g)) * u;
+            }
+            double *out = rows + (size_t)tk * n_embd;
+            for (int h = 0; h < n_embd; ++h) {
+                double acc = 0.0;
+                const float *rd = wd + (size_t)h * n_ff;
+                for (int i = 0; i < n_ff; ++i) acc += (double)rd[i] * act[i];
+                out[h] = acc;
+            }
+        }
+        free(wg); free(wu); free(wd); free(act);
+    }
+    for (int t = 0; t < n_tok; ++t)
+        for (int h = 0; h < n_embd; ++h) {
+            double acc = 0.0;
+            for (int i = 0; i < k; ++i) acc += (double)w[t * k + i] * rows[((size_t)t * k + i) * n_embd + h];
+            y_out[(size_t)t * n_embd + h] = (float)acc;
+        }
+    free(rows);
+}
+
 void or_moe_layer(const float *x, int n_tok, int n_embd, int n_ff, int n_expert,
                   int k, const float *router_w, const float *prior,
                   const uint8_t *gate, const uint8_t *up, const uint8_t *down,

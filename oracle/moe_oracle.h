@@ -120,6 +120,12 @@ void or_moe_layer(const float *x, int n_tok, int n_embd, int n_ff, int n_expert,
                   const uint8_t *gate, const uint8_t *up, const uint8_t *down,
                   int down_type, int32_t *ids_out, float *w_out, float *y_out,
                   int n_threads);
+/* The expert half with unquantised activations and exact dequantised weights,
+ * fp64 accumulation: the reference of the fp16 tensor-core GEMM path. */
+void or_moe_experts_f32(const float *x, int n_tok, int n_embd, int n_ff, int n_expert, int k,
+                        const int32_t *ids, const float *w, const uint8_t *gate,
+                        const uint8_t *up, const uint8_t *down, int down_type, float *y_out,
+                        int n_threads);
 /* The expert half alone: given ids / w [n_tok][k], y = sum_i w_i row(ids_i, x). */
 void or_moe_experts(const float *x, int n_tok, int n_embd, int n_ff, int k,
                     const int32_t *ids, const float *w, const uint8_t *gate,

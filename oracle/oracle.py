@@ -75,6 +75,9 @@ def _declare(L):
     layer_args = [P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, P, P, P, P, P,
                   C.c_int, P, P, P, C.c_int]
     L.or_moe_layer.argtypes = layer_args
+    L.or_moe_experts_f32.argtypes = [P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, P, P, P, P,
+                                     P, C.c_int, P, C.c_int]
+    L.or_moe_experts_f32.restype = None
     L.or_moe_experts.argtypes = [P, C.c_int, C.c_int, C.c_int, C.c_int, P, P, P, P, P, C.c_int,
                                  P, C.c_int]
     L.or_moe_layer_q8K.argtypes = layer_args
@@ -247,8 +250,11 @@ def moe_layer(x, router_w, gate, up, down, down_type, n_ff, k, prior=None,
     return ids, w, y
 
 
-def moe_experts(x, ids, w, gate, up, down, down_type, n_ff, n_threads=None):
-    """y [n_tok, n_embd] = sum_i w[t, i] * expert_row(ids[t, i], x[t])."""
+def moe_experts(x, ids, w, gate, up, down, down_type, n_ff, n_threads=None, path="q8_1"):
+    """y [n_tok, n_embd] = sum_i w[t, i] * expert_row(ids[t, i], x[t]).
+    path "q8_1": Q8_1 activations (the GEMV kernels' arithmetic); "f32":
+    unquantised activations, exact weights, fp64 accumulation (the reference
+    of the fp16 tensor-core GEMM)."""
     x = _c(np.atleast_2d(x), np.float32)
     n_tok, n_embd = x.shape
     ids = _c(np.atleast_2d(ids), np.int32)
@@ -256,6 +262,11 @@ def moe_experts(x, ids, w, gate, up, down, down_type, n_ff, n_threads=None):
     k = ids.shape[1]
     gate, up, down = (_c(a, np.uint8) for a in (gate, up, down))
     y = np.empty((n_tok, n_embd), np.float32)
+    if path == "f32":
+        lib().or_moe_experts_f32(_p(x), n_tok, n_embd, n_ff, gate.shape[0], k, _p(ids), _p(w),
+                                 _p(gate), _p(up), _p(down), down_type, _p(y),
+                                 n_threads or os.cpu_count())
+        return y
     lib().or_moe_experts(_p(x), n_tok, n_embd, n_ff, k, _p(ids), _p(w), _p(gate), _p(up),
                          _p(down), down_type, _p(y), n_threads or os.cpu_count())
     return y
