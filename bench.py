@@ -339,6 +339,93 @@ def run_config2(args):
 
 
 # ---------------------------------------------------------------------------
+# config 3: batched decode and prefill, expert-parallel over the ranks
+# ---------------------------------------------------------------------------
+def run_config3(args):
+    """Config 3: the config-1 stack, expert-parallel (rank g owns experts
+    [g E/N, (g+1) E/N) of every layer; NCCL all-to-all dispatch and combine).
+    Workloads: 32 sequences decoding 128 tokens (32 / N home tokens per rank
+    per step) and one 512-token prefill chunk (512 / N per rank).  Inputs are
+    i.i.d. N(0, 1) RMS-normed rows.  Total work is fixed as N grows (strong
+    scaling).  Device time is CUDA events on each rank, max over ranks.  One
+    JSON line per workload from rank 0."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    from moe_prefetch_b200.ep import ExpertParallelStack
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    n_layers = args.layers
+    ep = ExpertParallelStack(n_layers)
+    ep.synth(seed=11)
+    stream = torch.cuda.current_stream()
+
+    def rows(n, seed):
+        rng = np.random.default_rng(seed)
+        h = rng.standard_normal((n, N_EMBD))
+        return (h / np.sqrt((h ** 2).mean(-1, keepdims=True))).astype(np.float32)
+
+    def timed(x, steps, warmup, path):
+        for _ in range(warmup):
+            for il in range(n_layers):
+                ep.layer_forward(il, x, path)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            for il in range(n_layers):
+                ep.layer_forward(il, x, path)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1)], device="cuda", dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t[0])
+
+    lines = []
+    dec_seqs, dec_steps = 32, args.c3_decode_steps
+    if dec_seqs % world == 0:
+        x = torch.from_numpy(rows(dec_seqs, 500)[rank::world].copy()).cuda()
+        ms = timed(x, dec_steps, args.warmup, "auto")
+        lines.append({
+            "metric": "config3 expert-parallel batched decode", "value": dec_seqs * dec_steps / (ms / 1e3),
+            "unit": "tok/s", "n_gpus": world, "steps": dec_steps, "warmup": args.warmup,
+            "ms_per_step": ms / dec_steps, "higher_is_better": True, "scaling": "strong",
+            "config": {"workload": f"config3 decode: {dec_seqs} sequences x {dec_steps} steps, "
+                                   f"{n_layers} layers, EP {N_EXPERT // world} experts/GPU",
+                       "path": "auto (grouped GEMV at 32 tokens)", "data": "synthetic"}})
+    pre_tok, chunks = 512, args.c3_prefill_chunks
+    if pre_tok % world == 0:
+        x = torch.from_numpy(rows(pre_tok, 501)[rank::world].copy()).cuda()
+        ms = timed(x, chunks, max(1, args.warmup), "auto")
+        flops = 2.0 * pre_tok * TOP_K * 3 * N_EMBD * N_FF * n_layers * chunks
+        lines.append({
+            "metric": "config3 expert-parallel prefill", "value": pre_tok * chunks / (ms / 1e3),
+            "unit": "tok/s", "n_gpus": world, "steps": chunks, "warmup": max(1, args.warmup),
+            "ms_per_step": ms / chunks, "higher_is_better": True, "scaling": "strong",
+            "expert_tflops_whole_job": flops / (ms / 1e3) / 1e12,
+            "config": {"workload": f"config3 prefill: one {pre_tok}-token chunk per step, "
+                                   f"{n_layers} layers, EP {N_EXPERT // world} experts/GPU",
+                       "path": "auto (tcgen05 grouped GEMM)", "data": "synthetic"}})
+    if rank == 0:
+        for ln in lines:
+            print(json.dumps(ln), flush=True)
+    ep.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+# ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
 def main():
@@ -353,7 +440,9 @@ def main():
     ap.add_argument("--ref-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--workload", default="config1", choices=["config1", "config2"])
+    ap.add_argument("--workload", default="config1", choices=["config1", "config2", "config3"])
+    ap.add_argument("--c3-decode-steps", type=int, default=128)
+    ap.add_argument("--c3-prefill-chunks", type=int, default=4)
     ap.add_argument("--c2-warm", type=int, default=64)
     ap.add_argument("--c2-tokens", type=int, default=128)
     args = ap.parse_args()
@@ -361,6 +450,8 @@ def main():
         return run_reference(args)
     if args.workload == "config2":
         return run_config2(args)
+    if args.workload == "config3":
+        return run_config3(args)
 
     import torch
     import torch.distributed as dist

@@ -169,6 +169,37 @@ int moe_layer_forward(moe_ctx *ctx, int layer, const float *x, float *y, int n_t
 int moe_layer_forward_path(moe_ctx *ctx, int layer, const float *x, float *y, int n_tok,
                            int32_t *ids, float *w, int path, void *stream);
 
+/* ---- expert parallelism (batched decode and prefill over several GPUs) --------- */
+/* These three calls have no counterpart in the reference, which runs on one
+ * GPU.  Rank g of `world` owns experts [g*E/world, (g+1)*E/world) of every
+ * layer (its context holds only those in slots).  Per layer:
+ *   moe_ep_route_pack -> all-to-all of send_count, then of send_ids/send_x
+ *   (NCCL, by the caller) -> moe_experts_rows on the received rows ->
+ *   all-to-all of the rows back -> moe_ep_combine.
+ * The result equals moe_layer_forward_path on one GPU: bit for bit with
+ * the GEMV path. */
+
+/* Route the n_tok home tokens x [n_tok][n_embd] (no cache prior, no
+ * observation): ids/w [n_tok][n_used].  Pack the pairs for their owners in
+ * rank order, pair order within a rank:
+ *   send_count [world] (device), pos [n_tok*n_used] (send slot of pair
+ *   t*n_used + r, -1 for an id out of range), send_ids / send_x
+ *   [n_tok*n_used][...] (expert id and token row of each slot). */
+int moe_ep_route_pack(moe_ctx *ctx, int layer, const float *x, int n_tok, int world,
+                      int32_t *ids, float *w, int32_t *send_count, int32_t *pos,
+                      int32_t *send_ids, float *send_x, void *stream);
+
+/* The expert half for n_rows received rows: y_rows[i] = expert ids[i] applied
+ * to x_rows[i], unweighted (path as moe_layer_forward_path; AUTO takes the
+ * GEMM from 4 rows per slot of the layer on). */
+int moe_experts_rows(moe_ctx *ctx, int layer, const float *x_rows, const int32_t *ids,
+                     int n_rows, float *y_rows, int path, void *stream);
+
+/* out[t] = sum over r in rank order of w[t][r] * y_rows[pos[t*n_used + r]]:
+ * the combine of moe_layer_forward over the rows that came back. */
+int moe_ep_combine(moe_ctx *ctx, const float *y_rows, const int32_t *pos, const float *w,
+                   int n_tok, float *out, void *stream);
+
 /* moe_layer_forward that allocates no device memory.  This entry point has no
  * counterpart in the reference, whose CPU expert path allocates nothing on
  * the GPU.

@@ -59,6 +59,7 @@ struct moe_ctx {
     // per-pair down rows [P][n_embd]
     int32_t *s_group = nullptr;
     GroupBufs grp{};
+    int32_t *s_dest = nullptr;         // expert parallelism: destination rank per pair
     float *s_ypair = nullptr;
     // tensor-core GEMM operand tiles (fp16)
     void *s_gemm = nullptr;
@@ -482,8 +483,8 @@ static int ensure_scratch(moe_ctx *c, int n_tok) {
     c->s_group = nullptr; c->s_ypair = nullptr;
     const int K = c->cfg.n_used, E = c->cfg.n_expert;
     const size_t P = (size_t)n_tok * K;
-    // cnt [E] | off [E + 1] | pair_pos [P] | pos_pair [P] | tiles [E + P] | n_tiles [1]
-    const size_t gints = (size_t)E + (E + 1) + P + P + (E + P) + 1;
+    // cnt [E] | off [E + 1] | pair_pos [P] | pos_pair [P] | tiles [E + P] | n_tiles [1] | dest [P]
+    const size_t gints = (size_t)E + (E + 1) + P + P + (E + P) + 1 + P;
     if (cudaMalloc(&c->s_ids, sizeof(int32_t) * P) != cudaSuccess ||
         cudaMalloc(&c->s_w, sizeof(float) * P) != cudaSuccess ||
         cudaMalloc(&c->s_act, sizeof(float) * P * c->cfg.n_ff) != cudaSuccess ||
@@ -498,7 +499,8 @@ static int ensure_scratch(moe_ctx *c, int n_tok) {
     c->grp.pair_pos = g; g += P;
     c->grp.pos_pair = g; g += P;
     c->grp.tiles = g; g += E + P;
-    c->grp.n_tiles = g;
+    c->grp.n_tiles = g; g += 1;
+    c->s_dest = g;
     c->s_cap_tok = n_tok;
     return MOE_OK;
 }
@@ -582,6 +584,73 @@ extern "C" int moe_layer_forward_path(moe_ctx *c, int layer, const float *x, flo
     CK(launch_group(ids_d, n_tok * g.n_used, g.n_expert, GM_NT, c->grp, c->err, s));
     CK(launch_experts_gemm(make_src(c, layer), x, c->grp, n_tok, g.n_used, g.n_embd, g.n_ff,
                            g.down_type, w_d, c->s_gemm, c->s_ypair, nullptr, y, c->err, s));
+    return MOE_OK;
+}
+
+// ---- expert parallelism -------------------------------------------------------
+
+extern "C" int moe_ep_route_pack(moe_ctx *c, int layer, const float *x, int n_tok, int world,
+                                 int32_t *ids, float *w, int32_t *send_count, int32_t *pos,
+                                 int32_t *send_ids, float *send_x, void *stream) {
+    if (!c || !x || !ids || !w || !send_count || !pos || !send_ids || !send_x || n_tok <= 0 ||
+        layer < 0 || layer >= c->cfg.n_layers)
+        return fail(c, MOE_ERR_ARG, "moe_ep_route_pack: bad argument");
+    const moe_cfg &g = c->cfg;
+    if (world < 1 || world > 256 || g.n_expert % world)
+        return fail(c, MOE_ERR_ARG, "moe_ep_route_pack: world %d does not divide %d experts", world,
+                    g.n_expert);
+    CK(cudaSetDevice(g.device));
+    const int r = ensure_scratch(c, n_tok);
+    if (r != MOE_OK) return r;
+    cudaStream_t s = (cudaStream_t)stream;
+    const int32_t *table = c->st.table + (size_t)layer * g.n_expert;
+    CK(launch_router(c->router + (size_t)layer * g.n_expert * g.n_embd, x, n_tok, g.n_expert, g.n_embd,
+                     table, c->L[layer].ns, 0.0f, 0, g.n_used, ids, w, nullptr, &c->st, -1, s));
+    GroupBufs gg = c->grp;
+    gg.cnt = send_count;
+    gg.pair_pos = pos;
+    CK(launch_ep_pack(ids, x, n_tok, g.n_used, g.n_expert, g.n_embd, world, c->s_dest, gg, send_ids,
+                      send_x, c->err, s));
+    return MOE_OK;
+}
+
+extern "C" int moe_experts_rows(moe_ctx *c, int layer, const float *x_rows, const int32_t *ids,
+                                int n_rows, float *y_rows, int path, void *stream) {
+    if (!c || n_rows < 0 || layer < 0 || layer >= c->cfg.n_layers || (n_rows && (!x_rows || !ids || !y_rows)))
+        return fail(c, MOE_ERR_ARG, "moe_experts_rows: bad argument");
+    if (n_rows == 0) return MOE_OK;
+    const moe_cfg &g = c->cfg;
+    const bool gemm_ok = g.down_type == MOE_QTYPE_Q6_K && g.n_ff % 128 == 0 && g.n_embd % 128 == 0;
+    if (path == MOE_PATH_AUTO)
+        path = gemm_ok && n_rows >= 4 * c->L[layer].ns ? MOE_PATH_GEMM : MOE_PATH_GEMV;
+    if (path != MOE_PATH_GEMV && path != MOE_PATH_GEMM)
+        return fail(c, MOE_ERR_ARG, "moe_experts_rows: unknown path %d", path);
+    if (path == MOE_PATH_GEMM && !gemm_ok)
+        return fail(c, MOE_ERR_UNSUPPORTED, "the GEMM path needs Q6_K down weights and n_ff, n_embd multiples of 128");
+    CK(cudaSetDevice(g.device));
+    const int n_tok_eq = (n_rows + g.n_used - 1) / g.n_used;   // scratch is sized in tokens of n_used pairs
+    int r = ensure_scratch(c, n_tok_eq);
+    if (r != MOE_OK) return r;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (path == MOE_PATH_GEMV) {
+        CK(launch_group(ids, n_rows, g.n_expert, GROUP_TILE, c->grp, c->err, s));
+        CK(launch_experts_grouped(make_src(c, layer), x_rows, c->grp, n_rows, 1, g.n_embd, g.n_ff,
+                                  g.down_type, nullptr, c->s_act, c->s_ypair, nullptr, y_rows, c->err, s));
+    } else {
+        if ((r = ensure_gemm_scratch(c, n_tok_eq)) != MOE_OK) return r;
+        CK(launch_group(ids, n_rows, g.n_expert, GM_NT, c->grp, c->err, s));
+        CK(launch_experts_gemm(make_src(c, layer), x_rows, c->grp, n_rows, 1, g.n_embd, g.n_ff,
+                               g.down_type, nullptr, c->s_gemm, c->s_ypair, nullptr, y_rows, c->err, s));
+    }
+    return MOE_OK;
+}
+
+extern "C" int moe_ep_combine(moe_ctx *c, const float *y_rows, const int32_t *pos, const float *w,
+                              int n_tok, float *out, void *stream) {
+    if (!c || !pos || !w || !out || n_tok <= 0) return fail(c, MOE_ERR_ARG, "moe_ep_combine: bad argument");
+    CK(cudaSetDevice(c->cfg.device));
+    CK(launch_combine(y_rows, pos, w, n_tok, c->cfg.n_used, c->cfg.n_embd, nullptr, out,
+                      (cudaStream_t)stream));
     return MOE_OK;
 }
 

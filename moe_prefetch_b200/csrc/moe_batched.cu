@@ -218,8 +218,9 @@ __global__ void __launch_bounds__(256) k_down_grouped(ExpertSrc src, const float
 }
 
 // y[t][h] = sum over ranks r in order of w[t][r] * ypair[pair_pos[t*k + r]][h]
-// (an fma chain from 0, then + resid): the per-pair kernel's combine.  grid
-// (ceil(n_embd / 256), n_tok); block 256.
+// (an fma chain from 0, then + resid): the per-pair kernel's combine.  With
+// w == null (k == 1) the row is copied unweighted.  grid (ceil(n_embd / 256),
+// n_tok); block 256.
 __global__ void __launch_bounds__(256) k_combine(const float *__restrict__ ypair,
                                                  const int32_t *__restrict__ pair_pos,
                                                  const float *__restrict__ w, int k, int n_embd,
@@ -227,6 +228,11 @@ __global__ void __launch_bounds__(256) k_combine(const float *__restrict__ ypair
                                                  float *__restrict__ y) {
     const int t = blockIdx.y, h = blockIdx.x * blockDim.x + threadIdx.x;
     if (h >= n_embd) return;
+    if (!w) {   // unweighted (k == 1): the row itself, for an expert-parallel owner
+        const int pos = pair_pos[t];
+        y[(size_t)t * n_embd + h] = pos >= 0 ? ypair[(size_t)pos * n_embd + h] : 0.0f;
+        return;
+    }
     float acc = 0.0f;
     for (int r = 0; r < k; ++r) {
         const int pos = pair_pos[(size_t)t * k + r];

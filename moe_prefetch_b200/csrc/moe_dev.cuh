@@ -76,6 +76,7 @@ __device__ __forceinline__ float router_dot_warp(const float *__restrict__ w,
                                                  const float *__restrict__ x, int n_embd,
                                                  int lane) {
     float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+#pragma unroll 16
     for (int kk = 0; kk < n_embd / 128; ++kk) {
         const int j = 128 * kk + 4 * lane;
         const float4 wv = *reinterpret_cast<const float4 *>(w + j);

@@ -193,6 +193,65 @@ __global__ void __launch_bounds__(512) k_router(const float *__restrict__ W,
     }
 }
 
+// Router for a batch (no prior, no observation: both apply to single tokens
+// only).  grid ceil(n_tok / RB_TOK); block 512.  The CTA keeps RB_TOK token
+// rows in shared memory.  Warp w takes experts w, w + 16, ...: it loads its
+// lanes' slice of the router row once (n_embd == 2048: 16 float4 per lane)
+// and runs the four fma chains of router_dot_warp for every token.  Every
+// logit is therefore computed in router_dot_warp's order, bit-identical to
+// k_router.  Then warp t selects for token t (router_select_warp).
+#define RB_TOK 8
+
+__global__ void __launch_bounds__(512) k_router_batch(const float *__restrict__ W,
+                                                      const float *__restrict__ x, int n_tok,
+                                                      int n_expert, int k,
+                                                      int32_t *__restrict__ ids,
+                                                      float *__restrict__ w) {
+    extern __shared__ __align__(16) float sm[];
+    float *xs = sm;                                   // [RB_TOK][2048]
+    float *lg = sm + RB_TOK * 2048;                   // [RB_TOK][n_expert]
+    const int t0 = blockIdx.x * RB_TOK;
+    const int nt = min(RB_TOK, n_tok - t0);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int i = threadIdx.x; i < nt * 512; i += blockDim.x)
+        reinterpret_cast<float4 *>(xs)[i] = reinterpret_cast<const float4 *>(x + (size_t)t0 * 2048)[i];
+    __syncthreads();
+    for (int e = warp; e < n_expert; e += nw) {
+        float4 wv[16];
+#pragma unroll
+        for (int kk = 0; kk < 16; ++kk)
+            wv[kk] = __ldg(reinterpret_cast<const float4 *>(W + (size_t)e * 2048 + 128 * kk + 4 * lane));
+        for (int t = 0; t < nt; ++t) {
+            const float *xt = xs + t * 2048;
+            float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+#pragma unroll
+            for (int kk = 0; kk < 16; ++kk) {
+                const float4 xv = *reinterpret_cast<const float4 *>(xt + 128 * kk + 4 * lane);
+                a0 = __fmaf_rn(wv[kk].x, xv.x, a0);
+                a1 = __fmaf_rn(wv[kk].y, xv.y, a1);
+                a2 = __fmaf_rn(wv[kk].z, xv.z, a2);
+                a3 = __fmaf_rn(wv[kk].w, xv.w, a3);
+            }
+            float v = __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(MOE_FULL, v, off));
+            if (lane == 0) lg[t * n_expert + e] = v;
+        }
+    }
+    __syncthreads();
+    if (warp < nt) {
+        __shared__ int32_t sids[RB_TOK][MOE_KMAX];
+        __shared__ float sw[RB_TOK][MOE_KMAX];
+        router_select_warp(lg + warp * n_expert, n_expert, nullptr, 0, 0.0f, false, k, sids[warp],
+                           sw[warp], lane);
+        __syncwarp();
+        if (lane < k) {
+            ids[(size_t)(t0 + warp) * k + lane] = sids[warp][lane];
+            w[(size_t)(t0 + warp) * k + lane] = sw[warp][lane];
+        }
+    }
+}
+
 // ===========================================================================
 // gate/up GEMV with fused SiLU*mul (stand-alone; direct global loads)
 // grid: (ceil(n_ff / GU_ROWS), n_tok * k); block 256 (8 warps)
@@ -511,6 +570,14 @@ cudaError_t launch_router(const float *W, const float *x, int n_tok, int n_exper
                           const int32_t *table, int ns, float delta, int use_prior, int k,
                           int32_t *ids, float *w, float *logits, const SlotState *st,
                           int observe_layer_idx, cudaStream_t s) {
+    if (n_tok > 1 && n_embd == 2048 && !use_prior && observe_layer_idx < 0 && !logits) {
+        const size_t sm = sizeof(float) * ((size_t)RB_TOK * 2048 + (size_t)RB_TOK * n_expert);
+        cudaError_t e = cudaFuncSetAttribute(k_router_batch, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)sm);
+        if (e != cudaSuccess) return e;
+        k_router_batch<<<(n_tok + RB_TOK - 1) / RB_TOK, 512, sm, s>>>(W, x, n_tok, n_expert, k, ids, w);
+        return cudaGetLastError();
+    }
     const size_t smem = sizeof(float) * ((size_t)n_embd + n_expert);
     SlotState dummy{};
     const int threads = n_expert >= 512 ? 512 : (n_expert < 32 ? 32 : n_expert);

@@ -75,6 +75,15 @@ cudaError_t launch_experts_grouped(const ExpertSrc &src, const float *x, const G
 cudaError_t launch_combine(const float *ypair, const int32_t *pair_pos, const float *w, int n_tok,
                            int k, int n_embd, const float *resid, float *y, cudaStream_t s);
 
+// ---- expert-parallel dispatch (moe_ep.cu) ----------------------------------
+
+// Route pairs to ranks: dest [P] scratch; the grouping `g` over `world` rank
+// buckets (g.cnt = send counts, g.pair_pos = send slot of each pair, g.n_tiles
+// = slots filled); send_ids [P], send_x [P][n_embd] in send-slot order.
+cudaError_t launch_ep_pack(const int32_t *ids, const float *x, int n_tok, int k, int n_expert,
+                           int n_embd, int world, int32_t *dest, const GroupBufs &g,
+                           int32_t *send_ids, float *send_x, int *err, cudaStream_t s);
+
 // ---- tensor-core grouped GEMM (moe_gemm.cu) --------------------------------
 
 #define GM_NT 64       // pairs per token tile of the GEMM (MMA N <= 64)

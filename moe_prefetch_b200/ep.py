@@ -1,0 +1,148 @@
+"""Expert-parallel MoE layers for batched decode and prefill.
+
+Rank g of a process group of `world` ranks (one per GPU) owns experts
+[g * E / world, (g + 1) * E / world) of every layer; its MoeStack holds only
+those, in slots 0 .. E/world - 1.  The router weights are replicated.  One
+layer over a rank's home tokens:
+
+  1. route + pack (libmoeb200): ids/w of the home tokens and the pairs in
+     owner-rank order, each with its token row and expert id;
+  2. all-to-all of the per-rank counts, then of the ids and rows (NCCL over
+     NVLink on GPUs);
+  3. the owner runs its experts on the rows it received (grouped GEMV or
+     tcgen05 GEMM, unweighted rows);
+  4. all-to-all of the rows back, in the order they came;
+  5. the home rank combines them in rank order.
+
+The reference has no multi-GPU code; the result equals the single-GPU layer
+(bit for bit on the GEMV path).  The orchestration works on any
+torch.distributed backend: the three device steps come from an `ops` object,
+so the exchange logic is testable with gloo on the CPU.
+"""
+import ctypes as C
+
+import torch
+import torch.distributed as dist
+
+from .config import MoeCacheConfig
+from .stack import MoeStack, Q4K_BYTES, Q6K_BYTES, _ptr, _stream
+
+PATHS = {"auto": 0, "gemv": 1, "gemm": 2}
+
+
+def _a2a(out, inp, out_splits, in_splits, group, world):
+    if world == 1:
+        out.copy_(inp)
+    else:
+        dist.all_to_all_single(out, inp, out_splits, in_splits, group=group)
+
+
+def ep_layer_forward(ops, layer, x, group=None, path="auto"):
+    """One expert-parallel MoE layer over this rank's home tokens x
+    [n_tok, n_embd]; returns (out, ids, w).  Every rank of the group must
+    call it for the same layer (the exchange is collective)."""
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    n_tok = x.shape[0]
+    ids, w, send_count, pos, send_ids, send_x = ops.route_pack(layer, x, world)
+    recv_count = torch.empty_like(send_count)
+    _a2a(recv_count, send_count, None, None, group, world)
+    counts = torch.stack([send_count, recv_count]).cpu()
+    send_splits = [int(v) for v in counts[0]]
+    recv_splits = [int(v) for v in counts[1]]
+    n_send, n_recv = sum(send_splits), sum(recv_splits)
+    recv_ids = torch.empty(n_recv, dtype=send_ids.dtype, device=x.device)
+    recv_x = torch.empty(n_recv, x.shape[1], dtype=send_x.dtype, device=x.device)
+    _a2a(recv_ids, send_ids[:n_send], recv_splits, send_splits, group, world)
+    _a2a(recv_x, send_x[:n_send], recv_splits, send_splits, group, world)
+    y_rows = ops.experts_rows(layer, recv_x, recv_ids, path)
+    back = torch.empty(n_send, x.shape[1], dtype=y_rows.dtype, device=x.device)
+    _a2a(back, y_rows, send_splits, recv_splits, group, world)
+    out = ops.combine(back, pos, w, n_tok)
+    return out, ids, w
+
+
+class LibEPOps:
+    """The three device steps of ep_layer_forward, from libmoeb200.so."""
+
+    def __init__(self, stack):
+        self.st = stack
+
+    def route_pack(self, layer, x, world):
+        st = self.st
+        x = x.contiguous()
+        n_tok, P = x.shape[0], x.shape[0] * st.n_used
+        dev = x.device
+        ids = torch.empty(n_tok, st.n_used, dtype=torch.int32, device=dev)
+        w = torch.empty(n_tok, st.n_used, dtype=torch.float32, device=dev)
+        send_count = torch.empty(world, dtype=torch.int32, device=dev)
+        pos = torch.empty(P, dtype=torch.int32, device=dev)
+        send_ids = torch.empty(P, dtype=torch.int32, device=dev)
+        send_x = torch.empty(P, st.n_embd, dtype=torch.float32, device=dev)
+        st._ck(st.lib.moe_ep_route_pack(st.ctx, layer, _ptr(x), n_tok, world, _ptr(ids), _ptr(w),
+                                        _ptr(send_count), _ptr(pos), _ptr(send_ids), _ptr(send_x),
+                                        _stream()), "moe_ep_route_pack")
+        return ids, w, send_count, pos, send_ids, send_x
+
+    def experts_rows(self, layer, x_rows, ids, path):
+        st = self.st
+        y = torch.empty_like(x_rows)
+        st._ck(st.lib.moe_experts_rows(st.ctx, layer, _ptr(x_rows), _ptr(ids), x_rows.shape[0],
+                                       _ptr(y), PATHS[path], _stream()), "moe_experts_rows")
+        return y
+
+    def combine(self, y_rows, pos, w, n_tok):
+        st = self.st
+        out = torch.empty(n_tok, st.n_embd, dtype=torch.float32, device=w.device)
+        st._ck(st.lib.moe_ep_combine(st.ctx, _ptr(y_rows), _ptr(pos), _ptr(w), n_tok, _ptr(out),
+                                     _stream()), "moe_ep_combine")
+        return out
+
+
+class ExpertParallelStack:
+    """The MoE stack of this rank under expert parallelism: its share of the
+    experts in slots, the full router, and ep_layer_forward over `group`."""
+
+    def __init__(self, n_layers, n_expert=128, n_used=8, n_embd=2048, n_ff=768, group=None,
+                 device=None):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if n_expert % self.world:
+            raise ValueError(f"{self.world} ranks do not divide {n_expert} experts")
+        self.per_rank = n_expert // self.world
+        self.e0 = self.rank * self.per_rank
+        dev = device if device is not None else torch.cuda.current_device()
+        self.st = MoeStack(n_layers, n_expert=n_expert, n_used=n_used, n_embd=n_embd, n_ff=n_ff,
+                           cache=MoeCacheConfig(n_slots=self.per_rank), device=dev)
+        self.ops = LibEPOps(self.st)
+
+    def synth(self, seed=0, sigma=0.02, router_sigma=0.02):
+        """The weights MoeStack.synth_resident(seed) generates, this rank's
+        experts only: each layer's full expert set is generated into a
+        temporary buffer and the owned range copied into the slots."""
+        st = self.st
+        E, per = st.n_expert, self.per_rank
+        nbg = E * st.gate_bytes // Q4K_BYTES
+        nbd = E * st.down_bytes // Q6K_BYTES
+        tmp = torch.empty(E * max(st.gate_bytes, st.down_bytes), dtype=torch.uint8, device=st.device)
+        s = _stream()
+        for il in range(st.n_layers):
+            base = (seed + 1000 * il) & 0xFFFFFFFF
+            g, u, d = st.slot_views(il)
+            for view, nb, qt, off, nbytes in ((g, nbg, 12, 0, st.gate_bytes), (u, nbg, 12, 1, st.gate_bytes),
+                                              (d, nbd, 14, 2, st.down_bytes)):
+                st._ck(st.lib.moe_synth_weights(C.c_void_p(tmp.data_ptr()), nb, qt, base + off, sigma, s),
+                       "synth")
+                view[:per].copy_(tmp[:E * nbytes].view(E, nbytes)[self.e0:self.e0 + per])
+            r = torch.empty(E, st.n_embd, device=st.device)
+            st._ck(st.lib.moe_synth_f32(_ptr(r), r.numel(), base + 3, router_sigma, s), "synth")
+            torch.cuda.synchronize(st.device)
+            st.set_router(il, r)
+            st.place(il, list(range(self.e0, self.e0 + per)), copy=False)
+        del tmp
+
+    def layer_forward(self, layer, x, path="auto"):
+        return ep_layer_forward(self.ops, layer, x, self.group, path)
+
+    def close(self):
+        self.st.close()

@@ -464,8 +464,9 @@ void or_router_select(const float *logits, int n_expert, const float *prior, int
     /* lane l holds experts l, l+32, ... summed in that order, then butterfly */
     float lane[32];
     for (int l = 0; l < 32; ++l) {
-        float sacc = ex[l];
-        for (int m = 1; m < n_expert / 32; ++m) sacc = sacc + ex[l + 32 * m];
+        /* a lane past n_expert (fewer than 32 experts) holds 0 */
+        float sacc = l < n_expert ? ex[l] : 0.0f;
+        for (int m = 1; l + 32 * m < n_expert; ++m) sacc = sacc + ex[l + 32 * m];
         lane[l] = sacc;
     }
     for (int off = 16; off >= 1; off >>= 1) {
