@@ -69,6 +69,10 @@ typedef struct moe_cfg {
     int32_t freeze;            /* LLAMA_MOE_CACHE_FREEZE                           */
     int32_t use_heat_counts;   /* a heat file is configured (LLAMA_MOE_HEAT_FILE)  */
     int32_t device;            /* CUDA device ordinal                              */
+    int32_t n_shared;          /* always-on shared experts per layer: 0 or 1.  A
+                                  shared expert joins every token after the k
+                                  routed ones with weight 1; it is never cached,
+                                  observed or routed (moe_set_shared_expert)      */
 } moe_cfg;
 
 /* What llama_moe_cache_lookup(up_exps) returns for one layer
@@ -136,6 +140,15 @@ int moe_set_expert_weights(moe_ctx *ctx, int layer, const void *gate, const void
  * the slots (moe_get_layer).  Replaces the map replay frame (patches/0008:435-475)
  * and the heat warm start placement (0007:567-618). Synchronous. */
 int moe_place(moe_ctx *ctx, int layer, const int32_t *slot_expert, int copy);
+
+/* The shared expert of `layer` (cfg->n_shared == 1): gate, up [n_ff rows
+ * of n_embd] Q4_K and down [n_embd rows of n_ff] in the model's layout, host
+ * or device memory, copied to a device buffer of its own.  It is always
+ * resident.  Replaces the ffn_*_shexp tensors of the upstream Qwen MoE
+ * graphs (upstream llama.cpp, not in the reference patches); the reference's
+ * 35B model has one shared expert per layer (README.md:33-36). */
+int moe_set_shared_expert(moe_ctx *ctx, int layer, const void *gate, const void *up,
+                          const void *down);
 
 /* ---- the hot path -------------------------------------------------------------- */
 

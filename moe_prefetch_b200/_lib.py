@@ -36,6 +36,7 @@ class MoeCfg(C.Structure):
         ("admit_floor", C.c_float), ("spec_probation", C.c_int32),
         ("batch_tables", C.c_int32), ("cache_prior", C.c_float), ("early_issue", C.c_int32),
         ("freeze", C.c_int32), ("use_heat_counts", C.c_int32), ("device", C.c_int32),
+        ("n_shared", C.c_int32),
     ]
 
 
@@ -64,6 +65,7 @@ SIGNATURES = {
     "moe_set_router": (I, [P, I, P]),
     "moe_set_expert_weights": (I, [P, I, P, P, P]),
     "moe_place": (I, [P, I, P, I]),
+    "moe_set_shared_expert": (I, [P, I, P, P, P]),
     "moe_layer_forward": (I, [P, I, P, P, I, P, P, P]),
     "moe_layer_forward_noalloc": (I, [P, I, P, P, I, P, P, P]),
     "moe_layer_forward_path": (I, [P, I, P, P, I, P, P, I, P]),

@@ -25,6 +25,9 @@ struct LayerMem {
     const void *hgate_user = nullptr, *hup_user = nullptr, *hdown_user = nullptr;
     bool registered[3] = {false, false, false};
     int32_t ns = 0;
+    uint8_t *shared = nullptr;        // shared expert: gate | up | down (n_shared == 1)
+    uint8_t *sgate = nullptr, *sup = nullptr, *sdown = nullptr;
+    bool shared_set = false;
 };
 
 }  // namespace
@@ -130,6 +133,7 @@ extern "C" int moe_create(const moe_cfg *cfg, moe_ctx **out) {
         return bad(MOE_ERR_UNSUPPORTED, "down_type must be Q6_K or Q4_K");
     if (g.early_issue) return bad(MOE_ERR_UNSUPPORTED, "early issue is not implemented on the device");
     if (g.admit_mode < 0 || g.admit_mode > 2) return bad(MOE_ERR_ARG, "admit_mode");
+    if (g.n_shared < 0 || g.n_shared > 1) return bad(MOE_ERR_UNSUPPORTED, "n_shared must be 0 or 1");
     if (g.n_slots <= 0 && !cfg->slot_profile) return bad(MOE_ERR_ARG, "n_slots must be > 0");
     c->ns.resize(g.n_layers);
     c->slot_off.resize(g.n_layers);
@@ -171,6 +175,14 @@ extern "C" int moe_create(const moe_cfg *cfg, moe_ctx **out) {
         m.down = m.slab + 2 * gsz;
         cudaMemsetAsync(m.slab + 2 * gsz + (size_t)m.ns * c->down_bytes, 0,
                         (size_t)c->down_bytes + 64);   // dummy slot + pad
+        if (g.n_shared) {
+            const size_t sg = al256((size_t)c->gate_bytes), sd = al256((size_t)c->down_bytes + 64);
+            if (cudaMalloc(&m.shared, 2 * sg + sd) != cudaSuccess) return cleanup_fail(MOE_ERR_OOM);
+            cudaMemsetAsync(m.shared, 0, 2 * sg + sd);
+            m.sgate = m.shared;
+            m.sup = m.shared + sg;
+            m.sdown = m.shared + 2 * sg;
+        }
     }
     if (cudaMalloc(&c->router, sizeof(float) * (size_t)L * E * H) != cudaSuccess) return cleanup_fail(MOE_ERR_OOM);
     cudaMemset(c->router, 0, sizeof(float) * (size_t)L * E * H);
@@ -248,7 +260,7 @@ extern "C" int moe_create(const moe_cfg *cfg, moe_ctx **out) {
         // per warp group, so at most 160 CTAs
         const int G = dev_sms > 0 ? std::min(dev_sms, 160) : 1;
         std::vector<int32_t> part(4 * (size_t)G);
-        const int64_t R = (int64_t)K * I;
+        const int64_t R = (int64_t)(K + g.n_shared) * I;
         int gmax = 0, dmax = 0;
         for (int cc = 0; cc < G; ++cc) {
             part[cc] = (int32_t)(cc * R / G);
@@ -260,6 +272,7 @@ extern "C" int moe_create(const moe_cfg *cfg, moe_ctx **out) {
         }
         DecodeParams &p = c->dp;
         p.n_layers = L; p.n_expert = E; p.k = K; p.n_embd = H; p.n_ff = I; p.down_type = g.down_type;
+        p.kx = K + g.n_shared;
         p.gate_bytes = c->gate_bytes; p.down_bytes = c->down_bytes;
         p.gu_rows_max = gmax; p.dn_rows_max = dmax;
         decode_smem_layout(p, G);
@@ -306,6 +319,7 @@ extern "C" void moe_destroy(moe_ctx *c) {
     cudaDeviceSynchronize();
     for (auto &m : c->L) {
         if (m.slab) cudaFree(m.slab);
+        if (m.shared) cudaFree(m.shared);
         for (int i = 0; i < 3; ++i) {
             const void *p = i == 0 ? m.hgate_user : i == 1 ? m.hup_user : m.hdown_user;
             if (m.registered[i] && p) cudaHostUnregister(const_cast<void *>(p));
@@ -366,9 +380,24 @@ static int refresh_layer_desc(moe_ctx *c, int layer) {
     d.gate = m.gate; d.up = m.up; d.down = m.down;
     d.hgate = m.hgate; d.hup = m.hup; d.hdown = m.hdown;
     d.table = c->st.table + (size_t)layer * c->cfg.n_expert;
+    d.sgate = m.sgate; d.sup = m.sup; d.sdown = m.sdown;
     d.ns = m.ns;
     CK(cudaMemcpy(c->d_layers + layer, &d, sizeof(d), cudaMemcpyHostToDevice));
     return MOE_OK;
+}
+
+extern "C" int moe_set_shared_expert(moe_ctx *c, int layer, const void *gate, const void *up,
+                                     const void *down) {
+    if (!c || layer < 0 || layer >= c->cfg.n_layers || !gate || !up || !down)
+        return fail(c, MOE_ERR_ARG, "moe_set_shared_expert: bad argument");
+    if (!c->cfg.n_shared) return fail(c, MOE_ERR_STATE, "moe_set_shared_expert: the context has n_shared = 0");
+    CK(cudaSetDevice(c->cfg.device));
+    LayerMem &m = c->L[layer];
+    CK(cudaMemcpy(m.sgate, gate, (size_t)c->gate_bytes, cudaMemcpyDefault));
+    CK(cudaMemcpy(m.sup, up, (size_t)c->gate_bytes, cudaMemcpyDefault));
+    CK(cudaMemcpy(m.sdown, down, (size_t)c->down_bytes, cudaMemcpyDefault));
+    m.shared_set = true;
+    return refresh_layer_desc(c, layer);
 }
 
 extern "C" int moe_set_router(moe_ctx *c, int layer, const float *w) {
@@ -481,12 +510,13 @@ static int ensure_scratch(moe_ctx *c, int n_tok) {
     cudaFree(c->s_group); cudaFree(c->s_ypair);
     c->s_ids = nullptr; c->s_w = nullptr; c->s_act = nullptr;
     c->s_group = nullptr; c->s_ypair = nullptr;
-    const int K = c->cfg.n_used, E = c->cfg.n_expert;
-    const size_t P = (size_t)n_tok * K;
+    const int K = c->cfg.n_used, KX = K + c->cfg.n_shared, E = c->cfg.n_expert + c->cfg.n_shared;
+    const size_t P = (size_t)n_tok * KX;   // pairs, the shared expert's included
     // cnt [E] | off [E + 1] | pair_pos [P] | pos_pair [P] | tiles [E + P] | n_tiles [1] | dest [P]
     const size_t gints = (size_t)E + (E + 1) + P + P + (E + P) + 1 + P;
-    if (cudaMalloc(&c->s_ids, sizeof(int32_t) * P) != cudaSuccess ||
-        cudaMalloc(&c->s_w, sizeof(float) * P) != cudaSuccess ||
+    // s_ids / s_w: [n_tok][K] router outputs, then [n_tok][KX] with the shared pair
+    if (cudaMalloc(&c->s_ids, sizeof(int32_t) * (size_t)n_tok * (K + KX)) != cudaSuccess ||
+        cudaMalloc(&c->s_w, sizeof(float) * (size_t)n_tok * (K + KX)) != cudaSuccess ||
         cudaMalloc(&c->s_act, sizeof(float) * P * c->cfg.n_ff) != cudaSuccess ||
         cudaMalloc(&c->s_group, sizeof(int32_t) * gints) != cudaSuccess ||
         cudaMalloc(&c->s_ypair, sizeof(float) * P * c->cfg.n_embd) != cudaSuccess) {
@@ -511,18 +541,45 @@ static ExpertSrc make_src(moe_ctx *c, int layer) {
     s.gate = m.gate; s.up = m.up; s.down = m.down;
     s.hgate = m.hgate; s.hup = m.hup; s.hdown = m.hdown;
     s.table = c->st.table + (size_t)layer * c->cfg.n_expert;
+    s.sgate = m.sgate; s.sup = m.sup; s.sdown = m.sdown;
     s.gate_bytes = c->gate_bytes; s.down_bytes = c->down_bytes;
     s.ns = m.ns; s.n_expert = c->cfg.n_expert;
     return s;
+}
+
+// The pairs the expert kernels see: the routed ids/w, or with a shared
+// expert the routed pairs plus (n_expert, 1) per token, built in the second
+// half of the id/weight scratch.  Sets *k_out to the pairs per token.
+static int expert_pairs(moe_ctx *c, const int32_t *ids, const float *w, int n_tok,
+                        cudaStream_t s, const int32_t **ids_e, const float **w_e, int *k_out) {
+    const moe_cfg &g = c->cfg;
+    *ids_e = ids;
+    *w_e = w;
+    *k_out = g.n_used;
+    if (!g.n_shared) return MOE_OK;
+    int32_t *ix = c->s_ids + (size_t)n_tok * g.n_used;
+    float *wx = c->s_w + (size_t)n_tok * g.n_used;
+    CK(launch_append_shared(ids, w, n_tok, g.n_used, g.n_expert, ix, wx, s));
+    *ids_e = ix;
+    *w_e = wx;
+    *k_out = g.n_used + 1;
+    return MOE_OK;
+}
+
+static int check_shared(moe_ctx *c, int layer) {
+    if (c->cfg.n_shared && !c->L[layer].shared_set)
+        return fail(c, MOE_ERR_STATE, "the shared expert of layer %d is not set", layer);
+    return MOE_OK;
 }
 
 extern "C" int moe_layer_forward(moe_ctx *c, int layer, const float *x, float *y, int n_tok,
                                  int32_t *ids, float *w, void *stream) {
     if (!c || !x || !y || n_tok <= 0 || layer < 0 || layer >= c->cfg.n_layers)
         return fail(c, MOE_ERR_ARG, "moe_layer_forward: bad argument");
-    CK(cudaSetDevice(c->cfg.device));
-    int r = ensure_scratch(c, n_tok);
+    int r = check_shared(c, layer);
     if (r != MOE_OK) return r;
+    CK(cudaSetDevice(c->cfg.device));
+    if ((r = ensure_scratch(c, n_tok)) != MOE_OK) return r;
     cudaStream_t s = (cudaStream_t)stream;
     const moe_cfg &g = c->cfg;
     int32_t *ids_d = ids ? ids : c->s_ids;
@@ -531,15 +588,19 @@ extern "C" int moe_layer_forward(moe_ctx *c, int layer, const float *x, float *y
     CK(launch_router(c->router + (size_t)layer * g.n_expert * g.n_embd, x, n_tok, g.n_expert, g.n_embd,
                      table, c->L[layer].ns, g.cache_prior, n_tok == 1 && g.cache_prior > 0.0f, g.n_used,
                      ids_d, w_d, nullptr, &c->st, n_tok == 1 ? layer : -1, s));
+    const int32_t *ids_e;
+    const float *w_e;
+    int kx;
+    if ((r = expert_pairs(c, ids_d, w_d, n_tok, s, &ids_e, &w_e, &kx)) != MOE_OK) return r;
     if (n_tok == 1) {
-        CK(launch_experts(make_src(c, layer), x, ids_d, w_d, n_tok, g.n_used, g.n_embd, g.n_ff,
+        CK(launch_experts(make_src(c, layer), x, ids_e, w_e, n_tok, kx, g.n_embd, g.n_ff,
                           g.down_type, c->s_act, nullptr, y, c->err, s));
     } else {
         // a batch: group the pairs by expert so that each expert's rows are
         // read once per tile of its tokens (bit-identical results)
-        CK(launch_group(ids_d, n_tok * g.n_used, g.n_expert, GROUP_TILE, c->grp, c->err, s));
-        CK(launch_experts_grouped(make_src(c, layer), x, c->grp, n_tok, g.n_used, g.n_embd, g.n_ff,
-                                  g.down_type, w_d, c->s_act, c->s_ypair, nullptr, y, c->err, s));
+        CK(launch_group(ids_e, n_tok * kx, g.n_expert + g.n_shared, GROUP_TILE, c->grp, c->err, s));
+        CK(launch_experts_grouped(make_src(c, layer), x, c->grp, n_tok, kx, g.n_embd, g.n_ff,
+                                  g.down_type, w_e, c->s_act, c->s_ypair, nullptr, y, c->err, s));
     }
     return MOE_OK;
 }
@@ -549,7 +610,8 @@ static int ensure_gemm_scratch(moe_ctx *c, int n_tok) {
     cudaFree(c->s_gemm);
     c->s_gemm = nullptr;
     const moe_cfg &g = c->cfg;
-    const size_t halves = gemm_scratch_halves(g.n_expert, n_tok * g.n_used, g.n_embd, g.n_ff);
+    const size_t halves = gemm_scratch_halves(g.n_expert + g.n_shared, n_tok * (g.n_used + g.n_shared),
+                                              g.n_embd, g.n_ff);
     if (cudaMalloc(&c->s_gemm, 2 * halves) != cudaSuccess) {
         c->s_gemm_cap_tok = 0;
         return fail(c, MOE_ERR_OOM, "GEMM scratch allocation for %d tokens failed", n_tok);
@@ -570,9 +632,10 @@ extern "C" int moe_layer_forward_path(moe_ctx *c, int layer, const float *x, flo
     if (path != MOE_PATH_GEMM) return fail(c, MOE_ERR_ARG, "moe_layer_forward_path: unknown path %d", path);
     if (!gemm_ok)
         return fail(c, MOE_ERR_UNSUPPORTED, "the GEMM path needs Q6_K down weights and n_ff, n_embd multiples of 128");
-    CK(cudaSetDevice(g.device));
-    int r = ensure_scratch(c, n_tok);
+    int r = check_shared(c, layer);
     if (r != MOE_OK) return r;
+    CK(cudaSetDevice(g.device));
+    if ((r = ensure_scratch(c, n_tok)) != MOE_OK) return r;
     if ((r = ensure_gemm_scratch(c, n_tok)) != MOE_OK) return r;
     cudaStream_t s = (cudaStream_t)stream;
     int32_t *ids_d = ids ? ids : c->s_ids;
@@ -581,9 +644,13 @@ extern "C" int moe_layer_forward_path(moe_ctx *c, int layer, const float *x, flo
     CK(launch_router(c->router + (size_t)layer * g.n_expert * g.n_embd, x, n_tok, g.n_expert, g.n_embd,
                      table, c->L[layer].ns, g.cache_prior, n_tok == 1 && g.cache_prior > 0.0f, g.n_used,
                      ids_d, w_d, nullptr, &c->st, n_tok == 1 ? layer : -1, s));
-    CK(launch_group(ids_d, n_tok * g.n_used, g.n_expert, GM_NT, c->grp, c->err, s));
-    CK(launch_experts_gemm(make_src(c, layer), x, c->grp, n_tok, g.n_used, g.n_embd, g.n_ff,
-                           g.down_type, w_d, c->s_gemm, c->s_ypair, nullptr, y, c->err, s));
+    const int32_t *ids_e;
+    const float *w_e;
+    int kx;
+    if ((r = expert_pairs(c, ids_d, w_d, n_tok, s, &ids_e, &w_e, &kx)) != MOE_OK) return r;
+    CK(launch_group(ids_e, n_tok * kx, g.n_expert + g.n_shared, GM_NT, c->grp, c->err, s));
+    CK(launch_experts_gemm(make_src(c, layer), x, c->grp, n_tok, kx, g.n_embd, g.n_ff,
+                           g.down_type, w_e, c->s_gemm, c->s_ypair, nullptr, y, c->err, s));
     return MOE_OK;
 }
 
@@ -596,6 +663,8 @@ extern "C" int moe_ep_route_pack(moe_ctx *c, int layer, const float *x, int n_to
         layer < 0 || layer >= c->cfg.n_layers)
         return fail(c, MOE_ERR_ARG, "moe_ep_route_pack: bad argument");
     const moe_cfg &g = c->cfg;
+    if (g.n_shared)
+        return fail(c, MOE_ERR_UNSUPPORTED, "moe_ep_route_pack: expert parallelism with a shared expert is not built");
     if (world < 1 || world > 256 || g.n_expert % world)
         return fail(c, MOE_ERR_ARG, "moe_ep_route_pack: world %d does not divide %d experts", world,
                     g.n_expert);
@@ -704,6 +773,8 @@ extern "C" int moe_layer_forward_noalloc(moe_ctx *c, int layer, const float *x, 
     if (!c || !x || !y || n_tok <= 0 || layer < 0 || layer >= c->cfg.n_layers)
         return fail(c, MOE_ERR_ARG, "moe_layer_forward_noalloc: bad argument");
     const moe_cfg &g = c->cfg;
+    if (g.n_shared)
+        return fail(c, MOE_ERR_UNSUPPORTED, "moe_layer_forward_noalloc: contexts with a shared expert are not supported");
     const size_t K = (size_t)g.n_used, I = (size_t)g.n_ff;
     if (noalloc_need((size_t)n_tok, K, I) > MOE_NOALLOC_SCRATCH_BYTES) {
         size_t max_tok = MOE_NOALLOC_SCRATCH_BYTES / (4 * K * I);
@@ -735,6 +806,10 @@ extern "C" int moe_layer_forward_noalloc(moe_ctx *c, int layer, const float *x, 
 extern "C" int moe_decode(moe_ctx *c, const float *h, float *out, int n_tok,
                           const moe_decode_dbg *dbg, void *stream) {
     if (!c || !h || !out || n_tok <= 0) return fail(c, MOE_ERR_ARG, "moe_decode: bad argument");
+    for (int l = 0; l < c->cfg.n_layers; ++l) {
+        const int r = check_shared(c, l);
+        if (r != MOE_OK) return r;
+    }
     CK(cudaSetDevice(c->cfg.device));
     if (c->dp.smem_bytes > 227 * 1024)
         return fail(c, MOE_ERR_UNSUPPORTED, "decode needs %d bytes of shared memory", c->dp.smem_bytes);

@@ -21,6 +21,7 @@
 namespace moe {
 
 #define GROUP_THREADS 1024
+#define GROUP_MAX_BUCKETS 264   // 256 routed experts + the shared one, rounded up
 
 // One CTA.  Pair p = t * k + r (token t, rank r).  Positions are stable: the
 // pairs of an expert keep pair order.  Writes cnt[E], off[E + 1],
@@ -31,8 +32,8 @@ __global__ void __launch_bounds__(GROUP_THREADS) k_group(const int32_t *__restri
                                                          int32_t *off, int32_t *pair_pos,
                                                          int32_t *pos_pair, int32_t *tiles,
                                                          int32_t *n_tiles, int *err) {
-    __shared__ int s_cnt[256], s_off[257], s_base[256];
-    __shared__ int s_wc[GROUP_THREADS / 32][256];
+    __shared__ int s_cnt[GROUP_MAX_BUCKETS], s_off[GROUP_MAX_BUCKETS + 1], s_base[GROUP_MAX_BUCKETS];
+    __shared__ int s_wc[GROUP_THREADS / 32][GROUP_MAX_BUCKETS];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     for (int e = tid; e < n_expert; e += GROUP_THREADS) { s_cnt[e] = 0; s_base[e] = 0; }
     __syncthreads();
@@ -116,9 +117,8 @@ __global__ void __launch_bounds__(256) k_gate_up_grouped(ExpertSrc src, const fl
                       xd + j * nblk + bb, xs + j * nblk + bb);
     }
     __syncthreads();
-    const int32_t slot = src.table ? src.table[e] : src.ns;
-    const uint8_t *gbase = expert_base(src, 0, e, slot);
-    const uint8_t *ubase = expert_base(src, 1, e, slot);
+    const uint8_t *gbase = expert_ptr(src, 0, e);
+    const uint8_t *ubase = expert_ptr(src, 1, e);
     if (!gbase || !ubase) {
         if (threadIdx.x == 0) atomicOr(err, MOE_DEV_ERR_INDEX);
         return;
@@ -172,8 +172,7 @@ __global__ void __launch_bounds__(256) k_down_grouped(ExpertSrc src, const float
                       aq + (size_t)j * n_ff + 32 * bb, ad + j * nblk + bb, as + j * nblk + bb);
     }
     __syncthreads();
-    const int32_t slot = src.table ? src.table[e] : src.ns;
-    const uint8_t *dbase = expert_base(src, 2, e, slot);
+    const uint8_t *dbase = expert_ptr(src, 2, e);
     if (!dbase) {
         if (threadIdx.x == 0) atomicOr(err, MOE_DEV_ERR_INDEX);
         return;
@@ -243,11 +242,30 @@ __global__ void __launch_bounds__(256) k_combine(const float *__restrict__ ypair
     y[(size_t)t * n_embd + h] = acc;
 }
 
+// ids_x/w_x [n_tok][k + 1] = the k routed pairs of each token, then the
+// shared expert (id n_expert) with weight 1.
+__global__ void k_append_shared(const int32_t *__restrict__ ids, const float *__restrict__ w,
+                                int n_tok, int k, int n_expert, int32_t *__restrict__ ids_x,
+                                float *__restrict__ w_x) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n_tok * (k + 1)) return;
+    const int t = i / (k + 1), r = i % (k + 1);
+    ids_x[i] = r < k ? ids[t * k + r] : n_expert;
+    w_x[i] = r < k ? w[t * k + r] : 1.0f;
+}
+
+cudaError_t launch_append_shared(const int32_t *ids, const float *w, int n_tok, int k, int n_expert,
+                                 int32_t *ids_x, float *w_x, cudaStream_t s) {
+    const int n = n_tok * (k + 1);
+    k_append_shared<<<(n + 255) / 256, 256, 0, s>>>(ids, w, n_tok, k, n_expert, ids_x, w_x);
+    return cudaGetLastError();
+}
+
 int group_max_tiles(int n_expert, int P, int tile) { return n_expert + (P + tile - 1) / tile; }
 
 cudaError_t launch_group(const int32_t *ids, int P, int n_expert, int tile, const GroupBufs &g,
                          int *err, cudaStream_t s) {
-    if (n_expert > 256 || tile > 0xFFFF) return cudaErrorInvalidValue;
+    if (n_expert > GROUP_MAX_BUCKETS || tile > 0xFFFF) return cudaErrorInvalidValue;
     k_group<<<1, GROUP_THREADS, 0, s>>>(ids, P, n_expert, tile, g.cnt, g.off, g.pair_pos,
                                         g.pos_pair, g.tiles, g.n_tiles, err);
     return cudaGetLastError();
@@ -258,7 +276,7 @@ cudaError_t launch_experts_grouped(const ExpertSrc &src, const float *x, const G
                                    const float *w, float *act, float *ypair, const float *resid,
                                    float *y, int *err, cudaStream_t s) {
     const int P = n_tok * k;
-    const int maxt = group_max_tiles(src.n_expert, P, GROUP_TILE);
+    const int maxt = group_max_tiles(src.n_expert + 1, P, GROUP_TILE);
     const size_t sm1 = (size_t)GROUP_TILE * n_embd + 2 * sizeof(float) * GROUP_TILE * (n_embd / 32);
     cudaError_t e;
     if (sm1 > 48 * 1024) {

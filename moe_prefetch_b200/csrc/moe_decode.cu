@@ -218,6 +218,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
     const int G = gridDim.x, c = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int E = E_T;
     const int K = p.k, H = p.n_embd, I = p.n_ff, NL = p.n_layers;
+    const int KX = p.kx;   // experts per token in the expert work: K, plus the shared one
     const int gurow = (H / MOE_QK) * MOE_Q4K_BYTES;
     const int drow = (I / MOE_QK) * (Q6_T ? MOE_Q6K_BYTES : MOE_Q4K_BYTES);
     const int r0 = p.gu_r0[c], r1 = p.gu_r1[c];
@@ -381,6 +382,11 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                     s_slot[lane] = slot;
                     if (id < 0 || id >= E) { atomicOr(p.err, MOE_DEV_ERR_INDEX); s_bad = 1; }
                 }
+                if (KX > K && lane == K) {   // the shared expert: always on, weight 1, own buffer
+                    s_ids[K] = E;
+                    s_w[K] = 1.0f;
+                    s_slot[K] = -1;
+                }
                 const unsigned miss = __ballot_sync(MOE_FULL, lane < K && s_slot[lane] == ld.ns);
                 if (lane == 0) s_any_miss = miss != 0;
             }
@@ -411,20 +417,23 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                         const uint32_t bytes = (uint32_t)(ch_n[q] * gurow);
                         fence_proxy_async();
                         if (slot != ld.ns) {
-                            const size_t off = (size_t)slot * p.gate_bytes + (size_t)ch_i0[q] * gurow;
+                            // slot -1: the shared expert's own buffer
+                            const size_t off = (size_t)ch_i0[q] * gurow;
+                            const uint8_t *gsrc = slot < 0 ? ld.sgate : ld.gate + (size_t)slot * p.gate_bytes;
+                            const uint8_t *usrc = slot < 0 ? ld.sup : ld.up + (size_t)slot * p.gate_bytes;
                             mbar_arrive_expect_tx(&mb[MB_GU + q], 2 * bytes);
-                            bulk_g2s(gate_sm + (size_t)ch_off[q] * gurow, ld.gate + off, bytes, &mb[MB_GU + q]);
-                            bulk_g2s(up_sm + (size_t)ch_off[q] * gurow, ld.up + off, bytes, &mb[MB_GU + q]);
+                            bulk_g2s(gate_sm + (size_t)ch_off[q] * gurow, gsrc + off, bytes, &mb[MB_GU + q]);
+                            bulk_g2s(up_sm + (size_t)ch_off[q] * gurow, usrc + off, bytes, &mb[MB_GU + q]);
                         } else {
                             mbar_arrive_expect_tx(&mb[MB_GU + q], 0);
                         }
                     }
-                    if (lane >= 8 && lane < 8 + K) {
+                    if (lane >= 8 && lane < 8 + KX) {
                         const int kk = lane - 8;
                         const int slot = s_slot[kk];
                         fence_proxy_async();
                         if (rows > 0 && slot != ld.ns) {
-                            const uint8_t *base = ld.down + (size_t)slot * p.down_bytes;
+                            const uint8_t *base = slot < 0 ? ld.sdown : ld.down + (size_t)slot * p.down_bytes;
                             const uintptr_t a0 = reinterpret_cast<uintptr_t>(base + (size_t)h0 * drow);
                             const uintptr_t a1 = reinterpret_cast<uintptr_t>(base + (size_t)h1 * drow);
                             const uintptr_t s0 = a0 & ~uintptr_t(15), s1 = (a1 + 15) & ~uintptr_t(15);
@@ -514,19 +523,20 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
             pend_gu = false;
 
             // ---- 5. activations -> Q8_1 ---------------------------------------------
-            q8_quantize_cta(p.act, true, K * I / 32, aq, ad, as_, tid, DEC_THREADS);
+            q8_quantize_cta(p.act, true, KX * I / 32, aq, ad, as_, tid, DEC_THREADS);
             __syncthreads();
             PROF(10)
 
             // ---- 6. down GEMV: one lane per half super-block, 8-lane row groups ------
             if (rows > 0) {
-                const int wpk = DEC_WARPS / K;   // warps per expert (>= 1)
-                if (warp < K * wpk) {
+                const int wpk = DEC_WARPS / KX;   // warps per expert (>= 1)
+                if (warp < KX * wpk) {
                     const int kk = warp / wpk, sub = warp % wpk;
                     const int grp = lane >> 3, u = lane & 7;   // row group, unit in group
-                    const uint8_t *base = s_slot[kk] != ld.ns
-                        ? ld.down + (size_t)s_slot[kk] * p.down_bytes
-                        : ld.hdown + (size_t)s_ids[kk] * p.down_bytes;
+                    const int sl = s_slot[kk];
+                    const uint8_t *base = sl < 0 ? ld.sdown
+                        : sl != ld.ns ? ld.down + (size_t)sl * p.down_bytes
+                                      : ld.hdown + (size_t)s_ids[kk] * p.down_bytes;
                     const uintptr_t a0 = reinterpret_cast<uintptr_t>(base + (size_t)h0 * drow);
                     const uint8_t *rws = dn + (size_t)kk * p.dn_stride + (int)(a0 & 15);
                     if (!mbar_wait(&mb[MB_DN + kk], par)) {
@@ -565,7 +575,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
             const bool last = L == NL - 1;
             for (int i = tid; i < rows; i += DEC_THREADS) {
                 float y = 0.0f;
-                for (int kk = 0; kk < K; ++kk) y = __fmaf_rn(s_w[kk], ys[kk * p.dn_rows_max + i], y);
+                for (int kk = 0; kk < KX; ++kk) y = __fmaf_rn(s_w[kk], ys[kk * p.dn_rows_max + i], y);
                 const float rn = __fadd_rn(rown[i], y);
                 if (last) {
                     p.out[(size_t)t * H + h0 + i] = rn;
@@ -613,7 +623,7 @@ abort:
             if (pend_gu)
                 for (int q = 0; q < nch; ++q) mbar_wait(&mb[MB_GU + q], par);
             if (pend_dn)
-                for (int kk = 0; kk < K; ++kk) mbar_wait(&mb[MB_DN + kk], par);
+                for (int kk = 0; kk < KX; ++kk) mbar_wait(&mb[MB_DN + kk], par);
             if (c == 0) p.st.g[G_CLOCK] = s_clock;
         }
         __syncthreads();
@@ -623,7 +633,7 @@ abort:
 static inline int align16(int v) { return (v + 15) & ~15; }
 
 int decode_smem_layout(DecodeParams &p, int grid) {
-    const int H = p.n_embd, I = p.n_ff, K = p.k, E = p.n_expert;
+    const int H = p.n_embd, I = p.n_ff, K = p.kx, E = p.n_expert;   // K: experts per token incl. shared
     const int gurow = (H / MOE_QK) * MOE_Q4K_BYTES;
     const int drow = (I / MOE_QK) * (p.down_type == MOE_QT_Q6K ? MOE_Q6K_BYTES : MOE_Q4K_BYTES);
     (void)grid;

@@ -230,9 +230,8 @@ __global__ void __launch_bounds__(GM_THREADS, 2) k_gemm_gate_up(
     const int N = (np + 15) & ~15;
     const int r0 = blockIdx.x * GM_ROWS;
     const int S = n_embd / GM_KS_GU;
-    const int32_t slot = src.table ? src.table[e] : src.ns;
-    const uint8_t *gbase = expert_base(src, 0, e, slot);
-    const uint8_t *ubase = expert_base(src, 1, e, slot);
+    const uint8_t *gbase = expert_ptr(src, 0, e);
+    const uint8_t *ubase = expert_ptr(src, 1, e);
     if (!gbase || !ubase) {
         if (tid == 0) atomicOr(err, MOE_DEV_ERR_INDEX);
         return;
@@ -378,8 +377,7 @@ __global__ void __launch_bounds__(GM_THREADS, 2) k_gemm_down(
     const int N = (np + 15) & ~15;
     const int r0 = blockIdx.x * GM_ROWS;
     const int S = n_ff / GM_KS_DN;
-    const int32_t slot = src.table ? src.table[e] : src.ns;
-    const uint8_t *dbase = expert_base(src, 2, e, slot);
+    const uint8_t *dbase = expert_ptr(src, 2, e);
     if (!dbase) {
         if (tid == 0) atomicOr(err, MOE_DEV_ERR_INDEX);
         return;
@@ -475,7 +473,7 @@ cudaError_t launch_experts_gemm(const ExpertSrc &src, const float *x, const Grou
     if (down_type != MOE_QT_Q6K || n_ff % GM_KS_DN || n_embd % GM_ROWS || n_ff % GM_ROWS)
         return cudaErrorInvalidValue;
     const int P = n_tok * k;
-    const int maxt = group_max_tiles(src.n_expert, P, GM_NT);
+    const int maxt = group_max_tiles(src.n_expert + 1, P, GM_NT);
     __half *xt = scratch;
     __half *at = scratch + (size_t)maxt * GM_NT * n_embd;
     cudaError_t e;

@@ -270,13 +270,8 @@ __global__ void __launch_bounds__(256) k_gate_up(ExpertSrc src, const float *__r
         q8_block_warp(xt[32 * b + lane], lane, xq + 32 * b, xd + b, xsum + b);
     __syncthreads();
     const int id = ids[tk];
-    if (id < 0 || id >= src.n_expert) {
-        if (threadIdx.x == 0) atomicOr(err, MOE_DEV_ERR_INDEX);
-        return;
-    }
-    const int32_t slot = src.table ? src.table[id] : src.ns;
-    const uint8_t *gbase = expert_base(src, 0, id, slot);
-    const uint8_t *ubase = expert_base(src, 1, id, slot);
+    const uint8_t *gbase = expert_ptr(src, 0, id);
+    const uint8_t *ubase = expert_ptr(src, 1, id);
     if (!gbase || !ubase) {
         if (threadIdx.x == 0) atomicOr(err, MOE_DEV_ERR_INDEX);
         return;
@@ -331,13 +326,12 @@ __global__ void __launch_bounds__(256) k_down(ExpertSrc src, const float *__rest
     const int nb = n_ff / MOE_QK;
     for (int kk = warp; kk < k; kk += nw) {
         const int id = ids[(size_t)t * k + kk];
-        if (id < 0 || id >= src.n_expert) {
+        const uint8_t *dbase = expert_ptr(src, 2, id);
+        if (!dbase) {
             if (lane == 0) atomicOr(err, MOE_DEV_ERR_INDEX);
             for (int r = 0; r < DN_ROWS; ++r) if (lane == 0) ys[kk * DN_ROWS + r] = 0.0f;
             continue;
         }
-        const int32_t slot = src.table ? src.table[id] : src.ns;
-        const uint8_t *dbase = expert_base(src, 2, id, slot);
         const int8_t *q = aq + (size_t)kk * n_ff;
         const float *dq = ad + (size_t)kk * (n_ff / 32);
         const float *sq = as + (size_t)kk * (n_ff / 32);

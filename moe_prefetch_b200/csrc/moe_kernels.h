@@ -10,21 +10,25 @@
 namespace moe {
 
 // Where one layer's experts live: slot slabs on the device (slot stride =
-// per-expert bytes; table[e] == ns means not resident) and the registered
-// host copies (expert stride), read zero-copy for misses.
+// per-expert bytes; table[e] == ns means not resident), the registered host
+// copies (expert stride), read zero-copy for misses, and the always-resident
+// shared expert, addressed as expert id n_expert.
 struct ExpertSrc {
     const uint8_t *gate, *up, *down;      // device slabs [ns+1][...]
     const uint8_t *hgate, *hup, *hdown;   // mapped host [n_expert][...] or null
+    const uint8_t *sgate, *sup, *sdown;   // shared expert (device) or null
     const int32_t *table;                 // [n_expert] or null (= all host)
     int64_t gate_bytes, down_bytes;
     int32_t ns, n_expert;
 };
 
-// Row bytes of expert `id` (which: 0 gate, 1 up, 2 down) in its slot, or in
-// the registered host copy when the slot is the dummy (a miss); null when
-// neither exists.
-__device__ __forceinline__ const uint8_t *expert_base(const ExpertSrc &s, int which, int id,
-                                                      int32_t slot) {
+// Bytes of expert `id`'s matrix (which: 0 gate, 1 up, 2 down): the shared
+// expert for id == n_expert, else its slot, else (a miss) the registered host
+// copy; null when there is none or the id is out of range.
+__device__ __forceinline__ const uint8_t *expert_ptr(const ExpertSrc &s, int which, int id) {
+    if (id == s.n_expert) return which == 0 ? s.sgate : which == 1 ? s.sup : s.sdown;
+    if (id < 0 || id > s.n_expert) return nullptr;
+    const int32_t slot = s.table ? s.table[id] : s.ns;
     const uint8_t *slab = which == 0 ? s.gate : which == 1 ? s.up : s.down;
     const uint8_t *host = which == 0 ? s.hgate : which == 1 ? s.hup : s.hdown;
     const int64_t bytes = which == 2 ? s.down_bytes : s.gate_bytes;
@@ -64,6 +68,9 @@ struct GroupBufs {
 };
 
 int group_max_tiles(int n_expert, int P, int tile);
+// the routed pairs of each token followed by the shared expert (id n_expert, weight 1)
+cudaError_t launch_append_shared(const int32_t *ids, const float *w, int n_tok, int k, int n_expert,
+                                 int32_t *ids_x, float *w_x, cudaStream_t s);
 cudaError_t launch_group(const int32_t *ids, int P, int n_expert, int tile, const GroupBufs &g,
                          int *err, cudaStream_t s);
 // gate/up + down over the grouped pairs (act [P][n_ff], ypair [P][n_embd]
@@ -105,12 +112,14 @@ struct LayerDesc {
     const uint8_t *gate, *up, *down;       // slot slabs
     const uint8_t *hgate, *hup, *hdown;    // mapped host or null
     const int32_t *table;                  // [E]
+    const uint8_t *sgate, *sup, *sdown;    // shared expert (device) or null
     int32_t ns;
     int32_t pad_;
 };
 
 struct DecodeParams {
     int n_layers, n_expert, k, n_embd, n_ff, down_type;
+    int kx;                                // experts per token: k, plus 1 with a shared expert
     int64_t gate_bytes, down_bytes;        // per expert
     const LayerDesc *layers;               // device [n_layers]
     const int32_t *gu_r0, *gu_r1;          // per CTA: flattened (k, row) range

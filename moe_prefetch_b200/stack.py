@@ -52,11 +52,12 @@ class _CudaView:
 
 class MoeStack:
     def __init__(self, n_layers, n_expert=128, n_used=8, n_embd=2048, n_ff=768,
-                 down_type=QTYPE_Q6_K, cache=None, device=0):
+                 down_type=QTYPE_Q6_K, cache=None, device=0, n_shared=0):
         self.lib = _lib.load()
         self.cache = cache or MoeCacheConfig()
         self.n_layers, self.n_expert, self.n_used = n_layers, n_expert, n_used
         self.n_embd, self.n_ff, self.down_type = n_embd, n_ff, down_type
+        self.n_shared = n_shared
         self.device = torch.device("cuda", device)
         self.gate_bytes, self.down_bytes = expert_bytes(n_embd, n_ff, down_type)
         self.ns = self.cache.slots_per_layer(n_layers, n_expert)
@@ -67,7 +68,7 @@ class MoeStack:
                      self.cache.admit_window, self.cache.admit_half, self.cache.admit_floor,
                      int(self.cache.spec_probation), int(self.cache.batch_tables),
                      self.cache.cache_prior, int(self.cache.early_issue),
-                     int(self.cache.freeze), int(bool(self.cache.heat_file)), device)
+                     int(self.cache.freeze), int(bool(self.cache.heat_file)), device, n_shared)
         torch.cuda.set_device(self.device)
         ctx = C.c_void_p()
         check(self.lib.moe_create(C.byref(cfg), C.byref(ctx)), None, "moe_create")
@@ -116,6 +117,12 @@ class MoeStack:
         self._ck(self.lib.moe_set_expert_weights(self.ctx, layer, _ptr(gate), _ptr(up), _ptr(down)),
                  "moe_set_expert_weights")
 
+    def set_shared_expert(self, layer, gate, up, down):
+        """The always-on shared expert of a layer (n_shared == 1): uint8 gate,
+        up, down bytes in ggml layout, host or device; copied by the library."""
+        self._ck(self.lib.moe_set_shared_expert(self.ctx, layer, _ptr(gate), _ptr(up), _ptr(down)),
+                 "moe_set_shared_expert")
+
     def place(self, layer, slot_expert, copy=True):
         se = np.ascontiguousarray(slot_expert, np.int32)
         self._ck(self.lib.moe_place(self.ctx, layer, _ptr(se), int(copy)), "moe_place")
@@ -124,8 +131,11 @@ class MoeStack:
         """Every layer: synthetic N(0, sigma^2) experts generated on the device
         straight into slots 0..n_expert-1 (needs n_slots >= n_expert) and an
         fp32 N(0, router_sigma^2) router; experts placed identity.  With
-        keep_router the router tensors stay in self.routers."""
+        keep_router the router tensors stay in self.routers.  With a shared
+        expert, its gate/up/down come from seeds base + 4, 5, 6 (self.shared
+        keeps them when keep_router)."""
         self.routers = [] if keep_router else None
+        self.shared = [] if keep_router and self.n_shared else None
         for il in range(self.n_layers):
             if self.ns[il] < self.n_expert:
                 raise ValueError("synth_resident needs n_slots >= n_expert")
@@ -147,6 +157,19 @@ class MoeStack:
                 self.routers.append(r)
             se = list(range(self.n_expert)) + [-1] * (self.ns[il] - self.n_expert)
             self.place(il, se, copy=False)
+            if self.n_shared:
+                parts = []
+                for off, nbytes, qt in ((4, self.gate_bytes, QTYPE_Q4_K), (5, self.gate_bytes, QTYPE_Q4_K),
+                                        (6, self.down_bytes, self.down_type)):
+                    t = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+                    bb = Q4K_BYTES if qt == QTYPE_Q4_K else Q6K_BYTES
+                    self._ck(self.lib.moe_synth_weights(_ptr(t), nbytes // bb, qt, base + off, sigma, s),
+                             "synth")
+                    parts.append(t)
+                torch.cuda.synchronize(self.device)
+                self.set_shared_expert(il, *parts)
+                if self.shared is not None:
+                    self.shared.append(tuple(parts))
 
     # -- hot path -------------------------------------------------------------
     def layer_forward(self, layer, x, stream=None):

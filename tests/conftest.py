@@ -44,12 +44,25 @@ def decode_partition(n_embd, grid):
     return h0, h1
 
 
+def with_shared(ids, w, gate, up, down, shared):
+    """The expert arrays and pairs with an always-on shared expert appended as
+    expert E (weight 1, after the routed ones); unchanged when shared is None."""
+    if shared is None:
+        return ids, w, gate, up, down
+    E = gate.shape[0]
+    ids = np.concatenate([ids, np.full(ids.shape[:-1] + (1,), E, np.int32)], axis=-1)
+    w = np.concatenate([w, np.ones(w.shape[:-1] + (1,), np.float32)], axis=-1)
+    gate, up, down = (np.concatenate([a, np.asarray(b).reshape(1, -1)]) for a, b in zip((gate, up, down), shared))
+    return ids, w, gate, up, down
+
+
 def check_decode_layer(oracle_lib, h_tok, dumps, t, L, W, gate, up, down, grid, n_ff=768,
-                       down_type=14, prior=None):
+                       down_type=14, prior=None, shared=None):
     """One (token, layer) of a decode against the oracle: the residual before
     the layer is h + y_0 + ... + y_{L-1} in fp32 (the kernel's order); the
     fused router must give the same ids, weights and normalised x bit for bit;
-    the layer output must be within the output tolerance."""
+    the layer output must be within the output tolerance.  `shared`: the
+    layer's shared expert (gate, up, down bytes) or None."""
     r = np.asarray(h_tok, np.float32).copy()
     ys = dumps["y"]
     for Lp in range(L):
@@ -60,7 +73,8 @@ def check_decode_layer(oracle_lib, h_tok, dumps, t, L, W, gate, up, down, grid, 
     assert np.array_equal(dumps["ids"][t, L], rid), f"ids (t={t}, L={L})"
     assert np.array_equal(dumps["w"][t, L].view(np.uint32), rw.view(np.uint32)), f"w (t={t}, L={L})"
     assert np.array_equal(dumps["x"][t, L].view(np.uint32), rx.view(np.uint32)), f"x (t={t}, L={L})"
-    ry = oracle_lib.moe_experts(rx[None], rid[None], rw[None], gate, up, down, down_type, n_ff)[0]
+    xi, xw, xg, xu, xd = with_shared(rid[None], rw[None], gate, up, down, shared)
+    ry = oracle_lib.moe_experts(rx[None], xi, xw, xg, xu, xd, down_type, n_ff)[0]
     assert rel_l2(ys[t, L], ry) <= REL_L2_TOL, (t, L, rel_l2(ys[t, L], ry))
     assert np.abs(ys[t, L] - ry).max() <= MAX_ABS_TOL
 
