@@ -426,6 +426,164 @@ def run_config3(args):
 
 
 # ---------------------------------------------------------------------------
+# config 4: 256 experts, n_ff 512, one always-on shared expert, 40 layers
+# ---------------------------------------------------------------------------
+C4_LAYERS, C4_EXPERT, C4_FF = 40, 256, 512
+C4_EXPERT_BYTES = 2 * C4_FF * (N_EMBD // 256) * 144 + N_EMBD * (C4_FF // 256) * 210   # 2,039,808
+C4_LAYER_TOKEN_BYTES = C4_EXPERT * N_EMBD * 4 + (TOP_K + 1) * C4_EXPERT_BYTES + XY_BYTES
+
+
+def run_config4(args):
+    """Config 4: 40 layers of 256 routed experts (top-8, n_ff 512) plus one
+    always-on shared expert.  At N = 1: (a) resident batch-1 decode (one
+    persistent launch per step) with its HBM roofline; (b) batch-1 decode
+    through a 96-slot cache, delta 0.01, experts in pinned host memory, window
+    admission, token by token with the cache step between tokens.  At every N:
+    (c) 32-sequence expert-parallel decode (the shared expert replicated).
+    One JSON line per measurement from rank 0."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    from moe_prefetch_b200 import MoeCacheConfig, MoeStack
+    from moe_prefetch_b200.ep import ExpertParallelStack
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    L = C4_LAYERS
+    stream = torch.cuda.current_stream()
+    lines = []
+    cfg_base = {"n_layers": L, "n_expert": C4_EXPERT, "top_k": TOP_K, "n_ff": C4_FF, "n_shared": 1,
+                "quant": "Q4_K gate/up, Q6_K down", "data": "synthetic"}
+    if world == 1:
+        # (a) resident decode
+        tokens = 128
+        st = MoeStack(n_layers=L, n_expert=C4_EXPERT, n_ff=C4_FF, n_shared=1,
+                      cache=MoeCacheConfig(cache_prior=0.01))
+        st.synth_resident(seed=17, keep_router=True)
+        h = torch.from_numpy(ar1_states(tokens, N_EMBD, seed=321)).cuda()
+        out = torch.empty_like(h)
+        for _ in range(args.warmup):
+            st.decode(h, out)
+        st.sync()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        steps = max(3, args.steps // 4)
+        e0.record(stream)
+        for _ in range(steps):
+            st.decode(h, out)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        st.sync()
+        ms = e0.elapsed_time(e1) / steps
+        peak, peak_kind = measured_peaks()
+        achieved = C4_LAYER_TOKEN_BYTES * L * tokens / (ms / 1e3) / 1e9
+        lines.append({"metric": "config4 batch-1 decode, all experts resident", "value": tokens / (ms / 1e3),
+                      "unit": "tok/s", "n_gpus": 1, "steps": steps, "ms_per_step": ms,
+                      "higher_is_better": True,
+                      "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                                   "frac": achieved / peak, "peak_kind": peak_kind,
+                                   "algorithmic_bytes_per_layer_token": C4_LAYER_TOKEN_BYTES},
+                      "config": dict(cfg_base, workload=f"config4 resident decode, {tokens} tokens per step")})
+        # (b) 96-slot cache, delta 0.01: host copies of every layer's experts
+        host = []
+        for il in range(L):
+            g, u, d = st.slot_views(il)
+            hl = []
+            for v in (g, u, d):
+                t = torch.empty(C4_EXPERT * v.shape[1], dtype=torch.uint8, pin_memory=True)
+                t.view(C4_EXPERT, -1).copy_(v[:C4_EXPERT])
+                hl.append(t)
+            host.append(tuple(hl))
+        routers = [r.clone() for r in st.routers]
+        shared = [tuple(p.clone() for p in sp) for sp in st.shared]
+        st.close()
+        torch.cuda.synchronize()
+        warm, timed = args.c2_warm, args.c2_tokens
+        cc = MoeStack(n_layers=L, n_expert=C4_EXPERT, n_ff=C4_FF, n_shared=1,
+                      cache=MoeCacheConfig(n_slots=96, max_inserts=2, admit="window", admit_window=8,
+                                           batch_tables=True, cache_prior=0.01))
+        for il in range(L):
+            cc.set_router(il, routers[il])
+            cc.set_expert_weights(il, *host[il])
+            cc.set_shared_expert(il, *shared[il])
+        hc = torch.from_numpy(ar1_states(warm + timed, N_EMBD, seed=654)).cuda()
+        oc = torch.empty_like(hc)
+        for t in range(warm):
+            cc.decode(hc[t:t + 1], oc[t:t + 1])
+            cc.step()
+        cc.sync()
+        s0 = cc.stats()
+        e0.record(stream)
+        for t in range(warm, warm + timed):
+            cc.decode(hc[t:t + 1], oc[t:t + 1])
+            cc.step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        cc.sync()
+        s1 = cc.stats()
+        ms = e0.elapsed_time(e1)
+        d = {k: s1[k] - s0[k] for k in s1}
+        routed = d["hits"] + d["misses"]
+        lines.append({"metric": "config4 batch-1 decode, 96-slot cache, delta 0.01",
+                      "value": timed / (ms / 1e3), "unit": "tok/s", "n_gpus": 1, "higher_is_better": True,
+                      "hit_rate": d["hits"] / routed if routed else None,
+                      "uploads_per_token": d["scheduled"] / timed,
+                      "upload_gbs": d["upload_bytes"] / (ms / 1e3) / 1e9,
+                      "zero_copy_miss_gbs": d["misses"] * C4_EXPERT_BYTES / (ms / 1e3) / 1e9,
+                      "ms_per_token": ms / timed,
+                      "config": dict(cfg_base, workload="config4 cache decode: 96 slots/layer, window "
+                                                        "admission W=8, batched tables",
+                                     warm_tokens=warm, timed_tokens=timed)})
+        cc.close()
+        del host
+        torch.cuda.synchronize()
+    # (c) 32-sequence expert-parallel decode
+    seqs, steps = 32, args.c3_decode_steps
+    if seqs % world == 0 and C4_EXPERT % world == 0:
+        ep = ExpertParallelStack(L, n_expert=C4_EXPERT, n_ff=C4_FF, n_shared=1)
+        ep.synth(seed=17)
+        rng = np.random.default_rng(502)
+        xx = rng.standard_normal((seqs, N_EMBD))
+        xx = (xx / np.sqrt((xx ** 2).mean(-1, keepdims=True))).astype(np.float32)
+        x = torch.from_numpy(xx[rank::world].copy()).cuda()
+        for _ in range(args.warmup):
+            for il in range(L):
+                ep.layer_forward(il, x, "auto")
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            for il in range(L):
+                ep.layer_forward(il, x, "auto")
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1)], device="cuda", dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t[0])
+        lines.append({"metric": "config4 expert-parallel batched decode", "value": seqs * steps / (ms / 1e3),
+                      "unit": "tok/s", "n_gpus": world, "steps": steps, "ms_per_step": ms / steps,
+                      "higher_is_better": True, "scaling": "strong",
+                      "config": dict(cfg_base, workload=f"config4 decode: {seqs} sequences x {steps} steps, "
+                                                        f"EP {C4_EXPERT // world} experts/GPU, shared replicated")})
+        ep.close()
+    if rank == 0:
+        for ln in lines:
+            print(json.dumps(ln), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+# ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
 def main():
@@ -440,7 +598,7 @@ def main():
     ap.add_argument("--ref-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--workload", default="config1", choices=["config1", "config2", "config3"])
+    ap.add_argument("--workload", default="config1", choices=["config1", "config2", "config3", "config4"])
     ap.add_argument("--c3-decode-steps", type=int, default=128)
     ap.add_argument("--c3-prefill-chunks", type=int, default=4)
     ap.add_argument("--c2-warm", type=int, default=64)
@@ -452,6 +610,8 @@ def main():
         return run_config2(args)
     if args.workload == "config3":
         return run_config3(args)
+    if args.workload == "config4":
+        return run_config4(args)
 
     import torch
     import torch.distributed as dist

@@ -208,10 +208,13 @@ int moe_ep_route_pack(moe_ctx *ctx, int layer, const float *x, int n_tok, int wo
 int moe_experts_rows(moe_ctx *ctx, int layer, const float *x_rows, const int32_t *ids,
                      int n_rows, float *y_rows, int path, void *stream);
 
-/* out[t] = sum over r in rank order of w[t][r] * y_rows[pos[t*n_used + r]]:
- * the combine of moe_layer_forward over the rows that came back. */
+/* out[t] = sum over r in rank order of w[t][r] * y_rows[pos[t*n_used + r]],
+ * then + add_rows[t] when given: the combine of moe_layer_forward over the
+ * rows that came back.  With a shared expert, add_rows are its rows for the
+ * home tokens (moe_experts_rows with id n_expert on every row; each rank
+ * keeps a replica of the shared expert); required then, else NULL. */
 int moe_ep_combine(moe_ctx *ctx, const float *y_rows, const int32_t *pos, const float *w,
-                   int n_tok, float *out, void *stream);
+                   int n_tok, const float *add_rows, float *out, void *stream);
 
 /* moe_layer_forward that allocates no device memory.  This entry point has no
  * counterpart in the reference, whose CPU expert path allocates nothing on

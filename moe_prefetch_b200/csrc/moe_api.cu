@@ -663,8 +663,6 @@ extern "C" int moe_ep_route_pack(moe_ctx *c, int layer, const float *x, int n_to
         layer < 0 || layer >= c->cfg.n_layers)
         return fail(c, MOE_ERR_ARG, "moe_ep_route_pack: bad argument");
     const moe_cfg &g = c->cfg;
-    if (g.n_shared)
-        return fail(c, MOE_ERR_UNSUPPORTED, "moe_ep_route_pack: expert parallelism with a shared expert is not built");
     if (world < 1 || world > 256 || g.n_expert % world)
         return fail(c, MOE_ERR_ARG, "moe_ep_route_pack: world %d does not divide %d experts", world,
                     g.n_expert);
@@ -701,13 +699,14 @@ extern "C" int moe_experts_rows(moe_ctx *c, int layer, const float *x_rows, cons
     int r = ensure_scratch(c, n_tok_eq);
     if (r != MOE_OK) return r;
     cudaStream_t s = (cudaStream_t)stream;
+    const int buckets = g.n_expert + g.n_shared;   // id n_expert: the shared expert
     if (path == MOE_PATH_GEMV) {
-        CK(launch_group(ids, n_rows, g.n_expert, GROUP_TILE, c->grp, c->err, s));
+        CK(launch_group(ids, n_rows, buckets, GROUP_TILE, c->grp, c->err, s));
         CK(launch_experts_grouped(make_src(c, layer), x_rows, c->grp, n_rows, 1, g.n_embd, g.n_ff,
                                   g.down_type, nullptr, c->s_act, c->s_ypair, nullptr, y_rows, c->err, s));
     } else {
         if ((r = ensure_gemm_scratch(c, n_tok_eq)) != MOE_OK) return r;
-        CK(launch_group(ids, n_rows, g.n_expert, GM_NT, c->grp, c->err, s));
+        CK(launch_group(ids, n_rows, buckets, GM_NT, c->grp, c->err, s));
         CK(launch_experts_gemm(make_src(c, layer), x_rows, c->grp, n_rows, 1, g.n_embd, g.n_ff,
                                g.down_type, nullptr, c->s_gemm, c->s_ypair, nullptr, y_rows, c->err, s));
     }
@@ -715,10 +714,12 @@ extern "C" int moe_experts_rows(moe_ctx *c, int layer, const float *x_rows, cons
 }
 
 extern "C" int moe_ep_combine(moe_ctx *c, const float *y_rows, const int32_t *pos, const float *w,
-                              int n_tok, float *out, void *stream) {
+                              int n_tok, const float *add_rows, float *out, void *stream) {
     if (!c || !pos || !w || !out || n_tok <= 0) return fail(c, MOE_ERR_ARG, "moe_ep_combine: bad argument");
+    if (c->cfg.n_shared && !add_rows)
+        return fail(c, MOE_ERR_ARG, "moe_ep_combine: the shared expert's rows are missing");
     CK(cudaSetDevice(c->cfg.device));
-    CK(launch_combine(y_rows, pos, w, n_tok, c->cfg.n_used, c->cfg.n_embd, nullptr, out,
+    CK(launch_combine(y_rows, pos, w, n_tok, c->cfg.n_used, c->cfg.n_embd, add_rows, out,
                       (cudaStream_t)stream));
     return MOE_OK;
 }

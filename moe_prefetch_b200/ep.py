@@ -57,7 +57,9 @@ def ep_layer_forward(ops, layer, x, group=None, path="auto"):
     y_rows = ops.experts_rows(layer, recv_x, recv_ids, path)
     back = torch.empty(n_send, x.shape[1], dtype=y_rows.dtype, device=x.device)
     _a2a(back, y_rows, send_splits, recv_splits, group, world)
-    out = ops.combine(back, pos, w, n_tok)
+    # an always-on shared expert is replicated on every rank: rows of the home tokens
+    shared = ops.shared_rows(layer, x, path) if getattr(ops, "n_shared", 0) else None
+    out = ops.combine(back, pos, w, n_tok, shared)
     return out, ids, w
 
 
@@ -66,6 +68,7 @@ class LibEPOps:
 
     def __init__(self, stack):
         self.st = stack
+        self.n_shared = stack.n_shared
 
     def route_pack(self, layer, x, world):
         st = self.st
@@ -90,11 +93,15 @@ class LibEPOps:
                                        _ptr(y), PATHS[path], _stream()), "moe_experts_rows")
         return y
 
-    def combine(self, y_rows, pos, w, n_tok):
+    def shared_rows(self, layer, x, path):
+        ids = torch.full((x.shape[0],), self.st.n_expert, dtype=torch.int32, device=x.device)
+        return self.experts_rows(layer, x.contiguous(), ids, path)
+
+    def combine(self, y_rows, pos, w, n_tok, add_rows=None):
         st = self.st
         out = torch.empty(n_tok, st.n_embd, dtype=torch.float32, device=w.device)
-        st._ck(st.lib.moe_ep_combine(st.ctx, _ptr(y_rows), _ptr(pos), _ptr(w), n_tok, _ptr(out),
-                                     _stream()), "moe_ep_combine")
+        st._ck(st.lib.moe_ep_combine(st.ctx, _ptr(y_rows), _ptr(pos), _ptr(w), n_tok, _ptr(add_rows),
+                                     _ptr(out), _stream()), "moe_ep_combine")
         return out
 
 
@@ -103,7 +110,7 @@ class ExpertParallelStack:
     experts in slots, the full router, and ep_layer_forward over `group`."""
 
     def __init__(self, n_layers, n_expert=128, n_used=8, n_embd=2048, n_ff=768, group=None,
-                 device=None):
+                 device=None, n_shared=0):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -113,7 +120,7 @@ class ExpertParallelStack:
         self.e0 = self.rank * self.per_rank
         dev = device if device is not None else torch.cuda.current_device()
         self.st = MoeStack(n_layers, n_expert=n_expert, n_used=n_used, n_embd=n_embd, n_ff=n_ff,
-                           cache=MoeCacheConfig(n_slots=self.per_rank), device=dev)
+                           cache=MoeCacheConfig(n_slots=self.per_rank), device=dev, n_shared=n_shared)
         self.ops = LibEPOps(self.st)
 
     def synth(self, seed=0, sigma=0.02, router_sigma=0.02):
@@ -139,6 +146,15 @@ class ExpertParallelStack:
             torch.cuda.synchronize(st.device)
             st.set_router(il, r)
             st.place(il, list(range(self.e0, self.e0 + per)), copy=False)
+            if st.n_shared:   # replicated on every rank, seeds as MoeStack.synth_resident
+                parts = []
+                for off, nbytes, qt in ((4, st.gate_bytes, 12), (5, st.gate_bytes, 12), (6, st.down_bytes, 14)):
+                    t = torch.empty(nbytes, dtype=torch.uint8, device=st.device)
+                    bb = Q4K_BYTES if qt == 12 else Q6K_BYTES
+                    st._ck(st.lib.moe_synth_weights(_ptr(t), nbytes // bb, qt, base + off, sigma, s), "synth")
+                    parts.append(t)
+                torch.cuda.synchronize(st.device)
+                st.set_shared_expert(il, *parts)
         del tmp
 
     def layer_forward(self, layer, x, path="auto"):

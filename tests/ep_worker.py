@@ -1,6 +1,8 @@
 """Worker of tests/test_gpu_ep.py: expert parallelism over NCCL, one rank per GPU.
 
-Every rank builds its share of a 2-layer stack (ExpertParallelStack.synth),
+For two stacks -- config 1's shapes, and config 4's (256 experts, n_ff 512,
+one always-on shared expert) -- every rank builds its share of a 2-layer stack
+(ExpertParallelStack.synth),
 runs both layers on its home tokens through ep_layer_forward for the GEMV and
 the GEMM paths, and all-gathers the outputs.  Rank 0 then builds the whole
 stack on its own GPU with the same seed (MoeStack.synth_resident) and checks:
@@ -37,41 +39,8 @@ def main():
                             device_id=torch.device("cuda", local))
     ok = True
     try:
-        ep = ExpertParallelStack(L)
-        ep.synth(SEED)
-        X = rms(np.random.default_rng(100).standard_normal((world * TOK_PER_RANK, H)))
-        mine = torch.from_numpy(X[rank::world].copy()).cuda()
-        got = {}
-        for path in ("gemv", "gemm"):
-            for layer in range(L):
-                out, ids, w = ep.layer_forward(layer, mine, path)
-                allo = torch.empty(world, *out.shape, device=out.device)
-                alli = torch.empty(world, *ids.shape, dtype=ids.dtype, device=ids.device)
-                dist.all_gather_into_tensor(allo, out.contiguous())
-                dist.all_gather_into_tensor(alli, ids.contiguous())
-                got[(path, layer)] = (allo.cpu().numpy(), alli.cpu().numpy())
-        torch.cuda.synchronize()
-        if rank == 0:
-            ref = MoeStack(n_layers=L)
-            ref.synth_resident(seed=SEED)
-            for (path, layer), (allo, alli) in got.items():
-                y, ids, _ = ref.layer_forward_path(layer, torch.from_numpy(X).cuda(), path)
-                y, ids = y.cpu().numpy(), ids.cpu().numpy()
-                for r in range(world):
-                    yr, ir = y[r::world], ids[r::world]
-                    if not np.array_equal(alli[r], ir):
-                        print(f"ids differ: path {path} layer {layer} rank {r}")
-                        ok = False
-                    if path == "gemv":
-                        same = np.array_equal(allo[r].view(np.uint32), yr.view(np.uint32))
-                    else:
-                        rel = np.linalg.norm(allo[r] - yr) / np.linalg.norm(yr)
-                        same = rel <= 1e-3 and np.abs(allo[r] - yr).max() <= 1e-2
-                    if not same:
-                        print(f"outputs differ: path {path} layer {layer} rank {r}")
-                        ok = False
-            ref.close()
-        ep.close()
+        for shape in ((128, 768, 0), (256, 512, 1)):
+            ok = run_shape(rank, world, shape, MoeStack, ExpertParallelStack) and ok
         flag = torch.tensor([1 if ok else 0], device="cuda")
         dist.broadcast(flag, 0)
         ok = bool(flag.item())
@@ -80,6 +49,47 @@ def main():
     if rank == 0 and ok:
         print("EP_OK")
     return 0 if ok else 1
+
+
+def run_shape(rank, world, shape, MoeStack, ExpertParallelStack):
+    E, I, n_shared = shape
+    ok = True
+    ep = ExpertParallelStack(L, n_expert=E, n_ff=I, n_shared=n_shared)
+    ep.synth(SEED)
+    X = rms(np.random.default_rng(100).standard_normal((world * TOK_PER_RANK, H)))
+    mine = torch.from_numpy(X[rank::world].copy()).cuda()
+    got = {}
+    for path in ("gemv", "gemm"):
+        for layer in range(L):
+            out, ids, w = ep.layer_forward(layer, mine, path)
+            allo = torch.empty(world, *out.shape, device=out.device)
+            alli = torch.empty(world, *ids.shape, dtype=ids.dtype, device=ids.device)
+            dist.all_gather_into_tensor(allo, out.contiguous())
+            dist.all_gather_into_tensor(alli, ids.contiguous())
+            got[(path, layer)] = (allo.cpu().numpy(), alli.cpu().numpy())
+    torch.cuda.synchronize()
+    if rank == 0:
+        ref = MoeStack(n_layers=L, n_expert=E, n_ff=I, n_shared=n_shared)
+        ref.synth_resident(seed=SEED)
+        for (path, layer), (allo, alli) in got.items():
+            y, ids, _ = ref.layer_forward_path(layer, torch.from_numpy(X).cuda(), path)
+            y, ids = y.cpu().numpy(), ids.cpu().numpy()
+            for r in range(world):
+                yr, ir = y[r::world], ids[r::world]
+                if not np.array_equal(alli[r], ir):
+                    print(f"ids differ: path {path} layer {layer} rank {r}")
+                    ok = False
+                if path == "gemv":
+                    same = np.array_equal(allo[r].view(np.uint32), yr.view(np.uint32))
+                else:
+                    rel = np.linalg.norm(allo[r] - yr) / np.linalg.norm(yr)
+                    same = rel <= 1e-3 and np.abs(allo[r] - yr).max() <= 1e-2
+                if not same:
+                    print(f"outputs differ: shape {shape} path {path} layer {layer} rank {r}")
+                    ok = False
+        ref.close()
+    ep.close()
+    return ok
 
 
 if __name__ == "__main__":

@@ -72,7 +72,8 @@ class OracleOps:
                                self.up, self.down, 14, I, n_threads=2)
         return torch.from_numpy(y)
 
-    def combine(self, back, pos, w, n_tok):
+    def combine(self, back, pos, w, n_tok, add_rows=None):
+        assert add_rows is None
         rows = back.numpy()[pos.numpy().reshape(n_tok, K)]     # [n_tok, K, H]
         wn = w.numpy().astype(np.float64)
         acc = np.zeros((n_tok, H))

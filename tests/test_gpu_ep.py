@@ -25,15 +25,16 @@ H = 2048
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-@pytest.fixture(scope="module")
-def stacks():
+@pytest.fixture(scope="module", params=[(128, 768, 0), (256, 512, 1)], ids=["c1", "c4shared"])
+def stacks(request):
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     from moe_prefetch_b200 import MoeStack
     from moe_prefetch_b200.ep import ExpertParallelStack
-    ep = ExpertParallelStack(1)
+    E, I, n_shared = request.param
+    ep = ExpertParallelStack(1, n_expert=E, n_ff=I, n_shared=n_shared)
     ep.synth(seed=29)
-    ref = MoeStack(n_layers=1)
+    ref = MoeStack(n_layers=1, n_expert=E, n_ff=I, n_shared=n_shared)
     ref.synth_resident(seed=29)
     yield ep, ref
     ep.close()
