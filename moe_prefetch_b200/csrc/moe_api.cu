@@ -56,7 +56,8 @@ struct moe_ctx {
     int *abort_flag = nullptr, *err = nullptr;
     // scratch for moe_layer_forward / moe_decode_host
     int32_t *s_ids = nullptr;
-    float *s_w = nullptr, *s_act = nullptr, *s_io = nullptr;
+    float *s_w = nullptr, *s_io = nullptr;
+    float *s_act = nullptr;            // per-pair fp32 activations, or the grouped path's Q8_1 scratch
     int s_cap_tok = 0, s_io_cap = 0;
     // grouping of the routed pairs by expert (n_tok > 1) and the unweighted
     // per-pair down rows [P][n_embd]
@@ -517,7 +518,8 @@ static int ensure_scratch(moe_ctx *c, int n_tok) {
     // s_ids / s_w: [n_tok][K] router outputs, then [n_tok][KX] with the shared pair
     if (cudaMalloc(&c->s_ids, sizeof(int32_t) * (size_t)n_tok * (K + KX)) != cudaSuccess ||
         cudaMalloc(&c->s_w, sizeof(float) * (size_t)n_tok * (K + KX)) != cudaSuccess ||
-        cudaMalloc(&c->s_act, sizeof(float) * P * c->cfg.n_ff) != cudaSuccess ||
+        cudaMalloc(&c->s_act, std::max(sizeof(float) * P * c->cfg.n_ff,
+                                        grouped_scratch_bytes((int)P, c->cfg.n_embd, c->cfg.n_ff))) != cudaSuccess ||
         cudaMalloc(&c->s_group, sizeof(int32_t) * gints) != cudaSuccess ||
         cudaMalloc(&c->s_ypair, sizeof(float) * P * c->cfg.n_embd) != cudaSuccess) {
         c->s_cap_tok = 0;

@@ -7,7 +7,9 @@
 //
 //   k_group           pairs -> per-expert counts, offsets, stable positions,
 //                     and the tile list (expert, token tile)
-//   k_gate_up_grouped gate/up GEMV (Q4_K x Q8_1) + SiLU*mul per pair
+//   k_quant_rows      token rows -> Q8_1, once
+//   k_gate_up_grouped gate/up GEMV (Q4_K x Q8_1) + SiLU*mul per pair, the
+//                     activations quantised to Q8_1 per 32-row block
 //   k_down_grouped    down GEMV per pair -> unweighted rows ypair[pos][h]
 //   k_combine         y[t] = sum_r w[t][r] * ypair[pos(t, r)] in rank order
 //
@@ -17,6 +19,8 @@
 // path, while the weights cross DRAM once per (expert, CTA) instead of once per
 // pair.
 #include "moe_kernels.h"
+
+#include <algorithm>
 
 namespace moe {
 
@@ -43,15 +47,34 @@ __global__ void __launch_bounds__(GROUP_THREADS) k_group(const int32_t *__restri
         else atomicOr(err, MOE_DEV_ERR_INDEX);
     }
     __syncthreads();
-    if (tid == 0) {
-        int acc = 0, nt = 0;
-        for (int e = 0; e < n_expert; ++e) {
-            s_off[e] = acc;
-            acc += s_cnt[e];
-            for (int t0 = 0; t0 < s_cnt[e]; t0 += tile) tiles[nt++] = (e << 16) | (t0 / tile);
+    if (warp == 0) {
+        // lane l owns buckets [l*per, (l+1)*per): local sums of pairs and
+        // tiles, an exclusive scan across lanes, then offsets and tile entries
+        const int per = (n_expert + 31) / 32;
+        int cs = 0, ts = 0;
+        for (int i = 0; i < per; ++i) {
+            const int e = lane * per + i;
+            if (e < n_expert) { cs += s_cnt[e]; ts += (s_cnt[e] + tile - 1) / tile; }
         }
-        s_off[n_expert] = acc;
-        *n_tiles = nt;
+        int ci = cs, ti = ts;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int cu = __shfl_up_sync(MOE_FULL, ci, o), tu = __shfl_up_sync(MOE_FULL, ti, o);
+            if (lane >= o) { ci += cu; ti += tu; }
+        }
+        int acc = ci - cs, nt = ti - ts;
+        for (int i = 0; i < per; ++i) {
+            const int e = lane * per + i;
+            if (e < n_expert) {
+                s_off[e] = acc;
+                acc += s_cnt[e];
+                for (int t0 = 0; t0 < s_cnt[e]; t0 += tile) tiles[nt++] = (e << 16) | (t0 / tile);
+            }
+        }
+        if (lane == 31) {
+            s_off[n_expert] = acc;
+            *n_tiles = nt;
+        }
     }
     __syncthreads();
     for (int e = tid; e <= n_expert; e += GROUP_THREADS) {
@@ -88,129 +111,274 @@ __global__ void __launch_bounds__(GROUP_THREADS) k_group(const int32_t *__restri
     }
 }
 
-// Gate/up for the pairs of one tile.  grid (ceil(n_ff / GU_ROWS), max tiles);
-// block 256.  Each pair's token is quantised to Q8_1 in shared memory (the
-// same quantiser as k_gate_up); every row is dotted with every pair's
-// activations, lane per unit, then warp_sum: the per-pair kernel's order.
-__global__ void __launch_bounds__(256) k_gate_up_grouped(ExpertSrc src, const float *__restrict__ x,
-                                                         const int32_t *__restrict__ off,
-                                                         const int32_t *__restrict__ cnt,
-                                                         const int32_t *__restrict__ pos_pair,
-                                                         const int32_t *__restrict__ tiles,
-                                                         const int32_t *__restrict__ n_tiles,
-                                                         int k, int n_embd, int n_ff,
-                                                         float *__restrict__ act, int *err) {
-    extern __shared__ __align__(16) uint8_t smg[];
+#define GU2_ROWS 32    // gate/up rows per CTA: one Q8_1 block of every pair's activations
+#define DN2_ROWS 64    // down rows per CTA: 8 per warp
+
+// x [n_rows][n_embd] -> Q8_1 (xq, d, s per 32-block), with the quantiser of
+// k_gate_up, once per row.  grid n_rows; block 256.
+__global__ void __launch_bounds__(256) k_quant_rows(const float *__restrict__ x, int n_embd,
+                                                    int8_t *__restrict__ xq, float *__restrict__ xd,
+                                                    float *__restrict__ xs) {
+    const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int nblk = n_embd / 32;
+    for (int b = warp; b < nblk; b += nw)
+        q8_block_warp(x[(size_t)t * n_embd + 32 * b + lane], lane, xq + (size_t)t * n_embd + 32 * b,
+                      xd + (size_t)t * nblk + b, xs + (size_t)t * nblk + b);
+}
+
+// Sum of each of 16 values over the 32 lanes, with every lane pair (l, l ^ o)
+// combined at o = 16, 8, 4, 2, 1 exactly as warp_sum combines them, so each
+// sum is bit-identical to warp_sum of that value.  Values are halved at each
+// level: lane l ends with the sum of value l >> 1.
+__device__ __forceinline__ float warp_sum16(float (&v)[16], int lane) {
+    float a[8], b[4], c[2];
+    const bool u16 = lane & 16, u8 = lane & 8, u4 = lane & 4, u2 = lane & 2;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float keep = u16 ? v[8 + i] : v[i], send = u16 ? v[i] : v[8 + i];
+        a[i] = keep + __shfl_xor_sync(MOE_FULL, send, 16);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float keep = u8 ? a[4 + i] : a[i], send = u8 ? a[i] : a[4 + i];
+        b[i] = keep + __shfl_xor_sync(MOE_FULL, send, 8);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const float keep = u4 ? b[2 + i] : b[i], send = u4 ? b[i] : b[2 + i];
+        c[i] = keep + __shfl_xor_sync(MOE_FULL, send, 4);
+    }
+    const float keep = u2 ? c[1] : c[0], send = u2 ? c[0] : c[1];
+    float d = keep + __shfl_xor_sync(MOE_FULL, send, 2);
+    return d + __shfl_xor_sync(MOE_FULL, d, 1);
+}
+
+// Padded shared-memory layouts of the tile's Q8_1 rows.  A lane reads one
+// contiguous unit of a row (Q4_K: 64 int8, Q6_K: 128 int8) with 16-byte
+// loads.  Units are stored at a 16-byte-padded stride (80 and 144 bytes), so
+// the 8 lanes of a load phase hit disjoint banks.
+#define PAD_U64 80     // stride of a 64-int8 unit
+#define PAD_U128 144   // stride of a 128-int8 unit
+
+// Copy rows[j] (j < np) of a Q8_1 buffer (values q [.][n], d/s [.][n/32])
+// into shared memory: values unit-padded (`unit` int8 per unit, `stride`
+// bytes apart), d and s dense [j][n/32].
+__device__ __forceinline__ void stage_q8_padded(int8_t *q_s, float *d_s, float *s_s, const int8_t *q,
+                                                const float *d, const float *sg, const int *rows,
+                                                int np, int n, int unit, int stride) {
+    const int c16 = n / 16, cpu = unit / 16, nb = n / 32;
+    const int rowb = (n / unit) * stride;
+    for (int i = threadIdx.x; i < np * c16; i += blockDim.x) {
+        const int j = i / c16, c = i % c16;
+        *reinterpret_cast<int4 *>(q_s + (size_t)j * rowb + (c / cpu) * stride + (c % cpu) * 16) =
+            reinterpret_cast<const int4 *>(q + (size_t)rows[j] * n)[c];
+    }
+    for (int i = threadIdx.x; i < np * nb; i += blockDim.x) {
+        const int j = i / nb, c = i % nb;
+        d_s[j * nb + c] = d[(size_t)rows[j] * nb + c];
+        if (s_s) s_s[j * nb + c] = sg[(size_t)rows[j] * nb + c];
+    }
+}
+
+// Gate/up for the pairs of one tile over GU2_ROWS rows.  grid (n_ff / 32, max
+// tiles); block 256.  The CTA stages in shared memory:
+// - its 32 gate and 32 up rows (bulk copy; plain loads for a missed expert);
+// - the tile's Q8_1 token rows.
+// Each warp takes 4 rows:
+// - every lane decodes its unit of the row once;
+// - for every pair, the per-pair kernel's unit dots;
+// - one transposed reduction of all 2 x np sums (warp_sum's pairing).
+// Every activation is therefore bit-identical to k_gate_up's.  The 32
+// activations of each pair form one Q8_1 block, quantised as k_down does,
+// into aq/ad/as [pos][...].
+__global__ void __launch_bounds__(256, 2) k_gate_up_grouped(
+    ExpertSrc src, const int8_t *__restrict__ xq, const float *__restrict__ xd,
+    const float *__restrict__ xs, const int32_t *__restrict__ off, const int32_t *__restrict__ cnt,
+    const int32_t *__restrict__ pos_pair, const int32_t *__restrict__ tiles,
+    const int32_t *__restrict__ n_tiles, int k, int n_embd, int n_ff, int8_t *__restrict__ aq,
+    float *__restrict__ ad, float *__restrict__ as, int *err) {
+    extern __shared__ __align__(128) uint8_t smg[];
+    __shared__ float act_s[GROUP_TILE][GU2_ROWS];
+    __shared__ int s_tok[GROUP_TILE];
+    __shared__ __align__(8) uint64_t bar;
     if ((int)blockIdx.y >= *n_tiles) return;
     const int tl = tiles[blockIdx.y], e = tl >> 16, tt = tl & 0xFFFF;
     const int pos0 = off[e] + tt * GROUP_TILE;
     const int np = min(GROUP_TILE, cnt[e] - tt * GROUP_TILE);
-    const int nblk = n_embd / 32;
-    int8_t *xq = reinterpret_cast<int8_t *>(smg);                           // [np][n_embd]
-    float *xd = reinterpret_cast<float *>(smg + (size_t)GROUP_TILE * n_embd); // [np][nblk]
-    float *xs = xd + GROUP_TILE * nblk;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    for (int b = warp; b < np * nblk; b += nw) {
-        const int j = b / nblk, bb = b % nblk;
-        const int t = pos_pair[pos0 + j] / k;
-        q8_block_warp(x[(size_t)t * n_embd + 32 * bb + lane], lane, xq + (size_t)j * n_embd + 32 * bb,
-                      xd + j * nblk + bb, xs + j * nblk + bb);
-    }
-    __syncthreads();
     const uint8_t *gbase = expert_ptr(src, 0, e);
     const uint8_t *ubase = expert_ptr(src, 1, e);
     if (!gbase || !ubase) {
         if (threadIdx.x == 0) atomicOr(err, MOE_DEV_ERR_INDEX);
         return;
     }
-    const int nb = n_embd / MOE_QK;
-    const size_t rb = (size_t)nb * MOE_Q4K_BYTES;
-    const int units = nb * 4;
-    const int i0 = blockIdx.x * GU_ROWS;
-    for (int r = warp; r < GU_ROWS; r += nw) {
-        const int i = i0 + r;
-        if (i >= n_ff) break;
-        for (int j = 0; j < np; ++j) {
-            const int8_t *q = xq + (size_t)j * n_embd;
-            float g = 0.0f, up = 0.0f;
-            for (int uu = lane; uu < units; uu += 32) {
-                ActQ4 aa;
-                load_act_q4(aa, q, xd + j * nblk, xs + j * nblk, uu >> 2, uu & 3);
-                g += q4k_unit_dot(gbase + i * rb + (uu >> 2) * MOE_Q4K_BYTES, uu & 3, aa);
-                up += q4k_unit_dot(ubase + i * rb + (uu >> 2) * MOE_Q4K_BYTES, uu & 3, aa);
-            }
-            g = warp_sum(g);
-            up = warp_sum(up);
-            if (lane == 0) act[(size_t)(pos0 + j) * n_ff + i] = silu_mul(g, up);
+    if (threadIdx.x < np) s_tok[threadIdx.x] = pos_pair[pos0 + threadIdx.x] / k;
+    const size_t rb = (size_t)(n_embd / MOE_QK) * MOE_Q4K_BYTES;
+    const int i0 = blockIdx.x * GU2_ROWS;
+    const uint32_t bytes = (uint32_t)(GU2_ROWS * rb);
+    const int nblk = n_embd / 32;
+    const int xrow = (n_embd / 64) * PAD_U64;                                    // padded row bytes
+    uint8_t *g_sm = smg, *u_sm = smg + bytes;
+    int8_t *xq_s = reinterpret_cast<int8_t *>(smg + 2 * bytes);                 // [8][xrow]
+    float *xd_s = reinterpret_cast<float *>(xq_s + (size_t)GROUP_TILE * xrow);   // [8][nblk]
+    float *xs_s = xd_s + GROUP_TILE * nblk;
+    const bool dev = expert_on_device(src, e);
+    if (dev && threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+        mbar_arrive_expect_tx(&bar, 2 * bytes);
+        bulk_g2s(g_sm, gbase + i0 * rb, bytes, &bar);
+        bulk_g2s(u_sm, ubase + i0 * rb, bytes, &bar);
+    }
+    __syncthreads();
+    stage_q8_padded(xq_s, xd_s, xs_s, xq, xd, xs, s_tok, np, n_embd, 64, PAD_U64);
+    if (!dev)
+        for (uint32_t o = threadIdx.x * 16; o < bytes; o += blockDim.x * 16) {
+            *reinterpret_cast<uint4 *>(g_sm + o) = *reinterpret_cast<const uint4 *>(gbase + i0 * rb + o);
+            *reinterpret_cast<uint4 *>(u_sm + o) = *reinterpret_cast<const uint4 *>(ubase + i0 * rb + o);
         }
+    const bool ok = !dev || mbar_wait(&bar, 0);
+    if (__syncthreads_or(!ok)) {
+        if (threadIdx.x == 0) atomicOr(err, MOE_DEV_ERR_TIMEOUT);
+        return;
+    }
+    const int units = (n_embd / MOE_QK) * 4;   // n_embd == 2048: one unit per lane
+    const bool on = lane < units;
+    const int sb = lane >> 2, pp = lane & 3;
+    for (int r = warp; r < GU2_ROWS; r += nw) {
+        Q4UnitDec dg, du;
+        if (on) {
+            Q4Unit w;
+            q4k_unit_load(g_sm + r * rb + sb * MOE_Q4K_BYTES, pp, w);
+            q4k_unit_decode(w, pp, dg);
+            q4k_unit_load(u_sm + r * rb + sb * MOE_Q4K_BYTES, pp, w);
+            q4k_unit_decode(w, pp, du);
+        }
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < GROUP_TILE; ++j) {
+            float g = 0.0f, up = 0.0f;
+            if (on && j < np) {
+                ActQ4 a;
+                load_act_q4_unit(a, xq_s + (size_t)j * xrow + lane * PAD_U64, xd_s + j * nblk,
+                                 xs_s + j * nblk, 2 * lane);
+                g += q4k_dec_compute(dg, a);
+                up += q4k_dec_compute(du, a);
+            }
+            v[j] = g;
+            v[GROUP_TILE + j] = up;
+        }
+        const float sum = warp_sum16(v, lane);      // lane l: value l >> 1
+        const float other = __shfl_down_sync(MOE_FULL, sum, 16);   // lane l < 16: value 8 + (l >> 1)
+        if (lane < 16 && !(lane & 1) && (lane >> 1) < np)
+            act_s[lane >> 1][r] = silu_mul(sum, other);
+    }
+    __syncthreads();
+    const int ablk = n_ff / 32;
+    for (int j = warp; j < np; j += nw) {
+        const size_t pos = (size_t)(pos0 + j);
+        q8_block_warp(act_s[j][lane], lane, aq + pos * n_ff + i0, ad + pos * ablk + i0 / 32,
+                      as + pos * ablk + i0 / 32);
     }
 }
 
 // Down rows for the pairs of one tile, unweighted: ypair[pos][h].  grid
-// (ceil(n_embd / DN_ROWS), max tiles); block 256; warp j takes pair j with
-// the per-pair kernel's lane mapping (Q6_K: 8-lane groups over half blocks).
-__global__ void __launch_bounds__(256) k_down_grouped(ExpertSrc src, const float *__restrict__ act,
-                                                      const int32_t *__restrict__ off,
-                                                      const int32_t *__restrict__ cnt,
-                                                      const int32_t *__restrict__ tiles,
-                                                      const int32_t *__restrict__ n_tiles,
-                                                      int n_embd, int n_ff, int down_type,
-                                                      float *__restrict__ ypair, int *err) {
-    extern __shared__ __align__(16) uint8_t smg[];
+// (n_embd / 64, max tiles); block 256.  The CTA stages its 64 rows and the
+// tile's Q8_1 activations in shared memory; warp w takes rows 8w .. 8w + 7.
+// Each lane decodes its half block (Q6_K; 8-lane row groups) or unit (Q4_K)
+// once per row and dots it with every pair's activations: the per-pair
+// kernel's arithmetic and reduction, bit for bit.
+__global__ void __launch_bounds__(256, 2) k_down_grouped(
+    ExpertSrc src, const int8_t *__restrict__ aq, const float *__restrict__ ad,
+    const float *__restrict__ as, const int32_t *__restrict__ off, const int32_t *__restrict__ cnt,
+    const int32_t *__restrict__ tiles, const int32_t *__restrict__ n_tiles, int n_embd, int n_ff,
+    int down_type, float *__restrict__ ypair, int *err) {
+    extern __shared__ __align__(128) uint8_t smg[];
+    __shared__ int s_pos[GROUP_TILE];
+    __shared__ __align__(8) uint64_t bar;
     if ((int)blockIdx.y >= *n_tiles) return;
     const int tl = tiles[blockIdx.y], e = tl >> 16, tt = tl & 0xFFFF;
     const int pos0 = off[e] + tt * GROUP_TILE;
     const int np = min(GROUP_TILE, cnt[e] - tt * GROUP_TILE);
-    const int nblk = n_ff / 32;
-    int8_t *aq = reinterpret_cast<int8_t *>(smg);                            // [np][n_ff]
-    float *ad = reinterpret_cast<float *>(smg + (size_t)GROUP_TILE * n_ff);  // [np][nblk]
-    float *as = ad + GROUP_TILE * nblk;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    for (int b = warp; b < np * nblk; b += nw) {
-        const int j = b / nblk, bb = b % nblk;
-        q8_block_warp(act[(size_t)(pos0 + j) * n_ff + 32 * bb + lane], lane,
-                      aq + (size_t)j * n_ff + 32 * bb, ad + j * nblk + bb, as + j * nblk + bb);
-    }
-    __syncthreads();
     const uint8_t *dbase = expert_ptr(src, 2, e);
     if (!dbase) {
         if (threadIdx.x == 0) atomicOr(err, MOE_DEV_ERR_INDEX);
         return;
     }
-    const int h0 = blockIdx.x * DN_ROWS;
-    const int nb = n_ff / MOE_QK;
-    for (int j = warp; j < np; j += nw) {
-        const int8_t *q = aq + (size_t)j * n_ff;
-        const float *dq = ad + j * nblk;
-        const float *sq = as + j * nblk;
-        float *yrow = ypair + (size_t)(pos0 + j) * n_embd;
-        if (down_type == MOE_QT_Q6K) {
-            const size_t rb = (size_t)nb * MOE_Q6K_BYTES;
-            const int grp = lane >> 3, u = lane & 7;
-            const bool on = u < nb * 2;
-            const int sb = u >> 1, hh = u & 1;
-            ActHalf a;
-            if (on) load_act_half(a, q, dq, sb, hh);
-            for (int r0w = 0; r0w < DN_ROWS; r0w += 4) {
-                const int r = r0w + grp, h = h0 + r;
-                float v = 0.0f;
-                if (on && h < n_embd) v = q6k_half_dot(dbase + h * rb + sb * MOE_Q6K_BYTES, hh, a);
-                v = group8_sum(v);
-                if (u == 0 && h < n_embd) yrow[h] = v;
+    if (threadIdx.x < np) s_pos[threadIdx.x] = pos0 + threadIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nb = n_ff / MOE_QK, ablk = n_ff / 32;
+    const bool q6 = down_type == MOE_QT_Q6K;
+    const size_t rb = (size_t)nb * (q6 ? MOE_Q6K_BYTES : MOE_Q4K_BYTES);
+    const int h0 = blockIdx.x * DN2_ROWS;
+    const uint32_t bytes = (uint32_t)(DN2_ROWS * rb);
+    const int unit = q6 ? 128 : 64, stride = q6 ? PAD_U128 : PAD_U64;
+    const int arow = (n_ff / unit) * stride;                                      // padded row bytes
+    int8_t *aq_s = reinterpret_cast<int8_t *>(smg + ((bytes + 15) & ~15u));     // [8][arow]
+    float *ad_s = reinterpret_cast<float *>(aq_s + (size_t)GROUP_TILE * arow);   // [8][ablk]
+    float *as_s = ad_s + GROUP_TILE * ablk;
+    const bool dev = expert_on_device(src, e);
+    if (dev && threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+        mbar_arrive_expect_tx(&bar, bytes);
+        bulk_g2s(smg, dbase + h0 * rb, bytes, &bar);
+    }
+    __syncthreads();
+    stage_q8_padded(aq_s, ad_s, q6 ? nullptr : as_s, aq, ad, as, s_pos, np, n_ff, unit, stride);
+    if (!dev)
+        for (uint32_t o = threadIdx.x * 16; o < bytes; o += blockDim.x * 16)
+            *reinterpret_cast<uint4 *>(smg + o) = *reinterpret_cast<const uint4 *>(dbase + h0 * rb + o);
+    const bool ok = !dev || mbar_wait(&bar, 0);
+    if (__syncthreads_or(!ok)) {
+        if (threadIdx.x == 0) atomicOr(err, MOE_DEV_ERR_TIMEOUT);
+        return;
+    }
+    const int rw = warp * (DN2_ROWS / 8);        // first local row of this warp
+    if (q6) {
+        const int grp = lane >> 3, u = lane & 7;
+        const bool on = u < nb * 2;
+        const int sb = u >> 1, hh = u & 1;
+        for (int r0w = 0; r0w < DN2_ROWS / 8; r0w += 4) {
+            const int r = rw + r0w + grp;
+            Q6HalfDec w;
+            if (on) {
+                Q6Half raw;
+                q6k_half_load(smg + r * rb + sb * MOE_Q6K_BYTES, hh, raw);
+                q6k_half_decode(raw, w);
             }
-        } else {
-            const size_t rb = (size_t)nb * MOE_Q4K_BYTES;
-            const int units = nb * 4;
-            const bool active = lane < units;
-            ActQ4 a;
-            if (active) load_act_q4(a, q, dq, sq, lane >> 2, lane & 3);
-            for (int r = 0; r < DN_ROWS; ++r) {
-                const int h = h0 + r;
+            for (int j = 0; j < np; ++j) {
                 float v = 0.0f;
-                if (active && h < n_embd)
-                    v = q4k_unit_dot(dbase + h * rb + (lane >> 2) * MOE_Q4K_BYTES, lane & 3, a);
+                if (on) {
+                    ActHalf a;
+                    load_act_half_at(a, aq_s + (size_t)j * arow + u * PAD_U128, ad_s + j * ablk + 4 * u);
+                    v = q6k_dec_compute(w, a);
+                }
+                v = group8_sum(v);
+                if (u == 0) ypair[(size_t)s_pos[j] * n_embd + h0 + r] = v;
+            }
+        }
+    } else {
+        const int units = nb * 4;
+        const bool on = lane < units;
+        for (int rr = 0; rr < DN2_ROWS / 8; ++rr) {
+            const int r = rw + rr;
+            Q4UnitDec w;
+            if (on) {
+                Q4Unit raw;
+                q4k_unit_load(smg + r * rb + (lane >> 2) * MOE_Q4K_BYTES, lane & 3, raw);
+                q4k_unit_decode(raw, lane & 3, w);
+            }
+            for (int j = 0; j < np; ++j) {
+                float v = 0.0f;
+                if (on) {
+                    ActQ4 a;
+                    load_act_q4_unit(a, aq_s + (size_t)j * arow + lane * PAD_U64, ad_s + j * ablk,
+                                     as_s + j * ablk, 2 * lane);
+                    v = q4k_dec_compute(w, a);
+                }
                 v = warp_sum(v);
-                if (lane == 0 && h < n_embd) yrow[h] = v;
+                if (lane == 0) ypair[(size_t)s_pos[j] * n_embd + h0 + r] = v;
             }
         }
     }
@@ -271,28 +439,50 @@ cudaError_t launch_group(const int32_t *ids, int P, int n_expert, int tile, cons
     return cudaGetLastError();
 }
 
+size_t grouped_scratch_bytes(int P, int n_embd, int n_ff) {
+    // Q8_1 token rows, then Q8_1 activations: int8 values + d + s per 32
+    const size_t xq = (size_t)P * n_embd + 2 * sizeof(float) * (size_t)P * (n_embd / 32);
+    const size_t aq = (size_t)P * n_ff + 2 * sizeof(float) * (size_t)P * (n_ff / 32);
+    return ((xq + 255) & ~(size_t)255) + aq;
+}
+
 cudaError_t launch_experts_grouped(const ExpertSrc &src, const float *x, const GroupBufs &g,
                                    int n_tok, int k, int n_embd, int n_ff, int down_type,
-                                   const float *w, float *act, float *ypair, const float *resid,
+                                   const float *w, void *scratch, float *ypair, const float *resid,
                                    float *y, int *err, cudaStream_t s) {
+    if (n_embd != 2048 || n_ff % GU2_ROWS || n_embd % DN2_ROWS) return cudaErrorInvalidValue;
     const int P = n_tok * k;
     const int maxt = group_max_tiles(src.n_expert + 1, P, GROUP_TILE);
-    const size_t sm1 = (size_t)GROUP_TILE * n_embd + 2 * sizeof(float) * GROUP_TILE * (n_embd / 32);
-    cudaError_t e;
-    if (sm1 > 48 * 1024) {
-        e = cudaFuncSetAttribute(k_gate_up_grouped, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm1);
-        if (e != cudaSuccess) return e;
-    }
-    k_gate_up_grouped<<<dim3((n_ff + GU_ROWS - 1) / GU_ROWS, maxt), 256, sm1, s>>>(
-        src, x, g.off, g.cnt, g.pos_pair, g.tiles, g.n_tiles, k, n_embd, n_ff, act, err);
+    uint8_t *sc = static_cast<uint8_t *>(scratch);
+    int8_t *xq = reinterpret_cast<int8_t *>(sc);
+    float *xd = reinterpret_cast<float *>(sc + (size_t)n_tok * n_embd);
+    float *xs = xd + (size_t)n_tok * (n_embd / 32);
+    const size_t xbytes = (size_t)P * n_embd + 2 * sizeof(float) * (size_t)P * (n_embd / 32);
+    int8_t *aq = reinterpret_cast<int8_t *>(sc + ((xbytes + 255) & ~(size_t)255));
+    float *ad = reinterpret_cast<float *>(aq + (size_t)P * n_ff);
+    float *as = ad + (size_t)P * (n_ff / 32);
+    k_quant_rows<<<n_tok, 256, 0, s>>>(x, n_embd, xq, xd, xs);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const bool q6 = down_type == MOE_QT_Q6K;
+    const size_t sm1 = 2 * (size_t)GU2_ROWS * (n_embd / MOE_QK) * MOE_Q4K_BYTES +
+                       (size_t)GROUP_TILE * (n_embd / 64) * PAD_U64 +
+                       2 * sizeof(float) * GROUP_TILE * (n_embd / 32);
+    const size_t sm2 = (((size_t)DN2_ROWS * (n_ff / MOE_QK) * (q6 ? MOE_Q6K_BYTES : MOE_Q4K_BYTES) + 15) &
+                        ~(size_t)15) +
+                       (size_t)GROUP_TILE * (q6 ? (n_ff / 128) * PAD_U128 : (n_ff / 64) * PAD_U64) +
+                       2 * sizeof(float) * GROUP_TILE * (n_ff / 32);
+    if ((e = cudaFuncSetAttribute(k_gate_up_grouped, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)sm1)) != cudaSuccess)
+        return e;
+    if ((e = cudaFuncSetAttribute(k_down_grouped, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)sm2)) != cudaSuccess)
+        return e;
+    k_gate_up_grouped<<<dim3(n_ff / GU2_ROWS, maxt), 256, sm1, s>>>(
+        src, xq, xd, xs, g.off, g.cnt, g.pos_pair, g.tiles, g.n_tiles, k, n_embd, n_ff, aq, ad, as, err);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    const size_t sm2 = (size_t)GROUP_TILE * n_ff + 2 * sizeof(float) * GROUP_TILE * (n_ff / 32);
-    if (sm2 > 48 * 1024) {
-        e = cudaFuncSetAttribute(k_down_grouped, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2);
-        if (e != cudaSuccess) return e;
-    }
-    k_down_grouped<<<dim3((n_embd + DN_ROWS - 1) / DN_ROWS, maxt), 256, sm2, s>>>(
-        src, act, g.off, g.cnt, g.tiles, g.n_tiles, n_embd, n_ff, down_type, ypair, err);
+    k_down_grouped<<<dim3(n_embd / DN2_ROWS, maxt), 256, sm2, s>>>(
+        src, aq, ad, as, g.off, g.cnt, g.tiles, g.n_tiles, n_embd, n_ff, down_type, ypair, err);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     return launch_combine(ypair, g.pair_pos, w, n_tok, k, n_embd, resid, y, s);
 }

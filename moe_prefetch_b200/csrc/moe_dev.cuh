@@ -351,6 +351,20 @@ __device__ __forceinline__ void load_act_q4(ActQ4 &a, const int8_t *q, const flo
     a.s0 = s[b]; a.s1 = s[b + 1];
 }
 
+// load_act_q4 from a unit-padded copy: the 64 int8 of the unit at `qu`
+// (16-byte aligned) and its two Q8_1 blocks' d/s at d[b], s[b].
+__device__ __forceinline__ void load_act_q4_unit(ActQ4 &a, const int8_t *qu, const float *d,
+                                                 const float *s, int b) {
+    const int4 *ql = reinterpret_cast<const int4 *>(qu);
+    const int4 v0 = ql[0], v1 = ql[1], v2 = ql[2], v3 = ql[3];
+    a.lo[0] = v0.x; a.lo[1] = v0.y; a.lo[2] = v0.z; a.lo[3] = v0.w;
+    a.lo[4] = v1.x; a.lo[5] = v1.y; a.lo[6] = v1.z; a.lo[7] = v1.w;
+    a.hi[0] = v2.x; a.hi[1] = v2.y; a.hi[2] = v2.z; a.hi[3] = v2.w;
+    a.hi[4] = v3.x; a.hi[5] = v3.y; a.hi[6] = v3.z; a.hi[7] = v3.w;
+    a.d0 = d[b]; a.d1 = d[b + 1];
+    a.s0 = s[b]; a.s1 = s[b + 1];
+}
+
 __device__ __forceinline__ int byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xFF; }
 
 // 6-bit scale and min of sub-block j from the 12 scale bytes held in
@@ -368,13 +382,20 @@ __device__ __forceinline__ void q4k_sm(uint32_t w0, uint32_t w1, uint32_t w2, in
     }
 }
 
-// Partial dot of one unit of a Q4_K row (16-byte aligned block pointer `blk`
-// of super-block sb) with the unit's activations.  Loads are 128-bit.
-__device__ __forceinline__ float q4k_unit_dot(const uint8_t *blk, int p, const ActQ4 &a) {
-    const uint4 hdr = *reinterpret_cast<const uint4 *>(blk);
-    const uint4 q0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * p);
-    const uint4 q1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * p);
-    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+// The bytes of one unit of a Q4_K row: the block header (d, dmin, scales)
+// and the 32 quant bytes of sub-block pair p.
+struct Q4Unit {
+    uint4 hdr, q0, q1;
+};
+
+__device__ __forceinline__ void q4k_unit_load(const uint8_t *blk, int p, Q4Unit &w) {
+    w.hdr = *reinterpret_cast<const uint4 *>(blk);
+    w.q0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * p);
+    w.q1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * p);
+}
+
+__device__ __forceinline__ float q4k_unit_compute(const Q4Unit &u, int p, const ActQ4 &a) {
+    const uint32_t w[8] = {u.q0.x, u.q0.y, u.q0.z, u.q0.w, u.q1.x, u.q1.y, u.q1.z, u.q1.w};
     int slo = 0, shi = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -382,12 +403,55 @@ __device__ __forceinline__ float q4k_unit_dot(const uint8_t *blk, int p, const A
         shi = __dp4a((int)((w[i] >> 4) & 0x0F0F0F0Fu), a.hi[i], shi);
     }
     int sc0, m0, sc1, m1;
-    q4k_sm(hdr.y, hdr.z, hdr.w, 2 * p, sc0, m0);
-    q4k_sm(hdr.y, hdr.z, hdr.w, 2 * p + 1, sc1, m1);
-    const float d = h2f(hdr.x), dmin = h2f(hdr.x >> 16);
+    q4k_sm(u.hdr.y, u.hdr.z, u.hdr.w, 2 * p, sc0, m0);
+    q4k_sm(u.hdr.y, u.hdr.z, u.hdr.w, 2 * p + 1, sc1, m1);
+    const float d = h2f(u.hdr.x), dmin = h2f(u.hdr.x >> 16);
     const float acc = (float)(sc0 * slo) * a.d0 + (float)(sc1 * shi) * a.d1;
     const float mm = (float)m0 * a.s0 + (float)m1 * a.s1;
     return d * acc - dmin * mm;
+}
+
+// A Q4_K unit decoded once for many activation rows: the nibble words, the
+// integer scales / mins of its two sub-blocks, d and dmin.
+struct Q4UnitDec {
+    int lo[8], hi[8];
+    int sc0, m0, sc1, m1;
+    float d, dmin;
+};
+
+__device__ __forceinline__ void q4k_unit_decode(const Q4Unit &u, int p, Q4UnitDec &o) {
+    const uint32_t w[8] = {u.q0.x, u.q0.y, u.q0.z, u.q0.w, u.q1.x, u.q1.y, u.q1.z, u.q1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        o.lo[i] = (int)(w[i] & 0x0F0F0F0Fu);
+        o.hi[i] = (int)((w[i] >> 4) & 0x0F0F0F0Fu);
+    }
+    q4k_sm(u.hdr.y, u.hdr.z, u.hdr.w, 2 * p, o.sc0, o.m0);
+    q4k_sm(u.hdr.y, u.hdr.z, u.hdr.w, 2 * p + 1, o.sc1, o.m1);
+    o.d = h2f(u.hdr.x);
+    o.dmin = h2f(u.hdr.x >> 16);
+}
+
+// q4k_unit_compute on a decoded unit: the same integer sums and the same
+// float expression, bit for bit.
+__device__ __forceinline__ float q4k_dec_compute(const Q4UnitDec &u, const ActQ4 &a) {
+    int slo = 0, shi = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        slo = __dp4a(u.lo[i], a.lo[i], slo);
+        shi = __dp4a(u.hi[i], a.hi[i], shi);
+    }
+    const float acc = (float)(u.sc0 * slo) * a.d0 + (float)(u.sc1 * shi) * a.d1;
+    const float mm = (float)u.m0 * a.s0 + (float)u.m1 * a.s1;
+    return u.d * acc - u.dmin * mm;
+}
+
+// Partial dot of one unit of a Q4_K row (16-byte aligned block pointer `blk`
+// of super-block sb) with the unit's activations.  Loads are 128-bit.
+__device__ __forceinline__ float q4k_unit_dot(const uint8_t *blk, int p, const ActQ4 &a) {
+    Q4Unit u;
+    q4k_unit_load(blk, p, u);
+    return q4k_unit_compute(u, p, a);
 }
 
 // ---------------------------------------------------------------------------
@@ -497,37 +561,110 @@ __device__ __forceinline__ void load_act_half(ActHalf &a, const int8_t *q, const
     }
 }
 
-// Partial dot of half h of the Q6_K block at `blk` (2-byte aligned): for each
-// of its 8 scale groups (m, lower/upper 16 of l) an integer sum, scaled by the
-// group scale and the Q8_1 d, accumulated in (m, group) order; times the
-// block's d.
-__device__ __forceinline__ float q6k_half_dot(const uint8_t *blk, int h, const ActHalf &a) {
+// The bytes of half h of a Q6_K block, realigned into words: ql (low and
+// high 32), qh, the 8 scales and d.
+struct Q6Half {
     uint32_t lo[8], hi[8], qh[8], sc[2];
-    ldw_a2<8>(blk + 64 * h, lo);          // ql[64h + l],      l = 0..31
-    ldw_a2<8>(blk + 64 * h + 32, hi);     // ql[64h + 32 + l]
-    ldw_a2<8>(blk + 128 + 32 * h, qh);    // qh[32h + l]
-    ldw_a2<2>(blk + 192 + 8 * h, sc);     // scales[8h .. 8h+7]
-    const float d = h2f(*reinterpret_cast<const uint16_t *>(blk + 208));
+    float d;
+};
+
+// Load half h of the Q6_K block at `blk` (2-byte aligned).
+__device__ __forceinline__ void q6k_half_load(const uint8_t *blk, int h, Q6Half &w) {
+    ldw_a2<8>(blk + 64 * h, w.lo);          // ql[64h + l],      l = 0..31
+    ldw_a2<8>(blk + 64 * h + 32, w.hi);     // ql[64h + 32 + l]
+    ldw_a2<8>(blk + 128 + 32 * h, w.qh);    // qh[32h + l]
+    ldw_a2<2>(blk + 192 + 8 * h, w.sc);     // scales[8h .. 8h+7]
+    w.d = h2f(*reinterpret_cast<const uint16_t *>(blk + 208));
+}
+
+// Partial dot of a loaded Q6_K half with a half of Q8_1 activations: for
+// each of its 8 scale groups (m, lower/upper 16 of l) an integer sum, scaled
+// by the group scale and the Q8_1 d, accumulated in (m, group) order; times
+// the block's d.
+__device__ __forceinline__ float q6k_half_compute(const Q6Half &w, const ActHalf &a) {
     float acc = 0.0f;
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
         int is0 = 0, is1 = 0;
 #pragma unroll
-        for (int w = 0; w < 8; ++w) {
-            const uint32_t src = (m & 1) ? hi[w] : lo[w];
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t src = (m & 1) ? w.hi[i] : w.lo[i];
             const uint32_t nib = (m >> 1) ? ((src >> 4) & 0x0F0F0F0Fu) : (src & 0x0F0F0F0Fu);
-            const uint32_t hb = ((qh[w] >> (2 * m)) & 0x03030303u) << 4;
+            const uint32_t hb = ((w.qh[i] >> (2 * m)) & 0x03030303u) << 4;
             const int v = (int)__vsub4(nib | hb, 0x20202020u);
-            if (w < 4) is0 = __dp4a(v, a.q[m][w], is0);
-            else is1 = __dp4a(v, a.q[m][w], is1);
+            if (i < 4) is0 = __dp4a(v, a.q[m][i], is0);
+            else is1 = __dp4a(v, a.q[m][i], is1);
         }
         const int g0 = 2 * m, g1 = 2 * m + 1;   // scale bytes within the 8 loaded
-        const int s0 = (int)(int8_t)((sc[g0 >> 2] >> (8 * (g0 & 3))) & 0xFF);
-        const int s1 = (int)(int8_t)((sc[g1 >> 2] >> (8 * (g1 & 3))) & 0xFF);
+        const int s0 = (int)(int8_t)((w.sc[g0 >> 2] >> (8 * (g0 & 3))) & 0xFF);
+        const int s1 = (int)(int8_t)((w.sc[g1 >> 2] >> (8 * (g1 & 3))) & 0xFF);
         acc += (float)(s0 * is0) * a.d[m];
         acc += (float)(s1 * is1) * a.d[m];
     }
-    return d * acc;
+    return w.d * acc;
+}
+
+// A Q6_K half decoded once for many activation rows: the signed 6-bit values
+// (q - 32) as int8x4 words per quarter m, the 8 scales and d.
+struct Q6HalfDec {
+    int v[4][8];
+    int sc[8];
+    float d;
+};
+
+__device__ __forceinline__ void q6k_half_decode(const Q6Half &w, Q6HalfDec &o) {
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t src = (m & 1) ? w.hi[i] : w.lo[i];
+            const uint32_t nib = (m >> 1) ? ((src >> 4) & 0x0F0F0F0Fu) : (src & 0x0F0F0F0Fu);
+            const uint32_t hb = ((w.qh[i] >> (2 * m)) & 0x03030303u) << 4;
+            o.v[m][i] = (int)__vsub4(nib | hb, 0x20202020u);
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < 8; ++g) o.sc[g] = (int)(int8_t)((w.sc[g >> 2] >> (8 * (g & 3))) & 0xFF);
+    o.d = w.d;
+}
+
+// q6k_half_compute on a decoded half: the same integer sums, scales and
+// float accumulation order, bit for bit.
+__device__ __forceinline__ float q6k_dec_compute(const Q6HalfDec &w, const ActHalf &a) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        int is0 = 0, is1 = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if (i < 4) is0 = __dp4a(w.v[m][i], a.q[m][i], is0);
+            else is1 = __dp4a(w.v[m][i], a.q[m][i], is1);
+        }
+        acc += (float)(w.sc[2 * m] * is0) * a.d[m];
+        acc += (float)(w.sc[2 * m + 1] * is1) * a.d[m];
+    }
+    return w.d * acc;
+}
+
+// load_act_half from a half-padded copy: the 128 int8 of the half at `qh`
+// (16-byte aligned) and the d of its four Q8_1 blocks at d[0..3].
+__device__ __forceinline__ void load_act_half_at(ActHalf &a, const int8_t *qh, const float *d) {
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        const int4 *qp = reinterpret_cast<const int4 *>(qh + 32 * m);
+        const int4 v0 = qp[0], v1 = qp[1];
+        a.q[m][0] = v0.x; a.q[m][1] = v0.y; a.q[m][2] = v0.z; a.q[m][3] = v0.w;
+        a.q[m][4] = v1.x; a.q[m][5] = v1.y; a.q[m][6] = v1.z; a.q[m][7] = v1.w;
+        a.d[m] = d[m];
+    }
+}
+
+// Partial dot of half h of the Q6_K block at `blk` (2-byte aligned) with a
+// half of Q8_1 activations.
+__device__ __forceinline__ float q6k_half_dot(const uint8_t *blk, int h, const ActHalf &a) {
+    Q6Half w;
+    q6k_half_load(blk, h, w);
+    return q6k_half_compute(w, a);
 }
 
 // Sum over the 8 lanes of an aligned 8-lane group, butterfly 1, 2, 4 (fixed

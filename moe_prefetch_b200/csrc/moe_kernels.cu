@@ -6,6 +6,8 @@
 // The persistent multi-layer decode kernel lives in moe_decode.cu.
 #include "moe_kernels.h"
 
+#include <algorithm>
+
 namespace moe {
 
 // ===========================================================================
@@ -194,48 +196,62 @@ __global__ void __launch_bounds__(512) k_router(const float *__restrict__ W,
 }
 
 // Router for a batch (no prior, no observation: both apply to single tokens
-// only).  grid ceil(n_tok / RB_TOK); block 512.  The CTA keeps RB_TOK token
-// rows in shared memory.  Warp w takes experts w, w + 16, ...: it loads its
-// lanes' slice of the router row once (n_embd == 2048: 16 float4 per lane)
-// and runs the four fma chains of router_dot_warp for every token.  Every
-// logit is therefore computed in router_dot_warp's order, bit-identical to
+// only).  grid ceil(n_tok / tpc); block 256; tpc <= RB_TOK tokens per CTA.
+// The CTA keeps its token rows in shared memory.  Warp w takes experts
+// w, w + 8, ... two at a time: it loads its lanes' slice of both router
+// rows (n_embd == 2048: 16 float4 per lane each) before using either, then
+// runs the four fma chains of router_dot_warp for every token.  Every logit
+// is therefore computed in router_dot_warp's order, bit-identical to
 // k_router.  Then warp t selects for token t (router_select_warp).
 #define RB_TOK 8
 
-__global__ void __launch_bounds__(512) k_router_batch(const float *__restrict__ W,
+__device__ __forceinline__ float router_chain_dot(const float4 (&wv)[16], const float *xt, int lane) {
+    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+        const float4 xv = *reinterpret_cast<const float4 *>(xt + 128 * kk + 4 * lane);
+        a0 = __fmaf_rn(wv[kk].x, xv.x, a0);
+        a1 = __fmaf_rn(wv[kk].y, xv.y, a1);
+        a2 = __fmaf_rn(wv[kk].z, xv.z, a2);
+        a3 = __fmaf_rn(wv[kk].w, xv.w, a3);
+    }
+    float v = __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(MOE_FULL, v, off));
+    return v;
+}
+
+__global__ void __launch_bounds__(256) k_router_batch(const float *__restrict__ W,
                                                       const float *__restrict__ x, int n_tok,
-                                                      int n_expert, int k,
+                                                      int tpc, int n_expert, int k,
                                                       int32_t *__restrict__ ids,
                                                       float *__restrict__ w) {
     extern __shared__ __align__(16) float sm[];
-    float *xs = sm;                                   // [RB_TOK][2048]
-    float *lg = sm + RB_TOK * 2048;                   // [RB_TOK][n_expert]
-    const int t0 = blockIdx.x * RB_TOK;
-    const int nt = min(RB_TOK, n_tok - t0);
+    float *xs = sm;                                   // [tpc][2048]
+    float *lg = sm + tpc * 2048;                      // [tpc][n_expert]
+    const int t0 = blockIdx.x * tpc;
+    const int nt = min(tpc, n_tok - t0);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     for (int i = threadIdx.x; i < nt * 512; i += blockDim.x)
         reinterpret_cast<float4 *>(xs)[i] = reinterpret_cast<const float4 *>(x + (size_t)t0 * 2048)[i];
     __syncthreads();
-    for (int e = warp; e < n_expert; e += nw) {
-        float4 wv[16];
+    for (int e = warp; e < n_expert; e += 2 * nw) {
+        const int e2 = e + nw;
+        const bool two = e2 < n_expert;
+        float4 wa[16], wb[16];
 #pragma unroll
-        for (int kk = 0; kk < 16; ++kk)
-            wv[kk] = __ldg(reinterpret_cast<const float4 *>(W + (size_t)e * 2048 + 128 * kk + 4 * lane));
+        for (int kk = 0; kk < 16; ++kk) {
+            wa[kk] = __ldg(reinterpret_cast<const float4 *>(W + (size_t)e * 2048 + 128 * kk + 4 * lane));
+            wb[kk] = two ? __ldg(reinterpret_cast<const float4 *>(W + (size_t)e2 * 2048 + 128 * kk + 4 * lane))
+                         : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
         for (int t = 0; t < nt; ++t) {
-            const float *xt = xs + t * 2048;
-            float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-#pragma unroll
-            for (int kk = 0; kk < 16; ++kk) {
-                const float4 xv = *reinterpret_cast<const float4 *>(xt + 128 * kk + 4 * lane);
-                a0 = __fmaf_rn(wv[kk].x, xv.x, a0);
-                a1 = __fmaf_rn(wv[kk].y, xv.y, a1);
-                a2 = __fmaf_rn(wv[kk].z, xv.z, a2);
-                a3 = __fmaf_rn(wv[kk].w, xv.w, a3);
+            const float va = router_chain_dot(wa, xs + t * 2048, lane);
+            const float vb = router_chain_dot(wb, xs + t * 2048, lane);
+            if (lane == 0) {
+                lg[t * n_expert + e] = va;
+                if (two) lg[t * n_expert + e2] = vb;
             }
-            float v = __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
-#pragma unroll
-            for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(MOE_FULL, v, off));
-            if (lane == 0) lg[t * n_expert + e] = v;
         }
     }
     __syncthreads();
@@ -565,11 +581,16 @@ cudaError_t launch_router(const float *W, const float *x, int n_tok, int n_exper
                           int32_t *ids, float *w, float *logits, const SlotState *st,
                           int observe_layer_idx, cudaStream_t s) {
     if (n_tok > 1 && n_embd == 2048 && !use_prior && observe_layer_idx < 0 && !logits) {
-        const size_t sm = sizeof(float) * ((size_t)RB_TOK * 2048 + (size_t)RB_TOK * n_expert);
+        // tokens per CTA: enough CTAs to cover the SMs, at most RB_TOK
+        int dev = 0, sms = 148;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const int tpc = std::max(1, std::min(RB_TOK, n_tok / std::max(1, sms)));
+        const size_t sm = sizeof(float) * ((size_t)tpc * 2048 + (size_t)tpc * n_expert);
         cudaError_t e = cudaFuncSetAttribute(k_router_batch, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)sm);
         if (e != cudaSuccess) return e;
-        k_router_batch<<<(n_tok + RB_TOK - 1) / RB_TOK, 512, sm, s>>>(W, x, n_tok, n_expert, k, ids, w);
+        k_router_batch<<<(n_tok + tpc - 1) / tpc, 256, sm, s>>>(W, x, n_tok, tpc, n_expert, k, ids, w);
         return cudaGetLastError();
     }
     const size_t smem = sizeof(float) * ((size_t)n_embd + n_expert);

@@ -36,6 +36,14 @@ __device__ __forceinline__ const uint8_t *expert_ptr(const ExpertSrc &s, int whi
     return host ? host + (int64_t)id * bytes : nullptr;
 }
 
+// True when expert `id`'s bytes are in device memory (a slot or the shared
+// expert), false for a miss read from the registered host copy.
+__device__ __forceinline__ bool expert_on_device(const ExpertSrc &s, int id) {
+    if (id == s.n_expert) return true;
+    const int32_t slot = s.table ? s.table[id] : s.ns;
+    return slot != s.ns && s.gate;
+}
+
 #define GU_ROWS 32   // gate/up rows per CTA of the stand-alone GEMVs
 #define DN_ROWS 16   // down rows per CTA of the stand-alone GEMVs
 
@@ -73,11 +81,13 @@ cudaError_t launch_append_shared(const int32_t *ids, const float *w, int n_tok, 
                                  int32_t *ids_x, float *w_x, cudaStream_t s);
 cudaError_t launch_group(const int32_t *ids, int P, int n_expert, int tile, const GroupBufs &g,
                          int *err, cudaStream_t s);
-// gate/up + down over the grouped pairs (act [P][n_ff], ypair [P][n_embd]
-// scratch), then the combine into y.
+// bytes of scratch launch_experts_grouped needs for P pairs
+size_t grouped_scratch_bytes(int P, int n_embd, int n_ff);
+// gate/up + down over the grouped pairs (`scratch`: Q8_1 token rows and
+// activations; ypair [P][n_embd]), then the combine into y.  n_embd 2048.
 cudaError_t launch_experts_grouped(const ExpertSrc &src, const float *x, const GroupBufs &g,
                                    int n_tok, int k, int n_embd, int n_ff, int down_type,
-                                   const float *w, float *act, float *ypair, const float *resid,
+                                   const float *w, void *scratch, float *ypair, const float *resid,
                                    float *y, int *err, cudaStream_t s);
 cudaError_t launch_combine(const float *ypair, const int32_t *pair_pos, const float *w, int n_tok,
                            int k, int n_embd, const float *resid, float *y, cudaStream_t s);
