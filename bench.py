@@ -50,6 +50,24 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
+def capture(step):
+    """One CUDA graph of step(), replayed once to check it; None when the
+    capture is refused (then the step runs eagerly)."""
+    import torch
+    g = torch.cuda.CUDAGraph()
+    try:
+        with torch.cuda.graph(g):
+            step()
+        g.replay()
+        torch.cuda.synchronize()
+        return g
+    except Exception as e:   # capture unsupported here: eager steps
+        print(f"cuda graph capture failed ({type(e).__name__}: {str(e)[:120]}); eager steps",
+              file=sys.stderr)
+        torch.cuda.synchronize()
+        return None
+
+
 def ar1_states(n_tok, n_embd, seed, rho=0.9):
     rng = np.random.default_rng(seed)
     h = np.empty((n_tok, n_embd), np.float32)
@@ -371,10 +389,17 @@ def run_config3(args):
         h = rng.standard_normal((n, N_EMBD))
         return (h / np.sqrt((h ** 2).mean(-1, keepdims=True))).astype(np.float32)
 
-    def timed(x, steps, warmup, path):
-        for _ in range(warmup):
+    def timed(x, steps, warmup, path, graph):
+        def step():
             for il in range(n_layers):
                 ep.layer_forward(il, x, path)
+        for _ in range(warmup):
+            step()
+        g = None
+        if graph:   # fixed-capacity exchange: the whole step replays as one CUDA graph
+            torch.cuda.synchronize()
+            g = capture(step)
+        used_graph[0] = g is not None
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
@@ -382,31 +407,36 @@ def run_config3(args):
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(steps):
-            for il in range(n_layers):
-                ep.layer_forward(il, x, path)
+            if g is not None:
+                g.replay()
+            else:
+                step()
         e1.record(stream)
         torch.cuda.synchronize()
         t = torch.tensor([e0.elapsed_time(e1)], device="cuda", dtype=torch.float64)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        del g
         return float(t[0])
 
+    used_graph = [False]
     lines = []
     dec_seqs, dec_steps = 32, args.c3_decode_steps
     if dec_seqs % world == 0:
         x = torch.from_numpy(rows(dec_seqs, 500)[rank::world].copy()).cuda()
-        ms = timed(x, dec_steps, args.warmup, "auto")
+        ms = timed(x, dec_steps, args.warmup, "auto", graph=True)
         lines.append({
             "metric": "config3 expert-parallel batched decode", "value": dec_seqs * dec_steps / (ms / 1e3),
             "unit": "tok/s", "n_gpus": world, "steps": dec_steps, "warmup": args.warmup,
             "ms_per_step": ms / dec_steps, "higher_is_better": True, "scaling": "strong",
             "config": {"workload": f"config3 decode: {dec_seqs} sequences x {dec_steps} steps, "
                                    f"{n_layers} layers, EP {N_EXPERT // world} experts/GPU",
-                       "path": "auto (grouped GEMV at 32 tokens)", "data": "synthetic"}})
+                       "path": "grouped GEMV, fixed-capacity exchange",
+                       "cuda_graph": used_graph[0], "data": "synthetic"}})
     pre_tok, chunks = 512, args.c3_prefill_chunks
     if pre_tok % world == 0:
         x = torch.from_numpy(rows(pre_tok, 501)[rank::world].copy()).cuda()
-        ms = timed(x, chunks, max(1, args.warmup), "auto")
+        ms = timed(x, chunks, max(1, args.warmup), "auto", graph=False)
         flops = 2.0 * pre_tok * TOP_K * 3 * N_EMBD * N_FF * n_layers * chunks
         lines.append({
             "metric": "config3 expert-parallel prefill", "value": pre_tok * chunks / (ms / 1e3),
@@ -551,9 +581,14 @@ def run_config4(args):
         xx = rng.standard_normal((seqs, N_EMBD))
         xx = (xx / np.sqrt((xx ** 2).mean(-1, keepdims=True))).astype(np.float32)
         x = torch.from_numpy(xx[rank::world].copy()).cuda()
-        for _ in range(args.warmup):
+
+        def step():
             for il in range(L):
                 ep.layer_forward(il, x, "auto")
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        g = capture(step)   # fixed-capacity exchange: one graph per step
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
@@ -561,10 +596,14 @@ def run_config4(args):
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(steps):
-            for il in range(L):
-                ep.layer_forward(il, x, "auto")
+            if g is not None:
+                g.replay()
+            else:
+                step()
         e1.record(stream)
         torch.cuda.synchronize()
+        graphed = g is not None
+        del g
         t = torch.tensor([e0.elapsed_time(e1)], device="cuda", dtype=torch.float64)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -573,7 +612,8 @@ def run_config4(args):
                       "unit": "tok/s", "n_gpus": world, "steps": steps, "ms_per_step": ms / steps,
                       "higher_is_better": True, "scaling": "strong",
                       "config": dict(cfg_base, workload=f"config4 decode: {seqs} sequences x {steps} steps, "
-                                                        f"EP {C4_EXPERT // world} experts/GPU, shared replicated")})
+                                                        f"EP {C4_EXPERT // world} experts/GPU, shared replicated",
+                                     cuda_graph=graphed)})
         ep.close()
     if rank == 0:
         for ln in lines:

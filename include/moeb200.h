@@ -195,16 +195,23 @@ int moe_layer_forward_path(moe_ctx *ctx, int layer, const float *x, float *y, in
 /* Route the n_tok home tokens x [n_tok][n_embd] (no cache prior, no
  * observation): ids/w [n_tok][n_used].  Pack the pairs for their owners in
  * rank order, pair order within a rank:
- *   send_count [world] (device), pos [n_tok*n_used] (send slot of pair
- *   t*n_used + r, -1 for an id out of range), send_ids / send_x
- *   [n_tok*n_used][...] (expert id and token row of each slot). */
+ *   send_count [world] (device);
+ *   pos [n_tok*n_used]: the send slot of pair t*n_used + r, -1 for an id
+ *   out of range;
+ *   send_ids / send_x: the expert id and token row of each slot.
+ * capacity == 0: the slots are dense, [n_tok*n_used][...], so an exchange
+ * needs send_count on the host.  capacity >= n_tok*n_used: rank d's pairs
+ * fill slots [d*capacity, ...) of [world*capacity][...] and the rest keep id
+ * -1 (moe_experts_rows skips them), so the exchange uses equal splits and
+ * never waits for the host. */
 int moe_ep_route_pack(moe_ctx *ctx, int layer, const float *x, int n_tok, int world,
-                      int32_t *ids, float *w, int32_t *send_count, int32_t *pos,
+                      int capacity, int32_t *ids, float *w, int32_t *send_count, int32_t *pos,
                       int32_t *send_ids, float *send_x, void *stream);
 
 /* The expert half for n_rows received rows: y_rows[i] = expert ids[i] applied
  * to x_rows[i], unweighted (path as moe_layer_forward_path; AUTO takes the
- * GEMM from 4 rows per slot of the layer on). */
+ * GEMM from 4 rows per slot of the layer on).  Rows with id -1 (empty slots)
+ * are skipped and their y_rows left as they were. */
 int moe_experts_rows(moe_ctx *ctx, int layer, const float *x_rows, const int32_t *ids,
                      int n_rows, float *y_rows, int path, void *stream);
 

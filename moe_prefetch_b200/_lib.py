@@ -69,7 +69,7 @@ SIGNATURES = {
     "moe_layer_forward": (I, [P, I, P, P, I, P, P, P]),
     "moe_layer_forward_noalloc": (I, [P, I, P, P, I, P, P, P]),
     "moe_layer_forward_path": (I, [P, I, P, P, I, P, P, I, P]),
-    "moe_ep_route_pack": (I, [P, I, P, I, I, P, P, P, P, P, P, P]),
+    "moe_ep_route_pack": (I, [P, I, P, I, I, I, P, P, P, P, P, P, P]),
     "moe_experts_rows": (I, [P, I, P, P, I, P, I, P]),
     "moe_ep_combine": (I, [P, P, P, P, I, P, P, P]),
     "moe_decode": (I, [P, P, P, I, P, P]),

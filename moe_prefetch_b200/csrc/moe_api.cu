@@ -659,8 +659,8 @@ extern "C" int moe_layer_forward_path(moe_ctx *c, int layer, const float *x, flo
 // ---- expert parallelism -------------------------------------------------------
 
 extern "C" int moe_ep_route_pack(moe_ctx *c, int layer, const float *x, int n_tok, int world,
-                                 int32_t *ids, float *w, int32_t *send_count, int32_t *pos,
-                                 int32_t *send_ids, float *send_x, void *stream) {
+                                 int capacity, int32_t *ids, float *w, int32_t *send_count,
+                                 int32_t *pos, int32_t *send_ids, float *send_x, void *stream) {
     if (!c || !x || !ids || !w || !send_count || !pos || !send_ids || !send_x || n_tok <= 0 ||
         layer < 0 || layer >= c->cfg.n_layers)
         return fail(c, MOE_ERR_ARG, "moe_ep_route_pack: bad argument");
@@ -668,6 +668,9 @@ extern "C" int moe_ep_route_pack(moe_ctx *c, int layer, const float *x, int n_to
     if (world < 1 || world > 256 || g.n_expert % world)
         return fail(c, MOE_ERR_ARG, "moe_ep_route_pack: world %d does not divide %d experts", world,
                     g.n_expert);
+    if (capacity < 0 || (capacity > 0 && capacity < n_tok * g.n_used))
+        return fail(c, MOE_ERR_ARG, "moe_ep_route_pack: capacity %d is below the %d pairs of a rank",
+                    capacity, n_tok * g.n_used);
     CK(cudaSetDevice(g.device));
     const int r = ensure_scratch(c, n_tok);
     if (r != MOE_OK) return r;
@@ -678,8 +681,8 @@ extern "C" int moe_ep_route_pack(moe_ctx *c, int layer, const float *x, int n_to
     GroupBufs gg = c->grp;
     gg.cnt = send_count;
     gg.pair_pos = pos;
-    CK(launch_ep_pack(ids, x, n_tok, g.n_used, g.n_expert, g.n_embd, world, c->s_dest, gg, send_ids,
-                      send_x, c->err, s));
+    CK(launch_ep_pack(ids, x, n_tok, g.n_used, g.n_expert, g.n_embd, world, capacity, c->s_dest, gg,
+                      send_ids, send_x, c->err, s));
     return MOE_OK;
 }
 

@@ -29,7 +29,8 @@ namespace moe {
 
 // One CTA.  Pair p = t * k + r (token t, rank r).  Positions are stable: the
 // pairs of an expert keep pair order.  Writes cnt[E], off[E + 1],
-// pair_pos[P] (-1 for an id out of range, flagged in *err), pos_pair[P], and
+// pair_pos[P] (-1 for an id out of range, flagged in *err, and for the
+// empty-slot id -1, skipped silently), pos_pair[P], and
 // tiles[0 .. n_tiles) = (expert << 16) | token-tile for tiles of `tile` pairs.
 __global__ void __launch_bounds__(GROUP_THREADS) k_group(const int32_t *__restrict__ ids, int P,
                                                          int n_expert, int tile, int32_t *cnt,
@@ -44,7 +45,7 @@ __global__ void __launch_bounds__(GROUP_THREADS) k_group(const int32_t *__restri
     for (int p = tid; p < P; p += GROUP_THREADS) {
         const int e = ids[p];
         if (e >= 0 && e < n_expert) atomicAdd(&s_cnt[e], 1);
-        else atomicOr(err, MOE_DEV_ERR_INDEX);
+        else if (e >= 0 || e < -1) atomicOr(err, MOE_DEV_ERR_INDEX);   // -1: an empty slot, skipped
     }
     __syncthreads();
     if (warp == 0) {

@@ -97,8 +97,10 @@ cudaError_t launch_combine(const float *ypair, const int32_t *pair_pos, const fl
 // Route pairs to ranks: dest [P] scratch; the grouping `g` over `world` rank
 // buckets (g.cnt = send counts, g.pair_pos = send slot of each pair, g.n_tiles
 // = slots filled); send_ids [P], send_x [P][n_embd] in send-slot order.
+// capacity > 0: rank d's pairs go to slots [d * capacity, d * capacity +
+// count), the other slots keep id -1, and g.pair_pos holds each pair's slot.
 cudaError_t launch_ep_pack(const int32_t *ids, const float *x, int n_tok, int k, int n_expert,
-                           int n_embd, int world, int32_t *dest, const GroupBufs &g,
+                           int n_embd, int world, int capacity, int32_t *dest, const GroupBufs &g,
                            int32_t *send_ids, float *send_x, int *err, cudaStream_t s);
 
 // ---- tensor-core grouped GEMM (moe_gemm.cu) --------------------------------

@@ -7,8 +7,9 @@ layer over a rank's home tokens:
 
   1. route + pack (libmoeb200): ids/w of the home tokens and the pairs in
      owner-rank order, each with its token row and expert id;
-  2. all-to-all of the per-rank counts, then of the ids and rows (NCCL over
-     NVLink on GPUs);
+  2. all-to-all of the ids and rows (NCCL over NVLink on GPUs): in fixed
+     per-rank blocks for small batches, or dense after an exchange of the
+     per-rank counts;
   3. the owner runs its experts on the rows it received (grouped GEMV or
      tcgen05 GEMM, unweighted rows);
   4. all-to-all of the rows back, in the order they came;
@@ -37,26 +38,54 @@ def _a2a(out, inp, out_splits, in_splits, group, world):
         dist.all_to_all_single(out, inp, out_splits, in_splits, group=group)
 
 
-def ep_layer_forward(ops, layer, x, group=None, path="auto"):
+CAPACITY_MAX_TOKENS = 64   # home tokens up to which the exchange uses fixed-capacity slots
+
+
+def ep_layer_forward(ops, layer, x, group=None, path="auto", capacity=None):
     """One expert-parallel MoE layer over this rank's home tokens x
     [n_tok, n_embd]; returns (out, ids, w).  Every rank of the group must
-    call it for the same layer (the exchange is collective)."""
+    call it for the same layer (the exchange is collective).
+
+    capacity (slots per destination rank; None: automatic) selects the
+    exchange.  With capacity slots per rank, every rank's pairs for rank d
+    sit in a fixed block and the all-to-alls use equal splits, so nothing
+    waits for the host.  The padding moves world * capacity rows.  Without
+    it (capacity 0) the blocks are dense, and the send counts travel first
+    and are read on the host to size the exchange.  The automatic choice
+    takes capacity = n_tok * n_used for up to CAPACITY_MAX_TOKENS home tokens
+    (batched decode) and the dense exchange above (prefill).  Every rank must
+    pass the same choice.  With capacity slots the "auto" path is the GEMV
+    (few pairs per expert), and no step of the layer waits for the host, so
+    a sequence of layers can be captured in a CUDA graph."""
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     n_tok = x.shape[0]
-    ids, w, send_count, pos, send_ids, send_x = ops.route_pack(layer, x, world)
-    recv_count = torch.empty_like(send_count)
-    _a2a(recv_count, send_count, None, None, group, world)
-    counts = torch.stack([send_count, recv_count]).cpu()
-    send_splits = [int(v) for v in counts[0]]
-    recv_splits = [int(v) for v in counts[1]]
-    n_send, n_recv = sum(send_splits), sum(recv_splits)
-    recv_ids = torch.empty(n_recv, dtype=send_ids.dtype, device=x.device)
-    recv_x = torch.empty(n_recv, x.shape[1], dtype=send_x.dtype, device=x.device)
-    _a2a(recv_ids, send_ids[:n_send], recv_splits, send_splits, group, world)
-    _a2a(recv_x, send_x[:n_send], recv_splits, send_splits, group, world)
-    y_rows = ops.experts_rows(layer, recv_x, recv_ids, path)
-    back = torch.empty(n_send, x.shape[1], dtype=y_rows.dtype, device=x.device)
-    _a2a(back, y_rows, send_splits, recv_splits, group, world)
+    if capacity is None:
+        capacity = n_tok * ops.n_used if n_tok <= CAPACITY_MAX_TOKENS else 0
+    if capacity > 0 and path == "auto":
+        path = "gemv"   # the padded slots are mostly empty: few pairs per expert
+    ids, w, send_count, pos, send_ids, send_x = ops.route_pack(layer, x, world, capacity)
+    if capacity > 0:
+        recv_ids = torch.empty_like(send_ids)
+        recv_x = torch.empty_like(send_x)
+        _a2a(recv_ids, send_ids, None, None, group, world)
+        _a2a(recv_x, send_x, None, None, group, world)
+        y_rows = ops.experts_rows(layer, recv_x, recv_ids, path)
+        back = torch.empty_like(y_rows)
+        _a2a(back, y_rows, None, None, group, world)
+    else:
+        recv_count = torch.empty_like(send_count)
+        _a2a(recv_count, send_count, None, None, group, world)
+        counts = torch.stack([send_count, recv_count]).cpu()
+        send_splits = [int(v) for v in counts[0]]
+        recv_splits = [int(v) for v in counts[1]]
+        n_send, n_recv = sum(send_splits), sum(recv_splits)
+        recv_ids = torch.empty(n_recv, dtype=send_ids.dtype, device=x.device)
+        recv_x = torch.empty(n_recv, x.shape[1], dtype=send_x.dtype, device=x.device)
+        _a2a(recv_ids, send_ids[:n_send], recv_splits, send_splits, group, world)
+        _a2a(recv_x, send_x[:n_send], recv_splits, send_splits, group, world)
+        y_rows = ops.experts_rows(layer, recv_x, recv_ids, path)
+        back = torch.empty(n_send, x.shape[1], dtype=y_rows.dtype, device=x.device)
+        _a2a(back, y_rows, send_splits, recv_splits, group, world)
     # an always-on shared expert is replicated on every rank: rows of the home tokens
     shared = ops.shared_rows(layer, x, path) if getattr(ops, "n_shared", 0) else None
     out = ops.combine(back, pos, w, n_tok, shared)
@@ -69,21 +98,23 @@ class LibEPOps:
     def __init__(self, stack):
         self.st = stack
         self.n_shared = stack.n_shared
+        self.n_used = stack.n_used
 
-    def route_pack(self, layer, x, world):
+    def route_pack(self, layer, x, world, capacity=0):
         st = self.st
         x = x.contiguous()
         n_tok, P = x.shape[0], x.shape[0] * st.n_used
+        slots = world * capacity if capacity > 0 else P
         dev = x.device
         ids = torch.empty(n_tok, st.n_used, dtype=torch.int32, device=dev)
         w = torch.empty(n_tok, st.n_used, dtype=torch.float32, device=dev)
         send_count = torch.empty(world, dtype=torch.int32, device=dev)
         pos = torch.empty(P, dtype=torch.int32, device=dev)
-        send_ids = torch.empty(P, dtype=torch.int32, device=dev)
-        send_x = torch.empty(P, st.n_embd, dtype=torch.float32, device=dev)
-        st._ck(st.lib.moe_ep_route_pack(st.ctx, layer, _ptr(x), n_tok, world, _ptr(ids), _ptr(w),
-                                        _ptr(send_count), _ptr(pos), _ptr(send_ids), _ptr(send_x),
-                                        _stream()), "moe_ep_route_pack")
+        send_ids = torch.empty(slots, dtype=torch.int32, device=dev)
+        send_x = torch.empty(slots, st.n_embd, dtype=torch.float32, device=dev)
+        st._ck(st.lib.moe_ep_route_pack(st.ctx, layer, _ptr(x), n_tok, world, capacity, _ptr(ids),
+                                        _ptr(w), _ptr(send_count), _ptr(pos), _ptr(send_ids),
+                                        _ptr(send_x), _stream()), "moe_ep_route_pack")
         return ids, w, send_count, pos, send_ids, send_x
 
     def experts_rows(self, layer, x_rows, ids, path):

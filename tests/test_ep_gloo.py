@@ -43,7 +43,9 @@ class OracleOps:
         self.per = E // world
         self.e0 = rank * self.per
 
-    def route_pack(self, layer, x, world):
+    n_used = K
+
+    def route_pack(self, layer, x, world, capacity=0):
         import oracle
         xn = x.numpy()
         n_tok = xn.shape[0]
@@ -54,12 +56,22 @@ class OracleOps:
         flat = ids.ravel()
         dest = flat // self.per
         order = np.argsort(dest, kind="stable")          # rank order, pair order within
-        pos = np.empty(flat.size, np.int32)
-        pos[order] = np.arange(flat.size, dtype=np.int32)
         send_count = np.bincount(dest, minlength=world).astype(np.int32)
+        if capacity == 0:
+            slot = np.arange(flat.size)
+            send_ids, send_x = flat[order].copy(), xn[order // K].copy()
+        else:                                            # rank d's block at d * capacity
+            start = np.concatenate([[0], np.cumsum(send_count)[:-1]])
+            q = np.arange(flat.size)
+            slot = dest[order] * capacity + (q - start[dest[order]])
+            send_ids = np.full(world * capacity, -1, np.int32)
+            send_x = np.zeros((world * capacity, xn.shape[1]), np.float32)
+            send_ids[slot] = flat[order]
+            send_x[slot] = xn[order // K]
+        pos = np.empty(flat.size, np.int32)
+        pos[order] = slot
         return (torch.from_numpy(ids), torch.from_numpy(w), torch.from_numpy(send_count),
-                torch.from_numpy(pos), torch.from_numpy(flat[order].copy()),
-                torch.from_numpy(xn[order // K].copy()))
+                torch.from_numpy(pos), torch.from_numpy(send_ids), torch.from_numpy(send_x))
 
     def experts_rows(self, layer, x_rows, ids, path):
         import oracle
@@ -67,9 +79,13 @@ class OracleOps:
         if n == 0:
             return torch.empty(0, H)
         ids = ids.numpy()
-        assert ((ids >= self.e0) & (ids < self.e0 + self.per)).all(), "a row reached a non-owner"
-        y = oracle.moe_experts(x_rows.numpy(), ids[:, None], np.ones((n, 1), np.float32), self.gate,
-                               self.up, self.down, 14, I, n_threads=2)
+        live = ids >= 0                                  # -1: an empty capacity slot
+        assert ((ids[live] >= self.e0) & (ids[live] < self.e0 + self.per)).all(), "a row reached a non-owner"
+        y = np.zeros((n, H), np.float32)
+        if live.any():
+            y[live] = oracle.moe_experts(x_rows.numpy()[live], ids[live][:, None],
+                                         np.ones((int(live.sum()), 1), np.float32), self.gate, self.up,
+                                         self.down, 14, I, n_threads=2)
         return torch.from_numpy(y)
 
     def combine(self, back, pos, w, n_tok, add_rows=None):
@@ -82,7 +98,7 @@ class OracleOps:
         return torch.from_numpy(acc.astype(np.float32))
 
 
-def _worker(rank, world, port, skew, out_dir):
+def _worker(rank, world, port, skew, capacity, out_dir):
     import sys
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     import torch.distributed as dist
@@ -94,7 +110,7 @@ def _worker(rank, world, port, skew, out_dir):
         W, gate, up, down, X = _weights(skew)
         mine = X[rank::world]                                 # this rank's home tokens
         ops = OracleOps(W, gate, up, down, rank, world)
-        out, ids, w = ep_layer_forward(ops, 0, torch.from_numpy(mine))
+        out, ids, w = ep_layer_forward(ops, 0, torch.from_numpy(mine), capacity=capacity)
         np.save(os.path.join(out_dir, f"out{rank}.npy"), out.numpy())
         np.save(os.path.join(out_dir, f"ids{rank}.npy"), ids.numpy())
     finally:
@@ -108,10 +124,14 @@ def _free_port():
 
 
 @pytest.mark.parametrize("skew", [False, True])
-def test_ep_world2_equals_single_process_layer(tmp_path, oracle_lib, skew):
+@pytest.mark.parametrize("capacity", [0, None], ids=["dense", "slots"])
+def test_ep_world2_equals_single_process_layer(tmp_path, oracle_lib, skew, capacity):
+    """capacity 0: dense blocks sized by an exchange of the counts; None: the
+    automatic choice for these 6 home tokens, fixed-capacity slots with
+    equal splits and empty slots (id -1)."""
     import torch.multiprocessing as mp
     world = 2
-    mp.spawn(_worker, args=(world, _free_port(), skew, str(tmp_path)), nprocs=world, join=True)
+    mp.spawn(_worker, args=(world, _free_port(), skew, capacity, str(tmp_path)), nprocs=world, join=True)
     W, gate, up, down, X = _weights(skew)
     rids, rw, ry = oracle_lib.moe_layer(X, W, gate, up, down, 14, I, K)
     for rank in range(world):
