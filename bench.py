@@ -624,6 +624,41 @@ def run_config4(args):
 
 
 # ---------------------------------------------------------------------------
+# one layer through one expert path (the profiling case of the batched kernels)
+# ---------------------------------------------------------------------------
+def run_layer(args):
+    """One resident 128-expert layer (config-0 shapes), --tokens RMS-normed
+    tokens through moe_layer_forward_path(--path), --warmup untimed calls,
+    then --steps timed calls (CUDA events).  One JSON line: us per layer."""
+    import torch
+    from moe_prefetch_b200 import MoeStack
+    torch.cuda.set_device(0)
+    st = MoeStack(n_layers=1)
+    st.synth_resident(seed=5)
+    h = np.random.default_rng(1).standard_normal((args.tokens, N_EMBD))
+    x = torch.from_numpy((h / np.sqrt((h ** 2).mean(-1, keepdims=True))).astype(np.float32)).cuda()
+    for _ in range(args.warmup):
+        st.layer_forward_path(0, x, args.path)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        st.layer_forward_path(0, x, args.path)
+    e1.record()
+    torch.cuda.synchronize()
+    st.sync()
+    us = e0.elapsed_time(e1) * 1000.0 / max(args.steps, 1)
+    print(json.dumps({"metric": "one MoE layer", "value": us, "unit": "us/layer", "n_gpus": 1,
+                      "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
+                      "config": {"workload": f"1 layer, {args.tokens} tokens, path {args.path}",
+                                 "n_expert": N_EXPERT, "n_ff": N_FF, "data": "synthetic"}}),
+          flush=True)
+    st.close()
+    return 0
+
+
+# ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
 def main():
@@ -638,7 +673,8 @@ def main():
     ap.add_argument("--ref-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--workload", default="config1", choices=["config1", "config2", "config3", "config4"])
+    ap.add_argument("--workload", default="config1", choices=["config1", "config2", "config3", "config4", "layer"])
+    ap.add_argument("--path", default="gemv", choices=["auto", "gemv", "gemm"])
     ap.add_argument("--c3-decode-steps", type=int, default=128)
     ap.add_argument("--c3-prefill-chunks", type=int, default=4)
     ap.add_argument("--c2-warm", type=int, default=64)
@@ -652,6 +688,8 @@ def main():
         return run_config3(args)
     if args.workload == "config4":
         return run_config4(args)
+    if args.workload == "layer":
+        return run_layer(args)
 
     import torch
     import torch.distributed as dist
