@@ -286,7 +286,7 @@ extern "C" int moe_create(const moe_cfg *cfg, moe_ctx **out) {
         if (cudaMalloc(&c->resid, sizeof(float) * H) != cudaSuccess ||
             cudaMalloc(&c->logits, sizeof(float) * 256) != cudaSuccess ||
             cudaMalloc(&c->part_p, sizeof(float) * (size_t)G * E) != cudaSuccess ||
-            cudaMalloc(&c->part_s, sizeof(float) * (size_t)G) != cudaSuccess ||
+            cudaMalloc(&c->part_s, sizeof(float) * moe::PART_S_STRIDE * (size_t)G) != cudaSuccess ||
             cudaMalloc(&c->act, sizeof(float) * (size_t)MOE_KMAX * I) != cudaSuccess ||
             cudaMalloc(&c->bar, 64) != cudaSuccess || cudaMalloc(&c->abort_flag, 64) != cudaSuccess ||
             cudaMalloc(&c->err, 64) != cudaSuccess)

@@ -75,6 +75,7 @@ __device__ __forceinline__ bool grid_sync(const DecodeParams &p, unsigned &epoch
                 }
             }
         }
+        if (ok && ld_relaxed_i32(p.abort_flag)) ok = 0;   // a CTA gave up during the layer
         *s_flag = ok;
     }
     __syncthreads();
@@ -147,8 +148,12 @@ __device__ __forceinline__ void observe_decode(const SlotState &st, int layer,
 }
 
 // Cold path: missed experts read zero-copy from the registered host weights
-// into the staging buffers (out of line to keep the hot loop's code compact).
-__device__ __noinline__ void host_miss_copies(const DecodeParams &p, const LayerDesc &ld,
+// into the staging buffers (out of line to keep the hot loop's code compact;
+// every argument by value or as a shared-memory pointer, so that nothing of
+// the kernel's parameters has to live in local memory).
+__device__ __noinline__ void host_miss_copies(const uint8_t *hgate, const uint8_t *hup,
+                                              const uint8_t *hdown, int ns, int64_t gate_bytes,
+                                              int64_t down_bytes, int dn_stride, int *err,
                                               const int32_t *s_ids, const int32_t *s_slot,
                                               int K, int nch, const int *ch_k, const int *ch_i0,
                                               const int *ch_n, const int *ch_off,
@@ -157,27 +162,27 @@ __device__ __noinline__ void host_miss_copies(const DecodeParams &p, const Layer
     const int tid = threadIdx.x;
     for (int q = 0; q < nch; ++q) {
         const int kk = ch_k[q];
-        if (s_slot[kk] == ld.ns) {
-            const size_t off = (size_t)s_ids[kk] * p.gate_bytes + (size_t)ch_i0[q] * gurow;
-            if (ld.hgate && ld.hup) {
-                copy_host16(gate_sm + (size_t)ch_off[q] * gurow, ld.hgate + off, ch_n[q] * gurow);
-                copy_host16(up_sm + (size_t)ch_off[q] * gurow, ld.hup + off, ch_n[q] * gurow);
+        if (s_slot[kk] == ns) {
+            const size_t off = (size_t)s_ids[kk] * gate_bytes + (size_t)ch_i0[q] * gurow;
+            if (hgate && hup) {
+                copy_host16(gate_sm + (size_t)ch_off[q] * gurow, hgate + off, ch_n[q] * gurow);
+                copy_host16(up_sm + (size_t)ch_off[q] * gurow, hup + off, ch_n[q] * gurow);
             } else if (tid == 0) {
-                atomicOr(p.err, MOE_DEV_ERR_INDEX);
+                atomicOr(err, MOE_DEV_ERR_INDEX);
             }
         }
     }
     for (int kk = 0; kk < K; ++kk) {
-        if (h1 > h0 && s_slot[kk] == ld.ns) {
-            if (ld.hdown) {
-                const uint8_t *base = ld.hdown + (size_t)s_ids[kk] * p.down_bytes;
+        if (h1 > h0 && s_slot[kk] == ns) {
+            if (hdown) {
+                const uint8_t *base = hdown + (size_t)s_ids[kk] * down_bytes;
                 const uintptr_t a0 = reinterpret_cast<uintptr_t>(base + (size_t)h0 * drow);
                 const uintptr_t a1 = reinterpret_cast<uintptr_t>(base + (size_t)h1 * drow);
                 const uintptr_t s0 = a0 & ~uintptr_t(15), s1 = (a1 + 15) & ~uintptr_t(15);
-                copy_host16(dn + (size_t)kk * p.dn_stride, reinterpret_cast<const uint8_t *>(s0),
+                copy_host16(dn + (size_t)kk * dn_stride, reinterpret_cast<const uint8_t *>(s0),
                             (int)(s1 - s0));
             } else if (tid == 0) {
-                atomicOr(p.err, MOE_DEV_ERR_INDEX);
+                atomicOr(err, MOE_DEV_ERR_INDEX);
             }
         }
     }
@@ -194,6 +199,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
     int8_t *aq = reinterpret_cast<int8_t *>(sm + p.off_aq);
     float *ad = reinterpret_cast<float *>(sm + p.off_ad);
     float *as_ = reinterpret_cast<float *>(sm + p.off_as);
+    int *ac = reinterpret_cast<int *>(sm + p.off_ac);          // [kx][I/16] -32 * group sums
     float *wt = reinterpret_cast<float *>(sm + p.off_rt);       // [rows][E] router^T rows
     int32_t *tbl = reinterpret_cast<int32_t *>(sm + p.off_tbl); // [E] table row
     float *rown = reinterpret_cast<float *>(sm + p.off_rown);   // [rows] own residual rows
@@ -201,11 +207,6 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
     uint8_t *dn = sm + p.off_dn;
     float *ys = reinterpret_cast<float *>(sm + p.off_ys);
 
-    __shared__ float s_lg[256];
-    __shared__ float s_p[256];
-    __shared__ float s_sel[256];
-    __shared__ uint64_t s_key[256];
-    __shared__ float s_psel[MOE_KMAX];
     __shared__ int32_t s_ids[MOE_KMAX];
     __shared__ float s_w[MOE_KMAX];
     __shared__ int32_t s_slot[MOE_KMAX];
@@ -227,13 +228,14 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
     uint8_t *gate_sm = gu;
     uint8_t *up_sm = gu + (size_t)p.gu_rows_max * gurow;
 
-    // static gate/up pieces of this CTA: [r0, r1) of the flattened (k, row)
-    int ch_k[4], ch_i0[4], ch_n[4], ch_off[4];
+    // static gate/up pieces of this CTA: [r0, r1) of the flattened (k, row);
+    // the table lives in shared memory (it is indexed with run-time indices)
+    __shared__ int ch_k[4], ch_i0[4], ch_n[4], ch_off[4];
     int nch = 0;
     for (int r = r0; r < r1 && nch < 4;) {
         const int kk = r / I, i0 = r % I;
         const int n = min(I - i0, r1 - r);
-        ch_k[nch] = kk; ch_i0[nch] = i0; ch_n[nch] = n; ch_off[nch] = r - r0;
+        if (tid == 0) { ch_k[nch] = kk; ch_i0[nch] = i0; ch_n[nch] = n; ch_off[nch] = r - r0; }
         ++nch;
         r += n;
     }
@@ -274,7 +276,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
     if (tid == DEC_THREADS - 1) {
         float s = 0.0f;
         for (int i = 0; i < rows; ++i) s = __fmaf_rn(rown[i], rown[i], s);
-        __stcg(p.part_s + c, s);
+        __stcg(p.part_s + (size_t)c * PART_S_STRIDE, s);
     }
 
     for (int t = 0; t < p.n_tok; ++t) {
@@ -315,7 +317,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                         const int cc = min(cA + j, G - 1);   // clamped: always in bounds
                         v[j] = has_col ? __ldcg(reinterpret_cast<const float4 *>(p.part_p + (size_t)cc * E) + col)
                                        : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                        sv[j] = with_s ? __ldcg(p.part_s + cc) : 0.0f;
+                        sv[j] = with_s ? __ldcg(p.part_s + (size_t)cc * PART_S_STRIDE) : 0.0f;
                     }
                     if (cbase == 0 && has_x) *reinterpret_cast<float4 *>(xf + tid * 4) = xv;
                     float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
@@ -335,67 +337,51 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                 }
                 __syncthreads();
                 PROF(2)
-                // group sums in group order; S redundantly in every thread
+                // S in group order, redundantly in every thread
                 float S = s_red16[0];
                 for (int gg = 1; gg < 16; ++gg) S = __fadd_rn(S, s_red16[gg]);
                 const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(S, (float)H), p.rms_eps)));
-                for (int e = tid; e < E; e += DEC_THREADS) {
-                    float tot = red[e];
-                    for (int gg = 1; gg < 16; ++gg) tot = __fadd_rn(tot, red[gg * E + e]);
-                    s_lg[e] = __fmul_rn(tot, inv);
+                if (pend_tbl) {
+                    if (!mbar_wait(&mb[MB_TBL], tbl_par)) {
+                        if (tid == 0) { atomicOr(p.err, MOE_DEV_ERR_TIMEOUT); s_bad = 1; }
+                    }
+                    pend_tbl = false;
+                    tbl_par ^= 1;
                 }
-                for (int i = tid; i < H; i += DEC_THREADS) xf[i] = __fmul_rn(xf[i], inv);
+                // ---- 2. warp 0: logits, softmax, prior, top-k, weights and slots in
+                //         registers; warps 1..15: x = r * inv -> Q8_1 -----------------
+                if (warp == 0) {
+                    int id_r;
+                    float w_r;
+                    select_warp<E / 32>(red, inv, tbl, ld.ns, p.delta, p.delta > 0.0f, K, lane, id_r, w_r);
+                    if (lane < K) {
+                        const bool okid = id_r >= 0 && id_r < E;
+                        s_ids[lane] = id_r;
+                        s_w[lane] = w_r;
+                        s_slot[lane] = okid ? tbl[id_r] : ld.ns;
+                        if (!okid) { atomicOr(p.err, MOE_DEV_ERR_INDEX); s_bad = 1; }
+                    }
+                    if (KX > K && lane == K) {   // the shared expert: always on, weight 1, own buffer
+                        s_ids[K] = E;
+                        s_w[K] = 1.0f;
+                        s_slot[K] = -1;
+                    }
+                    const bool missed = lane < K && (id_r < 0 || id_r >= E || tbl[id_r] == ld.ns);
+                    const unsigned miss = __ballot_sync(MOE_FULL, missed);
+                    if (lane == 0) s_any_miss = miss != 0;
+                } else {
+                    q8_scale_quantize_cta(xf, inv, H / 32, xq, xd, xs, tid - 32, DEC_THREADS - 32);
+                }
                 __syncthreads();
-                PROF(3)
+                PROF(6)
+                if (s_bad) {
+                    if (tid == 0) atomicExch(p.abort_flag, 1);
+                    goto abort;
+                }
                 if (p.dbg_x && c == 0)
                     for (int i = tid; i < H; i += DEC_THREADS)
                         p.dbg_x[((size_t)t * NL + L) * H + i] = xf[i];
             }
-
-            // ---- 2. select (warp 0 softmax; x -> Q8_1 on warps 1..) -------------
-            if (pend_tbl) {
-                if (!mbar_wait(&mb[MB_TBL], tbl_par)) {
-                    if (tid == 0) { atomicOr(p.err, MOE_DEV_ERR_TIMEOUT); atomicExch(p.abort_flag, 1); s_bad = 1; }
-                }
-                pend_tbl = false;
-                tbl_par ^= 1;
-            }
-            if (warp == 0)
-                router_softmax_warp(s_lg, E, tbl, ld.ns, p.delta, p.delta > 0.0f, s_p, s_sel, lane,
-                                    s_key);
-            else
-                q8_quantize_cta(xf, false, H / 32, xq, xd, xs, tid - 32, DEC_THREADS - 32);
-            __syncthreads();
-            PROF(4)
-            if (s_bad) goto abort;
-            topk_key_block(s_key, s_p, E, K, s_ids, s_psel, tid, DEC_THREADS);
-            __syncthreads();
-            PROF(5)
-            if (warp == 0) {
-                // weights lane-parallel: each lane forms the sum in rank order
-                if (lane < K) {
-                    float ws = s_psel[0];
-                    for (int r = 1; r < K; ++r) ws = __fadd_rn(ws, s_psel[r]);
-                    s_w[lane] = __fdiv_rn(s_psel[lane], ws);
-                    const int id = s_ids[lane];
-                    const int slot = (id >= 0 && id < E) ? tbl[id] : ld.ns;
-                    s_slot[lane] = slot;
-                    if (id < 0 || id >= E) { atomicOr(p.err, MOE_DEV_ERR_INDEX); s_bad = 1; }
-                }
-                if (KX > K && lane == K) {   // the shared expert: always on, weight 1, own buffer
-                    s_ids[K] = E;
-                    s_w[K] = 1.0f;
-                    s_slot[K] = -1;
-                }
-                const unsigned miss = __ballot_sync(MOE_FULL, lane < K && s_slot[lane] == ld.ns);
-                if (lane == 0) s_any_miss = miss != 0;
-            }
-            __syncthreads();
-            if (s_bad) {
-                if (tid == 0) atomicExch(p.abort_flag, 1);
-                goto abort;
-            }
-            PROF(6)
             if (c == 0 && warp == 1) {
                 if (p.observe) observe_decode(p.st, L, s_ids, s_slot, K, ld.ns, &s_clock, lane);
                 if (p.dbg_ids && lane < K) {
@@ -460,7 +446,8 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                 pend_gu = pend_dn = true;
                 // missed experts: zero-copy reads of the registered host weights
                 if (s_any_miss) {
-                    host_miss_copies(p, ld, s_ids, s_slot, K, nch, ch_k, ch_i0, ch_n, ch_off, gate_sm,
+                    host_miss_copies(ld.hgate, ld.hup, ld.hdown, ld.ns, p.gate_bytes, p.down_bytes,
+                                     p.dn_stride, p.err, s_ids, s_slot, K, nch, ch_k, ch_i0, ch_n, ch_off, gate_sm,
                                      up_sm, dn, gurow, drow, h0, h1);
                     __syncthreads();
                 }
@@ -523,50 +510,54 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
             pend_gu = false;
 
             // ---- 5. activations -> Q8_1 ---------------------------------------------
-            q8_quantize_cta(p.act, true, KX * I / 32, aq, ad, as_, tid, DEC_THREADS);
+            q8_quantize_cta16(p.act, KX * I / 32, aq, ad, as_, ac, tid, DEC_THREADS);
             __syncthreads();
             PROF(10)
 
-            // ---- 6. down GEMV: one lane per half super-block, 8-lane row groups ------
+            // ---- 6. down GEMV: items (expert, group of 4 rows) over all warps; one
+            //         lane per half super-block, 8-lane row groups ---------------------
             if (rows > 0) {
-                const int wpk = DEC_WARPS / KX;   // warps per expert (>= 1)
-                if (warp < KX * wpk) {
-                    const int kk = warp / wpk, sub = warp % wpk;
-                    const int grp = lane >> 3, u = lane & 7;   // row group, unit in group
+                const int grp = lane >> 3, u = lane & 7;   // row in the group, unit
+                const int nrg = Q6_T ? (rows + 3) >> 2 : rows;
+                for (int it = warp; it < KX * nrg; it += DEC_WARPS) {
+                    const int kk = it / nrg, rg = it - kk * nrg;
                     const int sl = s_slot[kk];
                     const uint8_t *base = sl < 0 ? ld.sdown
                         : sl != ld.ns ? ld.down + (size_t)sl * p.down_bytes
                                       : ld.hdown + (size_t)s_ids[kk] * p.down_bytes;
                     const uintptr_t a0 = reinterpret_cast<uintptr_t>(base + (size_t)h0 * drow);
                     const uint8_t *rws = dn + (size_t)kk * p.dn_stride + (int)(a0 & 15);
-                    if (!mbar_wait(&mb[MB_DN + kk], par)) {
+                    if (!__all_sync(MOE_FULL, mbar_wait(&mb[MB_DN + kk], par))) {
                         if (lane == 0) { atomicOr(p.err, MOE_DEV_ERR_TIMEOUT); atomicExch(p.abort_flag, 1); }
-                    } else if constexpr (Q6_T) {
+                        break;
+                    }
+                    if constexpr (Q6_T) {
                         const int nunits = (I / MOE_QK) * 2;           // half blocks per row
                         const bool on = u < nunits;
                         const int sb = u >> 1, hh = u & 1;
-                        ActHalf a;
-                        if (on) load_act_half(a, aq + (size_t)kk * I, ad + (size_t)kk * (I / 32), sb, hh);
-                        for (int i0 = sub * 4; i0 < rows; i0 += 4 * wpk) {
-                            const int i = i0 + grp;
-                            float v = 0.0f;
-                            if (on && i < rows) v = q6k_half_dot(rws + (size_t)i * drow + sb * MOE_Q6K_BYTES, hh, a);
-                            v = group8_sum(v);
-                            if (u == 0 && i < rows) ys[kk * p.dn_rows_max + i] = v;
+                        const int i = rg * 4 + grp;
+                        ActHalfU a;
+                        float v = 0.0f;
+                        if (on) {
+                            load_act_half_u(a, aq + (size_t)kk * I, ad + (size_t)kk * (I / 32),
+                                            ac + (size_t)kk * (I / 16), sb, hh);
+                            if (i < rows)
+                                v = q6k_half_dot_u(rws + (size_t)i * drow + sb * MOE_Q6K_BYTES, hh, a);
                         }
+                        v = group8_sum(v);
+                        if (u == 0 && i < rows) ys[kk * p.dn_rows_max + i] = v;
                     } else {
                         const int units = (I / MOE_QK) * 4;
-                        ActQ4 a;
                         const bool on = lane < units;
-                        if (on)
+                        float v = 0.0f;
+                        if (on) {
+                            ActQ4 a;
                             load_act_q4(a, aq + (size_t)kk * I, ad + (size_t)kk * (I / 32),
                                         as_ + (size_t)kk * (I / 32), lane >> 2, lane & 3);
-                        for (int i = sub; i < rows; i += wpk) {
-                            float v = 0.0f;
-                            if (on) v = q4k_unit_dot(rws + (size_t)i * drow + (lane >> 2) * MOE_Q4K_BYTES, lane & 3, a);
-                            v = warp_sum(v);
-                            if (lane == 0) ys[kk * p.dn_rows_max + i] = v;
+                            v = q4k_unit_dot(rws + (size_t)rg * drow + (lane >> 2) * MOE_Q4K_BYTES, lane & 3, a);
                         }
+                        v = warp_sum(v);
+                        if (lane == 0) ys[kk * p.dn_rows_max + rg] = v;
                     }
                 }
             }
@@ -603,11 +594,10 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                 if (tid == DEC_THREADS - 1) {
                     float s = 0.0f;
                     for (int i = 0; i < rows; ++i) s = __fmaf_rn(rown[i], rown[i], s);
-                    __stcg(p.part_s + c, s);
+                    __stcg(p.part_s + (size_t)c * PART_S_STRIDE, s);
                 }
             }
 #undef PROF
-            if (ld_relaxed_i32(p.abort_flag)) goto abort;
         }
     }
     if (c == 0 && tid == 0) p.st.g[G_CLOCK] = s_clock;
@@ -645,6 +635,7 @@ int decode_smem_layout(DecodeParams &p, int grid) {
     p.off_aq = off; off = align16(off + K * I);
     p.off_ad = off; off = align16(off + K * (I / 32) * 4);
     p.off_as = off; off = align16(off + K * (I / 32) * 4);
+    p.off_ac = off; off = align16(off + K * (I / 16) * 4);
     p.off_rt = off; off = align16(off + p.dn_rows_max * E * 4);
     p.off_tbl = off; off = align16(off + E * 4);
     p.off_rown = off; off = align16(off + p.dn_rows_max * 4);

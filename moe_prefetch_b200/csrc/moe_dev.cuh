@@ -222,6 +222,85 @@ __device__ __forceinline__ void router_softmax_warp(const float *logits, int n_e
     }
 }
 
+// The whole selection of one token in one warp, in registers: the logits
+// from the 16 group rows of `red` (summed in group order, times inv), the
+// softmax and cache prior of router_softmax_warp, top-k as k rounds of
+// arg-max over the keys (selection bits << 32 | ~id: the total order of
+// topk_key_block), and the weights p / sum(p) with the sum formed in rank
+// order.  The same operations in the same order as those three steps, so
+// the same bits.  Lane r < k returns rank r's id and weight.  M experts per
+// lane (n_expert = 32 * M).
+template <int M>
+__device__ __forceinline__ void select_warp(const float *red, float inv, const int32_t *table,
+                                            int ns, float delta, bool use_prior, int k, int lane,
+                                            int &id_r, float &w_r) {
+    constexpr int E = 32 * M;
+    float lg[M], ex[M], pr[M];
+    uint32_t kh[M], kl[M];
+#pragma unroll
+    for (int i = 0; i < M; ++i) {
+        const int e = lane + 32 * i;
+        float tot = red[e];
+#pragma unroll
+        for (int g = 1; g < 16; ++g) tot = __fadd_rn(tot, red[g * E + e]);
+        lg[i] = __fmul_rn(tot, inv);
+    }
+    float mx = lg[0];
+#pragma unroll
+    for (int i = 1; i < M; ++i) mx = fmaxf(mx, lg[i]);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(MOE_FULL, mx, off));
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < M; ++i) {
+        ex[i] = expf_exact(__fsub_rn(lg[i], mx));
+        s = i == 0 ? ex[0] : __fadd_rn(s, ex[i]);
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) s = __fadd_rn(s, __shfl_xor_sync(MOE_FULL, s, off));
+#pragma unroll
+    for (int i = 0; i < M; ++i) {
+        const int e = lane + 32 * i;
+        pr[i] = __fdiv_rn(ex[i], s);
+        const bool res = use_prior && table != nullptr && table[e] != ns;
+        const float sv = res ? __fadd_rn(pr[i], delta) : pr[i];
+        kh[i] = __float_as_uint(sv);
+        kl[i] = ~(uint32_t)e;
+    }
+    uint32_t taken = 0;
+    float ws = 0.0f, my_p = 0.0f;
+    int my_id = -1;
+    for (int r = 0; r < k; ++r) {
+        // this lane's best untaken key; (0, 0) is below every real key (~id > 0)
+        uint32_t bh = 0, bl = 0;
+#pragma unroll
+        for (int i = 0; i < M; ++i) {
+            const bool better = kh[i] > bh || (kh[i] == bh && kl[i] > bl);
+            if (!((taken >> i) & 1u) && better) {
+                bh = kh[i];
+                bl = kl[i];
+            }
+        }
+        const uint32_t mh = __reduce_max_sync(MOE_FULL, bh);
+        const uint32_t ml = __reduce_max_sync(MOE_FULL, bh == mh ? bl : 0u);
+        const int e = (int)(~ml);
+        const int owner = e & 31, idx = e >> 5;
+        float pv = 0.0f;
+#pragma unroll
+        for (int i = 0; i < M; ++i)
+            if (i == idx) pv = pr[i];
+        if (lane == owner) taken |= 1u << idx;
+        const float pw = __shfl_sync(MOE_FULL, pv, owner);
+        ws = r == 0 ? pw : __fadd_rn(ws, pw);
+        if (lane == r) {
+            my_id = e;
+            my_p = pw;
+        }
+    }
+    id_r = my_id;
+    w_r = lane < k ? __fdiv_rn(my_p, ws) : 0.0f;
+}
+
 // Top-k by rank, all threads of the CTA: rank(e) = #experts before e in the
 // order (selection value descending, id ascending); the k experts with rank < k
 // land at position rank.  The same total order as k rounds of arg-max with
@@ -299,6 +378,116 @@ __device__ __forceinline__ void q8_quantize_cta(const float *src, bool from_glob
             const uint32_t hi = (uint32_t)(qi[4] & 0xFF) | ((uint32_t)(qi[5] & 0xFF) << 8) |
                                 ((uint32_t)(qi[6] & 0xFF) << 16) | ((uint32_t)(qi[7] & 0xFF) << 24);
             *reinterpret_cast<uint2 *>(q + 32 * blk + 8 * part) = make_uint2(lo, hi);
+            if (part == 0) {
+                d[blk] = db;
+                s[blk] = __fmul_rn(db, (float)sum);
+            }
+        }
+    }
+}
+
+// q8_quantize_cta of x = xf * inv for x in shared memory, each thread scaling
+// the 8 values it quantises (__fmul_rn, written back to xf) -- the same bits
+// as scaling the whole vector first.
+__device__ __forceinline__ void q8_scale_quantize_cta(float *xf, float inv, int n_blocks, int8_t *q,
+                                                      float *d, float *s, int tid, int nthreads) {
+    const int lane = tid & 31;
+    for (int base = tid - lane; base < n_blocks * 4; base += nthreads) {
+        const int b4 = base + lane;
+        const int blk = b4 >> 2, part = b4 & 3;
+        const bool valid = b4 < n_blocks * 4;
+        float v[8];
+        if (valid) {
+            float4 *p = reinterpret_cast<float4 *>(xf + 32 * blk + 8 * part);
+            float4 a = p[0], c = p[1];
+            a.x = __fmul_rn(a.x, inv); a.y = __fmul_rn(a.y, inv);
+            a.z = __fmul_rn(a.z, inv); a.w = __fmul_rn(a.w, inv);
+            c.x = __fmul_rn(c.x, inv); c.y = __fmul_rn(c.y, inv);
+            c.z = __fmul_rn(c.z, inv); c.w = __fmul_rn(c.w, inv);
+            p[0] = a;
+            p[1] = c;
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+            v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+        }
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+        amax = fmaxf(amax, __shfl_xor_sync(MOE_FULL, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(MOE_FULL, amax, 2));
+        const float db = __fdiv_rn(amax, 127.0f);
+        const float id = amax > 0.0f ? __fdiv_rn(1.0f, db) : 0.0f;
+        int qi[8];
+        int sum = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            qi[i] = (int)roundf(__fmul_rn(v[i], id));
+            sum += qi[i];
+        }
+        sum += __shfl_xor_sync(MOE_FULL, sum, 1);
+        sum += __shfl_xor_sync(MOE_FULL, sum, 2);
+        if (valid) {
+            const uint32_t lo = (uint32_t)(qi[0] & 0xFF) | ((uint32_t)(qi[1] & 0xFF) << 8) |
+                                ((uint32_t)(qi[2] & 0xFF) << 16) | ((uint32_t)(qi[3] & 0xFF) << 24);
+            const uint32_t hi = (uint32_t)(qi[4] & 0xFF) | ((uint32_t)(qi[5] & 0xFF) << 8) |
+                                ((uint32_t)(qi[6] & 0xFF) << 16) | ((uint32_t)(qi[7] & 0xFF) << 24);
+            *reinterpret_cast<uint2 *>(q + 32 * blk + 8 * part) = make_uint2(lo, hi);
+            if (part == 0) {
+                d[blk] = db;
+                s[blk] = __fmul_rn(db, (float)sum);
+            }
+        }
+    }
+}
+
+// All threads quantise n_blocks blocks read from global memory that other
+// CTAs wrote (ld.global.cg), two threads per block (16 values each), every
+// load issued before the arithmetic: the same d, q and s as q8_quantize_cta.
+// Also c16[2 * blk + half] = -32 * (sum of the 16 q of that half): the start
+// value that turns a dot of unsigned 6-bit values with q into a dot of
+// (value - 32) with q (dp4a_us).
+__device__ __forceinline__ void q8_quantize_cta16(const float *src, int n_blocks, int8_t *q,
+                                                  float *d, float *s, int *c16, int tid,
+                                                  int nthreads) {
+    const int lane = tid & 31;
+    for (int base = tid - lane; base < n_blocks * 2; base += nthreads) {
+        const int t2 = base + lane;
+        const int blk = t2 >> 1, part = t2 & 1;
+        const bool valid = t2 < n_blocks * 2;
+        float4 v4[4];
+        if (valid) {
+            const float4 *p = reinterpret_cast<const float4 *>(src + 32 * blk + 16 * part);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) v4[j] = __ldcg(p + j);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) v4[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            v[4 * j] = v4[j].x; v[4 * j + 1] = v4[j].y; v[4 * j + 2] = v4[j].z; v[4 * j + 3] = v4[j].w;
+        }
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+        amax = fmaxf(amax, __shfl_xor_sync(MOE_FULL, amax, 1));
+        const float db = __fdiv_rn(amax, 127.0f);
+        const float id = amax > 0.0f ? __fdiv_rn(1.0f, db) : 0.0f;
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+        int sum16 = 0;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int qi = (int)roundf(__fmul_rn(v[i], id));
+            sum16 += qi;
+            w[i >> 2] |= (uint32_t)(qi & 0xFF) << (8 * (i & 3));
+        }
+        const int sum = sum16 + __shfl_xor_sync(MOE_FULL, sum16, 1);
+        if (valid) {
+            *reinterpret_cast<uint4 *>(q + 32 * blk + 16 * part) = make_uint4(w[0], w[1], w[2], w[3]);
+            c16[2 * blk + part] = -32 * sum16;
             if (part == 0) {
                 d[blk] = db;
                 s[blk] = __fmul_rn(db, (float)sum);
@@ -665,6 +854,72 @@ __device__ __forceinline__ float q6k_half_dot(const uint8_t *blk, int h, const A
     Q6Half w;
     q6k_half_load(blk, h, w);
     return q6k_half_compute(w, a);
+}
+
+// 4-way byte dot: unsigned bytes of a times signed bytes of b, plus c.
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+    int r;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+
+// ActHalf plus, per scale group g (16 values), c[g] = -32 * (sum of its q):
+// the start value of the group's integer sum in q6k_half_compute_u.
+struct ActHalfU {
+    int q[4][8];
+    float d[4];
+    int c[8];
+};
+
+__device__ __forceinline__ void load_act_half_u(ActHalfU &a, const int8_t *q, const float *d,
+                                                const int *c16, int sb, int h) {
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        const int e = 256 * sb + 128 * h + 32 * m;
+        const int4 *qp = reinterpret_cast<const int4 *>(q + e);
+        const int4 v0 = qp[0], v1 = qp[1];
+        a.q[m][0] = v0.x; a.q[m][1] = v0.y; a.q[m][2] = v0.z; a.q[m][3] = v0.w;
+        a.q[m][4] = v1.x; a.q[m][5] = v1.y; a.q[m][6] = v1.z; a.q[m][7] = v1.w;
+        a.d[m] = d[e >> 5];
+        const int2 cc = *reinterpret_cast<const int2 *>(c16 + (e >> 4));
+        a.c[2 * m] = cc.x;
+        a.c[2 * m + 1] = cc.y;
+    }
+}
+
+// q6k_half_compute with the 6-bit values left unsigned: each group's integer
+// sum starts at -32 * sum(q) and adds q_unsigned * q, which is the same
+// integer as sum((q_unsigned - 32) * q); the float steps are unchanged, so
+// the result is the same bits.
+__device__ __forceinline__ float q6k_half_compute_u(const Q6Half &w, const ActHalfU &a) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        int is0 = a.c[2 * m], is1 = a.c[2 * m + 1];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t src = (m & 1) ? w.hi[i] : w.lo[i];
+            const uint32_t nib = (m >> 1) ? (src >> 4) : src;
+            const uint32_t hb = m == 0 ? (w.qh[i] << 4)
+                              : m == 1 ? (w.qh[i] << 2)
+                              : m == 2 ? w.qh[i] : (w.qh[i] >> 2);
+            const uint32_t v = (nib & 0x0F0F0F0Fu) | (hb & 0x30303030u);
+            if (i < 4) is0 = dp4a_us(v, a.q[m][i], is0);
+            else is1 = dp4a_us(v, a.q[m][i], is1);
+        }
+        const int g0 = 2 * m, g1 = 2 * m + 1;
+        const int s0 = (int)(int8_t)((w.sc[g0 >> 2] >> (8 * (g0 & 3))) & 0xFF);
+        const int s1 = (int)(int8_t)((w.sc[g1 >> 2] >> (8 * (g1 & 3))) & 0xFF);
+        acc += (float)(s0 * is0) * a.d[m];
+        acc += (float)(s1 * is1) * a.d[m];
+    }
+    return w.d * acc;
+}
+
+__device__ __forceinline__ float q6k_half_dot_u(const uint8_t *blk, int h, const ActHalfU &a) {
+    Q6Half w;
+    q6k_half_load(blk, h, w);
+    return q6k_half_compute_u(w, a);
 }
 
 // Sum over the 8 lanes of an aligned 8-lane group, butterfly 1, 2, 4 (fixed

@@ -129,6 +129,11 @@ struct LayerDesc {
     int32_t pad_;
 };
 
+// One 128-byte line per CTA for its partial sum of squares: every warp of
+// every CTA reads these after the grid barrier, and packing 32 CTAs' values
+// into one line turns those reads into a hot spot at one L2 slice.
+constexpr int PART_S_STRIDE = 32;
+
 struct DecodeParams {
     int n_layers, n_expert, k, n_embd, n_ff, down_type;
     int kx;                                // experts per token: k, plus 1 with a shared expert
@@ -143,7 +148,7 @@ struct DecodeParams {
     float *resid;                          // [H]  residual stream
     float *logits;                         // [E] (unused by the 2-barrier kernel)
     float *part_p;                         // [grid][E] partial logits
-    float *part_s;                         // [grid] partial sums of squares
+    float *part_s;                         // [grid][PART_S_STRIDE] partial sums of squares (first float)
     float *act;                            // [k][I]
     unsigned *bar;                         // grid barrier counter (zeroed per launch)
     int *abort_flag;
@@ -158,7 +163,7 @@ struct DecodeParams {
     float *dbg_y;                          // [n_tok][L][H]
     uint64_t *prof;                        // [n_tok][L][DEC_PHASES][grid] or null
     // shared-memory layout (bytes from the start of dynamic smem)
-    int off_xf, off_xq, off_xd, off_xs, off_aq, off_ad, off_as, off_rt, off_tbl, off_rown,
+    int off_xf, off_xq, off_xd, off_xs, off_aq, off_ad, off_as, off_ac, off_rt, off_tbl, off_rown,
         off_gu, off_dn, off_ys, smem_bytes;
     int dn_stride;                         // bytes per expert chunk in the down staging
     int rt_rows;                           // router rows per CTA (ceil(E / grid))
