@@ -51,7 +51,7 @@ struct moe_ctx {
     int grid = 0;
     DecodeParams dp{};
     float *resid = nullptr, *logits = nullptr, *act = nullptr;
-    float *part_p = nullptr, *part_s = nullptr;
+    long long *acc = nullptr;   // decode router accumulators
     unsigned *bar = nullptr;
     int *abort_flag = nullptr, *err = nullptr;
     // scratch for moe_layer_forward / moe_decode_host
@@ -285,15 +285,14 @@ extern "C" int moe_create(const moe_cfg *cfg, moe_ctx **out) {
         p.layers = c->d_layers;
         if (cudaMalloc(&c->resid, sizeof(float) * H) != cudaSuccess ||
             cudaMalloc(&c->logits, sizeof(float) * 256) != cudaSuccess ||
-            cudaMalloc(&c->part_p, sizeof(float) * (size_t)G * E) != cudaSuccess ||
-            cudaMalloc(&c->part_s, sizeof(float) * moe::PART_S_STRIDE * (size_t)G) != cudaSuccess ||
+            cudaMalloc(&c->acc, sizeof(long long) * 2 * (size_t)(E + 1) * moe::ACC_LINE) != cudaSuccess ||
             cudaMalloc(&c->act, sizeof(float) * (size_t)MOE_KMAX * I) != cudaSuccess ||
             cudaMalloc(&c->bar, 64) != cudaSuccess || cudaMalloc(&c->abort_flag, 64) != cudaSuccess ||
             cudaMalloc(&c->err, 64) != cudaSuccess)
             return cleanup_fail(MOE_ERR_OOM);
         cudaMemset(c->err, 0, 64);
         p.resid = c->resid; p.logits = c->logits; p.act = c->act; p.bar = c->bar;
-        p.part_p = c->part_p; p.part_s = c->part_s;
+        p.acc = c->acc;
         p.abort_flag = c->abort_flag; p.err = c->err; p.st = c->st;
         p.observe = 1; p.delta = g.cache_prior; p.rms_eps = 1e-6f;
     }
@@ -328,8 +327,7 @@ extern "C" void moe_destroy(moe_ctx *c) {
     }
     cudaFree(c->router);
     cudaFree(c->router_t);
-    cudaFree(c->part_p);
-    cudaFree(c->part_s);
+    cudaFree(c->acc);
     cudaFree(c->state_mem);
     cudaFree(c->d_layers);
     cudaFree(c->d_part);
@@ -832,6 +830,7 @@ extern "C" int moe_decode(moe_ctx *c, const float *h, float *out, int n_tok,
     if (p.dbg_ids && !p.dbg_w) return fail(c, MOE_ERR_ARG, "moe_decode: dbg ids without w");
     CK(cudaMemsetAsync(c->bar, 0, 64, s));
     CK(cudaMemsetAsync(c->abort_flag, 0, 64, s));
+    CK(cudaMemsetAsync(c->acc, 0, sizeof(long long) * 2 * (size_t)(c->cfg.n_expert + 1) * moe::ACC_LINE, s));
     CK(launch_decode(p, c->grid, s));
     return MOE_OK;
 }

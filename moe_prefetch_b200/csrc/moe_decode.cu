@@ -188,6 +188,24 @@ __device__ __noinline__ void host_miss_copies(const uint8_t *hgate, const uint8_
     }
 }
 
+// This CTA's share of the next step's fused router: partial logits over its
+// residual rows (an FMA chain per expert, rows in order) and the partial sum of
+// squares, added in fixed point to the step's accumulators A[e * ACC_LINE]
+// (e < E) and A[E * ACC_LINE].
+__device__ __forceinline__ void add_router_partials(long long *A, const float *wt, const float *rown,
+                                                    int rows, int E) {
+    for (int e = threadIdx.x; e < E; e += DEC_THREADS) {
+        float acc = 0.0f;
+        for (int i = 0; i < rows; ++i) acc = __fmaf_rn(wt[i * E + e], rown[i], acc);
+        red_add_u64(reinterpret_cast<uint64_t *>(A + (size_t)e * ACC_LINE), (uint64_t)fx_logit(acc));
+    }
+    if (threadIdx.x == DEC_THREADS - 1) {
+        float s = 0.0f;
+        for (int i = 0; i < rows; ++i) s = __fmaf_rn(rown[i], rown[i], s);
+        red_add_u64(reinterpret_cast<uint64_t *>(A + (size_t)E * ACC_LINE), (uint64_t)fx_sumsq(s));
+    }
+}
+
 template <int E_T, bool Q6_T>
 __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
     extern __shared__ __align__(128) uint8_t sm[];
@@ -210,7 +228,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
     __shared__ int32_t s_ids[MOE_KMAX];
     __shared__ float s_w[MOE_KMAX];
     __shared__ int32_t s_slot[MOE_KMAX];
-    __shared__ float s_red16[16];
+    __shared__ float s_sumsq;
     __shared__ int s_flag;
     __shared__ int s_bad;
     __shared__ int s_any_miss;
@@ -268,16 +286,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
     pend_wt = false;
     wt_par = 1;
     __syncthreads();
-    for (int e = tid; e < E; e += DEC_THREADS) {
-        float acc = 0.0f;
-        for (int i = 0; i < rows; ++i) acc = __fmaf_rn(wt[i * E + e], rown[i], acc);
-        __stcg(p.part_p + (size_t)c * E + e, acc);
-    }
-    if (tid == DEC_THREADS - 1) {
-        float s = 0.0f;
-        for (int i = 0; i < rows; ++i) s = __fmaf_rn(rown[i], rown[i], s);
-        __stcg(p.part_s + (size_t)c * PART_S_STRIDE, s);
-    }
+    add_router_partials(p.acc, wt, rown, rows, E);   // step 0: buffer 0
 
     for (int t = 0; t < p.n_tok; ++t) {
         for (int L = 0; L < NL; ++L, ++use) {
@@ -292,54 +301,31 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
             if (!grid_sync(p, epoch, &s_flag)) goto abort;
             PROF(1)
 
-            // ---- 1. residual, reduced logits, x = r * inv_rms, x -> Q8_1 ---------
-            // Every global load of the phase is issued before the first use: the
-            // residual (one float4 per thread), this warp's row group of partial
-            // logits (16 groups x float4 expert columns) and its partial sums of
-            // squares.
+            // ---- 1. residual, the step's router totals, x = r * inv_rms ------------
+            // Every CTA reads the full residual (one float4 per thread) and the
+            // E + 1 fixed-point totals (one line each), and zeroes its share of
+            // the other buffer: read during the previous step, next added to
+            // after barrier B of this one.
             {
-                float *red = reinterpret_cast<float *>(gu);   // [16][E] scratch
-                const int g = warp, cA = g * G / 16, cB = (g + 1) * G / 16;
+                float *tot = reinterpret_cast<float *>(gu);   // [E] logit totals (before * inv)
+                const long long *A = p.acc + (size_t)(use & 1) * (E + 1) * ACC_LINE;
                 const float *src = L == 0 ? p.h_in + (size_t)t * H : p.resid;
                 float4 xv = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
                 const bool has_x = tid * 4 < H;
                 if (has_x)
                     xv = L == 0 ? __ldg(reinterpret_cast<const float4 *>(src + tid * 4))
                                 : __ldcg(reinterpret_cast<const float4 *>(src + tid * 4));
-                for (int cbase = 0; cbase < E / 4; cbase += 32) {   // 1 pass (E=128), 2 (E=256)
-                    const int col = cbase + lane;
-                    const bool has_col = col < E / 4;
-                    const bool with_s = cbase == 0 && lane == 0;
-                    float4 v[10];
-                    float sv[10];
-#pragma unroll
-                    for (int j = 0; j < 10; ++j) {
-                        const int cc = min(cA + j, G - 1);   // clamped: always in bounds
-                        v[j] = has_col ? __ldcg(reinterpret_cast<const float4 *>(p.part_p + (size_t)cc * E) + col)
-                                       : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                        sv[j] = with_s ? __ldcg(p.part_s + (size_t)cc * PART_S_STRIDE) : 0.0f;
-                    }
-                    if (cbase == 0 && has_x) *reinterpret_cast<float4 *>(xf + tid * 4) = xv;
-                    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                    float accs = 0.0f;
-#pragma unroll
-                    for (int j = 0; j < 10; ++j) {
-                        if (cA + j < cB) {
-                            acc.x = __fadd_rn(acc.x, v[j].x);
-                            acc.y = __fadd_rn(acc.y, v[j].y);
-                            acc.z = __fadd_rn(acc.z, v[j].z);
-                            acc.w = __fadd_rn(acc.w, v[j].w);
-                            accs = __fadd_rn(accs, sv[j]);
-                        }
-                    }
-                    if (has_col) *reinterpret_cast<float4 *>(red + g * E + 4 * col) = acc;
-                    if (with_s) s_red16[g] = accs;
+                const long long q = tid <= E ? __ldcg(A + (size_t)tid * ACC_LINE) : 0ll;
+                if (tid == 0) {
+                    long long *Z = p.acc + (size_t)((use + 1) & 1) * (E + 1) * ACC_LINE;
+                    for (int e = c; e <= E; e += G) __stcg(Z + (size_t)e * ACC_LINE, 0ll);
                 }
+                if (has_x) *reinterpret_cast<float4 *>(xf + tid * 4) = xv;
+                if (tid < E) tot[tid] = __fmul_rn(__ll2float_rn(q), FX_LOGIT_INV);
+                if (tid == E) s_sumsq = __fmul_rn(__ll2float_rn(q), FX_SUMSQ_INV);
                 __syncthreads();
                 PROF(2)
-                // S in group order, redundantly in every thread
-                float S = s_red16[0];
-                for (int gg = 1; gg < 16; ++gg) S = __fadd_rn(S, s_red16[gg]);
+                const float S = s_sumsq;
                 const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(S, (float)H), p.rms_eps)));
                 if (pend_tbl) {
                     if (!mbar_wait(&mb[MB_TBL], tbl_par)) {
@@ -353,7 +339,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                 if (warp == 0) {
                     int id_r;
                     float w_r;
-                    select_warp<E / 32>(red, inv, tbl, ld.ns, p.delta, p.delta > 0.0f, K, lane, id_r, w_r);
+                    select_warp<E / 32>(tot, inv, tbl, ld.ns, p.delta, p.delta > 0.0f, K, lane, id_r, w_r);
                     if (lane < K) {
                         const bool okid = id_r >= 0 && id_r < E;
                         s_ids[lane] = id_r;
@@ -586,16 +572,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                 __syncthreads();
                 pend_wt = false;
                 wt_par ^= 1;
-                for (int e = tid; e < E; e += DEC_THREADS) {
-                    float acc = 0.0f;
-                    for (int i = 0; i < rows; ++i) acc = __fmaf_rn(wt[i * E + e], rown[i], acc);
-                    __stcg(p.part_p + (size_t)c * E + e, acc);
-                }
-                if (tid == DEC_THREADS - 1) {
-                    float s = 0.0f;
-                    for (int i = 0; i < rows; ++i) s = __fmaf_rn(rown[i], rown[i], s);
-                    __stcg(p.part_s + (size_t)c * PART_S_STRIDE, s);
-                }
+                add_router_partials(p.acc + (size_t)((use + 1) & 1) * (E + 1) * ACC_LINE, wt, rown, rows, E);
             }
 #undef PROF
         }

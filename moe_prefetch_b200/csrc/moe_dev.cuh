@@ -222,29 +222,41 @@ __device__ __forceinline__ void router_softmax_warp(const float *logits, int n_e
     }
 }
 
+// Fixed-point partial sums of the fused decode router.  A CTA's partial
+// logit is clamped to [-2^20, 2^20] and rounded to the nearest multiple of
+// 2^-32 (ties to even), its partial sum of squares clamped to 2^36 and rounded
+// to a multiple of 2^-16; the int64 totals (at most 256 terms, no overflow)
+// do not depend on the order of the additions, and each total becomes a float
+// with one rounding.  or_router_fused restates this.
+#define FX_LOGIT_SCALE 4294967296.0f            // 2^32
+#define FX_LOGIT_INV 2.3283064365386963e-10f    // 2^-32
+#define FX_SUMSQ_SCALE 65536.0f                 // 2^16
+#define FX_SUMSQ_INV 1.52587890625e-05f         // 2^-16
+
+__device__ __forceinline__ long long fx_logit(float v) {
+    return __float2ll_rn(__fmul_rn(fminf(fmaxf(v, -1048576.0f), 1048576.0f), FX_LOGIT_SCALE));
+}
+
+__device__ __forceinline__ long long fx_sumsq(float v) {
+    return __float2ll_rn(__fmul_rn(fminf(v, 68719476736.0f), FX_SUMSQ_SCALE));
+}
+
 // The whole selection of one token in one warp, in registers: the logits
-// from the 16 group rows of `red` (summed in group order, times inv), the
-// softmax and cache prior of router_softmax_warp, top-k as k rounds of
+// tot[e] * inv, the softmax and cache prior of router_softmax_warp, top-k as k rounds of
 // arg-max over the keys (selection bits << 32 | ~id: the total order of
 // topk_key_block), and the weights p / sum(p) with the sum formed in rank
 // order.  The same operations in the same order as those three steps, so
 // the same bits.  Lane r < k returns rank r's id and weight.  M experts per
 // lane (n_expert = 32 * M).
 template <int M>
-__device__ __forceinline__ void select_warp(const float *red, float inv, const int32_t *table,
+__device__ __forceinline__ void select_warp(const float *tot, float inv, const int32_t *table,
                                             int ns, float delta, bool use_prior, int k, int lane,
                                             int &id_r, float &w_r) {
     constexpr int E = 32 * M;
     float lg[M], ex[M], pr[M];
     uint32_t kh[M], kl[M];
 #pragma unroll
-    for (int i = 0; i < M; ++i) {
-        const int e = lane + 32 * i;
-        float tot = red[e];
-#pragma unroll
-        for (int g = 1; g < 16; ++g) tot = __fadd_rn(tot, red[g * E + e]);
-        lg[i] = __fmul_rn(tot, inv);
-    }
+    for (int i = 0; i < M; ++i) lg[i] = __fmul_rn(tot[lane + 32 * i], inv);
     float mx = lg[0];
 #pragma unroll
     for (int i = 1; i < M; ++i) mx = fmaxf(mx, lg[i]);

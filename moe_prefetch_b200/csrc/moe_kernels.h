@@ -129,10 +129,10 @@ struct LayerDesc {
     int32_t pad_;
 };
 
-// One 128-byte line per CTA for its partial sum of squares: every warp of
-// every CTA reads these after the grid barrier, and packing 32 CTAs' values
-// into one line turns those reads into a hot spot at one L2 slice.
-constexpr int PART_S_STRIDE = 32;
+// Fixed-point router accumulators of the persistent decode kernel: one
+// 128-byte line (16 int64) per total, so that the 148 CTAs' additions and
+// reads of one total meet at one line each and no line becomes a hot spot.
+constexpr int ACC_LINE = 16;
 
 struct DecodeParams {
     int n_layers, n_expert, k, n_embd, n_ff, down_type;
@@ -147,8 +147,7 @@ struct DecodeParams {
     int n_tok;
     float *resid;                          // [H]  residual stream
     float *logits;                         // [E] (unused by the 2-barrier kernel)
-    float *part_p;                         // [grid][E] partial logits
-    float *part_s;                         // [grid][PART_S_STRIDE] partial sums of squares (first float)
+    long long *acc;                        // [2][E + 1][ACC_LINE]: router totals, double-buffered
     float *act;                            // [k][I]
     unsigned *bar;                         // grid barrier counter (zeroed per launch)
     int *abort_flag;

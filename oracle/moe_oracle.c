@@ -424,24 +424,21 @@ void or_router_fused(const float *Wt, const float *r, int n_expert, int n_embd,
         for (int h = h0[c]; h < h1[c]; ++h) s = fmaf(r[h], r[h], s);
         S[c] = s;
     }
-    /* 16 contiguous groups of c, each summed sequentially from 0; the group
-     * sums added in group order */
+    /* fixed-point totals (the decode kernel's red.add accumulators); the
+     * device converts with __float2ll_rn / __ll2float_rn, both round to
+     * nearest even like llrintf and the int64 -> float cast here */
     float logits[256];
     for (int e = 0; e < n_expert; ++e) {
-        float tot = 0.0f;
-        for (int g = 0; g < 16; ++g) {
-            float acc = 0.0f;
-            for (int c = g * G / 16; c < (g + 1) * G / 16; ++c) acc = acc + P[(size_t)c * n_expert + e];
-            tot = g == 0 ? acc : tot + acc;
+        long long tot = 0;
+        for (int c = 0; c < G; ++c) {
+            const float v = fminf(fmaxf(P[(size_t)c * n_expert + e], -1048576.0f), 1048576.0f);
+            tot += llrintf(v * 4294967296.0f);
         }
-        logits[e] = tot;
+        logits[e] = (float)tot * 2.3283064365386963e-10f;
     }
-    float st = 0.0f;
-    for (int g = 0; g < 16; ++g) {
-        float acc = 0.0f;
-        for (int c = g * G / 16; c < (g + 1) * G / 16; ++c) acc = acc + S[c];
-        st = g == 0 ? acc : st + acc;
-    }
+    long long stot = 0;
+    for (int c = 0; c < G; ++c) stot += llrintf(fminf(S[c], 68719476736.0f) * 65536.0f);
+    const float st = (float)stot * 1.52587890625e-05f;
     const float inv = 1.0f / sqrtf(st / (float)n_embd + eps);
     for (int e = 0; e < n_expert; ++e) logits[e] = logits[e] * inv;
     if (x_out) for (int h = 0; h < n_embd; ++h) x_out[h] = r[h] * inv;

@@ -88,10 +88,11 @@ void or_router_select(const float *logits, int n_expert, const float *prior, int
 /* The decode kernel's fused RMSNorm + router (canonical order of the
  * persistent kernel): the residual r [n_embd] is split in G row ranges
  * [h0[c], h1[c]); per range, partial logits P[c][e] = sum_h Wt[h][e] r[h]
- * (fma chain in h order) and S[c] = sum_h r[h]^2 (fma chain); partials are
- * summed in 16 contiguous groups of c ([g*G/16, (g+1)*G/16), sequential adds
- * from 0), the group sums added in group order; inv = 1 / sqrtf(S / n_embd +
- * eps); logits = sum * inv;
+ * (fma chain in h order) and S[c] = sum_h r[h]^2 (fma chain); the partials
+ * are summed in fixed point: P clamped to [-2^20, 2^20], S to [.., 2^36],
+ * rounded to int64 multiples of 2^-32 (P) and 2^-16 (S) with ties to even,
+ * added as integers (order-free), each total converted to float once and
+ * scaled back; inv = 1 / sqrtf(S / n_embd + eps); logits = total * inv;
  * x = r * inv.  Wt is the router transposed, [n_embd][n_expert].  x_out and
  * logits_out optional. */
 void or_router_fused(const float *Wt, const float *r, int n_expert, int n_embd,
