@@ -53,15 +53,19 @@ __device__ __forceinline__ void red_release_add(unsigned *p, unsigned v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Grid barrier: every CTA adds 1 (release) and waits (acquire) until the
-// counter reaches epoch * gridDim.x.  Bounded by MOE_TIMEOUT_NS; gives up on
-// the shared abort flag.
-__device__ __forceinline__ bool grid_sync(const DecodeParams &p, unsigned &epoch, int *s_flag) {
+// Grid barrier in two halves, so that a CTA can do work that no other CTA
+// waits for between its arrival and its wait: every CTA adds 1 (release),
+// then waits (acquire) until the counter reaches epoch * gridDim.x.  Bounded
+// by MOE_TIMEOUT_NS; gives up on the shared abort flag.
+__device__ __forceinline__ void grid_arrive(const DecodeParams &p, unsigned &epoch) {
     epoch += 1;
-    const unsigned target = epoch * gridDim.x;
     __syncthreads();
+    if (threadIdx.x == 0) red_release_add(p.bar, 1u);
+}
+
+__device__ __forceinline__ bool grid_wait(const DecodeParams &p, unsigned epoch, int *s_flag) {
+    const unsigned target = epoch * gridDim.x;
     if (threadIdx.x == 0) {
-        red_release_add(p.bar, 1u);
         int ok = 1;
         if (ld_acquire_u32(p.bar) < target) {
             const uint64_t t0 = gtimer();
@@ -80,6 +84,11 @@ __device__ __forceinline__ bool grid_sync(const DecodeParams &p, unsigned &epoch
     }
     __syncthreads();
     return *s_flag != 0;
+}
+
+__device__ __forceinline__ bool grid_sync(const DecodeParams &p, unsigned &epoch, int *s_flag) {
+    grid_arrive(p, epoch);
+    return grid_wait(p, epoch, s_flag);
 }
 
 __device__ __forceinline__ void copy_host16(uint8_t *dst, const uint8_t *src, int bytes) {
@@ -206,6 +215,33 @@ __device__ __forceinline__ void add_router_partials(long long *A, const float *w
     }
 }
 
+// The previous token's experts of the next step's layer into L2, while HBM
+// has nothing else to do until the next selection: one bulk prefetch per
+// (expert, matrix) slice of this CTA (1/G of each matrix), one lane each.
+// The next step's loads of the experts routed again then come from L2.
+// Resident experts only (a miss lives in host memory); pred: ids by rank,
+// -1 unknown; the shared expert (rank K when kx > k) always.
+__device__ __forceinline__ void prefetch_next_l2(const LayerDesc &ldn, const int32_t *pred,
+                                                 const int32_t *tbl, int K, int KX, int E,
+                                                 int64_t gate_bytes, int64_t down_bytes, int c,
+                                                 int G, int lane) {
+    for (int item = lane; item < 3 * KX; item += 32) {
+        const int r = item / 3, m = item - 3 * r;
+        const int id = r < K ? pred[r] : E;
+        if (id < 0 || id > E) continue;
+        const int slot = id == E ? -1 : tbl[id];
+        if (slot == ldn.ns || slot < -1) continue;
+        const int64_t B = m < 2 ? gate_bytes : down_bytes;
+        const uint8_t *base = m == 0 ? (slot < 0 ? ldn.sgate : ldn.gate + (size_t)slot * gate_bytes)
+                            : m == 1 ? (slot < 0 ? ldn.sup : ldn.up + (size_t)slot * gate_bytes)
+                                     : (slot < 0 ? ldn.sdown : ldn.down + (size_t)slot * down_bytes);
+        if (!base) continue;
+        const int64_t o0 = ((int64_t)c * B / G) & ~int64_t(15);
+        const int64_t o1 = c + 1 == G ? B : (((int64_t)(c + 1) * B / G) & ~int64_t(15));
+        if (o1 > o0) prefetch_l2(base + o0, (uint32_t)(o1 - o0));
+    }
+}
+
 template <int E_T, bool Q6_T>
 __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
     extern __shared__ __align__(128) uint8_t sm[];
@@ -220,6 +256,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
     int *ac = reinterpret_cast<int *>(sm + p.off_ac);          // [kx][I/16] -32 * group sums
     float *wt = reinterpret_cast<float *>(sm + p.off_rt);       // [rows][E] router^T rows
     int32_t *tbl = reinterpret_cast<int32_t *>(sm + p.off_tbl); // [E] table row
+    int32_t *prev = reinterpret_cast<int32_t *>(sm + p.off_prev); // [NL][MOE_KMAX] last token's ids
     float *rown = reinterpret_cast<float *>(sm + p.off_rown);   // [rows] own residual rows
     uint8_t *gu = sm + p.off_gu;
     uint8_t *dn = sm + p.off_dn;
@@ -264,6 +301,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
         s_bad = 0;
         if (c == 0) s_clock = p.st.g[G_CLOCK];
     }
+    for (int i = tid; i < NL * MOE_KMAX; i += DEC_THREADS) prev[i] = -1;
     __syncthreads();
 
     unsigned epoch = 0;
@@ -343,6 +381,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                     if (lane < K) {
                         const bool okid = id_r >= 0 && id_r < E;
                         s_ids[lane] = id_r;
+                        prev[(size_t)L * MOE_KMAX + lane] = id_r;
                         s_w[lane] = w_r;
                         s_slot[lane] = okid ? tbl[id_r] : ld.ns;
                         if (!okid) { atomicOr(p.err, MOE_DEV_ERR_INDEX); s_bad = 1; }
@@ -490,8 +529,18 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
             }
             PROF(8)
 
-            // ---- B: activations complete ----------------------------------------------
-            if (!grid_sync(p, epoch, &s_flag)) goto abort;
+            // ---- B: activations complete.  Between its arrival and its wait, warp 15
+            //      puts the previous token's experts of the next step's layer into L2
+            //      (HBM has nothing else to do until the next selection) -------------
+            grid_arrive(p, epoch);
+            if (warp == DEC_WARPS - 1 && (L + 1 < NL || t + 1 < p.n_tok)) {
+                // the next layer's table was queued with this layer's copies
+                const int nl = L + 1 < NL ? L + 1 : 0;
+                if (mbar_wait(&mb[MB_TBL], tbl_par))
+                    prefetch_next_l2(p.layers[nl], prev + (size_t)nl * MOE_KMAX, tbl, K, KX, E,
+                                     p.gate_bytes, p.down_bytes, c, G, lane);
+            }
+            if (!grid_wait(p, epoch, &s_flag)) goto abort;
             PROF(9)
             pend_gu = false;
 
@@ -620,6 +669,7 @@ int decode_smem_layout(DecodeParams &p, int grid) {
     p.dn_stride = align16(p.dn_rows_max * drow + 32) + 16;
     p.off_dn = off; off = align16(off + K * p.dn_stride);
     p.off_ys = off; off = align16(off + K * p.dn_rows_max * 4);
+    p.off_prev = off; off = align16(off + p.n_layers * MOE_KMAX * 4);
     p.smem_bytes = off;
     return off;
 }

@@ -252,7 +252,6 @@ template <int M>
 __device__ __forceinline__ void select_warp(const float *tot, float inv, const int32_t *table,
                                             int ns, float delta, bool use_prior, int k, int lane,
                                             int &id_r, float &w_r) {
-    constexpr int E = 32 * M;
     float lg[M], ex[M], pr[M];
     uint32_t kh[M], kl[M];
 #pragma unroll
@@ -1001,14 +1000,17 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
                  : "memory");
 }
 
+// One try_wait with a suspend-time hint of 1 ms: a waiting warp sleeps until
+// the phase completes (the hardware wakes it) or the hint runs out, instead
+// of polling and taking issue slots from the warps that produce the data.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
         : "memory");
     return ok != 0;
 }

@@ -163,7 +163,7 @@ struct DecodeParams {
     uint64_t *prof;                        // [n_tok][L][DEC_PHASES][grid] or null
     // shared-memory layout (bytes from the start of dynamic smem)
     int off_xf, off_xq, off_xd, off_xs, off_aq, off_ad, off_as, off_ac, off_rt, off_tbl, off_rown,
-        off_gu, off_dn, off_ys, smem_bytes;
+        off_gu, off_dn, off_ys, off_prev, smem_bytes;
     int dn_stride;                         // bytes per expert chunk in the down staging
     int rt_rows;                           // router rows per CTA (ceil(E / grid))
 };

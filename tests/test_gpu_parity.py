@@ -253,6 +253,19 @@ def test_decode_stack_parity(stack4, oracle_lib):
         r = (r + ys[:, L]).astype(np.float32)
 
 
+def test_decode_prefetch_invariant(stack4):
+    """The persistent kernel prefetches into L2, for the next layer, the
+    experts the previous token used there.  That may change when bytes move,
+    never the result: one launch over 8 tokens (prefetch hits and misses)
+    gives the same bits as 8 one-token launches (no prefetch at all)."""
+    st = stack4
+    h = torch.from_numpy(ar1_states(8, H, seed=12)).cuda()
+    out = st.decode(h)
+    for t in range(8):
+        assert torch.equal(st.decode(h[t:t + 1].contiguous()), out[t:t + 1])
+    st.sync()
+
+
 def test_decode_matches_layer_forward(stack4):
     """Same x and same routed experts -> the persistent kernel and the
     stand-alone kernels give the same output bits (same unit mapping, same
