@@ -659,6 +659,58 @@ def run_layer(args):
 
 
 # ---------------------------------------------------------------------------
+# where a decode layer's time goes (the kernel's own phase stamps)
+# ---------------------------------------------------------------------------
+PHASES = [(0, 1, "grid barrier A"), (1, 2, "router totals"), (2, 6, "selection"),
+          (6, 7, "copy issue (warp 0)"), (6, 8, "gate/up rows done (warp 1)"),
+          (8, 9, "grid barrier B"), (9, 10, "activations -> Q8_1"), (10, 11, "down rows + combine")]
+
+
+def run_phases(args):
+    """Config-1 shapes (or config 4 with --c4), --layers x --tokens AR(1)
+    tokens through one moe_decode launch with phase stamps (%globaltimer, one
+    per CTA per phase boundary); prints per phase the median over CTAs and
+    layer-tokens (the first token's layers skipped), the median of the
+    per-layer-token maximum over CTAs, and the layer time."""
+    import ctypes as C
+    import torch
+    from moe_prefetch_b200 import MoeStack
+    from moe_prefetch_b200._lib import MoeDecodeDbg
+    torch.cuda.set_device(0)
+    L, T, PH = args.layers, args.tokens, 12
+    kw = dict(n_expert=256, n_ff=512, n_shared=1) if args.c4 else {}
+    st = MoeStack(n_layers=L, **kw)
+    st.synth_resident(seed=3)
+    h = torch.from_numpy(ar1_states(T, N_EMBD, 5)).cuda()
+    out = torch.empty_like(h)
+    for _ in range(max(args.warmup, 1)):
+        st.decode(h, out)
+    st.sync()
+    G = st.decode_info()["grid"]
+    prof = torch.zeros(T, L, PH, G, dtype=torch.int64, device="cuda")
+    dbg = MoeDecodeDbg(None, None, None, None, prof.data_ptr())
+    s = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    rc = st.lib.moe_decode(st.ctx, C.c_void_p(h.data_ptr()), C.c_void_p(out.data_ptr()), T, C.byref(dbg), s)
+    st.sync()
+    if rc != 0:
+        print(f"moe_decode failed: {rc}", file=sys.stderr)
+        return 1
+    flat = prof.cpu().numpy().astype(np.int64).reshape(T * L, PH, G)[L:]
+    res = {}
+    for a, b, name in PHASES:
+        d = (flat[:, b, :] - flat[:, a, :]).astype(np.float64) / 1000.0
+        res[name] = {"median_us": round(float(np.median(d)), 3),
+                     "max_over_ctas_us": round(float(np.median(d.max(-1))), 3)}
+    lay = (flat[1:, 0, :] - flat[:-1, 0, :]).astype(np.float64) / 1000.0
+    print(json.dumps({"metric": "decode layer phases", "unit": "us", "layer_us": round(float(np.median(lay)), 3),
+                      "phases": res, "config": {"workload": f"{L} layers x {T} tokens, "
+                                                f"{'config-4' if args.c4 else 'config-1'} shapes",
+                                                "grid": G, "data": "synthetic"}}), flush=True)
+    st.close()
+    return 0
+
+
+# ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
 def main():
@@ -673,7 +725,9 @@ def main():
     ap.add_argument("--ref-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--workload", default="config1", choices=["config1", "config2", "config3", "config4", "layer"])
+    ap.add_argument("--workload", default="config1",
+                    choices=["config1", "config2", "config3", "config4", "layer", "phases"])
+    ap.add_argument("--c4", action="store_true", help="phases: config-4 shapes")
     ap.add_argument("--path", default="gemv", choices=["auto", "gemv", "gemm"])
     ap.add_argument("--c3-decode-steps", type=int, default=128)
     ap.add_argument("--c3-prefill-chunks", type=int, default=4)
@@ -690,6 +744,8 @@ def main():
         return run_config4(args)
     if args.workload == "layer":
         return run_layer(args)
+    if args.workload == "phases":
+        return run_phases(args)
 
     import torch
     import torch.distributed as dist

@@ -263,7 +263,10 @@ int moe_layer_forward_noalloc(moe_ctx *ctx, int layer, const float *x, float *y,
  * x [n_tok][n_layers][n_embd] (router input), ids/w [n_tok][n_layers][n_used],
  * y [n_tok][n_layers][n_embd] (the layer's MoE output), and phase timestamps
  * prof [n_tok][n_layers][MOE_DECODE_PHASES][grid] (%globaltimer ns, one per CTA
- * at each phase boundary). */
+ * at each phase boundary: 0 layer start, 1 after the first grid barrier, 2
+ * router totals read, 6 selection done, 7 copies issued, 8 gate/up rows done
+ * (warp 1), 9 after the second grid barrier, 10 activations quantised, 11
+ * combine done; 3-5 unused). */
 #define MOE_DECODE_PHASES 12
 typedef struct moe_decode_dbg {
     float    *x;
