@@ -439,6 +439,11 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                             mbar_arrive_expect_tx(&mb[MB_GU + q], 0);
                         }
                     }
+                    // The down rows are read only after the second grid barrier: the
+                    // gate/up pieces get the copy engine and HBM to themselves first.
+                    __syncwarp();
+                    if (lane < nch) mbar_wait(&mb[MB_GU + lane], par);
+                    __syncwarp();
                     if (lane >= 8 && lane < 8 + KX) {
                         const int kk = lane - 8;
                         const int slot = s_slot[kk];
