@@ -550,7 +550,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
             pend_gu = false;
 
             // ---- 5. activations -> Q8_1 ---------------------------------------------
-            q8_quantize_cta16(p.act, KX * I / 32, aq, ad, as_, ac, tid, DEC_THREADS);
+            q8_quantize_cta16(p.act, KX * I / 32, aq, ad, as_, ac, tid, DEC_THREADS, Q6_T ? I / 32 : 0);
             __syncthreads();
             PROF(10)
 
@@ -579,8 +579,8 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                         ActHalfU a;
                         float v = 0.0f;
                         if (on) {
-                            load_act_half_u(a, aq + (size_t)kk * I, ad + (size_t)kk * (I / 32),
-                                            ac + (size_t)kk * (I / 16), sb, hh);
+                            load_act_half_up(a, aq + (size_t)kk * (I + I / 8), ad + (size_t)kk * (I / 32),
+                                             ac + (size_t)kk * ACT_C_STRIDE(I / 32), sb, hh);
                             if (i < rows)
                                 v = q6k_half_dot_u(rws + (size_t)i * drow + sb * MOE_Q6K_BYTES, hh, a);
                         }
@@ -663,10 +663,10 @@ int decode_smem_layout(DecodeParams &p, int grid) {
     p.off_xq = off; off = align16(off + H);
     p.off_xd = off; off = align16(off + (H / 32) * 4);
     p.off_xs = off; off = align16(off + (H / 32) * 4);
-    p.off_aq = off; off = align16(off + K * I);
+    p.off_aq = off; off = align16(off + K * (I + I / 8));   // padded (load_act_half_up)
     p.off_ad = off; off = align16(off + K * (I / 32) * 4);
     p.off_as = off; off = align16(off + K * (I / 32) * 4);
-    p.off_ac = off; off = align16(off + K * (I / 16) * 4);
+    p.off_ac = off; off = align16(off + K * ACT_C_STRIDE(I / 32) * 4);
     p.off_rt = off; off = align16(off + p.dn_rows_max * E * 4);
     p.off_tbl = off; off = align16(off + E * 4);
     p.off_rown = off; off = align16(off + p.dn_rows_max * 4);

@@ -453,15 +453,22 @@ __device__ __forceinline__ void q8_scale_quantize_cta(float *xf, float inv, int 
     }
 }
 
+// Padded activation layout of the decode kernel's down rows: 16 bytes after
+// every 128 int8 of q, and per expert ACT_C_STRIDE(bpe) group offsets with 4
+// ints after every 32, so that the six half super-blocks a row group reads
+// fall in different shared-memory banks.  bpe: Q8_1 blocks per expert.
+#define ACT_C_STRIDE(bpe) (2 * (bpe) + (bpe) / 4)
+
 // All threads quantise n_blocks blocks read from global memory that other
 // CTAs wrote (ld.global.cg), two threads per block (16 values each), every
 // load issued before the arithmetic: the same d, q and s as q8_quantize_cta.
+// With bpe > 0, q and c16 are written in the padded layout above.
 // Also c16[2 * blk + half] = -32 * (sum of the 16 q of that half): the start
 // value that turns a dot of unsigned 6-bit values with q into a dot of
 // (value - 32) with q (dp4a_us).
 __device__ __forceinline__ void q8_quantize_cta16(const float *src, int n_blocks, int8_t *q,
                                                   float *d, float *s, int *c16, int tid,
-                                                  int nthreads) {
+                                                  int nthreads, int bpe = 0) {
     const int lane = tid & 31;
     for (int base = tid - lane; base < n_blocks * 2; base += nthreads) {
         const int t2 = base + lane;
@@ -497,8 +504,14 @@ __device__ __forceinline__ void q8_quantize_cta16(const float *src, int n_blocks
         }
         const int sum = sum16 + __shfl_xor_sync(MOE_FULL, sum16, 1);
         if (valid) {
-            *reinterpret_cast<uint4 *>(q + 32 * blk + 16 * part) = make_uint4(w[0], w[1], w[2], w[3]);
-            c16[2 * blk + part] = -32 * sum16;
+            const int e = 32 * blk + 16 * part;
+            int ci = 2 * blk + part;
+            if (bpe > 0) {   // padded layout (load_act_half_up): bpe blocks per expert
+                const int kk = blk / bpe, lci = ci - 2 * kk * bpe;
+                ci = kk * ACT_C_STRIDE(bpe) + lci + 4 * (lci >> 5);
+            }
+            *reinterpret_cast<uint4 *>(q + (bpe > 0 ? e + 16 * (e >> 7) : e)) = make_uint4(w[0], w[1], w[2], w[3]);
+            c16[ci] = -32 * sum16;
             if (part == 0) {
                 d[blk] = db;
                 s[blk] = __fmul_rn(db, (float)sum);
@@ -893,6 +906,24 @@ __device__ __forceinline__ void load_act_half_u(ActHalfU &a, const int8_t *q, co
         a.q[m][4] = v1.x; a.q[m][5] = v1.y; a.q[m][6] = v1.z; a.q[m][7] = v1.w;
         a.d[m] = d[e >> 5];
         const int2 cc = *reinterpret_cast<const int2 *>(c16 + (e >> 4));
+        a.c[2 * m] = cc.x;
+        a.c[2 * m + 1] = cc.y;
+    }
+}
+
+// load_act_half_u from the padded layout (q16_base and c16 of one expert).
+__device__ __forceinline__ void load_act_half_up(ActHalfU &a, const int8_t *q, const float *d,
+                                                 const int *c16, int sb, int h) {
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+        const int e = 256 * sb + 128 * h + 32 * m;
+        const int4 *qp = reinterpret_cast<const int4 *>(q + e + 16 * (e >> 7));
+        const int4 v0 = qp[0], v1 = qp[1];
+        a.q[m][0] = v0.x; a.q[m][1] = v0.y; a.q[m][2] = v0.z; a.q[m][3] = v0.w;
+        a.q[m][4] = v1.x; a.q[m][5] = v1.y; a.q[m][6] = v1.z; a.q[m][7] = v1.w;
+        a.d[m] = d[e >> 5];
+        const int ci = e >> 4;
+        const int2 cc = *reinterpret_cast<const int2 *>(c16 + ci + 4 * (ci >> 5));
         a.c[2 * m] = cc.x;
         a.c[2 * m + 1] = cc.y;
     }
