@@ -765,7 +765,7 @@ def main():
             dist.barrier()
 
     n_layers, tokens = args.layers, args.tokens
-    st = MoeStack(n_layers=n_layers)
+    st = MoeStack(n_layers=n_layers, device=local)
     st.synth_resident(seed=7919 * rank + 11)
     h = torch.from_numpy(ar1_states(tokens, N_EMBD, seed=12345 + rank)).cuda()
     out = torch.empty_like(h)

@@ -52,12 +52,16 @@ class _CudaView:
 
 class MoeStack:
     def __init__(self, n_layers, n_expert=128, n_used=8, n_embd=2048, n_ff=768,
-                 down_type=QTYPE_Q6_K, cache=None, device=0, n_shared=0):
+                 down_type=QTYPE_Q6_K, cache=None, device=None, n_shared=0):
         self.lib = _lib.load()
         self.cache = cache or MoeCacheConfig()
         self.n_layers, self.n_expert, self.n_used = n_layers, n_expert, n_used
         self.n_embd, self.n_ff, self.down_type = n_embd, n_ff, down_type
         self.n_shared = n_shared
+        # default: the caller's current CUDA device (one stack per rank under
+        # torch.distributed, each on its own GPU)
+        if device is None:
+            device = torch.cuda.current_device()
         self.device = torch.device("cuda", device)
         self.gate_bytes, self.down_bytes = expert_bytes(n_embd, n_ff, down_type)
         self.ns = self.cache.slots_per_layer(n_layers, n_expert)
