@@ -663,7 +663,8 @@ def run_layer(args):
 # ---------------------------------------------------------------------------
 PHASES = [(0, 1, "grid barrier A"), (1, 2, "router totals"), (2, 6, "selection"),
           (6, 7, "copy issue (warp 0)"), (6, 8, "gate/up rows done (warp 1)"),
-          (8, 9, "grid barrier B"), (9, 10, "activations -> Q8_1"), (10, 11, "down rows + combine")]
+          (8, 9, "rank signals"), (9, 10, "rank 0: wait, activations -> Q8_1, down rows"),
+          (10, 11, "other ranks + combine")]
 
 
 def run_phases(args):

@@ -265,8 +265,8 @@ int moe_layer_forward_noalloc(moe_ctx *ctx, int layer, const float *x, float *y,
  * prof [n_tok][n_layers][MOE_DECODE_PHASES][grid] (%globaltimer ns, one per CTA
  * at each phase boundary: 0 layer start, 1 after the first grid barrier, 2
  * router totals read, 6 selection done, 7 copies issued, 8 gate/up rows done
- * (warp 1), 9 after the second grid barrier, 10 activations quantised, 11
- * combine done; 3-5 unused). */
+ * (warp 1), 9 this CTA's ranks signalled, 10 rank 0's down rows done (warp 0's
+ * group), 11 combine done; 3-5 unused). */
 #define MOE_DECODE_PHASES 12
 typedef struct moe_decode_dbg {
     float    *x;

@@ -53,6 +53,7 @@ struct moe_ctx {
     float *resid = nullptr, *logits = nullptr, *act = nullptr;
     long long *acc = nullptr;   // decode router accumulators
     unsigned *bar = nullptr;
+    unsigned *ready = nullptr;         // decode per-rank activation signals
     int *abort_flag = nullptr, *err = nullptr;
     // scratch for moe_layer_forward / moe_decode_host
     int32_t *s_ids = nullptr;
@@ -288,10 +289,19 @@ extern "C" int moe_create(const moe_cfg *cfg, moe_ctx **out) {
             cudaMalloc(&c->acc, sizeof(long long) * 2 * (size_t)(E + 1) * moe::ACC_LINE) != cudaSuccess ||
             cudaMalloc(&c->act, sizeof(float) * (size_t)MOE_KMAX * I) != cudaSuccess ||
             cudaMalloc(&c->bar, 64) != cudaSuccess || cudaMalloc(&c->abort_flag, 64) != cudaSuccess ||
+            cudaMalloc(&c->ready, sizeof(unsigned) * MOE_KMAX * moe::READY_STRIDE) != cudaSuccess ||
             cudaMalloc(&c->err, 64) != cudaSuccess)
             return cleanup_fail(MOE_ERR_OOM);
         cudaMemset(c->err, 0, 64);
-        p.resid = c->resid; p.logits = c->logits; p.act = c->act; p.bar = c->bar;
+        p.resid = c->resid; p.logits = c->logits; p.act = c->act; p.bar = c->bar; p.ready = c->ready;
+        // producers of each rank's activations: the CTAs whose gate/up range
+        // [r0, r1) of the flattened (rank, row) space meets that rank
+        for (int q = 0; q < MOE_KMAX; ++q) p.n_prod[q] = 0;
+        for (int cc = 0; cc < G; ++cc) {
+            const int a0 = part[cc], a1 = part[G + cc];
+            if (a1 > a0)
+                for (int q = a0 / I; q <= (a1 - 1) / I && q < MOE_KMAX; ++q) p.n_prod[q] += 1;
+        }
         p.acc = c->acc;
         p.abort_flag = c->abort_flag; p.err = c->err; p.st = c->st;
         p.observe = 1; p.delta = g.cache_prior; p.rms_eps = 1e-6f;
@@ -335,6 +345,7 @@ extern "C" void moe_destroy(moe_ctx *c) {
     cudaFree(c->logits);
     cudaFree(c->act);
     cudaFree(c->bar);
+    cudaFree(c->ready);
     cudaFree(c->abort_flag);
     cudaFree(c->err);
     cudaFree(c->s_ids);
@@ -830,6 +841,7 @@ extern "C" int moe_decode(moe_ctx *c, const float *h, float *out, int n_tok,
     if (p.dbg_ids && !p.dbg_w) return fail(c, MOE_ERR_ARG, "moe_decode: dbg ids without w");
     CK(cudaMemsetAsync(c->bar, 0, 64, s));
     CK(cudaMemsetAsync(c->abort_flag, 0, 64, s));
+    CK(cudaMemsetAsync(c->ready, 0, sizeof(unsigned) * MOE_KMAX * moe::READY_STRIDE, s));
     CK(cudaMemsetAsync(c->acc, 0, sizeof(long long) * 2 * (size_t)(c->cfg.n_expert + 1) * moe::ACC_LINE, s));
     CK(launch_decode(p, c->grid, s));
     return MOE_OK;

@@ -269,6 +269,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
     __shared__ int s_flag;
     __shared__ int s_bad;
     __shared__ int s_any_miss;
+    __shared__ int s_fail;
     __shared__ uint64_t s_clock;
 
     const int G = gridDim.x, c = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -534,10 +535,17 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
             }
             PROF(8)
 
-            // ---- B: activations complete.  Between its arrival and its wait, warp 15
-            //      puts the previous token's experts of the next step's layer into L2
-            //      (HBM has nothing else to do until the next selection) -------------
-            grid_arrive(p, epoch);
+            // ---- B: this CTA's gate/up rows are done: signal the ranks it produced
+            //      (release; after the zeroing of the other router buffer, so that
+            //      a CTA that has seen every rank's signal may add into it) --------
+            if (tid == 0) s_fail = 0;
+            __syncthreads();
+            if (tid == 0)
+                for (int q = 0; q < nch; ++q) red_release_add(p.ready + ch_k[q] * READY_STRIDE, 1u);
+            PROF(9)
+            pend_gu = false;
+            // warp 15 puts the previous token's experts of the next step's layer
+            // into L2 (HBM has nothing else to do until the next selection)
             if (warp == DEC_WARPS - 1 && (L + 1 < NL || t + 1 < p.n_tok)) {
                 // the next layer's table was queued with this layer's copies
                 const int nl = L + 1 < NL ? L + 1 : 0;
@@ -545,64 +553,94 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                     prefetch_next_l2(p.layers[nl], prev + (size_t)nl * MOE_KMAX, tbl, K, KX, E,
                                      p.gate_bytes, p.down_bytes, c, G, lane);
             }
-            if (!grid_wait(p, epoch, &s_flag)) goto abort;
-            PROF(9)
-            pend_gu = false;
 
-            // ---- 5. activations -> Q8_1 ---------------------------------------------
-            q8_quantize_cta16(p.act, KX * I / 32, aq, ad, as_, ac, tid, DEC_THREADS, Q6_T ? I / 32 : 0);
-            __syncthreads();
-            PROF(10)
-
-            // ---- 6. down GEMV: items (expert, group of 4 rows) over all warps; one
-            //         lane per half super-block, 8-lane row groups ---------------------
-            if (rows > 0) {
-                const int grp = lane >> 3, u = lane & 7;   // row in the group, unit
-                const int nrg = Q6_T ? (rows + 3) >> 2 : rows;
-                for (int it = warp; it < KX * nrg; it += DEC_WARPS) {
-                    const int kk = it / nrg, rg = it - kk * nrg;
+            // ---- 5/6. per rank k, a group of one or two warps: wait until every CTA
+            //      producing rank k's activations has signalled, quantise them
+            //      (Q8_1), then the down GEMV rows of rank k -- one lane per half
+            //      super-block, 8-lane row groups.  Ranks whose producers finish
+            //      early are done while the others still run; no grid barrier. ----
+            {
+                int kk = 0;
+                while ((kk + 1) * DEC_WARPS / KX <= warp) ++kk;
+                const int w0 = kk * DEC_WARPS / KX, nw = (kk + 1) * DEC_WARPS / KX - w0, gw = warp - w0;
+                const unsigned gthreads = (unsigned)nw * 32u;
+                if (gw == 0 && lane == 0) {
+                    const unsigned target = (unsigned)(use + 1) * (unsigned)p.n_prod[kk];
+                    bool ok = true;
+                    if (ld_acquire_u32(p.ready + kk * READY_STRIDE) < target) {
+                        const uint64_t t0 = gtimer();
+                        while (ld_acquire_u32(p.ready + kk * READY_STRIDE) < target) {
+                            if (ld_relaxed_i32(p.abort_flag)) { ok = false; break; }
+                            if (gtimer() - t0 > MOE_TIMEOUT_NS) {
+                                atomicOr(p.err, MOE_DEV_ERR_TIMEOUT);
+                                atomicExch(p.abort_flag, 1);
+                                ok = false;
+                                break;
+                            }
+                        }
+                    }
+                    if (!ok) s_fail = 1;
+                }
+                if (nw > 1) asm volatile("bar.sync %0, %1;" ::"r"(1 + kk), "r"(gthreads) : "memory");
+                else __syncwarp();
+                // rank kk's activations -> Q8_1 (padded layout for the Q6_K rows)
+                q8_quantize_cta16(p.act + (size_t)kk * I, I / 32,
+                                  aq + (size_t)kk * (Q6_T ? I + I / 8 : I), ad + (size_t)kk * (I / 32),
+                                  as_ + (size_t)kk * (I / 32),
+                                  ac + (size_t)kk * (Q6_T ? ACT_C_STRIDE(I / 32) : I / 16),
+                                  gw * 32 + lane, (int)gthreads, Q6_T ? I / 32 : 0);
+                if (nw > 1) asm volatile("bar.sync %0, %1;" ::"r"(1 + kk), "r"(gthreads) : "memory");
+                else __syncwarp();
+                if (rows > 0) {
+                    const int grp = lane >> 3, u = lane & 7;   // row in the group, unit
+                    const int nrg = Q6_T ? (rows + 3) >> 2 : rows;
                     const int sl = s_slot[kk];
                     const uint8_t *base = sl < 0 ? ld.sdown
                         : sl != ld.ns ? ld.down + (size_t)sl * p.down_bytes
                                       : ld.hdown + (size_t)s_ids[kk] * p.down_bytes;
                     const uintptr_t a0 = reinterpret_cast<uintptr_t>(base + (size_t)h0 * drow);
                     const uint8_t *rws = dn + (size_t)kk * p.dn_stride + (int)(a0 & 15);
-                    if (!__all_sync(MOE_FULL, mbar_wait(&mb[MB_DN + kk], par))) {
-                        if (lane == 0) { atomicOr(p.err, MOE_DEV_ERR_TIMEOUT); atomicExch(p.abort_flag, 1); }
-                        break;
-                    }
-                    if constexpr (Q6_T) {
-                        const int nunits = (I / MOE_QK) * 2;           // half blocks per row
-                        const bool on = u < nunits;
-                        const int sb = u >> 1, hh = u & 1;
-                        const int i = rg * 4 + grp;
-                        ActHalfU a;
-                        float v = 0.0f;
-                        if (on) {
-                            load_act_half_up(a, aq + (size_t)kk * (I + I / 8), ad + (size_t)kk * (I / 32),
-                                             ac + (size_t)kk * ACT_C_STRIDE(I / 32), sb, hh);
-                            if (i < rows)
-                                v = q6k_half_dot_u(rws + (size_t)i * drow + sb * MOE_Q6K_BYTES, hh, a);
+                    const bool dn_ok = __all_sync(MOE_FULL, mbar_wait(&mb[MB_DN + kk], par));
+                    if (!dn_ok && lane == 0) { atomicOr(p.err, MOE_DEV_ERR_TIMEOUT); atomicExch(p.abort_flag, 1); s_fail = 1; }
+                    for (int rg = gw; rg < nrg && dn_ok; rg += nw) {
+                        if constexpr (Q6_T) {
+                            const int nunits = (I / MOE_QK) * 2;           // half blocks per row
+                            const bool on = u < nunits;
+                            const int sb = u >> 1, hh = u & 1;
+                            const int i = rg * 4 + grp;
+                            ActHalfU a;
+                            float v = 0.0f;
+                            if (on) {
+                                load_act_half_up(a, aq + (size_t)kk * (I + I / 8), ad + (size_t)kk * (I / 32),
+                                                 ac + (size_t)kk * ACT_C_STRIDE(I / 32), sb, hh);
+                                if (i < rows)
+                                    v = q6k_half_dot_u(rws + (size_t)i * drow + sb * MOE_Q6K_BYTES, hh, a);
+                            }
+                            v = group8_sum(v);
+                            if (u == 0 && i < rows) ys[kk * p.dn_rows_max + i] = v;
+                        } else {
+                            const int units = (I / MOE_QK) * 4;
+                            const bool on = lane < units;
+                            float v = 0.0f;
+                            if (on) {
+                                ActQ4 a;
+                                load_act_q4(a, aq + (size_t)kk * I, ad + (size_t)kk * (I / 32),
+                                            as_ + (size_t)kk * (I / 32), lane >> 2, lane & 3);
+                                v = q4k_unit_dot(rws + (size_t)rg * drow + (lane >> 2) * MOE_Q4K_BYTES, lane & 3, a);
+                            }
+                            v = warp_sum(v);
+                            if (lane == 0) ys[kk * p.dn_rows_max + rg] = v;
                         }
-                        v = group8_sum(v);
-                        if (u == 0 && i < rows) ys[kk * p.dn_rows_max + i] = v;
-                    } else {
-                        const int units = (I / MOE_QK) * 4;
-                        const bool on = lane < units;
-                        float v = 0.0f;
-                        if (on) {
-                            ActQ4 a;
-                            load_act_q4(a, aq + (size_t)kk * I, ad + (size_t)kk * (I / 32),
-                                        as_ + (size_t)kk * (I / 32), lane >> 2, lane & 3);
-                            v = q4k_unit_dot(rws + (size_t)rg * drow + (lane >> 2) * MOE_Q4K_BYTES, lane & 3, a);
-                        }
-                        v = warp_sum(v);
-                        if (lane == 0) ys[kk * p.dn_rows_max + rg] = v;
                     }
                 }
             }
+            PROF(10)
             __syncthreads();
             pend_dn = false;
+            if (s_fail) {
+                if (tid == 0) atomicExch(p.abort_flag, 1);
+                goto abort;
+            }
             const bool last = L == NL - 1;
             for (int i = tid; i < rows; i += DEC_THREADS) {
                 float y = 0.0f;

@@ -133,6 +133,8 @@ struct LayerDesc {
 // 128-byte line (16 int64) per total, so that the 148 CTAs' additions and
 // reads of one total meet at one line each and no line becomes a hot spot.
 constexpr int ACC_LINE = 16;
+// one 128-byte line per rank's activation signal in the decode kernel
+constexpr int READY_STRIDE = 32;
 
 struct DecodeParams {
     int n_layers, n_expert, k, n_embd, n_ff, down_type;
@@ -150,6 +152,8 @@ struct DecodeParams {
     long long *acc;                        // [2][E + 1][ACC_LINE]: router totals, double-buffered
     float *act;                            // [k][I]
     unsigned *bar;                         // grid barrier counter (zeroed per launch)
+    unsigned *ready;                       // [MOE_KMAX][READY_STRIDE] per-rank activation signals (zeroed per launch)
+    int n_prod[MOE_KMAX];                  // CTAs producing each rank's gate/up rows
     int *abort_flag;
     int *err;
     SlotState st;
