@@ -1,39 +1,40 @@
 // moe_decode.cu -- persistent batch-1 decode over the whole MoE stack.
 //
-// One cooperative launch, one CTA per SM, 16 warps; two grid barriers per
+// One cooperative launch, one CTA per SM, 16 warps; one grid barrier per
 // layer.  CTA c owns rows [h0, h1) of the residual stream for the whole
-// token and, inside every layer, the flattened (expert, row) range
-// [r0, r1) of the gate/up work.  Per token t and layer L:
+// token and, inside every layer, the flattened (rank, row) range [r0, r1)
+// of the gate/up work.  Per token t and layer L:
 //
-//   -- grid barrier A: partial logits / partial sums of squares of (t, L)
-//      and the residual rows are complete --
-//   1. every CTA reads the full residual (L2) and the G partial logit
-//      vectors, reduces them in a fixed order (so every CTA gets the same
-//      bits) into RMSNorm-scaled logits, normalises x = r * inv_rms, and
-//      quantises x to Q8_1 in shared memory;
-//   2. softmax, + cache prior from the layer's table row (prefetched into
-//      shared memory), top-k by rank (all threads), renormalised weights;
-//      slots from the table; the routed ids are observed (moe_obs_cb) by
-//      CTA 0 with its counters cached on chip;
-//   3. warp 0 issues, lane-parallel, one bulk copy (cp.async.bulk, TMA, no
-//      multicast) per contiguous piece of this CTA's share of the layer's
-//      expert bytes -- gate/up rows of its (expert, row) range and the down
-//      rows of its residual rows for all k experts -- plus the next layer's
-//      transposed router rows for its residual rows and the next table row;
+//   -- grid barrier: the router totals of (t, L) and the residual rows are
+//      complete --
+//   1. every CTA reads the full residual (L2) and the E + 1 fixed-point
+//      router totals (int64, added by every CTA with red.add: the same bits
+//      whatever the order), normalises x = r * inv_rms and zeroes its share
+//      of the other totals buffer;
+//   2. warp 0: softmax, + cache prior from the layer's table row (prefetched
+//      into shared memory), top-k and the renormalised weights in registers;
+//      slots from the table; warps 1-8 quantise x to Q8_1 meanwhile; CTA 0
+//      observes the routed ids (moe_obs_cb) with its counters on chip;
+//   3. warp 0 issues one bulk copy (cp.async.bulk, TMA, no multicast) per
+//      contiguous piece of this CTA's gate/up rows, waits for them to land,
+//      then issues the down rows of its residual rows for all k experts, the
+//      next layer's transposed router rows and its table row;
 //   4. gate/up GEMV (Q4_K x Q8_1, dp4a) with SiLU*mul as pieces land;
 //      activations to L2;
-//   -- grid barrier B: activations complete --
-//   5. the k activation vectors are re-quantised (Q8_1) in shared memory;
-//   6. down GEMV rows (Q6_K x Q8_1) of its residual rows for all k experts,
-//      weighted combine, residual add; the new rows go to L2, and the partial
-//      logits / sum of squares of the NEXT layer over these rows are
-//      computed on the spot from the prefetched router rows.
+//   5. the CTA signals every rank it produced (release); warp 15 prefetches
+//      the previous token's experts of the next layer into L2;
+//   6. per rank, a group of warps waits for that rank's producers, quantises
+//      its activations (Q8_1, padded shared-memory layout) and computes the
+//      down GEMV rows (Q6_K x Q8_1) of this CTA's residual rows; then the
+//      weighted combine in rank order and the residual add; the new rows go
+//      to L2, and the partial logits / sum of squares of the NEXT layer over
+//      these rows are added into the totals.
 //
 // Missed experts (table entry = n_slots) are read zero-copy from the
 // registered host weights instead of the slot slabs.  Every wait (grid
-// barrier, mbarrier) is bounded by %globaltimer; on expiry the kernel raises
-// an error bit and an abort flag, waits (bounded) for its own copies in
-// flight, and returns.
+// barrier, rank signal, mbarrier) is bounded by %globaltimer; on expiry the
+// kernel raises an error bit and an abort flag, waits (bounded) for its own
+// copies in flight, and returns.
 #include "moe_kernels.h"
 
 #include <algorithm>
