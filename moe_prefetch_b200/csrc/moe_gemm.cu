@@ -37,6 +37,7 @@ namespace moe {
 #define GM_THREADS 256
 #define GM_KS_GU 64        // K per gate/up stage (one Q4_K 64-element group)
 #define GM_KS_DN 128       // K per down stage (one Q6_K half block)
+#define DN_THREADS 512     // down GEMM: 4 threads per row, one quarter each
 
 // ---- tcgen05 / TMEM wrappers ------------------------------------------------
 
@@ -127,6 +128,13 @@ __device__ __forceinline__ float u2f(uint32_t q) {
     return __int_as_float(0x4B000000 | q) - 8388608.0f;
 }
 
+// Byte j of x as an exact float minus `bias`: the byte placed into the low
+// mantissa of 2^23 (0x4B0000xx) by one byte permute, then one subtraction
+// (exact for small integers), i.e. the same value as u2f(byte) - (bias - 2^23).
+__device__ __forceinline__ float byte_f(uint32_t x, int j, float bias) {
+    return __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7650u | (uint32_t)j)) - bias;
+}
+
 // ---- operand tiles --------------------------------------------------------
 // Canonical no-swizzle K-major tile of R rows x KS columns (fp16): element
 // (r, k) at byte ((k / 8) * R + r) * 16 + (k % 8) * 2, i.e. LBO = 16 R,
@@ -181,11 +189,13 @@ __device__ __forceinline__ void deq_q4k_group(const uint4 &hdr, const uint4 &q0,
 #pragma unroll
         for (int b = 0; b < 2; ++b) {
             const uint32_t v = w[2 * c + b];
+            const uint32_t L = v & 0x0F0F0F0Fu, Hh = (v >> 4) & 0x0F0F0F0Fu;
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
-                const uint32_t b0 = (v >> (16 * j)) & 0xFFu, b1 = (v >> (16 * j + 8)) & 0xFFu;
-                lo[2 * b + j] = pack_h2(fmaf(d1, u2f(b0 & 15u), -m1), fmaf(d1, u2f(b1 & 15u), -m1));
-                hi[2 * b + j] = pack_h2(fmaf(d2, u2f(b0 >> 4), -m2), fmaf(d2, u2f(b1 >> 4), -m2));
+                lo[2 * b + j] = pack_h2(fmaf(d1, byte_f(L, 2 * j, 8388608.0f), -m1),
+                                        fmaf(d1, byte_f(L, 2 * j + 1, 8388608.0f), -m1));
+                hi[2 * b + j] = pack_h2(fmaf(d2, byte_f(Hh, 2 * j, 8388608.0f), -m2),
+                                        fmaf(d2, byte_f(Hh, 2 * j + 1, 8388608.0f), -m2));
             }
         }
         st_shared_v4(row + c * 2048, lo[0], lo[1], lo[2], lo[3]);
@@ -318,46 +328,40 @@ __global__ void __launch_bounds__(GM_THREADS, 2) k_gemm_gate_up(
     if (warp == 0) tmem_dealloc(tmem, 128);
 }
 
-// Q6_K half block h of super-block `blk` (2-byte aligned) -> quarters
-// q = 2p, 2p+1 (64 elements) of row m of a canonical 128-row tile at `A`
-// (LBO 2048): w = d * sc * q6 in fp32, rounded to fp16 once.
-__device__ __forceinline__ void deq_q6k_part(const uint32_t (&lo)[8], const uint32_t (&hi)[8],
-                                             const uint32_t (&qh)[8], const uint32_t (&sc)[2],
-                                             float d, int p, uint8_t *A, int m) {
+// Quarter q (32 elements, l = 0..31) of a Q6_K half block -> row m of a
+// canonical 128-row tile at `A` (LBO 2048): w = d * sc * (q6 - 32) in fp32,
+// rounded to fp16 once.  src: the 8 ql words of the quarter (low half of the
+// half block for even q, high for odd), qh: the half's 8 qh words.
+__device__ __forceinline__ void deq_q6k_quarter(const uint32_t (&src)[8], const uint32_t (&qh)[8],
+                                                const uint32_t (&sc)[2], float d, int q, uint8_t *A,
+                                                int m) {
     uint8_t *row = A + (m >> 3) * 128 + (m & 7) * 16;
+    const int ns = 4 * (q >> 1), hs = 2 * q;
 #pragma unroll
-    for (int qq = 0; qq < 2; ++qq) {
-        const int q = 2 * p + qq;                      // quarter: elements 32q + l
-        const uint32_t(&src)[8] = qq ? hi : lo;
+    for (int c = 0; c < 4; ++c) {                      // l = 8c .. 8c+7
+        const int g = (c >> 1) + 2 * q;                // scale byte (l / 16) + 2q
+        const float ws = d * (float)(int8_t)((sc[g >> 2] >> (8 * (g & 3))) & 0xFFu);
+        uint32_t o[4];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {                  // l = 8c .. 8c+7
-            const int g = (c >> 1) + 2 * q;            // scale byte (l / 16) + 2q
-            const float ws = d * (float)(int8_t)((sc[g >> 2] >> (8 * (g & 3))) & 0xFFu);
-            uint32_t o[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                float v2[2];
-#pragma unroll
-                for (int t = 0; t < 2; ++t) {
-                    const int l = 8 * c + 2 * j + t;
-                    const uint32_t nib = (src[l >> 2] >> (8 * (l & 3) + 4 * p)) & 15u;
-                    const uint32_t hb = (qh[l >> 2] >> (8 * (l & 3) + 2 * q)) & 3u;
-                    v2[t] = ws * (u2f(nib | (hb << 4)) - 32.0f);
-                }
-                o[j] = pack_h2(v2[0], v2[1]);
-            }
-            st_shared_v4(row + (4 * q + c) * 2048, o[0], o[1], o[2], o[3]);
+        for (int wi = 0; wi < 2; ++wi) {
+            const int i = 2 * c + wi;
+            const uint32_t v6 = ((src[i] >> ns) & 0x0F0F0F0Fu) | (((qh[i] >> hs) & 0x03030303u) << 4);
+            o[2 * wi] = pack_h2(ws * byte_f(v6, 0, 8388640.0f), ws * byte_f(v6, 1, 8388640.0f));
+            o[2 * wi + 1] = pack_h2(ws * byte_f(v6, 2, 8388640.0f), ws * byte_f(v6, 3, 8388640.0f));
         }
+        st_shared_v4(row + (4 * q + c) * 2048, o[0], o[1], o[2], o[3]);
     }
 }
 
-// Shared memory of k_gemm_down: A[2][128 x 128 fp16] (32 KB each),
-// B[3][64 x 128 fp16] (16 KB each), barriers, TMEM address.
+// Shared memory of k_gemm_down: the CTA's 128 Q6_K rows (one bulk copy, the
+// rows being contiguous), A[2][128 x 128 fp16] (32 KB each), B[3][64 x 128
+// fp16] (16 KB each), barriers, TMEM address.
 #define DN_A_BYTES (GM_ROWS * GM_KS_DN * 2)
 #define DN_B_BYTES (GM_NT * GM_KS_DN * 2)
-#define DN_SMEM (2 * DN_A_BYTES + 3 * DN_B_BYTES + 128)
+static inline int dn_rows_bytes(int n_ff) { return ((GM_ROWS * (n_ff / MOE_QK) * MOE_Q6K_BYTES) + 127) & ~127; }
+static inline int dn_smem(int n_ff) { return dn_rows_bytes(n_ff) + 2 * DN_A_BYTES + 3 * DN_B_BYTES + 128; }
 
-__global__ void __launch_bounds__(GM_THREADS, 2) k_gemm_down(
+__global__ void __launch_bounds__(DN_THREADS, 1) k_gemm_down(
     ExpertSrc src, const __half *__restrict__ at, const int32_t *__restrict__ off,
     const int32_t *__restrict__ cnt, const int32_t *__restrict__ tiles,
     const int32_t *__restrict__ n_tiles, int n_embd, int n_ff, float *__restrict__ ypair,
@@ -365,11 +369,15 @@ __global__ void __launch_bounds__(GM_THREADS, 2) k_gemm_down(
     extern __shared__ __align__(1024) uint8_t sm[];
     const int i = blockIdx.y;
     if (i >= *n_tiles) return;
+    const size_t rb = (size_t)(n_ff / MOE_QK) * MOE_Q6K_BYTES;   // bytes per row
+    const int rows_bytes = (GM_ROWS * (int)rb + 127) & ~127;
     uint8_t *sA = sm;                                   // [2] 32 KB
     uint8_t *sB = sm + 2 * DN_A_BYTES;                  // [3] 16 KB
-    uint64_t *mma_done = reinterpret_cast<uint64_t *>(sB + 3 * DN_B_BYTES);   // [2]
+    uint8_t *sR = sB + 3 * DN_B_BYTES;                  // the CTA's rows
+    uint64_t *mma_done = reinterpret_cast<uint64_t *>(sR + rows_bytes);       // [2]
     uint64_t *b_full = mma_done + 2;                                           // [3]
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(b_full + 3);
+    uint64_t *r_full = b_full + 3;                                             // [1]
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(r_full + 1);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int tl = tiles[i], e = tl >> 16, tt = tl & 0xFFFF;
     const int pos0 = off[e] + tt * GM_NT;
@@ -385,6 +393,7 @@ __global__ void __launch_bounds__(GM_THREADS, 2) k_gemm_down(
     if (tid == 0) {
         for (int q = 0; q < 2; ++q) mbar_init(&mma_done[q], 1);
         for (int q = 0; q < 3; ++q) mbar_init(&b_full[q], 1);
+        mbar_init(r_full, 1);
         fence_mbar_init();
     }
     if (warp == 0) tmem_alloc(tslot, 64);
@@ -397,17 +406,31 @@ __global__ void __launch_bounds__(GM_THREADS, 2) k_gemm_down(
         mbar_arrive_expect_tx(&b_full[0], DN_B_BYTES);
         bulk_g2s(sB, atile, DN_B_BYTES, &b_full[0]);
     }
-    const int p = tid >> 7, m = tid & 127;
-    const size_t rb = (size_t)(n_ff / MOE_QK) * MOE_Q6K_BYTES;
-    const uint8_t *row = dbase + (size_t)(r0 + m) * rb;
+    const int qtr = tid >> 7, m = tid & 127;
+    // the CTA's 128 rows are contiguous: one bulk copy from device memory;
+    // an expert in host memory (a miss) is copied by the threads
+    const uint8_t *rows_g = dbase + (size_t)r0 * rb;
+    const bool dev = expert_on_device(src, e);
+    if (dev) {
+        if (tid == 0) {
+            fence_proxy_async();
+            mbar_arrive_expect_tx(r_full, (uint32_t)(GM_ROWS * rb));
+            bulk_g2s(sR, rows_g, (uint32_t)(GM_ROWS * rb), r_full);
+        }
+    } else {
+        for (int o = tid * 16; o < GM_ROWS * (int)rb; o += DN_THREADS * 16)
+            *reinterpret_cast<uint4 *>(sR + o) = *reinterpret_cast<const uint4 *>(rows_g + o);
+        __syncthreads();
+    }
+    const uint8_t *row = sR + (size_t)m * rb;
     const uint32_t idesc = idesc_f16(GM_ROWS, N);
     bool ok = true;
+    if (dev && !mbar_wait(r_full, 0)) ok = false;
     for (int s = 0; s < S; ++s) {
         const uint8_t *blk = row + (s >> 1) * MOE_Q6K_BYTES;
         const int h = s & 1;
-        uint32_t lo[8], hi[8], qh[8], sc[2];
-        ldw_a2<8>(blk + 64 * h, lo);
-        ldw_a2<8>(blk + 64 * h + 32, hi);
+        uint32_t src[8], qh[8], sc[2];
+        ldw_a2<8>(blk + 64 * h + 32 * (qtr & 1), src);
         ldw_a2<8>(blk + 128 + 32 * h, qh);
         ldw_a2<2>(blk + 192 + 8 * h, sc);
         const float d = h2f(*reinterpret_cast<const uint16_t *>(blk + 208));
@@ -419,7 +442,7 @@ __global__ void __launch_bounds__(GM_THREADS, 2) k_gemm_down(
             bulk_g2s(sB + nb * DN_B_BYTES, atile + (size_t)(s + 1) * GM_NT * GM_KS_DN, DN_B_BYTES,
                      &b_full[nb]);
         }
-        deq_q6k_part(lo, hi, qh, sc, d, p, sA + b * DN_A_BYTES, m);
+        deq_q6k_quarter(src, qh, sc, d, qtr, sA + b * DN_A_BYTES, m);
         fence_proxy_async();
         __syncthreads();
         if (tid == 0) {
@@ -470,7 +493,8 @@ cudaError_t launch_experts_gemm(const ExpertSrc &src, const float *x, const Grou
                                 const float *w, void *scratch_v, float *ypair, const float *resid,
                                 float *y, int *err, cudaStream_t s) {
     __half *scratch = static_cast<__half *>(scratch_v);
-    if (down_type != MOE_QT_Q6K || n_ff % GM_KS_DN || n_embd % GM_ROWS || n_ff % GM_ROWS)
+    if (down_type != MOE_QT_Q6K || n_ff % GM_KS_DN || n_embd % GM_ROWS || n_ff % GM_ROWS ||
+        dn_smem(n_ff) > 227 * 1024)
         return cudaErrorInvalidValue;
     const int P = n_tok * k;
     const int maxt = group_max_tiles(src.n_expert + 1, P, GM_NT);
@@ -483,12 +507,12 @@ cudaError_t launch_experts_gemm(const ExpertSrc &src, const float *x, const Grou
                                   GU_SMEM)) != cudaSuccess)
         return e;
     if ((e = cudaFuncSetAttribute(k_gemm_down, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  DN_SMEM)) != cudaSuccess)
+                                  dn_smem(n_ff))) != cudaSuccess)
         return e;
     k_gemm_gate_up<<<dim3(n_ff / GM_ROWS, maxt), GM_THREADS, GU_SMEM, s>>>(
         src, xt, g.off, g.cnt, g.tiles, g.n_tiles, n_embd, n_ff, at, err);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    k_gemm_down<<<dim3(n_embd / GM_ROWS, maxt), GM_THREADS, DN_SMEM, s>>>(
+    k_gemm_down<<<dim3(n_embd / GM_ROWS, maxt), DN_THREADS, dn_smem(n_ff), s>>>(
         src, at, g.off, g.cnt, g.tiles, g.n_tiles, n_embd, n_ff, ypair, err);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     return launch_combine(ypair, g.pair_pos, w, n_tok, k, n_embd, resid, y, s);
