@@ -740,11 +740,13 @@ __device__ __forceinline__ float q6k_unit_dot(const uint8_t *blk, int h, int j, 
 
 // n consecutive 32-bit words starting at a 2-byte-aligned address, read as
 // aligned words and realigned with funnel shifts; reads only words that hold
-// requested bytes.
+// requested bytes.  The aligned pointer is ptr minus the misalignment (not a
+// masked integer), so that the compiler still sees a shared-memory pointer
+// as one and emits shared loads.
 template <int N>
 __device__ __forceinline__ void ldw_a2(const uint8_t *ptr, uint32_t (&w)[N]) {
     const uintptr_t a = reinterpret_cast<uintptr_t>(ptr);
-    const uint32_t *p = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
+    const uint32_t *p = reinterpret_cast<const uint32_t *>(ptr - (a & 3));
     const uint32_t sh = (uint32_t)(a & 2) * 8u;
     uint32_t raw[N + 1];
 #pragma unroll
