@@ -22,7 +22,8 @@
 //   4. gate/up GEMV (Q4_K x Q8_1, dp4a) with SiLU*mul as pieces land;
 //      activations to L2;
 //   5. the CTA signals every rank it produced (release); warp 15 prefetches
-//      the previous token's experts of the next layer into L2;
+//      the gate/up matrices of the previous token's experts of the next layer
+//      into L2;
 //   6. per rank, a group of warps waits for that rank's producers, quantises
 //      its activations (Q8_1, padded shared-memory layout) and computes the
 //      down GEMV rows (Q6_K x Q8_1) of this CTA's residual rows; then the
@@ -216,29 +217,29 @@ __device__ __forceinline__ void add_router_partials(long long *A, const float *w
     }
 }
 
-// The previous token's experts of the next step's layer into L2, while HBM
-// has nothing else to do until the next selection: one bulk prefetch per
-// (expert, matrix) slice of this CTA (1/G of each matrix), one lane each.
-// The next step's loads of the experts routed again then come from L2.
+// The gate and up matrices of the previous token's experts of the next
+// step's layer into L2, while the down rows of this step stream in: one bulk
+// prefetch per (expert, matrix) slice of this CTA (1/G of each matrix), one
+// lane each.  The next step's gate/up loads of the experts routed again then
+// come from L2.  Measured and not done: prefetching the down matrices too,
+// and warming with real copies into the free gate/up buffer (both slowed
+// this step's down rows by more than they saved on the next).
 // Resident experts only (a miss lives in host memory); pred: ids by rank,
 // -1 unknown; the shared expert (rank K when kx > k) always.
 __device__ __forceinline__ void prefetch_next_l2(const LayerDesc &ldn, const int32_t *pred,
                                                  const int32_t *tbl, int K, int KX, int E,
-                                                 int64_t gate_bytes, int64_t down_bytes, int c,
-                                                 int G, int lane) {
-    for (int item = lane; item < 3 * KX; item += 32) {
-        const int r = item / 3, m = item - 3 * r;
+                                                 int64_t gate_bytes, int c, int G, int lane) {
+    for (int item = lane; item < 2 * KX; item += 32) {
+        const int r = item >> 1, m = item & 1;
         const int id = r < K ? pred[r] : E;
         if (id < 0 || id > E) continue;
         const int slot = id == E ? -1 : tbl[id];
         if (slot == ldn.ns || slot < -1) continue;
-        const int64_t B = m < 2 ? gate_bytes : down_bytes;
         const uint8_t *base = m == 0 ? (slot < 0 ? ldn.sgate : ldn.gate + (size_t)slot * gate_bytes)
-                            : m == 1 ? (slot < 0 ? ldn.sup : ldn.up + (size_t)slot * gate_bytes)
-                                     : (slot < 0 ? ldn.sdown : ldn.down + (size_t)slot * down_bytes);
+                                     : (slot < 0 ? ldn.sup : ldn.up + (size_t)slot * gate_bytes);
         if (!base) continue;
-        const int64_t o0 = ((int64_t)c * B / G) & ~int64_t(15);
-        const int64_t o1 = c + 1 == G ? B : (((int64_t)(c + 1) * B / G) & ~int64_t(15));
+        const int64_t o0 = ((int64_t)c * gate_bytes / G) & ~int64_t(15);
+        const int64_t o1 = c + 1 == G ? gate_bytes : (((int64_t)(c + 1) * gate_bytes / G) & ~int64_t(15));
         if (o1 > o0) prefetch_l2(base + o0, (uint32_t)(o1 - o0));
     }
 }
@@ -379,7 +380,8 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                 if (warp == 0) {
                     int id_r;
                     float w_r;
-                    select_warp<E / 32>(tot, inv, tbl, ld.ns, p.delta, p.delta > 0.0f, K, lane, id_r, w_r);
+                    select_warp<E / 32>(tot, inv, tbl, ld.ns, p.delta, p.delta > 0.0f, K, lane, id_r, w_r,
+                                        s_ids, s_w);
                     if (lane < K) {
                         const bool okid = id_r >= 0 && id_r < E;
                         s_ids[lane] = id_r;
@@ -545,14 +547,14 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                 for (int q = 0; q < nch; ++q) red_release_add(p.ready + ch_k[q] * READY_STRIDE, 1u);
             PROF(9)
             pend_gu = false;
-            // warp 15 puts the previous token's experts of the next step's layer
-            // into L2 (HBM has nothing else to do until the next selection)
+            // warp 15 puts the gate/up matrices of the previous token's experts
+            // of the next step's layer into L2
             if (warp == DEC_WARPS - 1 && (L + 1 < NL || t + 1 < p.n_tok)) {
                 // the next layer's table was queued with this layer's copies
                 const int nl = L + 1 < NL ? L + 1 : 0;
                 if (mbar_wait(&mb[MB_TBL], tbl_par))
                     prefetch_next_l2(p.layers[nl], prev + (size_t)nl * MOE_KMAX, tbl, K, KX, E,
-                                     p.gate_bytes, p.down_bytes, c, G, lane);
+                                     p.gate_bytes, c, G, lane);
             }
 
             // ---- 5/6. per rank k, a group of one or two warps: wait until every CTA

@@ -241,17 +241,39 @@ __device__ __forceinline__ long long fx_sumsq(float v) {
     return __float2ll_rn(__fmul_rn(fminf(v, 68719476736.0f), FX_SUMSQ_SCALE));
 }
 
-// The whole selection of one token in one warp, in registers: the logits
-// tot[e] * inv, the softmax and cache prior of router_softmax_warp, top-k as k rounds of
-// arg-max over the keys (selection bits << 32 | ~id: the total order of
-// topk_key_block), and the weights p / sum(p) with the sum formed in rank
-// order.  The same operations in the same order as those three steps, so
-// the same bits.  Lane r < k returns rank r's id and weight.  M experts per
-// lane (n_expert = 32 * M).
+// Compare-exchange of two (key high, key low, p) entries so that entry i holds
+// the larger key: the sorting step of select_warp.
+__device__ __forceinline__ void sel_cx(uint32_t &hi_a, uint32_t &lo_a, float &p_a, uint32_t &hi_b,
+                                       uint32_t &lo_b, float &p_b) {
+    const bool sw = hi_b > hi_a || (hi_b == hi_a && lo_b > lo_a);
+    const uint32_t th = sw ? hi_b : hi_a, tl = sw ? lo_b : lo_a;
+    const float tp = sw ? p_b : p_a;
+    hi_b = sw ? hi_a : hi_b;
+    lo_b = sw ? lo_a : lo_b;
+    p_b = sw ? p_a : p_b;
+    hi_a = th;
+    lo_a = tl;
+    p_a = tp;
+}
+
+// The whole selection of one token in one warp: the logits tot[e] * inv, the
+// softmax and cache prior of router_softmax_warp, top-k in the total order of
+// topk_key_block (selection bits, then ~id), and the weights p / sum(p) with
+// the sum formed in rank order.  The same operations in the same order as
+// those three steps, so the same bits.
+//
+// Top-k: every lane sorts its M keys once (descending); each round then
+// takes the largest list head in the warp with two reductions (high word,
+// then low word among the lanes holding that high word), and the lane that
+// holds it pops its head.  Ids are unique, so exactly one lane wins a round.
+// The winner writes rank r's id and p to s_id[r] / s_p[r] (shared, MOE_KMAX
+// each).  Lane r < k returns rank r's id and weight.  M experts per lane
+// (n_expert = 32 * M), M = 1, 2, 4 or 8.
 template <int M>
 __device__ __forceinline__ void select_warp(const float *tot, float inv, const int32_t *table,
                                             int ns, float delta, bool use_prior, int k, int lane,
-                                            int &id_r, float &w_r) {
+                                            int &id_r, float &w_r, int32_t *s_id, float *s_p) {
+    static_assert(M == 1 || M == 2 || M == 4 || M == 8, "select_warp: 32 to 256 experts");
     float lg[M], ex[M], pr[M];
     uint32_t kh[M], kl[M];
 #pragma unroll
@@ -259,8 +281,13 @@ __device__ __forceinline__ void select_warp(const float *tot, float inv, const i
     float mx = lg[0];
 #pragma unroll
     for (int i = 1; i < M; ++i) mx = fmaxf(mx, lg[i]);
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(MOE_FULL, mx, off));
+    // warp max through a signed integer image that orders like the floats
+    // (negative values: low 31 bits flipped); the max of the values, as the
+    // fmaxf butterfly gives it (a max of +-0 subtracts to the same exponent)
+    int oi = __float_as_int(mx);
+    oi = oi >= 0 ? oi : oi ^ 0x7FFFFFFF;
+    oi = __reduce_max_sync(MOE_FULL, oi);
+    mx = __int_as_float(oi >= 0 ? oi : oi ^ 0x7FFFFFFF);
     float s = 0.0f;
 #pragma unroll
     for (int i = 0; i < M; ++i) {
@@ -278,38 +305,55 @@ __device__ __forceinline__ void select_warp(const float *tot, float inv, const i
         kh[i] = __float_as_uint(sv);
         kl[i] = ~(uint32_t)e;
     }
-    uint32_t taken = 0;
-    float ws = 0.0f, my_p = 0.0f;
-    int my_id = -1;
-    for (int r = 0; r < k; ++r) {
-        // this lane's best untaken key; (0, 0) is below every real key (~id > 0)
-        uint32_t bh = 0, bl = 0;
+    // sort the lane's M entries, largest first (Batcher's odd-even merge sort)
+    if (M == 2) {
+        sel_cx(kh[0], kl[0], pr[0], kh[1], kl[1], pr[1]);
+    } else if (M == 4) {
+        sel_cx(kh[0], kl[0], pr[0], kh[1], kl[1], pr[1]);
+        sel_cx(kh[2], kl[2], pr[2], kh[3], kl[3], pr[3]);
+        sel_cx(kh[0], kl[0], pr[0], kh[2], kl[2], pr[2]);
+        sel_cx(kh[1], kl[1], pr[1], kh[3], kl[3], pr[3]);
+        sel_cx(kh[1], kl[1], pr[1], kh[2], kl[2], pr[2]);
+    } else if (M == 8) {
 #pragma unroll
-        for (int i = 0; i < M; ++i) {
-            const bool better = kh[i] > bh || (kh[i] == bh && kl[i] > bl);
-            if (!((taken >> i) & 1u) && better) {
-                bh = kh[i];
-                bl = kl[i];
-            }
+        for (int i = 0; i < 8; i += 2) sel_cx(kh[i], kl[i], pr[i], kh[i + 1], kl[i + 1], pr[i + 1]);
+#pragma unroll
+        for (int i = 0; i < 8; i += 4) {
+            sel_cx(kh[i], kl[i], pr[i], kh[i + 2], kl[i + 2], pr[i + 2]);
+            sel_cx(kh[i + 1], kl[i + 1], pr[i + 1], kh[i + 3], kl[i + 3], pr[i + 3]);
+            sel_cx(kh[i + 1], kl[i + 1], pr[i + 1], kh[i + 2], kl[i + 2], pr[i + 2]);
         }
-        const uint32_t mh = __reduce_max_sync(MOE_FULL, bh);
-        const uint32_t ml = __reduce_max_sync(MOE_FULL, bh == mh ? bl : 0u);
-        const int e = (int)(~ml);
-        const int owner = e & 31, idx = e >> 5;
-        float pv = 0.0f;
 #pragma unroll
-        for (int i = 0; i < M; ++i)
-            if (i == idx) pv = pr[i];
-        if (lane == owner) taken |= 1u << idx;
-        const float pw = __shfl_sync(MOE_FULL, pv, owner);
-        ws = r == 0 ? pw : __fadd_rn(ws, pw);
-        if (lane == r) {
-            my_id = e;
-            my_p = pw;
+        for (int i = 0; i < 4; ++i) sel_cx(kh[i], kl[i], pr[i], kh[i + 4], kl[i + 4], pr[i + 4]);
+        sel_cx(kh[2], kl[2], pr[2], kh[4], kl[4], pr[4]);
+        sel_cx(kh[3], kl[3], pr[3], kh[5], kl[5], pr[5]);
+        sel_cx(kh[1], kl[1], pr[1], kh[2], kl[2], pr[2]);
+        sel_cx(kh[3], kl[3], pr[3], kh[4], kl[4], pr[4]);
+        sel_cx(kh[5], kl[5], pr[5], kh[6], kl[6], pr[6]);
+    }
+    // (0, 0) is below every real key (~id > 0): an exhausted list never wins
+    for (int r = 0; r < k; ++r) {
+        const uint32_t mh = __reduce_max_sync(MOE_FULL, kh[0]);
+        const uint32_t ml = __reduce_max_sync(MOE_FULL, kh[0] == mh ? kl[0] : 0u);
+        if (kh[0] == mh && kl[0] == ml) {
+            s_id[r] = (int32_t)(~ml);
+            s_p[r] = pr[0];
+#pragma unroll
+            for (int i = 0; i + 1 < M; ++i) {
+                kh[i] = kh[i + 1];
+                kl[i] = kl[i + 1];
+                pr[i] = pr[i + 1];
+            }
+            kh[M - 1] = 0u;
+            kl[M - 1] = 0u;
         }
     }
-    id_r = my_id;
-    w_r = lane < k ? __fdiv_rn(my_p, ws) : 0.0f;
+    __syncwarp();
+    float ws = s_p[0];
+    for (int r = 1; r < k; ++r) ws = __fadd_rn(ws, s_p[r]);
+    id_r = lane < k ? s_id[lane] : -1;
+    w_r = lane < k ? __fdiv_rn(s_p[lane], ws) : 0.0f;
+    __syncwarp();
 }
 
 // Top-k by rank, all threads of the CTA: rank(e) = #experts before e in the
