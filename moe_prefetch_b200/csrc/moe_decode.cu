@@ -521,18 +521,13 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                             uB = q4k_unit_dot(up_sm + (size_t)lB * gurow + so, pp, a);
                         }
                     }
-#pragma unroll
-                    for (int off = 16; off >= 1; off >>= 1) {
-                        gA += __shfl_xor_sync(MOE_FULL, gA, off);
-                        uA += __shfl_xor_sync(MOE_FULL, uA, off);
-                        gB += __shfl_xor_sync(MOE_FULL, gB, off);
-                        uB += __shfl_xor_sync(MOE_FULL, uB, off);
-                    }
-                    if (lane == 0) {
-                        __stcg(p.act + (size_t)ch_k[qA] * I + ch_i0[qA] + (lA - ch_off[qA]), silu_mul(gA, uA));
-                        if (hasB)
-                            __stcg(p.act + (size_t)ch_k[qB] * I + ch_i0[qB] + (lB - ch_off[qB]), silu_mul(gB, uB));
-                    }
+                    // lanes 0-7: gate A, 8-15: up A, 16-23: gate B, 24-31: up B
+                    const float sum = warp_sum4_t(gA, uA, gB, uB, lane);
+                    const float up = __shfl_down_sync(MOE_FULL, sum, 8);
+                    if (lane == 0)
+                        __stcg(p.act + (size_t)ch_k[qA] * I + ch_i0[qA] + (lA - ch_off[qA]), silu_mul(sum, up));
+                    if (lane == 16 && hasB)
+                        __stcg(p.act + (size_t)ch_k[qB] * I + ch_i0[qB] + (lB - ch_off[qB]), silu_mul(sum, up));
                 }
                 if (fail && lane == 0) { atomicOr(p.err, MOE_DEV_ERR_TIMEOUT); atomicExch(p.abort_flag, 1); }
             }

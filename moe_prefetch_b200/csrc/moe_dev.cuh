@@ -624,6 +624,13 @@ __device__ __forceinline__ void load_act_q4_unit(ActQ4 &a, const int8_t *qu, con
 
 __device__ __forceinline__ int byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xFF; }
 
+// 4-way byte dot: unsigned bytes of a times signed bytes of b, plus c.
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+    int r;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+
 // 6-bit scale and min of sub-block j from the 12 scale bytes held in
 // (w0: bytes 0-3, w1: 4-7, w2: 8-11)  (upstream get_scale_min_k4).
 __device__ __forceinline__ void q4k_sm(uint32_t w0, uint32_t w1, uint32_t w2, int j, int &sc,
@@ -639,6 +646,23 @@ __device__ __forceinline__ void q4k_sm(uint32_t w0, uint32_t w1, uint32_t w2, in
     }
 }
 
+// q4k_sm for the pair of sub-blocks 2p, 2p + 1 at once, the same integers:
+// the four 6-bit scales (mins) of one half of the 12 bytes are formed in one
+// word with byte-wise masks (j < 4: the low 6 bits of bytes j / j + 4;
+// j >= 4: the low / high nibble of byte j + 4 below the top two bits of
+// bytes j - 4 / j), then bytes 2(p & 1) and 2(p & 1) + 1 are picked.
+__device__ __forceinline__ void q4k_sm_pair(uint32_t w0, uint32_t w1, uint32_t w2, int p, int &sc0,
+                                            int &m0, int &sc1, int &m1) {
+    const bool upper = p >= 2;
+    const uint32_t S = upper ? ((w2 & 0x0F0F0F0Fu) | ((w0 >> 2) & 0x30303030u)) : (w0 & 0x3F3F3F3Fu);
+    const uint32_t M = upper ? (((w2 >> 4) & 0x0F0F0F0Fu) | ((w1 >> 2) & 0x30303030u)) : (w1 & 0x3F3F3F3Fu);
+    const uint32_t b = (uint32_t)(p & 1) * 2u;
+    sc0 = (int)__byte_perm(S, 0u, 0x4440u | b);
+    sc1 = (int)__byte_perm(S, 0u, 0x4440u | (b + 1u));
+    m0 = (int)__byte_perm(M, 0u, 0x4440u | b);
+    m1 = (int)__byte_perm(M, 0u, 0x4440u | (b + 1u));
+}
+
 // The bytes of one unit of a Q4_K row: the block header (d, dmin, scales)
 // and the 32 quant bytes of sub-block pair p.
 struct Q4Unit {
@@ -651,17 +675,19 @@ __device__ __forceinline__ void q4k_unit_load(const uint8_t *blk, int p, Q4Unit 
     w.q1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * p);
 }
 
+// The high nibbles are dotted in place (bytes 16 n, unsigned) and the sum,
+// a multiple of 16, shifted down: the same integer as dotting n.
 __device__ __forceinline__ float q4k_unit_compute(const Q4Unit &u, int p, const ActQ4 &a) {
     const uint32_t w[8] = {u.q0.x, u.q0.y, u.q0.z, u.q0.w, u.q1.x, u.q1.y, u.q1.z, u.q1.w};
-    int slo = 0, shi = 0;
+    int slo = 0, shi16 = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         slo = __dp4a((int)(w[i] & 0x0F0F0F0Fu), a.lo[i], slo);
-        shi = __dp4a((int)((w[i] >> 4) & 0x0F0F0F0Fu), a.hi[i], shi);
+        shi16 = dp4a_us(w[i] & 0xF0F0F0F0u, a.hi[i], shi16);
     }
+    const int shi = shi16 >> 4;
     int sc0, m0, sc1, m1;
-    q4k_sm(u.hdr.y, u.hdr.z, u.hdr.w, 2 * p, sc0, m0);
-    q4k_sm(u.hdr.y, u.hdr.z, u.hdr.w, 2 * p + 1, sc1, m1);
+    q4k_sm_pair(u.hdr.y, u.hdr.z, u.hdr.w, p, sc0, m0, sc1, m1);
     const float d = h2f(u.hdr.x), dmin = h2f(u.hdr.x >> 16);
     const float acc = (float)(sc0 * slo) * a.d0 + (float)(sc1 * shi) * a.d1;
     const float mm = (float)m0 * a.s0 + (float)m1 * a.s1;
@@ -683,8 +709,7 @@ __device__ __forceinline__ void q4k_unit_decode(const Q4Unit &u, int p, Q4UnitDe
         o.lo[i] = (int)(w[i] & 0x0F0F0F0Fu);
         o.hi[i] = (int)((w[i] >> 4) & 0x0F0F0F0Fu);
     }
-    q4k_sm(u.hdr.y, u.hdr.z, u.hdr.w, 2 * p, o.sc0, o.m0);
-    q4k_sm(u.hdr.y, u.hdr.z, u.hdr.w, 2 * p + 1, o.sc1, o.m1);
+    q4k_sm_pair(u.hdr.y, u.hdr.z, u.hdr.w, p, o.sc0, o.m0, o.sc1, o.m1);
     o.d = h2f(u.hdr.x);
     o.dmin = h2f(u.hdr.x >> 16);
 }
@@ -926,12 +951,6 @@ __device__ __forceinline__ float q6k_half_dot(const uint8_t *blk, int h, const A
     return q6k_half_compute(w, a);
 }
 
-// 4-way byte dot: unsigned bytes of a times signed bytes of b, plus c.
-__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
-    int r;
-    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
-    return r;
-}
 
 // ActHalf plus, per scale group g (16 values), c[g] = -32 * (sum of its q):
 // the start value of the group's integer sum in q6k_half_compute_u.
@@ -1042,6 +1061,24 @@ __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(MOE_FULL, v, off);
     return v;
+}
+
+// Four warp_sum's at once, bit for bit: the same pairs at every level (xor
+// 16, 8, 4, 2, 1; own value first), but each level exchanges only the sums a
+// lane still needs.  Lanes 0-7 return the sum of a, 8-15 of b, 16-23 of c,
+// 24-31 of d.  7 shuffles instead of 20.
+__device__ __forceinline__ float warp_sum4_t(float a, float b, float c, float d, int lane) {
+    const bool u16 = (lane & 16) != 0;
+    float k0 = u16 ? c : a, k1 = u16 ? d : b;
+    k0 += __shfl_xor_sync(MOE_FULL, u16 ? a : c, 16);
+    k1 += __shfl_xor_sync(MOE_FULL, u16 ? b : d, 16);
+    const bool u8 = (lane & 8) != 0;
+    float k = u8 ? k1 : k0;
+    k += __shfl_xor_sync(MOE_FULL, u8 ? k0 : k1, 8);
+    k += __shfl_xor_sync(MOE_FULL, k, 4);
+    k += __shfl_xor_sync(MOE_FULL, k, 2);
+    k += __shfl_xor_sync(MOE_FULL, k, 1);
+    return k;
 }
 
 // ---------------------------------------------------------------------------

@@ -176,8 +176,7 @@ __global__ void __launch_bounds__(256) k_gather_x16(const float *__restrict__ x,
 __device__ __forceinline__ void deq_q4k_group(const uint4 &hdr, const uint4 &q0, const uint4 &q1,
                                               int g, uint8_t *A, int m) {
     int sc0, mn0, sc1, mn1;
-    q4k_sm(hdr.y, hdr.z, hdr.w, 2 * g, sc0, mn0);
-    q4k_sm(hdr.y, hdr.z, hdr.w, 2 * g + 1, sc1, mn1);
+    q4k_sm_pair(hdr.y, hdr.z, hdr.w, g, sc0, mn0, sc1, mn1);
     const float d = h2f(hdr.x & 0xFFFFu), dmin = h2f(hdr.x >> 16);
     const float d1 = d * (float)sc0, m1 = dmin * (float)mn0;
     const float d2 = d * (float)sc1, m2 = dmin * (float)mn1;
