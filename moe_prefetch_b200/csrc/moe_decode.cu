@@ -590,8 +590,12 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                 if (nw > 1) asm volatile("bar.sync %0, %1;" ::"r"(1 + kk), "r"(gthreads) : "memory");
                 else __syncwarp();
                 if (rows > 0) {
-                    const int grp = lane >> 3, u = lane & 7;   // row in the group, unit
-                    const int nrg = Q6_T ? (rows + 3) >> 2 : rows;
+                    // Q6_K: a row is gs half-block units on consecutive lanes, 32 / gs
+                    // rows per warp pass (5 with n_ff = 768)
+                    const int gs = Q6_T ? (I / MOE_QK) * 2 : 8;
+                    const int rpi = 32 / gs;
+                    const int rr = lane / gs, u = lane - rr * gs;   // row in the pass, unit
+                    const int nrg = Q6_T ? (rows + rpi - 1) / rpi : rows;
                     const int sl = s_slot[kk];
                     const uint8_t *base = sl < 0 ? ld.sdown
                         : sl != ld.ns ? ld.down + (size_t)sl * p.down_bytes
@@ -602,10 +606,9 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                     if (!dn_ok && lane == 0) { atomicOr(p.err, MOE_DEV_ERR_TIMEOUT); atomicExch(p.abort_flag, 1); s_fail = 1; }
                     for (int rg = gw; rg < nrg && dn_ok; rg += nw) {
                         if constexpr (Q6_T) {
-                            const int nunits = (I / MOE_QK) * 2;           // half blocks per row
-                            const bool on = u < nunits;
+                            const bool on = rr < rpi;
                             const int sb = u >> 1, hh = u & 1;
-                            const int i = rg * 4 + grp;
+                            const int i = rg * rpi + rr;
                             ActHalfU a;
                             float v = 0.0f;
                             if (on) {
@@ -614,8 +617,8 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                                 if (i < rows)
                                     v = q6k_half_dot_u(rws + (size_t)i * drow + sb * MOE_Q6K_BYTES, hh, a);
                             }
-                            v = group8_sum(v);
-                            if (u == 0 && i < rows) ys[kk * p.dn_rows_max + i] = v;
+                            v = groupn_sum(v, u, gs);
+                            if (on && u == 0 && i < rows) ys[kk * p.dn_rows_max + i] = v;
                         } else {
                             const int units = (I / MOE_QK) * 4;
                             const bool on = lane < units;

@@ -1038,6 +1038,19 @@ __device__ __forceinline__ float group8_sum(float v) {
     return v;
 }
 
+// group8_sum's value for a group of gs = 2, 4, 6 or 8 consecutive lanes
+// (unit u = 0 .. gs - 1) where group8_sum's lanes gs .. 7 would hold +0: the
+// same tree ((v0 + v1) + (v2 + v3)) + ((v4 + v5) + (v6 + v7)), each absent
+// pair taken as +0.  The result is valid in the group's lane u = 0, so that
+// groups need not be aligned to 8 lanes.
+__device__ __forceinline__ float groupn_sum(float v, int u, int gs) {
+    const float a = v + __shfl_down_sync(MOE_FULL, v, 1);
+    const float t2 = __shfl_down_sync(MOE_FULL, a, 2);
+    const float b = a + (u + 2 < gs ? t2 : 0.0f);
+    const float t4 = __shfl_down_sync(MOE_FULL, b, 4);
+    return b + (u + 4 < gs ? t4 : 0.0f);
+}
+
 // Top-k by rank over 64-bit keys (selection bits << 32 | ~id: larger is
 // better, ties to the lower id), thread (e, part) comparing against experts
 // part, part + parts, ...; the same total order as topk_rank_block.
