@@ -38,14 +38,28 @@ __global__ void __launch_bounds__(GROUP_THREADS) k_group(const int32_t *__restri
                                                          int32_t *pos_pair, int32_t *tiles,
                                                          int32_t *n_tiles, int *err) {
     __shared__ int s_cnt[GROUP_MAX_BUCKETS], s_off[GROUP_MAX_BUCKETS + 1], s_base[GROUP_MAX_BUCKETS];
+    // per warp and bucket: the warp's count in the chunk (low 16 bits), after
+    // the scan the exclusive prefix over the chunk's warps (high 16 bits)
     __shared__ int s_wc[GROUP_THREADS / 32][GROUP_MAX_BUCKETS];
+    __shared__ int s_bold[GROUP_MAX_BUCKETS];   // a bucket's base before the chunk
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     for (int e = tid; e < n_expert; e += GROUP_THREADS) { s_cnt[e] = 0; s_base[e] = 0; }
+    for (int i = tid; i < (GROUP_THREADS / 32) * GROUP_MAX_BUCKETS; i += GROUP_THREADS)
+        (&s_wc[0][0])[i] = 0;
     __syncthreads();
-    for (int p = tid; p < P; p += GROUP_THREADS) {
-        const int e = ids[p];
-        if (e >= 0 && e < n_expert) atomicAdd(&s_cnt[e], 1);
-        else if (e >= 0 || e < -1) atomicOr(err, MOE_DEV_ERR_INDEX);   // -1: an empty slot, skipped
+    for (int p0 = tid; p0 < P; p0 += 8 * GROUP_THREADS) {   // 8 loads in flight per thread
+        int ev[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int p = p0 + j * GROUP_THREADS;
+            ev[j] = p < P ? ids[p] : -1;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int e = ev[j];
+            if (e >= 0 && e < n_expert) atomicAdd(&s_cnt[e], 1);
+            else if (e >= 0 || e < -1) atomicOr(err, MOE_DEV_ERR_INDEX);   // -1: an empty slot, skipped
+        }
     }
     __syncthreads();
     if (warp == 0) {
@@ -83,32 +97,35 @@ __global__ void __launch_bounds__(GROUP_THREADS) k_group(const int32_t *__restri
         if (e < n_expert) cnt[e] = s_cnt[e];
     }
     const unsigned lt = (1u << lane) - 1u;
+    // chunks of GROUP_THREADS pairs: per-warp counts per bucket, then one
+    // thread per bucket turns them into the exclusive prefix over warps
+    // (counts cleared for the next chunk) and advances the bucket's base
     for (int c0 = 0; c0 < P; c0 += GROUP_THREADS) {
-        for (int i = tid; i < (GROUP_THREADS / 32) * n_expert; i += GROUP_THREADS)
-            s_wc[i / n_expert][i % n_expert] = 0;
-        __syncthreads();
         const int p = c0 + tid;
         int e = p < P ? ids[p] : -1;
         if (e >= n_expert) e = -1;
         const unsigned mask = __match_any_sync(MOE_FULL, e);
         if (e >= 0 && lane == __ffs(mask) - 1) s_wc[warp][e] = __popc(mask);
         __syncthreads();
+        for (int q = tid; q < n_expert; q += GROUP_THREADS) {
+            int rel = 0;
+#pragma unroll 8
+            for (int w = 0; w < GROUP_THREADS / 32; ++w) {
+                const int v = s_wc[w][q] & 0xFFFF;
+                s_wc[w][q] = rel << 16;
+                rel += v;
+            }
+            s_bold[q] = s_base[q];
+            s_base[q] += rel;
+        }
+        __syncthreads();
         if (e >= 0) {
-            int rank = s_base[e] + __popc(mask & lt);
-            for (int w = 0; w < warp; ++w) rank += s_wc[w][e];
-            const int pos = s_off[e] + rank;
+            const int pos = s_off[e] + s_bold[e] + (s_wc[warp][e] >> 16) + __popc(mask & lt);
             pair_pos[p] = pos;
             pos_pair[pos] = p;
         } else if (p < P) {
             pair_pos[p] = -1;
         }
-        __syncthreads();
-        for (int q = tid; q < n_expert; q += GROUP_THREADS) {
-            int sum = 0;
-            for (int w = 0; w < GROUP_THREADS / 32; ++w) sum += s_wc[w][q];
-            s_base[q] += sum;
-        }
-        __syncthreads();
     }
 }
 
@@ -122,9 +139,22 @@ __global__ void __launch_bounds__(256) k_quant_rows(const float *__restrict__ x,
                                                     float *__restrict__ xs) {
     const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int nblk = n_embd / 32;
-    for (int b = warp; b < nblk; b += nw)
-        q8_block_warp(x[(size_t)t * n_embd + 32 * b + lane], lane, xq + (size_t)t * n_embd + 32 * b,
-                      xd + (size_t)t * nblk + b, xs + (size_t)t * nblk + b);
+    // up to 8 blocks per warp: every load issued before the first block's arithmetic
+    for (int b0 = warp; b0 < nblk; b0 += 8 * nw) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int b = b0 + j * nw;
+            v[j] = b < nblk ? x[(size_t)t * n_embd + 32 * b + lane] : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int b = b0 + j * nw;
+            if (b < nblk)
+                q8_block_warp(v[j], lane, xq + (size_t)t * n_embd + 32 * b, xd + (size_t)t * nblk + b,
+                              xs + (size_t)t * nblk + b);
+        }
+    }
 }
 
 // Sum of each of 16 values over the 32 lanes, with every lane pair (l, l ^ o)

@@ -141,7 +141,11 @@ __device__ __forceinline__ float byte_f(uint32_t x, int j, float bias) {
 // SBO = 128.  A token tile has R = GM_NT rows.
 
 // x [n_tok][n_embd] fp32 -> xt[tile][stage][k / 8][n][8] fp16 for every
-// tile of the grouping (rows past the tile's pairs are zero).
+// tile of the grouping (rows past the tile's pairs are zero).  grid (max
+// tiles, n_embd / GX_COLS): CTA (i, cb) writes columns [cb GX_COLS,
+// (cb + 1) GX_COLS) of tile i; the tile's token indices are read once into
+// shared memory, and each thread's chunks are loaded before any is stored.
+#define GX_COLS 256
 __global__ void __launch_bounds__(256) k_gather_x16(const float *__restrict__ x,
                                                     const int32_t *__restrict__ off,
                                                     const int32_t *__restrict__ cnt,
@@ -149,24 +153,36 @@ __global__ void __launch_bounds__(256) k_gather_x16(const float *__restrict__ x,
                                                     const int32_t *__restrict__ tiles,
                                                     const int32_t *__restrict__ n_tiles, int k,
                                                     int n_embd, __half *__restrict__ xt) {
+    __shared__ int s_tok[GM_NT];
     const int i = blockIdx.x;
     if (i >= *n_tiles) return;
     const int tl = tiles[i], e = tl >> 16, tt = tl & 0xFFFF;
     const int pos0 = off[e] + tt * GM_NT;
     const int np = min(GM_NT, cnt[e] - tt * GM_NT);
+    if (threadIdx.x < GM_NT) s_tok[threadIdx.x] = threadIdx.x < np ? pos_pair[pos0 + threadIdx.x] / k : -1;
+    __syncthreads();
     __half *dst = xt + (size_t)i * n_embd * GM_NT;
-    const int chunks = (n_embd / 8) * GM_NT;      // (stage, k/8, n) in that order
-    for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
-        const int n = c % GM_NT, kc = c / GM_NT;  // kc over the whole row: stage = kc / 8
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (n < np) {
-            const int t = pos_pair[pos0 + n] / k;
+    constexpr int PER = (GX_COLS / 8) * GM_NT / 256;   // chunks per thread
+    const int c0 = blockIdx.y * (GX_COLS / 8) * GM_NT;   // first chunk: (k/8, n) with k/8 = blockIdx.y * 32
+    float4 va[PER], vb[PER];
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        const int c = c0 + threadIdx.x + 256 * j;
+        const int n = c % GM_NT, kc = c / GM_NT;
+        const int t = s_tok[n];
+        va[j] = vb[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (t >= 0) {
             const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)t * n_embd + 8 * kc);
-            const float4 a = src[0], b = src[1];
-            v = make_uint4(pack_h2(a.x, a.y), pack_h2(a.z, a.w), pack_h2(b.x, b.y),
-                           pack_h2(b.z, b.w));
+            va[j] = src[0];
+            vb[j] = src[1];
         }
-        *reinterpret_cast<uint4 *>(dst + (size_t)c * 8) = v;
+    }
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        const int c = c0 + threadIdx.x + 256 * j;
+        *reinterpret_cast<uint4 *>(dst + (size_t)c * 8) =
+            make_uint4(pack_h2(va[j].x, va[j].y), pack_h2(va[j].z, va[j].w), pack_h2(vb[j].x, vb[j].y),
+                       pack_h2(vb[j].z, vb[j].w));
     }
 }
 
@@ -493,14 +509,15 @@ cudaError_t launch_experts_gemm(const ExpertSrc &src, const float *x, const Grou
                                 float *y, int *err, cudaStream_t s) {
     __half *scratch = static_cast<__half *>(scratch_v);
     if (down_type != MOE_QT_Q6K || n_ff % GM_KS_DN || n_embd % GM_ROWS || n_ff % GM_ROWS ||
-        dn_smem(n_ff) > 227 * 1024)
+        n_embd % GX_COLS || dn_smem(n_ff) > 227 * 1024)
         return cudaErrorInvalidValue;
     const int P = n_tok * k;
     const int maxt = group_max_tiles(src.n_expert + 1, P, GM_NT);
     __half *xt = scratch;
     __half *at = scratch + (size_t)maxt * GM_NT * n_embd;
     cudaError_t e;
-    k_gather_x16<<<maxt, 256, 0, s>>>(x, g.off, g.cnt, g.pos_pair, g.tiles, g.n_tiles, k, n_embd, xt);
+    k_gather_x16<<<dim3(maxt, n_embd / GX_COLS), 256, 0, s>>>(x, g.off, g.cnt, g.pos_pair, g.tiles, g.n_tiles,
+                                                               k, n_embd, xt);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if ((e = cudaFuncSetAttribute(k_gemm_gate_up, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   GU_SMEM)) != cudaSuccess)

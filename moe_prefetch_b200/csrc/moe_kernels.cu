@@ -6,6 +6,8 @@
 // The persistent multi-layer decode kernel lives in moe_decode.cu.
 #include "moe_kernels.h"
 
+#include <cooperative_groups.h>
+
 #include <algorithm>
 
 namespace moe {
@@ -196,14 +198,17 @@ __global__ void __launch_bounds__(512) k_router(const float *__restrict__ W,
 }
 
 // Router for a batch (no prior, no observation: both apply to single tokens
-// only).  grid ceil(n_tok / tpc); block 256; tpc <= RB_TOK tokens per CTA.
-// The CTA keeps its token rows in shared memory.  Warp w takes experts
-// w, w + 8, ... two at a time: it loads its lanes' slice of both router
-// rows (n_embd == 2048: 16 float4 per lane each) before using either, then
-// runs the four fma chains of router_dot_warp for every token.  Every logit
-// is therefore computed in router_dot_warp's order, bit-identical to
-// k_router.  Then warp t selects for token t (router_select_warp).
+// only), one cluster of RB_CL CTAs per RB_TOK tokens.  CTA r of a cluster
+// computes the logits of experts [r E / RB_CL, (r + 1) E / RB_CL) for the
+// cluster's tokens: warp w takes two of them at a time, holds its lanes'
+// slice of both router rows in registers (n_embd == 2048: 16 float4 per lane
+// each) and runs the four fma chains of router_dot_warp for every token, so
+// every logit is computed in router_dot_warp's order, bit-identical to
+// k_router.  After a cluster barrier, CTA r gathers token r's E logits from
+// the cluster's shared memory and selects for it (router_select_warp).  Each
+// CTA reads only its 1/RB_CL of the router, instead of all of it.
 #define RB_TOK 8
+#define RB_CL 8
 
 __device__ __forceinline__ float router_chain_dot(const float4 (&wv)[16], const float *xt, int lane) {
     float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
@@ -221,51 +226,75 @@ __device__ __forceinline__ float router_chain_dot(const float4 (&wv)[16], const 
     return v;
 }
 
-__global__ void __launch_bounds__(256) k_router_batch(const float *__restrict__ W,
-                                                      const float *__restrict__ x, int n_tok,
-                                                      int tpc, int n_expert, int k,
-                                                      int32_t *__restrict__ ids,
-                                                      float *__restrict__ w) {
-    extern __shared__ __align__(16) float sm[];
-    float *xs = sm;                                   // [tpc][2048]
-    float *lg = sm + tpc * 2048;                      // [tpc][n_expert]
-    const int t0 = blockIdx.x * tpc;
-    const int nt = min(tpc, n_tok - t0);
+// grid RB_CL x ceil(n_tok / RB_TOK) (cluster dims RB_CL); block 256;
+// dynamic shared memory: the cluster's token rows [RB_TOK][2048].
+__global__ void __cluster_dims__(RB_CL, 1, 1) __launch_bounds__(256)
+    k_router_batch(const float *__restrict__ W, const float *__restrict__ x, int n_tok,
+                   int n_expert, int k, int32_t *__restrict__ ids, float *__restrict__ w) {
+    namespace cg = cooperative_groups;
+    extern __shared__ __align__(16) float xs[];          // [RB_TOK][2048]
+    __shared__ float lg[RB_TOK][256 / RB_CL];            // this CTA's experts' logits
+    __shared__ float lgf[256];                           // one token's logits, all experts
+    __shared__ int32_t sids[MOE_KMAX];
+    __shared__ float sw[MOE_KMAX];
+    cg::cluster_group cl = cg::this_cluster();
+    const int r = (int)cl.block_rank();
+    const int t0 = (blockIdx.x / RB_CL) * RB_TOK;
+    const int nt = min(RB_TOK, n_tok - t0);
+    const int epc = n_expert / RB_CL, e0 = r * epc;     // this CTA's experts
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    for (int i = threadIdx.x; i < nt * 512; i += blockDim.x)
-        reinterpret_cast<float4 *>(xs)[i] = reinterpret_cast<const float4 *>(x + (size_t)t0 * 2048)[i];
-    __syncthreads();
-    for (int e = warp; e < n_expert; e += 2 * nw) {
-        const int e2 = e + nw;
-        const bool two = e2 < n_expert;
-        float4 wa[16], wb[16];
+    {   // the token rows: every load issued before the first store
+        constexpr int PER = RB_TOK * 512 / 256;
+        const float4 *xg = reinterpret_cast<const float4 *>(x + (size_t)t0 * 2048);
+        float4 v[PER];
 #pragma unroll
-        for (int kk = 0; kk < 16; ++kk) {
-            wa[kk] = __ldg(reinterpret_cast<const float4 *>(W + (size_t)e * 2048 + 128 * kk + 4 * lane));
-            wb[kk] = two ? __ldg(reinterpret_cast<const float4 *>(W + (size_t)e2 * 2048 + 128 * kk + 4 * lane))
-                         : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int j = 0; j < PER; ++j) {
+            const int i = threadIdx.x + 256 * j;
+            v[j] = i < nt * 512 ? __ldg(xg + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         }
-        for (int t = 0; t < nt; ++t) {
-            const float va = router_chain_dot(wa, xs + t * 2048, lane);
-            const float vb = router_chain_dot(wb, xs + t * 2048, lane);
+#pragma unroll
+        for (int j = 0; j < PER; ++j) reinterpret_cast<float4 *>(xs)[threadIdx.x + 256 * j] = v[j];
+    }
+    __syncthreads();
+    for (int j = warp; j < epc; j += nw) {
+        // one router row per pass, two tokens per step (eight fma chains)
+        const float *Wr = W + (size_t)(e0 + j) * 2048;
+        float4 wr[16];
+#pragma unroll
+        for (int kk = 0; kk < 16; ++kk) wr[kk] = __ldg(reinterpret_cast<const float4 *>(Wr + 128 * kk + 4 * lane));
+        for (int t = 0; t < nt; t += 2) {
+            const int t2 = t + 1 < nt ? t + 1 : t;
+            const float va = router_chain_dot(wr, xs + t * 2048, lane);
+            const float vb = router_chain_dot(wr, xs + t2 * 2048, lane);
             if (lane == 0) {
-                lg[t * n_expert + e] = va;
-                if (two) lg[t * n_expert + e2] = vb;
+                lg[t][j] = va;
+                if (t + 1 < nt) lg[t + 1][j] = vb;
             }
         }
     }
-    __syncthreads();
-    if (warp < nt) {
-        __shared__ int32_t sids[RB_TOK][MOE_KMAX];
-        __shared__ float sw[RB_TOK][MOE_KMAX];
-        router_select_warp(lg + warp * n_expert, n_expert, nullptr, 0, 0.0f, false, k, sids[warp],
-                           sw[warp], lane);
+    cl.sync();   // every CTA's logits are in its shared memory
+    if (r < nt && warp == 0) {
+        for (int e = lane; e < n_expert; e += 32) {
+            const float *src = cl.map_shared_rank(&lg[r][0], e / epc);
+            lgf[e] = src[e % epc];
+        }
         __syncwarp();
+        // select_warp with inv = 1 and no prior: router_select_warp's result,
+        // in registers (no indexed local arrays)
+        int id_r = -1;
+        float w_r = 0.0f;
+        switch (n_expert) {
+            case 32: select_warp<1>(lgf, 1.0f, nullptr, 0, 0.0f, false, k, lane, id_r, w_r, sids, sw); break;
+            case 64: select_warp<2>(lgf, 1.0f, nullptr, 0, 0.0f, false, k, lane, id_r, w_r, sids, sw); break;
+            case 128: select_warp<4>(lgf, 1.0f, nullptr, 0, 0.0f, false, k, lane, id_r, w_r, sids, sw); break;
+            default: select_warp<8>(lgf, 1.0f, nullptr, 0, 0.0f, false, k, lane, id_r, w_r, sids, sw); break;
+        }
         if (lane < k) {
-            ids[(size_t)(t0 + warp) * k + lane] = sids[warp][lane];
-            w[(size_t)(t0 + warp) * k + lane] = sw[warp][lane];
+            ids[(size_t)(t0 + r) * k + lane] = id_r;
+            w[(size_t)(t0 + r) * k + lane] = w_r;
         }
     }
+    cl.sync();   // no CTA leaves while another still reads its logits
 }
 
 // ===========================================================================
@@ -581,16 +610,13 @@ cudaError_t launch_router(const float *W, const float *x, int n_tok, int n_exper
                           int32_t *ids, float *w, float *logits, const SlotState *st,
                           int observe_layer_idx, cudaStream_t s) {
     if (n_tok > 1 && n_embd == 2048 && !use_prior && observe_layer_idx < 0 && !logits) {
-        // tokens per CTA: enough CTAs to cover the SMs, at most RB_TOK
-        int dev = 0, sms = 148;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        const int tpc = std::max(1, std::min(RB_TOK, n_tok / std::max(1, sms)));
-        const size_t sm = sizeof(float) * ((size_t)tpc * 2048 + (size_t)tpc * n_expert);
+        // one cluster of RB_CL CTAs per RB_TOK tokens
+        const size_t sm = sizeof(float) * (size_t)RB_TOK * 2048;
         cudaError_t e = cudaFuncSetAttribute(k_router_batch, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)sm);
         if (e != cudaSuccess) return e;
-        k_router_batch<<<(n_tok + tpc - 1) / tpc, 256, sm, s>>>(W, x, n_tok, tpc, n_expert, k, ids, w);
+        const int groups = (n_tok + RB_TOK - 1) / RB_TOK;
+        k_router_batch<<<groups * RB_CL, 256, sm, s>>>(W, x, n_tok, n_expert, k, ids, w);
         return cudaGetLastError();
     }
     const size_t smem = sizeof(float) * ((size_t)n_embd + n_expert);
