@@ -231,7 +231,6 @@ __global__ void __launch_bounds__(256, 2) k_gate_up_grouped(
     extern __shared__ __align__(128) uint8_t smg[];
     __shared__ float act_s[GROUP_TILE][GU2_ROWS];
     __shared__ int s_tok[GROUP_TILE];
-    __shared__ __align__(8) uint64_t bar;
     if ((int)blockIdx.y >= *n_tiles) return;
     const int tl = tiles[blockIdx.y], e = tl >> 16, tt = tl & 0xFFFF;
     const int pos0 = off[e] + tt * GROUP_TILE;
@@ -246,63 +245,78 @@ __global__ void __launch_bounds__(256, 2) k_gate_up_grouped(
     if (threadIdx.x < np) s_tok[threadIdx.x] = pos_pair[pos0 + threadIdx.x] / k;
     const size_t rb = (size_t)(n_embd / MOE_QK) * MOE_Q4K_BYTES;
     const int i0 = blockIdx.x * GU2_ROWS;
-    const uint32_t bytes = (uint32_t)(GU2_ROWS * rb);
     const int nblk = n_embd / 32;
     const int xrow = (n_embd / 64) * PAD_U64;                                    // padded row bytes
-    uint8_t *g_sm = smg, *u_sm = smg + bytes;
-    int8_t *xq_s = reinterpret_cast<int8_t *>(smg + 2 * bytes);                 // [8][xrow]
+    int8_t *xq_s = reinterpret_cast<int8_t *>(smg);                              // [8][xrow]
     float *xd_s = reinterpret_cast<float *>(xq_s + (size_t)GROUP_TILE * xrow);   // [8][nblk]
     float *xs_s = xd_s + GROUP_TILE * nblk;
-    const bool dev = expert_on_device(src, e);
-    if (dev && threadIdx.x == 0) {
-        mbar_init(&bar, 1);
-        fence_mbar_init();
-        mbar_arrive_expect_tx(&bar, 2 * bytes);
-        bulk_g2s(g_sm, gbase + i0 * rb, bytes, &bar);
-        bulk_g2s(u_sm, ubase + i0 * rb, bytes, &bar);
-    }
-    __syncthreads();
-    stage_q8_padded(xq_s, xd_s, xs_s, xq, xd, xs, s_tok, np, n_embd, 64, PAD_U64);
-    if (!dev)
-        for (uint32_t o = threadIdx.x * 16; o < bytes; o += blockDim.x * 16) {
-            *reinterpret_cast<uint4 *>(g_sm + o) = *reinterpret_cast<const uint4 *>(gbase + i0 * rb + o);
-            *reinterpret_cast<uint4 *>(u_sm + o) = *reinterpret_cast<const uint4 *>(ubase + i0 * rb + o);
-        }
-    const bool ok = !dev || mbar_wait(&bar, 0);
-    if (__syncthreads_or(!ok)) {
-        if (threadIdx.x == 0) atomicOr(err, MOE_DEV_ERR_TIMEOUT);
-        return;
-    }
     const int units = (n_embd / MOE_QK) * 4;   // n_embd == 2048: one unit per lane
     const bool on = lane < units;
     const int sb = lane >> 2, pp = lane & 3;
+    // a lane reads its unit of each row straight from the expert's memory
+    // (device slot, or registered host memory for a missed expert): every
+    // weight byte is used by one lane once, so nothing is staged; the next
+    // row's loads are in flight while a row is computed
+    const uint8_t *grow = gbase + (size_t)i0 * rb + sb * MOE_Q4K_BYTES;
+    const uint8_t *urow = ubase + (size_t)i0 * rb + sb * MOE_Q4K_BYTES;
+    Q4Unit wg, wu;
+    if (on && warp < GU2_ROWS) {
+        q4k_unit_load(grow + (size_t)warp * rb, pp, wg);
+        q4k_unit_load(urow + (size_t)warp * rb, pp, wu);
+    }
+    __syncthreads();   // s_tok
+    stage_q8_padded(xq_s, xd_s, xs_s, xq, xd, xs, s_tok, np, n_embd, 64, PAD_U64);
+    __syncthreads();
     for (int r = warp; r < GU2_ROWS; r += nw) {
         Q4UnitDec dg, du;
         if (on) {
-            Q4Unit w;
-            q4k_unit_load(g_sm + r * rb + sb * MOE_Q4K_BYTES, pp, w);
-            q4k_unit_decode(w, pp, dg);
-            q4k_unit_load(u_sm + r * rb + sb * MOE_Q4K_BYTES, pp, w);
-            q4k_unit_decode(w, pp, du);
-        }
-        float v[16];
-#pragma unroll
-        for (int j = 0; j < GROUP_TILE; ++j) {
-            float g = 0.0f, up = 0.0f;
-            if (on && j < np) {
-                ActQ4 a;
-                load_act_q4_unit(a, xq_s + (size_t)j * xrow + lane * PAD_U64, xd_s + j * nblk,
-                                 xs_s + j * nblk, 2 * lane);
-                g += q4k_dec_compute(dg, a);
-                up += q4k_dec_compute(du, a);
+            q4k_unit_decode(wg, pp, dg);
+            q4k_unit_decode(wu, pp, du);
+            if (r + nw < GU2_ROWS) {
+                q4k_unit_load(grow + (size_t)(r + nw) * rb, pp, wg);
+                q4k_unit_load(urow + (size_t)(r + nw) * rb, pp, wu);
             }
-            v[j] = g;
-            v[GROUP_TILE + j] = up;
         }
-        const float sum = warp_sum16(v, lane);      // lane l: value l >> 1
-        const float other = __shfl_down_sync(MOE_FULL, sum, 16);   // lane l < 16: value 8 + (l >> 1)
-        if (lane < 16 && !(lane & 1) && (lane >> 1) < np)
-            act_s[lane >> 1][r] = silu_mul(sum, other);
+        if (np <= 2) {
+            // the common decode case: the four sums of at most two pairs by
+            // warp_sum4_t (bit-identical to warp_sum16's)
+            float g0 = 0.0f, u0 = 0.0f, g1 = 0.0f, u1 = 0.0f;
+            if (on) {
+                ActQ4 a;
+                load_act_q4_unit(a, xq_s + lane * PAD_U64, xd_s, xs_s, 2 * lane);
+                g0 += q4k_dec_compute(dg, a);
+                u0 += q4k_dec_compute(du, a);
+                if (np == 2) {
+                    load_act_q4_unit(a, xq_s + (size_t)xrow + lane * PAD_U64, xd_s + nblk, xs_s + nblk,
+                                     2 * lane);
+                    g1 += q4k_dec_compute(dg, a);
+                    u1 += q4k_dec_compute(du, a);
+                }
+            }
+            const float sum = warp_sum4_t(g0, u0, g1, u1, lane);   // lanes 0-7 g0, 8-15 u0, 16-23 g1, 24-31 u1
+            const float other = __shfl_down_sync(MOE_FULL, sum, 8);
+            if (lane == 0) act_s[0][r] = silu_mul(sum, other);
+            if (lane == 16 && np == 2) act_s[1][r] = silu_mul(sum, other);
+        } else {
+            float v[16];
+#pragma unroll
+            for (int j = 0; j < GROUP_TILE; ++j) {
+                float g = 0.0f, up = 0.0f;
+                if (on && j < np) {
+                    ActQ4 a;
+                    load_act_q4_unit(a, xq_s + (size_t)j * xrow + lane * PAD_U64, xd_s + j * nblk,
+                                     xs_s + j * nblk, 2 * lane);
+                    g += q4k_dec_compute(dg, a);
+                    up += q4k_dec_compute(du, a);
+                }
+                v[j] = g;
+                v[GROUP_TILE + j] = up;
+            }
+            const float sum = warp_sum16(v, lane);      // lane l: value l >> 1
+            const float other = __shfl_down_sync(MOE_FULL, sum, 16);   // lane l < 16: value 8 + (l >> 1)
+            if (lane < 16 && !(lane & 1) && (lane >> 1) < np)
+                act_s[lane >> 1][r] = silu_mul(sum, other);
+        }
     }
     __syncthreads();
     const int ablk = n_ff / 32;
@@ -496,8 +510,7 @@ cudaError_t launch_experts_grouped(const ExpertSrc &src, const float *x, const G
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     const bool q6 = down_type == MOE_QT_Q6K;
-    const size_t sm1 = 2 * (size_t)GU2_ROWS * (n_embd / MOE_QK) * MOE_Q4K_BYTES +
-                       (size_t)GROUP_TILE * (n_embd / 64) * PAD_U64 +
+    const size_t sm1 = (size_t)GROUP_TILE * (n_embd / 64) * PAD_U64 +
                        2 * sizeof(float) * GROUP_TILE * (n_embd / 32);
     const size_t sm2 = (((size_t)DN2_ROWS * (n_ff / MOE_QK) * (q6 ? MOE_Q6K_BYTES : MOE_Q4K_BYTES) + 15) &
                         ~(size_t)15) +
