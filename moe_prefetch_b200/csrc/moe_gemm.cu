@@ -437,6 +437,19 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_gemm_down(
             *reinterpret_cast<uint4 *>(sR + o) = *reinterpret_cast<const uint4 *>(rows_g + o);
         __syncthreads();
     }
+    // the CTA that will most likely take this SM next (one CTA per SM, launch
+    // order x fastest): its rows into L2 now, so that its copy lands sooner
+    if (tid == 32) {
+        uint32_t nsm;
+        asm("mov.u32 %0, %%nsmid;" : "=r"(nsm));
+        const int nxt = (int)(blockIdx.y * gridDim.x + blockIdx.x + nsm);
+        const int ny = nxt / (int)gridDim.x, nx = nxt % (int)gridDim.x;
+        if (ny < *n_tiles) {
+            const int en = tiles[ny] >> 16;
+            const uint8_t *dn = expert_on_device(src, en) ? expert_ptr(src, 2, en) : nullptr;
+            if (dn) prefetch_l2(dn + (size_t)nx * GM_ROWS * rb, (uint32_t)(GM_ROWS * rb));
+        }
+    }
     const uint8_t *row = sR + (size_t)m * rb;
     const uint32_t idesc = idesc_f16(GM_ROWS, N);
     bool ok = true;
