@@ -1163,6 +1163,17 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         : "memory");
 }
 
+// Launch-order index of the CTA `ahead` SM counts after this one (x fastest),
+// as (x, y) of the grid: with `ahead` CTAs per SM resident, the CTA likely
+// to start next when this one ends.
+__device__ __forceinline__ void next_wave_cta(int ahead, int &nx, int &ny) {
+    uint32_t nsm;
+    asm("mov.u32 %0, %%nsmid;" : "=r"(nsm));
+    const int nxt = (int)(blockIdx.y * gridDim.x + blockIdx.x + (uint32_t)ahead * nsm);
+    ny = nxt / (int)gridDim.x;
+    nx = nxt % (int)gridDim.x;
+}
+
 // Hint: bring [src, src + bytes) into L2 (no completion, no destination);
 // src 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {

@@ -440,10 +440,8 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_gemm_down(
     // the CTA that will most likely take this SM next (one CTA per SM, launch
     // order x fastest): its rows into L2 now, so that its copy lands sooner
     if (tid == 32) {
-        uint32_t nsm;
-        asm("mov.u32 %0, %%nsmid;" : "=r"(nsm));
-        const int nxt = (int)(blockIdx.y * gridDim.x + blockIdx.x + nsm);
-        const int ny = nxt / (int)gridDim.x, nx = nxt % (int)gridDim.x;
+        int nx, ny;
+        next_wave_cta(1, nx, ny);
         if (ny < *n_tiles) {
             const int en = tiles[ny] >> 16;
             const uint8_t *dn = expert_on_device(src, en) ? expert_ptr(src, 2, en) : nullptr;
