@@ -130,7 +130,11 @@ __global__ void __launch_bounds__(GROUP_THREADS) k_group(const int32_t *__restri
 }
 
 #define GU2_ROWS 32    // gate/up rows per CTA: one Q8_1 block of every pair's activations
-#define DN2_ROWS 64    // down rows per CTA: 8 per warp
+#define DN2_ROWS 64    // down rows per CTA for Q4_K down weights: 8 per warp
+
+// Down rows per CTA for Q6_K down weights: two warp passes of 32 / gs rows,
+// gs = 2 n_ff / 256 lanes per row (80 rows at n_ff = 768, 128 at 512).
+static inline int dn2_rows_q6(int n_ff) { return 8 * 2 * (32 / (2 * (n_ff / MOE_QK))); }
 
 // x [n_rows][n_embd] -> Q8_1 (xq, d, s per 32-block), with the quantiser of
 // k_gate_up, once per row.  grid n_rows; block 256.
@@ -337,7 +341,7 @@ __global__ void __launch_bounds__(256, 2) k_down_grouped(
     ExpertSrc src, const int8_t *__restrict__ aq, const float *__restrict__ ad,
     const float *__restrict__ as, const int32_t *__restrict__ off, const int32_t *__restrict__ cnt,
     const int32_t *__restrict__ tiles, const int32_t *__restrict__ n_tiles, int n_embd, int n_ff,
-    int down_type, float *__restrict__ ypair, int *err) {
+    int down_type, int dn_rows, float *__restrict__ ypair, int *err) {
     extern __shared__ __align__(128) uint8_t smg[];
     __shared__ int s_pos[GROUP_TILE];
     __shared__ __align__(8) uint64_t bar;
@@ -355,11 +359,12 @@ __global__ void __launch_bounds__(256, 2) k_down_grouped(
     const int nb = n_ff / MOE_QK, ablk = n_ff / 32;
     const bool q6 = down_type == MOE_QT_Q6K;
     const size_t rb = (size_t)nb * (q6 ? MOE_Q6K_BYTES : MOE_Q4K_BYTES);
-    const int h0 = blockIdx.x * DN2_ROWS;
-    const uint32_t bytes = (uint32_t)(DN2_ROWS * rb);
+    const int h0 = blockIdx.x * dn_rows;
+    const int rows = min(dn_rows, n_embd - h0);           // the last CTA may have fewer
+    const uint32_t bytes = (uint32_t)(rows * rb);         // rows a multiple of 8: bytes of 16
     const int unit = q6 ? 128 : 64, stride = q6 ? PAD_U128 : PAD_U64;
     const int arow = (n_ff / unit) * stride;                                      // padded row bytes
-    int8_t *aq_s = reinterpret_cast<int8_t *>(smg + ((bytes + 15) & ~15u));     // [8][arow]
+    int8_t *aq_s = reinterpret_cast<int8_t *>(smg + (((uint32_t)(dn_rows * rb) + 15) & ~15u));   // [8][arow]
     float *ad_s = reinterpret_cast<float *>(aq_s + (size_t)GROUP_TILE * arow);   // [8][ablk]
     float *as_s = ad_s + GROUP_TILE * ablk;
     const bool dev = expert_on_device(src, e);
@@ -379,34 +384,39 @@ __global__ void __launch_bounds__(256, 2) k_down_grouped(
         if (threadIdx.x == 0) atomicOr(err, MOE_DEV_ERR_TIMEOUT);
         return;
     }
-    const int rw = warp * (DN2_ROWS / 8);        // first local row of this warp
+    const int wrows = dn_rows / 8;              // rows per warp
+    const int rw = warp * wrows;                // first local row of this warp
     if (q6) {
-        const int grp = lane >> 3, u = lane & 7;
-        const bool on = u < nb * 2;
+        // a row is gs = 2 nb half-block units on consecutive lanes, 32 / gs rows
+        // per pass; groupn_sum forms group8_sum's value (8-lane groups with
+        // the lanes past the units at 0), so the rows match the per-pair kernel
+        const int gs = nb * 2, rpp = 32 / gs;
+        const int rr = lane / gs, u = lane - rr * gs;
         const int sb = u >> 1, hh = u & 1;
-        for (int r0w = 0; r0w < DN2_ROWS / 8; r0w += 4) {
-            const int r = rw + r0w + grp;
+        for (int p0 = 0; p0 < wrows; p0 += rpp) {
+            const int rl = p0 + rr, r = rw + rl;
+            const bool live = rr < rpp && rl < wrows && r < rows;
             Q6HalfDec w;
-            if (on) {
+            if (live) {
                 Q6Half raw;
                 q6k_half_load(smg + r * rb + sb * MOE_Q6K_BYTES, hh, raw);
                 q6k_half_decode(raw, w);
             }
             for (int j = 0; j < np; ++j) {
                 float v = 0.0f;
-                if (on) {
+                if (live) {
                     ActHalf a;
                     load_act_half_at(a, aq_s + (size_t)j * arow + u * PAD_U128, ad_s + j * ablk + 4 * u);
                     v = q6k_dec_compute(w, a);
                 }
-                v = group8_sum(v);
-                if (u == 0) ypair[(size_t)s_pos[j] * n_embd + h0 + r] = v;
+                v = groupn_sum(v, u, gs);
+                if (live && u == 0) ypair[(size_t)s_pos[j] * n_embd + h0 + r] = v;
             }
         }
     } else {
         const int units = nb * 4;
         const bool on = lane < units;
-        for (int rr = 0; rr < DN2_ROWS / 8; ++rr) {
+        for (int rr = 0; rr < wrows && rw + rr < rows; ++rr) {
             const int r = rw + rr;
             Q4UnitDec w;
             if (on) {
@@ -496,6 +506,8 @@ cudaError_t launch_experts_grouped(const ExpertSrc &src, const float *x, const G
                                    const float *w, void *scratch, float *ypair, const float *resid,
                                    float *y, int *err, cudaStream_t s) {
     if (n_embd != 2048 || n_ff % GU2_ROWS || n_embd % DN2_ROWS) return cudaErrorInvalidValue;
+    const bool q6d = down_type == MOE_QT_Q6K;
+    const int dn_rows = q6d ? dn2_rows_q6(n_ff) : DN2_ROWS;   // a multiple of 8 rows per CTA
     const int P = n_tok * k;
     const int maxt = group_max_tiles(src.n_expert + 1, P, GROUP_TILE);
     uint8_t *sc = static_cast<uint8_t *>(scratch);
@@ -512,7 +524,7 @@ cudaError_t launch_experts_grouped(const ExpertSrc &src, const float *x, const G
     const bool q6 = down_type == MOE_QT_Q6K;
     const size_t sm1 = (size_t)GROUP_TILE * (n_embd / 64) * PAD_U64 +
                        2 * sizeof(float) * GROUP_TILE * (n_embd / 32);
-    const size_t sm2 = (((size_t)DN2_ROWS * (n_ff / MOE_QK) * (q6 ? MOE_Q6K_BYTES : MOE_Q4K_BYTES) + 15) &
+    const size_t sm2 = (((size_t)dn_rows * (n_ff / MOE_QK) * (q6 ? MOE_Q6K_BYTES : MOE_Q4K_BYTES) + 15) &
                         ~(size_t)15) +
                        (size_t)GROUP_TILE * (q6 ? (n_ff / 128) * PAD_U128 : (n_ff / 64) * PAD_U64) +
                        2 * sizeof(float) * GROUP_TILE * (n_ff / 32);
@@ -525,8 +537,8 @@ cudaError_t launch_experts_grouped(const ExpertSrc &src, const float *x, const G
     k_gate_up_grouped<<<dim3(n_ff / GU2_ROWS, maxt), 256, sm1, s>>>(
         src, xq, xd, xs, g.off, g.cnt, g.pos_pair, g.tiles, g.n_tiles, k, n_embd, n_ff, aq, ad, as, err);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    k_down_grouped<<<dim3(n_embd / DN2_ROWS, maxt), 256, sm2, s>>>(
-        src, aq, ad, as, g.off, g.cnt, g.tiles, g.n_tiles, n_embd, n_ff, down_type, ypair, err);
+    k_down_grouped<<<dim3((n_embd + dn_rows - 1) / dn_rows, maxt), 256, sm2, s>>>(
+        src, aq, ad, as, g.off, g.cnt, g.tiles, g.n_tiles, n_embd, n_ff, down_type, dn_rows, ypair, err);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     return launch_combine(ypair, g.pair_pos, w, n_tok, k, n_embd, resid, y, s);
 }
