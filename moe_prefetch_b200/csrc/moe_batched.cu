@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(GROUP_THREADS) k_group(const int32_t *__restri
     }
 }
 
-#define GU2_ROWS 32    // gate/up rows per CTA: one Q8_1 block of every pair's activations
+#define GU2_ROWS 64    // gate/up rows per CTA: two Q8_1 blocks of every pair's activations
 #define DN2_ROWS 64    // down rows per CTA for Q4_K down weights: 8 per warp
 
 // Down rows per CTA for Q6_K down weights: two warp passes of 32 / gs rows,
@@ -215,17 +215,16 @@ __device__ __forceinline__ void stage_q8_padded(int8_t *q_s, float *d_s, float *
     }
 }
 
-// Gate/up for the pairs of one tile over GU2_ROWS rows.  grid (n_ff / 32, max
-// tiles); block 256.  The CTA stages in shared memory:
-// - its 32 gate and 32 up rows (bulk copy; plain loads for a missed expert);
-// - the tile's Q8_1 token rows.
-// Each warp takes 4 rows:
+// Gate/up for the pairs of one tile over GU2_ROWS rows.  grid (n_ff / GU2_ROWS, max
+// tiles); block 256.  The CTA stages the tile's Q8_1 token rows in shared
+// memory; the gate and up rows are read by the lanes from the expert's
+// memory.  Each warp takes GU2_ROWS / 8 rows:
 // - every lane decodes its unit of the row once;
 // - for every pair, the per-pair kernel's unit dots;
 // - one transposed reduction of all 2 x np sums (warp_sum's pairing).
-// Every activation is therefore bit-identical to k_gate_up's.  The 32
-// activations of each pair form one Q8_1 block, quantised as k_down does,
-// into aq/ad/as [pos][...].
+// Every activation is therefore bit-identical to k_gate_up's.  Each 32
+// activations of a pair form one Q8_1 block, quantised as k_down does, into
+// aq/ad/as [pos][...].
 __global__ void __launch_bounds__(256, 2) k_gate_up_grouped(
     ExpertSrc src, const int8_t *__restrict__ xq, const float *__restrict__ xd,
     const float *__restrict__ xs, const int32_t *__restrict__ off, const int32_t *__restrict__ cnt,
@@ -324,10 +323,11 @@ __global__ void __launch_bounds__(256, 2) k_gate_up_grouped(
     }
     __syncthreads();
     const int ablk = n_ff / 32;
-    for (int j = warp; j < np; j += nw) {
+    for (int jb = warp; jb < np * (GU2_ROWS / 32); jb += nw) {   // (pair, 32-row block)
+        const int j = jb / (GU2_ROWS / 32), b = jb % (GU2_ROWS / 32);
         const size_t pos = (size_t)(pos0 + j);
-        q8_block_warp(act_s[j][lane], lane, aq + pos * n_ff + i0, ad + pos * ablk + i0 / 32,
-                      as + pos * ablk + i0 / 32);
+        q8_block_warp(act_s[j][32 * b + lane], lane, aq + pos * n_ff + i0 + 32 * b,
+                      ad + pos * ablk + i0 / 32 + b, as + pos * ablk + i0 / 32 + b);
     }
 }
 
