@@ -1127,6 +1127,11 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
                  : "memory");
 }
 
+// A plain arrival (no transaction bytes) on an mbarrier.
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 // One try_wait with a suspend-time hint of 1 ms: a waiting warp sleeps until
 // the phase completes (the hardware wakes it) or the hint runs out, instead
 // of polling and taking issue slots from the warps that produce the data.

@@ -237,7 +237,14 @@ __device__ __forceinline__ GuRaw load_gu_raw(const uint8_t *row, int s) {
 #define GU_B_BYTES (GM_NT * GM_KS_GU * 2)
 #define GU_SMEM (4 * GU_A_BYTES + 3 * GU_B_BYTES + 128)
 
-__global__ void __launch_bounds__(GM_THREADS, 2) k_gemm_gate_up(
+// Warp roles: warps 0-7 (GM_THREADS) dequantise, thread (mat, m) row m of
+// gate (mat 0) or up (mat 1); warp 8 issues the token-tile copies and, on
+// one thread, the MMAs.  A stage's A buffer is handed over by a_full[b] (one
+// arrival per dequantising warp, after each thread's proxy fence) and given
+// back by the MMAs' commit to mma_done[b]; there is no CTA-wide barrier per
+// stage, so a warp can run a stage ahead of another within the two buffers.
+#define GU_THREADS (GM_THREADS + 32)
+__global__ void __launch_bounds__(GU_THREADS, 2) k_gemm_gate_up(
     ExpertSrc src, const __half *__restrict__ xt, const int32_t *__restrict__ off,
     const int32_t *__restrict__ cnt, const int32_t *__restrict__ tiles,
     const int32_t *__restrict__ n_tiles, int n_embd, int n_ff, __half *__restrict__ at, int *err) {
@@ -248,7 +255,8 @@ __global__ void __launch_bounds__(GM_THREADS, 2) k_gemm_gate_up(
     uint8_t *sB = sm + 4 * GU_A_BYTES;                  // [3] 8 KB
     uint64_t *mma_done = reinterpret_cast<uint64_t *>(sB + 3 * GU_B_BYTES);   // [2]
     uint64_t *b_full = mma_done + 2;                                           // [3]
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(b_full + 3);
+    uint64_t *a_full = b_full + 3;                                             // [2]
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(a_full + 2);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int tl = tiles[i], e = tl >> 16, tt = tl & 0xFFFF;
     const int np = min(GM_NT, cnt[e] - tt * GM_NT);
@@ -264,6 +272,7 @@ __global__ void __launch_bounds__(GM_THREADS, 2) k_gemm_gate_up(
     if (tid == 0) {
         for (int q = 0; q < 2; ++q) mbar_init(&mma_done[q], 1);
         for (int q = 0; q < 3; ++q) mbar_init(&b_full[q], 1);
+        for (int q = 0; q < 2; ++q) mbar_init(&a_full[q], GM_THREADS / 32);
         fence_mbar_init();
     }
     if (warp == 0) tmem_alloc(tslot, 128);
@@ -272,49 +281,60 @@ __global__ void __launch_bounds__(GM_THREADS, 2) k_gemm_gate_up(
     tc_fence_after();
     const uint32_t tmem = *tslot;               // gate accumulator: columns 0..63, up: 64..127
     const __half *xtile = xt + (size_t)i * n_embd * GM_NT;
-    if (tid == 0) {
-        mbar_arrive_expect_tx(&b_full[0], GU_B_BYTES);
-        bulk_g2s(sB, xtile, GU_B_BYTES, &b_full[0]);
-    }
-    const int mat = tid >> 7, m = tid & 127;
-    const size_t rb = (size_t)(n_embd / MOE_QK) * MOE_Q4K_BYTES;
-    const uint8_t *row = (mat ? ubase : gbase) + (size_t)(r0 + m) * rb;
-    const uint32_t idesc = idesc_f16(GM_ROWS, N);
     bool ok = true;
-    GuRaw nxt = load_gu_raw(row, 0);
-    for (int s = 0; s < S; ++s) {
-        const GuRaw cur = nxt;
-        if (s + 1 < S) nxt = load_gu_raw(row, s + 1);
-        const int b = s & 1;
-        if (s >= 2 && !mbar_wait(&mma_done[b], ((s - 2) >> 1) & 1)) ok = false;
-        if (tid == 0 && s + 1 < S) {
-            // B buffer (s+1) % 3 was last read by the MMAs of stage s-2
-            const int nb = (s + 1) % 3;
-            mbar_arrive_expect_tx(&b_full[nb], GU_B_BYTES);
-            bulk_g2s(sB + nb * GU_B_BYTES, xtile + (size_t)(s + 1) * GM_NT * GM_KS_GU, GU_B_BYTES,
-                     &b_full[nb]);
-        }
-        deq_q4k_group(cur.hdr, cur.q0, cur.q1, s & 3, sA + (2 * b + mat) * GU_A_BYTES, m);
-        fence_proxy_async();
-        __syncthreads();
-        if (tid == 0) {
-            tc_fence_after();
-            if (mbar_wait(&b_full[s % 3], (s / 3) & 1)) {
-                const uint32_t aG = smem_u32(sA + (2 * b) * GU_A_BYTES);
-                const uint32_t aU = smem_u32(sA + (2 * b + 1) * GU_A_BYTES);
-                const uint32_t bB = smem_u32(sB + (s % 3) * GU_B_BYTES);
-#pragma unroll
-                for (int j = 0; j < GM_KS_GU / 16; ++j) {
-                    const uint64_t db = smem_desc(bB + j * 2 * (GM_NT * 16), GM_NT * 16, 128);
-                    tc_mma(tmem, smem_desc(aG + j * 2 * (GM_ROWS * 16), GM_ROWS * 16, 128), db,
-                           idesc, (s | j) != 0);
-                    tc_mma(tmem + 64, smem_desc(aU + j * 2 * (GM_ROWS * 16), GM_ROWS * 16, 128), db,
-                           idesc, (s | j) != 0);
+    if (warp == GM_THREADS / 32) {
+        // ---- copy + MMA warp ----
+        if (lane == 0) {
+            const uint32_t idesc = idesc_f16(GM_ROWS, N);
+            mbar_arrive_expect_tx(&b_full[0], GU_B_BYTES);
+            bulk_g2s(sB, xtile, GU_B_BYTES, &b_full[0]);
+            for (int s = 0; s < S; ++s) {
+                const int b = s & 1;
+                if (s + 1 < S) {
+                    // B buffer (s+1) % 3 was last read by the MMAs of stage s-2
+                    if (s >= 2 && !mbar_wait(&mma_done[b], ((s - 2) >> 1) & 1)) ok = false;
+                    const int nb = (s + 1) % 3;
+                    fence_proxy_async();
+                    mbar_arrive_expect_tx(&b_full[nb], GU_B_BYTES);
+                    bulk_g2s(sB + nb * GU_B_BYTES, xtile + (size_t)(s + 1) * GM_NT * GM_KS_GU, GU_B_BYTES,
+                             &b_full[nb]);
                 }
-            } else {
-                ok = false;
+                const bool ready = mbar_wait(&a_full[b], (s >> 1) & 1) && mbar_wait(&b_full[s % 3], (s / 3) & 1);
+                tc_fence_after();
+                if (ready) {
+                    const uint32_t aG = smem_u32(sA + (2 * b) * GU_A_BYTES);
+                    const uint32_t aU = smem_u32(sA + (2 * b + 1) * GU_A_BYTES);
+                    const uint32_t bB = smem_u32(sB + (s % 3) * GU_B_BYTES);
+#pragma unroll
+                    for (int j = 0; j < GM_KS_GU / 16; ++j) {
+                        const uint64_t db = smem_desc(bB + j * 2 * (GM_NT * 16), GM_NT * 16, 128);
+                        tc_mma(tmem, smem_desc(aG + j * 2 * (GM_ROWS * 16), GM_ROWS * 16, 128), db,
+                               idesc, (s | j) != 0);
+                        tc_mma(tmem + 64, smem_desc(aU + j * 2 * (GM_ROWS * 16), GM_ROWS * 16, 128), db,
+                               idesc, (s | j) != 0);
+                    }
+                } else {
+                    ok = false;
+                }
+                tc_commit(&mma_done[b]);
             }
-            tc_commit(&mma_done[b]);
+        }
+        __syncwarp();
+    } else {
+        // ---- dequantising warps ----
+        const int mat = tid >> 7, m = tid & 127;
+        const size_t rb = (size_t)(n_embd / MOE_QK) * MOE_Q4K_BYTES;
+        const uint8_t *row = (mat ? ubase : gbase) + (size_t)(r0 + m) * rb;
+        GuRaw nxt = load_gu_raw(row, 0);
+        for (int s = 0; s < S; ++s) {
+            const GuRaw cur = nxt;
+            if (s + 1 < S) nxt = load_gu_raw(row, s + 1);
+            const int b = s & 1;
+            if (s >= 2 && !mbar_wait(&mma_done[b], ((s - 2) >> 1) & 1)) ok = false;
+            deq_q4k_group(cur.hdr, cur.q0, cur.q1, s & 3, sA + (2 * b + mat) * GU_A_BYTES, m);
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&a_full[b]);
         }
     }
     if (!mbar_wait(&mma_done[(S - 1) & 1], ((S - 1) >> 1) & 1)) ok = false;
@@ -336,7 +356,7 @@ __global__ void __launch_bounds__(GM_THREADS, 2) k_gemm_gate_up(
             }
         }
     }
-    if (!ok && tid == 0) atomicOr(err, MOE_DEV_ERR_TIMEOUT);
+    if (!ok) atomicOr(err, MOE_DEV_ERR_TIMEOUT);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -536,7 +556,7 @@ cudaError_t launch_experts_gemm(const ExpertSrc &src, const float *x, const Grou
     if ((e = cudaFuncSetAttribute(k_gemm_down, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   dn_smem(n_ff))) != cudaSuccess)
         return e;
-    k_gemm_gate_up<<<dim3(n_ff / GM_ROWS, maxt), GM_THREADS, GU_SMEM, s>>>(
+    k_gemm_gate_up<<<dim3(n_ff / GM_ROWS, maxt), GU_THREADS, GU_SMEM, s>>>(
         src, xt, g.off, g.cnt, g.tiles, g.n_tiles, n_embd, n_ff, at, err);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     k_gemm_down<<<dim3(n_embd / GM_ROWS, maxt), DN_THREADS, dn_smem(n_ff), s>>>(
