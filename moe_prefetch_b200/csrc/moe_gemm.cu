@@ -396,7 +396,10 @@ __device__ __forceinline__ void deq_q6k_quarter(const uint32_t (&src)[8], const 
 static inline int dn_rows_bytes(int n_ff) { return ((GM_ROWS * (n_ff / MOE_QK) * MOE_Q6K_BYTES) + 127) & ~127; }
 static inline int dn_smem(int n_ff) { return dn_rows_bytes(n_ff) + 2 * DN_A_BYTES + 3 * DN_B_BYTES + 128; }
 
-__global__ void __launch_bounds__(DN_THREADS, 1) k_gemm_down(
+// Warp roles as in k_gemm_gate_up: warps 0-15 (DN_THREADS) dequantise, four
+// threads per row; warp 16 issues the token-tile copies and the MMAs.
+#define DN_ALL_THREADS (DN_THREADS + 32)
+__global__ void __launch_bounds__(DN_ALL_THREADS, 1) k_gemm_down(
     ExpertSrc src, const __half *__restrict__ at, const int32_t *__restrict__ off,
     const int32_t *__restrict__ cnt, const int32_t *__restrict__ tiles,
     const int32_t *__restrict__ n_tiles, int n_embd, int n_ff, float *__restrict__ ypair,
@@ -412,7 +415,8 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_gemm_down(
     uint64_t *mma_done = reinterpret_cast<uint64_t *>(sR + rows_bytes);       // [2]
     uint64_t *b_full = mma_done + 2;                                           // [3]
     uint64_t *r_full = b_full + 3;                                             // [1]
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(r_full + 1);
+    uint64_t *a_full = r_full + 1;                                             // [2]
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(a_full + 2);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int tl = tiles[i], e = tl >> 16, tt = tl & 0xFFFF;
     const int pos0 = off[e] + tt * GM_NT;
@@ -429,6 +433,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_gemm_down(
         for (int q = 0; q < 2; ++q) mbar_init(&mma_done[q], 1);
         for (int q = 0; q < 3; ++q) mbar_init(&b_full[q], 1);
         mbar_init(r_full, 1);
+        for (int q = 0; q < 2; ++q) mbar_init(&a_full[q], DN_THREADS / 32);
         fence_mbar_init();
     }
     if (warp == 0) tmem_alloc(tslot, 64);
@@ -437,11 +442,6 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_gemm_down(
     tc_fence_after();
     const uint32_t tmem = *tslot;
     const __half *atile = at + (size_t)i * n_ff * GM_NT;
-    if (tid == 0) {
-        mbar_arrive_expect_tx(&b_full[0], DN_B_BYTES);
-        bulk_g2s(sB, atile, DN_B_BYTES, &b_full[0]);
-    }
-    const int qtr = tid >> 7, m = tid & 127;
     // the CTA's 128 rows are contiguous: one bulk copy from device memory;
     // an expert in host memory (a miss) is copied by the threads
     const uint8_t *rows_g = dbase + (size_t)r0 * rb;
@@ -453,7 +453,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_gemm_down(
             bulk_g2s(sR, rows_g, (uint32_t)(GM_ROWS * rb), r_full);
         }
     } else {
-        for (int o = tid * 16; o < GM_ROWS * (int)rb; o += DN_THREADS * 16)
+        for (int o = tid * 16; o < GM_ROWS * (int)rb; o += DN_ALL_THREADS * 16)
             *reinterpret_cast<uint4 *>(sR + o) = *reinterpret_cast<const uint4 *>(rows_g + o);
         __syncthreads();
     }
@@ -468,43 +468,59 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_gemm_down(
             if (dn) prefetch_l2(dn + (size_t)nx * GM_ROWS * rb, (uint32_t)(GM_ROWS * rb));
         }
     }
-    const uint8_t *row = sR + (size_t)m * rb;
-    const uint32_t idesc = idesc_f16(GM_ROWS, N);
     bool ok = true;
-    if (dev && !mbar_wait(r_full, 0)) ok = false;
-    for (int s = 0; s < S; ++s) {
-        const uint8_t *blk = row + (s >> 1) * MOE_Q6K_BYTES;
-        const int h = s & 1;
-        uint32_t src[8], qh[8], sc[2];
-        ldw_a2<8>(blk + 64 * h + 32 * (qtr & 1), src);
-        ldw_a2<8>(blk + 128 + 32 * h, qh);
-        ldw_a2<2>(blk + 192 + 8 * h, sc);
-        const float d = h2f(*reinterpret_cast<const uint16_t *>(blk + 208));
-        const int b = s & 1;
-        if (s >= 2 && !mbar_wait(&mma_done[b], ((s - 2) >> 1) & 1)) ok = false;
-        if (tid == 0 && s + 1 < S) {
-            const int nb = (s + 1) % 3;
-            mbar_arrive_expect_tx(&b_full[nb], DN_B_BYTES);
-            bulk_g2s(sB + nb * DN_B_BYTES, atile + (size_t)(s + 1) * GM_NT * GM_KS_DN, DN_B_BYTES,
-                     &b_full[nb]);
-        }
-        deq_q6k_quarter(src, qh, sc, d, qtr, sA + b * DN_A_BYTES, m);
-        fence_proxy_async();
-        __syncthreads();
-        if (tid == 0) {
-            tc_fence_after();
-            if (mbar_wait(&b_full[s % 3], (s / 3) & 1)) {
-                const uint32_t aA = smem_u32(sA + b * DN_A_BYTES);
-                const uint32_t bB = smem_u32(sB + (s % 3) * DN_B_BYTES);
+    if (warp == DN_THREADS / 32) {
+        // ---- copy + MMA warp ----
+        if (lane == 0) {
+            const uint32_t idesc = idesc_f16(GM_ROWS, N);
+            mbar_arrive_expect_tx(&b_full[0], DN_B_BYTES);
+            bulk_g2s(sB, atile, DN_B_BYTES, &b_full[0]);
+            for (int s = 0; s < S; ++s) {
+                const int b = s & 1;
+                if (s + 1 < S) {
+                    // B buffer (s+1) % 3 was last read by the MMAs of stage s-2
+                    if (s >= 2 && !mbar_wait(&mma_done[b], ((s - 2) >> 1) & 1)) ok = false;
+                    const int nb = (s + 1) % 3;
+                    mbar_arrive_expect_tx(&b_full[nb], DN_B_BYTES);
+                    bulk_g2s(sB + nb * DN_B_BYTES, atile + (size_t)(s + 1) * GM_NT * GM_KS_DN, DN_B_BYTES,
+                             &b_full[nb]);
+                }
+                const bool ready = mbar_wait(&a_full[b], (s >> 1) & 1) && mbar_wait(&b_full[s % 3], (s / 3) & 1);
+                tc_fence_after();
+                if (ready) {
+                    const uint32_t aA = smem_u32(sA + b * DN_A_BYTES);
+                    const uint32_t bB = smem_u32(sB + (s % 3) * DN_B_BYTES);
 #pragma unroll
-                for (int j = 0; j < GM_KS_DN / 16; ++j)
-                    tc_mma(tmem, smem_desc(aA + j * 2 * (GM_ROWS * 16), GM_ROWS * 16, 128),
-                           smem_desc(bB + j * 2 * (GM_NT * 16), GM_NT * 16, 128), idesc,
-                           (s | j) != 0);
-            } else {
-                ok = false;
+                    for (int j = 0; j < GM_KS_DN / 16; ++j)
+                        tc_mma(tmem, smem_desc(aA + j * 2 * (GM_ROWS * 16), GM_ROWS * 16, 128),
+                               smem_desc(bB + j * 2 * (GM_NT * 16), GM_NT * 16, 128), idesc,
+                               (s | j) != 0);
+                } else {
+                    ok = false;
+                }
+                tc_commit(&mma_done[b]);
             }
-            tc_commit(&mma_done[b]);
+        }
+        __syncwarp();
+    } else {
+        // ---- dequantising warps ----
+        const int qtr = tid >> 7, m = tid & 127;
+        const uint8_t *row = sR + (size_t)m * rb;
+        if (dev && !mbar_wait(r_full, 0)) ok = false;
+        for (int s = 0; s < S; ++s) {
+            const uint8_t *blk = row + (s >> 1) * MOE_Q6K_BYTES;
+            const int h = s & 1;
+            uint32_t src[8], qh[8], sc[2];
+            ldw_a2<8>(blk + 64 * h + 32 * (qtr & 1), src);
+            ldw_a2<8>(blk + 128 + 32 * h, qh);
+            ldw_a2<2>(blk + 192 + 8 * h, sc);
+            const float d = h2f(*reinterpret_cast<const uint16_t *>(blk + 208));
+            const int b = s & 1;
+            if (s >= 2 && !mbar_wait(&mma_done[b], ((s - 2) >> 1) & 1)) ok = false;
+            deq_q6k_quarter(src, qh, sc, d, qtr, sA + b * DN_A_BYTES, m);
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&a_full[b]);
         }
     }
     if (!mbar_wait(&mma_done[(S - 1) & 1], ((S - 1) >> 1) & 1)) ok = false;
@@ -522,7 +538,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_gemm_down(
             }
         }
     }
-    if (!ok && tid == 0) atomicOr(err, MOE_DEV_ERR_TIMEOUT);
+    if (!ok) atomicOr(err, MOE_DEV_ERR_TIMEOUT);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -559,7 +575,7 @@ cudaError_t launch_experts_gemm(const ExpertSrc &src, const float *x, const Grou
     k_gemm_gate_up<<<dim3(n_ff / GM_ROWS, maxt), GU_THREADS, GU_SMEM, s>>>(
         src, xt, g.off, g.cnt, g.tiles, g.n_tiles, n_embd, n_ff, at, err);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    k_gemm_down<<<dim3(n_embd / GM_ROWS, maxt), DN_THREADS, dn_smem(n_ff), s>>>(
+    k_gemm_down<<<dim3(n_embd / GM_ROWS, maxt), DN_ALL_THREADS, dn_smem(n_ff), s>>>(
         src, at, g.off, g.cnt, g.tiles, g.n_tiles, n_embd, n_ff, ypair, err);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     return launch_combine(ypair, g.pair_pos, w, n_tok, k, n_embd, resid, y, s);
