@@ -375,7 +375,8 @@ __device__ __forceinline__ void deq_q6k_quarter(const uint32_t (&src)[8], const 
 #pragma unroll
     for (int c = 0; c < 4; ++c) {                      // l = 8c .. 8c+7
         const int g = (c >> 1) + 2 * q;                // scale byte (l / 16) + 2q
-        const float ws = d * (float)(int8_t)((sc[g >> 2] >> (8 * (g & 3))) & 0xFFu);
+        const uint32_t scw = (g >> 2) ? sc[1] : sc[0];   // a select, not an indexed (local) array
+        const float ws = d * (float)(int8_t)((scw >> (8 * (g & 3))) & 0xFFu);
         uint32_t o[4];
 #pragma unroll
         for (int wi = 0; wi < 2; ++wi) {
