@@ -300,6 +300,26 @@ __global__ void __launch_bounds__(256, 2) k_gate_up_grouped(
             const float other = __shfl_down_sync(MOE_FULL, sum, 8);
             if (lane == 0) act_s[0][r] = silu_mul(sum, other);
             if (lane == 16 && np == 2) act_s[1][r] = silu_mul(sum, other);
+        } else if (np <= 4) {
+            // three or four pairs: the eight sums by warp_sum8_t (bit-identical)
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                float g = 0.0f, up = 0.0f;
+                if (on && j < np) {
+                    ActQ4 a;
+                    load_act_q4_unit(a, xq_s + (size_t)j * xrow + lane * PAD_U64, xd_s + j * nblk,
+                                     xs_s + j * nblk, 2 * lane);
+                    g += q4k_dec_compute(dg, a);
+                    up += q4k_dec_compute(du, a);
+                }
+                v[j] = g;
+                v[4 + j] = up;
+            }
+            const float sum = warp_sum8_t(v, lane);            // lane l: value l >> 2
+            const float other = __shfl_down_sync(MOE_FULL, sum, 16);   // lane l < 16: value 4 + (l >> 2)
+            if (lane < 16 && !(lane & 3) && (lane >> 2) < np)
+                act_s[lane >> 2][r] = silu_mul(sum, other);
         } else {
             float v[16];
 #pragma unroll

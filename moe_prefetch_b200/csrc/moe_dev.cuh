@@ -1076,6 +1076,21 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
+// Eight warp_sum's at once, bit for bit: lane l returns the sum of v[l >> 2].
+// 9 shuffles instead of 40.
+__device__ __forceinline__ float warp_sum8_t(const float (&v)[8], int lane) {
+    const bool u16 = (lane & 16) != 0, u8 = (lane & 8) != 0, u4 = (lane & 4) != 0;
+    float a[4], b[2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) a[i] = (u16 ? v[4 + i] : v[i]) + __shfl_xor_sync(MOE_FULL, u16 ? v[i] : v[4 + i], 16);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) b[i] = (u8 ? a[2 + i] : a[i]) + __shfl_xor_sync(MOE_FULL, u8 ? a[i] : a[2 + i], 8);
+    float c = (u4 ? b[1] : b[0]) + __shfl_xor_sync(MOE_FULL, u4 ? b[0] : b[1], 4);
+    c += __shfl_xor_sync(MOE_FULL, c, 2);
+    c += __shfl_xor_sync(MOE_FULL, c, 1);
+    return c;
+}
+
 // Four warp_sum's at once, bit for bit: the same pairs at every level (xor
 // 16, 8, 4, 2, 1; own value first), but each level exchanges only the sums a
 // lane still needs.  Lanes 0-7 return the sum of a, 8-15 of b, 16-23 of c,
