@@ -235,10 +235,19 @@ int moe_ep_combine(moe_ctx *ctx, const float *y_rows, const int32_t *pos, const 
  * also frees the old scratch, and cudaFree waits for the whole device.  This
  * variant never does either.
  *
- * Arguments, results and error behaviour are those of moe_layer_forward.  The
- * only difference is where the scratch lives: the router ids/weights and the
- * gate/up activations go to one static device array of
- * MOE_NOALLOC_SCRATCH_BYTES per device, built into the library.
+ * Arguments and results are those of moe_layer_forward, with two
+ * differences:
+ *  - contexts with a shared expert (moe_cfg.n_shared = 1) are refused with
+ *    MOE_ERR_UNSUPPORTED;
+ *  - a batch (n_tok > 1) always runs the per-pair kernels, which read an
+ *    expert's rows once per routed (token, expert) pair, where
+ *    moe_layer_forward groups the pairs by expert and reads them once per
+ *    tile.  The results are the same bits; a batch is slower (the measured
+ *    figure for 32 tokens is in the design notes).  n_tok = 1 is the same
+ *    launch sequence in both.
+ * The scratch lives in one static device array of MOE_NOALLOC_SCRATCH_BYTES
+ * per device, built into the library: the router ids/weights and the gate/up
+ * activations.
  *
  * Limit: a call needs 2 * round_up(4 * n_tok * n_used, 256) +
  * 4 * n_tok * n_used * n_ff bytes of that array.  For n_used 8 and n_ff 768
@@ -274,6 +283,9 @@ typedef struct moe_decode_dbg {
     float    *w;
     float    *y;
     uint64_t *prof;
+    int32_t   starve;   /* tests of the watchdog only: r + 1 makes rank r's first
+                           activation wait target one signal more than its
+                           producers give, so that it can only run out; 0 off */
 } moe_decode_dbg;
 
 /* Batch-1 decode of n_tok tokens, strictly one after another, through all
@@ -289,6 +301,16 @@ int moe_decode(moe_ctx *ctx, const float *h, float *out, int n_tok,
  * all on `stream`, synchronised before returning. */
 int moe_decode_host(moe_ctx *ctx, const float *h_host, float *out_host, int n_tok,
                     void *stream);
+
+/* Limit of every device-side wait of the decode kernel (grid barrier,
+ * activation signals, copy completions), in nanoseconds; 0 restores the
+ * default of 2 s.  When a wait runs out, the kernel sets the error word and an
+ * abort flag that ends every CTA, waits (bounded) for its own copies, and
+ * returns; moe_decode_host / moe_sync then report MOE_ERR_TIMEOUT once, and the
+ * context stays usable.  The reference's counterpart is the sidecar's
+ * deadline, whose expiry makes llama_context::decode return -3
+ * (patches/0009:652-655; cpp/test-moe-sidecar.cpp tests the dead host). */
+int moe_set_wait_limit(moe_ctx *ctx, uint64_t ns);
 
 /* Synchronise `stream` and report what the kernels flagged since the last
  * call (MOE_ERR_TIMEOUT: a bounded device wait gave up; MOE_ERR_DEVICE: an

@@ -48,7 +48,7 @@ class MoeLayerInfo(C.Structure):
 
 class MoeDecodeDbg(C.Structure):
     _fields_ = [("x", C.c_void_p), ("ids", C.c_void_p), ("w", C.c_void_p), ("y", C.c_void_p),
-                ("prof", C.c_void_p)]
+                ("prof", C.c_void_p), ("starve", C.c_int32)]
 
 
 P = C.c_void_p
@@ -75,6 +75,7 @@ SIGNATURES = {
     "moe_decode": (I, [P, P, P, I, P, P]),
     "moe_decode_host": (I, [P, P, P, I, P]),
     "moe_sync": (I, [P, P]),
+    "moe_set_wait_limit": (I, [P, C.c_uint64]),
     "moe_decode_info": (I, [P, P, I]),
     "moe_observe": (I, [P, I, P, I, I, P]),
     "moe_step": (I, [P, P]),

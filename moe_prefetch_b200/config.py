@@ -175,45 +175,52 @@ def format_slot_profile(caps):
 
 def greedy_allocate_bytes(per_layer_miss8, grid, n_layers, uniform_cap, frozen_layers,
                           expert_bytes):
-    """Byte-priced greedy slot allocation (experiments/p7_slot_allocation.py:144-185):
-    the budget is the VRAM the uniform allocation uses; repeatedly give the next
-    grid step to the layer whose step removes the most misses per byte (ties to
-    the lower layer), while the budget lasts.  Returns (caps, used, budget)."""
-    known = [b for b in expert_bytes if b]
-    mean_b = sum(known) / len(known)
-    cost = [b or mean_b for b in expert_bytes]
-    budget = sum(uniform_cap * cost[L] for L in range(n_layers))
-    idx = [0] * n_layers
-    cap = [grid[0]] * n_layers
-    frozen = set(frozen_layers)
-    for L in frozen:
-        cap[L] = uniform_cap
-    remaining = budget - sum(cap[L] * cost[L] for L in range(n_layers))
+    """Byte-priced greedy slot allocation, the reference's
+    experiments/p7_slot_allocation.py:144-185 (greedy_allocate_bytes).
 
-    def step(L):
-        if L in frozen or idx[L] + 1 >= len(grid):
-            return -1.0, 0.0
-        i = idx[L]
-        d_slots = grid[i + 1] - grid[i]
-        d_miss = per_layer_miss8[grid[i]][L] - per_layer_miss8[grid[i + 1]][L]
-        return d_miss / (d_slots * cost[L]), d_slots * cost[L]
+    Each layer starts at the bottom of `grid` (frozen layers sit at
+    uniform_cap and never move).  The byte budget is what uniform_cap slots in
+    every layer would take.  A move lifts one layer to its next grid size; its
+    value is the drop in that layer's misses (per_layer_miss8[slots][layer])
+    per byte it costs.  The most valuable move is made while it fits in what
+    is left of the budget (ties: lower layer first); a move that does not fit
+    is dropped for good, as in the reference.  A layer with no recorded
+    expert size is priced at the mean of the known sizes.
+    Returns (caps, bytes used, budget)."""
+    sized = [b for b in expert_bytes if b]
+    fallback = sum(sized) / len(sized)
+    price = [b if b else fallback for b in expert_bytes]        # bytes per slot
+    budget = sum(uniform_cap * price[il] for il in range(n_layers))
+    pinned = set(frozen_layers)
+    level = [0] * n_layers                                       # grid position
+    caps = [uniform_cap if il in pinned else grid[0] for il in range(n_layers)]
+    left = budget - sum(caps[il] * price[il] for il in range(n_layers))
 
-    active = {}
-    for L in range(n_layers):
-        v, _ = step(L)
-        if v > 0:
-            active[L] = v
-    while active:
-        L = min(active, key=lambda q: (-active[q], q))
-        del active[L]
-        v, c = step(L)
-        if v <= 0 or c > remaining:
+    def next_move(il):
+        """(misses saved per byte, bytes) of lifting layer il one grid step,
+        or None at the top of the grid or for a frozen layer."""
+        if il in pinned or level[il] + 1 >= len(grid):
+            return None
+        lo, hi = grid[level[il]], grid[level[il] + 1]
+        nbytes = (hi - lo) * price[il]
+        return (per_layer_miss8[lo][il] - per_layer_miss8[hi][il]) / nbytes, nbytes
+
+    open_moves = {}                                              # layer -> value
+    for il in range(n_layers):
+        mv = next_move(il)
+        if mv is not None and mv[0] > 0:
+            open_moves[il] = mv[0]
+    while open_moves:
+        il = max(open_moves, key=lambda q: (open_moves[q], -q))
+        del open_moves[il]
+        _, nbytes = next_move(il)
+        if nbytes > left:
             continue
-        idx[L] += 1
-        cap[L] = grid[idx[L]]
-        remaining -= c
-        v, c = step(L)
-        if v > 0:
-            active[L] = v
-    used = sum(cap[L] * cost[L] for L in range(n_layers))
-    return cap, used, budget
+        level[il] += 1
+        caps[il] = grid[level[il]]
+        left -= nbytes
+        mv = next_move(il)
+        if mv is not None and mv[0] > 0:
+            open_moves[il] = mv[0]
+    used = sum(caps[il] * price[il] for il in range(n_layers))
+    return caps, used, budget

@@ -305,6 +305,7 @@ extern "C" int moe_create(const moe_cfg *cfg, moe_ctx **out) {
         p.acc = c->acc;
         p.abort_flag = c->abort_flag; p.err = c->err; p.st = c->st;
         p.observe = 1; p.delta = g.cache_prior; p.rms_eps = 1e-6f;
+        p.wait_ns = MOE_TIMEOUT_NS; p.starve = 0;
     }
     // uploader
     {
@@ -838,6 +839,8 @@ extern "C" int moe_decode(moe_ctx *c, const float *h, float *out, int n_tok,
     p.dbg_w = dbg ? dbg->w : nullptr;
     p.dbg_y = dbg ? dbg->y : nullptr;
     p.prof = dbg ? dbg->prof : nullptr;
+    p.starve = dbg ? dbg->starve : 0;
+    if (p.starve < 0 || p.starve > p.kx) return fail(c, MOE_ERR_ARG, "moe_decode: dbg starve out of range");
     if (p.dbg_ids && !p.dbg_w) return fail(c, MOE_ERR_ARG, "moe_decode: dbg ids without w");
     CK(cudaMemsetAsync(c->bar, 0, 64, s));
     CK(cudaMemsetAsync(c->abort_flag, 0, 64, s));
@@ -869,8 +872,18 @@ extern "C" int moe_decode_host(moe_ctx *c, const float *h_host, float *out_host,
     CK(cudaStreamSynchronize(s));
     int e = 0;
     CK(cudaMemcpy(&e, c->err, sizeof(int), cudaMemcpyDeviceToHost));
-    if (e & MOE_DEV_ERR_TIMEOUT) return fail(c, MOE_ERR_TIMEOUT, "a device-side wait timed out");
-    if (e & MOE_DEV_ERR_INDEX) return fail(c, MOE_ERR_DEVICE, "a kernel saw an out-of-range index");
+    if (e) {
+        // reported once: the next call starts from a clean error word
+        CK(cudaMemset(c->err, 0, sizeof(int)));
+        if (e & MOE_DEV_ERR_TIMEOUT) return fail(c, MOE_ERR_TIMEOUT, "a device-side wait timed out");
+        return fail(c, MOE_ERR_DEVICE, "a kernel saw an out-of-range index");
+    }
+    return MOE_OK;
+}
+
+extern "C" int moe_set_wait_limit(moe_ctx *c, uint64_t ns) {
+    if (!c) return MOE_ERR_ARG;
+    c->dp.wait_ns = ns ? ns : MOE_TIMEOUT_NS;
     return MOE_OK;
 }
 

@@ -58,7 +58,7 @@ __device__ __forceinline__ void red_release_add(unsigned *p, unsigned v) {
 // Grid barrier in two halves, so that a CTA can do work that no other CTA
 // waits for between its arrival and its wait: every CTA adds 1 (release),
 // then waits (acquire) until the counter reaches epoch * gridDim.x.  Bounded
-// by MOE_TIMEOUT_NS; gives up on the shared abort flag.
+// by p.wait_ns; gives up on the shared abort flag.
 __device__ __forceinline__ void grid_arrive(const DecodeParams &p, unsigned &epoch) {
     epoch += 1;
     __syncthreads();
@@ -73,7 +73,7 @@ __device__ __forceinline__ bool grid_wait(const DecodeParams &p, unsigned epoch,
             const uint64_t t0 = gtimer();
             while (ld_acquire_u32(p.bar) < target) {
                 if (ld_relaxed_i32(p.abort_flag)) { ok = 0; break; }
-                if (gtimer() - t0 > MOE_TIMEOUT_NS) {
+                if (gtimer() - t0 > p.wait_ns) {
                     atomicOr(p.err, MOE_DEV_ERR_TIMEOUT);
                     atomicExch(p.abort_flag, 1);
                     ok = 0;
@@ -321,7 +321,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
     }
     pend_wt = pend_tbl = true;
     for (int i = tid; i < rows; i += DEC_THREADS) rown[i] = __ldg(p.h_in + h0 + i);
-    if (!mbar_wait(&mb[MB_WT], 0)) {
+    if (!mbar_wait(&mb[MB_WT], 0, p.wait_ns)) {
         if (tid == 0) { atomicOr(p.err, MOE_DEV_ERR_TIMEOUT); atomicExch(p.abort_flag, 1); }
     }
     pend_wt = false;
@@ -369,7 +369,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                 const float S = s_sumsq;
                 const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(S, (float)H), p.rms_eps)));
                 if (pend_tbl) {
-                    if (!mbar_wait(&mb[MB_TBL], tbl_par)) {
+                    if (!mbar_wait(&mb[MB_TBL], tbl_par, p.wait_ns)) {
                         if (tid == 0) { atomicOr(p.err, MOE_DEV_ERR_TIMEOUT); s_bad = 1; }
                     }
                     pend_tbl = false;
@@ -446,7 +446,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                     // The down rows are read only after the second grid barrier: the
                     // gate/up pieces get the copy engine and HBM to themselves first.
                     __syncwarp();
-                    if (lane < nch) mbar_wait(&mb[MB_GU + lane], par);
+                    if (lane < nch) mbar_wait(&mb[MB_GU + lane], par, p.wait_ns);
                     __syncwarp();
                     if (lane >= 8 && lane < 8 + KX) {
                         const int kk = lane - 8;
@@ -504,11 +504,11 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                     while (qA + 1 < nch && lA >= ch_off[qA + 1]) ++qA;
                     while (hasB && qB + 1 < nch && lB >= ch_off[qB + 1]) ++qB;
                     if (!(waited & (1 << qA))) {
-                        if (!mbar_wait(&mb[MB_GU + qA], par)) { fail = true; break; }
+                        if (!mbar_wait(&mb[MB_GU + qA], par, p.wait_ns)) { fail = true; break; }
                         waited |= 1 << qA;
                     }
                     if (hasB && !(waited & (1 << qB))) {
-                        if (!mbar_wait(&mb[MB_GU + qB], par)) { fail = true; break; }
+                        if (!mbar_wait(&mb[MB_GU + qB], par, p.wait_ns)) { fail = true; break; }
                         waited |= 1 << qB;
                     }
                     float gA = 0.0f, uA = 0.0f, gB = 0.0f, uB = 0.0f;
@@ -547,7 +547,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
             if (warp == DEC_WARPS - 1 && (L + 1 < NL || t + 1 < p.n_tok)) {
                 // the next layer's table was queued with this layer's copies
                 const int nl = L + 1 < NL ? L + 1 : 0;
-                if (mbar_wait(&mb[MB_TBL], tbl_par))
+                if (mbar_wait(&mb[MB_TBL], tbl_par, p.wait_ns))
                     prefetch_next_l2(p.layers[nl], prev + (size_t)nl * MOE_KMAX, tbl, K, KX, E,
                                      p.gate_bytes, c, G, lane);
             }
@@ -563,13 +563,16 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                 const int w0 = kk * DEC_WARPS / KX, nw = (kk + 1) * DEC_WARPS / KX - w0, gw = warp - w0;
                 const unsigned gthreads = (unsigned)nw * 32u;
                 if (gw == 0 && lane == 0) {
-                    const unsigned target = (unsigned)(use + 1) * (unsigned)p.n_prod[kk];
+                    // p.starve = r + 1 (a test of the watchdog): rank r's first wait
+                    // targets one signal more than its producers give
+                    const unsigned target = (unsigned)(use + 1) * (unsigned)p.n_prod[kk] +
+                                            (use == 0 && p.starve == kk + 1 ? 1u : 0u);
                     bool ok = true;
                     if (ld_acquire_u32(p.ready + kk * READY_STRIDE) < target) {
                         const uint64_t t0 = gtimer();
                         while (ld_acquire_u32(p.ready + kk * READY_STRIDE) < target) {
                             if (ld_relaxed_i32(p.abort_flag)) { ok = false; break; }
-                            if (gtimer() - t0 > MOE_TIMEOUT_NS) {
+                            if (gtimer() - t0 > p.wait_ns) {
                                 atomicOr(p.err, MOE_DEV_ERR_TIMEOUT);
                                 atomicExch(p.abort_flag, 1);
                                 ok = false;
@@ -602,7 +605,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                                       : ld.hdown + (size_t)s_ids[kk] * p.down_bytes;
                     const uintptr_t a0 = reinterpret_cast<uintptr_t>(base + (size_t)h0 * drow);
                     const uint8_t *rws = dn + (size_t)kk * p.dn_stride + (int)(a0 & 15);
-                    const bool dn_ok = __all_sync(MOE_FULL, mbar_wait(&mb[MB_DN + kk], par));
+                    const bool dn_ok = __all_sync(MOE_FULL, mbar_wait(&mb[MB_DN + kk], par, p.wait_ns));
                     if (!dn_ok && lane == 0) { atomicOr(p.err, MOE_DEV_ERR_TIMEOUT); atomicExch(p.abort_flag, 1); s_fail = 1; }
                     for (int rg = gw; rg < nrg && dn_ok; rg += nw) {
                         if constexpr (Q6_T) {
@@ -659,7 +662,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
             PROF(11)
             // partials of the next (token, layer) over this CTA's rows
             if (pend_wt) {
-                if (!mbar_wait(&mb[MB_WT], wt_par)) {
+                if (!mbar_wait(&mb[MB_WT], wt_par, p.wait_ns)) {
                     if (tid == 0) { atomicOr(p.err, MOE_DEV_ERR_TIMEOUT); atomicExch(p.abort_flag, 1); }
                 }
                 __syncthreads();
@@ -678,12 +681,12 @@ abort:
     {
         const uint32_t par = (uint32_t)(use & 1);
         if (tid == 0) {
-            if (pend_wt) mbar_wait(&mb[MB_WT], wt_par);
-            if (pend_tbl) mbar_wait(&mb[MB_TBL], tbl_par);
+            if (pend_wt) mbar_wait(&mb[MB_WT], wt_par, p.wait_ns);
+            if (pend_tbl) mbar_wait(&mb[MB_TBL], tbl_par, p.wait_ns);
             if (pend_gu)
-                for (int q = 0; q < nch; ++q) mbar_wait(&mb[MB_GU + q], par);
+                for (int q = 0; q < nch; ++q) mbar_wait(&mb[MB_GU + q], par, p.wait_ns);
             if (pend_dn)
-                for (int kk = 0; kk < KX; ++kk) mbar_wait(&mb[MB_DN + kk], par);
+                for (int kk = 0; kk < KX; ++kk) mbar_wait(&mb[MB_DN + kk], par, p.wait_ns);
             if (c == 0) p.st.g[G_CLOCK] = s_clock;
         }
         __syncthreads();

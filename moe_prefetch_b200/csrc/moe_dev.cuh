@@ -1162,12 +1162,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait: false after MOE_TIMEOUT_NS.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+// Bounded wait: false after limit_ns (MOE_TIMEOUT_NS unless given).
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
+                                          uint64_t limit_ns = MOE_TIMEOUT_NS) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = gtimer();
     while (!mbar_try_wait(bar, parity)) {
-        if (gtimer() - t0 > MOE_TIMEOUT_NS) return false;
+        if (gtimer() - t0 > limit_ns) return false;
     }
     return true;
 }

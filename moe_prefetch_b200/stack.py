@@ -218,11 +218,12 @@ class MoeStack:
                  "moe_layer_forward_noalloc")
         return y
 
-    def decode(self, h, out=None, debug=False, stream=None, profile=False):
+    def decode(self, h, out=None, debug=False, stream=None, profile=False, starve=0):
         """Batch-1 decode of h [n_tok, n_embd] (device) through every layer,
         one token after another; returns out (and the per-layer dumps when
         debug; with profile, dumps["prof"] holds the per-CTA phase timestamps
-        [n_tok, n_layers, 12, grid] in ns)."""
+        [n_tok, n_layers, 12, grid] in ns).  starve = r + 1 is for tests of
+        the watchdog: rank r's first activation wait can then only run out."""
         h = h.contiguous()
         n_tok = h.shape[0]
         out = torch.empty_like(h) if out is None else out
@@ -242,7 +243,9 @@ class MoeStack:
                 dumps["prof"] = torch.zeros(n_tok, L, 12, grid, dtype=torch.int64, device=h.device)
                 prof_ptr = dumps["prof"].data_ptr()
             dbg = MoeDecodeDbg(dumps["x"].data_ptr(), dumps["ids"].data_ptr(),
-                               dumps["w"].data_ptr(), dumps["y"].data_ptr(), prof_ptr)
+                               dumps["w"].data_ptr(), dumps["y"].data_ptr(), prof_ptr, starve)
+        elif starve:
+            dbg = MoeDecodeDbg(None, None, None, None, None, starve)
         self._ck(self.lib.moe_decode(self.ctx, _ptr(h), _ptr(out), n_tok,
                                      C.byref(dbg) if dbg is not None else None, _stream(stream)),
                  "moe_decode")
@@ -257,6 +260,10 @@ class MoeStack:
 
     def sync(self, stream=None):
         self._ck(self.lib.moe_sync(self.ctx, _stream(stream)), "moe_sync")
+
+    def set_wait_limit(self, ns):
+        """Limit of the decode kernel's device waits in ns (0: the 2 s default)."""
+        self._ck(self.lib.moe_set_wait_limit(self.ctx, int(ns)), "moe_set_wait_limit")
 
     def decode_info(self):
         out = np.zeros(5, np.int32)

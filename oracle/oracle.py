@@ -13,6 +13,13 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "liboracle.so")
 REF_PRED_PATH = os.path.join(HERE, "_ref", "libref_predictor.so")
 
+
+def reference_dir():
+    """Where the reference project's tree is read from (test set-up only):
+    $MOE_REFERENCE_DIR, else a `reference` directory beside this repository."""
+    return os.environ.get("MOE_REFERENCE_DIR") or os.path.join(
+        os.path.dirname(os.path.dirname(HERE)), "reference")
+
 QTYPE_Q4_K = 12
 QTYPE_Q6_K = 14
 Q4K_BYTES = 144
@@ -25,8 +32,9 @@ def build(force=False):
     tree is present) with oracle/Makefile."""
     if force or not os.path.exists(LIB_PATH):
         subprocess.check_call(["make", "-s", "-C", HERE])
-    if os.path.isdir("/root/reference/cpp") and (force or not os.path.exists(REF_PRED_PATH)):
-        subprocess.check_call(["make", "-s", "-C", HERE, "ref"])
+    ref = reference_dir()
+    if os.path.isdir(os.path.join(ref, "cpp")) and (force or not os.path.exists(REF_PRED_PATH)):
+        subprocess.check_call(["make", "-s", "-C", HERE, "ref", "REF=" + ref])
 
 
 _lib = None

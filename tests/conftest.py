@@ -8,7 +8,9 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-REFERENCE = "/root/reference"
+from oracle.oracle import reference_dir  # noqa: E402
+
+REFERENCE = reference_dir()
 
 # Output tolerances of north_star, against the fp32-accumulated oracle
 REL_L2_TOL = 1e-3

@@ -26,7 +26,9 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
-REF = "/root/reference"
+from oracle.oracle import reference_dir  # noqa: E402
+
+REF = reference_dir()
 
 
 def gguf_fixture():

@@ -6,6 +6,8 @@ import os
 
 import pytest
 
+from conftest import REFERENCE
+
 from moe_prefetch_b200.config import (MoeCacheConfig, format_slot_profile,
                                       greedy_allocate_bytes, parse_slot_profile)
 
@@ -89,7 +91,7 @@ def test_greedy_oracle_restatement_matches(oracle_lib):
 
 
 def test_greedy_against_live_reference():
-    path = "/root/reference/experiments/p7_slot_allocation.py"
+    path = os.path.join(REFERENCE, "experiments", "p7_slot_allocation.py")
     if not os.path.exists(path):
         pytest.skip("reference tree not present")
     import importlib.util

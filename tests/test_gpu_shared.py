@@ -91,3 +91,16 @@ def test_shared_must_be_set(c4):
             st.layer_forward(0, torch.zeros(1, H, device="cuda"))
     finally:
         st.close()
+
+
+def test_noalloc_refuses_shared_expert(c4):
+    """The allocation-free layer entry point does not run shared experts: a
+    context with n_shared = 1 gets MOE_ERR_UNSUPPORTED, and nothing is written."""
+    from moe_prefetch_b200._lib import MoeError
+    st, _ = c4
+    x = torch.from_numpy(rms_norm(np.random.default_rng(3).standard_normal((2, H)))).cuda()
+    y = torch.full((2, H), 7.0, device="cuda")
+    with pytest.raises(MoeError) as ei:
+        st.layer_forward_noalloc(0, x, y)
+    assert ei.value.code == -4
+    assert torch.all(y == 7.0)

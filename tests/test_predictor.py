@@ -12,7 +12,9 @@ from moe_prefetch_b200.predictor import MoePredictor, MoepError
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 GOLD = os.path.join(HERE, "golden")
-MODELS = "/root/reference/models"
+from conftest import REFERENCE  # noqa: E402
+
+MODELS = os.path.join(REFERENCE, "models")
 
 
 def test_scores_match_reference_golden():
