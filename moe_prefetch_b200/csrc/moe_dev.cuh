@@ -663,6 +663,20 @@ __device__ __forceinline__ void q4k_sm_pair(uint32_t w0, uint32_t w1, uint32_t w
     m1 = (int)__byte_perm(M, 0u, 0x4440u | (b + 1u));
 }
 
+// The float steps of one Q4_K unit from its integer sums (slo, shi: the two
+// sub-blocks' dots with the activations; sc / m: their 6-bit scales and mins),
+// with every rounding explicit so that no contraction choice of the compiler
+// can change the bits:
+//   acc = fma(sc1 * shi, d1, (sc0 * slo) * d0),  mm = fma(m1, s1, m0 * s0),
+//   v   = fma(d, acc, -(dmin * mm)).
+// Every GEMV path and the oracle's kernel-order rows use exactly this.
+__device__ __forceinline__ float q4k_unit_float(int slo, int shi, int sc0, int m0, int sc1, int m1,
+                                                float d, float dmin, const ActQ4 &a) {
+    const float acc = __fmaf_rn((float)(sc1 * shi), a.d1, __fmul_rn((float)(sc0 * slo), a.d0));
+    const float mm = __fmaf_rn((float)m1, a.s1, __fmul_rn((float)m0, a.s0));
+    return __fmaf_rn(d, acc, -__fmul_rn(dmin, mm));
+}
+
 // The bytes of one unit of a Q4_K row: the block header (d, dmin, scales)
 // and the 32 quant bytes of sub-block pair p.
 struct Q4Unit {
@@ -689,9 +703,7 @@ __device__ __forceinline__ float q4k_unit_compute(const Q4Unit &u, int p, const 
     int sc0, m0, sc1, m1;
     q4k_sm_pair(u.hdr.y, u.hdr.z, u.hdr.w, p, sc0, m0, sc1, m1);
     const float d = h2f(u.hdr.x), dmin = h2f(u.hdr.x >> 16);
-    const float acc = (float)(sc0 * slo) * a.d0 + (float)(sc1 * shi) * a.d1;
-    const float mm = (float)m0 * a.s0 + (float)m1 * a.s1;
-    return d * acc - dmin * mm;
+    return q4k_unit_float(slo, shi, sc0, m0, sc1, m1, d, dmin, a);
 }
 
 // A Q4_K unit decoded once for many activation rows: the nibble words, the
@@ -723,9 +735,7 @@ __device__ __forceinline__ float q4k_dec_compute(const Q4UnitDec &u, const ActQ4
         slo = __dp4a(u.lo[i], a.lo[i], slo);
         shi = __dp4a(u.hi[i], a.hi[i], shi);
     }
-    const float acc = (float)(u.sc0 * slo) * a.d0 + (float)(u.sc1 * shi) * a.d1;
-    const float mm = (float)u.m0 * a.s0 + (float)u.m1 * a.s1;
-    return u.d * acc - u.dmin * mm;
+    return q4k_unit_float(slo, shi, u.sc0, u.m0, u.sc1, u.m1, u.d, u.dmin, a);
 }
 
 // Partial dot of one unit of a Q4_K row (16-byte aligned block pointer `blk`
@@ -734,73 +744,6 @@ __device__ __forceinline__ float q4k_unit_dot(const uint8_t *blk, int p, const A
     Q4Unit u;
     q4k_unit_load(blk, p, u);
     return q4k_unit_compute(u, p, a);
-}
-
-// ---------------------------------------------------------------------------
-// Q6_K x Q8_1
-// ---------------------------------------------------------------------------
-
-// 8 bytes at a 2-byte-aligned address, through aligned 32-bit loads and
-// funnel shifts (Q6_K blocks are 210 bytes, so rows are only 2-byte aligned).
-// Only the words that hold requested bytes are read: never past ptr + 8.
-__device__ __forceinline__ uint2 ld8_a2(const uint8_t *ptr) {
-    const uintptr_t a = reinterpret_cast<uintptr_t>(ptr);
-    const uint32_t *p = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
-    const uint32_t sh = (uint32_t)(a & 2) * 8u;
-    const uint32_t w0 = p[0], w1 = p[1];
-    const uint32_t w2 = sh ? p[2] : 0u;
-    return make_uint2(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh));
-}
-
-// Activations of one lane's Q6_K unit (super-block sb, half h, l in
-// [8j, 8j+8)): for m = 0..3 the 8 int8 values at 128h + 32m + 8j, and the d of
-// their Q8_1 block.
-struct ActQ6 {
-    int q[4][2];
-    float d[4];
-};
-
-__device__ __forceinline__ void load_act_q6(ActQ6 &a, const int8_t *q, const float *d, int sb,
-                                            int h, int j) {
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-        const int e = 256 * sb + 128 * h + 32 * m + 8 * j;
-        const int2 v = *reinterpret_cast<const int2 *>(q + e);
-        a.q[m][0] = v.x;
-        a.q[m][1] = v.y;
-        a.d[m] = d[e >> 5];
-    }
-}
-
-__device__ __forceinline__ float q6k_unit_dot(const uint8_t *blk, int h, int j, const ActQ6 &a) {
-    const uint2 lo = ld8_a2(blk + 64 * h + 8 * j);
-    const uint2 hi = ld8_a2(blk + 64 * h + 32 + 8 * j);
-    const uint2 qh = ld8_a2(blk + 128 + 32 * h + 8 * j);
-    const uint2 scw = ld8_a2(blk + 192 + 8 * h);
-    const float d = h2f(*reinterpret_cast<const uint16_t *>(blk + 208));
-    const int c = j >= 2 ? 1 : 0;
-    const uint32_t L[2] = {lo.x, lo.y}, Hh[2] = {hi.x, hi.y}, Q[2] = {qh.x, qh.y};
-    int is[4] = {0, 0, 0, 0};
-#pragma unroll
-    for (int wi = 0; wi < 2; ++wi) {
-        const uint32_t v0 = (L[wi] & 0x0F0F0F0Fu) | ((Q[wi] << 4) & 0x30303030u);
-        const uint32_t v1 = (Hh[wi] & 0x0F0F0F0Fu) | ((Q[wi] << 2) & 0x30303030u);
-        const uint32_t v2 = ((L[wi] >> 4) & 0x0F0F0F0Fu) | (Q[wi] & 0x30303030u);
-        const uint32_t v3 = ((Hh[wi] >> 4) & 0x0F0F0F0Fu) | ((Q[wi] >> 2) & 0x30303030u);
-        is[0] = __dp4a((int)__vsub4(v0, 0x20202020u), a.q[0][wi], is[0]);
-        is[1] = __dp4a((int)__vsub4(v1, 0x20202020u), a.q[1][wi], is[1]);
-        is[2] = __dp4a((int)__vsub4(v2, 0x20202020u), a.q[2][wi], is[2]);
-        is[3] = __dp4a((int)__vsub4(v3, 0x20202020u), a.q[3][wi], is[3]);
-    }
-    float acc = 0.0f;
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-        const int pos = c + 2 * m;   // scale byte index within the 8 loaded
-        const uint32_t wsel = pos < 4 ? scw.x : scw.y;
-        const int sc = (int)(int8_t)((wsel >> (8 * (pos & 3))) & 0xFF);
-        acc += (float)(sc * is[m]) * a.d[m];
-    }
-    return d * acc;
 }
 
 // ---------------------------------------------------------------------------
@@ -882,10 +825,10 @@ __device__ __forceinline__ float q6k_half_compute(const Q6Half &w, const ActHalf
         const int g0 = 2 * m, g1 = 2 * m + 1;   // scale bytes within the 8 loaded
         const int s0 = (int)(int8_t)((w.sc[g0 >> 2] >> (8 * (g0 & 3))) & 0xFF);
         const int s1 = (int)(int8_t)((w.sc[g1 >> 2] >> (8 * (g1 & 3))) & 0xFF);
-        acc += (float)(s0 * is0) * a.d[m];
-        acc += (float)(s1 * is1) * a.d[m];
+        acc = __fmaf_rn((float)(s0 * is0), a.d[m], acc);
+        acc = __fmaf_rn((float)(s1 * is1), a.d[m], acc);
     }
-    return w.d * acc;
+    return __fmul_rn(w.d, acc);
 }
 
 // A Q6_K half decoded once for many activation rows: the signed 6-bit values
@@ -924,10 +867,10 @@ __device__ __forceinline__ float q6k_dec_compute(const Q6HalfDec &w, const ActHa
             if (i < 4) is0 = __dp4a(w.v[m][i], a.q[m][i], is0);
             else is1 = __dp4a(w.v[m][i], a.q[m][i], is1);
         }
-        acc += (float)(w.sc[2 * m] * is0) * a.d[m];
-        acc += (float)(w.sc[2 * m + 1] * is1) * a.d[m];
+        acc = __fmaf_rn((float)(w.sc[2 * m] * is0), a.d[m], acc);
+        acc = __fmaf_rn((float)(w.sc[2 * m + 1] * is1), a.d[m], acc);
     }
-    return w.d * acc;
+    return __fmul_rn(w.d, acc);
 }
 
 // load_act_half from a half-padded copy: the 128 int8 of the half at `qh`
@@ -1017,10 +960,10 @@ __device__ __forceinline__ float q6k_half_compute_u(const Q6Half &w, const ActHa
         const int g0 = 2 * m, g1 = 2 * m + 1;
         const int s0 = (int)(int8_t)((w.sc[g0 >> 2] >> (8 * (g0 & 3))) & 0xFF);
         const int s1 = (int)(int8_t)((w.sc[g1 >> 2] >> (8 * (g1 & 3))) & 0xFF);
-        acc += (float)(s0 * is0) * a.d[m];
-        acc += (float)(s1 * is1) * a.d[m];
+        acc = __fmaf_rn((float)(s0 * is0), a.d[m], acc);
+        acc = __fmaf_rn((float)(s1 * is1), a.d[m], acc);
     }
-    return w.d * acc;
+    return __fmul_rn(w.d, acc);
 }
 
 __device__ __forceinline__ float q6k_half_dot_u(const uint8_t *blk, int h, const ActHalfU &a) {

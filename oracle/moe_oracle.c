@@ -86,7 +86,7 @@ float or_f16_to_f32(uint16_t h) {
  * ln2 split into a 12-bit-trimmed head (n * LN2_HI exact for |n| < 2^12) and
  * a tail, then the degree-7 Taylor polynomial of e^r in Horner form (truncation
  * error < 6e-9 relative on the reduced range), then scaling by 2^n through the
- * exponent field.  The device copy (moe_prefetch_b200/csrc/moe_math.cuh) runs
+ * exponent field.  The device copy (moe_prefetch_b200/csrc/moe_dev.cuh) runs
  * the identical sequence of fp32 operations, so both give the same bits. */
 #define OR_LOG2E  0x1.715476p+0f      /* 1/ln2 rounded to fp32          */
 #define OR_LN2_HI 0x1.62e000p-1f      /* ln2 with the low 12 bits zero  */
@@ -369,6 +369,108 @@ double or_dot_q6_K_q8_1(const uint8_t *row, const int8_t *q, const float *d,
 }
 
 /* ------------------------------------------------------------------------ */
+/* the GEMV kernels' fp32 order                                              */
+/* ------------------------------------------------------------------------ */
+/* These restate, operation for operation, the fp32 arithmetic of the GEMV
+ * paths (per-pair, grouped and persistent decode kernels; their shared unit
+ * helpers in moe_prefetch_b200/csrc/moe_dev.cuh): the integer sums of a unit
+ * are exact, and every float rounding is written out with fmaf, so the row
+ * values, and with them the SiLU*up activations and their Q8_1 blocks, are
+ * the same bits.  The double versions above are the precision reference. */
+
+/* One Q4_K unit: super-block yb, sub-block pair p (64 weights), with that
+ * super-block's 256 activations qb and its 8 block d / s. */
+static float q4k_unit_f32(const uint8_t *yb, int p, const int8_t *qb, const float *db,
+                          const float *sb) {
+    const uint8_t *qs = yb + 16 + 32 * p;
+    int slo = 0, shi = 0;
+    for (int l = 0; l < 32; ++l) {
+        slo += (qs[l] & 0xF) * qb[64 * p + l];
+        shi += (qs[l] >> 4) * qb[64 * p + 32 + l];
+    }
+    int sc0, m0, sc1, m1;
+    q4k_scale_min(2 * p, yb + 4, &sc0, &m0);
+    q4k_scale_min(2 * p + 1, yb + 4, &sc1, &m1);
+    const float d = or_f16_to_f32((uint16_t)(yb[0] | (yb[1] << 8)));
+    const float dmin = or_f16_to_f32((uint16_t)(yb[2] | (yb[3] << 8)));
+    const float acc = fmaf((float)(sc1 * shi), db[2 * p + 1], (float)(sc0 * slo) * db[2 * p]);
+    const float mm = fmaf((float)m1, sb[2 * p + 1], (float)m0 * sb[2 * p]);
+    return fmaf(d, acc, -(dmin * mm));
+}
+
+/* The 32-lane xor butterfly (offsets 16, 8, 4, 2, 1, own value first) as lane
+ * 0 sees it. */
+static float lane_tree32(float *v) {
+    for (int off = 16; off >= 1; off >>= 1)
+        for (int l = 0; l < off; ++l) v[l] = v[l] + v[l + off];
+    return v[0];
+}
+
+/* A Q4_K row: unit u = 4 b + p sits on lane u mod 32, each lane adds its
+ * units to 0.0f in order, then the butterfly.  n % 256 == 0. */
+float or_dot_q4_K_q8_1_f32(const uint8_t *row, const int8_t *q, const float *d,
+                           const float *s, int64_t n) {
+    float lane[32];
+    for (int l = 0; l < 32; ++l) lane[l] = 0.0f;
+    const int units = (int)(n / OR_QK_K) * 4;
+    for (int u = 0; u < units; ++u) {
+        const int b = u >> 2;
+        lane[u & 31] = lane[u & 31] + q4k_unit_f32(row + (size_t)b * OR_Q4K_BYTES, u & 3,
+                                                   q + (size_t)b * OR_QK_K, d + 8 * b, s + 8 * b);
+    }
+    return lane_tree32(lane);
+}
+
+/* Half h of a Q6_K super-block (128 weights) with its 128 activations qh and
+ * their 4 block d: per quarter m the integer sums of the two 16-value scale
+ * groups, accumulated as fma(scale * isum, d_m, acc) in (m, group) order,
+ * times the block's d. */
+static float q6k_half_f32(const uint8_t *yb, int h, const int8_t *qa, const float *dh) {
+    const uint8_t *ql = yb + 64 * h, *qhb = yb + 128 + 32 * h;
+    const int8_t *sc = (const int8_t *)(yb + 192 + 8 * h);
+    float acc = 0.0f;
+    for (int m = 0; m < 4; ++m) {
+        int is[2] = {0, 0};
+        for (int l = 0; l < 32; ++l) {
+            const int lo = (ql[32 * (m & 1) + l] >> (4 * (m >> 1))) & 0xF;
+            const int hb = (qhb[l] >> (2 * m)) & 3;
+            is[l >> 4] += ((lo | (hb << 4)) - 32) * qa[32 * m + l];
+        }
+        acc = fmaf((float)(sc[2 * m] * is[0]), dh[m], acc);
+        acc = fmaf((float)(sc[2 * m + 1] * is[1]), dh[m], acc);
+    }
+    const float d = or_f16_to_f32((uint16_t)(yb[208] | (yb[209] << 8)));
+    return d * acc;
+}
+
+/* A Q6_K row: half-units u = 2 b + h on the lanes of a row group, summed by
+ * the group tree ((v0+v1)+(v2+v3))+((v4+v5)+(v6+v7)), absent lanes +0.
+ * n % 256 == 0, n <= 1024. */
+float or_dot_q6_K_q8_1_f32(const uint8_t *row, const int8_t *q, const float *d,
+                           const float *s, int64_t n) {
+    (void)s;
+    float v[8];
+    for (int u = 0; u < 8; ++u) v[u] = 0.0f;
+    const int units = (int)(n / OR_QK_K) * 2;
+    for (int u = 0; u < units && u < 8; ++u) {
+        const int b = u >> 1, h = u & 1;
+        v[u] = q6k_half_f32(row + (size_t)b * OR_Q6K_BYTES, h, q + (size_t)b * OR_QK_K + 128 * h,
+                            d + 8 * b + 4 * h);
+    }
+    return ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+}
+
+/* The kernels' combine: per output element an fp32 fma chain from 0 over the
+ * pairs in rank order. */
+static void or_combine_f32(const float *w, const float *rows, int k, int n_embd, float *y) {
+    for (int h = 0; h < n_embd; ++h) {
+        float acc = 0.0f;
+        for (int i = 0; i < k; ++i) acc = fmaf(w[i], rows[(size_t)i * n_embd + h], acc);
+        y[h] = acc;
+    }
+}
+
+/* ------------------------------------------------------------------------ */
 /* router                                                                    */
 /* ------------------------------------------------------------------------ */
 
@@ -517,8 +619,8 @@ void or_expert_row(const uint8_t *gate, const uint8_t *up, const uint8_t *down,
     or_quantize_q8_1(x, xq, xd, xs, n_embd);
     const size_t grb = row_bytes(OR_QTYPE_Q4_K, n_embd);
     for (int i = 0; i < n_ff; ++i) {
-        const float g = (float)or_dot_q4_K_q8_1(gate + i * grb, xq, xd, xs, n_embd);
-        const float u = (float)or_dot_q4_K_q8_1(up + i * grb, xq, xd, xs, n_embd);
+        const float g = or_dot_q4_K_q8_1_f32(gate + i * grb, xq, xd, xs, n_embd);
+        const float u = or_dot_q4_K_q8_1_f32(up + i * grb, xq, xd, xs, n_embd);
         act[i] = or_silu_mul(g, u);
     }
     if (act_out) memcpy(act_out, act, sizeof(float) * (size_t)n_ff);
@@ -526,8 +628,8 @@ void or_expert_row(const uint8_t *gate, const uint8_t *up, const uint8_t *down,
     const size_t drb = row_bytes(down_type, n_ff);
     for (int h = 0; h < n_embd; ++h) {
         out[h] = down_type == OR_QTYPE_Q6_K
-            ? (float)or_dot_q6_K_q8_1(down + h * drb, aq, ad, as, n_ff)
-            : (float)or_dot_q4_K_q8_1(down + h * drb, aq, ad, as, n_ff);
+            ? or_dot_q6_K_q8_1_f32(down + h * drb, aq, ad, as, n_ff)
+            : or_dot_q4_K_q8_1_f32(down + h * drb, aq, ad, as, n_ff);
     }
     free(xq); free(xd); free(xs); free(act); free(aq); free(ad); free(as);
 }
@@ -597,6 +699,11 @@ static void or_layer_impl(or_row_fn fn, const float *x, int n_tok, int n_embd, i
     }
     (void)n_threads;
     for (int t = 0; t < n_tok; ++t) {
+        if (fn == or_expert_row_q81) {   /* the GPU paths' combine */
+            or_combine_f32(w_out + (size_t)t * k, rows + (size_t)t * k * n_embd, k, n_embd,
+                           y_out + (size_t)t * n_embd);
+            continue;
+        }
         for (int h = 0; h < n_embd; ++h) {
             double acc = 0.0;
             for (int i = 0; i < k; ++i) {
@@ -625,13 +732,9 @@ void or_moe_experts(const float *x, int n_tok, int n_embd, int n_ff, int k,
                       x + (size_t)t * n_embd, rows + (size_t)tk * n_embd, NULL);
     }
     (void)n_threads;
-    for (int t = 0; t < n_tok; ++t) {
-        for (int h = 0; h < n_embd; ++h) {
-            double acc = 0.0;
-            for (int i = 0; i < k; ++i) acc += (double)w[t * k + i] * rows[((size_t)t * k + i) * n_embd + h];
-            y_out[(size_t)t * n_embd + h] = (float)acc;
-        }
-    }
+    for (int t = 0; t < n_tok; ++t)
+        or_combine_f32(w + (size_t)t * k, rows + (size_t)t * k * n_embd, k, n_embd,
+                       y_out + (size_t)t * n_embd);
     free(rows);
 }
 

@@ -70,6 +70,12 @@ double or_dot_q4_K_q8_1(const uint8_t *row, const int8_t *q, const float *d,
                         const float *s, int64_t n);
 double or_dot_q6_K_q8_1(const uint8_t *row, const int8_t *q, const float *d,
                         const float *s, int64_t n);
+/* the same dots in the GPU GEMV kernels' fp32 order (unit partials, lane
+ * butterfly / row-group tree): the bits those kernels produce.  Q6_K: n <= 1024. */
+float or_dot_q4_K_q8_1_f32(const uint8_t *row, const int8_t *q, const float *d,
+                           const float *s, int64_t n);
+float or_dot_q6_K_q8_1_f32(const uint8_t *row, const int8_t *q, const float *d,
+                           const float *s, int64_t n);
 
 /* ---- router -------------------------------------------------------------------- */
 /* logits = W x (canonical fp32 order), probs = softmax, sel = probs (+ prior),
@@ -103,7 +109,9 @@ void or_router_fused(const float *Wt, const float *r, int n_expert, int n_embd,
 /* ---- expert rows / layer ---------------------------------------------------------- */
 /* One expert: act = silu(gate x) * (up x) with x, act quantised to Q8_1;
  * out[n_embd] = down act.  gate/up: n_ff rows of n_embd (Q4_K);
- * down: n_embd rows of n_ff (Q6_K or Q4_K per down_type). act_out optional. */
+ * down: n_embd rows of n_ff (Q6_K or Q4_K per down_type). act_out optional.
+ * Every dot in the GPU GEMV kernels' fp32 order (or_dot_*_f32): the rows,
+ * activations and Q8_1 blocks are those kernels' bits. */
 void or_expert_row(const uint8_t *gate, const uint8_t *up, const uint8_t *down,
                    int down_type, int n_embd, int n_ff, const float *x,
                    float *out, float *act_out);
@@ -127,7 +135,9 @@ void or_moe_experts_f32(const float *x, int n_tok, int n_embd, int n_ff, int n_e
                         const int32_t *ids, const float *w, const uint8_t *gate,
                         const uint8_t *up, const uint8_t *down, int down_type, float *y_out,
                         int n_threads);
-/* The expert half alone: given ids / w [n_tok][k], y = sum_i w_i row(ids_i, x). */
+/* The expert half alone: given ids / w [n_tok][k], y = sum_i w_i row(ids_i, x),
+ * the sum an fp32 fma chain from 0 in rank order (the kernels' combine; also
+ * or_moe_layer's). */
 void or_moe_experts(const float *x, int n_tok, int n_embd, int n_ff, int k,
                     const int32_t *ids, const float *w, const uint8_t *gate,
                     const uint8_t *up, const uint8_t *down, int down_type, float *y_out,

@@ -72,6 +72,9 @@ def _declare(L):
     L.or_dot_q4_K_q8_1.restype = C.c_double
     L.or_dot_q6_K_q8_1.argtypes = [P, P, P, P, I64]
     L.or_dot_q6_K_q8_1.restype = C.c_double
+    for n in ("or_dot_q4_K_q8_1_f32", "or_dot_q6_K_q8_1_f32"):
+        getattr(L, n).argtypes = [P, P, P, P, I64]
+        getattr(L, n).restype = F32
     L.or_router.argtypes = [P, P, C.c_int, C.c_int, P, C.c_int, P, P, P, P]
     L.or_router_select.argtypes = [P, C.c_int, P, C.c_int, P, P, P]
     L.or_router_fused.argtypes = [P, P, C.c_int, C.c_int, P, P, C.c_int, F32, P, C.c_int, P, P,
@@ -174,9 +177,14 @@ def q8_K_roundtrip(x):
     return out
 
 
-def dot_q8_1(row, qtype, q, d, s):
+def dot_q8_1(row, qtype, q, d, s, order="f64"):
+    """One quantised row with Q8_1 activations: "f64" accumulates in double
+    (the precision reference), "kernel" in the GPU GEMV kernels' fp32 order."""
     row = _c(row, np.uint8)
-    fn = lib().or_dot_q4_K_q8_1 if qtype == QTYPE_Q4_K else lib().or_dot_q6_K_q8_1
+    if order == "kernel":
+        fn = lib().or_dot_q4_K_q8_1_f32 if qtype == QTYPE_Q4_K else lib().or_dot_q6_K_q8_1_f32
+    else:
+        fn = lib().or_dot_q4_K_q8_1 if qtype == QTYPE_Q4_K else lib().or_dot_q6_K_q8_1
     return fn(_p(row), _p(q), _p(d), _p(s), q.size)
 
 

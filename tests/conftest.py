@@ -34,6 +34,16 @@ def rel_l2(a, b):
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
 
+def assert_same_bits(a, b, what):
+    """The GEMV paths and the oracle's kernel-order rows (oracle
+    or_dot_*_f32, or_combine_f32) round every float step alike: outputs are
+    equal bit for bit, not only within the tolerance."""
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    diff = int((a.view(np.uint32) != b.view(np.uint32)).sum())
+    assert diff == 0, f"{what}: {diff} of {a.size} values differ in their bits"
+
+
 def rms_norm(h, eps=0.0):
     h = np.asarray(h, np.float32)
     return (h / np.sqrt((h.astype(np.float64) ** 2).mean(-1, keepdims=True) + eps)).astype(np.float32)
@@ -63,8 +73,9 @@ def check_decode_layer(oracle_lib, h_tok, dumps, t, L, W, gate, up, down, grid, 
     """One (token, layer) of a decode against the oracle: the residual before
     the layer is h + y_0 + ... + y_{L-1} in fp32 (the kernel's order); the
     fused router must give the same ids, weights and normalised x bit for bit;
-    the layer output must be within the output tolerance.  `shared`: the
-    layer's shared expert (gate, up, down bytes) or None."""
+    the layer output must be within the output tolerance and equal to the
+    oracle's kernel-order rows bit for bit.  `shared`: the layer's shared
+    expert (gate, up, down bytes) or None."""
     r = np.asarray(h_tok, np.float32).copy()
     ys = dumps["y"]
     for Lp in range(L):
@@ -79,6 +90,7 @@ def check_decode_layer(oracle_lib, h_tok, dumps, t, L, W, gate, up, down, grid, 
     ry = oracle_lib.moe_experts(rx[None], xi, xw, xg, xu, xd, down_type, n_ff)[0]
     assert rel_l2(ys[t, L], ry) <= REL_L2_TOL, (t, L, rel_l2(ys[t, L], ry))
     assert np.abs(ys[t, L] - ry).max() <= MAX_ABS_TOL
+    assert_same_bits(ys[t, L], ry, f"layer output (t={t}, L={L})")
 
 
 def ar1_states(n_tok, n_embd, rho=0.9, seed=12345):

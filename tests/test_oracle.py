@@ -138,3 +138,20 @@ def test_cpu_fast_path_matches_q8K_oracle(oracle_lib):
     rids, rw, ry = oracle_lib.moe_layer(x[None], W, g, u, d, 14, I, K, path="q8K")
     assert np.array_equal(ids, rids[0]) and np.array_equal(w, rw[0])
     assert rel_l2(y, ry[0]) < 1e-5
+
+
+@pytest.mark.parametrize("qtype,n", [(12, 2048), (12, 768), (14, 768), (14, 512), (12, 4096)])
+def test_kernel_order_dots_match_double(oracle_lib, qtype, n):
+    """The kernel-order fp32 dots (unit partials, lane butterfly / row-group
+    tree) are the double-accumulated dots up to fp32 rounding, relative to
+    the sum of the products' magnitudes."""
+    rng = np.random.default_rng(11 + n)
+    rows = oracle_lib.quantize((rng.standard_normal((64, n)) * 0.02).astype(np.float32), qtype)
+    q, d, s = oracle_lib.quantize_q8_1(rms_norm(rng.standard_normal(n)))
+    err = 0.0
+    for r in rows:
+        a = oracle_lib.dot_q8_1(r, qtype, q, d, s)
+        b = oracle_lib.dot_q8_1(r, qtype, q, d, s, order="kernel")
+        scale = np.abs(oracle_lib.dequantize(r, qtype, n)).sum() * np.abs(q * np.repeat(d, 32)).max()
+        err = max(err, abs(a - b) / scale)
+    assert err < 1e-6
