@@ -13,8 +13,11 @@ do not).
   predictor_toy.json   the scores / top-k / update results of the reference's
                        own cpp/moe-predictor.cpp (compiled into oracle/_ref by
                        oracle/Makefile) on it.
+  expert_cache.json    a scripted prefetch / admit / query sequence through the
+                       reference's own ExpertCache (src/prefetch_engine.py),
+                       its CUDA stream calls replaced by host stand-ins.
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py [gguf greedy predictor expert_cache]
 """
 import importlib.util
 import json
@@ -118,8 +121,109 @@ def predictor_fixture():
                               "hit": hit, "scores_after": after.tolist()}}, f)
 
 
+class _CpuStream:
+    """Stand-in for torch.cuda.Stream on a host without a GPU: copies are
+    synchronous, so every recorded event has completed."""
+
+    def __init__(self, device=None):
+        pass
+
+    def synchronize(self):
+        pass
+
+
+class _DoneEvent:
+    def record(self, stream=None):
+        pass
+
+    def query(self):
+        return True
+
+
+def _cpu_torch():
+    """The real torch module with its CUDA stream / event / pinned-memory
+    calls replaced by host stand-ins, so that the reference's ExpertCache runs
+    its own bookkeeping unchanged on the CPU."""
+    import contextlib
+    import types
+
+    import torch
+    shim = types.ModuleType("torch")
+    shim.__dict__.update({k: getattr(torch, k) for k in dir(torch) if not k.startswith("__")})
+
+    def empty(*shape, device=None, pin_memory=False, **kw):
+        return torch.empty(*shape, **kw)
+    shim.empty = empty
+    shim.cuda = types.SimpleNamespace(Stream=_CpuStream, Event=_DoneEvent,
+                                      stream=lambda s: contextlib.nullcontext())
+    return shim
+
+
+def expert_cache_fixture():
+    with open(os.path.join(HERE, "expert_cache.json"), "w") as f:
+        json.dump(expert_cache_cases(), f)
+
+
+def expert_cache_cases():
+    """A scripted sequence of prefetch / admit / sync / query calls run
+    through the reference's own ExpertCache (src/prefetch_engine.py:47-168),
+    imported from the reference tree with host stand-ins for its CUDA calls.
+    Recorded after every call: the return value, each layer's expert -> slot
+    map in LRU order, and the statistics; at the end, which staging row every
+    slot holds.  Queries follow a sync(), so no copy is in flight (no `late`:
+    on a GPU that outcome depends on timing)."""
+    path = os.path.join(REF, "src", "prefetch_engine.py")
+    spec = importlib.util.spec_from_file_location("ref_prefetch_engine", path)
+    mod = importlib.util.module_from_spec(spec)
+    import torch
+    shim = _cpu_torch()
+    saved = sys.modules["torch"]
+    sys.modules["torch"] = shim
+    try:
+        spec.loader.exec_module(mod)
+    finally:
+        sys.modules["torch"] = saved
+    cases = []
+    for case, (L, E, cap, nb, steps) in enumerate(((3, 16, 5, 256, 120), (2, 128, 24, 4096, 200),
+                                                    (1, 8, 8, 64, 60))):
+        rng = np.random.default_rng(100 + case)
+        xc = mod.ExpertCache(L, E, cap, device="cpu", bytes_per_expert=nb)
+        # staging row e: bytes (e * 37 + j) % 251, so a slot's bytes name its expert
+        xc.staging.copy_(torch.from_numpy(
+            ((np.arange(E)[:, None] * 37 + np.arange(nb)[None, :]) % 251).astype(np.uint8)))
+        ops = []
+        for _ in range(steps):
+            layer = int(rng.integers(L))
+            kind = ("prefetch", "admit", "query")[int(rng.integers(3))]
+            n = int(rng.integers(1, min(E, 12) + 1))
+            ids = [int(v) for v in rng.integers(0, E, n)]   # duplicates included
+            if kind == "prefetch":
+                ret = xc.prefetch(layer, ids)
+            elif kind == "admit":
+                ret = xc.admit(layer, ids)
+            else:
+                xc.sync()
+                ret = [list(v) for v in xc.query(layer, ids)]
+            ops.append({"op": kind, "layer": layer, "ids": ids, "ret": ret,
+                        "maps": [[[int(e), int(s)] for e, s in m.items()] for m in xc.maps],
+                        "stats": dict(xc.stats)})
+        xc.sync()
+        held = [[int(xc.slabs[l][s][0]) for s in range(cap)] for l in range(L)]
+        cases.append({"n_layers": L, "n_experts": E, "capacity": cap, "bytes_per_expert": nb,
+                      "ops": ops, "summary": xc.summary(), "vram_bytes": xc.vram_bytes(),
+                      "slab_first_byte": held})
+    return {"source": "src/prefetch_engine.py:47-168 (reference ExpertCache, run on the host)",
+            "cases": cases}
+
+
 if __name__ == "__main__":
-    gguf_fixture()
-    greedy_fixture()
-    predictor_fixture()
+    which = sys.argv[1:] or ["gguf", "greedy", "predictor", "expert_cache"]
+    if "gguf" in which:
+        gguf_fixture()
+    if "greedy" in which:
+        greedy_fixture()
+    if "predictor" in which:
+        predictor_fixture()
+    if "expert_cache" in which:
+        expert_cache_fixture()
     print("golden fixtures written to", HERE)

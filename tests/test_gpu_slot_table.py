@@ -106,18 +106,18 @@ def test_slot_table_matches_oracle(oracle_lib, admit, max_inserts, batch, profil
     st.close()
 
 
-def test_decode_with_cache_end_to_end(oracle_lib):
-    """Config-2 flow at small scale: batch-1 decode token by token with
-    misses served zero-copy, second-miss admission, uploads on the copy
-    stream and deterministic publication; the device tables after every
-    step equal the oracle's, fed the same routed ids, and every layer output
-    is within tolerance of the oracle's."""
-    _needs_gpu()
-    from moe_prefetch_b200 import MoeCacheConfig, MoeStack
-    L, E, k = 2, 128, 8
+def _decode_with_cache(oracle_lib, L, n_tok, ns, profile=None, prior=0.01, seed=33):
+    """Batch-1 decode token by token through a constrained cache: misses
+    served zero-copy, second-miss (window) admission, uploads on the copy
+    stream, deterministic publication.  After every step the device tables
+    equal the oracle's (fed the same routed ids), and every layer's ids and
+    weights are bit-exact and its output within tolerance, with the router's
+    prior taken from the oracle's published table."""
+    from moe_prefetch_b200 import MoeCacheConfig, MoeStack, format_slot_profile
+    E, k = 128, 8
     # weights: generate resident on a helper stack, then host copies
     src = MoeStack(n_layers=L)
-    src.synth_resident(seed=33, keep_router=True)
+    src.synth_resident(seed=seed, keep_router=True)
     host = []
     for il in range(L):
         g, u, d = src.slot_views(il)
@@ -125,27 +125,27 @@ def test_decode_with_cache_end_to_end(oracle_lib):
     routers = [r.clone() for r in src.routers]
     src.close()
     torch.cuda.synchronize()
-    cfg = MoeCacheConfig(n_slots=24, max_inserts=2, admit="window", batch_tables=True,
-                         cache_prior=0.01)
+    cfg = MoeCacheConfig(n_slots=ns, max_inserts=2, admit="window", batch_tables=True,
+                         cache_prior=prior,
+                         slot_profile=format_slot_profile(profile) if profile else "")
     st = MoeStack(n_layers=L, cache=cfg)
     for il in range(L):
         st.set_router(il, routers[il])
         st.set_expert_weights(il, *host[il])
-    oc = oracle_lib.OracleCache(L, E, 24, max_inserts=2, admit_mode=2, batch_tables=True,
-                                cache_prior=0.01)
-    h = ar1_states(24, H, seed=2)
+    oc = oracle_lib.OracleCache(L, E, ns, slot_profile=st.ns, max_inserts=2, admit_mode=2,
+                                batch_tables=True, cache_prior=prior)
+    h = ar1_states(n_tok, H, seed=2)
     grid = st.decode_info()["grid"]
     for t in range(h.shape[0]):
-        # the router's prior must see the oracle's published table
         out, dm = st.decode(torch.from_numpy(h[t:t + 1]).cuda(), debug=True)
         st.sync()
         dumps = {q: v.cpu().numpy() for q, v in dm.items()}
         for il in range(L):
-            tbl, prior = oc.dev_table(il)
+            tbl, pri = oc.dev_table(il)
             W = routers[il].cpu().numpy()
             gate, up, down = (x.numpy().reshape(E, -1) for x in host[il])
             check_decode_layer(oracle_lib, h[t], dumps, 0, il, W, gate, up, down, grid,
-                               prior=prior)
+                               prior=pri)
             oc.observe(il, dumps["ids"][0, il])
         st.step()
         oc.step()
@@ -153,3 +153,29 @@ def test_decode_with_cache_end_to_end(oracle_lib):
     s = st.stats()
     assert s["misses"] > 0 and s["scheduled"] > 0 and s["published"] > 0
     st.close()
+    return s
+
+
+def test_decode_with_cache_end_to_end(oracle_lib):
+    """The config-2 flow at small scale: 2 layers, 24 slots, 24 tokens."""
+    _needs_gpu()
+    _decode_with_cache(oracle_lib, L=2, n_tok=24, ns=24)
+
+
+def test_decode_with_cache_config2_scale(oracle_lib):
+    """The config-2 flow at its own scale: 128 experts, a 56-slot budget
+    spread over 8 layers by the byte-priced greedy allocation (grid 16 / 32 /
+    56 / 96), delta = 0.01, window admission, batched tables, 64 tokens."""
+    _needs_gpu()
+    from moe_prefetch_b200 import greedy_allocate_bytes
+    L = 8
+    grid = [16, 32, 56, 96]
+    # per-layer miss curves (misses per 8 routed ids at each grid size):
+    # layers differ in how much a slot helps, so the greedy spreads the budget
+    rng = np.random.default_rng(5)
+    scale = rng.uniform(0.5, 2.0, L)
+    miss8 = {n: [float(8 * scale[il] * (1 - n / 128) ** (1 + il % 3)) for il in range(L)] for n in grid}
+    caps, used, budget = greedy_allocate_bytes(miss8, grid, L, 56, [], [3059712] * L)
+    assert used <= budget and len(set(caps)) > 1
+    s = _decode_with_cache(oracle_lib, L=L, n_tok=64, ns=56, profile=caps, seed=44)
+    assert s["hits"] > 0 and s["copied"] > 0
