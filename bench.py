@@ -347,6 +347,8 @@ def run_config2(args):
                 "uploads_per_token": d["scheduled"] / timed,
                 "published_per_token": d["published"] / timed,
                 "upload_gbs": d["upload_bytes"] / (ms / 1000.0) / 1e9,
+                # while the copy stream runs the uploads (the host link's share)
+                "upload_gbs_during_copies": (d["upload_bytes"] / d["upload_ns"] if d["upload_ns"] else None),
                 "zero_copy_miss_gbs": d["misses"] * EXPERT_BYTES / (ms / 1000.0) / 1e9,
                 "ms_per_token": ms / timed,
             }
@@ -359,27 +361,19 @@ def run_config2(args):
 # ---------------------------------------------------------------------------
 # config 3: batched decode and prefill, expert-parallel over the ranks
 # ---------------------------------------------------------------------------
-def run_config3(args):
-    """Config 3: the config-1 stack, expert-parallel (rank g owns experts
-    [g E/N, (g+1) E/N) of every layer; NCCL all-to-all dispatch and combine).
-    Workloads: 32 sequences decoding 128 tokens (32 / N home tokens per rank
-    per step) and one 512-token prefill chunk (512 / N per rank).  Inputs are
+def ep_measure(world, rank, n_layers, dec_steps, pre_chunks, warmup):
+    """The config-3 expert-parallel workloads on the ranks of the current
+    process group (or one GPU): rank g owns experts [g E/N, (g+1) E/N) of
+    every layer; NCCL all-to-all dispatch and combine.  32 sequences decoding
+    (32 / N home tokens per rank per step; the whole step captured in a CUDA
+    graph) and one 512-token prefill chunk (512 / N per rank).  Inputs are
     i.i.d. N(0, 1) RMS-normed rows.  Total work is fixed as N grows (strong
-    scaling).  Device time is CUDA events on each rank, max over ranks.  One
-    JSON line per workload from rank 0."""
-    import datetime
+    scaling).  Device time is CUDA events on each rank, max over ranks.
+    Returns the JSON lines (every rank computes them)."""
     import torch
     import torch.distributed as dist
     from moe_prefetch_b200.ep import ExpertParallelStack
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
-    n_layers = args.layers
     ep = ExpertParallelStack(n_layers)
     ep.synth(seed=11)
     stream = torch.cuda.current_stream()
@@ -389,11 +383,11 @@ def run_config3(args):
         h = rng.standard_normal((n, N_EMBD))
         return (h / np.sqrt((h ** 2).mean(-1, keepdims=True))).astype(np.float32)
 
-    def timed(x, steps, warmup, path, graph):
+    def timed(x, steps, warm, path, graph):
         def step():
             for il in range(n_layers):
                 ep.layer_forward(il, x, path)
-        for _ in range(warmup):
+        for _ in range(warm):
             step()
         g = None
         if graph:   # fixed-capacity exchange: the whole step replays as one CUDA graph
@@ -416,40 +410,59 @@ def run_config3(args):
         t = torch.tensor([e0.elapsed_time(e1)], device="cuda", dtype=torch.float64)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        del g
+        del g   # a graph holding NCCL calls goes before the process group
         return float(t[0])
 
     used_graph = [False]
     lines = []
-    dec_seqs, dec_steps = 32, args.c3_decode_steps
+    dec_seqs = 32
     if dec_seqs % world == 0:
         x = torch.from_numpy(rows(dec_seqs, 500)[rank::world].copy()).cuda()
-        ms = timed(x, dec_steps, args.warmup, "auto", graph=True)
+        ms = timed(x, dec_steps, warmup, "auto", graph=True)
         lines.append({
             "metric": "config3 expert-parallel batched decode", "value": dec_seqs * dec_steps / (ms / 1e3),
-            "unit": "tok/s", "n_gpus": world, "steps": dec_steps, "warmup": args.warmup,
+            "unit": "tok/s", "n_gpus": world, "steps": dec_steps, "warmup": warmup,
             "ms_per_step": ms / dec_steps, "higher_is_better": True, "scaling": "strong",
             "config": {"workload": f"config3 decode: {dec_seqs} sequences x {dec_steps} steps, "
                                    f"{n_layers} layers, EP {N_EXPERT // world} experts/GPU",
                        "path": "grouped GEMV, fixed-capacity exchange",
                        "cuda_graph": used_graph[0], "data": "synthetic"}})
-    pre_tok, chunks = 512, args.c3_prefill_chunks
+    pre_tok = 512
     if pre_tok % world == 0:
         x = torch.from_numpy(rows(pre_tok, 501)[rank::world].copy()).cuda()
-        ms = timed(x, chunks, max(1, args.warmup), "auto", graph=False)
-        flops = 2.0 * pre_tok * TOP_K * 3 * N_EMBD * N_FF * n_layers * chunks
+        ms = timed(x, pre_chunks, max(1, warmup), "auto", graph=False)
+        flops = 2.0 * pre_tok * TOP_K * 3 * N_EMBD * N_FF * n_layers * pre_chunks
         lines.append({
-            "metric": "config3 expert-parallel prefill", "value": pre_tok * chunks / (ms / 1e3),
-            "unit": "tok/s", "n_gpus": world, "steps": chunks, "warmup": max(1, args.warmup),
-            "ms_per_step": ms / chunks, "higher_is_better": True, "scaling": "strong",
+            "metric": "config3 expert-parallel prefill", "value": pre_tok * pre_chunks / (ms / 1e3),
+            "unit": "tok/s", "n_gpus": world, "steps": pre_chunks, "warmup": max(1, warmup),
+            "ms_per_step": ms / pre_chunks, "higher_is_better": True, "scaling": "strong",
             "expert_tflops_whole_job": flops / (ms / 1e3) / 1e12,
             "config": {"workload": f"config3 prefill: one {pre_tok}-token chunk per step, "
                                    f"{n_layers} layers, EP {N_EXPERT // world} experts/GPU",
                        "path": "auto (tcgen05 grouped GEMM)", "data": "synthetic"}})
+    ep.close()
+    torch.cuda.synchronize()
+    return lines
+
+
+def run_config3(args):
+    """Config 3 on its own: ep_measure, one JSON line per workload from rank 0."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    lines = ep_measure(world, rank, args.layers, args.c3_decode_steps, args.c3_prefill_chunks,
+                       args.warmup)
     if rank == 0:
         for ln in lines:
             print(json.dumps(ln), flush=True)
-    ep.close()
     if world > 1:
         dist.destroy_process_group()
     return 0
@@ -659,6 +672,104 @@ def run_layer(args):
 
 
 # ---------------------------------------------------------------------------
+# the host link: the denominators of config 2's upload and zero-copy rates
+# ---------------------------------------------------------------------------
+def run_hostlink(args):
+    """Host-link peaks on this box, and the library's own rates against them.
+    (1) one 1 GiB pinned host -> device cudaMemcpyAsync on a dedicated
+    non-blocking stream (the copy engine's peak); (2) the uploader's pattern:
+    64 expert jobs of three copies (gate, up, down slices) from pinned host
+    memory, back to back on that stream; (3) zero-copy reads by the decode
+    kernel: a frozen cache that holds nothing, so that every routed expert of
+    every layer is read from registered host memory (--layers x --tokens
+    layer-tokens, 8 experts each).  One JSON line."""
+    import torch
+    from moe_prefetch_b200 import MoeCacheConfig, MoeStack
+    torch.cuda.set_device(0)
+    cs = torch.cuda.Stream(priority=0)
+
+    def copy_rate(dst, src_views, reps):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        nbytes = 0
+        with torch.cuda.stream(cs):
+            for d, v in src_views:               # warm-up
+                d.copy_(v, non_blocking=True)
+            e0.record(cs)
+            for _ in range(reps):
+                for d, v in src_views:
+                    d.copy_(v, non_blocking=True)
+                    nbytes += v.numel()
+            e1.record(cs)
+        cs.synchronize()
+        return nbytes / (e0.elapsed_time(e1) / 1000.0) / 1e9
+
+    big = torch.empty(1 << 30, dtype=torch.uint8, pin_memory=True)
+    dbig = torch.empty(1 << 30, dtype=torch.uint8, device="cuda")
+    peak = copy_rate(dbig, [(dbig, big)], 5)
+    del big, dbig
+    gb, db = GATE_BYTES, DOWN_BYTES
+    n_jobs = 64
+    hs = torch.empty(n_jobs * (2 * gb + db), dtype=torch.uint8, pin_memory=True)
+    ds = torch.empty_like(hs, device="cuda")
+    views = []
+    for j in range(n_jobs):
+        o = j * (2 * gb + db)
+        for a, n in ((o, gb), (o + gb, gb), (o + 2 * gb, db)):
+            views.append((ds[a:a + n], hs[a:a + n]))
+    jobs = copy_rate(None, views, 4)
+    del hs, ds
+    torch.cuda.synchronize()
+    # zero-copy: every expert host-resident, nothing admitted
+    L, T = args.layers, args.tokens
+    res = MoeStack(n_layers=L)
+    res.synth_resident(seed=11, keep_router=True)
+    host = []
+    for il in range(L):
+        g, u, d = res.slot_views(il)
+        hl = []
+        for v in (g, u, d):
+            t = torch.empty(N_EXPERT * v.shape[1], dtype=torch.uint8, pin_memory=True)
+            t.view(N_EXPERT, -1).copy_(v[:N_EXPERT])
+            hl.append(t)
+        host.append(tuple(hl))
+    routers = [r.clone() for r in res.routers]
+    res.close()
+    torch.cuda.synchronize()
+    st = MoeStack(n_layers=L, cache=MoeCacheConfig(n_slots=8, freeze=True))
+    for il in range(L):
+        st.set_router(il, routers[il])
+        st.set_expert_weights(il, *host[il])
+    h = torch.from_numpy(ar1_states(T, N_EMBD, seed=5)).cuda()
+    out = torch.empty_like(h)
+    st.decode(h, out)
+    st.sync()
+    s0 = st.stats()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    st.decode(h, out)
+    e1.record()
+    torch.cuda.synchronize()
+    st.sync()
+    s1 = st.stats()
+    ms = e0.elapsed_time(e1)
+    misses = s1["misses"] - s0["misses"]
+    zc = misses * EXPERT_BYTES / (ms / 1000.0) / 1e9
+    st.close()
+    print(json.dumps({
+        "metric": "host link", "unit": "GB/s",
+        "pinned_h2d_1GiB_gbs": peak, "upload_pattern_gbs": jobs,
+        "upload_pattern_frac": jobs / peak,
+        "decode_zero_copy_gbs": zc, "decode_zero_copy_frac": zc / peak,
+        "zero_copy_layer_tokens": L * T, "zero_copy_misses": misses,
+        "config": {"workload": "pinned copies on a dedicated stream; decode with every expert in host memory",
+                   "upload_jobs": n_jobs, "expert_bytes": EXPERT_BYTES, "layers": L, "tokens": T,
+                   "data": "synthetic"}}), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
 # where a decode layer's time goes (the kernel's own phase stamps)
 # ---------------------------------------------------------------------------
 PHASES = [(0, 1, "grid barrier A"), (1, 2, "router totals"), (2, 6, "selection"),
@@ -727,11 +838,16 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--workload", default="config1",
-                    choices=["config1", "config2", "config3", "config4", "layer", "phases"])
+                    choices=["config1", "config2", "config3", "config4", "layer", "phases",
+                             "hostlink"])
     ap.add_argument("--c4", action="store_true", help="phases: config-4 shapes")
     ap.add_argument("--path", default="gemv", choices=["auto", "gemv", "gemm"])
     ap.add_argument("--c3-decode-steps", type=int, default=128)
     ap.add_argument("--c3-prefill-chunks", type=int, default=4)
+    ap.add_argument("--no-ep", action="store_true",
+                    help="headline: skip the expert-parallel (config 3) keys")
+    ap.add_argument("--ep-decode-steps", type=int, default=32)
+    ap.add_argument("--ep-prefill-chunks", type=int, default=2)
     ap.add_argument("--c2-warm", type=int, default=64)
     ap.add_argument("--c2-tokens", type=int, default=128)
     args = ap.parse_args()
@@ -747,6 +863,8 @@ def main():
         return run_layer(args)
     if args.workload == "phases":
         return run_phases(args)
+    if args.workload == "hostlink":
+        return run_hostlink(args)
 
     import torch
     import torch.distributed as dist
@@ -863,6 +981,26 @@ def main():
                          "(oracle's integer-dot CPU rows path, Q8_K activations, OpenMP); "
                          "tok/s = layer-tokens/s / 48"}
 
+    # the expert-parallel workloads (config 3) on the same N GPUs, so that a
+    # scaling run of this line carries their strong-scaling curve too; the
+    # decode stack is freed first
+    decode_geometry = st.decode_info()
+    st.close()
+    st = None
+    ep = None
+    if not args.no_ep:
+        torch.cuda.empty_cache()
+        ep_lines = ep_measure(world, rank, n_layers, args.ep_decode_steps, args.ep_prefill_chunks,
+                              args.warmup)
+        ep = {}
+        for ln in ep_lines:
+            key = "decode" if "decode" in ln["metric"] else "prefill"
+            ep[key] = {"value": ln["value"], "unit": "tok/s", "ms_per_step": ln["ms_per_step"],
+                       "steps": ln["steps"], "workload": ln["config"]["workload"],
+                       "scaling": "strong"}
+            if key == "decode":
+                ep[key]["cuda_graph"] = ln["config"]["cuda_graph"]
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
@@ -871,10 +1009,11 @@ def main():
             "data": "synthetic (seeded N(0,0.02) weights quantised on device; AR(1) inputs)",
             "config": config_block(tokens), "roofline": roofline, "cpu_baseline": cpu,
             "e2e": e2e, "gpu_launches": args.steps, "clocks": clocks,
-            "decode_geometry": st.decode_info(),
+            "decode_geometry": decode_geometry,
+            # config 3, expert-parallel over the same N GPUs (strong scaling)
+            "expert_parallel": ep,
         }
         print(json.dumps(line), flush=True)
-    st.close()
     if world > 1:
         dist.destroy_process_group()
     return 0

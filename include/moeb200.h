@@ -91,12 +91,16 @@ typedef struct moe_layer_info {
 } moe_layer_info;
 
 /* Counters (the reference's every-512-steps stderr line, patches/0006:928-953,
- * 0007:762-770), read with moe_get_stats in this order. */
+ * 0007:762-770), read with moe_get_stats in this order.  UPLOAD_NS is ours:
+ * the time the copy stream spent on the upload batches moe_step issued (from
+ * the start of a batch's first copy to the end of its last, measured with
+ * events), so that UPLOAD_BYTES / UPLOAD_NS is the host-link rate while
+ * uploads run. */
 enum moe_stat {
     MOE_STAT_STEPS = 0, MOE_STAT_CLOCK, MOE_STAT_HITS, MOE_STAT_MISSES,
     MOE_STAT_UPLOADS, MOE_STAT_SCHEDULED, MOE_STAT_COPIED, MOE_STAT_PUBLISHED,
     MOE_STAT_ADMIT_OK, MOE_STAT_ADMIT_DENIED, MOE_STAT_TABLE_FLUSHES,
-    MOE_STAT_UPLOAD_BYTES, MOE_STAT_COUNT
+    MOE_STAT_UPLOAD_BYTES, MOE_STAT_UPLOAD_NS, MOE_STAT_COUNT
 };
 
 /* ---- lifetime ---------------------------------------------------------------- */

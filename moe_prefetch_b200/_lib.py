@@ -17,7 +17,7 @@ ERRORS = {
 QTYPE_Q4_K = 12
 QTYPE_Q6_K = 14
 STAT_NAMES = ["steps", "clock", "hits", "misses", "uploads", "scheduled", "copied",
-              "published", "admit_ok", "admit_denied", "table_flushes", "upload_bytes"]
+              "published", "admit_ok", "admit_denied", "table_flushes", "upload_bytes", "upload_ns"]
 
 
 class MoeError(RuntimeError):

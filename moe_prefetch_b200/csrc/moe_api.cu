@@ -76,6 +76,9 @@ struct moe_ctx {
     int32_t *h_jobs = nullptr;         // mapped pinned [L*MI*4 + 4]
     int32_t *d_jobs_alias = nullptr;
     uint64_t upload_bytes = 0;
+    uint64_t upload_ns = 0;          // time the copy stream spent on step uploads
+    cudaEvent_t ev_up0 = nullptr, ev_up1 = nullptr;   // around the last step's uploads
+    bool up_timed = false;           // ev_up0/ev_up1 hold an unharvested pair
     std::string err_msg;
 };
 
@@ -316,7 +319,8 @@ extern "C" int moe_create(const moe_cfg *cfg, moe_ctx **out) {
         if (cudaHostGetDevicePointer((void **)&c->d_jobs_alias, c->h_jobs, 0) != cudaSuccess) return cleanup_fail(MOE_ERR_CUDA);
         if (cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking) != cudaSuccess ||
             cudaEventCreateWithFlags(&c->ev_step, cudaEventDisableTiming) != cudaSuccess ||
-            cudaEventCreateWithFlags(&c->ev_copy, cudaEventDisableTiming) != cudaSuccess)
+            cudaEventCreateWithFlags(&c->ev_copy, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreate(&c->ev_up0) != cudaSuccess || cudaEventCreate(&c->ev_up1) != cudaSuccess)
             return cleanup_fail(MOE_ERR_CUDA);
     }
     if (cudaDeviceSynchronize() != cudaSuccess) return cleanup_fail(MOE_ERR_CUDA);
@@ -359,6 +363,8 @@ extern "C" void moe_destroy(moe_ctx *c) {
     if (c->h_jobs) cudaFreeHost(c->h_jobs);
     if (c->ev_step) cudaEventDestroy(c->ev_step);
     if (c->ev_copy) cudaEventDestroy(c->ev_copy);
+    if (c->ev_up0) cudaEventDestroy(c->ev_up0);
+    if (c->ev_up1) cudaEventDestroy(c->ev_up1);
     if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
     delete c;
 }
@@ -915,6 +921,16 @@ extern "C" int moe_observe(moe_ctx *c, int layer, const int32_t *ids, int n_tok,
     return MOE_OK;
 }
 
+// Adds the duration of the last timed upload batch to upload_ns once both
+// events have completed.
+static void harvest_upload_time(moe_ctx *c) {
+    if (!c->up_timed || cudaEventQuery(c->ev_up1) != cudaSuccess) return;
+    float ms = 0.0f;
+    if (cudaEventElapsedTime(&ms, c->ev_up0, c->ev_up1) == cudaSuccess)
+        c->upload_ns += (uint64_t)((double)ms * 1e6);
+    c->up_timed = false;
+}
+
 extern "C" int moe_step(moe_ctx *c, void *stream) {
     if (!c) return MOE_ERR_ARG;
     CK(cudaSetDevice(c->cfg.device));
@@ -928,6 +944,10 @@ extern "C" int moe_step(moe_ctx *c, void *stream) {
     volatile int32_t *nj_p = c->h_jobs + (size_t)c->cfg.n_layers * MI * 4;
     const int nj = *nj_p;
     c->copies_pending = false;
+    harvest_upload_time(c);   // the previous batch is done: the step kernel waited for it
+    if (nj > 0 && !c->up_timed) {
+        CK(cudaEventRecord(c->ev_up0, c->copy_stream));
+    }
     for (int j = 0; j < nj; ++j) {
         const int l = c->h_jobs[4 * j], e = c->h_jobs[4 * j + 1], slot = c->h_jobs[4 * j + 2];
         if (l < 0 || l >= c->cfg.n_layers || e < 0 || e >= c->cfg.n_expert || slot < 0 || slot >= c->L[l].ns)
@@ -945,6 +965,10 @@ extern "C" int moe_step(moe_ctx *c, void *stream) {
         c->upload_bytes += 2 * c->gate_bytes + c->down_bytes;
     }
     if (nj > 0) {
+        if (!c->up_timed) {
+            CK(cudaEventRecord(c->ev_up1, c->copy_stream));
+            c->up_timed = true;
+        }
         CK(cudaEventRecord(c->ev_copy, c->copy_stream));
         c->copies_pending = true;
     }
@@ -995,9 +1019,10 @@ extern "C" int moe_get_stats(moe_ctx *c, uint64_t *out, int n) {
     CK(cudaMemcpy(miss.data(), c->st.n_miss, 8 * L, cudaMemcpyDeviceToHost));
     uint64_t h = 0, m = 0;
     for (int l = 0; l < L; ++l) { h += hit[l]; m += miss[l]; }
+    harvest_upload_time(c);
     uint64_t all[MOE_STAT_COUNT] = {g[G_STEPS], g[G_CLOCK], h, m, g[G_UPLOADS], g[G_SCHEDULED],
                                     g[G_COPIED], g[G_PUBLISHED], g[G_ADMIT_OK], g[G_ADMIT_DENIED],
-                                    g[G_FLUSHES], c->upload_bytes};
+                                    g[G_FLUSHES], c->upload_bytes, c->upload_ns};
     for (int i = 0; i < n && i < MOE_STAT_COUNT; ++i) out[i] = all[i];
     return MOE_OK;
 }
