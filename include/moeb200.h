@@ -246,9 +246,9 @@ int moe_ep_combine(moe_ctx *ctx, const float *y_rows, const int32_t *pos, const 
  *  - a batch (n_tok > 1) always runs the per-pair kernels, which read an
  *    expert's rows once per routed (token, expert) pair, where
  *    moe_layer_forward groups the pairs by expert and reads them once per
- *    tile.  The results are the same bits; a batch is slower (the measured
- *    figure for 32 tokens is in the design notes).  n_tok = 1 is the same
- *    launch sequence in both.
+ *    tile.  The results are the same bits; a batch is slower: 481 us vs
+ *    161 us for 32 tokens of a Qwen3-30B-A3B-shape layer on one B200, 151 us
+ *    vs 86 us for 8.  n_tok = 1 is the same launch sequence in both.
  * The scratch lives in one static device array of MOE_NOALLOC_SCRATCH_BYTES
  * per device, built into the library: the router ids/weights and the gate/up
  * activations.

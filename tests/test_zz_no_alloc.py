@@ -23,6 +23,7 @@ H, I, E, K = 2048, 768, 128, 8
 SCRATCH_BYTES = 4 << 20          # MOE_NOALLOC_SCRATCH_BYTES
 MAX_TOK = 170                    # largest n_tok that fits for n_used 8, n_ff 768
 MOE_ERR_ARG = -1
+MOE_ERR_UNSUPPORTED = -4
 
 
 def _need(n_tok):
@@ -113,3 +114,19 @@ def test_noalloc_rejects_batches_beyond_the_scratch(stack):
     from moe_prefetch_b200._lib import MoeError
     with pytest.raises(MoeError):
         st.layer_forward_noalloc(0, x, y)
+
+
+def test_noalloc_refuses_shared_expert_contexts(stack):
+    """A context with an always-on shared expert is refused before anything
+    is launched (the allocating entry point serves it)."""
+    from moe_prefetch_b200 import MoeStack
+    st = MoeStack(n_layers=1, n_expert=256, n_ff=512, n_shared=1)
+    try:
+        x = torch.zeros(2, H, device="cuda")
+        y = torch.zeros_like(x)
+        rc = st.lib.moe_layer_forward_noalloc(st.ctx, 0, _p(x), _p(y), 2, None, None, _s())
+        assert rc == MOE_ERR_UNSUPPORTED
+        assert "shared expert" in st.lib.moe_last_error(st.ctx).decode()
+        assert torch.count_nonzero(y).item() == 0
+    finally:
+        st.close()
