@@ -227,6 +227,44 @@ int moe_experts_rows(moe_ctx *ctx, int layer, const float *x_rows, const int32_t
 int moe_ep_combine(moe_ctx *ctx, const float *y_rows, const int32_t *pos, const float *w,
                    int n_tok, const float *add_rows, float *out, void *stream);
 
+/* ---- expert parallelism over peer memory ------------------------------------------
+ * No counterpart in the reference (it runs on one GPU).  The same layer as
+ * moe_ep_route_pack + all-to-all + moe_experts_rows + all-to-all +
+ * moe_ep_combine, with the two exchanges done by this library's own kernels
+ * over NVLink instead of a collective library: every rank owns a mailbox in
+ * its device memory, mapped into the other ranks' processes with CUDA IPC,
+ * and the kernels store rows straight into the owner's (then the home
+ * rank's) mailbox and raise a flag there.  Only pairs that exist cross the
+ * link, nothing waits for the host, and a whole step can be captured in a
+ * CUDA graph.  Plain loads and stores only: no multicast, no bulk copy from
+ * a peer's memory.  Waits are bounded by the context's wait limit
+ * (moe_set_wait_limit); a wait that runs out sets the error word that
+ * moe_sync reports as MOE_ERR_TIMEOUT.  Every rank must issue the same
+ * sequence of layers (push, serve, collect), one layer after another on one
+ * stream. */
+#define MOE_EP_HANDLE_BYTES 64
+/* Allocate this rank's mailbox for up to max_home_tokens home tokens per
+ * layer and write its IPC handle (MOE_EP_HANDLE_BYTES) to handle_out.
+ * world >= 2; rank g owns experts [g E / world, (g + 1) E / world). */
+int moe_ep_mailbox_create(moe_ctx *ctx, int world, int rank, int max_home_tokens, void *handle_out);
+/* Open the other ranks' mailboxes: handles = the world handles in rank order
+ * (host memory).  Call once, on every rank, after every rank has created its
+ * mailbox; keep the ranks apart from one another's mailboxes until all have
+ * connected (a barrier), and again before moe_destroy. */
+int moe_ep_mailbox_connect(moe_ctx *ctx, const void *handles);
+/* Send this rank's routed pairs: send_count/send_ids/send_x as
+ * moe_ep_route_pack wrote them with capacity 0 (compact, in owner order),
+ * n_tok the home tokens of that call. */
+int moe_ep_push(moe_ctx *ctx, int n_tok, const int32_t *send_count, const int32_t *send_ids,
+                const float *send_x, void *stream);
+/* Owner side: wait for every rank's pairs, run this rank's experts on them
+ * (path MOE_PATH_GEMV or MOE_PATH_GEMM), send the unweighted rows back. */
+int moe_ep_serve(moe_ctx *ctx, int layer, int path, void *stream);
+/* Home side: wait for every owner's rows, then the combine of moe_ep_combine
+ * (pos / w from moe_ep_route_pack; add_rows the shared expert's rows or NULL). */
+int moe_ep_collect(moe_ctx *ctx, const int32_t *pos, const float *w, int n_tok, const float *add_rows,
+                   float *out, void *stream);
+
 /* moe_layer_forward that allocates no device memory.  This entry point has no
  * counterpart in the reference, whose CPU expert path allocates nothing on
  * the GPU.

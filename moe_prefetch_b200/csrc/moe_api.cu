@@ -66,6 +66,16 @@ struct moe_ctx {
     GroupBufs grp{};
     int32_t *s_dest = nullptr;         // expert parallelism: destination rank per pair
     float *s_ypair = nullptr;
+    // expert parallelism over peer memory: this rank's mailbox (exported with
+    // CUDA IPC), the other ranks' mailboxes opened in this process, the
+    // device table of all world bases, the owner's y rows, the epoch
+    EpMail ep{};
+    uint8_t *ep_mail = nullptr;
+    std::vector<uint8_t *> ep_open;    // opened peer mailboxes (closed at destroy)
+    uint8_t **ep_peer = nullptr;       // device [world]
+    float *ep_y = nullptr;             // [world * cap][n_embd]
+    unsigned long long *ep_epoch = nullptr;
+    bool ep_connected = false;
     // tensor-core GEMM operand tiles (fp16)
     void *s_gemm = nullptr;
     int s_gemm_cap_tok = 0;
@@ -332,6 +342,11 @@ extern "C" void moe_destroy(moe_ctx *c) {
     cudaSetDevice(c->cfg.device);
     if (c->copy_stream) cudaStreamSynchronize(c->copy_stream);
     cudaDeviceSynchronize();
+    for (uint8_t *p : c->ep_open) cudaIpcCloseMemHandle(p);
+    cudaFree(c->ep_mail);
+    cudaFree(c->ep_peer);
+    cudaFree(c->ep_y);
+    cudaFree(c->ep_epoch);
     for (auto &m : c->L) {
         if (m.slab) cudaFree(m.slab);
         if (m.shared) cudaFree(m.shared);
@@ -742,6 +757,125 @@ extern "C" int moe_ep_combine(moe_ctx *c, const float *y_rows, const int32_t *po
     CK(cudaSetDevice(c->cfg.device));
     CK(launch_combine(y_rows, pos, w, n_tok, c->cfg.n_used, c->cfg.n_embd, add_rows, out,
                       (cudaStream_t)stream));
+    return MOE_OK;
+}
+
+// ---- expert parallelism over peer memory --------------------------------------
+
+static size_t up256(size_t b) { return (b + 255) & ~(size_t)255; }
+
+extern "C" int moe_ep_mailbox_create(moe_ctx *c, int world, int rank, int max_home_tokens,
+                                     void *handle_out) {
+    if (!c || !handle_out || world < 2 || world > 256 || rank < 0 || rank >= world || max_home_tokens <= 0)
+        return fail(c, MOE_ERR_ARG, "moe_ep_mailbox_create: bad argument");
+    if (c->ep_mail) return fail(c, MOE_ERR_ARG, "moe_ep_mailbox_create: the mailbox exists already");
+    const moe_cfg &g = c->cfg;
+    if (g.n_expert % world)
+        return fail(c, MOE_ERR_ARG, "moe_ep_mailbox_create: world %d does not divide %d experts", world,
+                    g.n_expert);
+    CK(cudaSetDevice(g.device));
+    EpMail m{};
+    m.world = world;
+    m.rank = rank;
+    m.cap = max_home_tokens * g.n_used;     // a source may send all its pairs to one owner
+    m.n_embd = g.n_embd;
+    size_t off = 0;
+    m.off_fflag = off; off = up256(off + 8 * (size_t)world);
+    m.off_rflag = off; off = up256(off + 8 * (size_t)world);
+    m.off_meta = off;  off = up256(off + 8 * (size_t)world);
+    m.off_ids = off;   off = up256(off + 4 * (size_t)world * m.cap);
+    m.off_x = off;     off = up256(off + 4 * (size_t)world * m.cap * m.n_embd);
+    m.off_rety = off;  off = up256(off + 4 * (size_t)m.cap * m.n_embd);
+    m.bytes = off;
+    if (cudaMalloc(&c->ep_mail, m.bytes) != cudaSuccess ||
+        cudaMalloc(&c->ep_peer, sizeof(uint8_t *) * world) != cudaSuccess ||
+        cudaMalloc(&c->ep_y, sizeof(float) * (size_t)world * m.cap * m.n_embd) != cudaSuccess ||
+        cudaMalloc(&c->ep_epoch, sizeof(unsigned long long)) != cudaSuccess) {
+        cudaFree(c->ep_mail); cudaFree(c->ep_peer); cudaFree(c->ep_y); cudaFree(c->ep_epoch);
+        c->ep_mail = nullptr; c->ep_peer = nullptr; c->ep_y = nullptr; c->ep_epoch = nullptr;
+        return fail(c, MOE_ERR_OOM, "moe_ep_mailbox_create: %zu bytes of mailbox", m.bytes);
+    }
+    CK(cudaMemset(c->ep_mail, 0, m.bytes));
+    CK(cudaMemset(c->ep_epoch, 0, sizeof(unsigned long long)));
+    cudaIpcMemHandle_t h;
+    CK(cudaIpcGetMemHandle(&h, c->ep_mail));
+    static_assert(sizeof(cudaIpcMemHandle_t) == MOE_EP_HANDLE_BYTES, "IPC handle size");
+    memcpy(handle_out, &h, sizeof(h));
+    c->ep = m;
+    return MOE_OK;
+}
+
+extern "C" int moe_ep_mailbox_connect(moe_ctx *c, const void *handles) {
+    if (!c || !handles) return fail(c, MOE_ERR_ARG, "moe_ep_mailbox_connect: bad argument");
+    if (!c->ep_mail || c->ep_connected)
+        return fail(c, MOE_ERR_ARG, "moe_ep_mailbox_connect: create the mailbox first, once");
+    CK(cudaSetDevice(c->cfg.device));
+    const EpMail &m = c->ep;
+    std::vector<uint8_t *> base(m.world, nullptr);
+    for (int r = 0; r < m.world; ++r) {
+        if (r == m.rank) {
+            base[r] = c->ep_mail;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, static_cast<const uint8_t *>(handles) + (size_t)r * MOE_EP_HANDLE_BYTES, sizeof(h));
+        void *p = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess)
+            return fail(c, MOE_ERR_CUDA, "moe_ep_mailbox_connect: rank %d's mailbox: %s", r,
+                        cudaGetErrorString(e));
+        base[r] = static_cast<uint8_t *>(p);
+        c->ep_open.push_back(base[r]);
+    }
+    CK(cudaMemcpy(c->ep_peer, base.data(), sizeof(uint8_t *) * m.world, cudaMemcpyHostToDevice));
+    c->ep_connected = true;
+    return MOE_OK;
+}
+
+extern "C" int moe_ep_push(moe_ctx *c, int n_tok, const int32_t *send_count, const int32_t *send_ids,
+                           const float *send_x, void *stream) {
+    if (!c || n_tok < 0 || !send_count || !send_ids || !send_x)
+        return fail(c, MOE_ERR_ARG, "moe_ep_push: bad argument");
+    if (!c->ep_connected) return fail(c, MOE_ERR_ARG, "moe_ep_push: no connected mailbox");
+    if ((int64_t)n_tok * c->cfg.n_used > c->ep.cap)
+        return fail(c, MOE_ERR_ARG, "moe_ep_push: %d home tokens exceed the mailbox's %d", n_tok,
+                    c->ep.cap / c->cfg.n_used);
+    CK(cudaSetDevice(c->cfg.device));
+    CK(launch_ep_push(c->ep, c->ep_peer, send_count, send_ids, send_x, c->ep_epoch, (cudaStream_t)stream));
+    return MOE_OK;
+}
+
+extern "C" int moe_ep_serve(moe_ctx *c, int layer, int path, void *stream) {
+    if (!c || layer < 0 || layer >= c->cfg.n_layers) return fail(c, MOE_ERR_ARG, "moe_ep_serve: bad argument");
+    if (!c->ep_connected) return fail(c, MOE_ERR_ARG, "moe_ep_serve: no connected mailbox");
+    if (path != MOE_PATH_GEMV && path != MOE_PATH_GEMM)
+        return fail(c, MOE_ERR_ARG, "moe_ep_serve: the path must be MOE_PATH_GEMV or MOE_PATH_GEMM");
+    CK(cudaSetDevice(c->cfg.device));
+    const EpMail &m = c->ep;
+    cudaStream_t s = (cudaStream_t)stream;
+    CK(launch_ep_wait(reinterpret_cast<const unsigned long long *>(c->ep_mail + m.off_fflag), m.world,
+                      c->ep_epoch, c->dp.wait_ns, c->err, s));
+    const int r = moe_experts_rows(c, layer, reinterpret_cast<const float *>(c->ep_mail + m.off_x),
+                                   reinterpret_cast<const int32_t *>(c->ep_mail + m.off_ids), m.world * m.cap,
+                                   c->ep_y, path, stream);
+    if (r != MOE_OK) return r;
+    CK(launch_ep_push(m, c->ep_peer, nullptr, nullptr, c->ep_y, c->ep_epoch, s));
+    return MOE_OK;
+}
+
+extern "C" int moe_ep_collect(moe_ctx *c, const int32_t *pos, const float *w, int n_tok,
+                              const float *add_rows, float *out, void *stream) {
+    if (!c || !pos || !w || !out || n_tok <= 0) return fail(c, MOE_ERR_ARG, "moe_ep_collect: bad argument");
+    if (!c->ep_connected) return fail(c, MOE_ERR_ARG, "moe_ep_collect: no connected mailbox");
+    if (c->cfg.n_shared && !add_rows)
+        return fail(c, MOE_ERR_ARG, "moe_ep_collect: the shared expert's rows are missing");
+    CK(cudaSetDevice(c->cfg.device));
+    const EpMail &m = c->ep;
+    cudaStream_t s = (cudaStream_t)stream;
+    CK(launch_ep_wait(reinterpret_cast<const unsigned long long *>(c->ep_mail + m.off_rflag), m.world,
+                      c->ep_epoch, c->dp.wait_ns, c->err, s));
+    CK(launch_combine(reinterpret_cast<const float *>(c->ep_mail + m.off_rety), pos, w, n_tok,
+                      c->cfg.n_used, c->cfg.n_embd, add_rows, out, s));
     return MOE_OK;
 }
 

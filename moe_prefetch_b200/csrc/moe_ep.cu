@@ -82,4 +82,155 @@ cudaError_t launch_ep_pack(const int32_t *ids, const float *x, int n_tok, int k,
     return cudaGetLastError();
 }
 
+// ===========================================================================
+// The exchange over peer memory.  Every rank owns a mailbox in its device
+// memory, mapped into the other ranks with CUDA IPC (plain loads and stores
+// over NVLink; no multicast, no bulk copies from peer memory).  One layer:
+//
+//   source s (after route + pack, compact send order):
+//     k_ep_push_rows   block d of its send list -> rank d's mailbox:
+//                      ids[s][0 .. cap) (-1 past the count) and x[s][j]
+//     k_ep_signal      epoch += 1; on rank d: meta[s] = (count, offset),
+//                      then flag_fwd[s] = epoch (release, system scope)
+//   owner d:
+//     k_ep_wait        every flag_fwd[s] == epoch (bounded)
+//     expert rows      on its mailbox's world * cap slots (id -1: empty)
+//     k_ep_push_rows   (return) y rows of source s -> rank s's ret_y at
+//                      offset + j
+//     k_ep_signal      on rank s: flag_ret[d] = epoch
+//   home s:
+//     k_ep_wait        every flag_ret[d] == epoch, then the combine of ret_y
+//
+// A source writes rank d's mailbox for the next layer only after its own
+// combine, which waited for every owner's return rows, which each owner
+// sends after its expert rows have read the mailbox: one mailbox suffices.
+// Every rank runs the same sequence of exchanges, so the epochs agree.
+// ===========================================================================
+
+#define EP_RPC 4   // rows per CTA of the copy kernels
+
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Send counts and offsets of blocks d (forward: the compact send list's
+// exclusive scan) or the meta a source wrote (return), clamped to the slots.
+__device__ __forceinline__ void ep_block(const EpMail &m, int d, const int32_t *send_count,
+                                         const int32_t *meta, int &cnt, int &off) {
+    if (send_count) {
+        off = 0;
+        for (int q = 0; q < d; ++q) off += send_count[q];
+        cnt = send_count[d];
+    } else {
+        cnt = meta[2 * d];
+        off = meta[2 * d + 1];
+    }
+    cnt = min(max(cnt, 0), m.cap);
+    off = min(max(off, 0), m.cap - cnt);
+}
+
+// grid (ceil(cap / EP_RPC), world); block 256.  Forward (send_count != null):
+// rows off + j of src -> rank d's x[me][j], and ids[me][j] (-1 past the
+// count).  Return (send_count null): rows (d * cap + j) of src -> rank d's
+// ret_y[off + j], (count, off) from this rank's meta[d].
+__global__ void __launch_bounds__(256) k_ep_push_rows(EpMail m, uint8_t *const *peer,
+                                                      const int32_t *__restrict__ send_count,
+                                                      const int32_t *__restrict__ send_ids,
+                                                      const float *__restrict__ src) {
+    const int d = blockIdx.y;
+    const int32_t *meta = reinterpret_cast<const int32_t *>(peer[m.rank] + m.off_meta);
+    int cnt, off;
+    ep_block(m, d, send_count, meta, cnt, off);
+    uint8_t *dst = peer[d];
+    const int j0 = blockIdx.x * EP_RPC;
+    const int n4 = m.n_embd / 4;
+    float *out;
+    const float *in;
+    if (send_count) {
+        int32_t *pids = reinterpret_cast<int32_t *>(dst + m.off_ids) + (size_t)m.rank * m.cap;
+        for (int j = j0 + (int)threadIdx.x; j < min(j0 + EP_RPC, m.cap); j += blockDim.x)
+            pids[j] = j < cnt ? send_ids[off + j] : -1;
+        out = reinterpret_cast<float *>(dst + m.off_x) + (size_t)m.rank * m.cap * m.n_embd;
+        in = src + (size_t)off * m.n_embd;
+    } else {
+        out = reinterpret_cast<float *>(dst + m.off_rety) + (size_t)off * m.n_embd;
+        in = src + (size_t)d * m.cap * m.n_embd;
+    }
+    const int j1 = min(j0 + EP_RPC, cnt);
+    for (int i = threadIdx.x; i < (j1 - j0) * n4; i += blockDim.x) {
+        const int j = j0 + i / n4, c = i - (i / n4) * n4;
+        reinterpret_cast<float4 *>(out + (size_t)j * m.n_embd)[c] =
+            __ldcg(reinterpret_cast<const float4 *>(in + (size_t)j * m.n_embd) + c);
+    }
+    __threadfence_system();
+}
+
+// One CTA, thread d < world.  Forward (send_count != null): thread 0 first
+// advances the epoch; then (count, offset) of block d into rank d's
+// meta[me] and the epoch into its flag_fwd[me].  Return: the epoch into rank
+// d's flag_ret[me].  The stores before a flag are the same thread's, and the
+// rows came from the previous kernel on this stream (each of its CTAs ended
+// with a system-scope fence).
+__global__ void k_ep_signal(EpMail m, uint8_t *const *peer, const int32_t *__restrict__ send_count,
+                            unsigned long long *epoch) {
+    __shared__ unsigned long long s_e;
+    if (threadIdx.x == 0) s_e = send_count ? ++*epoch : *epoch;
+    __syncthreads();
+    const int d = threadIdx.x;
+    if (d >= m.world) return;
+    uint8_t *dst = peer[d];
+    if (send_count) {
+        int cnt, off;
+        ep_block(m, d, send_count, nullptr, cnt, off);
+        int32_t *meta = reinterpret_cast<int32_t *>(dst + m.off_meta) + 2 * m.rank;
+        meta[0] = cnt;
+        meta[1] = off;
+        st_release_sys_u64(reinterpret_cast<unsigned long long *>(dst + m.off_fflag) + m.rank, s_e);
+    } else {
+        st_release_sys_u64(reinterpret_cast<unsigned long long *>(dst + m.off_rflag) + m.rank, s_e);
+    }
+}
+
+// One CTA, thread s < world: wait until this rank's flag s carries the epoch
+// (bounded by wait_ns; on expiry the timeout bit goes into *err and the
+// kernel returns, so the context stays usable).
+__global__ void k_ep_wait(const unsigned long long *flags, int world, const unsigned long long *epoch,
+                          uint64_t wait_ns, int *err) {
+    const int s = threadIdx.x;
+    if (s >= world) return;
+    const unsigned long long e = *epoch;
+    if (ld_acquire_sys_u64(flags + s) >= e) return;
+    const uint64_t t0 = gtimer();
+    while (ld_acquire_sys_u64(flags + s) < e) {
+        if (gtimer() - t0 > wait_ns) {
+            atomicOr(err, MOE_DEV_ERR_TIMEOUT);
+            return;
+        }
+        __nanosleep(200);
+    }
+}
+
+cudaError_t launch_ep_push(const EpMail &m, uint8_t *const *peer, const int32_t *send_count,
+                           const int32_t *send_ids, const float *src, unsigned long long *epoch,
+                           cudaStream_t s) {
+    k_ep_push_rows<<<dim3((m.cap + EP_RPC - 1) / EP_RPC, m.world), 256, 0, s>>>(m, peer, send_count,
+                                                                                 send_ids, src);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    k_ep_signal<<<1, 256, 0, s>>>(m, peer, send_count, epoch);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_wait(const unsigned long long *flags, int world, const unsigned long long *epoch,
+                           uint64_t wait_ns, int *err, cudaStream_t s) {
+    k_ep_wait<<<1, 256, 0, s>>>(flags, world, epoch, wait_ns, err);
+    return cudaGetLastError();
+}
+
 }  // namespace moe

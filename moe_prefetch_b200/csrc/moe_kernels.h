@@ -103,6 +103,22 @@ cudaError_t launch_ep_pack(const int32_t *ids, const float *x, int n_tok, int k,
                            int n_embd, int world, int capacity, int32_t *dest, const GroupBufs &g,
                            int32_t *send_ids, float *send_x, int *err, cudaStream_t s);
 
+// The peer-memory exchange (moe_ep.cu): byte offsets of one rank's mailbox.
+struct EpMail {
+    int world, rank, cap, n_embd;          // cap: slots per (source, owner) block
+    size_t off_fflag, off_rflag, off_meta, off_ids, off_x, off_rety, bytes;
+};
+// forward (send_count != null): the compact send list's blocks to every
+// owner's mailbox, then meta + flags (advancing *epoch); return (send_count
+// null): the owner's y rows [world][cap][n_embd] to every source's ret_y,
+// then the return flags.  peer: device array of the world mailbox bases.
+cudaError_t launch_ep_push(const EpMail &m, uint8_t *const *peer, const int32_t *send_count,
+                           const int32_t *send_ids, const float *src, unsigned long long *epoch,
+                           cudaStream_t s);
+// wait (bounded) until flags[0 .. world) all carry *epoch
+cudaError_t launch_ep_wait(const unsigned long long *flags, int world, const unsigned long long *epoch,
+                           uint64_t wait_ns, int *err, cudaStream_t s);
+
 // ---- tensor-core grouped GEMM (moe_gemm.cu) --------------------------------
 
 #define GM_NT 64       // pairs per token tile of the GEMM (MMA N <= 64)

@@ -15,6 +15,14 @@ layer over a rank's home tokens:
   4. all-to-all of the rows back, in the order they came;
   5. the home rank combines them in rank order.
 
+With exchange="peer" (ExpertParallelStack on GPUs, world >= 2) steps 2 and
+4 are the library's own kernels instead of NCCL: every rank's device memory
+holds a mailbox, opened by the other ranks' processes with CUDA IPC; the
+pairs are stored straight into the owner's mailbox and the rows straight
+back into the home rank's, each followed by a flag the receiver waits for
+on the device.  Only routed pairs cross NVLink and nothing waits for the
+host, so prefill too can be captured in a CUDA graph.
+
 The reference has no multi-GPU code; the result equals the single-GPU layer
 (bit for bit on the GEMV path).  The orchestration works on any
 torch.distributed backend: the three device steps come from an `ops` object,
@@ -39,6 +47,23 @@ def _a2a(out, inp, out_splits, in_splits, group, world):
 
 
 CAPACITY_MAX_TOKENS = 64   # home tokens up to which the exchange uses fixed-capacity slots
+
+
+def ep_layer_forward_peer(ops, layer, x, path="auto"):
+    """ep_layer_forward over the peer-memory mailboxes (ops: LibEPOps of a
+    stack whose mailbox is connected).  path "auto" takes the GEMV for up to
+    CAPACITY_MAX_TOKENS home tokens and the GEMM above; every rank must pass
+    the same path (the owners run one path on everyone's pairs), so with
+    "auto" every rank must have the same number of home tokens."""
+    n_tok = x.shape[0]
+    if path == "auto":
+        path = "gemv" if n_tok <= CAPACITY_MAX_TOKENS else "gemm"
+    ids, w, send_count, pos, send_ids, send_x = ops.route_pack(layer, x, ops.world, 0)
+    ops.push(n_tok, send_count, send_ids, send_x)
+    ops.serve(layer, path)
+    shared = ops.shared_rows(layer, x, path) if getattr(ops, "n_shared", 0) else None
+    out = ops.collect(pos, w, n_tok, shared)
+    return out, ids, w
 
 
 def ep_layer_forward(ops, layer, x, group=None, path="auto", capacity=None):
@@ -95,10 +120,11 @@ def ep_layer_forward(ops, layer, x, group=None, path="auto", capacity=None):
 class LibEPOps:
     """The three device steps of ep_layer_forward, from libmoeb200.so."""
 
-    def __init__(self, stack):
+    def __init__(self, stack, world=1):
         self.st = stack
         self.n_shared = stack.n_shared
         self.n_used = stack.n_used
+        self.world = world
 
     def route_pack(self, layer, x, world, capacity=0):
         st = self.st
@@ -128,6 +154,22 @@ class LibEPOps:
         ids = torch.full((x.shape[0],), self.st.n_expert, dtype=torch.int32, device=x.device)
         return self.experts_rows(layer, x.contiguous(), ids, path)
 
+    def push(self, n_tok, send_count, send_ids, send_x):
+        st = self.st
+        st._ck(st.lib.moe_ep_push(st.ctx, n_tok, _ptr(send_count), _ptr(send_ids), _ptr(send_x), _stream()),
+               "moe_ep_push")
+
+    def serve(self, layer, path):
+        st = self.st
+        st._ck(st.lib.moe_ep_serve(st.ctx, layer, PATHS[path], _stream()), "moe_ep_serve")
+
+    def collect(self, pos, w, n_tok, add_rows=None):
+        st = self.st
+        out = torch.empty(n_tok, st.n_embd, dtype=torch.float32, device=w.device)
+        st._ck(st.lib.moe_ep_collect(st.ctx, _ptr(pos), _ptr(w), n_tok, _ptr(add_rows), _ptr(out), _stream()),
+               "moe_ep_collect")
+        return out
+
     def combine(self, y_rows, pos, w, n_tok, add_rows=None):
         st = self.st
         out = torch.empty(n_tok, st.n_embd, dtype=torch.float32, device=w.device)
@@ -141,7 +183,10 @@ class ExpertParallelStack:
     experts in slots, the full router, and ep_layer_forward over `group`."""
 
     def __init__(self, n_layers, n_expert=128, n_used=8, n_embd=2048, n_ff=768, group=None,
-                 device=None, n_shared=0):
+                 device=None, n_shared=0, exchange="nccl", max_home_tokens=256):
+        """exchange: "nccl" (torch.distributed all-to-all) or "peer" (this
+        library's kernels over peer-memory mailboxes; GPUs, world >= 2, up to
+        max_home_tokens home tokens per layer)."""
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -152,7 +197,28 @@ class ExpertParallelStack:
         dev = device if device is not None else torch.cuda.current_device()
         self.st = MoeStack(n_layers, n_expert=n_expert, n_used=n_used, n_embd=n_embd, n_ff=n_ff,
                            cache=MoeCacheConfig(n_slots=self.per_rank), device=dev, n_shared=n_shared)
-        self.ops = LibEPOps(self.st)
+        self.ops = LibEPOps(self.st, self.world)
+        self.exchange = exchange if self.world > 1 else "nccl"
+        if exchange not in ("nccl", "peer"):
+            raise ValueError(f"unknown exchange {exchange!r}")
+        if self.exchange == "peer":
+            self._connect(max_home_tokens)
+
+    def _connect(self, max_home_tokens):
+        """Create this rank's mailbox, all-gather the IPC handles, open the
+        others'.  A barrier keeps ranks from sending before everyone is
+        connected."""
+        st = self.st
+        h = torch.zeros(64, dtype=torch.uint8)
+        st._ck(st.lib.moe_ep_mailbox_create(st.ctx, self.world, self.rank, max_home_tokens, _ptr(h)),
+               "moe_ep_mailbox_create")
+        hd = h.to(st.device)
+        allh = torch.empty(self.world * 64, dtype=torch.uint8, device=st.device)
+        dist.all_gather_into_tensor(allh, hd, group=self.group)
+        allh = allh.cpu()
+        st._ck(st.lib.moe_ep_mailbox_connect(st.ctx, _ptr(allh)), "moe_ep_mailbox_connect")
+        torch.cuda.synchronize(st.device)
+        dist.barrier(group=self.group)
 
     def synth(self, seed=0, sigma=0.02, router_sigma=0.02):
         """The weights MoeStack.synth_resident(seed) generates, this rank's
@@ -189,7 +255,14 @@ class ExpertParallelStack:
         del tmp
 
     def layer_forward(self, layer, x, path="auto"):
+        if self.exchange == "peer":
+            return ep_layer_forward_peer(self.ops, layer, x, path)
         return ep_layer_forward(self.ops, layer, x, self.group, path)
 
     def close(self):
+        """With mailboxes: every rank's work done, then free (no rank frees
+        memory another may still write)."""
+        if self.exchange == "peer" and self.st.ctx:
+            torch.cuda.synchronize(self.st.device)
+            dist.barrier(group=self.group)
         self.st.close()

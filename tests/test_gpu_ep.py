@@ -5,8 +5,10 @@
   - the GEMV path bit for bit;
   - the GEMM path bit for bit as well: the expert tiles hold the same pairs
     in the same order.
-- World size 2 (two GPUs, NCCL): tests/ep_worker.py under torch.distributed.run
-  against a single-GPU stack with the same weights; skipped on one GPU.
+- World size 2 (two GPUs): tests/ep_worker.py under torch.distributed.run,
+  with the NCCL exchange and with the peer-memory mailboxes (eager and
+  captured in a CUDA graph), against a single-GPU stack with the same
+  weights; skipped on one GPU.
 """
 import os
 import socket
@@ -58,7 +60,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_ep_two_gpus_nccl():
+def test_ep_two_gpus():
     if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", MASTER_ADDR="127.0.0.1")
