@@ -361,12 +361,15 @@ def run_config2(args):
 # ---------------------------------------------------------------------------
 # config 3: batched decode and prefill, expert-parallel over the ranks
 # ---------------------------------------------------------------------------
-def ep_measure(world, rank, n_layers, dec_steps, pre_chunks, warmup):
+def ep_measure(world, rank, n_layers, dec_steps, pre_chunks, warmup, exchange="peer"):
     """The config-3 expert-parallel workloads on the ranks of the current
     process group (or one GPU): rank g owns experts [g E/N, (g+1) E/N) of
-    every layer; NCCL all-to-all dispatch and combine.  32 sequences decoding
-    (32 / N home tokens per rank per step; the whole step captured in a CUDA
-    graph) and one 512-token prefill chunk (512 / N per rank).  Inputs are
+    every layer.  The dispatch and combine go through the library's
+    peer-memory mailboxes (exchange "peer", the default) or NCCL all-to-all
+    ("nccl").  32 sequences decoding (32 / N home tokens per rank per step)
+    and one 512-token prefill chunk (512 / N per rank); with the mailboxes
+    both whole steps replay as CUDA graphs (with NCCL only the decode step,
+    whose fixed-capacity exchange does not wait for the host).  Inputs are
     i.i.d. N(0, 1) RMS-normed rows.  Total work is fixed as N grows (strong
     scaling).  Device time is CUDA events on each rank, max over ranks.
     Returns the JSON lines (every rank computes them)."""
@@ -374,7 +377,8 @@ def ep_measure(world, rank, n_layers, dec_steps, pre_chunks, warmup):
     import torch.distributed as dist
     from moe_prefetch_b200.ep import ExpertParallelStack
 
-    ep = ExpertParallelStack(n_layers)
+    ep = ExpertParallelStack(n_layers, exchange=exchange, max_home_tokens=max(512 // world, 32))
+    exchange = ep.exchange   # one GPU: no exchange
     ep.synth(seed=11)
     stream = torch.cuda.current_stream()
 
@@ -390,7 +394,7 @@ def ep_measure(world, rank, n_layers, dec_steps, pre_chunks, warmup):
         for _ in range(warm):
             step()
         g = None
-        if graph:   # fixed-capacity exchange: the whole step replays as one CUDA graph
+        if graph:   # nothing in the step waits for the host: it replays as one CUDA graph
             torch.cuda.synchronize()
             g = capture(step)
         used_graph[0] = g is not None
@@ -419,18 +423,19 @@ def ep_measure(world, rank, n_layers, dec_steps, pre_chunks, warmup):
     if dec_seqs % world == 0:
         x = torch.from_numpy(rows(dec_seqs, 500)[rank::world].copy()).cuda()
         ms = timed(x, dec_steps, warmup, "auto", graph=True)
+        xpath = "peer-memory mailboxes" if exchange == "peer" else "NCCL fixed-capacity all-to-all"
         lines.append({
             "metric": "config3 expert-parallel batched decode", "value": dec_seqs * dec_steps / (ms / 1e3),
             "unit": "tok/s", "n_gpus": world, "steps": dec_steps, "warmup": warmup,
             "ms_per_step": ms / dec_steps, "higher_is_better": True, "scaling": "strong",
             "config": {"workload": f"config3 decode: {dec_seqs} sequences x {dec_steps} steps, "
                                    f"{n_layers} layers, EP {N_EXPERT // world} experts/GPU",
-                       "path": "grouped GEMV, fixed-capacity exchange",
+                       "path": f"grouped GEMV, {xpath if world > 1 else 'no exchange'}",
                        "cuda_graph": used_graph[0], "data": "synthetic"}})
     pre_tok = 512
     if pre_tok % world == 0:
         x = torch.from_numpy(rows(pre_tok, 501)[rank::world].copy()).cuda()
-        ms = timed(x, pre_chunks, max(1, warmup), "auto", graph=False)
+        ms = timed(x, pre_chunks, max(1, warmup), "auto", graph=exchange == "peer" or world == 1)
         flops = 2.0 * pre_tok * TOP_K * 3 * N_EMBD * N_FF * n_layers * pre_chunks
         lines.append({
             "metric": "config3 expert-parallel prefill", "value": pre_tok * pre_chunks / (ms / 1e3),
@@ -439,7 +444,10 @@ def ep_measure(world, rank, n_layers, dec_steps, pre_chunks, warmup):
             "expert_tflops_whole_job": flops / (ms / 1e3) / 1e12,
             "config": {"workload": f"config3 prefill: one {pre_tok}-token chunk per step, "
                                    f"{n_layers} layers, EP {N_EXPERT // world} experts/GPU",
-                       "path": "auto (tcgen05 grouped GEMM)", "data": "synthetic"}})
+                       "path": "tcgen05 grouped GEMM, " + (("peer-memory mailboxes" if exchange == "peer"
+                                                           else "NCCL all-to-all sized on the host")
+                                                          if world > 1 else "no exchange"),
+                       "cuda_graph": used_graph[0], "data": "synthetic"}})
     ep.close()
     torch.cuda.synchronize()
     return lines
@@ -459,7 +467,7 @@ def run_config3(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     lines = ep_measure(world, rank, args.layers, args.c3_decode_steps, args.c3_prefill_chunks,
-                       args.warmup)
+                       args.warmup, args.ep_exchange)
     if rank == 0:
         for ln in lines:
             print(json.dumps(ln), flush=True)
@@ -848,6 +856,8 @@ def main():
                     help="headline: skip the expert-parallel (config 3) keys")
     ap.add_argument("--ep-decode-steps", type=int, default=32)
     ap.add_argument("--ep-prefill-chunks", type=int, default=2)
+    ap.add_argument("--ep-exchange", default="peer", choices=["peer", "nccl"],
+                    help="expert-parallel dispatch/combine: peer-memory mailboxes or NCCL")
     ap.add_argument("--c2-warm", type=int, default=64)
     ap.add_argument("--c2-tokens", type=int, default=128)
     args = ap.parse_args()
@@ -991,15 +1001,14 @@ def main():
     if not args.no_ep:
         torch.cuda.empty_cache()
         ep_lines = ep_measure(world, rank, n_layers, args.ep_decode_steps, args.ep_prefill_chunks,
-                              args.warmup)
+                              args.warmup, args.ep_exchange)
         ep = {}
         for ln in ep_lines:
             key = "decode" if "decode" in ln["metric"] else "prefill"
             ep[key] = {"value": ln["value"], "unit": "tok/s", "ms_per_step": ln["ms_per_step"],
                        "steps": ln["steps"], "workload": ln["config"]["workload"],
+                       "path": ln["config"]["path"], "cuda_graph": ln["config"]["cuda_graph"],
                        "scaling": "strong"}
-            if key == "decode":
-                ep[key]["cuda_graph"] = ln["config"]["cuda_graph"]
 
     if rank == 0:
         line = {

@@ -254,12 +254,14 @@ int moe_ep_mailbox_create(moe_ctx *ctx, int world, int rank, int max_home_tokens
 int moe_ep_mailbox_connect(moe_ctx *ctx, const void *handles);
 /* Send this rank's routed pairs: send_count/send_ids/send_x as
  * moe_ep_route_pack wrote them with capacity 0 (compact, in owner order),
- * n_tok the home tokens of that call. */
+ * n_tok the home tokens of that call.  Every rank passes the same n_tok to
+ * the three calls of a layer (1 .. max_home_tokens): the mailbox blocks of
+ * that layer hold n_tok * n_used slots. */
 int moe_ep_push(moe_ctx *ctx, int n_tok, const int32_t *send_count, const int32_t *send_ids,
                 const float *send_x, void *stream);
 /* Owner side: wait for every rank's pairs, run this rank's experts on them
  * (path MOE_PATH_GEMV or MOE_PATH_GEMM), send the unweighted rows back. */
-int moe_ep_serve(moe_ctx *ctx, int layer, int path, void *stream);
+int moe_ep_serve(moe_ctx *ctx, int layer, int n_tok, int path, void *stream);
 /* Home side: wait for every owner's rows, then the combine of moe_ep_combine
  * (pos / w from moe_ep_route_pack; add_rows the shared expert's rows or NULL). */
 int moe_ep_collect(moe_ctx *ctx, const int32_t *pos, const float *w, int n_tok, const float *add_rows,

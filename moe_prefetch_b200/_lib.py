@@ -75,7 +75,7 @@ SIGNATURES = {
     "moe_ep_mailbox_create": (I, [P, I, I, I, P]),
     "moe_ep_mailbox_connect": (I, [P, P]),
     "moe_ep_push": (I, [P, I, P, P, P, P]),
-    "moe_ep_serve": (I, [P, I, I, P]),
+    "moe_ep_serve": (I, [P, I, I, I, P]),
     "moe_ep_collect": (I, [P, P, P, I, P, P, P]),
     "moe_decode": (I, [P, P, P, I, P, P]),
     "moe_decode_host": (I, [P, P, P, I, P]),

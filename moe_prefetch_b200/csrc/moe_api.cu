@@ -832,26 +832,38 @@ extern "C" int moe_ep_mailbox_connect(moe_ctx *c, const void *handles) {
     return MOE_OK;
 }
 
-extern "C" int moe_ep_push(moe_ctx *c, int n_tok, const int32_t *send_count, const int32_t *send_ids,
-                           const float *send_x, void *stream) {
-    if (!c || n_tok < 0 || !send_count || !send_ids || !send_x)
-        return fail(c, MOE_ERR_ARG, "moe_ep_push: bad argument");
-    if (!c->ep_connected) return fail(c, MOE_ERR_ARG, "moe_ep_push: no connected mailbox");
-    if ((int64_t)n_tok * c->cfg.n_used > c->ep.cap)
-        return fail(c, MOE_ERR_ARG, "moe_ep_push: %d home tokens exceed the mailbox's %d", n_tok,
+// The mailbox layout of one call: blocks of n_tok * n_used slots (every
+// rank passes the same n_tok), inside the regions sized for the maximum.
+static int ep_call_mail(moe_ctx *c, int n_tok, const char *who, EpMail *m) {
+    if (!c->ep_connected) return fail(c, MOE_ERR_ARG, "%s: no connected mailbox", who);
+    if (n_tok <= 0 || (int64_t)n_tok * c->cfg.n_used > c->ep.cap)
+        return fail(c, MOE_ERR_ARG, "%s: %d home tokens; the mailbox holds 1 to %d", who, n_tok,
                     c->ep.cap / c->cfg.n_used);
-    CK(cudaSetDevice(c->cfg.device));
-    CK(launch_ep_push(c->ep, c->ep_peer, send_count, send_ids, send_x, c->ep_epoch, (cudaStream_t)stream));
+    *m = c->ep;
+    m->cap = n_tok * c->cfg.n_used;
     return MOE_OK;
 }
 
-extern "C" int moe_ep_serve(moe_ctx *c, int layer, int path, void *stream) {
+extern "C" int moe_ep_push(moe_ctx *c, int n_tok, const int32_t *send_count, const int32_t *send_ids,
+                           const float *send_x, void *stream) {
+    if (!c || !send_count || !send_ids || !send_x)
+        return fail(c, MOE_ERR_ARG, "moe_ep_push: bad argument");
+    EpMail m;
+    const int r = ep_call_mail(c, n_tok, "moe_ep_push", &m);
+    if (r != MOE_OK) return r;
+    CK(cudaSetDevice(c->cfg.device));
+    CK(launch_ep_push(m, c->ep_peer, send_count, send_ids, send_x, c->ep_epoch, (cudaStream_t)stream));
+    return MOE_OK;
+}
+
+extern "C" int moe_ep_serve(moe_ctx *c, int layer, int n_tok, int path, void *stream) {
     if (!c || layer < 0 || layer >= c->cfg.n_layers) return fail(c, MOE_ERR_ARG, "moe_ep_serve: bad argument");
-    if (!c->ep_connected) return fail(c, MOE_ERR_ARG, "moe_ep_serve: no connected mailbox");
     if (path != MOE_PATH_GEMV && path != MOE_PATH_GEMM)
         return fail(c, MOE_ERR_ARG, "moe_ep_serve: the path must be MOE_PATH_GEMV or MOE_PATH_GEMM");
+    EpMail m;
+    const int rc = ep_call_mail(c, n_tok, "moe_ep_serve", &m);
+    if (rc != MOE_OK) return rc;
     CK(cudaSetDevice(c->cfg.device));
-    const EpMail &m = c->ep;
     cudaStream_t s = (cudaStream_t)stream;
     CK(launch_ep_wait(reinterpret_cast<const unsigned long long *>(c->ep_mail + m.off_fflag), m.world,
                       c->ep_epoch, c->dp.wait_ns, c->err, s));
@@ -865,12 +877,13 @@ extern "C" int moe_ep_serve(moe_ctx *c, int layer, int path, void *stream) {
 
 extern "C" int moe_ep_collect(moe_ctx *c, const int32_t *pos, const float *w, int n_tok,
                               const float *add_rows, float *out, void *stream) {
-    if (!c || !pos || !w || !out || n_tok <= 0) return fail(c, MOE_ERR_ARG, "moe_ep_collect: bad argument");
-    if (!c->ep_connected) return fail(c, MOE_ERR_ARG, "moe_ep_collect: no connected mailbox");
+    if (!c || !pos || !w || !out) return fail(c, MOE_ERR_ARG, "moe_ep_collect: bad argument");
     if (c->cfg.n_shared && !add_rows)
         return fail(c, MOE_ERR_ARG, "moe_ep_collect: the shared expert's rows are missing");
+    EpMail m;
+    const int rc = ep_call_mail(c, n_tok, "moe_ep_collect", &m);
+    if (rc != MOE_OK) return rc;
     CK(cudaSetDevice(c->cfg.device));
-    const EpMail &m = c->ep;
     cudaStream_t s = (cudaStream_t)stream;
     CK(launch_ep_wait(reinterpret_cast<const unsigned long long *>(c->ep_mail + m.off_rflag), m.world,
                       c->ep_epoch, c->dp.wait_ns, c->err, s));

@@ -52,15 +52,16 @@ CAPACITY_MAX_TOKENS = 64   # home tokens up to which the exchange uses fixed-cap
 def ep_layer_forward_peer(ops, layer, x, path="auto"):
     """ep_layer_forward over the peer-memory mailboxes (ops: LibEPOps of a
     stack whose mailbox is connected).  path "auto" takes the GEMV for up to
-    CAPACITY_MAX_TOKENS home tokens and the GEMM above; every rank must pass
-    the same path (the owners run one path on everyone's pairs), so with
-    "auto" every rank must have the same number of home tokens."""
+    CAPACITY_MAX_TOKENS home tokens and the GEMM above.  Every rank must
+    pass the same number of home tokens (the mailbox blocks of a layer hold
+    n_tok * n_used pairs) and the same path (the owners run one path on
+    everyone's pairs)."""
     n_tok = x.shape[0]
     if path == "auto":
         path = "gemv" if n_tok <= CAPACITY_MAX_TOKENS else "gemm"
     ids, w, send_count, pos, send_ids, send_x = ops.route_pack(layer, x, ops.world, 0)
     ops.push(n_tok, send_count, send_ids, send_x)
-    ops.serve(layer, path)
+    ops.serve(layer, n_tok, path)
     shared = ops.shared_rows(layer, x, path) if getattr(ops, "n_shared", 0) else None
     out = ops.collect(pos, w, n_tok, shared)
     return out, ids, w
@@ -78,15 +79,15 @@ def ep_layer_forward(ops, layer, x, group=None, path="auto", capacity=None):
     it (capacity 0) the blocks are dense, and the send counts travel first
     and are read on the host to size the exchange.  The automatic choice
     takes capacity = n_tok * n_used for up to CAPACITY_MAX_TOKENS home tokens
-    (batched decode) and the dense exchange above (prefill).  Every rank must
+    (batched decode) or on one rank, and the dense exchange above (prefill).  Every rank must
     pass the same choice.  With capacity slots the "auto" path is the GEMV
     (few pairs per expert), and no step of the layer waits for the host, so
     a sequence of layers can be captured in a CUDA graph."""
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     n_tok = x.shape[0]
-    if capacity is None:
-        capacity = n_tok * ops.n_used if n_tok <= CAPACITY_MAX_TOKENS else 0
-    if capacity > 0 and path == "auto":
+    if capacity is None:   # one rank: every pair stays, no padding and no count exchange
+        capacity = n_tok * ops.n_used if n_tok <= CAPACITY_MAX_TOKENS or world == 1 else 0
+    if capacity > 0 and world > 1 and path == "auto":
         path = "gemv"   # the padded slots are mostly empty: few pairs per expert
     ids, w, send_count, pos, send_ids, send_x = ops.route_pack(layer, x, world, capacity)
     if capacity > 0:
@@ -159,9 +160,9 @@ class LibEPOps:
         st._ck(st.lib.moe_ep_push(st.ctx, n_tok, _ptr(send_count), _ptr(send_ids), _ptr(send_x), _stream()),
                "moe_ep_push")
 
-    def serve(self, layer, path):
+    def serve(self, layer, n_tok, path):
         st = self.st
-        st._ck(st.lib.moe_ep_serve(st.ctx, layer, PATHS[path], _stream()), "moe_ep_serve")
+        st._ck(st.lib.moe_ep_serve(st.ctx, layer, n_tok, PATHS[path], _stream()), "moe_ep_serve")
 
     def collect(self, pos, w, n_tok, add_rows=None):
         st = self.st

@@ -462,7 +462,7 @@ float or_dot_q6_K_q8_1_f32(const uint8_t *row, const int8_t *q, const float *d,
 
 /* The kernels' combine: per output element an fp32 fma chain from 0 over the
  * pairs in rank order. */
-static void or_combine_f32(const float *w, const float *rows, int k, int n_embd, float *y) {
+void or_combine_f32(const float *w, const float *rows, int k, int n_embd, float *y) {
     for (int h = 0; h < n_embd; ++h) {
         float acc = 0.0f;
         for (int i = 0; i < k; ++i) acc = fmaf(w[i], rows[(size_t)i * n_embd + h], acc);

@@ -70,6 +70,9 @@ double or_dot_q4_K_q8_1(const uint8_t *row, const int8_t *q, const float *d,
                         const float *s, int64_t n);
 double or_dot_q6_K_q8_1(const uint8_t *row, const int8_t *q, const float *d,
                         const float *s, int64_t n);
+/* the GPU kernels' combine of one token: y[h] = fma chain from 0 over the k
+ * rows in rank order (w [k], rows [k][n_embd]) */
+void or_combine_f32(const float *w, const float *rows, int k, int n_embd, float *y);
 /* the same dots in the GPU GEMV kernels' fp32 order (unit partials, lane
  * butterfly / row-group tree): the bits those kernels produce.  Q6_K: n <= 1024. */
 float or_dot_q4_K_q8_1_f32(const uint8_t *row, const int8_t *q, const float *d,

@@ -72,6 +72,8 @@ def _declare(L):
     L.or_dot_q4_K_q8_1.restype = C.c_double
     L.or_dot_q6_K_q8_1.argtypes = [P, P, P, P, I64]
     L.or_dot_q6_K_q8_1.restype = C.c_double
+    L.or_combine_f32.argtypes = [P, P, C.c_int, C.c_int, P]
+    L.or_combine_f32.restype = None
     for n in ("or_dot_q4_K_q8_1_f32", "or_dot_q6_K_q8_1_f32"):
         getattr(L, n).argtypes = [P, P, P, P, I64]
         getattr(L, n).restype = F32
@@ -175,6 +177,18 @@ def q8_K_roundtrip(x):
     out = np.empty_like(x)
     lib().or_q8_K_roundtrip(_p(x), _p(out), x.size)
     return out
+
+
+def combine_rows(w, rows):
+    """The kernels' combine: w [n_tok, k], rows [n_tok, k, n_embd] -> y
+    [n_tok, n_embd], per element an fp32 fma chain from 0 in rank order."""
+    w = _c(w, np.float32)
+    rows = _c(rows, np.float32)
+    n_tok, k, n = rows.shape
+    y = np.empty((n_tok, n), np.float32)
+    for t in range(n_tok):
+        lib().or_combine_f32(_p(w[t]), _p(rows[t]), k, n, _p(y[t]))
+    return y
 
 
 def dot_q8_1(row, qtype, q, d, s, order="f64"):

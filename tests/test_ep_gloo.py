@@ -89,13 +89,10 @@ class OracleOps:
         return torch.from_numpy(y)
 
     def combine(self, back, pos, w, n_tok, add_rows=None):
+        import oracle
         assert add_rows is None
         rows = back.numpy()[pos.numpy().reshape(n_tok, K)]     # [n_tok, K, H]
-        wn = w.numpy().astype(np.float64)
-        acc = np.zeros((n_tok, H))
-        for r in range(K):
-            acc += wn[:, r:r + 1] * rows[:, r].astype(np.float64)
-        return torch.from_numpy(acc.astype(np.float32))
+        return torch.from_numpy(oracle.combine_rows(w.numpy(), rows))   # the kernels' order
 
 
 def _worker(rank, world, port, skew, capacity, out_dir):
