@@ -10,12 +10,13 @@ patches/0006:765-953).  PyTorch is used only for device/pinned buffers and
 streams; every computation is a CUDA kernel of libmoeb200.so.
 """
 import ctypes as C
+import sys
 
 import numpy as np
 import torch
 
 from . import _lib
-from ._lib import MoeCfg, MoeDecodeDbg, MoeLayerInfo, QTYPE_Q4_K, QTYPE_Q6_K, STAT_NAMES, check
+from ._lib import MoeCfg, MoeDecodeDbg, MoeError, MoeLayerInfo, QTYPE_Q4_K, QTYPE_Q6_K, STAT_NAMES, check
 from .config import MoeCacheConfig
 
 Q4K_BYTES, Q6K_BYTES, QK_K = 144, 210, 256
@@ -78,9 +79,82 @@ class MoeStack:
         check(self.lib.moe_create(C.byref(cfg), C.byref(ctx)), None, "moe_create")
         self.ctx = ctx
         self._host = {}          # keep registered host weights alive
+        # the reference's files (LLAMA_MOE_HEAT_FILE / MAP_RECORD / MAP_REPLAY /
+        # ROUTE_TRACE): opened at the first forward, decode or step, once the
+        # host weights are in (start())
+        self._started = False
+        self._map_rec = self._map_rep = self._trace = None
 
     # -- lifetime -------------------------------------------------------------
+    def start(self):
+        """What llama_moe_cache_init does once the weights exist
+        (patches/0007:567-618, 0008:549-571): the heat-file warm start, and
+        the map record / replay and route trace files with their header and
+        the frame of step 0.  Runs by itself at the first layer_forward,
+        decode or step; call it earlier to time it apart."""
+        if self._started or not self.ctx:
+            return
+        self._started = True
+        c = self.cache
+        if c.heat_file and self.cache.n_slots > 0:
+            counts = load_heat(c.heat_file, self.n_layers, self.n_expert)
+            placed = 0
+            if counts is not None:
+                self.warm_start(counts)
+                placed = sum(int((self.tables(il)["slot_expert"] >= 0).sum()) for il in range(self.n_layers))
+            # loud either way, as the reference: a missing file is a cold start
+            print(f"moe-cache: heat file {c.heat_file}: "
+                  f"{0 if counts is None else int((counts > 0).sum())} records, {placed} experts placed before "
+                  f"the first token{'' if counts is not None else ' (COLD START - file missing, empty or refused)'}",
+                  file=sys.stderr)
+        if c.map_record:
+            self._map_rec = open(c.map_record, "w")
+            self._map_rec.write(self.map_header())
+        if c.map_replay:
+            self._map_rep = open(c.map_replay)
+            head = [self._map_rep.readline() for _ in range(self.n_layers + 1)]
+            if "".join(head) != self.map_header():
+                raise MoeError(-6, f"map replay {c.map_replay}: the header does not match this stack")
+        if c.route_trace:
+            self._trace = open(c.route_trace, "w")
+        self._map_frame()
+
+    def _map_frame(self):
+        """After every step (and once at start): replay -- read the frame of
+        this step and place it (uploads of the experts a slot does not hold
+        yet, then the tables); record -- write the published placement
+        (patches/0008:440-489)."""
+        if self._map_rep is not None:
+            steps = self.stats()["steps"]
+            head = self._map_rep.readline().split()
+            if head != ["step", str(steps)]:
+                raise MoeError(-6, f"map replay: expected frame 'step {steps}', read {' '.join(head)!r}")
+            torch.cuda.synchronize(self.device)   # no upload may land after the placement
+            for il in range(self.n_layers):
+                toks = self._map_rep.readline().split()
+                if len(toks) != 2 + self.ns[il] or toks[:2] != ["map", str(il)]:
+                    raise MoeError(-6, f"map replay: bad frame line for layer {il}")
+                self.place(il, [int(v) for v in toks[2:]], copy=True)
+        if self._map_rec is not None:
+            self._map_rec.write(self.map_frame())
+            self._map_rec.flush()
+
+    def _trace_routes(self, layer_ids, slots):
+        """Route trace lines "route <steps> <layer> <n_ids> <n_tokens> id:slot
+        ..." (patches/0008:508-518): layer_ids {layer: ids [n_tok, n_used]},
+        slots {layer: expert -> slot (-1 absent)} as the router saw them."""
+        steps = self.stats()["steps"]
+        for il, ids in layer_ids.items():
+            ids = np.asarray(ids).reshape(-1, self.n_used)
+            es = slots[il]
+            body = " ".join(f"{int(e)}:{int(es[e])}" for e in ids.ravel())
+            self._trace.write(f"route {steps} {il} {self.n_used} {ids.shape[0]} {body}\n")
+
     def close(self):
+        for f in (self._map_rec, self._map_rep, self._trace):
+            if f is not None:
+                f.close()
+        self._map_rec = self._map_rep = self._trace = None
         if getattr(self, "ctx", None):
             self.lib.moe_destroy(self.ctx)
             self.ctx = None
@@ -178,6 +252,8 @@ class MoeStack:
     # -- hot path -------------------------------------------------------------
     def layer_forward(self, layer, x, stream=None):
         """x [n_tok, n_embd] fp32 (device) -> (y, ids, w)."""
+        self.start()
+        slots = {layer: self.tables(layer)["expert_slot"]} if self._trace is not None else None
         x = x.contiguous()
         n_tok = x.shape[0]
         y = torch.empty_like(x)
@@ -185,6 +261,8 @@ class MoeStack:
         w = torch.empty(n_tok, self.n_used, dtype=torch.float32, device=x.device)
         self._ck(self.lib.moe_layer_forward(self.ctx, layer, _ptr(x), _ptr(y), n_tok, _ptr(ids),
                                             _ptr(w), _stream(stream)), "moe_layer_forward")
+        if slots is not None:
+            self._trace_routes({layer: ids.cpu().numpy()}, slots)
         return y, ids, w
 
     def layer_forward_path(self, layer, x, path="auto", stream=None):
@@ -224,11 +302,16 @@ class MoeStack:
         debug; with profile, dumps["prof"] holds the per-CTA phase timestamps
         [n_tok, n_layers, 12, grid] in ns).  starve = r + 1 is for tests of
         the watchdog: rank r's first activation wait can then only run out."""
+        self.start()
         h = h.contiguous()
         n_tok = h.shape[0]
         out = torch.empty_like(h) if out is None else out
         dbg = None
         dumps = None
+        trace = self._trace is not None
+        if trace:   # the routed ids are needed: take the dumps, return them only on request
+            slots = {il: self.tables(il)["expert_slot"] for il in range(self.n_layers)}
+            want_dumps, debug = debug, True
         if debug:
             L, K, H = self.n_layers, self.n_used, self.n_embd
             dumps = {
@@ -249,6 +332,10 @@ class MoeStack:
         self._ck(self.lib.moe_decode(self.ctx, _ptr(h), _ptr(out), n_tok,
                                      C.byref(dbg) if dbg is not None else None, _stream(stream)),
                  "moe_decode")
+        if trace:
+            ids = dumps["ids"].cpu().numpy()   # [n_tok, L, k]
+            self._trace_routes({il: ids[:, il] for il in range(self.n_layers)}, slots)
+            debug = want_dumps
         return (out, dumps) if debug else out
 
     def decode_host(self, h_host, out_host, stream=None):
@@ -279,7 +366,21 @@ class MoeStack:
                                       _stream(stream)), "moe_observe")
 
     def step(self, stream=None):
+        """llama_moe_cache_step: publish, schedule, flush (moe_step); then, as
+        the reference, the heat file every 512 steps (patches/0007:749-753)
+        and the map frame of this step."""
+        self.start()
         self._ck(self.lib.moe_step(self.ctx, _stream(stream)), "moe_step")
+        c = self.cache
+        if c.heat_file and not c.freeze and self.stats()["steps"] % 512 == 0:
+            try:
+                save_heat(c.heat_file, np.stack([self.gate_state(il)["use_count"]
+                                                 for il in range(self.n_layers)]))
+            except OSError:
+                print(f"moe-cache: heat file write FAILED: {c.heat_file}", file=sys.stderr)
+        self._map_frame()
+        if self._trace is not None:
+            self._trace.flush()
 
     def tables(self, layer):
         ns = self.ns[layer]

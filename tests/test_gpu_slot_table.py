@@ -179,3 +179,113 @@ def test_decode_with_cache_config2_scale(oracle_lib):
     assert used <= budget and len(set(caps)) > 1
     s = _decode_with_cache(oracle_lib, L=L, n_tok=64, ns=56, profile=caps, seed=44)
     assert s["hits"] > 0 and s["copied"] > 0
+
+
+def _cached_pair(tmp_path, seed=61, L=3, ns=20):
+    """A stack with a constrained cache over host weights (misses zero-copy,
+    uploads on the copy stream), plus the host weights and routers to build
+    another one with the same weights."""
+    from moe_prefetch_b200 import MoeCacheConfig, MoeStack
+    E = 128
+    src = MoeStack(n_layers=L)
+    src.synth_resident(seed=seed, keep_router=True)
+    host = []
+    for il in range(L):
+        g, u, d = src.slot_views(il)
+        host.append(tuple(v[:E].contiguous().cpu().pin_memory() for v in (g, u, d)))
+    routers = [r.clone() for r in src.routers]
+    src.close()
+    torch.cuda.synchronize()
+
+    def make(**kw):
+        args = dict(n_slots=ns, max_inserts=2, admit="window", batch_tables=True, cache_prior=0.01)
+        args.update(kw)
+        cfg = MoeCacheConfig(**args)
+        st = MoeStack(n_layers=L, cache=cfg)
+        for il in range(L):
+            st.set_router(il, routers[il])
+            st.set_expert_weights(il, *host[il])
+        return st
+    return make
+
+
+def _run_tokens(st, h):
+    outs, tabs = [], []
+    for t in range(h.shape[0]):
+        outs.append(st.decode(torch.from_numpy(h[t:t + 1]).cuda()).cpu().numpy())
+        st.step()
+        st.sync()
+        tabs.append([st.tables(il)["expert_slot"].copy() for il in range(st.n_layers)])
+    return np.concatenate(outs), tabs
+
+
+def test_map_record_replay_reproduces_tables_and_outputs(tmp_path):
+    """LLAMA_MOE_MAP_RECORD writes the published placement after every step;
+    a stack with LLAMA_MOE_MAP_REPLAY of that file (and a different insert
+    budget of its own) reproduces every step's tables and every output bit
+    for bit (patches/0008:417-518).  LLAMA_MOE_ROUTE_TRACE lines carry the
+    routed ids and the slots the router saw."""
+    _needs_gpu()
+    make = _cached_pair(tmp_path)
+    rec, trace = str(tmp_path / "map.txt"), str(tmp_path / "route.txt")
+    h = ar1_states(20, H, seed=9)
+    st = make(map_record=rec, route_trace=trace)
+    out_a, tabs_a = _run_tokens(st, h)
+    s_a = st.stats()
+    st.close()
+    assert s_a["published"] > 0 and s_a["misses"] > 0
+    lines = open(rec).read().splitlines()
+    assert lines[0] == "moe-map 1 3" and lines[1] == "layer 0 20 128"
+    assert sum(1 for ln in lines if ln.startswith("step ")) == 21          # step 0 .. 20
+    routes = open(trace).read().splitlines()
+    assert len(routes) == 20 * 3
+    f = routes[4].split()                                                 # token 1, layer 1
+    assert f[:5] == ["route", "1", "1", "8", "1"] and len(f) == 5 + 8
+    assert all(int(p.split(":")[0]) in range(128) and int(p.split(":")[1]) in range(-1, 20) for p in f[5:])
+    # replay with another budget of its own: the frames decide the placement
+    st = make(map_replay=rec, max_inserts=1)
+    out_b, tabs_b = _run_tokens(st, h)
+    st.close()
+    assert np.array_equal(out_a.view(np.uint32), out_b.view(np.uint32))
+    for ta, tb in zip(tabs_a, tabs_b):
+        for a, b in zip(ta, tb):
+            assert np.array_equal(a, b)
+    # a frame that does not match the stack is refused
+    from moe_prefetch_b200._lib import MoeError
+    bad = str(tmp_path / "bad.txt")
+    with open(bad, "w") as fh:
+        fh.write("moe-map 1 2\nlayer 0 20 128\nlayer 1 20 128\n")
+    st = make(map_replay=bad)
+    with pytest.raises(MoeError):
+        st.decode(torch.from_numpy(h[:1]).cuda())
+    st.close()
+
+
+def test_heat_file_saved_every_512_steps_and_warm_starts(tmp_path):
+    """LLAMA_MOE_HEAT_FILE: the routed-use counts go to the file every 512
+    steps (patches/0007:749-753), and a new stack places the hottest experts
+    before its first token (0007:567-618): the counts halved on load, the
+    hottest in slot 0, never-routed experts left out."""
+    _needs_gpu()
+    from moe_prefetch_b200.stack import load_heat
+    make = _cached_pair(tmp_path, L=2, ns=6)
+    path = str(tmp_path / "heat.txt")
+    st = make(heat_file=path)
+    hot = [[5, 9, 17, 33, 40, 64, 70, 99], [1, 2, 3, 4, 5, 6, 7, 8]]
+    for step in range(512):
+        for il in range(2):
+            ids = torch.tensor(hot[il] if step % 2 == 0 else hot[il][:4], dtype=torch.int32, device="cuda")
+            st.observe(il, ids)
+        st.step()
+    st.sync()
+    st.close()
+    counts = load_heat(path, 2, 128)
+    assert counts is not None
+    assert counts[0, 5] == 512 // 2 and counts[0, 40] == 256 // 2 and counts[0, 6] == 0
+    st = make(heat_file=path)
+    st.start()
+    for il in range(2):
+        se = st.tables(il)["slot_expert"]
+        assert list(se[:4]) == hot[il][:4]                    # 512 uses each, in id order
+        assert set(se[4:6]) <= set(hot[il][4:]) and (se >= 0).all()
+    st.close()
