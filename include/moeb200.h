@@ -65,7 +65,8 @@ typedef struct moe_cfg {
     int32_t batch_tables;      /* LLAMA_MOE_BATCH_TABLES (tables always move in one
                                   device step here; kept for the stats counter)   */
     float   cache_prior;       /* LLAMA_MOE_CACHE_PRIOR, delta (0 = off)           */
-    int32_t early_issue;       /* LLAMA_MOE_EARLY_ISSUE (must be 0 on device)      */
+    int32_t early_issue;       /* LLAMA_MOE_EARLY_ISSUE: uploads start when a layer
+                                  is observed, into a free pool the step refills  */
     int32_t freeze;            /* LLAMA_MOE_CACHE_FREEZE                           */
     int32_t use_heat_counts;   /* a heat file is configured (LLAMA_MOE_HEAT_FILE)  */
     int32_t device;            /* CUDA device ordinal                              */
@@ -73,6 +74,8 @@ typedef struct moe_cfg {
                                   shared expert joins every token after the k
                                   routed ones with weight 1; it is never cached,
                                   observed or routed (moe_set_shared_expert)      */
+    int32_t predict_top;       /* LLAMA_MOE_PREDICT_TOP (0 -> 3): speculative
+                                  uploads per observed layer with a predictor     */
 } moe_cfg;
 
 /* What llama_moe_cache_lookup(up_exps) returns for one layer
@@ -369,10 +372,35 @@ int moe_decode_info(const moe_ctx *ctx, int32_t *out, int n);
 
 /* ---- the slot cache step ------------------------------------------------------- */
 
+/* Host callbacks of the per-layer entry points (moe_layer_forward,
+ * moe_layer_forward_path and moe_observe with one token), called after the
+ * layer's observation on the device, with the stream synchronised.
+ *
+ * moe_observe_fn replaces ggml_set_moe_obs_callback's callback
+ * (patches/0006:752): the layer and its routed ids (host copy, n_tok x n_ids).
+ *
+ * moe_predict_fn is the reference's predictor hook (cpp/moe-predictor.h:38-106
+ * as called from moe_obs_cb, patches/0006:367-397, 0007:294-321): given this
+ * layer's ids `cur` and the ids the next layer saw at the previous token
+ * (`next_prev`), write up to k ids for the next layer to `out` and return how
+ * many.  With early issue they become speculative uploads (at most
+ * predict_top, keeping max_inserts slots of the pool for demand; probation
+ * with spec_probation); an installed predictor also grows the free pool's
+ * target by predict_top.  The persistent decode kernel (moe_decode) observes
+ * on the device and issues the admitted misses early, but calls neither
+ * callback: the host does not see its layers one at a time. */
+typedef void (*moe_observe_fn)(void *ud, int layer, const int32_t *ids, int n_tok, int n_ids);
+typedef int (*moe_predict_fn)(void *ud, int layer, const int32_t *cur, int n_cur,
+                              const int32_t *next_prev, int n_next_prev, int32_t *out, int k);
+int moe_set_observe_hook(moe_ctx *ctx, moe_observe_fn fn, void *ud);
+int moe_set_predictor(moe_ctx *ctx, moe_predict_fn fn, void *ud);
+
 /* Observe one layer's routed ids (device [n_tok][n_ids]) outside
  * moe_layer_forward: hits refresh recency, misses feed the second-miss window
- * and the pending list.  Only n_tok == 1 is observed.  Replaces moe_obs_cb
- * (patches/0006:295-400, 0007:247-321). */
+ * and the pending list; with early issue the admitted misses take slots of
+ * the free pool and their uploads start (then the predictor, below).  Only
+ * n_tok == 1 is observed.  Replaces moe_obs_cb (patches/0006:295-400,
+ * 0007:247-321). */
 int moe_observe(moe_ctx *ctx, int layer, const int32_t *ids, int n_tok, int n_ids,
                 void *stream);
 

@@ -36,8 +36,14 @@ class MoeCfg(C.Structure):
         ("admit_floor", C.c_float), ("spec_probation", C.c_int32),
         ("batch_tables", C.c_int32), ("cache_prior", C.c_float), ("early_issue", C.c_int32),
         ("freeze", C.c_int32), ("use_heat_counts", C.c_int32), ("device", C.c_int32),
-        ("n_shared", C.c_int32),
+        ("n_shared", C.c_int32), ("predict_top", C.c_int32),
     ]
+
+
+# host callbacks of include/moeb200.h
+OBSERVE_FN = C.CFUNCTYPE(None, C.c_void_p, C.c_int, C.POINTER(C.c_int32), C.c_int, C.c_int)
+PREDICT_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_int, C.POINTER(C.c_int32), C.c_int,
+                         C.POINTER(C.c_int32), C.c_int, C.POINTER(C.c_int32), C.c_int)
 
 
 class MoeLayerInfo(C.Structure):
@@ -72,6 +78,8 @@ SIGNATURES = {
     "moe_ep_route_pack": (I, [P, I, P, I, I, I, P, P, P, P, P, P, P]),
     "moe_experts_rows": (I, [P, I, P, P, I, P, I, P]),
     "moe_ep_combine": (I, [P, P, P, P, I, P, P, P]),
+    "moe_set_observe_hook": (I, [P, P, P]),
+    "moe_set_predictor": (I, [P, P, P]),
     "moe_ep_mailbox_create": (I, [P, I, I, I, P]),
     "moe_ep_mailbox_connect": (I, [P, P]),
     "moe_ep_push": (I, [P, I, P, P, P, P]),

@@ -83,7 +83,14 @@ struct moe_ctx {
     cudaStream_t copy_stream = nullptr;
     cudaEvent_t ev_step = nullptr, ev_copy = nullptr;
     bool copies_pending = false;
-    int32_t *h_jobs = nullptr;         // mapped pinned [L*MI*4 + 4]
+    int32_t *h_jobs = nullptr;         // mapped pinned [L * job_cap * 4 + 4]
+    int jobs_issued = 0;               // early issue: jobs of this step already copying
+    // host callbacks (moe_set_predictor / moe_set_observe_hook)
+    moe_predict_fn predict = nullptr;
+    void *predict_ud = nullptr;
+    moe_observe_fn obs_hook = nullptr;
+    void *obs_ud = nullptr;
+    int32_t *d_pred = nullptr;         // device [64]: the predictor's ids
     int32_t *d_jobs_alias = nullptr;
     uint64_t upload_bytes = 0;
     uint64_t upload_ns = 0;          // time the copy stream spent on step uploads
@@ -146,7 +153,8 @@ extern "C" int moe_create(const moe_cfg *cfg, moe_ctx **out) {
     if (g.n_ff % 256 || g.n_ff > 1024) return bad(MOE_ERR_UNSUPPORTED, "n_ff must be a multiple of 256, <= 1024");
     if (g.down_type != MOE_QTYPE_Q6_K && g.down_type != MOE_QTYPE_Q4_K)
         return bad(MOE_ERR_UNSUPPORTED, "down_type must be Q6_K or Q4_K");
-    if (g.early_issue) return bad(MOE_ERR_UNSUPPORTED, "early issue is not implemented on the device");
+    if (g.predict_top <= 0) g.predict_top = 3;
+    if (g.predict_top > 64) return bad(MOE_ERR_ARG, "predict_top must be <= 64");
     if (g.admit_mode < 0 || g.admit_mode > 2) return bad(MOE_ERR_ARG, "admit_mode");
     if (g.n_shared < 0 || g.n_shared > 1) return bad(MOE_ERR_UNSUPPORTED, "n_shared must be 0 or 1");
     if (g.n_slots <= 0 && !cfg->slot_profile) return bad(MOE_ERR_ARG, "n_slots must be > 0");
@@ -205,7 +213,8 @@ extern "C" int moe_create(const moe_cfg *cfg, moe_ctx **out) {
     cudaMemset(c->router_t, 0, sizeof(float) * (size_t)L * E * H);
     // slot state
     {
-        const size_t LE = (size_t)L * E, S = (size_t)c->sum_ns, MI = (size_t)g.max_inserts > 0 ? g.max_inserts : 1;
+        const size_t LE = (size_t)L * E, S = (size_t)c->sum_ns;
+        const size_t MI = (size_t)(g.max_inserts > 0 ? g.max_inserts : 1) + (g.early_issue ? g.predict_top : 0);
         std::vector<size_t> sz = {
             LE * 4,            // table
             S * 4,             // slot_expert
@@ -222,7 +231,10 @@ extern "C" int moe_create(const moe_cfg *cfg, moe_ctx **out) {
             (size_t)G_COUNT * 8,                // globals
             (size_t)L * MI * 16,                // jobs
             (size_t)L * 4,                      // n_jobs
-            (size_t)L * 4, (size_t)L * 4        // ns, slot_off
+            (size_t)L * 4, (size_t)L * 4,       // ns, slot_off
+            S * 4, (size_t)L * 4,               // free_slots, n_free
+            LE * 4,                             // admitted
+            (size_t)L * CUR_IDS * 4, (size_t)L * 4   // cur_ids, n_cur
         };
         size_t total = 0;
         std::vector<size_t> off;
@@ -255,6 +267,24 @@ extern "C" int moe_create(const moe_cfg *cfg, moe_ctx **out) {
         c->d_slot_off = (int32_t *)(b + off[17]);
         st.ns = c->d_ns;
         st.slot_off = c->d_slot_off;
+        st.job_cap = (int)MI;
+        st.early_issue = g.early_issue;
+        st.predict_top = g.predict_top;
+        st.have_pred = 0;
+        st.free_slots = (int32_t *)(b + off[18]);
+        st.n_free = (int32_t *)(b + off[19]);
+        st.admitted = (int32_t *)(b + off[20]);
+        st.cur_ids = (int32_t *)(b + off[21]);
+        st.n_cur = (int32_t *)(b + off[22]);
+        {   // every slot free; the lowest on top of each pool
+            std::vector<int32_t> fs(S), nf(L);
+            for (int l = 0; l < L; ++l) {
+                for (int q = 0; q < c->ns[l]; ++q) fs[c->slot_off[l] + q] = c->ns[l] - 1 - q;
+                nf[l] = c->ns[l];
+            }
+            cudaMemcpy(st.free_slots, fs.data(), 4 * S, cudaMemcpyHostToDevice);
+            cudaMemcpy(st.n_free, nf.data(), 4 * (size_t)L, cudaMemcpyHostToDevice);
+        }
         cudaMemcpy(c->d_ns, c->ns.data(), 4 * L, cudaMemcpyHostToDevice);
         cudaMemcpy(c->d_slot_off, c->slot_off.data(), 4 * L, cudaMemcpyHostToDevice);
         std::vector<int32_t> tbl((size_t)L * E), se(S, -1);
@@ -322,11 +352,17 @@ extern "C" int moe_create(const moe_cfg *cfg, moe_ctx **out) {
     }
     // uploader
     {
-        const size_t MI = (size_t)(g.max_inserts > 0 ? g.max_inserts : 1);
+        const size_t MI = (size_t)c->st.job_cap;
         const size_t nb = ((size_t)L * MI + 4) * 4 * sizeof(int32_t);
         if (cudaHostAlloc((void **)&c->h_jobs, nb, cudaHostAllocMapped) != cudaSuccess) return cleanup_fail(MOE_ERR_OOM);
         memset(c->h_jobs, 0, nb);
         if (cudaHostGetDevicePointer((void **)&c->d_jobs_alias, c->h_jobs, 0) != cudaSuccess) return cleanup_fail(MOE_ERR_CUDA);
+        // the device side writes jobs there (at the step, or at observation
+        // with early issue); the count follows the L * job_cap entries
+        c->st.host_jobs = c->d_jobs_alias;
+        c->st.host_njobs = c->d_jobs_alias + (size_t)L * MI * 4;
+        c->dp.st = c->st;
+        if (cudaMalloc(&c->d_pred, 64 * sizeof(int32_t)) != cudaSuccess) return cleanup_fail(MOE_ERR_OOM);
         if (cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking) != cudaSuccess ||
             cudaEventCreateWithFlags(&c->ev_step, cudaEventDisableTiming) != cudaSuccess ||
             cudaEventCreateWithFlags(&c->ev_copy, cudaEventDisableTiming) != cudaSuccess ||
@@ -379,6 +415,7 @@ extern "C" void moe_destroy(moe_ctx *c) {
     if (c->ev_step) cudaEventDestroy(c->ev_step);
     if (c->ev_copy) cudaEventDestroy(c->ev_copy);
     if (c->ev_up0) cudaEventDestroy(c->ev_up0);
+    cudaFree(c->d_pred);
     if (c->ev_up1) cudaEventDestroy(c->ev_up1);
     if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
     delete c;
@@ -605,6 +642,39 @@ static int check_shared(moe_ctx *c, int layer) {
     return MOE_OK;
 }
 
+// After a single-token layer was observed (patches/0006:295-400, 0007:
+// 271-321): the observe hook with the routed ids; with early issue and a
+// predictor, the predictor's ids for the next layer go to k_issue_spec
+// (speculative uploads); with early issue the new jobs' copies start now.
+// Synchronises the stream only when one of these is on.
+static int issue_early_copies(moe_ctx *c, cudaStream_t s);
+static int after_observe(moe_ctx *c, int layer, const int32_t *ids_dev, int n_ids, cudaStream_t s) {
+    const bool pred = c->cfg.early_issue && c->predict && layer + 1 < c->cfg.n_layers;
+    if (!c->obs_hook && !pred && !c->cfg.early_issue) return MOE_OK;
+    CK(cudaStreamSynchronize(s));
+    int32_t cur[64];
+    const int n = n_ids < 64 ? n_ids : 64;
+    if (c->obs_hook || pred) CK(cudaMemcpy(cur, ids_dev, 4 * (size_t)n, cudaMemcpyDeviceToHost));
+    if (c->obs_hook) c->obs_hook(c->obs_ud, layer, cur, 1, n);
+    if (pred) {
+        int32_t nprev[CUR_IDS];
+        int n_nprev = 0;
+        CK(cudaMemcpy(&n_nprev, c->st.n_cur + layer + 1, 4, cudaMemcpyDeviceToHost));
+        n_nprev = std::min(std::max(n_nprev, 0), CUR_IDS);
+        if (n_nprev)
+            CK(cudaMemcpy(nprev, c->st.cur_ids + (size_t)(layer + 1) * CUR_IDS, 4 * (size_t)n_nprev,
+                          cudaMemcpyDeviceToHost));
+        int32_t top[64];
+        const int k = c->cfg.predict_top;
+        int nt = c->predict(c->predict_ud, layer, cur, n, nprev, n_nprev, top, k);
+        nt = std::min(std::max(nt, 0), k);
+        if (nt) CK(cudaMemcpy(c->d_pred, top, 4 * (size_t)nt, cudaMemcpyHostToDevice));
+        CK(launch_issue_spec(c->st, layer + 1, c->d_pred, nt, s));
+    }
+    if (c->cfg.early_issue) return issue_early_copies(c, s);
+    return MOE_OK;
+}
+
 extern "C" int moe_layer_forward(moe_ctx *c, int layer, const float *x, float *y, int n_tok,
                                  int32_t *ids, float *w, void *stream) {
     if (!c || !x || !y || n_tok <= 0 || layer < 0 || layer >= c->cfg.n_layers)
@@ -628,6 +698,7 @@ extern "C" int moe_layer_forward(moe_ctx *c, int layer, const float *x, float *y
     if (n_tok == 1) {
         CK(launch_experts(make_src(c, layer), x, ids_e, w_e, n_tok, kx, g.n_embd, g.n_ff,
                           g.down_type, c->s_act, nullptr, y, c->err, s));
+        return after_observe(c, layer, ids_d, g.n_used, s);
     } else {
         // a batch: group the pairs by expert so that each expert's rows are
         // read once per tile of its tokens (bit-identical results)
@@ -684,7 +755,7 @@ extern "C" int moe_layer_forward_path(moe_ctx *c, int layer, const float *x, flo
     CK(launch_group(ids_e, n_tok * kx, g.n_expert + g.n_shared, GM_NT, c->grp, c->err, s));
     CK(launch_experts_gemm(make_src(c, layer), x, c->grp, n_tok, kx, g.n_embd, g.n_ff,
                            g.down_type, w_e, c->s_gemm, c->s_ypair, nullptr, y, c->err, s));
-    return MOE_OK;
+    return n_tok == 1 ? after_observe(c, layer, ids_d, g.n_used, s) : MOE_OK;
 }
 
 // ---- expert parallelism -------------------------------------------------------
@@ -1065,6 +1136,22 @@ extern "C" int moe_observe(moe_ctx *c, int layer, const int32_t *ids, int n_tok,
     if (n_tok != 1) return MOE_OK;   // the reference's callback returns early for batches
     CK(cudaSetDevice(c->cfg.device));
     CK(launch_observe(c->st, layer, ids, n_ids, (cudaStream_t)stream));
+    return after_observe(c, layer, ids, n_ids, (cudaStream_t)stream);
+}
+
+extern "C" int moe_set_predictor(moe_ctx *c, moe_predict_fn fn, void *ud) {
+    if (!c) return MOE_ERR_ARG;
+    c->predict = fn;
+    c->predict_ud = ud;
+    c->st.have_pred = fn != nullptr;   // the free pool's target grows by predict_top
+    c->dp.st.have_pred = c->st.have_pred;
+    return MOE_OK;
+}
+
+extern "C" int moe_set_observe_hook(moe_ctx *c, moe_observe_fn fn, void *ud) {
+    if (!c) return MOE_ERR_ARG;
+    c->obs_hook = fn;
+    c->obs_ud = ud;
     return MOE_OK;
 }
 
@@ -1078,24 +1165,14 @@ static void harvest_upload_time(moe_ctx *c) {
     c->up_timed = false;
 }
 
-extern "C" int moe_step(moe_ctx *c, void *stream) {
-    if (!c) return MOE_ERR_ARG;
-    CK(cudaSetDevice(c->cfg.device));
-    cudaStream_t s = (cudaStream_t)stream;
-    if (c->copies_pending) CK(cudaStreamWaitEvent(s, c->ev_copy, 0));
-    CK(launch_step(c->st, c->d_jobs_alias, c->d_jobs_alias + (size_t)c->cfg.n_layers *
-                   (c->cfg.max_inserts > 0 ? c->cfg.max_inserts : 1) * 4, s));
-    CK(cudaEventRecord(c->ev_step, s));
-    CK(cudaEventSynchronize(c->ev_step));
-    const size_t MI = (size_t)(c->cfg.max_inserts > 0 ? c->cfg.max_inserts : 1);
-    volatile int32_t *nj_p = c->h_jobs + (size_t)c->cfg.n_layers * MI * 4;
-    const int nj = *nj_p;
-    c->copies_pending = false;
-    harvest_upload_time(c);   // the previous batch is done: the step kernel waited for it
-    if (nj > 0 && !c->up_timed) {
+// Copies for the jobs in the mapped list from index `from` on, on the copy
+// stream; ev_copy follows them.  The caller has synchronised with the
+// device work that wrote the list.
+static int issue_job_copies(moe_ctx *c, int from, int nj) {
+    if (nj > from && !c->up_timed) {
         CK(cudaEventRecord(c->ev_up0, c->copy_stream));
     }
-    for (int j = 0; j < nj; ++j) {
+    for (int j = from; j < nj; ++j) {
         const int l = c->h_jobs[4 * j], e = c->h_jobs[4 * j + 1], slot = c->h_jobs[4 * j + 2];
         if (l < 0 || l >= c->cfg.n_layers || e < 0 || e >= c->cfg.n_expert || slot < 0 || slot >= c->L[l].ns)
             return fail(c, MOE_ERR_DEVICE, "moe_step: bad job (%d, %d, %d)", l, e, slot);
@@ -1111,15 +1188,56 @@ extern "C" int moe_step(moe_ctx *c, void *stream) {
                            c->down_bytes, cudaMemcpyHostToDevice, c->copy_stream));
         c->upload_bytes += 2 * c->gate_bytes + c->down_bytes;
     }
-    if (nj > 0) {
-        if (!c->up_timed) {
-            CK(cudaEventRecord(c->ev_up1, c->copy_stream));
-            c->up_timed = true;
-        }
+    if (nj > from) {
+        CK(cudaEventRecord(c->ev_up1, c->copy_stream));   // the end of this step's copies so far
+        c->up_timed = true;
         CK(cudaEventRecord(c->ev_copy, c->copy_stream));
         c->copies_pending = true;
     }
     return MOE_OK;
+}
+
+static volatile int32_t *host_njobs(moe_ctx *c) {
+    return c->h_jobs + (size_t)c->cfg.n_layers * c->st.job_cap * 4;
+}
+
+// Early issue: copies for the jobs the device issued since the last call
+// (after the device work of `stream` that may have issued them).
+static int issue_early_copies(moe_ctx *c, cudaStream_t s) {
+    CK(cudaStreamSynchronize(s));
+    const int nj = *host_njobs(c);
+    const int r = issue_job_copies(c, c->jobs_issued, nj);
+    c->jobs_issued = nj;
+    return r;
+}
+
+extern "C" int moe_step(moe_ctx *c, void *stream) {
+    if (!c) return MOE_ERR_ARG;
+    CK(cudaSetDevice(c->cfg.device));
+    cudaStream_t s = (cudaStream_t)stream;
+    if (c->cfg.early_issue) {
+        // the jobs of this step were issued when the layers were observed:
+        // copy what is not copying yet, publish once every copy is done
+        // (deterministic publication), then top the free pools up
+        int r = issue_early_copies(c, s);
+        if (r != MOE_OK) return r;
+        if (c->copies_pending) CK(cudaStreamWaitEvent(s, c->ev_copy, 0));
+        CK(launch_step(c->st, c->st.host_jobs, c->st.host_njobs, s));
+        CK(cudaEventRecord(c->ev_step, s));
+        CK(cudaEventSynchronize(c->ev_step));
+        c->copies_pending = false;
+        c->jobs_issued = 0;
+        harvest_upload_time(c);
+        return MOE_OK;
+    }
+    if (c->copies_pending) CK(cudaStreamWaitEvent(s, c->ev_copy, 0));
+    CK(launch_step(c->st, c->st.host_jobs, c->st.host_njobs, s));
+    CK(cudaEventRecord(c->ev_step, s));
+    CK(cudaEventSynchronize(c->ev_step));
+    const int nj = *host_njobs(c);
+    c->copies_pending = false;
+    harvest_upload_time(c);   // the previous batch is done: the step kernel waited for it
+    return issue_job_copies(c, 0, nj);
 }
 
 extern "C" int moe_requires_sync(const moe_ctx *c) { return c ? 1 : 0; }
@@ -1188,7 +1306,10 @@ extern "C" int moe_warm_start(moe_ctx *c, const uint32_t *use_count) {
         for (int e = 0; e < E; ++e) order[e] = e;
         std::stable_sort(order.begin(), order.end(), [&](int32_t a, int32_t b) { return uc[a] > uc[b]; });
         const int ns = c->L[l].ns;
-        const int fill = ns;   // no reserve: early issue is off on the device
+        // with early issue the free pool keeps its target free (0007:577-579)
+        const int reserve = c->cfg.early_issue
+            ? c->cfg.max_inserts + (c->st.have_pred ? c->cfg.predict_top : 0) : 0;
+        const int fill = std::max(0, ns - reserve);
         std::vector<int32_t> se(ns, -1);
         std::vector<uint64_t> lu(ns, 0);
         int slot = 0;
@@ -1204,6 +1325,12 @@ extern "C" int moe_warm_start(moe_ctx *c, const uint32_t *use_count) {
         const int r = moe_place(c, l, se.data(), 1);
         if (r != MOE_OK) return r;
         CK(cudaMemcpy(c->st.last_use + c->slot_off[l], lu.data(), 8 * (size_t)ns, cudaMemcpyHostToDevice));
+        // the free pool: every slot past the placed ones, the lowest on top
+        std::vector<int32_t> fs;
+        for (int f = ns - 1; f >= slot; --f) fs.push_back(f);
+        const int nf = (int)fs.size();
+        if (nf) CK(cudaMemcpy(c->st.free_slots + c->slot_off[l], fs.data(), 4 * (size_t)nf, cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(c->st.n_free + l, &nf, 4, cudaMemcpyHostToDevice));
     }
     CK(cudaMemcpy(c->st.g + G_CLOCK, &clock, 8, cudaMemcpyHostToDevice));
     return placed;

@@ -102,7 +102,8 @@ __device__ __forceinline__ void red_add_u64(uint64_t *p, uint64_t v) {
     asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-// moe_obs_cb for one decode layer, one warp of CTA 0.  Hits are stamped in
+// moe_obs_cb for one decode layer, one warp of CTA 0 (with early issue,
+// lane 0 then issues the admitted misses' uploads).  Hits are stamped in
 // parallel: the i-th routed id, if resident, gets clock + (hits before i) + 1,
 // which is what the reference's sequential ++clock produces (the k ids are
 // distinct).  Counters that only CTA 0 writes during the launch (the clock)
@@ -155,6 +156,13 @@ __device__ __forceinline__ void observe_decode(const SlotState &st, int layer,
             st.n_pending[layer] = np;
         }
     }
+    // early issue: the admitted pending misses take slots of the free pool
+    // now, after every lane's heat and recency updates (the clock in st.g is
+    // not read there)
+    __syncwarp();
+    if (st.early_issue && lane == 0) early_issue_pending(st, layer);
+    if (st.cur_ids && in) st.cur_ids[(size_t)layer * CUR_IDS + lane] = id;
+    if (st.cur_ids && lane == 0) st.n_cur[layer] = k;
     __syncwarp();
 }
 

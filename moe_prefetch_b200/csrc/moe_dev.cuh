@@ -1181,16 +1181,129 @@ struct SlotState {
     uint64_t *n_hit;            // [L]
     uint64_t *n_miss;           // [L]
     uint64_t *g;                // globals: see G_* below
-    int32_t *jobs;              // [L][max_inserts][4] (expert, slot, spec, -)
+    int32_t *jobs;              // [L][job_cap][4] (expert, slot, spec, -)
     int32_t *n_jobs;            // [L]
+    int job_cap;                // jobs per layer: max_inserts (+ predict_top with early issue)
+    // early issue (patches/0006:251-293, 0007:230-246): uploads start when a
+    // layer is observed, into slots from a free pool that the step tops up
+    int early_issue, predict_top, have_pred;
+    int32_t *free_slots;        // [sum ns] each layer's free pool, a stack (top = last)
+    int32_t *n_free;            // [L]
+    int32_t *admitted;          // [L][E] scratch: the pending ids that passed admission
+    int32_t *cur_ids;           // [L][CUR_IDS] ids each layer observed last (the predictor's next_prev)
+    int32_t *n_cur;             // [L]
+    int32_t *host_jobs;         // mapped host: (layer, expert, slot, spec) since the last step
+    int32_t *host_njobs;        // mapped host: their count
 };
+
+// ids a layer keeps of its last observation, for the predictor
+#define CUR_IDS 64
 
 enum { G_CLOCK = 0, G_STEPS, G_UPLOADS, G_SCHEDULED, G_COPIED, G_PUBLISHED, G_ADMIT_OK,
        G_ADMIT_DENIED, G_FLUSHES, G_UPLOAD_BYTES, G_COUNT };
 
+// lru_resident (patches/0007:398-412): the resident expert of the least
+// recently used slot not in flight, or -1.
+__device__ __forceinline__ int lru_resident_dev(const SlotState &st, int l) {
+    const int ns = st.ns[l], so = st.slot_off[l];
+    int victim = -1;
+    uint64_t best = ~0ull;
+    for (int s = 0; s < ns; ++s) {
+        if (st.in_flight[so + s] || st.slot_expert[so + s] < 0) continue;
+        if (st.last_use[so + s] < best) {
+            best = st.last_use[so + s];
+            victim = st.slot_expert[so + s];
+        }
+    }
+    return victim;
+}
+
+// admit_ok (patches/0007:414-429), counted; one thread.
+__device__ __forceinline__ bool admit_ok_dev(const SlotState &st, int l, int id, int victim) {
+    if (st.admit_mode == 0 || victim < 0) return true;
+    const size_t E = (size_t)st.n_expert;
+    bool ok = true;
+    if (st.admit_mode == 1) {
+        // heat is added to with atomics (from the lanes of the decode
+        // kernel's observer): read it where those land
+        const float *ht = st.heat + (size_t)l * E;
+        ok = __ldcg(ht + id) > __fadd_rn(__fmul_rn(__ldcg(ht + victim), 1.25f), st.admit_floor);
+    } else if (st.admit_mode == 2) {
+        const uint64_t mp = st.miss_prev[(size_t)l * E + id], ml = st.miss_last[(size_t)l * E + id];
+        ok = mp != ~0ull && ml - mp < (uint64_t)st.admit_window;
+    }
+    st.g[ok ? G_ADMIT_OK : G_ADMIT_DENIED] += 1;
+    return ok;
+}
+
+// issue_uploads (patches/0006:251-293, 0007:230-246, 0008:498-500), one
+// thread: up to `budget` of ids (not resident, not already a job of this
+// layer) each take a slot from the layer's free pool while more than
+// min_keep slots are free; the job goes to the layer's list and, for the
+// uploader, to the mapped host list.
+__device__ __forceinline__ int issue_uploads_dev(const SlotState &st, int l, const int32_t *ids, int n,
+                                                 int budget, int min_keep, int spec) {
+    if (st.freeze) return 0;
+    const int E = st.n_expert, ns = st.ns[l], so = st.slot_off[l];
+    const int32_t *tbl = st.table + (size_t)l * E;
+    int32_t *jb = st.jobs + (size_t)l * st.job_cap * 4;
+    int issued = 0;
+    for (int i = 0; i < n && issued < budget; ++i) {
+        const int id = ids[i];
+        if (id < 0 || id >= E || tbl[id] != ns) continue;
+        if (st.n_free[l] <= min_keep) break;
+        const int nj = st.n_jobs[l];
+        bool dup = false;
+        for (int a = 0; a < nj; ++a)
+            if (jb[4 * a] == id) { dup = true; break; }
+        if (dup) continue;
+        if (nj >= st.job_cap) break;   // not reached: the free pool bounds a layer's jobs
+        const int nf = st.n_free[l] - 1;
+        const int slot = st.free_slots[so + nf];
+        st.n_free[l] = nf;
+        st.in_flight[so + slot] = 1;
+        jb[4 * nj] = id; jb[4 * nj + 1] = slot; jb[4 * nj + 2] = spec; jb[4 * nj + 3] = 0;
+        st.n_jobs[l] = nj + 1;
+        st.g[G_UPLOADS] += 1;
+        st.g[G_SCHEDULED] += 1;
+        volatile int32_t *hn = st.host_njobs;
+        const int h = *hn;
+        st.host_jobs[4 * h] = l; st.host_jobs[4 * h + 1] = id;
+        st.host_jobs[4 * h + 2] = slot; st.host_jobs[4 * h + 3] = spec;
+        __threadfence_system();
+        *hn = h + 1;
+        ++issued;
+    }
+    return issued;
+}
+
+// The early-issue half of moe_obs_cb (patches/0006:346-366, 0007:271-293),
+// after a layer's misses are pending: the admitted pending ids take slots of
+// the free pool now (budget max_inserts).  The admission of each pending id
+// is decided against the slot the next top-up would free.  One thread.
+__device__ __forceinline__ void early_issue_pending(const SlotState &st, int l) {
+    const int E = st.n_expert, ns = st.ns[l];
+    const int pool_target = st.freeze ? 0 : st.max_inserts + (st.have_pred ? st.predict_top : 0);
+    const int32_t *pend = st.pending + (size_t)l * E;
+    const int np = st.n_pending[l];
+    if (st.admit_mode == 0) {
+        issue_uploads_dev(st, l, pend, np, st.max_inserts, 0, 0);
+        return;
+    }
+    const int next_victim = st.n_free[l] > pool_target ? -1 : lru_resident_dev(st, l);
+    const int32_t *tbl = st.table + (size_t)l * E;
+    int32_t *adm = st.admitted + (size_t)l * E;
+    int na = 0;
+    for (int q = 0; q < np; ++q) {
+        const int id = pend[q];
+        if (tbl[id] == ns && admit_ok_dev(st, l, id, next_victim)) adm[na++] = id;
+    }
+    issue_uploads_dev(st, l, adm, na, st.max_inserts, 0, 0);
+}
+
 // moe_obs_cb for one single-token layer (patches/0006:295-400 with the
-// 0007:247-270 window/heat bookkeeping; early issue is not on the device).
-// One thread.
+// 0007:247-270 window/heat bookkeeping and, with early issue, the uploads of
+// the admitted misses).  One thread.
 __device__ __forceinline__ void observe_layer(const SlotState &st, int layer,
                                               const int32_t *ids, int n) {
     const int E = st.n_expert;
@@ -1230,6 +1343,12 @@ __device__ __forceinline__ void observe_layer(const SlotState &st, int layer,
         }
     }
     st.g[G_CLOCK] = clock;
+    if (st.early_issue) early_issue_pending(st, layer);
+    if (st.cur_ids) {
+        const int nc = n < CUR_IDS ? n : CUR_IDS;
+        for (int i = 0; i < nc; ++i) st.cur_ids[(size_t)layer * CUR_IDS + i] = ids[i];
+        st.n_cur[layer] = nc;
+    }
 }
 
 }  // namespace moe

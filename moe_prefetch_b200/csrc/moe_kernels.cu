@@ -448,15 +448,41 @@ __global__ void k_observe(SlotState st, int layer, const int32_t *__restrict__ i
     if (threadIdx.x == 0 && blockIdx.x == 0) observe_layer(st, layer, ids, n);
 }
 
-// llama_moe_cache_step on the device (patches/0006:765-953 non-early path,
-// 0007:655-773 admission / probation / heat decay, 0008:613-627 deterministic
+// The predictor's half of moe_obs_cb (patches/0006:367-397, 0007:294-321):
+// speculative uploads of the predicted ids `top` for layer l (the layer after
+// the observed one), with the heat gate when admission is by heat, at most
+// predict_top of them, keeping max_inserts slots of the pool for demand.
+// One thread.
+__global__ void k_issue_spec(SlotState st, int l, const int32_t *__restrict__ top, int n_top) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    const int E = st.n_expert, ns = st.ns[l];
+    if (st.admit_mode == 1) {
+        const int pool_target = st.freeze ? 0 : st.max_inserts + (st.have_pred ? st.predict_top : 0);
+        const int nv = st.n_free[l] > pool_target ? -1 : lru_resident_dev(st, l);
+        const int32_t *tbl = st.table + (size_t)l * E;
+        int32_t *adm = st.admitted + (size_t)l * E;
+        int n = 0;
+        for (int i = 0; i < n_top && n < E; ++i) {
+            const int id = top[i];
+            if (id >= 0 && id < E && tbl[id] == ns && admit_ok_dev(st, l, id, nv)) adm[n++] = id;
+        }
+        issue_uploads_dev(st, l, adm, n, st.predict_top, st.max_inserts, 1);
+    } else {
+        issue_uploads_dev(st, l, top, n_top, st.predict_top, st.max_inserts, 1);
+    }
+}
+
+// llama_moe_cache_step on the device (patches/0006:765-953, 0007:655-773
+// admission / probation / heat decay, 0008:613-627 deterministic
 // publication).  One CTA: thread 0 publishes (the clock order is global),
-// then one thread per layer schedules.  Jobs are also written to `host_jobs`
-// (mapped pinned memory) as (layer, expert, slot, spec) for the uploader.
+// then one thread per layer schedules (without early issue) or tops the free
+// pool back up (with it; the jobs were issued when the layers were
+// observed).  Scheduled jobs are also written to `host_jobs` (mapped pinned
+// memory) as (layer, expert, slot, spec) for the uploader.
 __global__ void __launch_bounds__(256) k_step(SlotState st, int32_t *host_jobs,
                                               int32_t *host_njobs) {
     __shared__ int s_dirty;
-    const int L = st.n_layers, E = st.n_expert, MI = st.max_inserts > 0 ? st.max_inserts : 1;
+    const int L = st.n_layers, E = st.n_expert, MI = st.job_cap;
     if (threadIdx.x == 0) {
         s_dirty = 0;
         uint64_t clock = st.g[G_CLOCK];
@@ -500,7 +526,35 @@ __global__ void __launch_bounds__(256) k_step(SlotState st, int32_t *host_jobs,
     }
     __syncthreads();
     const uint64_t n_steps = st.g[G_STEPS];
-    for (int l = threadIdx.x; l < L; l += blockDim.x) {
+    if (st.early_issue) {
+        // top the free pool back up to its target: evict the least recently
+        // used resident, unprotected slots not in flight (patches/0006:843-913)
+        const int pool_target = st.freeze ? 0 : st.max_inserts + (st.have_pred ? st.predict_top : 0);
+        for (int l = threadIdx.x; l < L; l += blockDim.x) {
+            st.n_pending[l] = 0;
+            const int ns = st.ns[l], so = st.slot_off[l];
+            int32_t *tbl = st.table + (size_t)l * E;
+            int nf = st.n_free[l];
+            bool dirty = false;
+            while (nf < pool_target) {
+                int slot = -1;
+                uint64_t best = ~0ull;
+                for (int q = 0; q < ns; ++q) {
+                    if (st.in_flight[so + q] || st.slot_expert[so + q] < 0) continue;
+                    if (st.protect[so + q] >= n_steps) continue;
+                    if (st.last_use[so + q] < best) { best = st.last_use[so + q]; slot = q; }
+                }
+                if (slot < 0) break;
+                tbl[st.slot_expert[so + slot]] = ns;
+                st.slot_expert[so + slot] = -1;
+                st.free_slots[so + nf++] = slot;
+                dirty = true;
+            }
+            st.n_free[l] = nf;
+            if (dirty) s_dirty = 1;
+        }
+    }
+    for (int l = threadIdx.x; l < L && !st.early_issue; l += blockDim.x) {
         const int np = st.n_pending[l];
         if (np == 0) continue;
         const int ns = st.ns[l], so = st.slot_off[l];
@@ -666,6 +720,12 @@ cudaError_t launch_observe(const SlotState &st, int layer, const int32_t *ids, i
 cudaError_t launch_step(const SlotState &st, int32_t *host_jobs, int32_t *host_njobs,
                         cudaStream_t s) {
     k_step<<<1, 256, 0, s>>>(st, host_jobs, host_njobs);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_issue_spec(const SlotState &st, int layer, const int32_t *top, int n_top,
+                              cudaStream_t s) {
+    k_issue_spec<<<1, 32, 0, s>>>(st, layer, top, n_top);
     return cudaGetLastError();
 }
 

@@ -63,6 +63,9 @@ cudaError_t launch_observe(const SlotState &st, int layer, const int32_t *ids, i
                            cudaStream_t s);
 cudaError_t launch_step(const SlotState &st, int32_t *host_jobs, int32_t *host_njobs,
                         cudaStream_t s);
+// speculative uploads of predicted ids for layer `layer` (early issue with a predictor)
+cudaError_t launch_issue_spec(const SlotState &st, int layer, const int32_t *top, int n_top,
+                              cudaStream_t s);
 
 // ---- batched layer, tokens grouped by expert (moe_batched.cu) -------------
 

@@ -73,7 +73,8 @@ class MoeStack:
                      self.cache.admit_window, self.cache.admit_half, self.cache.admit_floor,
                      int(self.cache.spec_probation), int(self.cache.batch_tables),
                      self.cache.cache_prior, int(self.cache.early_issue),
-                     int(self.cache.freeze), int(bool(self.cache.heat_file)), device, n_shared)
+                     int(self.cache.freeze), int(bool(self.cache.heat_file)), device, n_shared,
+                     self.cache.predict_top)
         torch.cuda.set_device(self.device)
         ctx = C.c_void_p()
         check(self.lib.moe_create(C.byref(cfg), C.byref(ctx)), None, "moe_create")
@@ -364,6 +365,46 @@ class MoeStack:
         ids2 = ids.view(1, -1) if ids.dim() == 1 else ids
         self._ck(self.lib.moe_observe(self.ctx, layer, _ptr(ids2), ids2.shape[0], ids2.shape[1],
                                       _stream(stream)), "moe_observe")
+
+    def set_predictor(self, fn):
+        """The predictor hook (cpp/moe-predictor.h as moe_obs_cb calls it):
+        fn(layer, cur, next_prev, k) -> up to k expert ids for layer + 1,
+        called after each single-token layer of layer_forward / observe.
+        With early issue they become speculative uploads.  None removes it."""
+        if fn is None:
+            self._pred_cb = None
+            self._ck(self.lib.moe_set_predictor(self.ctx, None, None), "moe_set_predictor")
+            return
+
+        def cb(ud, layer, cur, n_cur, nprev, n_nprev, out, k):
+            try:
+                got = list(fn(layer, [cur[i] for i in range(n_cur)], [nprev[i] for i in range(n_nprev)], k))[:k]
+            except Exception as e:   # a raising hook predicts nothing
+                print(f"moe predictor hook raised {e!r}", file=sys.stderr)
+                return 0
+            for i, v in enumerate(got):
+                out[i] = int(v)
+            return len(got)
+        self._pred_cb = _lib.PREDICT_FN(cb)
+        self._ck(self.lib.moe_set_predictor(self.ctx, C.cast(self._pred_cb, C.c_void_p), None),
+                 "moe_set_predictor")
+
+    def set_observe_hook(self, fn):
+        """fn(layer, ids [n_tok, n_ids] numpy) after each observed layer
+        (ggml_set_moe_obs_callback's callback).  None removes it."""
+        if fn is None:
+            self._obs_cb = None
+            self._ck(self.lib.moe_set_observe_hook(self.ctx, None, None), "moe_set_observe_hook")
+            return
+
+        def cb(ud, layer, ids, n_tok, n_ids):
+            try:
+                fn(layer, np.ctypeslib.as_array(ids, shape=(n_tok * n_ids,)).copy().reshape(n_tok, n_ids))
+            except Exception as e:
+                print(f"moe observe hook raised {e!r}", file=sys.stderr)
+        self._obs_cb = _lib.OBSERVE_FN(cb)
+        self._ck(self.lib.moe_set_observe_hook(self.ctx, C.cast(self._obs_cb, C.c_void_p), None),
+                 "moe_set_observe_hook")
 
     def step(self, stream=None):
         """llama_moe_cache_step: publish, schedule, flush (moe_step); then, as

@@ -106,7 +106,7 @@ def test_slot_table_matches_oracle(oracle_lib, admit, max_inserts, batch, profil
     st.close()
 
 
-def _decode_with_cache(oracle_lib, L, n_tok, ns, profile=None, prior=0.01, seed=33):
+def _decode_with_cache(oracle_lib, L, n_tok, ns, profile=None, prior=0.01, seed=33, early=False):
     """Batch-1 decode token by token through a constrained cache: misses
     served zero-copy, second-miss (window) admission, uploads on the copy
     stream, deterministic publication.  After every step the device tables
@@ -126,14 +126,14 @@ def _decode_with_cache(oracle_lib, L, n_tok, ns, profile=None, prior=0.01, seed=
     src.close()
     torch.cuda.synchronize()
     cfg = MoeCacheConfig(n_slots=ns, max_inserts=2, admit="window", batch_tables=True,
-                         cache_prior=prior,
+                         cache_prior=prior, early_issue=early,
                          slot_profile=format_slot_profile(profile) if profile else "")
     st = MoeStack(n_layers=L, cache=cfg)
     for il in range(L):
         st.set_router(il, routers[il])
         st.set_expert_weights(il, *host[il])
     oc = oracle_lib.OracleCache(L, E, ns, slot_profile=st.ns, max_inserts=2, admit_mode=2,
-                                batch_tables=True, cache_prior=prior)
+                                batch_tables=True, cache_prior=prior, early_issue=early)
     h = ar1_states(n_tok, H, seed=2)
     grid = st.decode_info()["grid"]
     for t in range(h.shape[0]):
@@ -289,3 +289,76 @@ def test_heat_file_saved_every_512_steps_and_warm_starts(tmp_path):
         assert list(se[:4]) == hot[il][:4]                    # 512 uses each, in id order
         assert set(se[4:6]) <= set(hot[il][4:]) and (se >= 0).all()
     st.close()
+
+
+@pytest.mark.parametrize("admit,predict,probation", [
+    ("off", False, False),
+    ("window", False, False),
+    ("heat", True, False),
+    ("window", True, True),
+    ("off", True, True),
+])
+def test_early_issue_matches_oracle(oracle_lib, admit, predict, probation):
+    """LLAMA_MOE_EARLY_ISSUE (patches/0006:251-293, :843-913; 0007:230-321):
+    admitted misses take slots of a free pool when the layer is observed,
+    the step publishes them and refills the pool; with a predictor hook its
+    ids for the next layer become speculative uploads (probation with
+    LLAMA_MOE_SPEC_PROBATION).  Tables, recency, flags and counters equal the
+    oracle's after every step; every published slot holds its expert's
+    bytes."""
+    _needs_gpu()
+    from moe_prefetch_b200 import MoeCacheConfig, MoeStack
+    L, E, k, n_ff, ns = 3, 32, 8, 256, 12
+    cfg = MoeCacheConfig(n_slots=ns, max_inserts=2, admit=admit, batch_tables=True, admit_half=16,
+                         early_issue=True, predict_top=3, spec_probation=probation)
+    st = MoeStack(n_layers=L, n_expert=E, n_used=k, n_ff=n_ff, cache=cfg)
+    hw = [_host_weights(E, st.gate_bytes, st.down_bytes, 40 + s) for s in range(L)]
+    for il in range(L):
+        st.set_expert_weights(il, *hw[il])
+    calls = []
+
+    def pred(layer, cur, next_prev, kk):
+        calls.append(layer)
+        return (list(next_prev) + [(v + 1) % E for v in cur])[:kk]
+    if predict:
+        st.set_predictor(pred)
+    oc = oracle_lib.OracleCache(L, E, ns, max_inserts=2, admit_mode=cfg.admit_mode,
+                                admit_window=cfg.admit_window, admit_half=16,
+                                admit_floor=cfg.admit_floor, batch_tables=True, spec_probation=probation,
+                                early_issue=True, predict_top=3, predictor=pred if predict else None)
+    seen = []
+    st.set_observe_hook(lambda layer, ids: seen.append((layer, ids.tolist())))
+    tr = _trace(40, L, E, k, seed=hash((admit, predict, probation)) & 0xFFFF)
+    for t in range(tr.shape[0]):
+        for il in range(L):
+            st.observe(il, torch.from_numpy(tr[t, il]).cuda())
+            oc.observe(il, tr[t, il])
+        st.step()
+        oc.step()
+        _compare(st, oc, L, f"token {t}")
+        assert st.stats()["uploads"] == oc.stats()["uploads"], f"token {t}: uploads"
+    assert st.stats()["uploads"] > 0
+    assert [x[0] for x in seen] == [il for _ in range(tr.shape[0]) for il in range(L)]
+    assert seen[4] == (1, [tr[1, 1].tolist()])
+    if predict:
+        assert len(calls) == 2 * tr.shape[0] * (L - 1)    # device stack and oracle, layers with a next one
+    st.step(); oc.step()
+    torch.cuda.synchronize()
+    for il in range(L):
+        g, u, d = st.slot_views(il)
+        se = st.tables(il)["slot_expert"]
+        hg, hu, hd = (x.numpy() for x in hw[il])
+        for sl, e in enumerate(se):
+            if e >= 0:
+                assert np.array_equal(g[sl].cpu().numpy(), hg[e * st.gate_bytes:(e + 1) * st.gate_bytes])
+                assert np.array_equal(d[sl].cpu().numpy(), hd[e * st.down_bytes:(e + 1) * st.down_bytes])
+    st.close()
+
+
+def test_decode_with_cache_early_issue(oracle_lib):
+    """The persistent decode kernel's own observation with early issue: the
+    admitted misses take pool slots inside the launch, the step publishes
+    them; tables equal the oracle's and outputs are bit-exact every step."""
+    _needs_gpu()
+    s = _decode_with_cache(oracle_lib, L=3, n_tok=24, ns=24, early=True)
+    assert s["uploads"] > 0
