@@ -680,6 +680,97 @@ def run_layer(args):
 
 
 # ---------------------------------------------------------------------------
+# config 0: one layer, 64 single-token forwards, L2 defeated
+# ---------------------------------------------------------------------------
+def run_config0(args):
+    """Config 0: the single Qwen3-30B-A3B-shape layer (all 128 experts
+    resident, delta 0), 64 RMS-normed N(0, 1) inputs, one token per forward.
+    L2 reuse is defeated by rotating 8 device copies of the layer (the same
+    weights and router in 8 places, 8 x 392 MB): forward t runs on copy t mod
+    8, so no forward finds the previous seven's bytes in the 126 MB L2.
+    Two arms, CUDA events around all 64 forwards after --warmup rounds:
+    - operator: moe_layer_forward per token (the per-layer entry point that
+      replaces build_moe_ffn's expert chain: router, gate/up, down launches);
+    - persistent: moe_decode over the 8 copies and 8 tokens, i.e. 64
+      layer-token forwards in one launch (the copies' inputs are then the
+      residual stream instead of fresh rows: the same bytes and arithmetic
+      per forward).
+    The CPU baseline is the oracle's integer-dot CPU path on the same layer
+    (all host threads, a 10 s sample).  One JSON line."""
+    import torch
+    from moe_prefetch_b200 import MoeStack
+    torch.cuda.set_device(0)
+    copies = 8
+    st = MoeStack(n_layers=copies)
+    st.synth_resident(seed=7, keep_router=True)
+    g0, u0, d0 = st.slot_views(0)
+    for il in range(1, copies):
+        g, u, d = st.slot_views(il)
+        g.copy_(g0); u.copy_(u0); d.copy_(d0)
+        st.set_router(il, st.routers[0])
+    torch.cuda.synchronize()
+    rng = np.random.default_rng(12345)
+    h = rng.standard_normal((64, N_EMBD))
+    x = torch.from_numpy((h / np.sqrt((h ** 2).mean(-1, keepdims=True))).astype(np.float32)).cuda()
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+
+    def op_round():
+        for t in range(64):
+            st.layer_forward(t % copies, x[t:t + 1])
+    for _ in range(max(args.warmup, 1)):
+        op_round()
+    torch.cuda.synchronize()
+    e0, e1 = ev(), ev()
+    e0.record()
+    op_round()
+    e1.record()
+    torch.cuda.synchronize()
+    us_op = e0.elapsed_time(e1) * 1000.0 / 64
+    xd = x[:copies].contiguous()          # 8 tokens x 8 copies = 64 forwards
+    out = torch.empty_like(xd)
+    for _ in range(max(args.warmup, 1)):
+        st.decode(xd, out)
+    torch.cuda.synchronize()
+    e0, e1 = ev(), ev()
+    e0.record()
+    st.decode(xd, out)
+    e1.record()
+    torch.cuda.synchronize()
+    st.sync()
+    us_dec = e0.elapsed_time(e1) * 1000.0 / 64
+    peak, peak_kind = measured_peaks()
+    frac = lambda us: LAYER_TOKEN_BYTES / (us * 1e-6) / 1e9 / peak
+    cpu = None
+    if not args.no_cpu_baseline:
+        import oracle
+        gate, up, down = (v[:N_EXPERT].cpu().numpy() for v in (g0, u0, d0))
+        W = st.routers[0].cpu().numpy()
+        xs = x.cpu().numpy()
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 10.0:
+            oracle.moe_layer_cpu_fast(xs[n % 64], W, gate, up, down, 14, N_FF, TOP_K,
+                                      n_threads=os.cpu_count())
+            n += 1
+        cpu = {"value": n / (time.perf_counter() - t0), "unit": "forwards/s", "cores": os.cpu_count(),
+               "kind": "port", "sample": f"{n} single-token forwards of the layer (10 s)"}
+    st.close()
+    print(json.dumps({
+        "metric": "config0 single-layer batch-1 forward", "value": 1e6 / us_dec, "unit": "forwards/s",
+        "n_gpus": 1, "steps": 64, "warmup": max(args.warmup, 1), "higher_is_better": True,
+        "us_per_forward": {"persistent": us_dec, "operator": us_op},
+        "operator_forwards_per_s": 1e6 / us_op,
+        "roofline": {"bound": "hbm", "unit": "GB/s", "peak": peak, "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_forward": LAYER_TOKEN_BYTES,
+                     "frac_persistent": frac(us_dec), "frac_operator": frac(us_op)},
+        "cpu_baseline": cpu,
+        "config": {"workload": "config0: 1 layer x 64 single-token forwards, all 128 experts resident, delta 0",
+                   "l2": "defeated: 8 device copies of the layer in rotation (8 x 392 MB)",
+                   "data": "synthetic (seeded N(0,0.02) weights quantised on device; N(0,1) RMS-normed inputs)"}}),
+        flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
 # the host link: the denominators of config 2's upload and zero-copy rates
 # ---------------------------------------------------------------------------
 def run_hostlink(args):
@@ -846,7 +937,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--workload", default="config1",
-                    choices=["config1", "config2", "config3", "config4", "layer", "phases",
+                    choices=["config0", "config1", "config2", "config3", "config4", "layer", "phases",
                              "hostlink"])
     ap.add_argument("--c4", action="store_true", help="phases: config-4 shapes")
     ap.add_argument("--path", default="gemv", choices=["auto", "gemv", "gemm"])
@@ -875,6 +966,8 @@ def main():
         return run_phases(args)
     if args.workload == "hostlink":
         return run_hostlink(args)
+    if args.workload == "config0":
+        return run_config0(args)
 
     import torch
     import torch.distributed as dist

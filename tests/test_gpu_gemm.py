@@ -49,8 +49,10 @@ def _check(oracle_lib, layer, X, path="gemm"):
     return y, ry
 
 
-@pytest.mark.parametrize("n_tok", [2, 16, 64, 200])
+@pytest.mark.parametrize("n_tok", [2, 16, 64, 200, 512])
 def test_gemm_matches_f32_reference(oracle_lib, layer, n_tok):
+    """Up to the 512-token prefill chunk of the benchmarks (4096 pairs, about
+    32 per expert: tiles of every size)."""
     X = rms_norm(np.random.default_rng(900 + n_tok).standard_normal((n_tok, H)))
     _check(oracle_lib, layer, X)
 
