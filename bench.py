@@ -690,7 +690,9 @@ def run_config0(args):
     8, so no forward finds the previous seven's bytes in the 126 MB L2.
     Two arms, CUDA events around all 64 forwards after --warmup rounds:
     - operator: moe_layer_forward per token (the per-layer entry point that
-      replaces build_moe_ffn's expert chain: router, gate/up, down launches);
+      replaces build_moe_ffn's expert chain: the router on an 8-CTA cluster,
+      then the grouped expert kernels), and beside it the allocation-free
+      entry point (the same router, the per-pair kernels);
     - persistent: moe_decode over the 8 copies and 8 tokens, i.e. 64
       layer-token forwards in one launch (the copies' inputs are then the
       residual stream instead of fresh rows: the same bytes and arithmetic
@@ -726,6 +728,20 @@ def run_config0(args):
     e1.record()
     torch.cuda.synchronize()
     us_op = e0.elapsed_time(e1) * 1000.0 / 64
+    # the allocation-free entry point: the per-pair kernels
+    y1 = torch.empty_like(x[:1])
+
+    def na_round():
+        for t in range(64):
+            st.layer_forward_noalloc(t % copies, x[t:t + 1], y1)
+    na_round()
+    torch.cuda.synchronize()
+    e0, e1 = ev(), ev()
+    e0.record()
+    na_round()
+    e1.record()
+    torch.cuda.synchronize()
+    us_na = e0.elapsed_time(e1) * 1000.0 / 64
     xd = x[:copies].contiguous()          # 8 tokens x 8 copies = 64 forwards
     out = torch.empty_like(xd)
     for _ in range(max(args.warmup, 1)):
@@ -757,7 +773,7 @@ def run_config0(args):
     print(json.dumps({
         "metric": "config0 single-layer batch-1 forward", "value": 1e6 / us_dec, "unit": "forwards/s",
         "n_gpus": 1, "steps": 64, "warmup": max(args.warmup, 1), "higher_is_better": True,
-        "us_per_forward": {"persistent": us_dec, "operator": us_op},
+        "us_per_forward": {"persistent": us_dec, "operator": us_op, "operator_noalloc_per_pair": us_na},
         "operator_forwards_per_s": 1e6 / us_op,
         "roofline": {"bound": "hbm", "unit": "GB/s", "peak": peak, "peak_kind": peak_kind,
                      "algorithmic_bytes_per_forward": LAYER_TOKEN_BYTES,

@@ -695,18 +695,14 @@ extern "C" int moe_layer_forward(moe_ctx *c, int layer, const float *x, float *y
     const float *w_e;
     int kx;
     if ((r = expert_pairs(c, ids_d, w_d, n_tok, s, &ids_e, &w_e, &kx)) != MOE_OK) return r;
-    if (n_tok == 1) {
-        CK(launch_experts(make_src(c, layer), x, ids_e, w_e, n_tok, kx, g.n_embd, g.n_ff,
-                          g.down_type, c->s_act, nullptr, y, c->err, s));
-        return after_observe(c, layer, ids_d, g.n_used, s);
-    } else {
-        // a batch: group the pairs by expert so that each expert's rows are
-        // read once per tile of its tokens (bit-identical results)
-        CK(launch_group(ids_e, n_tok * kx, g.n_expert + g.n_shared, GROUP_TILE, c->grp, c->err, s));
-        CK(launch_experts_grouped(make_src(c, layer), x, c->grp, n_tok, kx, g.n_embd, g.n_ff,
-                                  g.down_type, w_e, c->s_act, c->s_ypair, nullptr, y, c->err, s));
-    }
-    return MOE_OK;
+    // group the pairs by expert so that each expert's rows are read once per
+    // tile of its tokens (bit-identical to the per-pair kernels); one token
+    // takes the same path: its activations are quantised once per tile
+    // instead of once per CTA of the per-pair down kernel
+    CK(launch_group(ids_e, n_tok * kx, g.n_expert + g.n_shared, GROUP_TILE, c->grp, c->err, s));
+    CK(launch_experts_grouped(make_src(c, layer), x, c->grp, n_tok, kx, g.n_embd, g.n_ff,
+                              g.down_type, w_e, c->s_act, c->s_ypair, nullptr, y, c->err, s));
+    return n_tok == 1 ? after_observe(c, layer, ids_d, g.n_used, s) : MOE_OK;
 }
 
 static int ensure_gemm_scratch(moe_ctx *c, int n_tok) {

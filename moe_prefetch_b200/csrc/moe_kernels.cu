@@ -197,8 +197,9 @@ __global__ void __launch_bounds__(512) k_router(const float *__restrict__ W,
     }
 }
 
-// Router for a batch (no prior, no observation: both apply to single tokens
-// only), one cluster of RB_CL CTAs per RB_TOK tokens.  CTA r of a cluster
+// Router for any number of tokens, one cluster of RB_CL CTAs per RB_TOK
+// tokens (the cache prior and the observation apply to single tokens only,
+// and the caller passes them only then).  CTA r of a cluster
 // computes the logits of experts [r E / RB_CL, (r + 1) E / RB_CL) for the
 // cluster's tokens: warp w takes two of them at a time, holds its lanes'
 // slice of both router rows in registers (n_embd == 2048: 16 float4 per lane
@@ -230,7 +231,9 @@ __device__ __forceinline__ float router_chain_dot(const float4 (&wv)[16], const 
 // dynamic shared memory: the cluster's token rows [RB_TOK][2048].
 __global__ void __cluster_dims__(RB_CL, 1, 1) __launch_bounds__(256)
     k_router_batch(const float *__restrict__ W, const float *__restrict__ x, int n_tok,
-                   int n_expert, int k, int32_t *__restrict__ ids, float *__restrict__ w) {
+                   int n_expert, int k, int32_t *__restrict__ ids, float *__restrict__ w,
+                   const int32_t *__restrict__ table, int ns, float delta, int use_prior,
+                   SlotState st, int observe_layer_idx) {
     namespace cg = cooperative_groups;
     extern __shared__ __align__(16) float xs[];          // [RB_TOK][2048]
     __shared__ float lg[RB_TOK][256 / RB_CL];            // this CTA's experts' logits
@@ -279,20 +282,23 @@ __global__ void __cluster_dims__(RB_CL, 1, 1) __launch_bounds__(256)
             lgf[e] = src[e % epc];
         }
         __syncwarp();
-        // select_warp with inv = 1 and no prior: router_select_warp's result,
-        // in registers (no indexed local arrays)
+        // select_warp with inv = 1: router_select_warp's result (prior
+        // included), in registers (no indexed local arrays)
         int id_r = -1;
         float w_r = 0.0f;
+        const bool pri = use_prior != 0;
         switch (n_expert) {
-            case 32: select_warp<1>(lgf, 1.0f, nullptr, 0, 0.0f, false, k, lane, id_r, w_r, sids, sw); break;
-            case 64: select_warp<2>(lgf, 1.0f, nullptr, 0, 0.0f, false, k, lane, id_r, w_r, sids, sw); break;
-            case 128: select_warp<4>(lgf, 1.0f, nullptr, 0, 0.0f, false, k, lane, id_r, w_r, sids, sw); break;
-            default: select_warp<8>(lgf, 1.0f, nullptr, 0, 0.0f, false, k, lane, id_r, w_r, sids, sw); break;
+            case 32: select_warp<1>(lgf, 1.0f, table, ns, delta, pri, k, lane, id_r, w_r, sids, sw); break;
+            case 64: select_warp<2>(lgf, 1.0f, table, ns, delta, pri, k, lane, id_r, w_r, sids, sw); break;
+            case 128: select_warp<4>(lgf, 1.0f, table, ns, delta, pri, k, lane, id_r, w_r, sids, sw); break;
+            default: select_warp<8>(lgf, 1.0f, table, ns, delta, pri, k, lane, id_r, w_r, sids, sw); break;
         }
         if (lane < k) {
             ids[(size_t)(t0 + r) * k + lane] = id_r;
             w[(size_t)(t0 + r) * k + lane] = w_r;
         }
+        // a single token's layer is observed by one thread (moe_obs_cb)
+        if (observe_layer_idx >= 0 && lane == 0) observe_layer(st, observe_layer_idx, sids, k);
     }
     cl.sync();   // no CTA leaves while another still reads its logits
 }
@@ -663,14 +669,17 @@ cudaError_t launch_router(const float *W, const float *x, int n_tok, int n_exper
                           const int32_t *table, int ns, float delta, int use_prior, int k,
                           int32_t *ids, float *w, float *logits, const SlotState *st,
                           int observe_layer_idx, cudaStream_t s) {
-    if (n_tok > 1 && n_embd == 2048 && !use_prior && observe_layer_idx < 0 && !logits) {
+    if (n_embd == 2048 && !logits && (n_tok == 1 || (!use_prior && observe_layer_idx < 0))) {
         // one cluster of RB_CL CTAs per RB_TOK tokens
         const size_t sm = sizeof(float) * (size_t)RB_TOK * 2048;
         cudaError_t e = cudaFuncSetAttribute(k_router_batch, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)sm);
         if (e != cudaSuccess) return e;
         const int groups = (n_tok + RB_TOK - 1) / RB_TOK;
-        k_router_batch<<<groups * RB_CL, 256, sm, s>>>(W, x, n_tok, n_expert, k, ids, w);
+        SlotState dummy_st{};
+        k_router_batch<<<groups * RB_CL, 256, sm, s>>>(W, x, n_tok, n_expert, k, ids, w, table, ns, delta,
+                                                        use_prior, st ? *st : dummy_st,
+                                                        st ? observe_layer_idx : -1);
         return cudaGetLastError();
     }
     const size_t smem = sizeof(float) * ((size_t)n_embd + n_expert);
