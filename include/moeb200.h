@@ -76,6 +76,22 @@ typedef struct moe_cfg {
                                   observed or routed (moe_set_shared_expert)      */
     int32_t predict_top;       /* LLAMA_MOE_PREDICT_TOP (0 -> 3): speculative
                                   uploads per observed layer with a predictor     */
+    int32_t stream;            /* LLAMA_MOE_STREAM: just-in-time streaming (needs
+                                  early_issue): after each single-token layer,
+                                  the lookahead of the next two layers' routers
+                                  claims slots for their best non-resident
+                                  experts, copied earliest deadline first in
+                                  chunks, each made visible by its table word
+                                  as soon as its last byte lands               */
+    int32_t stream_per_layer;  /* LLAMA_MOE_STREAM_PER_LAYER: streamed experts per
+                                  target layer and token (0 -> 4)                */
+    int32_t stream_reserve;    /* LLAMA_MOE_STREAM_RESERVE: extra free slots kept
+                                  per layer at the token boundary (the
+                                  reference's default is 2; 0 keeps none)      */
+    float   stream_gbps;       /* LLAMA_MOE_STREAM_GBPS: the copy engine's rate
+                                  the deadlines assume (0 -> 45.7)               */
+    int32_t stream_topk;       /* LLAMA_MOE_STREAM_TOPK: lookahead candidates per
+                                  target layer, best scores first (0 -> 8, <= 16) */
 } moe_cfg;
 
 /* What llama_moe_cache_lookup(up_exps) returns for one layer
@@ -434,6 +450,17 @@ int moe_get_stats(moe_ctx *ctx, uint64_t *out, int n);
  * hottest experts before the first token (0007:567-618).  Returns the number
  * placed (>= 0) or an error. */
 int moe_warm_start(moe_ctx *ctx, const uint32_t *use_count);
+
+/* Just-in-time streaming counters (patches/0010's moe_stream counters and
+ * its in-time / late split), cumulative, in this order: lookahead records,
+ * jobs the planner accepted, chunks sent, bytes sent, table words written
+ * (experts made visible within the token), jobs dropped late, jobs dropped
+ * because their layer read its table first, claimed slots given back,
+ * streamed experts routed and found resident by their layer (in time),
+ * streamed experts routed before their table word landed (late).  Copies
+ * n <= MOE_STREAM_STAT_COUNT of them to out. */
+#define MOE_STREAM_STAT_COUNT 10
+int moe_stream_stats(moe_ctx *ctx, uint64_t *out, int n);
 
 /* ---- stateless kernels (device pointers) ------------------------------------------ */
 

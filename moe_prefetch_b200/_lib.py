@@ -18,6 +18,9 @@ QTYPE_Q4_K = 12
 QTYPE_Q6_K = 14
 STAT_NAMES = ["steps", "clock", "hits", "misses", "uploads", "scheduled", "copied",
               "published", "admit_ok", "admit_denied", "table_flushes", "upload_bytes", "upload_ns"]
+# moe_stream_stats, in the C ABI's order
+STREAM_STAT_NAMES = ["lookaheads", "offered", "chunks", "bytes", "words", "dropped_late",
+                     "dropped_posted", "given_back", "in_time", "late"]
 
 
 class MoeError(RuntimeError):
@@ -37,6 +40,8 @@ class MoeCfg(C.Structure):
         ("batch_tables", C.c_int32), ("cache_prior", C.c_float), ("early_issue", C.c_int32),
         ("freeze", C.c_int32), ("use_heat_counts", C.c_int32), ("device", C.c_int32),
         ("n_shared", C.c_int32), ("predict_top", C.c_int32),
+        ("stream", C.c_int32), ("stream_per_layer", C.c_int32), ("stream_reserve", C.c_int32),
+        ("stream_gbps", C.c_float), ("stream_topk", C.c_int32),
     ]
 
 
@@ -96,6 +101,7 @@ SIGNATURES = {
     "moe_get_tables": (I, [P, I, P, P, P, P, P]),
     "moe_get_gate_state": (I, [P, I, P, P, P, P]),
     "moe_get_stats": (I, [P, P, I]),
+    "moe_stream_stats": (I, [P, P, I]),
     "moe_warm_start": (I, [P, P]),
     "moe_router_run": (I, [P, P, I, I, I, P, I, F, I, P, P, P, P]),
     "moe_quantize": (I, [P, P, I64, I, P]),

@@ -28,6 +28,11 @@ class MoeCacheConfig:
     heat_file: str = ""            # LLAMA_MOE_HEAT_FILE
     early_issue: bool = False      # LLAMA_MOE_EARLY_ISSUE
     predict_top: int = 3           # LLAMA_MOE_PREDICT_TOP
+    stream: bool = False           # LLAMA_MOE_STREAM (just-in-time streaming; needs early_issue)
+    stream_per_layer: int = 4      # LLAMA_MOE_STREAM_PER_LAYER
+    stream_reserve: int = 2        # LLAMA_MOE_STREAM_RESERVE
+    stream_gbps: float = 45.7      # LLAMA_MOE_STREAM_GBPS
+    stream_topk: int = 8           # LLAMA_MOE_STREAM_TOPK
     freeze: bool = False           # LLAMA_MOE_CACHE_FREEZE
     deterministic: bool = True     # LLAMA_MOE_DETERMINISTIC (always on here)
     map_record: str = ""           # LLAMA_MOE_MAP_RECORD
@@ -85,6 +90,18 @@ class MoeCacheConfig:
             c.cache_prior = max(0.0, _atof(get("LLAMA_MOE_CACHE_PRIOR")))
         if get("LLAMA_MOE_PREDICT_TOP") is not None:
             c.predict_top = _atoi(get("LLAMA_MOE_PREDICT_TOP"))
+        # streaming switches (patches/0010:1828-1832, 1963): per_layer >= 1,
+        # reserve >= 0, GB/s >= 1, topk in [1, 8]
+        if get("LLAMA_MOE_STREAM") is not None:
+            c.stream = _atoi(get("LLAMA_MOE_STREAM")) != 0
+        if get("LLAMA_MOE_STREAM_PER_LAYER") is not None:
+            c.stream_per_layer = max(1, _atoi(get("LLAMA_MOE_STREAM_PER_LAYER")))
+        if get("LLAMA_MOE_STREAM_RESERVE") is not None:
+            c.stream_reserve = max(0, _atoi(get("LLAMA_MOE_STREAM_RESERVE")))
+        if get("LLAMA_MOE_STREAM_GBPS") is not None:
+            c.stream_gbps = max(1.0, _atof(get("LLAMA_MOE_STREAM_GBPS")))
+        if get("LLAMA_MOE_STREAM_TOPK") is not None:
+            c.stream_topk = min(8, max(1, _atoi(get("LLAMA_MOE_STREAM_TOPK"))))
         for name, attr in (("LLAMA_MOE_HEAT_FILE", "heat_file"),
                            ("LLAMA_MOE_MAP_RECORD", "map_record"),
                            ("LLAMA_MOE_MAP_REPLAY", "map_replay"),

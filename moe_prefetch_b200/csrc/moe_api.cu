@@ -3,6 +3,10 @@
 // step with its copy-stream uploader, and the ExpertCache prototype API.
 #include "moeb200.h"
 #include "moe_kernels.h"
+#include "moe_planner.h"
+
+#include <chrono>
+#include <memory>
 
 #include <algorithm>
 #include <cstdarg>
@@ -83,7 +87,7 @@ struct moe_ctx {
     cudaStream_t copy_stream = nullptr;
     cudaEvent_t ev_step = nullptr, ev_copy = nullptr;
     bool copies_pending = false;
-    int32_t *h_jobs = nullptr;         // mapped pinned [L * job_cap * 4 + 4]
+    int32_t *h_jobs = nullptr;         // mapped pinned [(host_cap + 1) * 4]
     int jobs_issued = 0;               // early issue: jobs of this step already copying
     // host callbacks (moe_set_predictor / moe_set_observe_hook)
     moe_predict_fn predict = nullptr;
@@ -91,6 +95,23 @@ struct moe_ctx {
     moe_observe_fn obs_hook = nullptr;
     void *obs_ud = nullptr;
     int32_t *d_pred = nullptr;         // device [64]: the predictor's ids
+    // just-in-time streaming (moe_cfg.stream): the planner and its jobs
+    struct StreamJob {
+        int layer, expert, slot, plan, word;   // word: index of its pinned table word
+        bool cancelled;
+    };
+    std::unique_ptr<moe_planner> planner;
+    std::vector<StreamJob> sjobs;
+    int stream_seen = 0;               // entries of the mapped job list examined
+    int32_t *h_words = nullptr;        // pinned: the slot value of each streamed job's table word
+    int32_t *d_cancel = nullptr;       // device scratch: (layer, expert, slot) to cancel
+    float *d_scores = nullptr;         // device [2][E] lookahead scores
+    int32_t *d_ahead = nullptr;        // device [2][16] + [2]: the lookahead's picks
+    double tau_ns = 103000.0;          // time per layer, running estimate
+    uint64_t last_call_ns = 0;
+    int last_layer = -1;
+    uint64_t free_at_ns = 0;           // when the copy engine runs out of queued bytes
+    uint64_t sst[MOE_STREAM_STAT_COUNT] = {};
     int32_t *d_jobs_alias = nullptr;
     uint64_t upload_bytes = 0;
     uint64_t upload_ns = 0;          // time the copy stream spent on step uploads
@@ -154,6 +175,13 @@ extern "C" int moe_create(const moe_cfg *cfg, moe_ctx **out) {
     if (g.down_type != MOE_QTYPE_Q6_K && g.down_type != MOE_QTYPE_Q4_K)
         return bad(MOE_ERR_UNSUPPORTED, "down_type must be Q6_K or Q4_K");
     if (g.predict_top <= 0) g.predict_top = 3;
+    if (g.stream && !g.early_issue) return bad(MOE_ERR_ARG, "streaming needs early issue");
+    if (g.stream_per_layer <= 0) g.stream_per_layer = 4;
+    if (g.stream_per_layer > 16) return bad(MOE_ERR_ARG, "stream_per_layer must be <= 16");
+    if (g.stream_reserve < 0) return bad(MOE_ERR_ARG, "stream_reserve must be >= 0");
+    if (g.stream_gbps <= 0.0f) g.stream_gbps = 45.7f;
+    if (g.stream_topk <= 0) g.stream_topk = 8;
+    if (g.stream_topk > 16) return bad(MOE_ERR_ARG, "stream_topk must be <= 16");
     if (g.predict_top > 64) return bad(MOE_ERR_ARG, "predict_top must be <= 64");
     if (g.admit_mode < 0 || g.admit_mode > 2) return bad(MOE_ERR_ARG, "admit_mode");
     if (g.n_shared < 0 || g.n_shared > 1) return bad(MOE_ERR_UNSUPPORTED, "n_shared must be 0 or 1");
@@ -214,7 +242,11 @@ extern "C" int moe_create(const moe_cfg *cfg, moe_ctx **out) {
     // slot state
     {
         const size_t LE = (size_t)L * E, S = (size_t)c->sum_ns;
-        const size_t MI = (size_t)(g.max_inserts > 0 ? g.max_inserts : 1) + (g.early_issue ? g.predict_top : 0);
+        // jobs per layer: with early issue every job holds a slot of the layer's
+        // pool, so at most its slot count
+        size_t max_ns = 0;
+        for (int l = 0; l < L; ++l) max_ns = std::max(max_ns, (size_t)c->ns[l]);
+        const size_t MI = g.early_issue ? max_ns : (size_t)(g.max_inserts > 0 ? g.max_inserts : 1);
         std::vector<size_t> sz = {
             LE * 4,            // table
             S * 4,             // slot_expert
@@ -271,6 +303,11 @@ extern "C" int moe_create(const moe_cfg *cfg, moe_ctx **out) {
         st.early_issue = g.early_issue;
         st.predict_top = g.predict_top;
         st.have_pred = 0;
+        st.stream = g.stream;
+        st.stream_reserve = g.stream ? g.stream_reserve : 0;
+        // the mapped job list: with streaming, a slot given back and claimed
+        // again takes a second entry before the step clears the list
+        st.host_cap = L * (int)MI * (g.stream ? 4 : 1);
         st.free_slots = (int32_t *)(b + off[18]);
         st.n_free = (int32_t *)(b + off[19]);
         st.admitted = (int32_t *)(b + off[20]);
@@ -352,17 +389,25 @@ extern "C" int moe_create(const moe_cfg *cfg, moe_ctx **out) {
     }
     // uploader
     {
-        const size_t MI = (size_t)c->st.job_cap;
-        const size_t nb = ((size_t)L * MI + 4) * 4 * sizeof(int32_t);
+        const size_t HC = (size_t)c->st.host_cap;
+        const size_t nb = (HC + 1) * 4 * sizeof(int32_t);
         if (cudaHostAlloc((void **)&c->h_jobs, nb, cudaHostAllocMapped) != cudaSuccess) return cleanup_fail(MOE_ERR_OOM);
         memset(c->h_jobs, 0, nb);
         if (cudaHostGetDevicePointer((void **)&c->d_jobs_alias, c->h_jobs, 0) != cudaSuccess) return cleanup_fail(MOE_ERR_CUDA);
         // the device side writes jobs there (at the step, or at observation
-        // with early issue); the count follows the L * job_cap entries
+        // with early issue); the count follows the host_cap entries
         c->st.host_jobs = c->d_jobs_alias;
-        c->st.host_njobs = c->d_jobs_alias + (size_t)L * MI * 4;
+        c->st.host_njobs = c->d_jobs_alias + HC * 4;
         c->dp.st = c->st;
         if (cudaMalloc(&c->d_pred, 64 * sizeof(int32_t)) != cudaSuccess) return cleanup_fail(MOE_ERR_OOM);
+        if (g.stream) {
+            c->planner.reset(new moe_planner(512 * 1024));
+            if (cudaHostAlloc((void **)&c->h_words, sizeof(int32_t) * HC, cudaHostAllocDefault) != cudaSuccess ||
+                cudaMalloc(&c->d_cancel, sizeof(int32_t) * 3 * HC) != cudaSuccess ||
+                cudaMalloc(&c->d_scores, sizeof(float) * 2 * (size_t)E) != cudaSuccess ||
+                cudaMalloc(&c->d_ahead, sizeof(int32_t) * 36) != cudaSuccess)
+                return cleanup_fail(MOE_ERR_OOM);
+        }
         if (cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking) != cudaSuccess ||
             cudaEventCreateWithFlags(&c->ev_step, cudaEventDisableTiming) != cudaSuccess ||
             cudaEventCreateWithFlags(&c->ev_copy, cudaEventDisableTiming) != cudaSuccess ||
@@ -416,6 +461,10 @@ extern "C" void moe_destroy(moe_ctx *c) {
     if (c->ev_copy) cudaEventDestroy(c->ev_copy);
     if (c->ev_up0) cudaEventDestroy(c->ev_up0);
     cudaFree(c->d_pred);
+    if (c->h_words) cudaFreeHost(c->h_words);
+    cudaFree(c->d_cancel);
+    cudaFree(c->d_scores);
+    cudaFree(c->d_ahead);
     if (c->ev_up1) cudaEventDestroy(c->ev_up1);
     if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
     delete c;
@@ -648,9 +697,166 @@ static int check_shared(moe_ctx *c, int layer) {
 // (speculative uploads); with early issue the new jobs' copies start now.
 // Synchronises the stream only when one of these is on.
 static int issue_early_copies(moe_ctx *c, cudaStream_t s);
-static int after_observe(moe_ctx *c, int layer, const int32_t *ids_dev, int n_ids, cudaStream_t s) {
+static volatile int32_t *host_njobs(moe_ctx *c);
+
+// ---- just-in-time streaming (patches/0010:951-1010 and its mover) -----------
+// After each single-token layer L of the per-layer entry points, the
+// lookahead applies the routers of L + 1 and L + 2 to L's input and claims
+// pool slots for their best non-resident experts (k_ahead_claim: jobs of
+// spec 2 in the device job lists and the mapped host list).  The host mover
+// offers them to the planner with deadlines (now + (target - L) * tau -
+// margin, tau the running time per layer) and sends them earliest deadline
+// first in 512 KiB chunks on the copy stream, keeping about one layer's worth
+// of bytes queued so that a more urgent job never waits behind much; after an
+// expert's last chunk the same stream writes its 4-byte table word, so the
+// expert's layer finds it resident if the word landed first.  A routed
+// expert reads the same bytes from its slot or from host memory, so outputs
+// do not depend on when a word lands; the cache prior counts published
+// residency only (prior_resident).  Jobs the planner drops (late, or their
+// layer read its table first) give their slot back (k_stream_cancel); the
+// step publishes the rest with every other job.
+
+static uint64_t now_ns() {
+    return (uint64_t)std::chrono::duration_cast<std::chrono::nanoseconds>(
+               std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+// Gives back the slot of every streamed job the planner dropped or refused
+// (a dropped job's partial copies land in a slot nothing references; later
+// copies into that slot are queued behind them on the same stream).
+static int stream_cancel_dropped(moe_ctx *c, cudaStream_t s) {
+    std::vector<int32_t> q;
+    for (auto &j : c->sjobs) {
+        if (j.cancelled || (j.plan >= 0 && !c->planner->get(j.plan).dropped)) continue;
+        j.cancelled = true;
+        q.push_back(j.layer); q.push_back(j.expert); q.push_back(j.slot);
+        c->sst[7]++;
+    }
+    if (q.empty()) return MOE_OK;
+    CK(cudaMemcpyAsync(c->d_cancel, q.data(), sizeof(int32_t) * q.size(), cudaMemcpyHostToDevice, s));
+    CK(launch_stream_cancel(c->st, c->d_cancel, (int)q.size() / 3, s));
+    CK(cudaStreamSynchronize(s));   // q is a host temporary
+    return MOE_OK;
+}
+
+// Copies bytes [off, off + len) of expert e's (gate | up | down) into slot
+// `slot` of layer l, on the copy stream.
+static int stream_copy_range(moe_ctx *c, int l, int e, int slot, size_t off, size_t len) {
+    LayerMem &m = c->L[l];
+    const size_t gb = (size_t)c->gate_bytes, db = (size_t)c->down_bytes;
+    const struct { uint8_t *dst; const uint8_t *src; size_t n; } part[3] = {
+        {m.gate + (size_t)slot * gb, (const uint8_t *)m.hgate_user + (size_t)e * gb, gb},
+        {m.up + (size_t)slot * gb, (const uint8_t *)m.hup_user + (size_t)e * gb, gb},
+        {m.down + (size_t)slot * db, (const uint8_t *)m.hdown_user + (size_t)e * db, db}};
+    size_t base = 0;
+    for (const auto &p : part) {
+        const size_t a = std::max(off, base), b = std::min(off + len, base + p.n);
+        if (a < b)
+            CK(cudaMemcpyAsync(p.dst + (a - base), p.src + (a - base), b - a, cudaMemcpyHostToDevice,
+                               c->copy_stream));
+        base += p.n;
+    }
+    return MOE_OK;
+}
+
+// Sends chunks while the copy engine holds less than about one layer's
+// worth of bytes (tau at the configured rate, at least 1 MiB).
+static int stream_drain(moe_ctx *c, cudaStream_t s) {
+    const uint64_t t = now_ns();
+    const double rate = (double)c->cfg.stream_gbps;   // GB/s = bytes per ns
+    uint64_t fa = std::max(t, c->free_at_ns);
+    const uint64_t horizon = t + (uint64_t)std::max(c->tau_ns, (double)(1u << 20) / rate);
+    std::vector<int> of_plan(c->planner->size(), -1);
+    for (int q = 0; q < (int)c->sjobs.size(); ++q)
+        if (c->sjobs[q].plan >= 0) of_plan[c->sjobs[q].plan] = q;
+    moe_planner::chunk ch;
+    bool sent = false;
+    while (fa < horizon && c->planner->next(fa, rate, -1, ch)) {
+        const moe_ctx::StreamJob sj = c->sjobs[of_plan[ch.job]];
+        int r = stream_copy_range(c, sj.layer, sj.expert, sj.slot, ch.offset, ch.len);
+        if (r != MOE_OK) return r;
+        if (ch.last) {
+            CK(cudaMemcpyAsync(c->st.table + (size_t)sj.layer * c->cfg.n_expert + sj.expert,
+                               c->h_words + sj.word, sizeof(int32_t), cudaMemcpyHostToDevice, c->copy_stream));
+            c->sst[4]++;
+        }
+        fa += (uint64_t)((double)ch.len / rate);
+        c->sst[2]++;
+        c->sst[3] += ch.len;
+        sent = true;
+    }
+    c->free_at_ns = fa;
+    c->sst[5] = c->planner->n_drop_late;
+    if (sent) {
+        CK(cudaEventRecord(c->ev_copy, c->copy_stream));
+        c->copies_pending = true;
+    }
+    return stream_cancel_dropped(c, s);
+}
+
+// Layer `layer` is about to read its table: its unsent jobs are of no use;
+// the others may go on.
+static int stream_enter(moe_ctx *c, int layer, cudaStream_t s) {
+    const uint64_t t = now_ns();
+    // time per layer from consecutive layers of one token (stream_take,
+    // patches/0010:1466-1472: a 0.9 / 0.1 average of gaps in (10 us, 1 ms))
+    if (c->last_layer >= 0 && layer == c->last_layer + 1 && t > c->last_call_ns) {
+        const double dt = (double)(t - c->last_call_ns);
+        if (dt > 10000.0 && dt < 1000000.0) c->tau_ns = 0.9 * c->tau_ns + 0.1 * dt;
+    }
+    c->last_layer = layer;
+    c->last_call_ns = t;
+    const uint64_t before = c->planner->n_drop_posted;
+    c->planner->posted(layer);
+    c->sst[6] += c->planner->n_drop_posted - before;
+    return stream_drain(c, s);
+}
+
+// The lookahead after layer `layer` (x: its input), then the mover's work.
+static int stream_after(moe_ctx *c, int layer, const float *x, cudaStream_t s) {
+    const moe_cfg &g = c->cfg;
+    const int n_targets = std::min(2, g.n_layers - 1 - layer);
+    if (n_targets <= 0) return stream_drain(c, s);
+    for (int l = layer + 1; l <= layer + n_targets; ++l)
+        if (!c->L[l].hgate_user) return stream_drain(c, s);   // nothing to stream from
+    CK(launch_ahead(c->st, c->router, x, layer + 1, n_targets, g.n_embd, g.stream_topk, g.stream_per_layer,
+                    c->d_scores, c->d_ahead, c->d_ahead + 32, s));
+    int32_t ahead[34];
+    CK(cudaMemcpyAsync(ahead, c->d_ahead, sizeof(ahead), cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    c->sst[0]++;
+    const uint64_t t = now_ns();
+    const size_t bytes = 2 * (size_t)c->gate_bytes + (size_t)c->down_bytes;
+    auto deadline_of = [&](int tl) {
+        const double lead = (double)(tl - layer) * c->tau_ns;
+        return t + (uint64_t)(lead > 5000.0 ? lead - 5000.0 : 0.0);   // 5 us margin
+    };
+    // candidates that already have a job: a nearer layer may tighten its deadline
+    for (int tt = 0; tt < n_targets; ++tt) {
+        const int nt = std::min(std::max(ahead[32 + tt], 0), 16);
+        for (int i = 0; i < nt; ++i)
+            for (const auto &j : c->sjobs)
+                if (!j.cancelled && j.layer == layer + 1 + tt && j.expert == ahead[16 * tt + i])
+                    c->planner->offer(j.layer, j.expert, bytes, deadline_of(j.layer));
+    }
+    const int nj = *host_njobs(c);
+    for (int j = c->stream_seen; j < nj; ++j) {
+        const int32_t *e = c->h_jobs + 4 * (size_t)j;
+        if (e[3] != 2) continue;
+        const int tl = e[0];
+        const int plan = c->planner->offer(tl, e[1], bytes, deadline_of(tl));
+        c->h_words[j] = e[2];
+        c->sjobs.push_back({tl, e[1], e[2], plan, j, false});
+        if (plan >= 0) c->sst[1]++;
+    }
+    c->stream_seen = nj;
+    return stream_drain(c, s);
+}
+
+static int after_observe(moe_ctx *c, int layer, const int32_t *ids_dev, int n_ids, cudaStream_t s,
+                         const float *x = nullptr) {
     const bool pred = c->cfg.early_issue && c->predict && layer + 1 < c->cfg.n_layers;
-    if (!c->obs_hook && !pred && !c->cfg.early_issue) return MOE_OK;
+    if (!c->obs_hook && !pred && !c->cfg.early_issue) return MOE_OK;   // (streaming needs early issue)
     CK(cudaStreamSynchronize(s));
     int32_t cur[64];
     const int n = n_ids < 64 ? n_ids : 64;
@@ -671,7 +877,11 @@ static int after_observe(moe_ctx *c, int layer, const int32_t *ids_dev, int n_id
         if (nt) CK(cudaMemcpy(c->d_pred, top, 4 * (size_t)nt, cudaMemcpyHostToDevice));
         CK(launch_issue_spec(c->st, layer + 1, c->d_pred, nt, s));
     }
-    if (c->cfg.early_issue) return issue_early_copies(c, s);
+    if (c->cfg.early_issue) {
+        const int r = issue_early_copies(c, s);   // demand first: it is the most urgent
+        if (r != MOE_OK || !c->cfg.stream || !x) return r;
+        return stream_after(c, layer, x, s);
+    }
     return MOE_OK;
 }
 
@@ -685,12 +895,14 @@ extern "C" int moe_layer_forward(moe_ctx *c, int layer, const float *x, float *y
     if ((r = ensure_scratch(c, n_tok)) != MOE_OK) return r;
     cudaStream_t s = (cudaStream_t)stream;
     const moe_cfg &g = c->cfg;
+    if (g.stream && n_tok == 1 && (r = stream_enter(c, layer, s)) != MOE_OK) return r;
     int32_t *ids_d = ids ? ids : c->s_ids;
     float *w_d = w ? w : c->s_w;
     const int32_t *table = c->st.table + (size_t)layer * g.n_expert;
     CK(launch_router(c->router + (size_t)layer * g.n_expert * g.n_embd, x, n_tok, g.n_expert, g.n_embd,
                      table, c->L[layer].ns, g.cache_prior, n_tok == 1 && g.cache_prior > 0.0f, g.n_used,
-                     ids_d, w_d, nullptr, &c->st, n_tok == 1 ? layer : -1, s));
+                     ids_d, w_d, nullptr, &c->st, n_tok == 1 ? layer : -1,
+                     c->st.slot_expert + c->slot_off[layer], s));
     const int32_t *ids_e;
     const float *w_e;
     int kx;
@@ -702,7 +914,7 @@ extern "C" int moe_layer_forward(moe_ctx *c, int layer, const float *x, float *y
     CK(launch_group(ids_e, n_tok * kx, g.n_expert + g.n_shared, GROUP_TILE, c->grp, c->err, s));
     CK(launch_experts_grouped(make_src(c, layer), x, c->grp, n_tok, kx, g.n_embd, g.n_ff,
                               g.down_type, w_e, c->s_act, c->s_ypair, nullptr, y, c->err, s));
-    return n_tok == 1 ? after_observe(c, layer, ids_d, g.n_used, s) : MOE_OK;
+    return n_tok == 1 ? after_observe(c, layer, ids_d, g.n_used, s, x) : MOE_OK;
 }
 
 static int ensure_gemm_scratch(moe_ctx *c, int n_tok) {
@@ -738,12 +950,14 @@ extern "C" int moe_layer_forward_path(moe_ctx *c, int layer, const float *x, flo
     if ((r = ensure_scratch(c, n_tok)) != MOE_OK) return r;
     if ((r = ensure_gemm_scratch(c, n_tok)) != MOE_OK) return r;
     cudaStream_t s = (cudaStream_t)stream;
+    if (g.stream && n_tok == 1 && (r = stream_enter(c, layer, s)) != MOE_OK) return r;
     int32_t *ids_d = ids ? ids : c->s_ids;
     float *w_d = w ? w : c->s_w;
     const int32_t *table = c->st.table + (size_t)layer * g.n_expert;
     CK(launch_router(c->router + (size_t)layer * g.n_expert * g.n_embd, x, n_tok, g.n_expert, g.n_embd,
                      table, c->L[layer].ns, g.cache_prior, n_tok == 1 && g.cache_prior > 0.0f, g.n_used,
-                     ids_d, w_d, nullptr, &c->st, n_tok == 1 ? layer : -1, s));
+                     ids_d, w_d, nullptr, &c->st, n_tok == 1 ? layer : -1,
+                     c->st.slot_expert + c->slot_off[layer], s));
     const int32_t *ids_e;
     const float *w_e;
     int kx;
@@ -751,7 +965,7 @@ extern "C" int moe_layer_forward_path(moe_ctx *c, int layer, const float *x, flo
     CK(launch_group(ids_e, n_tok * kx, g.n_expert + g.n_shared, GM_NT, c->grp, c->err, s));
     CK(launch_experts_gemm(make_src(c, layer), x, c->grp, n_tok, kx, g.n_embd, g.n_ff,
                            g.down_type, w_e, c->s_gemm, c->s_ypair, nullptr, y, c->err, s));
-    return n_tok == 1 ? after_observe(c, layer, ids_d, g.n_used, s) : MOE_OK;
+    return n_tok == 1 ? after_observe(c, layer, ids_d, g.n_used, s, x) : MOE_OK;
 }
 
 // ---- expert parallelism -------------------------------------------------------
@@ -775,7 +989,7 @@ extern "C" int moe_ep_route_pack(moe_ctx *c, int layer, const float *x, int n_to
     cudaStream_t s = (cudaStream_t)stream;
     const int32_t *table = c->st.table + (size_t)layer * g.n_expert;
     CK(launch_router(c->router + (size_t)layer * g.n_expert * g.n_embd, x, n_tok, g.n_expert, g.n_embd,
-                     table, c->L[layer].ns, 0.0f, 0, g.n_used, ids, w, nullptr, &c->st, -1, s));
+                     table, c->L[layer].ns, 0.0f, 0, g.n_used, ids, w, nullptr, &c->st, -1, nullptr, s));
     GroupBufs gg = c->grp;
     gg.cnt = send_count;
     gg.pair_pos = pos;
@@ -1033,7 +1247,8 @@ extern "C" int moe_layer_forward_noalloc(moe_ctx *c, int layer, const float *x, 
     const int32_t *table = c->st.table + (size_t)layer * g.n_expert;
     CK(launch_router(c->router + (size_t)layer * g.n_expert * g.n_embd, x, n_tok, g.n_expert, g.n_embd,
                      table, c->L[layer].ns, g.cache_prior, n_tok == 1 && g.cache_prior > 0.0f, g.n_used,
-                     ids_d, w_d, nullptr, &c->st, n_tok == 1 ? layer : -1, s));
+                     ids_d, w_d, nullptr, &c->st, n_tok == 1 ? layer : -1,
+                     c->st.slot_expert + c->slot_off[layer], s));
     CK(launch_experts(make_src(c, layer), x, ids_d, w_d, n_tok, g.n_used, g.n_embd, g.n_ff,
                       g.down_type, act, nullptr, y, c->err, s));
     return MOE_OK;
@@ -1172,6 +1387,7 @@ static int issue_job_copies(moe_ctx *c, int from, int nj) {
         const int l = c->h_jobs[4 * j], e = c->h_jobs[4 * j + 1], slot = c->h_jobs[4 * j + 2];
         if (l < 0 || l >= c->cfg.n_layers || e < 0 || e >= c->cfg.n_expert || slot < 0 || slot >= c->L[l].ns)
             return fail(c, MOE_ERR_DEVICE, "moe_step: bad job (%d, %d, %d)", l, e, slot);
+        if (c->h_jobs[4 * j + 3] == 2) continue;   // streamed: the mover copies it in chunks
         LayerMem &m = c->L[l];
         if (!m.hgate_user) return fail(c, MOE_ERR_STATE, "moe_step: layer %d has no host weights to upload from", l);
         const uint8_t *hg = (const uint8_t *)m.hgate_user, *hu = (const uint8_t *)m.hup_user,
@@ -1194,7 +1410,7 @@ static int issue_job_copies(moe_ctx *c, int from, int nj) {
 }
 
 static volatile int32_t *host_njobs(moe_ctx *c) {
-    return c->h_jobs + (size_t)c->cfg.n_layers * c->st.job_cap * 4;
+    return c->h_jobs + (size_t)c->st.host_cap * 4;
 }
 
 // Early issue: copies for the jobs the device issued since the last call
@@ -1217,12 +1433,24 @@ extern "C" int moe_step(moe_ctx *c, void *stream) {
         // (deterministic publication), then top the free pools up
         int r = issue_early_copies(c, s);
         if (r != MOE_OK) return r;
+        if (c->cfg.stream) {
+            // streamed jobs still unsent (their layers did not run) are
+            // given back rather than published half copied
+            for (int l = 0; l < c->cfg.n_layers; ++l) c->planner->posted(l);
+            if ((r = stream_cancel_dropped(c, s)) != MOE_OK) return r;
+        }
         if (c->copies_pending) CK(cudaStreamWaitEvent(s, c->ev_copy, 0));
         CK(launch_step(c->st, c->st.host_jobs, c->st.host_njobs, s));
         CK(cudaEventRecord(c->ev_step, s));
         CK(cudaEventSynchronize(c->ev_step));
         c->copies_pending = false;
         c->jobs_issued = 0;
+        if (c->cfg.stream) {
+            c->planner->reset();
+            c->sjobs.clear();
+            c->stream_seen = 0;
+            c->last_layer = -1;
+        }
         harvest_upload_time(c);
         return MOE_OK;
     }
@@ -1237,6 +1465,19 @@ extern "C" int moe_step(moe_ctx *c, void *stream) {
 }
 
 extern "C" int moe_requires_sync(const moe_ctx *c) { return c ? 1 : 0; }
+
+extern "C" int moe_stream_stats(moe_ctx *c, uint64_t *out, int n) {
+    if (!c || !out || n < 0) return fail(c, MOE_ERR_ARG, "moe_stream_stats: bad argument");
+    CK(cudaSetDevice(c->cfg.device));
+    uint64_t g[G_COUNT];
+    CK(cudaMemcpy(g, c->st.g, sizeof(g), cudaMemcpyDeviceToHost));
+    uint64_t all[MOE_STREAM_STAT_COUNT];
+    for (int i = 0; i < 8; ++i) all[i] = c->sst[i];
+    all[8] = g[G_STREAM_IN_TIME];
+    all[9] = g[G_STREAM_LATE];
+    for (int i = 0; i < n && i < MOE_STREAM_STAT_COUNT; ++i) out[i] = all[i];
+    return MOE_OK;
+}
 
 extern "C" int moe_get_tables(moe_ctx *c, int layer, int32_t *expert_slot, int32_t *slot_expert,
                               uint64_t *last_use, uint8_t *in_flight, uint64_t *protect) {
@@ -1304,7 +1545,7 @@ extern "C" int moe_warm_start(moe_ctx *c, const uint32_t *use_count) {
         const int ns = c->L[l].ns;
         // with early issue the free pool keeps its target free (0007:577-579)
         const int reserve = c->cfg.early_issue
-            ? c->cfg.max_inserts + (c->st.have_pred ? c->cfg.predict_top : 0) : 0;
+            ? pool_target_of(c->st) : 0;
         const int fill = std::max(0, ns - reserve);
         std::vector<int32_t> se(ns, -1);
         std::vector<uint64_t> lu(ns, 0);
@@ -1345,7 +1586,7 @@ extern "C" int moe_router_run(const float *W, const float *x, int n_tok, int n_e
     moe_ctx *c = nullptr;
     CK(launch_router(W, x, n_tok, n_expert, n_embd, table, n_slots, delta,
                      table != nullptr && delta > 0.0f && n_tok == 1, k, ids, w, logits, nullptr, -1,
-                     (cudaStream_t)stream));
+                     nullptr, (cudaStream_t)stream));
     return MOE_OK;
 }
 

@@ -92,14 +92,26 @@ __device__ __forceinline__ float router_dot_warp(const float *__restrict__ w,
     return v;
 }
 
-// Softmax over n_expert logits, + delta on resident experts (table[e] != ns)
+// The cache prior's residency test: expert e is resident as published at
+// the last token boundary.  With `pub` (the layer's slot -> expert map, set
+// only when a slot is published) a table word that a streamed copy wrote
+// within the token does not count, so routing never depends on when a copy
+// lands (the reference's prior tensor moves only at publication,
+// patches/0007:328-346).  Without it, table[e] != ns.
+__device__ __forceinline__ bool prior_resident(const int32_t *table, int ns, const int32_t *pub, int e) {
+    const int s = table[e];
+    return s != ns && (pub == nullptr || pub[s] == e);
+}
+
+// Softmax over n_expert logits, + delta on resident experts (prior_resident)
 // when use_prior, top-k by selection value (ties to the lower id), weights
 // from the unbiased probabilities renormalised over the k.  One warp; lane l
 // holds experts l, l+32, ...  ids/w written by lane 0 (any memory).
 __device__ __forceinline__ void router_select_warp(const float *logits, int n_expert,
                                                    const int32_t *table, int ns, float delta,
                                                    bool use_prior, int k, int32_t *ids_out,
-                                                   float *w_out, int lane) {
+                                                   float *w_out, int lane,
+                                                   const int32_t *pub = nullptr) {
     const int m = n_expert >> 5;   // <= 8
     float lg[8], ex[8], p[8], sel[8];
     bool taken[8];
@@ -129,7 +141,7 @@ __device__ __forceinline__ void router_select_warp(const float *logits, int n_ex
         if (i < m) {
             p[i] = __fdiv_rn(ex[i], s);
             const int e = lane + 32 * i;
-            const bool res = use_prior && table != nullptr && table[e] != ns;
+            const bool res = use_prior && table != nullptr && prior_resident(table, ns, pub, e);
             sel[i] = res ? __fadd_rn(p[i], delta) : p[i];
         } else {
             p[i] = 0.0f;
@@ -272,7 +284,8 @@ __device__ __forceinline__ void sel_cx(uint32_t &hi_a, uint32_t &lo_a, float &p_
 template <int M>
 __device__ __forceinline__ void select_warp(const float *tot, float inv, const int32_t *table,
                                             int ns, float delta, bool use_prior, int k, int lane,
-                                            int &id_r, float &w_r, int32_t *s_id, float *s_p) {
+                                            int &id_r, float &w_r, int32_t *s_id, float *s_p,
+                                            const int32_t *pub = nullptr) {
     static_assert(M == 1 || M == 2 || M == 4 || M == 8, "select_warp: 32 to 256 experts");
     float lg[M], ex[M], pr[M];
     uint32_t kh[M], kl[M];
@@ -300,7 +313,7 @@ __device__ __forceinline__ void select_warp(const float *tot, float inv, const i
     for (int i = 0; i < M; ++i) {
         const int e = lane + 32 * i;
         pr[i] = __fdiv_rn(ex[i], s);
-        const bool res = use_prior && table != nullptr && table[e] != ns;
+        const bool res = use_prior && table != nullptr && prior_resident(table, ns, pub, e);
         const float sv = res ? __fadd_rn(pr[i], delta) : pr[i];
         kh[i] = __float_as_uint(sv);
         kl[i] = ~(uint32_t)e;
@@ -1187,6 +1200,8 @@ struct SlotState {
     // early issue (patches/0006:251-293, 0007:230-246): uploads start when a
     // layer is observed, into slots from a free pool that the step tops up
     int early_issue, predict_top, have_pred;
+    int stream;                 // just-in-time streaming is on (jobs of spec 2)
+    int stream_reserve;         // its extra free slots kept per layer
     int32_t *free_slots;        // [sum ns] each layer's free pool, a stack (top = last)
     int32_t *n_free;            // [L]
     int32_t *admitted;          // [L][E] scratch: the pending ids that passed admission
@@ -1194,13 +1209,25 @@ struct SlotState {
     int32_t *n_cur;             // [L]
     int32_t *host_jobs;         // mapped host: (layer, expert, slot, spec) since the last step
     int32_t *host_njobs;        // mapped host: their count
+    int host_cap;               // entries host_jobs holds
 };
 
 // ids a layer keeps of its last observation, for the predictor
 #define CUR_IDS 64
 
+// Free slots a layer keeps at the step boundary (patches/0006:843-913,
+// 0010 pool_target_of): the demand path's inserts, the predictor's guesses
+// and the streaming reserve.
+__host__ __device__ __forceinline__ int pool_target_of(const SlotState &st) {
+    return st.freeze ? 0
+                     : st.max_inserts + (st.have_pred ? st.predict_top : 0) + st.stream_reserve;
+}
+
 enum { G_CLOCK = 0, G_STEPS, G_UPLOADS, G_SCHEDULED, G_COPIED, G_PUBLISHED, G_ADMIT_OK,
-       G_ADMIT_DENIED, G_FLUSHES, G_UPLOAD_BYTES, G_COUNT };
+       G_ADMIT_DENIED, G_FLUSHES, G_UPLOAD_BYTES,
+       G_STREAM_IN_TIME,   // a streamed expert was routed and found resident by its layer
+       G_STREAM_LATE,      // a streamed expert was routed before its table word landed
+       G_COUNT };
 
 // lru_resident (patches/0007:398-412): the resident expert of the least
 // recently used slot not in flight, or -1.
@@ -1258,6 +1285,10 @@ __device__ __forceinline__ int issue_uploads_dev(const SlotState &st, int l, con
             if (jb[4 * a] == id) { dup = true; break; }
         if (dup) continue;
         if (nj >= st.job_cap) break;   // not reached: the free pool bounds a layer's jobs
+        volatile int32_t *hn = st.host_njobs;
+        const int h = *hn;
+        if (h >= st.host_cap) break;   // the host list is full until the step (streamed
+                                       // jobs that were given back still hold entries)
         const int nf = st.n_free[l] - 1;
         const int slot = st.free_slots[so + nf];
         st.n_free[l] = nf;
@@ -1266,8 +1297,6 @@ __device__ __forceinline__ int issue_uploads_dev(const SlotState &st, int l, con
         st.n_jobs[l] = nj + 1;
         st.g[G_UPLOADS] += 1;
         st.g[G_SCHEDULED] += 1;
-        volatile int32_t *hn = st.host_njobs;
-        const int h = *hn;
         st.host_jobs[4 * h] = l; st.host_jobs[4 * h + 1] = id;
         st.host_jobs[4 * h + 2] = slot; st.host_jobs[4 * h + 3] = spec;
         __threadfence_system();
@@ -1283,7 +1312,7 @@ __device__ __forceinline__ int issue_uploads_dev(const SlotState &st, int l, con
 // is decided against the slot the next top-up would free.  One thread.
 __device__ __forceinline__ void early_issue_pending(const SlotState &st, int l) {
     const int E = st.n_expert, ns = st.ns[l];
-    const int pool_target = st.freeze ? 0 : st.max_inserts + (st.have_pred ? st.predict_top : 0);
+    const int pool_target = pool_target_of(st);
     const int32_t *pend = st.pending + (size_t)l * E;
     const int np = st.n_pending[l];
     if (st.admit_mode == 0) {
@@ -1319,6 +1348,15 @@ __device__ __forceinline__ void observe_layer(const SlotState &st, int layer,
         if (st.heat) st.heat[(size_t)layer * E + id] += 1.0f;
         if (st.use_count) st.use_count[(size_t)layer * E + id] += 1u;
         const int slot = tbl[id];
+        if (st.stream) {
+            // was it streamed for this token? (a job of spec 2 still listed)
+            const int32_t *jb = st.jobs + (size_t)layer * st.job_cap * 4;
+            for (int a = 0; a < st.n_jobs[layer]; ++a)
+                if (jb[4 * a] == id && jb[4 * a + 2] == 2) {
+                    st.g[slot != ns ? G_STREAM_IN_TIME : G_STREAM_LATE] += 1;
+                    break;
+                }
+        }
         if (slot != ns) {
             st.n_hit[layer] += 1;
             st.last_use[so + slot] = ++clock;

@@ -168,7 +168,8 @@ __global__ void __launch_bounds__(512) k_router(const float *__restrict__ W,
                                                 int ns, float delta, int use_prior, int k,
                                                 int32_t *__restrict__ ids, float *__restrict__ w,
                                                 float *__restrict__ logits_out,
-                                                SlotState st, int observe_layer_idx) {
+                                                SlotState st, int observe_layer_idx,
+                                                const int32_t *__restrict__ pub) {
     extern __shared__ __align__(16) float sm[];
     float *xs = sm;                   // [n_embd]
     float *lg = sm + n_embd;          // [n_expert]
@@ -187,7 +188,7 @@ __global__ void __launch_bounds__(512) k_router(const float *__restrict__ W,
     if (warp == 0) {
         __shared__ int32_t sids[MOE_KMAX];
         __shared__ float sw[MOE_KMAX];
-        router_select_warp(lg, n_expert, table, ns, delta, use_prior != 0, k, sids, sw, lane);
+        router_select_warp(lg, n_expert, table, ns, delta, use_prior != 0, k, sids, sw, lane, pub);
         __syncwarp();
         if (lane < k) {
             ids[(size_t)t * k + lane] = sids[lane];
@@ -233,7 +234,7 @@ __global__ void __cluster_dims__(RB_CL, 1, 1) __launch_bounds__(256)
     k_router_batch(const float *__restrict__ W, const float *__restrict__ x, int n_tok,
                    int n_expert, int k, int32_t *__restrict__ ids, float *__restrict__ w,
                    const int32_t *__restrict__ table, int ns, float delta, int use_prior,
-                   SlotState st, int observe_layer_idx) {
+                   SlotState st, int observe_layer_idx, const int32_t *__restrict__ pub) {
     namespace cg = cooperative_groups;
     extern __shared__ __align__(16) float xs[];          // [RB_TOK][2048]
     __shared__ float lg[RB_TOK][256 / RB_CL];            // this CTA's experts' logits
@@ -288,10 +289,10 @@ __global__ void __cluster_dims__(RB_CL, 1, 1) __launch_bounds__(256)
         float w_r = 0.0f;
         const bool pri = use_prior != 0;
         switch (n_expert) {
-            case 32: select_warp<1>(lgf, 1.0f, table, ns, delta, pri, k, lane, id_r, w_r, sids, sw); break;
-            case 64: select_warp<2>(lgf, 1.0f, table, ns, delta, pri, k, lane, id_r, w_r, sids, sw); break;
-            case 128: select_warp<4>(lgf, 1.0f, table, ns, delta, pri, k, lane, id_r, w_r, sids, sw); break;
-            default: select_warp<8>(lgf, 1.0f, table, ns, delta, pri, k, lane, id_r, w_r, sids, sw); break;
+            case 32: select_warp<1>(lgf, 1.0f, table, ns, delta, pri, k, lane, id_r, w_r, sids, sw, pub); break;
+            case 64: select_warp<2>(lgf, 1.0f, table, ns, delta, pri, k, lane, id_r, w_r, sids, sw, pub); break;
+            case 128: select_warp<4>(lgf, 1.0f, table, ns, delta, pri, k, lane, id_r, w_r, sids, sw, pub); break;
+            default: select_warp<8>(lgf, 1.0f, table, ns, delta, pri, k, lane, id_r, w_r, sids, sw, pub); break;
         }
         if (lane < k) {
             ids[(size_t)(t0 + r) * k + lane] = id_r;
@@ -463,7 +464,7 @@ __global__ void k_issue_spec(SlotState st, int l, const int32_t *__restrict__ to
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
     const int E = st.n_expert, ns = st.ns[l];
     if (st.admit_mode == 1) {
-        const int pool_target = st.freeze ? 0 : st.max_inserts + (st.have_pred ? st.predict_top : 0);
+        const int pool_target = pool_target_of(st);
         const int nv = st.n_free[l] > pool_target ? -1 : lru_resident_dev(st, l);
         const int32_t *tbl = st.table + (size_t)l * E;
         int32_t *adm = st.admitted + (size_t)l * E;
@@ -535,7 +536,7 @@ __global__ void __launch_bounds__(256) k_step(SlotState st, int32_t *host_jobs,
     if (st.early_issue) {
         // top the free pool back up to its target: evict the least recently
         // used resident, unprotected slots not in flight (patches/0006:843-913)
-        const int pool_target = st.freeze ? 0 : st.max_inserts + (st.have_pred ? st.predict_top : 0);
+        const int pool_target = pool_target_of(st);
         for (int l = threadIdx.x; l < L; l += blockDim.x) {
             st.n_pending[l] = 0;
             const int ns = st.ns[l], so = st.slot_off[l];
@@ -668,7 +669,7 @@ cudaError_t launch_synth_f32(float *y, int64_t n, uint64_t seed, float sigma, cu
 cudaError_t launch_router(const float *W, const float *x, int n_tok, int n_expert, int n_embd,
                           const int32_t *table, int ns, float delta, int use_prior, int k,
                           int32_t *ids, float *w, float *logits, const SlotState *st,
-                          int observe_layer_idx, cudaStream_t s) {
+                          int observe_layer_idx, const int32_t *pub, cudaStream_t s) {
     if (n_embd == 2048 && !logits && (n_tok == 1 || (!use_prior && observe_layer_idx < 0))) {
         // one cluster of RB_CL CTAs per RB_TOK tokens
         const size_t sm = sizeof(float) * (size_t)RB_TOK * 2048;
@@ -679,7 +680,7 @@ cudaError_t launch_router(const float *W, const float *x, int n_tok, int n_exper
         SlotState dummy_st{};
         k_router_batch<<<groups * RB_CL, 256, sm, s>>>(W, x, n_tok, n_expert, k, ids, w, table, ns, delta,
                                                         use_prior, st ? *st : dummy_st,
-                                                        st ? observe_layer_idx : -1);
+                                                        st ? observe_layer_idx : -1, pub);
         return cudaGetLastError();
     }
     const size_t smem = sizeof(float) * ((size_t)n_embd + n_expert);
@@ -692,7 +693,7 @@ cudaError_t launch_router(const float *W, const float *x, int n_tok, int n_exper
     }
     k_router<<<n_tok, threads, smem, s>>>(W, x, n_expert, n_embd, table, ns, delta, use_prior, k,
                                           ids, w, logits, st ? *st : dummy,
-                                          st ? observe_layer_idx : -1);
+                                          st ? observe_layer_idx : -1, pub);
     return cudaGetLastError();
 }
 
@@ -735,6 +736,126 @@ cudaError_t launch_step(const SlotState &st, int32_t *host_jobs, int32_t *host_n
 cudaError_t launch_issue_spec(const SlotState &st, int layer, const int32_t *top, int n_top,
                               cudaStream_t s) {
     k_issue_spec<<<1, 32, 0, s>>>(st, layer, top, n_top);
+    return cudaGetLastError();
+}
+
+// ---- just-in-time streaming: the lookahead (patches/0010:383-474) ----------
+
+#define AHEAD_WARPS 8
+
+// scores[t][e] = router row e of layer layer0 + t (t < n_targets) dotted with
+// the observed layer's input x, in router_dot_warp's order (the canonical
+// router arithmetic: a score is the logit that router would give x).
+// grid (n_expert / AHEAD_WARPS, n_targets); block AHEAD_WARPS warps.
+__global__ void __launch_bounds__(AHEAD_WARPS * 32) k_ahead_scores(const float *__restrict__ routers,
+                                                                   const float *__restrict__ x, int layer0,
+                                                                   int n_expert, int n_embd,
+                                                                   float *__restrict__ scores) {
+    const int t = blockIdx.y, lane = threadIdx.x & 31;
+    const int e = blockIdx.x * AHEAD_WARPS + (threadIdx.x >> 5);
+    if (e >= n_expert) return;
+    const float *w = routers + ((size_t)(layer0 + t) * n_expert + e) * n_embd;
+    const float v = router_dot_warp(w, x, n_embd, lane);
+    if (lane == 0) scores[(size_t)t * n_expert + e] = v;
+}
+
+// One CTA of 32 * n_targets threads: warp t takes the topk best scores of
+// target t (score descending, ties to the lower id) and keeps those its
+// layer's table says are not resident, in that order (out[t][...], count
+// n_out[t]: k_moe_ahead_post, patches/0010:407-474).  Then one thread claims
+// slots for them from the free pools (issue_uploads with spec 2 = streamed),
+// at most per_layer streamed jobs per layer and token, keeping max_inserts
+// slots for demand (stream_take, patches/0010:1477-1520); the claims are
+// listed for the host's mover.
+__global__ void k_ahead_claim(SlotState st, const float *__restrict__ scores, int layer0, int n_targets,
+                              int k, int per_layer, int32_t *__restrict__ out, int32_t *__restrict__ n_out) {
+    __shared__ int32_t s_ids[2][16];
+    __shared__ int s_n[2];
+    const int t = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int E = st.n_expert;
+    if (t < n_targets) {
+        const int l = layer0 + t, ns = st.ns[l];
+        const int32_t *tbl = st.table + (size_t)l * E;
+        const float *sc = scores + (size_t)t * E;
+        uint32_t taken = 0;       // bit j: this lane's expert lane + 32 j is picked
+        int n = 0;
+        for (int r = 0; r < k; ++r) {
+            float best = 0.0f;
+            int bi = -1;
+            for (int j = 0, e = lane; e < E; ++j, e += 32)
+                if (!(taken & (1u << j)) && (bi < 0 || sc[e] > best)) { best = sc[e]; bi = e; }
+            for (int off = 16; off >= 1; off >>= 1) {
+                const float ob = __shfl_xor_sync(MOE_FULL, best, off);
+                const int oi = __shfl_xor_sync(MOE_FULL, bi, off);
+                if (oi >= 0 && (bi < 0 || ob > best || (ob == best && oi < bi))) { best = ob; bi = oi; }
+            }
+            if (bi < 0) break;
+            if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+            if (tbl[bi] == ns) {
+                if (lane == 0) s_ids[t][n] = bi;
+                ++n;
+            }
+        }
+        if (lane == 0) {
+            s_n[t] = n;
+            n_out[t] = n;
+            for (int i = 0; i < n; ++i) out[t * 16 + i] = s_ids[t][i];
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0)
+        for (int tt = 0; tt < n_targets; ++tt) {
+            const int l = layer0 + tt;
+            const int32_t *jb = st.jobs + (size_t)l * st.job_cap * 4;
+            int streamed = 0;
+            for (int a = 0; a < st.n_jobs[l]; ++a) streamed += jb[4 * a + 2] == 2;
+            if (streamed < per_layer)
+                issue_uploads_dev(st, l, s_ids[tt], s_n[tt], per_layer - streamed, st.max_inserts, 2);
+        }
+}
+
+// Streamed jobs the mover gave up on (late, or their layer read its table
+// first): each (layer, expert, slot) leaves its layer's job list and the
+// slot goes back to the free pool (its partial copy is never published).
+// One thread.
+__global__ void k_stream_cancel(SlotState st, const int32_t *__restrict__ jobs, int n) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    for (int q = 0; q < n; ++q) {
+        const int l = jobs[3 * q], e = jobs[3 * q + 1], slot = jobs[3 * q + 2];
+        if (l < 0 || l >= st.n_layers) continue;
+        int32_t *jb = st.jobs + (size_t)l * st.job_cap * 4;
+        const int nj = st.n_jobs[l];
+        for (int a = 0; a < nj; ++a) {
+            if (jb[4 * a] != e || jb[4 * a + 1] != slot) continue;
+            for (int c = 0; c < 4; ++c) jb[4 * a + c] = jb[4 * (nj - 1) + c];
+            st.n_jobs[l] = nj - 1;
+            const int so = st.slot_off[l];
+            st.in_flight[so + slot] = 0;
+            st.free_slots[so + st.n_free[l]] = slot;
+            st.n_free[l] += 1;
+            st.g[G_SCHEDULED] -= 1;
+            st.g[G_UPLOADS] -= 1;
+            break;
+        }
+    }
+}
+
+cudaError_t launch_ahead(const SlotState &st, const float *routers, const float *x, int layer0,
+                         int n_targets, int n_embd, int k, int per_layer, float *scores, int32_t *out,
+                         int32_t *n_out, cudaStream_t s) {
+    if (n_targets < 1 || n_targets > 2 || k < 1 || k > 16 || per_layer < 1) return cudaErrorInvalidValue;
+    const int E = st.n_expert;
+    k_ahead_scores<<<dim3((E + AHEAD_WARPS - 1) / AHEAD_WARPS, n_targets), AHEAD_WARPS * 32, 0, s>>>(
+        routers, x, layer0, E, n_embd, scores);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    k_ahead_claim<<<1, 64, 0, s>>>(st, scores, layer0, n_targets, k, per_layer, out, n_out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_stream_cancel(const SlotState &st, const int32_t *jobs, int n, cudaStream_t s) {
+    if (n <= 0) return cudaSuccess;
+    k_stream_cancel<<<1, 32, 0, s>>>(st, jobs, n);
     return cudaGetLastError();
 }
 

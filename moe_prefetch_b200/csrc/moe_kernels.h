@@ -54,7 +54,7 @@ cudaError_t launch_synth_f32(float *y, int64_t n, uint64_t seed, float sigma, cu
 cudaError_t launch_router(const float *W, const float *x, int n_tok, int n_expert, int n_embd,
                           const int32_t *table, int ns, float delta, int use_prior, int k,
                           int32_t *ids, float *w, float *logits, const SlotState *st,
-                          int observe_layer_idx, cudaStream_t s);
+                          int observe_layer_idx, const int32_t *pub, cudaStream_t s);
 cudaError_t launch_experts(const ExpertSrc &src, const float *x, const int32_t *ids,
                            const float *w, int n_tok, int k, int n_embd, int n_ff, int down_type,
                            float *act, const float *resid, float *y, int *err, cudaStream_t s);
@@ -63,6 +63,15 @@ cudaError_t launch_observe(const SlotState &st, int layer, const int32_t *ids, i
                            cudaStream_t s);
 cudaError_t launch_step(const SlotState &st, int32_t *host_jobs, int32_t *host_njobs,
                         cudaStream_t s);
+// just-in-time streaming: the lookahead scores of layers layer0 .. layer0 +
+// n_targets - 1 (<= 2) on one token's x, the non-resident experts among
+// their k best (out [n_targets][16], n_out [n_targets]) and the streamed
+// jobs that claim pool slots for them (at most per_layer per layer and
+// token); and the cancellation of streamed jobs (l, e, slot)
+cudaError_t launch_ahead(const SlotState &st, const float *routers, const float *x, int layer0,
+                         int n_targets, int n_embd, int k, int per_layer, float *scores, int32_t *out,
+                         int32_t *n_out, cudaStream_t s);
+cudaError_t launch_stream_cancel(const SlotState &st, const int32_t *jobs, int n, cudaStream_t s);
 // speculative uploads of predicted ids for layer `layer` (early issue with a predictor)
 cudaError_t launch_issue_spec(const SlotState &st, int layer, const int32_t *top, int n_top,
                               cudaStream_t s);

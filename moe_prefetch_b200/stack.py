@@ -16,7 +16,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._lib import MoeCfg, MoeDecodeDbg, MoeError, MoeLayerInfo, QTYPE_Q4_K, QTYPE_Q6_K, STAT_NAMES, check
+from ._lib import MoeCfg, MoeDecodeDbg, MoeError, MoeLayerInfo, QTYPE_Q4_K, QTYPE_Q6_K, STAT_NAMES, STREAM_STAT_NAMES, check
 from .config import MoeCacheConfig
 
 Q4K_BYTES, Q6K_BYTES, QK_K = 144, 210, 256
@@ -74,7 +74,8 @@ class MoeStack:
                      int(self.cache.spec_probation), int(self.cache.batch_tables),
                      self.cache.cache_prior, int(self.cache.early_issue),
                      int(self.cache.freeze), int(bool(self.cache.heat_file)), device, n_shared,
-                     self.cache.predict_top)
+                     self.cache.predict_top, int(self.cache.stream), self.cache.stream_per_layer,
+                     self.cache.stream_reserve, self.cache.stream_gbps, self.cache.stream_topk)
         torch.cuda.set_device(self.device)
         ctx = C.c_void_p()
         check(self.lib.moe_create(C.byref(cfg), C.byref(ctx)), None, "moe_create")
@@ -449,6 +450,12 @@ class MoeStack:
         out = np.zeros(len(STAT_NAMES), np.uint64)
         self._ck(self.lib.moe_get_stats(self.ctx, _ptr(out), len(STAT_NAMES)), "moe_get_stats")
         return {k: int(v) for k, v in zip(STAT_NAMES, out)}
+
+    def stream_stats(self):
+        """Just-in-time streaming counters (moe_stream_stats), by name."""
+        out = np.zeros(len(STREAM_STAT_NAMES), np.uint64)
+        self._ck(self.lib.moe_stream_stats(self.ctx, _ptr(out), len(STREAM_STAT_NAMES)), "moe_stream_stats")
+        return {k: int(v) for k, v in zip(STREAM_STAT_NAMES, out)}
 
     def warm_start(self, use_count):
         uc = np.ascontiguousarray(use_count, np.uint32)

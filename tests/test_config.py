@@ -43,6 +43,20 @@ def test_env_parsing_rules(capsys):
     assert c.max_inserts == 2          # non-positive keeps the default
 
 
+def test_stream_env_rules():
+    # patches/0010:969-975 defaults; 1828-1832 clamps; 1963 LLAMA_MOE_STREAM
+    c = MoeCacheConfig.from_env({})
+    assert not c.stream and (c.stream_per_layer, c.stream_reserve, c.stream_gbps, c.stream_topk) == \
+        (4, 2, 45.7, 8)
+    c = MoeCacheConfig.from_env({"LLAMA_MOE_STREAM": "1", "LLAMA_MOE_STREAM_TOPK": "12",
+                                 "LLAMA_MOE_STREAM_PER_LAYER": "0", "LLAMA_MOE_STREAM_GBPS": "0.5",
+                                 "LLAMA_MOE_STREAM_RESERVE": "-4"})
+    assert c.stream and c.stream_topk == 8 and c.stream_per_layer == 1 and c.stream_gbps == 1.0
+    assert c.stream_reserve == 0
+    c = MoeCacheConfig.from_env({"LLAMA_MOE_STREAM": "0", "LLAMA_MOE_STREAM_TOPK": "-1"})
+    assert not c.stream and c.stream_topk == 1
+
+
 @pytest.mark.parametrize("spec,expect", [
     ("", {}),
     ("0:16,3:32", {0: 16, 3: 32}),
