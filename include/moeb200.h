@@ -411,6 +411,23 @@ typedef int (*moe_predict_fn)(void *ud, int layer, const int32_t *cur, int n_cur
 int moe_set_observe_hook(moe_ctx *ctx, moe_observe_fn fn, void *ud);
 int moe_set_predictor(moe_ctx *ctx, moe_predict_fn fn, void *ud);
 
+/* LLAMA_MOE_EVICTOR (patches/0006:521-537; evict_scores 0006:402-426; the
+ * victim choice 0006:790-913, 0007:680-727): a MOEP v3 model (the
+ * predictor's format, cpp/moe-predictor.cpp) scores each layer's experts at
+ * moe_step -- inputs: the next layer's previous-token ids, this layer's ids,
+ * the previous layer's ids, this layer's previous-token ids -- and the victim
+ * is the resident slot with the lowest score (recency breaking ties) instead
+ * of the least recently used one, in the scheduling and the early-issue pool
+ * top-up alike.  Empty, in-flight and protected slots are treated as before;
+ * layers without a model keep LRU.  Scores are computed on the device
+ * (moe_predictor::score, fp32, no fused multiply-adds).  n_model model slots,
+ * layer_of[n_model] the stack layer of each; w [n_model][feat_dim][n_expert],
+ * bias [n_model][n_expert], prior [n_model]; off[4] the row offsets of the
+ * prev, cur, below and self_prev blocks in feat_dim (-1: absent).  Host
+ * pointers, copied; n_model 0 removes the model. */
+int moe_set_evictor(moe_ctx *ctx, int n_model, const int32_t *layer_of, int feat_dim,
+                    const int32_t *off, const float *w, const float *bias, const float *prior);
+
 /* Observe one layer's routed ids (device [n_tok][n_ids]) outside
  * moe_layer_forward: hits refresh recency, misses feed the second-miss window
  * and the pending list; with early issue the admitted misses take slots of

@@ -102,6 +102,7 @@ SIGNATURES = {
     "moe_get_gate_state": (I, [P, I, P, P, P, P]),
     "moe_get_stats": (I, [P, P, I]),
     "moe_stream_stats": (I, [P, P, I]),
+    "moe_set_evictor": (I, [P, I, P, I, P, P, P, P]),
     "moe_warm_start": (I, [P, P]),
     "moe_router_run": (I, [P, P, I, I, I, P, I, F, I, P, P, P, P]),
     "moe_quantize": (I, [P, P, I64, I, P]),

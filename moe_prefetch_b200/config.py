@@ -28,6 +28,7 @@ class MoeCacheConfig:
     heat_file: str = ""            # LLAMA_MOE_HEAT_FILE
     early_issue: bool = False      # LLAMA_MOE_EARLY_ISSUE
     predict_top: int = 3           # LLAMA_MOE_PREDICT_TOP
+    evictor: str = ""              # LLAMA_MOE_EVICTOR (MOEP v3 file)
     stream: bool = False           # LLAMA_MOE_STREAM (just-in-time streaming; needs early_issue)
     stream_per_layer: int = 4      # LLAMA_MOE_STREAM_PER_LAYER
     stream_reserve: int = 2        # LLAMA_MOE_STREAM_RESERVE
@@ -103,6 +104,7 @@ class MoeCacheConfig:
         if get("LLAMA_MOE_STREAM_TOPK") is not None:
             c.stream_topk = min(8, max(1, _atoi(get("LLAMA_MOE_STREAM_TOPK"))))
         for name, attr in (("LLAMA_MOE_HEAT_FILE", "heat_file"),
+                           ("LLAMA_MOE_EVICTOR", "evictor"),
                            ("LLAMA_MOE_MAP_RECORD", "map_record"),
                            ("LLAMA_MOE_MAP_REPLAY", "map_replay"),
                            ("LLAMA_MOE_ROUTE_TRACE", "route_trace")):

@@ -95,6 +95,9 @@ struct moe_ctx {
     moe_observe_fn obs_hook = nullptr;
     void *obs_ud = nullptr;
     int32_t *d_pred = nullptr;         // device [64]: the predictor's ids
+    // LLAMA_MOE_EVICTOR: the model on the device (moe_set_evictor)
+    int32_t *d_ev_index = nullptr;     // [L] in the slot-state block
+    float *d_ev_model = nullptr;       // w, bias, prior
     // just-in-time streaming (moe_cfg.stream): the planner and its jobs
     struct StreamJob {
         int layer, expert, slot, plan, word;   // word: index of its pinned table word
@@ -266,7 +269,9 @@ extern "C" int moe_create(const moe_cfg *cfg, moe_ctx **out) {
             (size_t)L * 4, (size_t)L * 4,       // ns, slot_off
             S * 4, (size_t)L * 4,               // free_slots, n_free
             LE * 4,                             // admitted
-            (size_t)L * CUR_IDS * 4, (size_t)L * 4   // cur_ids, n_cur
+            (size_t)L * CUR_IDS * 4, (size_t)L * 4,  // cur_ids, n_cur
+            (size_t)L * CUR_IDS * 4, (size_t)L * 4,  // prev_ids, n_prev (the evictor's)
+            LE * 4, (size_t)L * 4                    // ev_scores, ev_index
         };
         size_t total = 0;
         std::vector<size_t> off;
@@ -313,6 +318,15 @@ extern "C" int moe_create(const moe_cfg *cfg, moe_ctx **out) {
         st.admitted = (int32_t *)(b + off[20]);
         st.cur_ids = (int32_t *)(b + off[21]);
         st.n_cur = (int32_t *)(b + off[22]);
+        st.prev_ids = (int32_t *)(b + off[23]);
+        st.n_prev = (int32_t *)(b + off[24]);
+        st.ev_scores = (float *)(b + off[25]);
+        c->d_ev_index = (int32_t *)(b + off[26]);
+        st.ev_index = c->d_ev_index;
+        st.have_evict = 0;
+        st.ev_feat = 0;
+        for (int q = 0; q < 4; ++q) st.ev_off[q] = -1;
+        st.ev_w = st.ev_bias = st.ev_prior = nullptr;
         {   // every slot free; the lowest on top of each pool
             std::vector<int32_t> fs(S), nf(L);
             for (int l = 0; l < L; ++l) {
@@ -463,6 +477,7 @@ extern "C" void moe_destroy(moe_ctx *c) {
     cudaFree(c->d_pred);
     if (c->h_words) cudaFreeHost(c->h_words);
     cudaFree(c->d_cancel);
+    cudaFree(c->d_ev_model);
     cudaFree(c->d_scores);
     cudaFree(c->d_ahead);
     if (c->ev_up1) cudaEventDestroy(c->ev_up1);
@@ -1356,6 +1371,48 @@ extern "C" int moe_set_predictor(moe_ctx *c, moe_predict_fn fn, void *ud) {
     c->predict_ud = ud;
     c->st.have_pred = fn != nullptr;   // the free pool's target grows by predict_top
     c->dp.st.have_pred = c->st.have_pred;
+    return MOE_OK;
+}
+
+extern "C" int moe_set_evictor(moe_ctx *c, int n_model, const int32_t *layer_of, int feat_dim,
+                               const int32_t *off, const float *w, const float *bias,
+                               const float *prior) {
+    if (!c) return MOE_ERR_ARG;
+    const int E = c->cfg.n_expert, L = c->cfg.n_layers;
+    if (n_model == 0) {   // remove: LRU again
+        CK(cudaSetDevice(c->cfg.device));
+        CK(cudaDeviceSynchronize());
+        c->st.have_evict = 0;
+        c->dp.st.have_evict = 0;
+        return MOE_OK;
+    }
+    if (n_model < 0 || !layer_of || feat_dim <= 0 || !off || !w || !bias || !prior)
+        return fail(c, MOE_ERR_ARG, "moe_set_evictor: bad argument");
+    for (int q = 0; q < 4; ++q)
+        if (off[q] >= 0 && off[q] + E > feat_dim)
+            return fail(c, MOE_ERR_ARG, "moe_set_evictor: block %d at row %d does not fit %d rows", q, off[q], feat_dim);
+    std::vector<int32_t> idx(L, -1);
+    for (int m = 0; m < n_model; ++m)
+        if (layer_of[m] >= 0 && layer_of[m] < L) idx[layer_of[m]] = m;
+    CK(cudaSetDevice(c->cfg.device));
+    CK(cudaDeviceSynchronize());
+    const size_t nw = (size_t)n_model * feat_dim * E, nb = (size_t)n_model * E;
+    cudaFree(c->d_ev_model);
+    c->d_ev_model = nullptr;
+    if (cudaMalloc(&c->d_ev_model, sizeof(float) * (nw + nb + n_model)) != cudaSuccess)
+        return fail(c, MOE_ERR_OOM, "moe_set_evictor: %zu bytes", sizeof(float) * (nw + nb + n_model));
+    CK(cudaMemcpy(c->d_ev_model, w, sizeof(float) * nw, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(c->d_ev_model + nw, bias, sizeof(float) * nb, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(c->d_ev_model + nw + nb, prior, sizeof(float) * n_model, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(c->d_ev_index, idx.data(), sizeof(int32_t) * L, cudaMemcpyHostToDevice));
+    SlotState &st = c->st;
+    st.ev_w = c->d_ev_model;
+    st.ev_bias = c->d_ev_model + nw;
+    st.ev_prior = c->d_ev_model + nw + nb;
+    st.ev_feat = feat_dim;
+    for (int q = 0; q < 4; ++q) st.ev_off[q] = off[q];
+    st.have_evict = 1;
+    c->dp.st = st;
     return MOE_OK;
 }
 

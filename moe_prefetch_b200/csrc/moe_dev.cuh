@@ -1210,6 +1210,17 @@ struct SlotState {
     int32_t *host_jobs;         // mapped host: (layer, expert, slot, spec) since the last step
     int32_t *host_njobs;        // mapped host: their count
     int host_cap;               // entries host_jobs holds
+    // LLAMA_MOE_EVICTOR (patches/0006:402-426, :790-913): an MOEP model whose
+    // per-layer score picks the victim instead of LRU
+    int have_evict, ev_feat;
+    int ev_off[4];              // row offsets of the prev, cur, below, self_prev blocks, -1 absent
+    const int32_t *ev_index;    // [L] model slot or -1
+    const float *ev_w;          // [n_model][ev_feat][E]
+    const float *ev_bias;       // [n_model][E]
+    const float *ev_prior;      // [n_model]
+    float *ev_scores;           // [L][E] this step's scores
+    int32_t *prev_ids;          // [L][CUR_IDS] cur_ids one token earlier
+    int32_t *n_prev;            // [L]
 };
 
 // ids a layer keeps of its last observation, for the predictor

@@ -479,6 +479,72 @@ __global__ void k_issue_spec(SlotState st, int l, const int32_t *__restrict__ to
     }
 }
 
+// evict_scores (patches/0006:402-426) for every layer with a model, one CTA
+// per layer, thread j = expert j: moe_predictor::score
+// (cpp/moe-predictor.cpp:165-223) with its inputs prev = the next layer's
+// previous-token ids, cur = this layer's ids, below = the previous layer's
+// ids, self_prev = this layer's previous-token ids.  Row adds per expert in
+// block and id order; the mean and variance as sequential fp32 sums on one
+// thread; no fused multiply-adds.  blockDim >= n_expert.
+__global__ void __launch_bounds__(256) k_evict_scores(SlotState st) {
+    __shared__ float s_out[256];
+    __shared__ float s_mu, s_sd;
+    const int l = blockIdx.x, j = threadIdx.x, E = st.n_expert, L = st.n_layers;
+    const int m = st.ev_index[l];
+    if (m < 0) return;
+    const float *W = st.ev_w + (size_t)m * st.ev_feat * E;
+    const int32_t *ids[4] = {l + 1 < L ? st.prev_ids + (size_t)(l + 1) * CUR_IDS : nullptr,
+                             st.cur_ids + (size_t)l * CUR_IDS,
+                             l > 0 ? st.cur_ids + (size_t)(l - 1) * CUR_IDS : nullptr,
+                             st.prev_ids + (size_t)l * CUR_IDS};
+    const int n[4] = {l + 1 < L ? st.n_prev[l + 1] : 0, st.n_cur[l], l > 0 ? st.n_cur[l - 1] : 0,
+                      st.n_prev[l]};
+    if (j < E) {
+        float o = st.ev_bias[(size_t)m * E + j];
+        for (int g = 0; g < 4; ++g) {
+            const int off = st.ev_off[g];
+            if (off < 0 || !ids[g]) continue;
+            for (int i = 0; i < n[g]; ++i) {
+                const int e = ids[g][i];
+                if (e >= 0 && e < E) o = __fadd_rn(o, W[(size_t)(off + e) * E + j]);
+            }
+        }
+        s_out[j] = o;
+    }
+    __syncthreads();
+    if (j == 0) {
+        float mu = 0.0f;
+        for (int q = 0; q < E; ++q) mu = __fadd_rn(mu, s_out[q]);
+        mu = __fdiv_rn(mu, (float)E);
+        float var = 0.0f;
+        for (int q = 0; q < E; ++q) {
+            const float d = __fsub_rn(s_out[q], mu);
+            var = __fadd_rn(var, __fmul_rn(d, d));
+        }
+        s_mu = mu;
+        s_sd = __fadd_rn(__fsqrt_rn(__fdiv_rn(var, (float)E)), 1e-9f);
+    }
+    __syncthreads();
+    if (j < E) s_out[j] = __fdiv_rn(__fsub_rn(s_out[j], s_mu), s_sd);
+    __syncthreads();
+    if (j == 0) {
+        const float pw = st.ev_prior[m];
+        if (pw != 0.0f && ids[0])
+            for (int i = 0; i < n[0]; ++i) {
+                const int e = ids[0][i];
+                if (e >= 0 && e < E) s_out[e] = __fadd_rn(s_out[e], pw);
+            }
+    }
+    __syncthreads();
+    if (j < E) st.ev_scores[(size_t)l * E + j] = s_out[j];
+}
+
+// The victim choice of llama_moe_cache_step with a model: the lowest score,
+// recency breaking ties (patches/0006:806-818, :871-889).
+__device__ __forceinline__ bool evict_better(float sc, uint64_t lu, float best_score, uint64_t best) {
+    return sc < best_score || (sc == best_score && lu < best);
+}
+
 // llama_moe_cache_step on the device (patches/0006:765-953, 0007:655-773
 // admission / probation / heat decay, 0008:613-627 deterministic
 // publication).  One CTA: thread 0 publishes (the clock order is global),
@@ -543,13 +609,22 @@ __global__ void __launch_bounds__(256) k_step(SlotState st, int32_t *host_jobs,
             int32_t *tbl = st.table + (size_t)l * E;
             int nf = st.n_free[l];
             bool dirty = false;
+            const float *esc = st.have_evict && st.ev_index[l] >= 0 ? st.ev_scores + (size_t)l * E : nullptr;
             while (nf < pool_target) {
                 int slot = -1;
                 uint64_t best = ~0ull;
+                float best_score = 3.4e38f;
                 for (int q = 0; q < ns; ++q) {
                     if (st.in_flight[so + q] || st.slot_expert[so + q] < 0) continue;
                     if (st.protect[so + q] >= n_steps) continue;
-                    if (st.last_use[so + q] < best) { best = st.last_use[so + q]; slot = q; }
+                    if (esc) {
+                        const float sc = esc[st.slot_expert[so + q]];
+                        if (evict_better(sc, st.last_use[so + q], best_score, best)) {
+                            best_score = sc; best = st.last_use[so + q]; slot = q;
+                        }
+                    } else if (st.last_use[so + q] < best) {
+                        best = st.last_use[so + q]; slot = q;
+                    }
                 }
                 if (slot < 0) break;
                 tbl[st.slot_expert[so + slot]] = ns;
@@ -571,6 +646,7 @@ __global__ void __launch_bounds__(256) k_step(SlotState st, int32_t *host_jobs,
         int nj = 0;
         uint64_t ok_n = 0, den_n = 0;
         bool dirty = false;
+        const float *esc = st.have_evict && st.ev_index[l] >= 0 ? st.ev_scores + (size_t)l * E : nullptr;
         for (int it = np - 1; it >= 0 && budget > 0; --it) {
             const int id = pend[it];
             if (tbl[id] != ns) {
@@ -579,11 +655,19 @@ __global__ void __launch_bounds__(256) k_step(SlotState st, int32_t *host_jobs,
             }
             int slot = -1;
             uint64_t best = ~0ull;
+            float best_score = 3.4e38f;
             for (int s = 0; s < ns; ++s) {
                 if (st.in_flight[so + s]) continue;
                 if (st.slot_expert[so + s] < 0) { slot = s; break; }
                 if (st.protect[so + s] >= n_steps) continue;
-                if (st.last_use[so + s] < best) { best = st.last_use[so + s]; slot = s; }
+                if (esc) {
+                    const float sc = esc[st.slot_expert[so + s]];
+                    if (evict_better(sc, st.last_use[so + s], best_score, best)) {
+                        best_score = sc; best = st.last_use[so + s]; slot = s;
+                    }
+                } else if (st.last_use[so + s] < best) {
+                    best = st.last_use[so + s]; slot = s;
+                }
             }
             if (slot < 0) break;
             const int victim = st.slot_expert[so + slot];
@@ -620,6 +704,14 @@ __global__ void __launch_bounds__(256) k_step(SlotState st, int32_t *host_jobs,
         if (dirty) s_dirty = 1;
     }
     __syncthreads();
+    // the token is over: its ids become the previous token's, after every
+    // eviction decision of the step (patches/0006:914-922)
+    if (st.have_evict)
+        for (int l = threadIdx.x; l < L; l += blockDim.x) {
+            const int nc = st.n_cur[l];
+            for (int i = 0; i < nc; ++i) st.prev_ids[(size_t)l * CUR_IDS + i] = st.cur_ids[(size_t)l * CUR_IDS + i];
+            st.n_prev[l] = nc;
+        }
     if (st.admit_mode == 1 && st.admit_half > 0 && n_steps % (uint64_t)st.admit_half == 0) {
         for (int i = threadIdx.x; i < L * E; i += blockDim.x) st.heat[i] = __fmul_rn(st.heat[i], 0.5f);
     }
@@ -729,6 +821,11 @@ cudaError_t launch_observe(const SlotState &st, int layer, const int32_t *ids, i
 
 cudaError_t launch_step(const SlotState &st, int32_t *host_jobs, int32_t *host_njobs,
                         cudaStream_t s) {
+    if (st.have_evict) {
+        k_evict_scores<<<st.n_layers, 256, 0, s>>>(st);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
     k_step<<<1, 256, 0, s>>>(st, host_jobs, host_njobs);
     return cudaGetLastError();
 }

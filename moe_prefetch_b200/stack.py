@@ -98,6 +98,19 @@ class MoeStack:
             return
         self._started = True
         c = self.cache
+        if c.evictor:
+            # loud either way (patches/0006:521-537): an evictor that silently
+            # fails to load looks exactly like one that does not help
+            from .predictor import MoePredictor, MoepError
+            try:
+                m = MoePredictor.load(c.evictor)
+                if m.n_expert != self.n_expert:
+                    raise MoepError(f"{c.evictor}: {m.n_expert} experts, the stack has {self.n_expert}")
+                self.set_evictor(m)
+                print(f"moe-cache: evictor loaded, {m.feat_dim} features, {len(m.layer_of)} layers",
+                      file=sys.stderr)
+            except (OSError, MoepError, MoeError) as e:
+                print(f"moe-cache: EVICTOR NOT LOADED: {e}", file=sys.stderr)
         if c.heat_file and self.cache.n_slots > 0:
             counts = load_heat(c.heat_file, self.n_layers, self.n_expert)
             placed = 0
@@ -366,6 +379,24 @@ class MoeStack:
         ids2 = ids.view(1, -1) if ids.dim() == 1 else ids
         self._ck(self.lib.moe_observe(self.ctx, layer, _ptr(ids2), ids2.shape[0], ids2.shape[1],
                                       _stream(stream)), "moe_observe")
+
+    def set_evictor(self, model):
+        """LLAMA_MOE_EVICTOR: `model` (a predictor.MoePredictor, MOEP v3)
+        scores each layer's resident experts at every step, and the victim is
+        the lowest score instead of the least recently used slot.  None
+        removes it."""
+        if model is None:
+            self._ck(self.lib.moe_set_evictor(self.ctx, 0, None, 0, None, None, None, None), "moe_set_evictor")
+            return
+        from .predictor import BLOCK_BELOW, BLOCK_CUR, BLOCK_PREV, BLOCK_SELF_PREV
+        lo = np.ascontiguousarray(model.layer_of, np.int32)
+        off = np.array([model.off[BLOCK_PREV], model.off[BLOCK_CUR], model.off[BLOCK_BELOW],
+                        model.off[BLOCK_SELF_PREV]], np.int32)
+        w = np.ascontiguousarray(model.w, np.float32)
+        b = np.ascontiguousarray(model.bias, np.float32)
+        pr = np.ascontiguousarray(model.prior, np.float32)
+        self._ck(self.lib.moe_set_evictor(self.ctx, len(lo), _ptr(lo), int(model.feat_dim), _ptr(off),
+                                          _ptr(w), _ptr(b), _ptr(pr)), "moe_set_evictor")
 
     def set_predictor(self, fn):
         """The predictor hook (cpp/moe-predictor.h as moe_obs_cb calls it):

@@ -985,6 +985,8 @@ typedef struct {
     int32_t n_pending;
     int32_t *cur_ids;
     int32_t n_cur;
+    int32_t *prev_ids;     /* cur_ids one token earlier (the evictor's features) */
+    int32_t n_prev;
     uint64_t n_hit, n_miss;
     float *heat;
     uint64_t *miss_last, *miss_prev;
@@ -996,9 +998,20 @@ typedef struct {
     int dirty;
 } or_layer;
 
+/* LLAMA_MOE_EVICTOR: an MOEP model scoring which resident expert is wanted
+ * again soon (patches/0006:521-537 load, :402-426 evict_scores) */
+typedef struct {
+    int32_t n_model, feat_dim;
+    int32_t off[4];        /* prev, cur, below, self_prev: row offsets, -1 absent */
+    int32_t *index_of;     /* [n_layers] model slot or -1 */
+    float *w, *bias, *prior;
+    float *scores;         /* [n_expert] scratch */
+} or_evictor;
+
 struct or_cache {
     or_cache_cfg cfg;
     or_layer *L;
+    or_evictor *ev;
     uint64_t clock, n_steps, n_uploads, n_scheduled, n_copied, n_published;
     uint64_t n_admit_ok, n_admit_denied, n_table_flushes;
     or_job *todo;
@@ -1029,6 +1042,7 @@ or_cache *or_cache_create(const or_cache_cfg *cfg) {
         L->free_slots = (int32_t *)malloc(sizeof(int32_t) * (size_t)ns);
         L->pending = (int32_t *)malloc(sizeof(int32_t) * (size_t)E);
         L->cur_ids = (int32_t *)malloc(sizeof(int32_t) * 4096);
+        L->prev_ids = (int32_t *)malloc(sizeof(int32_t) * 4096);
         L->tbl = (int32_t *)malloc(sizeof(int32_t) * (size_t)E);
         L->prior = (float *)calloc((size_t)E, sizeof(float));
         L->tbl_mirror = (int32_t *)malloc(sizeof(int32_t) * (size_t)E);
@@ -1061,13 +1075,99 @@ void or_cache_destroy(or_cache *c) {
     for (int l = 0; l < c->cfg.n_layers; ++l) {
         or_layer *L = &c->L[l];
         free(L->slot_expert); free(L->expert_slot); free(L->last_use); free(L->protect);
-        free(L->in_flight); free(L->free_slots); free(L->pending); free(L->cur_ids);
+        free(L->in_flight); free(L->free_slots); free(L->pending); free(L->cur_ids); free(L->prev_ids);
         free(L->tbl); free(L->prior); free(L->tbl_mirror); free(L->prior_mirror);
         free(L->heat); free(L->miss_last); free(L->miss_prev); free(L->use_count);
     }
     free(c->L);
     free(c->todo);
+    if (c->ev) {
+        free(c->ev->index_of); free(c->ev->w); free(c->ev->bias); free(c->ev->prior); free(c->ev->scores);
+        free(c->ev);
+    }
     free(c);
+}
+
+/* moe_predictor::score (cpp/moe-predictor.cpp:165-223), the evictor's and the
+ * predictor's score of one layer: the bias, plus the weight rows the ids of
+ * each block select (block order prev, cur, below, self_prev; ids in order;
+ * out-of-range ids skipped; a repeated id adds twice), z-scored with the mean
+ * and variance as running fp32 sums, then the repeat prior on the prev ids.
+ * No fused multiply-adds (-ffp-contract=off). */
+void or_evict_score(const float *W, const float *bias, float prior, const int32_t off[4], int E,
+                    const int32_t *prev, int n_prev, const int32_t *cur, int n_cur,
+                    const int32_t *below, int n_below, const int32_t *self_prev, int n_self_prev,
+                    float *out) {
+    const int32_t *ids[4] = {prev, cur, below, self_prev};
+    const int n[4] = {n_prev, n_cur, n_below, n_self_prev};
+    for (int j = 0; j < E; ++j) out[j] = bias[j];
+    for (int g = 0; g < 4; ++g) {
+        if (off[g] < 0 || !ids[g]) continue;
+        for (int i = 0; i < n[g]; ++i) {
+            const int32_t e = ids[g][i];
+            if (e < 0 || e >= E) continue;
+            const float *row = W + (size_t)(off[g] + e) * (size_t)E;
+            for (int j = 0; j < E; ++j) out[j] += row[j];
+        }
+    }
+    float mu = 0.0f;
+    for (int j = 0; j < E; ++j) mu += out[j];
+    mu /= (float)E;
+    float var = 0.0f;
+    for (int j = 0; j < E; ++j) {
+        const float d = out[j] - mu;
+        var += d * d;
+    }
+    const float sd = sqrtf(var / (float)E) + 1e-9f;
+    for (int j = 0; j < E; ++j) out[j] = (out[j] - mu) / sd;
+    if (prior != 0.0f && prev)
+        for (int i = 0; i < n_prev; ++i) {
+            const int32_t e = prev[i];
+            if (e >= 0 && e < E) out[e] += prior;
+        }
+}
+
+int or_cache_set_evictor(or_cache *c, int n_model, const int32_t *layer_of, int feat_dim,
+                         const int32_t off[4], const float *w, const float *bias, const float *prior) {
+    const int E = c->cfg.n_expert;
+    if (n_model <= 0 || feat_dim <= 0) return -1;
+    for (int g = 0; g < 4; ++g)
+        if (off[g] >= 0 && off[g] + E > feat_dim) return -1;
+    or_evictor *ev = (or_evictor *)calloc(1, sizeof(or_evictor));
+    ev->n_model = n_model;
+    ev->feat_dim = feat_dim;
+    for (int g = 0; g < 4; ++g) ev->off[g] = off[g];
+    ev->index_of = (int32_t *)malloc(sizeof(int32_t) * (size_t)c->cfg.n_layers);
+    for (int l = 0; l < c->cfg.n_layers; ++l) ev->index_of[l] = -1;
+    for (int m = 0; m < n_model; ++m)
+        if (layer_of[m] >= 0 && layer_of[m] < c->cfg.n_layers) ev->index_of[layer_of[m]] = m;
+    const size_t nw = (size_t)n_model * (size_t)feat_dim * (size_t)E;
+    ev->w = (float *)malloc(sizeof(float) * nw);
+    memcpy(ev->w, w, sizeof(float) * nw);
+    ev->bias = (float *)malloc(sizeof(float) * (size_t)n_model * (size_t)E);
+    memcpy(ev->bias, bias, sizeof(float) * (size_t)n_model * (size_t)E);
+    ev->prior = (float *)malloc(sizeof(float) * (size_t)n_model);
+    memcpy(ev->prior, prior, sizeof(float) * (size_t)n_model);
+    ev->scores = (float *)malloc(sizeof(float) * (size_t)E);
+    c->ev = ev;
+    return 0;
+}
+
+/* evict_scores (patches/0006:402-426) for layer li: false when the layer has
+ * no model.  Inputs: prev = the next layer's previous-token ids, cur = this
+ * layer's ids, below = the previous layer's ids, self_prev = this layer's
+ * previous-token ids. */
+static int evict_scores(or_cache *c, int li) {
+    or_evictor *ev = c->ev;
+    if (!ev || ev->index_of[li] < 0) return 0;
+    const int E = c->cfg.n_expert, m = ev->index_of[li];
+    const or_layer *L = &c->L[li];
+    const or_layer *A = li + 1 < c->cfg.n_layers ? &c->L[li + 1] : NULL;
+    const or_layer *B = li > 0 ? &c->L[li - 1] : NULL;
+    or_evict_score(ev->w + (size_t)m * ev->feat_dim * E, ev->bias + (size_t)m * E, ev->prior[m], ev->off, E,
+                   A ? A->prev_ids : NULL, A ? A->n_prev : 0, L->cur_ids, L->n_cur,
+                   B ? B->cur_ids : NULL, B ? B->n_cur : 0, L->prev_ids, L->n_prev, ev->scores);
+    return 1;
 }
 
 void or_cache_set_predictor(or_cache *c, or_predict_fn fn, void *ud) {
@@ -1276,6 +1376,11 @@ void or_cache_step(or_cache *c) {
         if (!c->cfg.early_issue) {
             if (L->n_pending == 0) continue;
             int budget = c->cfg.max_inserts;
+            /* the evictor on this path too (patches/0006:790-830, 0007:680-700):
+             * victim = an empty slot, else the lowest score (recency breaking
+             * ties), else LRU */
+            const int use_model = evict_scores(c, li);
+            const float *esc = use_model ? c->ev->scores : NULL;
             for (int it = L->n_pending - 1; it >= 0 && budget > 0; --it) {
                 const int32_t id = L->pending[it];
                 if (L->expert_slot[id] >= 0) {
@@ -1284,11 +1389,19 @@ void or_cache_step(or_cache *c) {
                 }
                 int32_t slot = -1;
                 uint64_t best = OR_U64_MAX;
+                float best_score = 3.4e38f;
                 for (int s = 0; s < L->ns; ++s) {
                     if (L->in_flight[s]) continue;
                     if (L->slot_expert[s] < 0) { slot = s; break; }
                     if (L->protect[s] >= c->n_steps) continue;
-                    if (L->last_use[s] < best) { best = L->last_use[s]; slot = s; }
+                    if (use_model) {
+                        const float sc = esc[L->slot_expert[s]];
+                        if (sc < best_score || (sc == best_score && L->last_use[s] < best)) {
+                            best_score = sc; best = L->last_use[s]; slot = s;
+                        }
+                    } else if (L->last_use[s] < best) {
+                        best = L->last_use[s]; slot = s;
+                    }
                 }
                 if (slot < 0) break;
                 const int32_t victim = L->slot_expert[slot];
@@ -1311,13 +1424,25 @@ void or_cache_step(or_cache *c) {
         const int have_pred = c->cfg.have_pred && c->pred;
         const int32_t pool_target = c->cfg.freeze ? 0
             : c->cfg.max_inserts + (have_pred ? c->cfg.predict_top : 0);
+        const int use_model = evict_scores(c, li);
+        const float *esc = use_model ? c->ev->scores : NULL;
         while (L->n_free < pool_target) {
             int32_t slot = -1;
             uint64_t best = OR_U64_MAX;
+            float best_score = 3.4e38f;
             for (int s = 0; s < L->ns; ++s) {
                 if (L->in_flight[s] || L->slot_expert[s] < 0) continue;
                 if (L->protect[s] >= c->n_steps) continue;
-                if (L->last_use[s] < best) { best = L->last_use[s]; slot = s; }
+                if (use_model) {
+                    /* lowest predicted chance of being wanted again; recency
+                     * breaks ties (patches/0006:871-889) */
+                    const float sc = esc[L->slot_expert[s]];
+                    if (sc < best_score || (sc == best_score && L->last_use[s] < best)) {
+                        best_score = sc; best = L->last_use[s]; slot = s;
+                    }
+                } else if (L->last_use[s] < best) {
+                    best = L->last_use[s]; slot = s;
+                }
             }
             if (slot < 0) break;
             const int32_t victim = L->slot_expert[slot];
@@ -1327,6 +1452,14 @@ void or_cache_step(or_cache *c) {
             L->free_slots[L->n_free++] = slot;
         }
     }
+    /* the token is over: its ids become the previous token's, after every
+     * eviction decision of the step (patches/0006:914-922) */
+    if (c->ev)
+        for (int li = 0; li < c->cfg.n_layers; ++li) {
+            or_layer *L = &c->L[li];
+            memcpy(L->prev_ids, L->cur_ids, sizeof(int32_t) * (size_t)L->n_cur);
+            L->n_prev = L->n_cur;
+        }
     /* heat decay (patches/0007:736-744) */
     if (c->cfg.admit_mode == 1 && c->cfg.admit_half > 0 &&
         c->n_steps % (uint64_t)c->cfg.admit_half == 0) {

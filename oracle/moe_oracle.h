@@ -189,6 +189,18 @@ typedef int (*or_predict_fn)(void *ud, int layer, const int32_t *cur, int n_cur,
                              int32_t *out, int k);
 
 or_cache *or_cache_create(const or_cache_cfg *cfg);
+/* moe_predictor::score (cpp/moe-predictor.cpp:165-223): W [feat_dim][E],
+ * bias [E]; off: row offsets of the prev, cur, below, self_prev blocks (-1:
+ * absent); any id list may be NULL. */
+void      or_evict_score(const float *W, const float *bias, float prior, const int32_t off[4], int E,
+                         const int32_t *prev, int n_prev, const int32_t *cur, int n_cur,
+                         const int32_t *below, int n_below, const int32_t *self_prev,
+                         int n_self_prev, float *out);
+/* LLAMA_MOE_EVICTOR: model slot m scores layer layer_of[m]; w [n_model][feat_dim][E],
+ * bias [n_model][E], prior [n_model]; copied.  0, or -1 on bad offsets. */
+int       or_cache_set_evictor(or_cache *c, int n_model, const int32_t *layer_of, int feat_dim,
+                               const int32_t off[4], const float *w, const float *bias,
+                               const float *prior);
 void      or_cache_destroy(or_cache *c);
 void      or_cache_set_predictor(or_cache *c, or_predict_fn fn, void *ud);
 /* moe_obs_cb for one layer: ids [n_tok][n_ids]; observed only when n_tok == 1

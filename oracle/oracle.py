@@ -120,6 +120,11 @@ def _declare(L):
     L.or_cache_warm_start.argtypes = [P]
     L.or_cache_warm_start.restype = I64
     L.or_cache_set_predictor.argtypes = [P, P, P]
+    L.or_evict_score.argtypes = [P, P, F32, P, C.c_int, P, C.c_int, P, C.c_int, P, C.c_int, P,
+                                 C.c_int, P]
+    L.or_evict_score.restype = None
+    L.or_cache_set_evictor.argtypes = [P, C.c_int, P, C.c_int, P, P, P, P]
+    L.or_cache_set_evictor.restype = C.c_int
     L.or_greedy_allocate_bytes.argtypes = [P, P, C.c_int, C.c_int, C.c_int, P, C.c_int, P, P, P]
     L.or_greedy_allocate_bytes.restype = C.c_double
 
@@ -446,6 +451,43 @@ class OracleCache:
 
     def warm_start(self):
         return int(lib().or_cache_warm_start(self.h))
+
+    def set_evictor(self, model):
+        """LLAMA_MOE_EVICTOR: `model` is a MoePredictor (MOEP v3)."""
+        arr = evictor_arrays(model, self.n_layers)
+        self._ev = arr
+        rc = lib().or_cache_set_evictor(self.h, arr["n_model"], _p(arr["layer_of"]), arr["feat_dim"],
+                                        _p(arr["off"]), _p(arr["w"]), _p(arr["bias"]), _p(arr["prior"]))
+        if rc != 0:
+            raise ValueError("or_cache_set_evictor refused the model")
+
+
+def evictor_arrays(model, n_layers):
+    """The arrays an evictor takes (MOEP v3 model of this stack's layers):
+    layer_of, off (prev, cur, below, self_prev), w, bias, prior."""
+    BLOCK_PREV, BLOCK_CUR, BLOCK_BELOW, BLOCK_SELF_PREV = 1, 2, 3, 4   # MOEP v3 block kinds
+    return {"n_model": int(len(model.layer_of)), "feat_dim": int(model.feat_dim),
+            "layer_of": np.ascontiguousarray(model.layer_of, np.int32),
+            "off": np.array([model.off[BLOCK_PREV], model.off[BLOCK_CUR], model.off[BLOCK_BELOW],
+                             model.off[BLOCK_SELF_PREV]], np.int32),
+            "w": np.ascontiguousarray(model.w, np.float32),
+            "bias": np.ascontiguousarray(model.bias, np.float32),
+            "prior": np.ascontiguousarray(model.prior, np.float32)}
+
+
+def evict_score(model, il, prev=(), cur=(), below=(), self_prev=()):
+    """or_evict_score on one layer of a MoePredictor (the C restatement)."""
+    arr = evictor_arrays(model, 0)
+    m = int(model.index_of[il])
+    E = model.n_expert
+    lists = [np.ascontiguousarray(x, np.int32) for x in (prev, cur, below, self_prev)]
+    out = np.empty(E, np.float32)
+    w = np.ascontiguousarray(arr["w"][m])
+    b = np.ascontiguousarray(arr["bias"][m])
+    lib().or_evict_score(_p(w), _p(b), float(arr["prior"][m]), _p(arr["off"]), E,
+                         _p(lists[0]), len(lists[0]), _p(lists[1]), len(lists[1]),
+                         _p(lists[2]), len(lists[2]), _p(lists[3]), len(lists[3]), _p(out))
+    return out
 
 
 def greedy_allocate_bytes(per_layer_miss8, grid, n_layers, uniform_cap, frozen_layers,

@@ -102,3 +102,25 @@ def ar1_states(n_tok, n_embd, rho=0.9, seed=12345):
         prev = rho * prev + np.sqrt(1 - rho * rho) * rng.standard_normal(n_embd)
         h[t] = prev
     return rms_norm(h)
+
+
+def toy_moep(n_layers, n_expert, layers, seed, blocks=(1, 2, 3, 4), prior=0.25):
+    """A seeded MOEP v3 model (moe_prefetch_b200.predictor.MoePredictor) with
+    the given layers and feature blocks (1 prev, 2 cur, 3 below, 4
+    self_prev), N(0, 1) weights and biases: a stand-in for a trained
+    evictor or predictor."""
+    from moe_prefetch_b200.predictor import MoePredictor
+    rng = np.random.default_rng(seed)
+    p = MoePredictor()
+    p.n_expert, p.n_layers, p.top_k = n_expert, n_layers, 8
+    for i, kind in enumerate(blocks):
+        p.off[kind] = i * n_expert
+    p.feat_dim = len(blocks) * n_expert
+    p.layer_of = np.asarray(layers, np.int32)
+    p.index_of = np.full(n_layers, -1, np.int32)
+    for i, il in enumerate(layers):
+        p.index_of[il] = i
+    p.prior = np.full(len(layers), prior, np.float32)
+    p.bias = rng.standard_normal((len(layers), n_expert)).astype(np.float32)
+    p.w = rng.standard_normal((len(layers), p.feat_dim, n_expert)).astype(np.float32)
+    return p

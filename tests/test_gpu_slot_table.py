@@ -362,3 +362,73 @@ def test_decode_with_cache_early_issue(oracle_lib):
     _needs_gpu()
     s = _decode_with_cache(oracle_lib, L=3, n_tok=24, ns=24, early=True)
     assert s["uploads"] > 0
+
+
+@pytest.mark.parametrize("early,admit,predict", [
+    (False, "off", False),
+    (False, "window", False),
+    (True, "off", False),
+    (True, "heat", True),
+])
+def test_evictor_matches_oracle(oracle_lib, early, admit, predict):
+    """LLAMA_MOE_EVICTOR (patches/0006:402-426, :790-913; 0007:680-727): the
+    device scores each layer with the model at every step and evicts the
+    lowest score (recency breaking ties) in the scheduling and the early-issue
+    top-up; layer 1 has no model and keeps LRU.  Tables, recency, flags and
+    counters equal the oracle's after every step; every published slot holds
+    its expert's bytes."""
+    _needs_gpu()
+    from conftest import toy_moep
+    from moe_prefetch_b200 import MoeCacheConfig, MoeStack
+    L, E, k, n_ff, ns = 3, 32, 8, 256, 12
+    model = toy_moep(L, E, [0, 2], seed=17, prior=0.25)
+    cfg = MoeCacheConfig(n_slots=ns, max_inserts=2, admit=admit, batch_tables=True, admit_half=16,
+                         early_issue=early, predict_top=3)
+    st = MoeStack(n_layers=L, n_expert=E, n_used=k, n_ff=n_ff, cache=cfg)
+    hw = [_host_weights(E, st.gate_bytes, st.down_bytes, 70 + s) for s in range(L)]
+    for il in range(L):
+        st.set_expert_weights(il, *hw[il])
+    st.set_evictor(model)
+
+    def pred(layer, cur, next_prev, kk):
+        return (list(next_prev) + [(v + 3) % E for v in cur])[:kk]
+    if predict:
+        st.set_predictor(pred)
+    oc = oracle_lib.OracleCache(L, E, ns, max_inserts=2, admit_mode=cfg.admit_mode,
+                                admit_window=cfg.admit_window, admit_half=16, admit_floor=cfg.admit_floor,
+                                batch_tables=True, early_issue=early, predict_top=3,
+                                predictor=pred if predict else None)
+    oc.set_evictor(model)
+    tr = _trace(40, L, E, k, seed=hash((early, admit, predict, 3)) & 0xFFFF)
+    lru = oracle_lib.OracleCache(L, E, ns, max_inserts=2, admit_mode=cfg.admit_mode,
+                                 admit_window=cfg.admit_window, admit_half=16, admit_floor=cfg.admit_floor,
+                                 batch_tables=True, early_issue=early, predict_top=3,
+                                 predictor=pred if predict else None)
+    differs = 0
+    for t in range(tr.shape[0]):
+        for il in range(L):
+            st.observe(il, torch.from_numpy(tr[t, il]).cuda())
+            oc.observe(il, tr[t, il])
+            lru.observe(il, tr[t, il])
+        st.step()
+        oc.step()
+        lru.step()
+        _compare(st, oc, L, f"token {t}")
+        differs += int(any(not np.array_equal(oc.tables(il)["slot_expert"], lru.tables(il)["slot_expert"])
+                           for il in (0, 2)))
+        assert np.array_equal(oc.tables(1)["slot_expert"], lru.tables(1)["slot_expert"]), "layer 1 keeps LRU"
+    assert differs > 0, "the model never chose another victim than LRU"
+    st.step(); oc.step()
+    torch.cuda.synchronize()
+    for il in range(L):
+        g, u, d = st.slot_views(il)
+        se = st.tables(il)["slot_expert"]
+        hg, hu, hd = (x.numpy() for x in hw[il])
+        for sl, e in enumerate(se):
+            if e >= 0:
+                assert np.array_equal(g[sl].cpu().numpy(), hg[e * st.gate_bytes:(e + 1) * st.gate_bytes])
+                assert np.array_equal(d[sl].cpu().numpy(), hd[e * st.down_bytes:(e + 1) * st.down_bytes])
+    st.set_evictor(None)
+    st.close()
+    oc.close()
+    lru.close()
