@@ -262,6 +262,109 @@ def lru_miss_rates(ids, grid):
     return out
 
 
+def run_stream(args):
+    """Just-in-time streaming (LLAMA_MOE_STREAM) measured: the config-2 stack
+    (48 layers, every expert in pinned host memory, a byte-priced 56-slot
+    profile, window admission, early issue, delta 0) decoded token by token
+    through the per-layer entry point moe_layer_forward, the next layer's
+    input being the RMS-normed residual sum.  The rest of a transformer layer
+    (attention) is stood in for by a fixed spin of --attn-us on the GPU per
+    layer (torch.cuda._sleep), the time in which streamed copies land.  One
+    JSON line per (attention time, streaming off/on)."""
+    import torch
+    from moe_prefetch_b200 import MoeCacheConfig, MoeStack
+    from moe_prefetch_b200.config import format_slot_profile, greedy_allocate_bytes
+
+    torch.cuda.set_device(0)
+    n_layers = args.layers
+    warm, timed = args.c2_warm, args.c2_tokens
+    res = MoeStack(n_layers=n_layers)
+    res.synth_resident(seed=11, keep_router=True)
+    host = []
+    for il in range(n_layers):
+        g, u, d = res.slot_views(il)
+        hl = []
+        for v in (g, u, d):
+            t = torch.empty(N_EXPERT * v.shape[1], dtype=torch.uint8, pin_memory=True)
+            t.view(N_EXPERT, -1).copy_(v[:N_EXPERT])
+            hl.append(t)
+        host.append(tuple(hl))
+    routers = [r.clone() for r in res.routers]
+    h_trace = torch.from_numpy(ar1_states(256, N_EMBD, seed=4242)).cuda()
+    _, dm = res.decode(h_trace, debug=True)
+    res.sync()
+    trace = dm["ids"].cpu().numpy()
+    del dm
+    res.close()
+    torch.cuda.synchronize()
+    miss8 = lru_miss_rates(trace, MISS_GRID)
+    grid = [g for g in MISS_GRID if g <= N_EXPERT]
+    caps, _, _ = greedy_allocate_bytes(miss8, grid, n_layers, 56, [], [EXPERT_BYTES] * n_layers)
+    h = torch.from_numpy(ar1_states(warm + timed, N_EMBD, seed=12345)).cuda()
+    # GPU clock cycles for the attention stand-in, from the measured SM clock
+    try:
+        mhz = int(torch.cuda.clock_rate()) or 1965
+    except Exception:   # no NVML: the B200's maximum SM clock
+        mhz = 1965
+    stream = torch.cuda.current_stream()
+    for attn_us in args.attn_us:
+        cycles = int(attn_us * mhz)
+        for on in (False, True):
+            cfg = MoeCacheConfig(n_slots=56, max_inserts=2, admit="window", admit_window=8,
+                                 batch_tables=True, early_issue=True, stream=on,
+                                 slot_profile=format_slot_profile(caps))
+            st = MoeStack(n_layers=n_layers, cache=cfg)
+            for il in range(n_layers):
+                st.set_router(il, routers[il])
+                st.set_expert_weights(il, *host[il])
+
+            def token(t):
+                x = h[t:t + 1]
+                for il in range(n_layers):
+                    if cycles:
+                        torch.cuda._sleep(cycles)
+                    y, _, _ = st.layer_forward(il, x)
+                    z = x + y
+                    x = z * torch.rsqrt((z * z).mean(-1, keepdim=True) + 1e-6)
+                st.step()
+            for t in range(warm):
+                token(t)
+            torch.cuda.synchronize()
+            s0, q0 = st.stats(), st.stream_stats()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for t in range(warm, warm + timed):
+                token(t)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            s1, q1 = st.stats(), st.stream_stats()
+            ms = e0.elapsed_time(e1)
+            d = {k: s1[k] - s0[k] for k in s1}
+            q = {k: q1[k] - q0[k] for k in q1}
+            routed = d["hits"] + d["misses"]
+            line = {
+                "metric": "config2 per-layer decode with just-in-time streaming", "value": timed / (ms / 1000.0),
+                "unit": "tok/s", "n_gpus": 1, "higher_is_better": True,
+                "config": {"workload": "config2 stack through moe_layer_forward, one token at a time, "
+                                       "56-slot byte-priced profile, window admission, early issue, delta 0",
+                           "stream": on, "attention_stand_in_us": attn_us,
+                           "warm_tokens": warm, "timed_tokens": timed},
+                "hit_rate": d["hits"] / routed if routed else None,
+                "misses_per_token": d["misses"] / timed,
+                "ms_per_token": ms / timed,
+                "stream": ({"experts_streamed_per_token": q["words"] / timed,
+                            "in_time_per_token": q["in_time"] / timed,
+                            "late_per_token": q["late"] / timed,
+                            "dropped_late_per_token": q["dropped_late"] / timed,
+                            "given_back_per_token": q["given_back"] / timed,
+                            "stream_gbs": q["bytes"] / (ms / 1000.0) / 1e9} if on else None),
+            }
+            print(json.dumps(line), flush=True)
+            st.close()
+    return 0
+
+
 def run_config2(args):
     """Config 2: the 48-layer stack with every expert in pinned host memory
     and a slot cache of n_slots per layer (byte-priced per-layer profile from
@@ -954,7 +1057,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--workload", default="config1",
                     choices=["config0", "config1", "config2", "config3", "config4", "layer", "phases",
-                             "hostlink"])
+                             "hostlink", "stream"])
+    ap.add_argument("--attn-us", type=float, nargs="+", default=[0.0, 60.0],
+                    help="stream: GPU time standing in for the rest of a layer, per layer")
     ap.add_argument("--c4", action="store_true", help="phases: config-4 shapes")
     ap.add_argument("--path", default="gemv", choices=["auto", "gemv", "gemm"])
     ap.add_argument("--c3-decode-steps", type=int, default=128)
@@ -984,6 +1089,8 @@ def main():
         return run_hostlink(args)
     if args.workload == "config0":
         return run_config0(args)
+    if args.workload == "stream":
+        return run_stream(args)
 
     import torch
     import torch.distributed as dist
