@@ -371,14 +371,17 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
 // TMEM address.  The A operand of the main term lives in TMEM (written by
 // the dequantising threads with tcgen05.st), so that the weights, once
 // dequantised, cross shared memory neither on the way in nor on the way to
-// the tensor cores.  TMEM columns: D [2 super-block parity][gate, up] x 64 at
-// 0..255, A [2 stage parity][gate, up] x 32 at 384..511.
+// the tensor cores.  A stage is K = 128 (two Q4_K groups, eight MMAs per
+// matrix per barrier round trip).  TMEM columns: D [2 super-block
+// parity][gate, up] x 64 at 0..255, A [2 stage parity][gate, up] x 64 at
+// 256..511.
 #define GU_RAW_BYTES (GM_ROWS * MOE_Q4K_BYTES)     // 18432
 #define GU_X_BYTES (GM_ROWS * GM_NT * 4)           // 32768
 #define GU_AM_BYTES (GM_ROWS * 32 * 2)             // 8192
-#define GU_B_BYTES (GM_NT * GM_KS_GU * 2)          // 8192
+#define GU_KS 128                                  // K per stage
+#define GU_B_BYTES (GM_NT * GU_KS * 2)             // 16384
 #define GU_BM_BYTES (GM_NT * 32 * 2)               // 4096
-#define GU_NB 6
+#define GU_NB 4
 #define GU_OFF_X (4 * GU_RAW_BYTES)
 #define GU_OFF_AM (GU_OFF_X + GU_X_BYTES)
 #define GU_OFF_B (GU_OFF_AM + 2 * GU_AM_BYTES)
@@ -460,7 +463,7 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gemm_gate_up(
     uint64_t *raw_free = raw_full + 2;   // [2]
     uint32_t *tslot = reinterpret_cast<uint32_t *>(raw_free + 2);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int S = n_embd / GM_KS_GU, NSB = S / 4;
+    const int S = n_embd / GU_KS, NSB = S / 2;   // two stages per super-block
     const size_t rb = (size_t)(n_embd / MOE_QK) * MOE_Q4K_BYTES;   // bytes per row
     if (tid == 0) {
         for (int q = 0; q < 4; ++q) {
@@ -508,18 +511,19 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gemm_gate_up(
                                     &raw_full[bf]);
                         ++rseq;
                     }
-                    for (int g = 0; g < 4; ++g, ++gs) {
+                    for (int h = 0; h < 2; ++h, ++gs) {
                         // ring slot gs % NB, last read by the MMAs of stage gs - NB
-                        // (the min-term buffer of a first stage, by stage gs - 8)
+                        // (the min-term buffer of a first stage, by stage gs - 4)
                         const int nb = gs % GU_NB;
                         if (gs >= GU_NB && !mbar_wait(&b_free[nb], ((gs / GU_NB) - 1) & 1)) ok = false;
-                        const int s = 4 * sb + g;
+                        const int s = 2 * sb + h;
                         fence_proxy_async();
-                        mbar_arrive_expect_tx(&b_full[nb], GU_B_BYTES + (g == 0 ? GU_BM_BYTES : 0));
-                        bulk_g2s(sB + nb * GU_B_BYTES, xtile + (size_t)s * GM_NT * GM_KS_GU, GU_B_BYTES,
+                        mbar_arrive_expect_tx(&b_full[nb], GU_B_BYTES + (h == 0 ? GU_BM_BYTES : 0));
+                        // two 64-wide blocks of the gathered tile, contiguous
+                        bulk_g2s(sB + nb * GU_B_BYTES, xtile + (size_t)s * GM_NT * GU_KS, GU_B_BYTES,
                                  &b_full[nb]);
-                        if (g == 0)
-                            bulk_g2s(sBm + ((gs >> 2) & 1) * GU_BM_BYTES, mtile + (size_t)sb * 32 * GM_NT,
+                        if (h == 0)
+                            bulk_g2s(sBm + ((gs >> 1) & 1) * GU_BM_BYTES, mtile + (size_t)sb * 32 * GM_NT,
                                      GU_BM_BYTES, &b_full[nb]);
                     }
                 }
@@ -536,20 +540,22 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gemm_gate_up(
                 if (!gu_item(src, tiles, cnt, w, RB, n_ff, it)) continue;
                 const uint32_t idesc = idesc_f16(GM_ROWS, it.N);
                 for (int s = 0; s < S; ++s, ++gs) {
-                    const int gsb = gs >> 2, g = s & 3, b = gsb & 1;
+                    const int gsb = gs >> 1, g = s & 1, b = gsb & 1;
                     // D[b] was last used by super-block gsb - 2: wait for its epilogue
                     if (g == 0 && gsb >= 2 && !mbar_wait(&d_free[mat * 2 + b], ((gsb - 2) >> 1) & 1)) ok = false;
                     const bool ready = mbar_wait(&a_full[mat * 2 + (gs & 1)], (gs >> 1) & 1) &&
                                        mbar_wait(&b_full[gs % GU_NB], (gs / GU_NB) & 1);
                     tc_fence_after();
                     if (ready) {
-                        const uint32_t aA = tmem + 384 + (uint32_t)((2 * (gs & 1) + mat) * 32);
+                        const uint32_t aA = tmem + 256 + (uint32_t)((2 * (gs & 1) + mat) * 64);
                         const uint32_t bB = smem_u32(sB + (gs % GU_NB) * GU_B_BYTES);
                         const uint32_t dD = tmem + (uint32_t)((2 * b + mat) * 64);
 #pragma unroll
-                        for (int j = 0; j < GM_KS_GU / 16; ++j)
-                            tc_mma_ts(dD, aA + 8 * j, smem_desc(bB + j * 2 * (GM_NT * 16), GM_NT * 16, 128), idesc,
-                                      (g | j) != 0);
+                        for (int j = 0; j < GU_KS / 16; ++j)   // K step j: block j / 4 of the two 64-wide ones
+                            tc_mma_ts(dD, aA + 8 * j,
+                                      smem_desc(bB + (j >> 2) * GM_NT * GM_KS_GU * 2 + (j & 3) * 2 * (GM_NT * 16),
+                                                GM_NT * 16, 128),
+                                      idesc, (g | j) != 0);
                         if (g == 0) {   // the folded min term of the super-block: K = 32
                             const uint32_t mA = smem_u32(sAm + mat * GU_AM_BYTES);
                             const uint32_t bM = smem_u32(sBm + b * GU_BM_BYTES);
@@ -563,7 +569,7 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gemm_gate_up(
                     }
                     tc_commit(&mma_done[mat * 2 + (gs & 1)]);
                     tc_commit(&b_free[gs % GU_NB]);
-                    if (g == 3) tc_commit(&d_full[mat * 2 + b]);
+                    if (g == 1) tc_commit(&d_full[mat * 2 + b]);
                 }
             }
         }
@@ -580,30 +586,34 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gemm_gate_up(
             }
             const uint8_t *hrow = (mat ? it.ubase : it.gbase) + (size_t)(it.r0 + m) * rb;   // a miss: host memory
             for (int s = 0; s < S; ++s, ++gs) {
-                const int gsb = gs >> 2, sb = s >> 2, g = s & 3, bf = rseq & 1;
+                const int gsb = gs >> 1, sb = s >> 1, g = s & 1, bf = rseq & 1;
                 if (it.dev && g == 0 && !mbar_wait(&raw_full[bf], (rseq >> 1) & 1)) ok = false;
                 if (gs >= 2 && !mbar_wait(&mma_done[mat * 2 + (gs & 1)], ((gs - 2) >> 1) & 1)) ok = false;
                 // this thread's TMEM lane (row m), A columns of (stage parity, mat)
-                const uint32_t A = tmem + ((uint32_t)((warp & 3) * 32) << 16) + 384 +
-                                   (uint32_t)((2 * (gs & 1) + mat) * 32);
-                // one min tile per matrix: the MMAs of stage gs - 4 (its last
-                // reader) are done when the wait for stage gs - 2 above returns
+                const uint32_t A = tmem + ((uint32_t)((warp & 3) * 32) << 16) + 256 +
+                                   (uint32_t)((2 * (gs & 1) + mat) * 64);
+                // one min tile per matrix: the MMAs of stage gs - 2 (its last
+                // reader) are done when the wait above returns
                 uint8_t *Am = g == 0 ? sAm + mat * GU_AM_BYTES : nullptr;
                 float *dd = &sD[((gsb & 3) * 2 + mat) * GM_ROWS + m];
-                // two calls, so that each reads its raw block in a known address
-                // space (shared loads, not generic ones, on the hot path)
-                if (it.dev)
-                    deq2_q4k(sRaw + (2 * bf + mat) * GU_RAW_BYTES + m * MOE_Q4K_BYTES, g, A, m, Am, dd);
-                else
-                    deq2_q4k(hrow + (size_t)sb * MOE_Q4K_BYTES, g, A, m, Am, dd);
+                // groups 2g, 2g + 1 of the super-block; each call reads its raw
+                // block in a known address space (shared loads on the hot path)
+                for (int h = 0; h < 2; ++h) {
+                    if (it.dev)
+                        deq2_q4k(sRaw + (2 * bf + mat) * GU_RAW_BYTES + m * MOE_Q4K_BYTES, 2 * g + h, A + 32 * h, m,
+                                 h == 0 ? Am : nullptr, dd);
+                    else
+                        deq2_q4k(hrow + (size_t)sb * MOE_Q4K_BYTES, 2 * g + h, A + 32 * h, m, h == 0 ? Am : nullptr,
+                                 dd);
+                }
                 if (g == 0) fence_proxy_async();   // the min tile, read by the tensor cores
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
                     mbar_arrive(&a_full[mat * 2 + (gs & 1)]);
-                    if (it.dev && g == 3) mbar_arrive(&raw_free[bf]);
+                    if (it.dev && g == 1) mbar_arrive(&raw_free[bf]);
                 }
-                if (it.dev && g == 3) ++rseq;
+                if (it.dev && g == 1) ++rseq;
             }
         }
     } else {
