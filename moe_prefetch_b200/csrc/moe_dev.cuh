@@ -719,11 +719,20 @@ __device__ __forceinline__ float q4k_unit_compute(const Q4Unit &u, int p, const 
     return q4k_unit_float(slo, shi, sc0, m0, sc1, m1, d, dmin, a);
 }
 
+// int -> float without the conversion unit, exact for |v| <= 2^22: v added
+// to the bits of 1.5 * 2^23 (a float whose ulp is 1 over [2^23, 2^24)),
+// then 1.5 * 2^23 subtracted.  An integer add and a float add instead of an
+// I2F, for the kernels in which conversions contend for the XU pipe.
+__device__ __forceinline__ float i2f_small(int v) {
+    return __fsub_rn(__int_as_float(0x4B400000 + v), 12582912.0f);
+}
+
 // A Q4_K unit decoded once for many activation rows: the nibble words, the
-// integer scales / mins of its two sub-blocks, d and dmin.
+// integer scales and (as floats) the mins of its two sub-blocks, d and dmin.
 struct Q4UnitDec {
     int lo[8], hi[8];
-    int sc0, m0, sc1, m1;
+    int sc0, sc1;
+    float m0, m1;
     float d, dmin;
 };
 
@@ -734,13 +743,17 @@ __device__ __forceinline__ void q4k_unit_decode(const Q4Unit &u, int p, Q4UnitDe
         o.lo[i] = (int)(w[i] & 0x0F0F0F0Fu);
         o.hi[i] = (int)((w[i] >> 4) & 0x0F0F0F0Fu);
     }
-    q4k_sm_pair(u.hdr.y, u.hdr.z, u.hdr.w, p, o.sc0, o.m0, o.sc1, o.m1);
+    int m0, m1;
+    q4k_sm_pair(u.hdr.y, u.hdr.z, u.hdr.w, p, o.sc0, m0, o.sc1, m1);
+    o.m0 = (float)m0;
+    o.m1 = (float)m1;
     o.d = h2f(u.hdr.x);
     o.dmin = h2f(u.hdr.x >> 16);
 }
 
 // q4k_unit_compute on a decoded unit: the same integer sums and the same
-// float expression, bit for bit.
+// float expression, bit for bit (sc * sum is at most 63 * 32 * 15 * 128 <
+// 2^22, so i2f_small converts it exactly).
 __device__ __forceinline__ float q4k_dec_compute(const Q4UnitDec &u, const ActQ4 &a) {
     int slo = 0, shi = 0;
 #pragma unroll
@@ -748,7 +761,9 @@ __device__ __forceinline__ float q4k_dec_compute(const Q4UnitDec &u, const ActQ4
         slo = __dp4a(u.lo[i], a.lo[i], slo);
         shi = __dp4a(u.hi[i], a.hi[i], shi);
     }
-    return q4k_unit_float(slo, shi, u.sc0, u.m0, u.sc1, u.m1, u.d, u.dmin, a);
+    const float acc = __fmaf_rn(i2f_small(u.sc1 * shi), a.d1, __fmul_rn(i2f_small(u.sc0 * slo), a.d0));
+    const float mm = __fmaf_rn(u.m1, a.s1, __fmul_rn(u.m0, a.s0));
+    return __fmaf_rn(u.d, acc, -__fmul_rn(u.dmin, mm));
 }
 
 // Partial dot of one unit of a Q4_K row (16-byte aligned block pointer `blk`
