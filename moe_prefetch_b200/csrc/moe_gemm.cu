@@ -28,7 +28,8 @@
 //
 // Numerics: activations are rounded to fp16 once, and products accumulate in
 // fp32.  Gate/up weights are not rounded (their min term's two factors are
-// carried as fp16 hi + lo); down weights are rounded to fp16 once.  The
+// carried as fp16 hi + lo); a down weight is its fp16 scale d * sc times the
+// exact integer q6 - 32, rounded to fp16 (two roundings).  The
 // reference for this path is exact weights times unquantised activations
 // with fp64 accumulation.  The GEMV kernels' Q8_1 activations are a
 // different rounding, so the two paths agree only within tolerance.
@@ -135,18 +136,6 @@ __device__ __forceinline__ void st_shared_v4(void *p, uint32_t a, uint32_t b, ui
     asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(p)), "r"(a), "r"(b),
                  "r"(c), "r"(d)
                  : "memory");
-}
-
-// Exact small integer -> float (0 <= q < 2^23).
-__device__ __forceinline__ float u2f(uint32_t q) {
-    return __int_as_float(0x4B000000 | q) - 8388608.0f;
-}
-
-// Byte j of x as an exact float minus `bias`: the byte placed into the low
-// mantissa of 2^23 (0x4B0000xx) by one byte permute, then one subtraction
-// (exact for small integers), i.e. the same value as u2f(byte) - (bias - 2^23).
-__device__ __forceinline__ float byte_f(uint32_t x, int j, float bias) {
-    return __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7650u | (uint32_t)j)) - bias;
 }
 
 // ---- operand tiles --------------------------------------------------------
@@ -671,26 +660,32 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gemm_gate_up(
 }
 
 // Quarter q (32 elements, l = 0..31) of a Q6_K half block -> row m of a
-// canonical 128-row tile at `A` (LBO 2048): w = d * sc * (q6 - 32) in fp32,
-// rounded to fp16 once.  src: the 8 ql words of the quarter (low half of the
-// half block for even q, high for odd), qh: the half's 8 qh words.
+// canonical 128-row tile at `A` (LBO 2048): w = ws * (q6 - 32) in fp16, with
+// ws = d * sc rounded to fp16 once per 16 elements, and the product of ws
+// and the exact integer q6 - 32 rounded once.  Per pair of weights: a byte
+// permute places q6 in the mantissa of 1024 (0x64xx), a packed subtraction
+// of 1056 leaves q6 - 32 exactly, and a packed multiplication applies ws.
+// src: the 8 ql words of the quarter (low half of the half block for even q,
+// high for odd), qh: the half's 8 qh words.
 __device__ __forceinline__ void deq_q6k_quarter(const uint32_t (&src)[8], const uint32_t (&qh)[8],
                                                 const uint32_t (&sc)[2], float d, int q, uint8_t *A,
                                                 int m) {
     uint8_t *row = A + (m >> 3) * 128 + (m & 7) * 16;
     const int ns = 4 * (q >> 1), hs = 2 * q;
+    const __half2 bias = __float2half2_rn(1056.0f);
 #pragma unroll
     for (int c = 0; c < 4; ++c) {                      // l = 8c .. 8c+7
         const int g = (c >> 1) + 2 * q;                // scale byte (l / 16) + 2q
         const uint32_t scw = (g >> 2) ? sc[1] : sc[0];   // a select, not an indexed (local) array
-        const float ws = d * (float)(int8_t)((scw >> (8 * (g & 3))) & 0xFFu);
+        const __half2 ws = __float2half2_rn(d * (float)(int8_t)((scw >> (8 * (g & 3))) & 0xFFu));
         uint32_t o[4];
 #pragma unroll
         for (int wi = 0; wi < 2; ++wi) {
             const int i = 2 * c + wi;
             const uint32_t v6 = ((src[i] >> ns) & 0x0F0F0F0Fu) | (((qh[i] >> hs) & 0x03030303u) << 4);
-            o[2 * wi] = pack_h2(ws * byte_f(v6, 0, 8388640.0f), ws * byte_f(v6, 1, 8388640.0f));
-            o[2 * wi + 1] = pack_h2(ws * byte_f(v6, 2, 8388640.0f), ws * byte_f(v6, 3, 8388640.0f));
+            const uint32_t lo = __byte_perm(v6, 0x64646464u, 0x4140u), hi = __byte_perm(v6, 0x64646464u, 0x4342u);
+            o[2 * wi] = h2_bits(__hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&lo), bias), ws));
+            o[2 * wi + 1] = h2_bits(__hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&hi), bias), ws));
         }
         st_shared_v4(row + (4 * q + c) * 2048, o[0], o[1], o[2], o[3]);
     }
