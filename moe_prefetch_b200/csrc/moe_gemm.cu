@@ -659,18 +659,28 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gemm_gate_up(
     if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
-// Quarter q (32 elements, l = 0..31) of a Q6_K half block -> row m of a
-// canonical 128-row tile at `A` (LBO 2048): w = ws * (q6 - 32) in fp16, with
-// ws = d * sc rounded to fp16 once per 16 elements, and the product of ws
-// and the exact integer q6 - 32 rounded once.  Per pair of weights: a byte
-// permute places q6 in the mantissa of 1024 (0x64xx), a packed subtraction
-// of 1056 leaves q6 - 32 exactly, and a packed multiplication applies ws.
-// src: the 8 ql words of the quarter (low half of the half block for even q,
-// high for odd), qh: the half's 8 qh words.
+// 16 consecutive 32-bit TMEM columns of the calling thread's lane, then
+// waited for.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+        "%13, %14, %15, %16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Quarter q (32 elements, l = 0..31) of a Q6_K half block -> 16 words of
+// packed fp16 in K order (word c: elements 2c, 2c + 1): w = ws * (q6 - 32),
+// with ws = d * sc rounded to fp16 once per 16 elements, and the product of
+// ws and the exact integer q6 - 32 rounded once.  Per pair of weights: a
+// byte permute places q6 in the mantissa of 1024 (0x64xx), a packed
+// subtraction of 1056 leaves q6 - 32 exactly, and a packed multiplication
+// applies ws.  src: the 8 ql words of the quarter (low half of the half
+// block for even q, high for odd), qh: the half's 8 qh words.
 __device__ __forceinline__ void deq_q6k_quarter(const uint32_t (&src)[8], const uint32_t (&qh)[8],
-                                                const uint32_t (&sc)[2], float d, int q, uint8_t *A,
-                                                int m) {
-    uint8_t *row = A + (m >> 3) * 128 + (m & 7) * 16;
+                                                const uint32_t (&sc)[2], float d, int q, uint32_t (&o)[16]) {
     const int ns = 4 * (q >> 1), hs = 2 * q;
     const __half2 bias = __float2half2_rn(1056.0f);
 #pragma unroll
@@ -678,174 +688,262 @@ __device__ __forceinline__ void deq_q6k_quarter(const uint32_t (&src)[8], const 
         const int g = (c >> 1) + 2 * q;                // scale byte (l / 16) + 2q
         const uint32_t scw = (g >> 2) ? sc[1] : sc[0];   // a select, not an indexed (local) array
         const __half2 ws = __float2half2_rn(d * (float)(int8_t)((scw >> (8 * (g & 3))) & 0xFFu));
-        uint32_t o[4];
 #pragma unroll
         for (int wi = 0; wi < 2; ++wi) {
             const int i = 2 * c + wi;
             const uint32_t v6 = ((src[i] >> ns) & 0x0F0F0F0Fu) | (((qh[i] >> hs) & 0x03030303u) << 4);
             const uint32_t lo = __byte_perm(v6, 0x64646464u, 0x4140u), hi = __byte_perm(v6, 0x64646464u, 0x4342u);
-            o[2 * wi] = h2_bits(__hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&lo), bias), ws));
-            o[2 * wi + 1] = h2_bits(__hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&hi), bias), ws));
+            o[4 * c + 2 * wi] = h2_bits(__hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&lo), bias), ws));
+            o[4 * c + 2 * wi + 1] = h2_bits(__hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&hi), bias), ws));
         }
-        st_shared_v4(row + (4 * q + c) * 2048, o[0], o[1], o[2], o[3]);
     }
 }
 
-// Shared memory of k_gemm_down: the CTA's 128 Q6_K rows (one bulk copy, the
-// rows being contiguous), A[2][128 x 128 fp16] (32 KB each), B[3][64 x 128
-// fp16] (16 KB each), barriers, TMEM address.
-#define DN_A_BYTES (GM_ROWS * GM_KS_DN * 2)
+// Shared memory of k_gemm_down (bytes): the 128 Q6_K rows of two items [2]
+// (one bulk copy each, the rows being contiguous), the token-tile ring
+// B [DN_NB] 64 x 128 fp16, barriers, TMEM address.  The A operand lives in
+// TMEM, written by the dequantising threads (tcgen05.st).  TMEM columns: D
+// [item parity] x 64 at 0..127, A [stage parity] x 64 (K = 128 as fp16
+// pairs) at 128..255.
 #define DN_B_BYTES (GM_NT * GM_KS_DN * 2)
-static inline int dn_rows_bytes(int n_ff) { return ((GM_ROWS * (n_ff / MOE_QK) * MOE_Q6K_BYTES) + 127) & ~127; }
-static inline int dn_smem(int n_ff) { return dn_rows_bytes(n_ff) + 2 * DN_A_BYTES + 3 * DN_B_BYTES + 128; }
+#define DN_NB 3
+__host__ __device__ static inline int dn_rows_bytes(int n_ff) {
+    return ((GM_ROWS * (n_ff / MOE_QK) * MOE_Q6K_BYTES) + 127) & ~127;
+}
+static inline int dn_smem(int n_ff) { return 2 * dn_rows_bytes(n_ff) + DN_NB * DN_B_BYTES + 256; }
+#define DN_EPI 4                                           // epilogue warps
+#define DN_ALL_THREADS (DN_THREADS + 2 * 32 + DN_EPI * 32)  // + copy warp, MMA warp, epilogue warps
 
-// Warp roles as in k_gemm_gate_up: warps 0-15 (DN_THREADS) dequantise, four
-// threads per row; warp 16 issues the token-tile copies and the MMAs.
-#define DN_ALL_THREADS (DN_THREADS + 32)
+// One work item of the persistent down kernel: 128 rows (row block r0 /
+// 128) of one expert tile.
+struct DnItem {
+    const uint8_t *rows;   // the item's first row (device slot, or host memory for a miss); null: none
+    int i, np, N, pos0, r0, dev;
+};
+
+__device__ __forceinline__ DnItem dn_item(const ExpertSrc &src, const int32_t *off, const int32_t *tiles,
+                                          const int32_t *cnt, int w, int RB, size_t rb) {
+    DnItem it;
+    it.i = w / RB;
+    it.r0 = (w % RB) * GM_ROWS;
+    const int tl = tiles[it.i], e = tl >> 16, tt = tl & 0xFFFF;
+    it.pos0 = off[e] + tt * GM_NT;
+    it.np = min(GM_NT, cnt[e] - tt * GM_NT);
+    it.N = (it.np + 15) & ~15;
+    const uint8_t *base = expert_ptr(src, 2, e);
+    it.dev = expert_on_device(src, e);
+    it.rows = base ? base + (size_t)it.r0 * rb : nullptr;
+    return it;
+}
+
+// The first DN_ITEMS items of a CTA are resolved once, at the start, by as
+// many threads; later ones (very large batches) by each role as it gets to
+// them.  Every role thus starts an item without a chain of dependent global
+// loads.
+#define DN_ITEMS 64
+
+// Persistent: CTA c takes work items c, c + gridDim.x, ... (item w = row
+// block w % (n_embd / 128) of tile w / (n_embd / 128)).  Every role walks
+// the same items; the barrier phases run on counters global over the items
+// (stage, item), so that the next item's rows arrive while this one is
+// dequantised, and its MMAs run while this one's accumulator is written out.
+// Warp roles:
+//   warps 0-15  dequantise, four threads per row, one quarter (32 of the
+//               stage's K = 128) each, into the A columns of the stage's
+//               parity in TMEM (a_full: one arrival per warp); the A
+//               columns come back through the MMAs' commit (mma_done), the
+//               item's rows through raw_free after its last stage;
+//   warp 16     lane 0 issues the item's row copy (2 buffers; for a miss
+//               only an arrival, the rows being read from host memory) and
+//               the token-tile copies (a ring of DN_NB, freed by b_free);
+//   warp 17     lane 0 issues the MMAs (M = 128, N = pairs rounded to 16, K
+//               = 16; eight per stage) into the item's accumulator (D
+//               double-buffered by item: d_full -> d_free);
+//   warps 18-21 epilogue: the accumulator's rows to ypair[pos][h], unweighted.
 __global__ void __launch_bounds__(DN_ALL_THREADS, 1) k_gemm_down(
     ExpertSrc src, const __half *__restrict__ at, const int32_t *__restrict__ off,
     const int32_t *__restrict__ cnt, const int32_t *__restrict__ tiles,
     const int32_t *__restrict__ n_tiles, int n_embd, int n_ff, float *__restrict__ ypair,
     int *err) {
     extern __shared__ __align__(1024) uint8_t sm[];
-    const int i = blockIdx.y;
-    if (i >= *n_tiles) return;
+    const int RB = n_embd / GM_ROWS;
+    const int n_items = *n_tiles * RB;
+    if ((int)blockIdx.x >= n_items) return;
     const size_t rb = (size_t)(n_ff / MOE_QK) * MOE_Q6K_BYTES;   // bytes per row
-    const int rows_bytes = (GM_ROWS * (int)rb + 127) & ~127;
-    uint8_t *sA = sm;                                   // [2] 32 KB
-    uint8_t *sB = sm + 2 * DN_A_BYTES;                  // [3] 16 KB
-    uint8_t *sR = sB + 3 * DN_B_BYTES;                  // the CTA's rows
-    uint64_t *mma_done = reinterpret_cast<uint64_t *>(sR + rows_bytes);       // [2]
-    uint64_t *b_full = mma_done + 2;                                           // [3]
-    uint64_t *r_full = b_full + 3;                                             // [1]
-    uint64_t *a_full = r_full + 1;                                             // [2]
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(a_full + 2);
+    const int rows_bytes = dn_rows_bytes(n_ff);
+    uint8_t *sR = sm;                                    // [2] the items' rows
+    uint8_t *sB = sm + 2 * rows_bytes;                   // [DN_NB]
+    uint64_t *raw_full = reinterpret_cast<uint64_t *>(sB + DN_NB * DN_B_BYTES);   // [2]
+    uint64_t *raw_free = raw_full + 2;    // [2]
+    uint64_t *a_full = raw_free + 2;      // [2]
+    uint64_t *mma_done = a_full + 2;      // [2]
+    uint64_t *b_full = mma_done + 2;      // [DN_NB]
+    uint64_t *b_free = b_full + DN_NB;    // [DN_NB]
+    uint64_t *d_full = b_free + DN_NB;    // [2]
+    uint64_t *d_free = d_full + 2;        // [2]
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(d_free + 2);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int tl = tiles[i], e = tl >> 16, tt = tl & 0xFFFF;
-    const int pos0 = off[e] + tt * GM_NT;
-    const int np = min(GM_NT, cnt[e] - tt * GM_NT);
-    const int N = (np + 15) & ~15;
-    const int r0 = blockIdx.x * GM_ROWS;
     const int S = n_ff / GM_KS_DN;
-    const uint8_t *dbase = expert_ptr(src, 2, e);
-    if (!dbase) {
-        if (tid == 0) atomicOr(err, MOE_DEV_ERR_INDEX);
-        return;
-    }
     if (tid == 0) {
-        for (int q = 0; q < 2; ++q) mbar_init(&mma_done[q], 1);
-        for (int q = 0; q < 3; ++q) mbar_init(&b_full[q], 1);
-        mbar_init(r_full, 1);
-        for (int q = 0; q < 2; ++q) mbar_init(&a_full[q], DN_THREADS / 32);
+        for (int q = 0; q < 2; ++q) {
+            mbar_init(&raw_full[q], 1);
+            mbar_init(&raw_free[q], DN_THREADS / 32);
+            mbar_init(&a_full[q], DN_THREADS / 32);
+            mbar_init(&mma_done[q], 1);
+            mbar_init(&d_full[q], 1);
+            mbar_init(&d_free[q], DN_EPI);
+        }
+        for (int q = 0; q < DN_NB; ++q) {
+            mbar_init(&b_full[q], 1);
+            mbar_init(&b_free[q], 1);
+        }
         fence_mbar_init();
     }
-    if (warp == 0) tmem_alloc(tslot, 64);
+    __shared__ DnItem s_items[DN_ITEMS];
+    const int G = gridDim.x;
+    if (tid < DN_ITEMS && (int)blockIdx.x + tid * G < n_items)
+        s_items[tid] = dn_item(src, off, tiles, cnt, blockIdx.x + tid * G, RB, rb);
+    if (warp == 0) tmem_alloc(tslot, 256);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tslot;
-    const __half *atile = at + (size_t)i * n_ff * GM_NT;
-    // the CTA's 128 rows are contiguous: one bulk copy from device memory;
-    // an expert in host memory (a miss) is copied by the threads
-    const uint8_t *rows_g = dbase + (size_t)r0 * rb;
-    const bool dev = expert_on_device(src, e);
-    if (dev) {
-        if (tid == 0) {
-            fence_proxy_async();
-            mbar_arrive_expect_tx(r_full, (uint32_t)(GM_ROWS * rb));
-            bulk_g2s(sR, rows_g, (uint32_t)(GM_ROWS * rb), r_full);
-        }
-    } else {
-        for (int o = tid * 16; o < GM_ROWS * (int)rb; o += DN_ALL_THREADS * 16)
-            *reinterpret_cast<uint4 *>(sR + o) = *reinterpret_cast<const uint4 *>(rows_g + o);
-        __syncthreads();
-    }
-    // the CTA that will most likely take this SM next (one CTA per SM, launch
-    // order x fastest): its rows into L2 now, so that its copy lands sooner
-    if (tid == 32) {
-        int nx, ny;
-        next_wave_cta(1, nx, ny);
-        if (ny < *n_tiles) {
-            const int en = tiles[ny] >> 16;
-            const uint8_t *dn = expert_on_device(src, en) ? expert_ptr(src, 2, en) : nullptr;
-            if (dn) prefetch_l2(dn + (size_t)nx * GM_ROWS * rb, (uint32_t)(GM_ROWS * rb));
-        }
-    }
     bool ok = true;
-    if (warp == DN_THREADS / 32) {
-        // ---- copy + MMA warp ----
+    const int W_COPY = DN_THREADS / 32, W_MMA = W_COPY + 1, W_EPI = W_MMA + 1;
+    // item k of this CTA (w = blockIdx.x + k G)
+    auto item = [&](int k) {
+        return k < DN_ITEMS ? s_items[k] : dn_item(src, off, tiles, cnt, blockIdx.x + k * G, RB, rb);
+    };
+    if (warp == W_COPY) {
+        // ---- copy warp: the items' rows and the token-tile ring ----
         if (lane == 0) {
-            const uint32_t idesc = idesc_f16(GM_ROWS, N);
-            mbar_arrive_expect_tx(&b_full[0], DN_B_BYTES);
-            bulk_g2s(sB, atile, DN_B_BYTES, &b_full[0]);
-            for (int s = 0; s < S; ++s) {
-                const int b = s & 1;
-                if (s + 1 < S) {
-                    // B buffer (s+1) % 3 was last read by the MMAs of stage s-2
-                    if (s >= 2 && !mbar_wait(&mma_done[b], ((s - 2) >> 1) & 1)) ok = false;
-                    const int nb = (s + 1) % 3;
-                    mbar_arrive_expect_tx(&b_full[nb], DN_B_BYTES);
-                    bulk_g2s(sB + nb * DN_B_BYTES, atile + (size_t)(s + 1) * GM_NT * GM_KS_DN, DN_B_BYTES,
-                             &b_full[nb]);
-                }
-                const bool ready = mbar_wait(&a_full[b], (s >> 1) & 1) && mbar_wait(&b_full[s % 3], (s / 3) & 1);
-                tc_fence_after();
-                if (ready) {
-                    const uint32_t aA = smem_u32(sA + b * DN_A_BYTES);
-                    const uint32_t bB = smem_u32(sB + (s % 3) * DN_B_BYTES);
-#pragma unroll
-                    for (int j = 0; j < GM_KS_DN / 16; ++j)
-                        tc_mma(tmem, smem_desc(aA + j * 2 * (GM_ROWS * 16), GM_ROWS * 16, 128),
-                               smem_desc(bB + j * 2 * (GM_NT * 16), GM_NT * 16, 128), idesc,
-                               (s | j) != 0);
+            int gi = 0, gs = 0;
+            for (int k = 0; (int)blockIdx.x + k * G < n_items; ++k) {
+                const DnItem it = item(k);
+                if (!it.rows) continue;
+                const int bf = gi & 1;
+                // rows buffer gi & 1, last read by item gi - 2
+                if (gi >= 2 && !mbar_wait(&raw_free[bf], ((gi - 2) >> 1) & 1)) ok = false;
+                if (it.dev) {
+                    mbar_arrive_expect_tx(&raw_full[bf], (uint32_t)(GM_ROWS * rb));
+                    bulk_g2s(sR + bf * rows_bytes, it.rows, (uint32_t)(GM_ROWS * rb), &raw_full[bf]);
                 } else {
-                    ok = false;
+                    mbar_arrive(&raw_full[bf]);
                 }
-                tc_commit(&mma_done[b]);
+                ++gi;
+                const __half *atile = at + (size_t)it.i * n_ff * GM_NT;
+                for (int s = 0; s < S; ++s, ++gs) {
+                    const int nb = gs % DN_NB;
+                    // ring slot gs % DN_NB, last read by the MMAs of stage gs - DN_NB
+                    if (gs >= DN_NB && !mbar_wait(&b_free[nb], ((gs / DN_NB) - 1) & 1)) ok = false;
+                    mbar_arrive_expect_tx(&b_full[nb], DN_B_BYTES);
+                    bulk_g2s(sB + nb * DN_B_BYTES, atile + (size_t)s * GM_NT * GM_KS_DN, DN_B_BYTES, &b_full[nb]);
+                }
             }
         }
         __syncwarp();
-    } else {
+    } else if (warp == W_MMA) {
+        // ---- MMA warp ----
+        if (lane == 0) {
+            int gi = 0, gs = 0;
+            for (int k = 0; (int)blockIdx.x + k * G < n_items; ++k) {
+                const DnItem it = item(k);
+                if (!it.rows) continue;
+                const uint32_t idesc = idesc_f16(GM_ROWS, it.N);
+                const int db = gi & 1;
+                // D[db] was last used by item gi - 2: wait for its epilogue
+                if (gi >= 2 && !mbar_wait(&d_free[db], ((gi - 2) >> 1) & 1)) ok = false;
+                const uint32_t dD = tmem + (uint32_t)(db * 64);
+                for (int s = 0; s < S; ++s, ++gs) {
+                    const bool ready = mbar_wait(&a_full[gs & 1], (gs >> 1) & 1) &&
+                                       mbar_wait(&b_full[gs % DN_NB], (gs / DN_NB) & 1);
+                    tc_fence_after();
+                    if (ready) {
+                        const uint32_t aA = tmem + 128 + (uint32_t)((gs & 1) * 64);
+                        const uint32_t bB = smem_u32(sB + (gs % DN_NB) * DN_B_BYTES);
+#pragma unroll
+                        for (int j = 0; j < GM_KS_DN / 16; ++j)
+                            tc_mma_ts(dD, aA + 8 * j, smem_desc(bB + j * 2 * (GM_NT * 16), GM_NT * 16, 128), idesc,
+                                      (s | j) != 0);
+                    } else {
+                        ok = false;
+                    }
+                    tc_commit(&mma_done[gs & 1]);
+                    tc_commit(&b_free[gs % DN_NB]);
+                }
+                tc_commit(&d_full[db]);
+                ++gi;
+            }
+        }
+        __syncwarp();
+    } else if (warp < W_COPY) {
         // ---- dequantising warps ----
         const int qtr = tid >> 7, m = tid & 127;
-        const uint8_t *row = sR + (size_t)m * rb;
-        if (dev && !mbar_wait(r_full, 0)) ok = false;
-        for (int s = 0; s < S; ++s) {
-            const uint8_t *blk = row + (s >> 1) * MOE_Q6K_BYTES;
-            const int h = s & 1;
-            uint32_t src[8], qh[8], sc[2];
-            ldw_a2<8>(blk + 64 * h + 32 * (qtr & 1), src);
-            ldw_a2<8>(blk + 128 + 32 * h, qh);
-            ldw_a2<2>(blk + 192 + 8 * h, sc);
-            const float d = h2f(*reinterpret_cast<const uint16_t *>(blk + 208));
-            const int b = s & 1;
-            if (s >= 2 && !mbar_wait(&mma_done[b], ((s - 2) >> 1) & 1)) ok = false;
-            deq_q6k_quarter(src, qh, sc, d, qtr, sA + b * DN_A_BYTES, m);
-            fence_proxy_async();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&a_full[b]);
-        }
-    }
-    if (!mbar_wait(&mma_done[(S - 1) & 1], ((S - 1) >> 1) & 1)) ok = false;
-    tc_fence_after();
-    if (warp < 4) {
-        const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16);
-        const int hrow = r0 + warp * 32 + lane;
-        for (int c0 = 0; c0 < N; c0 += 16) {
-            float v[16];
-            tmem_ld16(ta + c0, v);
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int n = c0 + j;
-                if (n < np) ypair[(size_t)(pos0 + n) * n_embd + hrow] = v[j];
+        int gi = 0, gs = 0;
+        for (int k = 0; (int)blockIdx.x + k * G < n_items; ++k) {
+            const DnItem it = item(k);
+            if (!it.rows) {
+                if (tid == 0) atomicOr(err, MOE_DEV_ERR_INDEX);
+                continue;
             }
+            const int bf = gi & 1;
+            if (!mbar_wait(&raw_full[bf], (gi >> 1) & 1)) ok = false;
+            // the item's row m: its copy in shared memory, or host memory for a miss
+            const uint8_t *row = it.dev ? sR + bf * rows_bytes + (size_t)m * rb : it.rows + (size_t)m * rb;
+            for (int s = 0; s < S; ++s, ++gs) {
+                const uint8_t *blk = row + (s >> 1) * MOE_Q6K_BYTES;
+                const int h = s & 1;
+                uint32_t src8[8], qh[8], sc[2];
+                ldw_a2<8>(blk + 64 * h + 32 * (qtr & 1), src8);
+                ldw_a2<8>(blk + 128 + 32 * h, qh);
+                ldw_a2<2>(blk + 192 + 8 * h, sc);
+                const float d = h2f(*reinterpret_cast<const uint16_t *>(blk + 208));
+                uint32_t o[16];
+                deq_q6k_quarter(src8, qh, sc, d, qtr, o);
+                // A columns of stage parity gs & 1, last read by the MMAs of stage gs - 2
+                if (gs >= 2 && !mbar_wait(&mma_done[gs & 1], ((gs - 2) >> 1) & 1)) ok = false;
+                tc_fence_after();
+                tmem_st16(tmem + ((uint32_t)((warp & 3) * 32) << 16) + 128 + (uint32_t)((gs & 1) * 64 + 16 * qtr), o);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&a_full[gs & 1]);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&raw_free[bf]);
+            ++gi;
+        }
+    } else {
+        // ---- epilogue warps ----
+        const int quad = warp & 3;
+        const uint32_t lanes = (uint32_t)(quad * 32) << 16;
+        int gi = 0;
+        for (int k = 0; (int)blockIdx.x + k * G < n_items; ++k) {
+            const DnItem it = item(k);
+            if (!it.rows) continue;
+            const int db = gi & 1;
+            if (!mbar_wait(&d_full[db], (gi >> 1) & 1)) ok = false;
+            tc_fence_after();
+            const int hrow = it.r0 + quad * 32 + lane;
+            for (int c0 = 0; c0 < it.N; c0 += 16) {
+                float v[16];
+                tmem_ld16(tmem + lanes + (uint32_t)(db * 64 + c0), v);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int n = c0 + j;
+                    if (n < it.np) ypair[(size_t)(it.pos0 + n) * n_embd + hrow] = v[j];
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&d_free[db]);
+            ++gi;
         }
     }
     if (!ok) atomicOr(err, MOE_DEV_ERR_TIMEOUT);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 0) tmem_dealloc(tmem, 64);
+    if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
 size_t gemm_scratch_halves(int n_expert, int P, int n_embd, int n_ff) {
@@ -927,8 +1025,14 @@ cudaError_t launch_experts_gemm(const ExpertSrc &src, const float *x, const Grou
             src, maps, xt, xm, g.off, g.cnt, g.tiles, g.n_tiles, n_embd, n_ff, at, err);
     }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    k_gemm_down<<<dim3(n_embd / GM_ROWS, maxt), DN_ALL_THREADS, dn_smem(n_ff), s>>>(
-        src, at, g.off, g.cnt, g.tiles, g.n_tiles, n_embd, n_ff, ypair, err);
+    {   // persistent as well
+        int dev = 0, sms = 0;
+        if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+        if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+        const int items = maxt * (n_embd / GM_ROWS);
+        k_gemm_down<<<dim3(std::max(1, std::min(sms, items))), DN_ALL_THREADS, dn_smem(n_ff), s>>>(
+            src, at, g.off, g.cnt, g.tiles, g.n_tiles, n_embd, n_ff, ypair, err);
+    }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     return launch_combine(ypair, g.pair_pos, w, n_tok, k, n_embd, resid, y, s);
 }
