@@ -386,9 +386,14 @@ static_assert((4 + 4 + 4 + 4 + 2 * GU_NB + 2 + 2) * 8 + 4 <= 512, "gate/up barri
 // of one expert tile.
 struct GuItem {
     int i, e, np, N, r0, yrow;
-    bool dev, shared_e;
+    bool dev, shared_e, ok;
     const uint8_t *gbase, *ubase;
 };
+
+// The first GU_ITEMS items of a CTA are resolved once, at the start (as in
+// the down kernel), so that no role starts an item with a chain of
+// dependent global loads.
+#define GU_ITEMS 32
 
 __device__ __forceinline__ bool gu_item(const ExpertSrc &src, const int32_t *tiles, const int32_t *cnt, int w,
                                         int RB, int n_ff, GuItem &it) {
@@ -403,7 +408,8 @@ __device__ __forceinline__ bool gu_item(const ExpertSrc &src, const int32_t *til
     it.shared_e = it.e == src.n_expert;
     it.dev = expert_on_device(src, it.e);
     it.yrow = (it.shared_e ? 0 : (it.dev ? src.table[it.e] : 0) * n_ff) + it.r0;
-    return it.gbase && it.ubase;
+    it.ok = it.gbase && it.ubase;
+    return it.ok;
 }
 
 // Persistent: CTA c takes work items c, c + gridDim.x, ... (item w = row
@@ -471,6 +477,10 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gemm_gate_up(
         }
         fence_mbar_init();
     }
+    __shared__ GuItem s_items[GU_ITEMS];
+    const int G = gridDim.x;
+    if (tid < GU_ITEMS && (int)blockIdx.x + tid * G < n_items)
+        gu_item(src, tiles, cnt, blockIdx.x + tid * G, RB, n_ff, s_items[tid]);
     if (warp == 0) tmem_alloc(tslot, 512);
     tc_fence_before();
     __syncthreads();
@@ -478,13 +488,20 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gemm_gate_up(
     const uint32_t tmem = *tslot;
     bool ok = true;
     const int W_COPY = GU_DQ_THREADS / 32, W_MMA = W_COPY + 1, W_EPI = W_MMA + 2;
+    // item k of this CTA (w = blockIdx.x + k G)
+    auto item = [&](int k) {
+        GuItem it;
+        if (k < GU_ITEMS) it = s_items[k];
+        else gu_item(src, tiles, cnt, blockIdx.x + k * G, RB, n_ff, it);
+        return it;
+    };
     if (warp == W_COPY) {
         // ---- copy warp: raw super-blocks and the token-tile ring ----
         if (lane == 0) {
             int gs = 0, rseq = 0;
-            for (int w = blockIdx.x; w < n_items; w += gridDim.x) {
-                GuItem it;
-                if (!gu_item(src, tiles, cnt, w, RB, n_ff, it)) continue;
+            for (int k = 0; (int)blockIdx.x + k * G < n_items; ++k) {
+                const GuItem it = item(k);
+                if (!it.ok) continue;
                 const CUtensorMap *mg = it.shared_e ? &maps.sg : &maps.g;
                 const CUtensorMap *mu = it.shared_e ? &maps.su : &maps.u;
                 const __half *xtile = xt + (size_t)it.i * n_embd * GM_NT;
@@ -524,9 +541,9 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gemm_gate_up(
         const int mat = warp - W_MMA;
         if (lane == 0) {
             int gs = 0;
-            for (int w = blockIdx.x; w < n_items; w += gridDim.x) {
-                GuItem it;
-                if (!gu_item(src, tiles, cnt, w, RB, n_ff, it)) continue;
+            for (int k = 0; (int)blockIdx.x + k * G < n_items; ++k) {
+                const GuItem it = item(k);
+                if (!it.ok) continue;
                 const uint32_t idesc = idesc_f16(GM_ROWS, it.N);
                 for (int s = 0; s < S; ++s, ++gs) {
                     const int gsb = gs >> 1, g = s & 1, b = gsb & 1;
@@ -567,9 +584,9 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gemm_gate_up(
         // ---- dequantising warps ----
         const int mat = tid >> 7, m = tid & 127;
         int gs = 0, rseq = 0;
-        for (int w = blockIdx.x; w < n_items; w += gridDim.x) {
-            GuItem it;
-            if (!gu_item(src, tiles, cnt, w, RB, n_ff, it)) {
+        for (int k = 0; (int)blockIdx.x + k * G < n_items; ++k) {
+            const GuItem it = item(k);
+            if (!it.ok) {
                 if (tid == 0) atomicOr(err, MOE_DEV_ERR_INDEX);
                 continue;
             }
@@ -612,9 +629,9 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gemm_gate_up(
         const uint32_t lanes = (uint32_t)(quad * 32) << 16;
         float *xch = reinterpret_cast<float *>(sX);   // [64][128]
         int gsb = 0;
-        for (int w = blockIdx.x; w < n_items; w += gridDim.x) {
-            GuItem it;
-            if (!gu_item(src, tiles, cnt, w, RB, n_ff, it)) continue;
+        for (int k = 0; (int)blockIdx.x + k * G < n_items; ++k) {
+            const GuItem it = item(k);
+            if (!it.ok) continue;
             float R[64];
 #pragma unroll
             for (int n = 0; n < 64; ++n) R[n] = 0.0f;
