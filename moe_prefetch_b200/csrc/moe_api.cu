@@ -68,7 +68,6 @@ struct moe_ctx {
     // per-pair down rows [P][n_embd]
     int32_t *s_group = nullptr;
     GroupBufs grp{};
-    int32_t *s_dest = nullptr;         // expert parallelism: destination rank per pair
     float *s_ypair = nullptr;
     // expert parallelism over peer memory: this rank's mailbox (exported with
     // CUDA IPC), the other ranks' mailboxes opened in this process, the
@@ -645,8 +644,8 @@ static int ensure_scratch(moe_ctx *c, int n_tok) {
     c->s_group = nullptr; c->s_ypair = nullptr;
     const int K = c->cfg.n_used, KX = K + c->cfg.n_shared, E = c->cfg.n_expert + c->cfg.n_shared;
     const size_t P = (size_t)n_tok * KX;   // pairs, the shared expert's included
-    // cnt [E] | off [E + 1] | pair_pos [P] | pos_pair [P] | tiles [E + P] | n_tiles [1] | dest [P]
-    const size_t gints = (size_t)E + (E + 1) + P + P + (E + P) + 1 + P;
+    // cnt [E] | off [E + 1] | pair_pos [P] | pos_pair [P] | tiles [E + P] | n_tiles [1]
+    const size_t gints = (size_t)E + (E + 1) + P + P + (E + P) + 1;
     // s_ids / s_w: [n_tok][K] router outputs, then [n_tok][KX] with the shared pair
     if (cudaMalloc(&c->s_ids, sizeof(int32_t) * (size_t)n_tok * (K + KX)) != cudaSuccess ||
         cudaMalloc(&c->s_w, sizeof(float) * (size_t)n_tok * (K + KX)) != cudaSuccess ||
@@ -663,8 +662,7 @@ static int ensure_scratch(moe_ctx *c, int n_tok) {
     c->grp.pair_pos = g; g += P;
     c->grp.pos_pair = g; g += P;
     c->grp.tiles = g; g += E + P;
-    c->grp.n_tiles = g; g += 1;
-    c->s_dest = g;
+    c->grp.n_tiles = g;
     c->s_cap_tok = n_tok;
     return MOE_OK;
 }
@@ -1008,8 +1006,8 @@ extern "C" int moe_ep_route_pack(moe_ctx *c, int layer, const float *x, int n_to
     GroupBufs gg = c->grp;
     gg.cnt = send_count;
     gg.pair_pos = pos;
-    CK(launch_ep_pack(ids, x, n_tok, g.n_used, g.n_expert, g.n_embd, world, capacity, c->s_dest, gg,
-                      send_ids, send_x, c->err, s));
+    CK(launch_ep_pack(ids, x, n_tok, g.n_used, g.n_expert, g.n_embd, world, capacity, gg, send_ids, send_x,
+                      c->err, s));
     return MOE_OK;
 }
 

@@ -27,13 +27,14 @@ namespace moe {
 #define GROUP_THREADS 1024
 #define GROUP_MAX_BUCKETS 264   // 256 routed experts + the shared one, rounded up
 
-// One CTA.  Pair p = t * k + r (token t, rank r).  Positions are stable: the
-// pairs of an expert keep pair order.  Writes cnt[E], off[E + 1],
+// One CTA.  Pair p = t * k + r (token t, rank r) goes to bucket ids[p] / div
+// (div 1: its expert; E / world: the rank owning the expert).  Positions are
+// stable: the pairs of a bucket keep pair order.  Writes cnt[E], off[E + 1],
 // pair_pos[P] (-1 for an id out of range, flagged in *err, and for the
 // empty-slot id -1, skipped silently), pos_pair[P], and
-// tiles[0 .. n_tiles) = (expert << 16) | token-tile for tiles of `tile` pairs.
+// tiles[0 .. n_tiles) = (bucket << 16) | token-tile for tiles of `tile` pairs.
 __global__ void __launch_bounds__(GROUP_THREADS) k_group(const int32_t *__restrict__ ids, int P,
-                                                         int n_expert, int tile, int32_t *cnt,
+                                                         int n_expert, int div, int tile, int32_t *cnt,
                                                          int32_t *off, int32_t *pair_pos,
                                                          int32_t *pos_pair, int32_t *tiles,
                                                          int32_t *n_tiles, int *err) {
@@ -57,7 +58,7 @@ __global__ void __launch_bounds__(GROUP_THREADS) k_group(const int32_t *__restri
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const int e = ev[j];
-            if (e >= 0 && e < n_expert) atomicAdd(&s_cnt[e], 1);
+            if (e >= 0 && e < n_expert * div) atomicAdd(&s_cnt[div == 1 ? e : e / div], 1);
             else if (e >= 0 || e < -1) atomicOr(err, MOE_DEV_ERR_INDEX);   // -1: an empty slot, skipped
         }
     }
@@ -103,7 +104,7 @@ __global__ void __launch_bounds__(GROUP_THREADS) k_group(const int32_t *__restri
     for (int c0 = 0; c0 < P; c0 += GROUP_THREADS) {
         const int p = c0 + tid;
         int e = p < P ? ids[p] : -1;
-        if (e >= n_expert) e = -1;
+        e = e < 0 || e >= n_expert * div ? -1 : div == 1 ? e : e / div;
         const unsigned mask = __match_any_sync(MOE_FULL, e);
         if (e >= 0 && lane == __ffs(mask) - 1) s_wc[warp][e] = __popc(mask);
         __syncthreads();
@@ -351,7 +352,8 @@ __global__ void __launch_bounds__(256, 2) k_gate_up_grouped(
     }
 }
 
-// Down rows for the pairs of one tile, unweighted: ypair[pos][h].  grid
+// Down rows for the pairs of one tile, unweighted: ypair[pos][h], or with
+// ydirect (one pair per row, nothing to combine) ydirect[pos_pair[pos]][h].  grid
 // (n_embd / 64, max tiles); block 256.  The CTA stages its 64 rows and the
 // tile's Q8_1 activations in shared memory; warp w takes rows 8w .. 8w + 7.
 // Each lane decodes its half block (Q6_K; 8-lane row groups) or unit (Q4_K)
@@ -361,9 +363,11 @@ __global__ void __launch_bounds__(256, 2) k_down_grouped(
     ExpertSrc src, const int8_t *__restrict__ aq, const float *__restrict__ ad,
     const float *__restrict__ as, const int32_t *__restrict__ off, const int32_t *__restrict__ cnt,
     const int32_t *__restrict__ tiles, const int32_t *__restrict__ n_tiles, int n_embd, int n_ff,
-    int down_type, int dn_rows, float *__restrict__ ypair, int *err) {
+    int down_type, int dn_rows, float *__restrict__ ypair, const int32_t *__restrict__ pos_pair,
+    float *__restrict__ ydirect, int *err) {
     extern __shared__ __align__(128) uint8_t smg[];
     __shared__ int s_pos[GROUP_TILE];
+    __shared__ int s_row[GROUP_TILE];   // output row: the position in ypair, or the pair in ydirect
     __shared__ __align__(8) uint64_t bar;
     if ((int)blockIdx.y >= *n_tiles) return;
     const int tl = tiles[blockIdx.y], e = tl >> 16, tt = tl & 0xFFFF;
@@ -374,7 +378,11 @@ __global__ void __launch_bounds__(256, 2) k_down_grouped(
         if (threadIdx.x == 0) atomicOr(err, MOE_DEV_ERR_INDEX);
         return;
     }
-    if (threadIdx.x < np) s_pos[threadIdx.x] = pos0 + threadIdx.x;
+    if (threadIdx.x < np) {
+        s_pos[threadIdx.x] = pos0 + threadIdx.x;
+        s_row[threadIdx.x] = ydirect ? pos_pair[pos0 + threadIdx.x] : pos0 + threadIdx.x;
+    }
+    float *const out = ydirect ? ydirect : ypair;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int nb = n_ff / MOE_QK, ablk = n_ff / 32;
     const bool q6 = down_type == MOE_QT_Q6K;
@@ -430,7 +438,7 @@ __global__ void __launch_bounds__(256, 2) k_down_grouped(
                     v = q6k_dec_compute(w, a);
                 }
                 v = groupn_sum(v, u, gs);
-                if (live && u == 0) ypair[(size_t)s_pos[j] * n_embd + h0 + r] = v;
+                if (live && u == 0) out[(size_t)s_row[j] * n_embd + h0 + r] = v;
             }
         }
     } else {
@@ -453,7 +461,7 @@ __global__ void __launch_bounds__(256, 2) k_down_grouped(
                     v = q4k_dec_compute(w, a);
                 }
                 v = warp_sum(v);
-                if (lane == 0) ypair[(size_t)s_pos[j] * n_embd + h0 + r] = v;
+                if (lane == 0) out[(size_t)s_row[j] * n_embd + h0 + r] = v;
             }
         }
     }
@@ -507,9 +515,9 @@ cudaError_t launch_append_shared(const int32_t *ids, const float *w, int n_tok, 
 int group_max_tiles(int n_expert, int P, int tile) { return n_expert + (P + tile - 1) / tile; }
 
 cudaError_t launch_group(const int32_t *ids, int P, int n_expert, int tile, const GroupBufs &g,
-                         int *err, cudaStream_t s) {
-    if (n_expert > GROUP_MAX_BUCKETS || tile > 0xFFFF) return cudaErrorInvalidValue;
-    k_group<<<1, GROUP_THREADS, 0, s>>>(ids, P, n_expert, tile, g.cnt, g.off, g.pair_pos,
+                         int *err, cudaStream_t s, int div) {
+    if (n_expert > GROUP_MAX_BUCKETS || tile > 0xFFFF || div < 1) return cudaErrorInvalidValue;
+    k_group<<<1, GROUP_THREADS, 0, s>>>(ids, P, n_expert, div, tile, g.cnt, g.off, g.pair_pos,
                                         g.pos_pair, g.tiles, g.n_tiles, err);
     return cudaGetLastError();
 }
@@ -557,10 +565,14 @@ cudaError_t launch_experts_grouped(const ExpertSrc &src, const float *x, const G
     k_gate_up_grouped<<<dim3(n_ff / GU2_ROWS, maxt), 256, sm1, s>>>(
         src, xq, xd, xs, g.off, g.cnt, g.pos_pair, g.tiles, g.n_tiles, k, n_embd, n_ff, aq, ad, as, err);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    // one pair per row and no weights: the down rows go straight to y (a
+    // combine would only copy them; rows of empty slots are left as they are)
+    const bool direct = k == 1 && !w && !resid;
     k_down_grouped<<<dim3((n_embd + dn_rows - 1) / dn_rows, maxt), 256, sm2, s>>>(
-        src, aq, ad, as, g.off, g.cnt, g.tiles, g.n_tiles, n_embd, n_ff, down_type, dn_rows, ypair, err);
+        src, aq, ad, as, g.off, g.cnt, g.tiles, g.n_tiles, n_embd, n_ff, down_type, dn_rows, ypair, g.pos_pair,
+        direct ? y : nullptr, err);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    return launch_combine(ypair, g.pair_pos, w, n_tok, k, n_embd, resid, y, s);
+    return direct ? cudaSuccess : launch_combine(ypair, g.pair_pos, w, n_tok, k, n_embd, resid, y, s);
 }
 
 cudaError_t launch_combine(const float *ypair, const int32_t *pair_pos, const float *w, int n_tok,

@@ -21,9 +21,11 @@
 //                   - epilogue warps scale each super-block's accumulator by
 //                     its d while the next fills, and form SiLU(g) * u as
 //                     fp16, directly in the down GEMM's operand layout;
-//   k_gemm_down     CTA = (128 rows of down, one token tile): Q6_K rows
-//                   dequantised to fp16 in shared memory, activations by bulk
-//                   copy, tcgen05.mma, unweighted rows to ypair[pos][h];
+//   k_gemm_down     persistent, one CTA per SM over (128 rows of down, one
+//                   token tile) items: Q6_K rows by bulk copy, dequantised to
+//                   fp16 into TMEM as the MMA's A operand, activations by
+//                   bulk copy, tcgen05.mma, unweighted rows to ypair[pos][h]
+//                   (or, one pair per row, straight to the output row);
 //   k_combine       the weighted sum over ranks, in rank order.
 //
 // Numerics: activations are rounded to fp16 once, and products accumulate in
@@ -781,7 +783,7 @@ __global__ void __launch_bounds__(DN_ALL_THREADS, 1) k_gemm_down(
     ExpertSrc src, const __half *__restrict__ at, const int32_t *__restrict__ off,
     const int32_t *__restrict__ cnt, const int32_t *__restrict__ tiles,
     const int32_t *__restrict__ n_tiles, int n_embd, int n_ff, float *__restrict__ ypair,
-    int *err) {
+    const int32_t *__restrict__ pos_pair, float *__restrict__ ydirect, int *err) {
     extern __shared__ __align__(1024) uint8_t sm[];
     const int RB = n_embd / GM_ROWS;
     const int n_items = *n_tiles * RB;
@@ -826,7 +828,7 @@ __global__ void __launch_bounds__(DN_ALL_THREADS, 1) k_gemm_down(
     tc_fence_after();
     const uint32_t tmem = *tslot;
     bool ok = true;
-    const int W_COPY = DN_THREADS / 32, W_MMA = W_COPY + 1, W_EPI = W_MMA + 1;
+    const int W_COPY = DN_THREADS / 32, W_MMA = W_COPY + 1;   // then the epilogue warps
     // item k of this CTA (w = blockIdx.x + k G)
     auto item = [&](int k) {
         return k < DN_ITEMS ? s_items[k] : dn_item(src, off, tiles, cnt, blockIdx.x + k * G, RB, rb);
@@ -947,7 +949,11 @@ __global__ void __launch_bounds__(DN_ALL_THREADS, 1) k_gemm_down(
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     const int n = c0 + j;
-                    if (n < it.np) ypair[(size_t)(it.pos0 + n) * n_embd + hrow] = v[j];
+                    if (n < it.np) {
+                        const int pos = it.pos0 + n;
+                        if (ydirect) ydirect[(size_t)pos_pair[pos] * n_embd + hrow] = v[j];
+                        else ypair[(size_t)pos * n_embd + hrow] = v[j];
+                    }
                 }
             }
             tc_fence_before();
@@ -1042,16 +1048,20 @@ cudaError_t launch_experts_gemm(const ExpertSrc &src, const float *x, const Grou
             src, maps, xt, xm, g.off, g.cnt, g.tiles, g.n_tiles, n_embd, n_ff, at, err);
     }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    // one pair per row and no weights: the down rows go straight to y (a
+    // combine would only copy them; rows of empty slots are left as they are)
+    const bool direct = k == 1 && !w && !resid;
     {   // persistent as well
         int dev = 0, sms = 0;
         if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
         if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
         const int items = maxt * (n_embd / GM_ROWS);
         k_gemm_down<<<dim3(std::max(1, std::min(sms, items))), DN_ALL_THREADS, dn_smem(n_ff), s>>>(
-            src, at, g.off, g.cnt, g.tiles, g.n_tiles, n_embd, n_ff, ypair, err);
+            src, at, g.off, g.cnt, g.tiles, g.n_tiles, n_embd, n_ff, ypair, g.pos_pair, direct ? y : nullptr,
+            err);
     }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    return launch_combine(ypair, g.pair_pos, w, n_tok, k, n_embd, resid, y, s);
+    return direct ? cudaSuccess : launch_combine(ypair, g.pair_pos, w, n_tok, k, n_embd, resid, y, s);
 }
 
 }  // namespace moe

@@ -92,7 +92,7 @@ int group_max_tiles(int n_expert, int P, int tile);
 cudaError_t launch_append_shared(const int32_t *ids, const float *w, int n_tok, int k, int n_expert,
                                  int32_t *ids_x, float *w_x, cudaStream_t s);
 cudaError_t launch_group(const int32_t *ids, int P, int n_expert, int tile, const GroupBufs &g,
-                         int *err, cudaStream_t s);
+                         int *err, cudaStream_t s, int div = 1);
 // bytes of scratch launch_experts_grouped needs for P pairs
 size_t grouped_scratch_bytes(int P, int n_embd, int n_ff);
 // gate/up + down over the grouped pairs (`scratch`: Q8_1 token rows and
@@ -106,14 +106,14 @@ cudaError_t launch_combine(const float *ypair, const int32_t *pair_pos, const fl
 
 // ---- expert-parallel dispatch (moe_ep.cu) ----------------------------------
 
-// Route pairs to ranks: dest [P] scratch; the grouping `g` over `world` rank
-// buckets (g.cnt = send counts, g.pair_pos = send slot of each pair, g.n_tiles
-// = slots filled); send_ids [P], send_x [P][n_embd] in send-slot order.
-// capacity > 0: rank d's pairs go to slots [d * capacity, d * capacity +
-// count), the other slots keep id -1, and g.pair_pos holds each pair's slot.
+// Route pairs to ranks: the grouping `g` over `world` rank buckets (g.cnt =
+// send counts, g.off[world] = pairs sent, g.pair_pos = send slot of each
+// pair); send_ids [P], send_x [P][n_embd] in send-slot order.  capacity > 0:
+// rank d's pairs go to slots [d * capacity, d * capacity + count), the other
+// slots keep id -1, and g.pair_pos holds each pair's slot.
 cudaError_t launch_ep_pack(const int32_t *ids, const float *x, int n_tok, int k, int n_expert,
-                           int n_embd, int world, int capacity, int32_t *dest, const GroupBufs &g,
-                           int32_t *send_ids, float *send_x, int *err, cudaStream_t s);
+                           int n_embd, int world, int capacity, const GroupBufs &g, int32_t *send_ids,
+                           float *send_x, int *err, cudaStream_t s);
 
 // The peer-memory exchange (moe_ep.cu): byte offsets of one rank's mailbox.
 struct EpMail {

@@ -44,6 +44,7 @@ def _check(oracle_lib, layer, X, path="gemm"):
     assert np.array_equal(w.view(np.uint32), rw.view(np.uint32))
     ry = oracle_lib.moe_experts(X, ids, w, gate, up, down, Q6K, I, path="f32")
     assert np.isfinite(y).all()
+    print(f"n_tok {X.shape[0]}: rel L2 {rel_l2(y, ry):.3e}, max abs {np.abs(y - ry).max():.3e}")
     assert rel_l2(y, ry) <= REL_L2_TOL, rel_l2(y, ry)
     assert np.abs(y - ry).max() <= MAX_ABS_TOL, np.abs(y - ry).max()
     return y, ry
