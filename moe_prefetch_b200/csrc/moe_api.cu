@@ -77,7 +77,7 @@ struct moe_ctx {
     std::vector<uint8_t *> ep_open;    // opened peer mailboxes (closed at destroy)
     uint8_t **ep_peer = nullptr;       // device [world]
     float *ep_y = nullptr;             // [world * cap][n_embd]
-    unsigned long long *ep_epoch = nullptr;
+    unsigned long long *ep_epoch = nullptr;   // [0] the exchange epoch, [1] the push kernel's CTA count
     bool ep_connected = false;
     // tensor-core GEMM operand tiles (fp16)
     void *s_gemm = nullptr;
@@ -1011,8 +1011,10 @@ extern "C" int moe_ep_route_pack(moe_ctx *c, int layer, const float *x, int n_to
     return MOE_OK;
 }
 
-extern "C" int moe_experts_rows(moe_ctx *c, int layer, const float *x_rows, const int32_t *ids,
-                                int n_rows, float *y_rows, int path, void *stream) {
+// moe_experts_rows, with the grouping kernel first waiting on `wait` (the
+// expert-parallel owner's rows arrive from peers).
+static int experts_rows(moe_ctx *c, int layer, const float *x_rows, const int32_t *ids, int n_rows,
+                        float *y_rows, int path, void *stream, const FlagWait *wait) {
     if (!c || n_rows < 0 || layer < 0 || layer >= c->cfg.n_layers || (n_rows && (!x_rows || !ids || !y_rows)))
         return fail(c, MOE_ERR_ARG, "moe_experts_rows: bad argument");
     if (n_rows == 0) return MOE_OK;
@@ -1031,16 +1033,21 @@ extern "C" int moe_experts_rows(moe_ctx *c, int layer, const float *x_rows, cons
     cudaStream_t s = (cudaStream_t)stream;
     const int buckets = g.n_expert + g.n_shared;   // id n_expert: the shared expert
     if (path == MOE_PATH_GEMV) {
-        CK(launch_group(ids, n_rows, buckets, GROUP_TILE, c->grp, c->err, s));
+        CK(launch_group(ids, n_rows, buckets, GROUP_TILE, c->grp, c->err, s, 1, wait));
         CK(launch_experts_grouped(make_src(c, layer), x_rows, c->grp, n_rows, 1, g.n_embd, g.n_ff,
                                   g.down_type, nullptr, c->s_act, c->s_ypair, nullptr, y_rows, c->err, s));
     } else {
         if ((r = ensure_gemm_scratch(c, n_tok_eq)) != MOE_OK) return r;
-        CK(launch_group(ids, n_rows, buckets, GM_NT, c->grp, c->err, s));
+        CK(launch_group(ids, n_rows, buckets, GM_NT, c->grp, c->err, s, 1, wait));
         CK(launch_experts_gemm(make_src(c, layer), x_rows, c->grp, n_rows, 1, g.n_embd, g.n_ff,
                                g.down_type, nullptr, c->s_gemm, c->s_ypair, nullptr, y_rows, c->err, s));
     }
     return MOE_OK;
+}
+
+extern "C" int moe_experts_rows(moe_ctx *c, int layer, const float *x_rows, const int32_t *ids,
+                                int n_rows, float *y_rows, int path, void *stream) {
+    return experts_rows(c, layer, x_rows, ids, n_rows, y_rows, path, stream, nullptr);
 }
 
 extern "C" int moe_ep_combine(moe_ctx *c, const float *y_rows, const int32_t *pos, const float *w,
@@ -1084,13 +1091,13 @@ extern "C" int moe_ep_mailbox_create(moe_ctx *c, int world, int rank, int max_ho
     if (cudaMalloc(&c->ep_mail, m.bytes) != cudaSuccess ||
         cudaMalloc(&c->ep_peer, sizeof(uint8_t *) * world) != cudaSuccess ||
         cudaMalloc(&c->ep_y, sizeof(float) * (size_t)world * m.cap * m.n_embd) != cudaSuccess ||
-        cudaMalloc(&c->ep_epoch, sizeof(unsigned long long)) != cudaSuccess) {
+        cudaMalloc(&c->ep_epoch, 2 * sizeof(unsigned long long)) != cudaSuccess) {
         cudaFree(c->ep_mail); cudaFree(c->ep_peer); cudaFree(c->ep_y); cudaFree(c->ep_epoch);
         c->ep_mail = nullptr; c->ep_peer = nullptr; c->ep_y = nullptr; c->ep_epoch = nullptr;
         return fail(c, MOE_ERR_OOM, "moe_ep_mailbox_create: %zu bytes of mailbox", m.bytes);
     }
     CK(cudaMemset(c->ep_mail, 0, m.bytes));
-    CK(cudaMemset(c->ep_epoch, 0, sizeof(unsigned long long)));
+    CK(cudaMemset(c->ep_epoch, 0, 2 * sizeof(unsigned long long)));
     cudaIpcMemHandle_t h;
     CK(cudaIpcGetMemHandle(&h, c->ep_mail));
     static_assert(sizeof(cudaIpcMemHandle_t) == MOE_EP_HANDLE_BYTES, "IPC handle size");
@@ -1146,7 +1153,8 @@ extern "C" int moe_ep_push(moe_ctx *c, int n_tok, const int32_t *send_count, con
     const int r = ep_call_mail(c, n_tok, "moe_ep_push", &m);
     if (r != MOE_OK) return r;
     CK(cudaSetDevice(c->cfg.device));
-    CK(launch_ep_push(m, c->ep_peer, send_count, send_ids, send_x, c->ep_epoch, (cudaStream_t)stream));
+    CK(launch_ep_push(m, c->ep_peer, send_count, send_ids, send_x, c->ep_epoch,
+                      reinterpret_cast<unsigned int *>(c->ep_epoch + 1), (cudaStream_t)stream));
     return MOE_OK;
 }
 
@@ -1159,13 +1167,15 @@ extern "C" int moe_ep_serve(moe_ctx *c, int layer, int n_tok, int path, void *st
     if (rc != MOE_OK) return rc;
     CK(cudaSetDevice(c->cfg.device));
     cudaStream_t s = (cudaStream_t)stream;
-    CK(launch_ep_wait(reinterpret_cast<const unsigned long long *>(c->ep_mail + m.off_fflag), m.world,
-                      c->ep_epoch, c->dp.wait_ns, c->err, s));
-    const int r = moe_experts_rows(c, layer, reinterpret_cast<const float *>(c->ep_mail + m.off_x),
-                                   reinterpret_cast<const int32_t *>(c->ep_mail + m.off_ids), m.world * m.cap,
-                                   c->ep_y, path, stream);
+    // the grouping kernel waits until every source's rows are in
+    const FlagWait fw{reinterpret_cast<const unsigned long long *>(c->ep_mail + m.off_fflag), m.world, c->ep_epoch,
+                      c->dp.wait_ns};
+    const int r = experts_rows(c, layer, reinterpret_cast<const float *>(c->ep_mail + m.off_x),
+                               reinterpret_cast<const int32_t *>(c->ep_mail + m.off_ids), m.world * m.cap, c->ep_y,
+                               path, stream, &fw);
     if (r != MOE_OK) return r;
-    CK(launch_ep_push(m, c->ep_peer, nullptr, nullptr, c->ep_y, c->ep_epoch, s));
+    CK(launch_ep_push(m, c->ep_peer, nullptr, nullptr, c->ep_y, c->ep_epoch,
+                      reinterpret_cast<unsigned int *>(c->ep_epoch + 1), s));
     return MOE_OK;
 }
 
@@ -1179,10 +1189,11 @@ extern "C" int moe_ep_collect(moe_ctx *c, const int32_t *pos, const float *w, in
     if (rc != MOE_OK) return rc;
     CK(cudaSetDevice(c->cfg.device));
     cudaStream_t s = (cudaStream_t)stream;
-    CK(launch_ep_wait(reinterpret_cast<const unsigned long long *>(c->ep_mail + m.off_rflag), m.world,
-                      c->ep_epoch, c->dp.wait_ns, c->err, s));
+    // every CTA of the combine waits until every owner's rows are back
+    const FlagWait fw{reinterpret_cast<const unsigned long long *>(c->ep_mail + m.off_rflag), m.world, c->ep_epoch,
+                      c->dp.wait_ns};
     CK(launch_combine(reinterpret_cast<const float *>(c->ep_mail + m.off_rety), pos, w, n_tok,
-                      c->cfg.n_used, c->cfg.n_embd, add_rows, out, s));
+                      c->cfg.n_used, c->cfg.n_embd, add_rows, out, s, &fw, c->err));
     return MOE_OK;
 }
 

@@ -27,7 +27,8 @@ namespace moe {
 #define GROUP_THREADS 1024
 #define GROUP_MAX_BUCKETS 264   // 256 routed experts + the shared one, rounded up
 
-// One CTA.  Pair p = t * k + r (token t, rank r) goes to bucket ids[p] / div
+// One CTA, after `wait` when it has flags (the ids may come from peers).
+// Pair p = t * k + r (token t, rank r) goes to bucket ids[p] / div
 // (div 1: its expert; E / world: the rank owning the expert).  Positions are
 // stable: the pairs of a bucket keep pair order.  Writes cnt[E], off[E + 1],
 // pair_pos[P] (-1 for an id out of range, flagged in *err, and for the
@@ -37,7 +38,8 @@ __global__ void __launch_bounds__(GROUP_THREADS) k_group(const int32_t *__restri
                                                          int n_expert, int div, int tile, int32_t *cnt,
                                                          int32_t *off, int32_t *pair_pos,
                                                          int32_t *pos_pair, int32_t *tiles,
-                                                         int32_t *n_tiles, int *err) {
+                                                         int32_t *n_tiles, int *err, FlagWait wait) {
+    if (wait.flags) cta_wait_flags(wait.flags, wait.world, wait.epoch, wait.wait_ns, err);
     __shared__ int s_cnt[GROUP_MAX_BUCKETS], s_off[GROUP_MAX_BUCKETS + 1], s_base[GROUP_MAX_BUCKETS];
     // per warp and bucket: the warp's count in the chunk (low 16 bits), after
     // the scan the exclusive prefix over the chunk's warps (high 16 bits)
@@ -469,13 +471,15 @@ __global__ void __launch_bounds__(256, 2) k_down_grouped(
 
 // y[t][h] = sum over ranks r in order of w[t][r] * ypair[pair_pos[t*k + r]][h]
 // (an fma chain from 0, then + resid): the per-pair kernel's combine.  With
-// w == null (k == 1) the row is copied unweighted.  grid (ceil(n_embd / 256),
-// n_tok); block 256.
+// w == null (k == 1) the row is copied unweighted.  Every CTA first does
+// `wait` when it has flags (the rows may come from peers).  grid
+// (ceil(n_embd / 256), n_tok); block 256.
 __global__ void __launch_bounds__(256) k_combine(const float *__restrict__ ypair,
                                                  const int32_t *__restrict__ pair_pos,
                                                  const float *__restrict__ w, int k, int n_embd,
                                                  const float *__restrict__ resid,
-                                                 float *__restrict__ y) {
+                                                 float *__restrict__ y, FlagWait wait, int *err) {
+    if (wait.flags) cta_wait_flags(wait.flags, wait.world, wait.epoch, wait.wait_ns, err);
     const int t = blockIdx.y, h = blockIdx.x * blockDim.x + threadIdx.x;
     if (h >= n_embd) return;
     if (!w) {   // unweighted (k == 1): the row itself, for an expert-parallel owner
@@ -515,10 +519,11 @@ cudaError_t launch_append_shared(const int32_t *ids, const float *w, int n_tok, 
 int group_max_tiles(int n_expert, int P, int tile) { return n_expert + (P + tile - 1) / tile; }
 
 cudaError_t launch_group(const int32_t *ids, int P, int n_expert, int tile, const GroupBufs &g,
-                         int *err, cudaStream_t s, int div) {
-    if (n_expert > GROUP_MAX_BUCKETS || tile > 0xFFFF || div < 1) return cudaErrorInvalidValue;
+                         int *err, cudaStream_t s, int div, const FlagWait *wait) {
+    if (n_expert > GROUP_MAX_BUCKETS || tile > 0xFFFF || div < 1 || (wait && wait->world > GROUP_THREADS))
+        return cudaErrorInvalidValue;
     k_group<<<1, GROUP_THREADS, 0, s>>>(ids, P, n_expert, div, tile, g.cnt, g.off, g.pair_pos,
-                                        g.pos_pair, g.tiles, g.n_tiles, err);
+                                        g.pos_pair, g.tiles, g.n_tiles, err, wait ? *wait : FlagWait{});
     return cudaGetLastError();
 }
 
@@ -576,9 +581,11 @@ cudaError_t launch_experts_grouped(const ExpertSrc &src, const float *x, const G
 }
 
 cudaError_t launch_combine(const float *ypair, const int32_t *pair_pos, const float *w, int n_tok,
-                           int k, int n_embd, const float *resid, float *y, cudaStream_t s) {
-    k_combine<<<dim3((n_embd + 255) / 256, n_tok), 256, 0, s>>>(ypair, pair_pos, w, k, n_embd,
-                                                                resid, y);
+                           int k, int n_embd, const float *resid, float *y, cudaStream_t s,
+                           const FlagWait *wait, int *err) {
+    if (wait && (wait->world > 256 || !err)) return cudaErrorInvalidValue;
+    k_combine<<<dim3((n_embd + 255) / 256, n_tok), 256, 0, s>>>(ypair, pair_pos, w, k, n_embd, resid, y,
+                                                                wait ? *wait : FlagWait{}, err);
     return cudaGetLastError();
 }
 

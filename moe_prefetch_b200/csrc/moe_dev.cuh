@@ -1133,6 +1133,33 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Thread s < world of the CTA waits until flags[s] carries at least *epoch
+// (acquire, system scope), bounded by wait_ns; then the whole CTA
+// synchronises.  On expiry the timeout bit goes into *err.  Every thread of
+// the CTA calls it.
+__device__ __forceinline__ void cta_wait_flags(const unsigned long long *flags, int world,
+                                               const unsigned long long *epoch, uint64_t wait_ns, int *err) {
+    const int s = threadIdx.x;
+    if (s < world) {
+        const unsigned long long e = *epoch;
+        unsigned long long v;
+        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flags + s) : "memory");
+        if (v < e) {
+            const uint64_t t0 = gtimer();
+            for (;;) {
+                asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(flags + s) : "memory");
+                if (v >= e) break;
+                if (gtimer() - t0 > wait_ns) {
+                    atomicOr(err, MOE_DEV_ERR_TIMEOUT);
+                    break;
+                }
+                __nanosleep(200);
+            }
+        }
+    }
+    __syncthreads();
+}
+
 // Bounded wait: false after limit_ns (MOE_TIMEOUT_NS unless given).
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
                                           uint64_t limit_ns = MOE_TIMEOUT_NS) {

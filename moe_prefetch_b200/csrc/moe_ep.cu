@@ -71,17 +71,19 @@ cudaError_t launch_ep_pack(const int32_t *ids, const float *x, int n_tok, int k,
 //
 //   source s (after route + pack, compact send order):
 //     k_ep_push_rows   block d of its send list -> rank d's mailbox:
-//                      ids[s][0 .. cap) (-1 past the count) and x[s][j]
-//     k_ep_signal      epoch += 1; on rank d: meta[s] = (count, offset),
-//                      then flag_fwd[s] = epoch (release, system scope)
+//                      ids[s][0 .. cap) (-1 past the count) and x[s][j];
+//                      its last CTA: epoch += 1; on rank d: meta[s] =
+//                      (count, offset), then flag_fwd[s] = epoch (release,
+//                      system scope)
 //   owner d:
-//     k_ep_wait        every flag_fwd[s] == epoch (bounded)
-//     expert rows      on its mailbox's world * cap slots (id -1: empty)
+//     expert rows      on its mailbox's world * cap slots (id -1: empty),
+//                      their grouping kernel first waiting (bounded) until
+//                      every flag_fwd[s] carries the epoch
 //     k_ep_push_rows   (return) y rows of source s -> rank s's ret_y at
-//                      offset + j
-//     k_ep_signal      on rank s: flag_ret[d] = epoch
+//                      offset + j; its last CTA: on rank s: flag_ret[d] = epoch
 //   home s:
-//     k_ep_wait        every flag_ret[d] == epoch, then the combine of ret_y
+//     the combine of ret_y, each CTA first waiting until every flag_ret[d]
+//     carries the epoch
 //
 // A source writes rank d's mailbox for the next layer only after its own
 // combine, which waited for every owner's return rows, which each owner
@@ -93,12 +95,6 @@ cudaError_t launch_ep_pack(const int32_t *ids, const float *x, int n_tok, int k,
 
 __device__ __forceinline__ void st_release_sys_u64(unsigned long long *p, unsigned long long v) {
     asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
-__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long *p) {
-    unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
 }
 
 // Send counts and offsets of blocks d (forward: the compact send list's
@@ -120,11 +116,20 @@ __device__ __forceinline__ void ep_block(const EpMail &m, int d, const int32_t *
 // grid (ceil(cap / EP_RPC), world); block 256.  Forward (send_count != null):
 // rows off + j of src -> rank d's x[me][j], and ids[me][j] (-1 past the
 // count).  Return (send_count null): rows (d * cap + j) of src -> rank d's
-// ret_y[off + j], (count, off) from this rank's meta[d].
+// ret_y[off + j], (count, off) from this rank's meta[d].  A thread loads all
+// of its float4s before it stores any (a load after a store would wait for
+// the store's round trip over NVLink).  Every CTA ends with a system-scope
+// fence and counts itself done; the last one raises the flags (ep_signal),
+// so that the flags follow every row.
+__device__ void ep_signal(const EpMail &m, uint8_t *const *peer, const int32_t *send_count,
+                          unsigned long long *epoch);
+
 __global__ void __launch_bounds__(256) k_ep_push_rows(EpMail m, uint8_t *const *peer,
                                                       const int32_t *__restrict__ send_count,
                                                       const int32_t *__restrict__ send_ids,
-                                                      const float *__restrict__ src) {
+                                                      const float *__restrict__ src, unsigned long long *epoch,
+                                                      unsigned int *done) {
+    __shared__ bool s_last;
     const int d = blockIdx.y;
     const int32_t *meta = reinterpret_cast<const int32_t *>(peer[m.rank] + m.off_meta);
     int cnt, off;
@@ -145,22 +150,49 @@ __global__ void __launch_bounds__(256) k_ep_push_rows(EpMail m, uint8_t *const *
         in = src + (size_t)d * m.cap * m.n_embd;
     }
     const int j1 = min(j0 + EP_RPC, cnt);
-    for (int i = threadIdx.x; i < (j1 - j0) * n4; i += blockDim.x) {
-        const int j = j0 + i / n4, c = i - (i / n4) * n4;
-        reinterpret_cast<float4 *>(out + (size_t)j * m.n_embd)[c] =
-            __ldcg(reinterpret_cast<const float4 *>(in + (size_t)j * m.n_embd) + c);
+    const int total = max(j1 - j0, 0) * n4;   // float4s of the CTA's rows
+    constexpr int PER = 8;                     // float4s in flight per thread
+    for (int i0 = threadIdx.x; i0 < total; i0 += PER * blockDim.x) {
+        float4 v[PER];
+#pragma unroll
+        for (int u = 0; u < PER; ++u) {
+            const int i = i0 + u * blockDim.x;
+            if (i < total) {
+                const int j = j0 + i / n4, c = i - (i / n4) * n4;
+                v[u] = __ldcg(reinterpret_cast<const float4 *>(in + (size_t)j * m.n_embd) + c);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < PER; ++u) {
+            const int i = i0 + u * blockDim.x;
+            if (i < total) {
+                const int j = j0 + i / n4, c = i - (i / n4) * n4;
+                reinterpret_cast<float4 *>(out + (size_t)j * m.n_embd)[c] = v[u];
+            }
+        }
     }
     __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned int n = gridDim.x * gridDim.y;
+        s_last = atomicAdd(done, 1u) == n - 1;
+        if (s_last) *done = 0;   // for the next launch (every CTA has counted)
+    }
+    __syncthreads();
+    if (s_last) {
+        __threadfence_system();   // every CTA's rows (their fences preceded their counts) before the flags
+        ep_signal(m, peer, send_count, epoch);
+    }
 }
 
-// One CTA, thread d < world.  Forward (send_count != null): thread 0 first
-// advances the epoch; then (count, offset) of block d into rank d's
-// meta[me] and the epoch into its flag_fwd[me].  Return: the epoch into rank
-// d's flag_ret[me].  The stores before a flag are the same thread's, and the
-// rows came from the previous kernel on this stream (each of its CTAs ended
-// with a system-scope fence).
-__global__ void k_ep_signal(EpMail m, uint8_t *const *peer, const int32_t *__restrict__ send_count,
-                            unsigned long long *epoch) {
+// The last CTA of k_ep_push_rows.  Forward (send_count != null): thread 0
+// first advances the epoch; then thread d < world writes (count, offset) of
+// block d into rank d's meta[me] and the epoch into its flag_fwd[me].
+// Return: the epoch into rank d's flag_ret[me].  The stores before a flag
+// are the same thread's, or the other CTAs' rows, whose system-scope fences
+// came before their counts.
+__device__ void ep_signal(const EpMail &m, uint8_t *const *peer, const int32_t *send_count,
+                          unsigned long long *epoch) {
     __shared__ unsigned long long s_e;
     if (threadIdx.x == 0) s_e = send_count ? ++*epoch : *epoch;
     __syncthreads();
@@ -179,39 +211,12 @@ __global__ void k_ep_signal(EpMail m, uint8_t *const *peer, const int32_t *__res
     }
 }
 
-// One CTA, thread s < world: wait until this rank's flag s carries the epoch
-// (bounded by wait_ns; on expiry the timeout bit goes into *err and the
-// kernel returns, so the context stays usable).
-__global__ void k_ep_wait(const unsigned long long *flags, int world, const unsigned long long *epoch,
-                          uint64_t wait_ns, int *err) {
-    const int s = threadIdx.x;
-    if (s >= world) return;
-    const unsigned long long e = *epoch;
-    if (ld_acquire_sys_u64(flags + s) >= e) return;
-    const uint64_t t0 = gtimer();
-    while (ld_acquire_sys_u64(flags + s) < e) {
-        if (gtimer() - t0 > wait_ns) {
-            atomicOr(err, MOE_DEV_ERR_TIMEOUT);
-            return;
-        }
-        __nanosleep(200);
-    }
-}
-
 cudaError_t launch_ep_push(const EpMail &m, uint8_t *const *peer, const int32_t *send_count,
                            const int32_t *send_ids, const float *src, unsigned long long *epoch,
-                           cudaStream_t s) {
-    k_ep_push_rows<<<dim3((m.cap + EP_RPC - 1) / EP_RPC, m.world), 256, 0, s>>>(m, peer, send_count,
-                                                                                 send_ids, src);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-    k_ep_signal<<<1, 256, 0, s>>>(m, peer, send_count, epoch);
-    return cudaGetLastError();
-}
-
-cudaError_t launch_ep_wait(const unsigned long long *flags, int world, const unsigned long long *epoch,
-                           uint64_t wait_ns, int *err, cudaStream_t s) {
-    k_ep_wait<<<1, 256, 0, s>>>(flags, world, epoch, wait_ns, err);
+                           unsigned int *done, cudaStream_t s) {
+    if (m.world > 256) return cudaErrorInvalidValue;   // one signalling thread per rank
+    k_ep_push_rows<<<dim3((m.cap + EP_RPC - 1) / EP_RPC, m.world), 256, 0, s>>>(m, peer, send_count, send_ids,
+                                                                                 src, epoch, done);
     return cudaGetLastError();
 }
 

@@ -87,12 +87,23 @@ struct GroupBufs {
     int32_t *cnt, *off, *pair_pos, *pos_pair, *tiles, *n_tiles;
 };
 
+// A wait that a kernel does before its work: until every flags[0 .. world)
+// carries *epoch (acquire, system scope), bounded by wait_ns (on expiry the
+// timeout bit goes into the kernel's error word and the kernel goes on).
+// The expert-parallel exchange raises such flags in peer memory.
+struct FlagWait {
+    const unsigned long long *flags;
+    int world;
+    const unsigned long long *epoch;
+    uint64_t wait_ns;
+};
+
 int group_max_tiles(int n_expert, int P, int tile);
 // the routed pairs of each token followed by the shared expert (id n_expert, weight 1)
 cudaError_t launch_append_shared(const int32_t *ids, const float *w, int n_tok, int k, int n_expert,
                                  int32_t *ids_x, float *w_x, cudaStream_t s);
 cudaError_t launch_group(const int32_t *ids, int P, int n_expert, int tile, const GroupBufs &g,
-                         int *err, cudaStream_t s, int div = 1);
+                         int *err, cudaStream_t s, int div = 1, const FlagWait *wait = nullptr);
 // bytes of scratch launch_experts_grouped needs for P pairs
 size_t grouped_scratch_bytes(int P, int n_embd, int n_ff);
 // gate/up + down over the grouped pairs (`scratch`: Q8_1 token rows and
@@ -102,7 +113,8 @@ cudaError_t launch_experts_grouped(const ExpertSrc &src, const float *x, const G
                                    const float *w, void *scratch, float *ypair, const float *resid,
                                    float *y, int *err, cudaStream_t s);
 cudaError_t launch_combine(const float *ypair, const int32_t *pair_pos, const float *w, int n_tok,
-                           int k, int n_embd, const float *resid, float *y, cudaStream_t s);
+                           int k, int n_embd, const float *resid, float *y, cudaStream_t s,
+                           const FlagWait *wait = nullptr, int *err = nullptr);
 
 // ---- expert-parallel dispatch (moe_ep.cu) ----------------------------------
 
@@ -123,13 +135,12 @@ struct EpMail {
 // forward (send_count != null): the compact send list's blocks to every
 // owner's mailbox, then meta + flags (advancing *epoch); return (send_count
 // null): the owner's y rows [world][cap][n_embd] to every source's ret_y,
-// then the return flags.  peer: device array of the world mailbox bases.
+// then the return flags.  peer: device array of the world mailbox bases;
+// done: a zeroed device counter the kernel's last CTA finds and resets.
 cudaError_t launch_ep_push(const EpMail &m, uint8_t *const *peer, const int32_t *send_count,
                            const int32_t *send_ids, const float *src, unsigned long long *epoch,
-                           cudaStream_t s);
-// wait (bounded) until flags[0 .. world) all carry *epoch
-cudaError_t launch_ep_wait(const unsigned long long *flags, int world, const unsigned long long *epoch,
-                           uint64_t wait_ns, int *err, cudaStream_t s);
+                           unsigned int *done, cudaStream_t s);
+
 
 // ---- tensor-core grouped GEMM (moe_gemm.cu) --------------------------------
 
