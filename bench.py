@@ -1017,25 +1017,30 @@ def run_phases(args):
         st.decode(h, out)
     st.sync()
     G = st.decode_info()["grid"]
-    prof = torch.zeros(T, L, PH, G, dtype=torch.int64, device="cuda")
-    dbg = MoeDecodeDbg(None, None, None, None, prof.data_ptr())
     s = C.c_void_p(torch.cuda.current_stream().cuda_stream)
-    rc = st.lib.moe_decode(st.ctx, C.c_void_p(h.data_ptr()), C.c_void_p(out.data_ptr()), T, C.byref(dbg), s)
-    st.sync()
-    if rc != 0:
-        print(f"moe_decode failed: {rc}", file=sys.stderr)
-        return 1
-    flat = prof.cpu().numpy().astype(np.int64).reshape(T * L, PH, G)[L:]
-    res = {}
-    for a, b, name in PHASES:
-        d = (flat[:, b, :] - flat[:, a, :]).astype(np.float64) / 1000.0
-        res[name] = {"median_us": round(float(np.median(d)), 3),
-                     "max_over_ctas_us": round(float(np.median(d.max(-1))), 3)}
-    lay = (flat[1:, 0, :] - flat[:-1, 0, :]).astype(np.float64) / 1000.0
-    print(json.dumps({"metric": "decode layer phases", "unit": "us", "layer_us": round(float(np.median(lay)), 3),
-                      "phases": res, "config": {"workload": f"{L} layers x {T} tokens, "
-                                                f"{'config-4' if args.c4 else 'config-1'} shapes",
-                                                "grid": G, "data": "synthetic"}}), flush=True)
+    # spec 0: gate/up copies issued from the logits' top-k before the exact
+    # selection (the default); 1: issued after it
+    for spec in (0, 1):
+        prof = torch.zeros(T, L, PH, G, dtype=torch.int64, device="cuda")
+        dbg = MoeDecodeDbg(None, None, None, None, prof.data_ptr(), 0, spec)
+        rc = st.lib.moe_decode(st.ctx, C.c_void_p(h.data_ptr()), C.c_void_p(out.data_ptr()), T, C.byref(dbg),
+                               s)
+        st.sync()
+        if rc != 0:
+            print(f"moe_decode failed: {rc}", file=sys.stderr)
+            return 1
+        flat = prof.cpu().numpy().astype(np.int64).reshape(T * L, PH, G)[L:]
+        res = {}
+        for a, b, name in PHASES:
+            d = (flat[:, b, :] - flat[:, a, :]).astype(np.float64) / 1000.0
+            res[name] = {"median_us": round(float(np.median(d)), 3),
+                         "max_over_ctas_us": round(float(np.median(d.max(-1))), 3)}
+        lay = (flat[1:, 0, :] - flat[:-1, 0, :]).astype(np.float64) / 1000.0
+        print(json.dumps({"metric": "decode layer phases", "unit": "us",
+                          "layer_us": round(float(np.median(lay)), 3), "phases": res,
+                          "config": {"workload": f"{L} layers x {T} tokens, "
+                                                 f"{'config-4' if args.c4 else 'config-1'} shapes",
+                                     "early_copies": spec == 0, "grid": G, "data": "synthetic"}}), flush=True)
     st.close()
     return 0
 

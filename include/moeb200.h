@@ -349,6 +349,13 @@ typedef struct moe_decode_dbg {
     int32_t   starve;   /* tests of the watchdog only: r + 1 makes rank r's first
                            activation wait target one signal more than its
                            producers give, so that it can only run out; 0 off */
+    int32_t   spec;     /* the early gate/up copies (cache prior off: copies
+                           requested for the top-k of the logits while the
+                           softmax and the exact top-k run, re-issued where a
+                           rank's id differs): 0 default (on), 1 off, 2 on with
+                           a wrong rank-0 prediction in every other (token,
+                           layer), for tests of the re-issue; results are the
+                           same bits in every mode */
 } moe_decode_dbg;
 
 /* Batch-1 decode of n_tok tokens, strictly one after another, through all

@@ -59,7 +59,7 @@ class MoeLayerInfo(C.Structure):
 
 class MoeDecodeDbg(C.Structure):
     _fields_ = [("x", C.c_void_p), ("ids", C.c_void_p), ("w", C.c_void_p), ("y", C.c_void_p),
-                ("prof", C.c_void_p), ("starve", C.c_int32)]
+                ("prof", C.c_void_p), ("starve", C.c_int32), ("spec", C.c_int32)]
 
 
 P = C.c_void_p

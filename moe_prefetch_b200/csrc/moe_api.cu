@@ -398,7 +398,7 @@ extern "C" int moe_create(const moe_cfg *cfg, moe_ctx **out) {
         p.acc = c->acc;
         p.abort_flag = c->abort_flag; p.err = c->err; p.st = c->st;
         p.observe = 1; p.delta = g.cache_prior; p.rms_eps = 1e-6f;
-        p.wait_ns = MOE_TIMEOUT_NS; p.starve = 0;
+        p.wait_ns = MOE_TIMEOUT_NS; p.starve = 0; p.spec = 1;
     }
     // uploader
     {
@@ -1300,6 +1300,9 @@ extern "C" int moe_decode(moe_ctx *c, const float *h, float *out, int n_tok,
     p.prof = dbg ? dbg->prof : nullptr;
     p.starve = dbg ? dbg->starve : 0;
     if (p.starve < 0 || p.starve > p.kx) return fail(c, MOE_ERR_ARG, "moe_decode: dbg starve out of range");
+    const int spec_mode = dbg ? dbg->spec : 0;
+    if (spec_mode < 0 || spec_mode > 2) return fail(c, MOE_ERR_ARG, "moe_decode: dbg spec out of range");
+    p.spec = spec_mode == 1 ? 0 : spec_mode == 2 ? 2 : 1;
     if (p.dbg_ids && !p.dbg_w) return fail(c, MOE_ERR_ARG, "moe_decode: dbg ids without w");
     CK(cudaMemsetAsync(c->bar, 0, 64, s));
     CK(cudaMemsetAsync(c->abort_flag, 0, 64, s));

@@ -48,7 +48,8 @@ namespace moe {
 #define MB_TBL 1
 #define MB_GU 2    // 4 barriers: gate/up pieces
 #define MB_DN 6    // MOE_KMAX barriers: down pieces
-#define N_MB (MB_DN + MOE_KMAX)
+#define MB_FX (MB_DN + MOE_KMAX)   // 4 barriers: gate/up pieces re-issued after a wrong prediction
+#define N_MB (MB_FX + 4)
 #define DEC_PHASES 12
 
 __device__ __forceinline__ void red_release_add(unsigned *p, unsigned v) {
@@ -207,6 +208,28 @@ __device__ __noinline__ void host_miss_copies(const uint8_t *hgate, const uint8_
     }
 }
 
+// One bulk copy (cp.async.bulk, TMA, no multicast) of gate/up piece q of
+// this CTA into the staging buffers, for `slot` of the piece's rank (ld.ns:
+// a miss, nothing copied here; -1: the shared expert's own buffer), completing
+// on `bar`.
+__device__ __forceinline__ void issue_gu_piece(const LayerDesc &ld, int slot, int q, const int *ch_i0,
+                                               const int *ch_n, const int *ch_off, int gurow,
+                                               int64_t gate_bytes, uint8_t *gate_sm, uint8_t *up_sm,
+                                               uint64_t *bar) {
+    const uint32_t bytes = (uint32_t)(ch_n[q] * gurow);
+    fence_proxy_async();
+    if (slot != ld.ns) {
+        const size_t off = (size_t)ch_i0[q] * gurow;
+        const uint8_t *gsrc = slot < 0 ? ld.sgate : ld.gate + (size_t)slot * gate_bytes;
+        const uint8_t *usrc = slot < 0 ? ld.sup : ld.up + (size_t)slot * gate_bytes;
+        mbar_arrive_expect_tx(bar, 2 * bytes);
+        bulk_g2s(gate_sm + (size_t)ch_off[q] * gurow, gsrc + off, bytes, bar);
+        bulk_g2s(up_sm + (size_t)ch_off[q] * gurow, usrc + off, bytes, bar);
+    } else {
+        mbar_arrive_expect_tx(bar, 0);
+    }
+}
+
 // This CTA's share of the next step's fused router: partial logits over its
 // residual rows (an FMA chain per expert, rows in order) and the partial sum of
 // squares, added in fixed point to the step's accumulators A[e * ACC_LINE]
@@ -280,6 +303,10 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
     __shared__ int s_bad;
     __shared__ int s_any_miss;
     __shared__ int s_fail;
+    __shared__ int s_fix;      // the gate/up pieces were requested again (wrong prediction)
+    __shared__ int s_sp;       // the predicted pieces were requested
+    __shared__ int s_go;       // ... and are all resident: the compute warps run ahead
+    __shared__ int s_rest;     // warp 0 requested the down rows (run-ahead path)
     __shared__ uint64_t s_clock;
 
     const int G = gridDim.x, c = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -319,6 +346,13 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
     int use = 0;                      // (token, layer) index; barrier parity = use & 1
     bool pend_wt = false, pend_tbl = false, pend_gu = false, pend_dn = false;
     uint32_t wt_par = 0, tbl_par = 0;
+    // Speculative copy issue (the cache prior off): warp 0 issues the gate/up
+    // copies for the top-k of the logits, then computes the exact selection
+    // while they land; a rank whose id differs makes it wait for those copies
+    // and issue the right ones on the MB_FX barriers (fixed), parity fx_par.
+    const bool spec = p.spec != 0 && !(p.delta > 0.0f);
+    bool fixed = false;
+    uint32_t fx_par = 0;
 
     // ---- prologue: router rows + table of layer 0, partials of (0, 0) --------
     if (tid == 0) {
@@ -356,7 +390,10 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
             // the other buffer: read during the previous step, next added to
             // after barrier B of this one.
             {
-                float *tot = reinterpret_cast<float *>(gu);   // [E] logit totals (before * inv)
+                // [E] logit totals (before * inv), in the down staging buffer: free
+                // until this layer's down copies, which are issued after the
+                // selection (the gate/up buffer may already be filling)
+                float *tot = reinterpret_cast<float *>(dn);
                 const long long *A = p.acc + (size_t)(use & 1) * (E + 1) * ACC_LINE;
                 const float *src = L == 0 ? p.h_in + (size_t)t * H : p.resid;
                 float4 xv = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
@@ -376,20 +413,29 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                 PROF(2)
                 const float S = s_sumsq;
                 const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(S, (float)H), p.rms_eps)));
+                bool tbl_ok = true;
                 if (pend_tbl) {
-                    if (!mbar_wait(&mb[MB_TBL], tbl_par, p.wait_ns)) {
-                        if (tid == 0) { atomicOr(p.err, MOE_DEV_ERR_TIMEOUT); s_bad = 1; }
-                    }
+                    tbl_ok = mbar_wait(&mb[MB_TBL], tbl_par, p.wait_ns);
+                    if (!tbl_ok && tid == 0) { atomicOr(p.err, MOE_DEV_ERR_TIMEOUT); s_bad = 1; }
                     pend_tbl = false;
                     tbl_par ^= 1;
                 }
-                // ---- 2. warp 0: logits, softmax, prior, top-k, weights and slots in
-                //         registers; warps 1..15: x = r * inv -> Q8_1 -----------------
-                if (warp == 0) {
+                const bool has_next = L + 1 < NL || t + 1 < p.n_tok;
+                const int nl = L + 1 < NL ? L + 1 : 0;
+
+                // warp 0: the exact selection (logits, softmax, prior, top-k, weights)
+                // into s_ids / s_w / s_slot; returns true when a predicted id
+                // (sp_id of rank `lane`, when sp_on) differs
+                auto select_exact = [&](int sp_id, bool sp_on) -> bool {
                     int id_r;
                     float w_r;
-                    select_warp<E / 32>(tot, inv, tbl, ld.ns, p.delta, p.delta > 0.0f, K, lane, id_r, w_r,
-                                        s_ids, s_w);
+                    // with a prediction (prior off), first the check that it is the
+                    // selection; the full top-k only where it is not
+                    const bool checked = sp_on && select_warp_check<E / 32>(tot, inv, K, lane, sp_id, id_r, w_r,
+                                                                            s_ids, s_w);
+                    if (!checked)
+                        select_warp<E / 32>(tot, inv, tbl, ld.ns, p.delta, p.delta > 0.0f, K, lane, id_r, w_r,
+                                            s_ids, s_w);
                     if (lane < K) {
                         const bool okid = id_r >= 0 && id_r < E;
                         s_ids[lane] = id_r;
@@ -406,55 +452,24 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                     const bool missed = lane < K && (id_r < 0 || id_r >= E || tbl[id_r] == ld.ns);
                     const unsigned miss = __ballot_sync(MOE_FULL, missed);
                     if (lane == 0) s_any_miss = miss != 0;
-                } else {
-                    q8_scale_quantize_cta(xf, inv, H / 32, xq, xd, xs, tid - 32, DEC_THREADS - 32);
-                }
-                __syncthreads();
-                PROF(6)
-                if (s_bad) {
-                    if (tid == 0) atomicExch(p.abort_flag, 1);
-                    goto abort;
-                }
-                if (p.dbg_x && c == 0)
-                    for (int i = tid; i < H; i += DEC_THREADS)
-                        p.dbg_x[((size_t)t * NL + L) * H + i] = xf[i];
-            }
-            if (c == 0 && warp == 1) {
-                if (p.observe) observe_decode(p.st, L, s_ids, s_slot, K, ld.ns, &s_clock, lane);
-                if (p.dbg_ids && lane < K) {
-                    p.dbg_ids[((size_t)t * NL + L) * K + lane] = s_ids[lane];
-                    p.dbg_w[((size_t)t * NL + L) * K + lane] = s_w[lane];
-                }
-            }
-
-            // ---- 3. warp 0 issues this layer's copies (+ next router rows / table);
-            //         the issue blocks at roughly the data rate, so the other warps
-            //         compute the gate/up rows meanwhile --------------------------------
-            {
-                const bool has_next = L + 1 < NL || t + 1 < p.n_tok;
-                const int nl = L + 1 < NL ? L + 1 : 0;
-                if (warp == 0) {
-                    if (lane < nch) {
-                        const int q = lane;
-                        const int slot = s_slot[ch_k[q]];
-                        const uint32_t bytes = (uint32_t)(ch_n[q] * gurow);
-                        fence_proxy_async();
-                        if (slot != ld.ns) {
-                            // slot -1: the shared expert's own buffer
-                            const size_t off = (size_t)ch_i0[q] * gurow;
-                            const uint8_t *gsrc = slot < 0 ? ld.sgate : ld.gate + (size_t)slot * p.gate_bytes;
-                            const uint8_t *usrc = slot < 0 ? ld.sup : ld.up + (size_t)slot * p.gate_bytes;
-                            mbar_arrive_expect_tx(&mb[MB_GU + q], 2 * bytes);
-                            bulk_g2s(gate_sm + (size_t)ch_off[q] * gurow, gsrc + off, bytes, &mb[MB_GU + q]);
-                            bulk_g2s(up_sm + (size_t)ch_off[q] * gurow, usrc + off, bytes, &mb[MB_GU + q]);
-                        } else {
-                            mbar_arrive_expect_tx(&mb[MB_GU + q], 0);
-                        }
-                    }
-                    // The down rows are read only after the second grid barrier: the
-                    // gate/up pieces get the copy engine and HBM to themselves first.
+                    const bool wrong = sp_on && __ballot_sync(MOE_FULL, lane < K && sp_id != id_r) != 0u;
                     __syncwarp();
-                    if (lane < nch) mbar_wait(&mb[MB_GU + lane], par, p.wait_ns);
+                    return wrong;
+                };
+                // one warp of CTA 0: moe_obs_cb for the routed ids, and the debug dumps
+                auto observe_ids = [&]() {
+                    if (p.observe) observe_decode(p.st, L, s_ids, s_slot, K, ld.ns, &s_clock, lane);
+                    if (p.dbg_ids && lane < K) {
+                        p.dbg_ids[((size_t)t * NL + L) * K + lane] = s_ids[lane];
+                        p.dbg_w[((size_t)t * NL + L) * K + lane] = s_w[lane];
+                    }
+                };
+                // warp 0: once the gate/up pieces (barriers gmb, parity gpar) have
+                // landed, which gives them the copy engine and HBM first, the down
+                // rows of every rank, the next router rows and the next table
+                auto issue_rest = [&](uint64_t *gmb, uint32_t gpar) {
+                    __syncwarp();
+                    if (lane < nch) mbar_wait(&gmb[lane], gpar, p.wait_ns);
                     __syncwarp();
                     if (lane >= 8 && lane < 8 + KX) {
                         const int kk = lane - 8;
@@ -483,61 +498,183 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                         mbar_arrive_expect_tx(&mb[MB_TBL], (uint32_t)(E * 4));
                         bulk_g2s(tbl, p.layers[nl].table, (uint32_t)(E * 4), &mb[MB_TBL]);
                     }
-                }
-                pend_wt = pend_tbl = has_next;
-                pend_gu = pend_dn = true;
-                // missed experts: zero-copy reads of the registered host weights
-                if (s_any_miss) {
-                    host_miss_copies(ld.hgate, ld.hup, ld.hdown, ld.ns, p.gate_bytes, p.down_bytes,
-                                     p.dn_stride, p.err, s_ids, s_slot, K, nch, ch_k, ch_i0, ch_n, ch_off, gate_sm,
-                                     up_sm, dn, gurow, drow, h0, h1);
-                    __syncthreads();
-                }
-            }
-            PROF(7)
-
-            // ---- 4. gate/up GEMV + SiLU*mul on warps 1..15, two rows per iteration -
-            if (warp > 0) {
-                const int units = (H / MOE_QK) * 4;
-                const int W = DEC_WARPS - 1, wi = warp - 1;
-                ActQ4 a;
-                if (lane < units) load_act_q4(a, xq, xd, xs, lane >> 2, lane & 3);
-                int waited = 0;
-                bool fail = false;
-                for (int rA = r0 + wi; rA < r1 && !fail; rA += 2 * W) {
-                    const int rB = rA + W;
-                    const bool hasB = rB < r1;
-                    const int lA = rA - r0, lB = rB - r0;
-                    int qA = 0, qB = 0;
-                    while (qA + 1 < nch && lA >= ch_off[qA + 1]) ++qA;
-                    while (hasB && qB + 1 < nch && lB >= ch_off[qB + 1]) ++qB;
-                    if (!(waited & (1 << qA))) {
-                        if (!mbar_wait(&mb[MB_GU + qA], par, p.wait_ns)) { fail = true; break; }
-                        waited |= 1 << qA;
-                    }
-                    if (hasB && !(waited & (1 << qB))) {
-                        if (!mbar_wait(&mb[MB_GU + qB], par, p.wait_ns)) { fail = true; break; }
-                        waited |= 1 << qB;
-                    }
-                    float gA = 0.0f, uA = 0.0f, gB = 0.0f, uB = 0.0f;
-                    if (lane < units) {
-                        const int so = (lane >> 2) * MOE_Q4K_BYTES, pp = lane & 3;
-                        gA = q4k_unit_dot(gate_sm + (size_t)lA * gurow + so, pp, a);
-                        uA = q4k_unit_dot(up_sm + (size_t)lA * gurow + so, pp, a);
-                        if (hasB) {
-                            gB = q4k_unit_dot(gate_sm + (size_t)lB * gurow + so, pp, a);
-                            uB = q4k_unit_dot(up_sm + (size_t)lB * gurow + so, pp, a);
+                };
+                // warps 1..15: gate/up GEMV + SiLU*mul of this CTA's pieces (barriers
+                // gmb, parity gpar), two rows per iteration; activations to L2
+                auto gate_up_rows = [&](uint64_t *gmb, uint32_t gpar) {
+                    const int units = (H / MOE_QK) * 4;
+                    const int W = DEC_WARPS - 1, wi = warp - 1;
+                    ActQ4 a;
+                    if (lane < units) load_act_q4(a, xq, xd, xs, lane >> 2, lane & 3);
+                    int waited = 0;
+                    bool fail = false;
+                    for (int rA = r0 + wi; rA < r1 && !fail; rA += 2 * W) {
+                        const int rB = rA + W;
+                        const bool hasB = rB < r1;
+                        const int lA = rA - r0, lB = rB - r0;
+                        int qA = 0, qB = 0;
+                        while (qA + 1 < nch && lA >= ch_off[qA + 1]) ++qA;
+                        while (hasB && qB + 1 < nch && lB >= ch_off[qB + 1]) ++qB;
+                        if (!(waited & (1 << qA))) {
+                            if (!mbar_wait(&gmb[qA], gpar, p.wait_ns)) { fail = true; break; }
+                            waited |= 1 << qA;
                         }
+                        if (hasB && !(waited & (1 << qB))) {
+                            if (!mbar_wait(&gmb[qB], gpar, p.wait_ns)) { fail = true; break; }
+                            waited |= 1 << qB;
+                        }
+                        float gA = 0.0f, uA = 0.0f, gB = 0.0f, uB = 0.0f;
+                        if (lane < units) {
+                            const int so = (lane >> 2) * MOE_Q4K_BYTES, pp = lane & 3;
+                            gA = q4k_unit_dot(gate_sm + (size_t)lA * gurow + so, pp, a);
+                            uA = q4k_unit_dot(up_sm + (size_t)lA * gurow + so, pp, a);
+                            if (hasB) {
+                                gB = q4k_unit_dot(gate_sm + (size_t)lB * gurow + so, pp, a);
+                                uB = q4k_unit_dot(up_sm + (size_t)lB * gurow + so, pp, a);
+                            }
+                        }
+                        // lanes 0-7: gate A, 8-15: up A, 16-23: gate B, 24-31: up B
+                        const float sum = warp_sum4_t(gA, uA, gB, uB, lane);
+                        const float up = __shfl_down_sync(MOE_FULL, sum, 8);
+                        if (lane == 0)
+                            __stcg(p.act + (size_t)ch_k[qA] * I + ch_i0[qA] + (lA - ch_off[qA]), silu_mul(sum, up));
+                        if (lane == 16 && hasB)
+                            __stcg(p.act + (size_t)ch_k[qB] * I + ch_i0[qB] + (lB - ch_off[qB]), silu_mul(sum, up));
                     }
-                    // lanes 0-7: gate A, 8-15: up A, 16-23: gate B, 24-31: up B
-                    const float sum = warp_sum4_t(gA, uA, gB, uB, lane);
-                    const float up = __shfl_down_sync(MOE_FULL, sum, 8);
-                    if (lane == 0)
-                        __stcg(p.act + (size_t)ch_k[qA] * I + ch_i0[qA] + (lA - ch_off[qA]), silu_mul(sum, up));
-                    if (lane == 16 && hasB)
-                        __stcg(p.act + (size_t)ch_k[qB] * I + ch_i0[qB] + (lB - ch_off[qB]), silu_mul(sum, up));
+                    if (fail && lane == 0) { atomicOr(p.err, MOE_DEV_ERR_TIMEOUT); atomicExch(p.abort_flag, 1); }
+                };
+
+                // ---- 2. prediction (cache prior off): warp 0 takes the top-k of the
+                //      logits and requests those experts' gate/up pieces; warps 1..15
+                //      quantise x = r * inv to Q8_1 meanwhile ----------------------------
+                int sp_id = -1;   // warp 0: the predicted id of rank `lane`
+                bool sp_on = false, go = false;
+                fixed = false;
+                if (spec) {
+                    if (warp == 0) {
+                        const bool ok = __all_sync(MOE_FULL, tbl_ok);
+                        bool resident = false;
+                        if (ok) {
+                            sp_id = spec_topk_warp<E / 32>(tot, inv, K, lane);
+                            // tests of the re-issue path: a wrong rank-0 prediction in
+                            // every other (token, layer)
+                            if (p.spec == 2 && (use & 1) && lane == 0) sp_id = (sp_id + 1) % E;
+                            int sp_slot = lane < K ? tbl[sp_id] : ld.ns;
+                            if ((unsigned)sp_slot > (unsigned)ld.ns) sp_slot = ld.ns;
+                            const int rk = lane < nch ? ch_k[lane] : 0;
+                            const int sl = __shfl_sync(MOE_FULL, sp_slot, rk);
+                            if (lane < nch)
+                                issue_gu_piece(ld, rk < K ? sl : -1, lane, ch_i0, ch_n, ch_off, gurow,
+                                               p.gate_bytes, gate_sm, up_sm, &mb[MB_GU + lane]);
+                            resident = __ballot_sync(MOE_FULL, lane < K && sp_slot == ld.ns) == 0u;
+                        }
+                        if (lane == 0) { s_sp = ok ? 1 : 0; s_go = resident ? 1 : 0; }
+                    } else {
+                        q8_scale_quantize_cta(xf, inv, H / 32, xq, xd, xs, tid - 32, DEC_THREADS - 32);
+                    }
+                    __syncthreads();
+                    sp_on = s_sp != 0;
+                    go = sp_on && s_go != 0;
+                    pend_gu = sp_on;
                 }
-                if (fail && lane == 0) { atomicOr(p.err, MOE_DEV_ERR_TIMEOUT); atomicExch(p.abort_flag, 1); }
+
+                if (go) {
+                    // ---- 3a. run ahead: warps 1..15 compute the predicted pieces while
+                    //      warp 0 makes the exact selection and requests the down rows.
+                    //      A wrong prediction is found before any activation is signalled:
+                    //      the right pieces are then requested and computed again. --------
+                    if (warp == 0) {
+                        const bool wrong = select_exact(sp_id, true);
+                        PROF(6)
+                        if (c == 0) observe_ids();
+                        const bool bad = s_bad != 0;
+                        if (!bad) issue_rest(&mb[MB_GU], par);
+                        if (lane == 0) { s_fix = wrong ? 1 : 0; s_rest = bad ? 0 : 1; }
+                        PROF(7)
+                    } else {
+                        gate_up_rows(&mb[MB_GU], par);
+                    }
+                    __syncthreads();
+                    pend_dn = s_rest != 0;
+                    pend_wt = pend_tbl = pend_dn && has_next;
+                    if (s_bad) {
+                        if (tid == 0) atomicExch(p.abort_flag, 1);
+                        goto abort;
+                    }
+                    if (s_fix) {
+                        // the compute warps are done with the predicted pieces: the right
+                        // ones go into the same buffers (missed experts from the host)
+                        fixed = true;
+                        if (warp == 0 && lane < nch)
+                            issue_gu_piece(ld, s_slot[ch_k[lane]], lane, ch_i0, ch_n, ch_off, gurow, p.gate_bytes,
+                                           gate_sm, up_sm, &mb[MB_FX + lane]);
+                        if (s_any_miss)
+                            host_miss_copies(ld.hgate, ld.hup, ld.hdown, ld.ns, p.gate_bytes, p.down_bytes,
+                                             p.dn_stride, p.err, s_ids, s_slot, K, nch, ch_k, ch_i0, ch_n, ch_off,
+                                             gate_sm, up_sm, dn, gurow, drow, h0, h1);
+                        __syncthreads();
+                    }
+                    if (p.dbg_x && c == 0)
+                        for (int i = tid; i < H; i += DEC_THREADS)
+                            p.dbg_x[((size_t)t * NL + L) * H + i] = xf[i];
+                } else {
+                    // ---- 3b. the exact selection first (warp 0; warps 1..15 quantise x
+                    //      unless the prediction did it), then the copies ---------------
+                    if (warp == 0) {
+                        const bool wrong = select_exact(sp_id, sp_on);
+                        int fx = 0;
+                        if (wrong) {
+                            // wrong prediction, nothing computed yet: the predicted copies
+                            // land first (the buffers are theirs until then), then the
+                            // right ones go out
+                            bool ok = lane < nch ? mbar_wait(&mb[MB_GU + lane], par, p.wait_ns) : true;
+                            ok = __all_sync(MOE_FULL, ok);
+                            if (!ok) {
+                                if (lane == 0) { atomicOr(p.err, MOE_DEV_ERR_TIMEOUT); s_bad = 1; }
+                            } else if (lane < nch) {
+                                issue_gu_piece(ld, s_slot[ch_k[lane]], lane, ch_i0, ch_n, ch_off, gurow,
+                                               p.gate_bytes, gate_sm, up_sm, &mb[MB_FX + lane]);
+                            }
+                            fx = ok ? 1 : 0;
+                        }
+                        if (lane == 0) s_fix = fx;
+                    } else if (!spec) {
+                        q8_scale_quantize_cta(xf, inv, H / 32, xq, xd, xs, tid - 32, DEC_THREADS - 32);
+                    }
+                    __syncthreads();
+                    PROF(6)
+                    fixed = s_fix != 0;
+                    if (s_bad) {
+                        if (tid == 0) atomicExch(p.abort_flag, 1);
+                        goto abort;
+                    }
+                    if (p.dbg_x && c == 0)
+                        for (int i = tid; i < H; i += DEC_THREADS)
+                            p.dbg_x[((size_t)t * NL + L) * H + i] = xf[i];
+                    if (c == 0 && warp == 1) observe_ids();
+                    // warp 0 issues this layer's copies (+ next router rows / table); the
+                    // issue blocks at roughly the data rate, so the other warps compute
+                    // the gate/up rows meanwhile
+                    if (warp == 0) {
+                        if (!sp_on && lane < nch)
+                            issue_gu_piece(ld, s_slot[ch_k[lane]], lane, ch_i0, ch_n, ch_off, gurow, p.gate_bytes,
+                                           gate_sm, up_sm, &mb[MB_GU + lane]);
+                        issue_rest(&mb[fixed ? MB_FX : MB_GU], fixed ? fx_par : par);
+                    }
+                    pend_wt = pend_tbl = has_next;
+                    pend_gu = pend_dn = true;
+                    // missed experts: zero-copy reads of the registered host weights
+                    if (s_any_miss) {
+                        host_miss_copies(ld.hgate, ld.hup, ld.hdown, ld.ns, p.gate_bytes, p.down_bytes,
+                                         p.dn_stride, p.err, s_ids, s_slot, K, nch, ch_k, ch_i0, ch_n, ch_off,
+                                         gate_sm, up_sm, dn, gurow, drow, h0, h1);
+                        __syncthreads();
+                    }
+                    PROF(7)
+                }
+                // the pieces of the exact selection (after a run ahead: only when the
+                // prediction was wrong)
+                if (warp > 0 && (!go || fixed)) gate_up_rows(&mb[fixed ? MB_FX : MB_GU], fixed ? fx_par : par);
             }
             PROF(8)
 
@@ -550,6 +687,7 @@ __global__ void __launch_bounds__(DEC_THREADS, 1) k_decode(DecodeParams p) {
                 for (int q = 0; q < nch; ++q) red_release_add(p.ready + ch_k[q] * READY_STRIDE, 1u);
             PROF(9)
             pend_gu = false;
+            if (fixed) fx_par ^= 1;
             // warp 15 puts the gate/up matrices of the previous token's experts
             // of the next step's layer into L2
             if (warp == DEC_WARPS - 1 && (L + 1 < NL || t + 1 < p.n_tok)) {
@@ -691,8 +829,11 @@ abort:
         if (tid == 0) {
             if (pend_wt) mbar_wait(&mb[MB_WT], wt_par, p.wait_ns);
             if (pend_tbl) mbar_wait(&mb[MB_TBL], tbl_par, p.wait_ns);
-            if (pend_gu)
+            if (pend_gu) {
                 for (int q = 0; q < nch; ++q) mbar_wait(&mb[MB_GU + q], par, p.wait_ns);
+                if (fixed)
+                    for (int q = 0; q < nch; ++q) mbar_wait(&mb[MB_FX + q], fx_par, p.wait_ns);
+            }
             if (pend_dn)
                 for (int kk = 0; kk < KX; ++kk) mbar_wait(&mb[MB_DN + kk], par, p.wait_ns);
             if (c == 0) p.st.g[G_CLOCK] = s_clock;

@@ -369,6 +369,137 @@ __device__ __forceinline__ void select_warp(const float *tot, float inv, const i
     __syncwarp();
 }
 
+// The ids that select_warp is expected to return when the cache prior is off,
+// without the softmax: top-k of the logits tot[e] * inv in the order (logit
+// descending, id ascending).  exp and the division by the common sum keep
+// that order except where they round two logits to one probability, so the
+// result is a prediction that the caller checks against select_warp's ids.
+// Returns the id of rank `lane` for lane < k, else -1.
+template <int M>
+__device__ __forceinline__ int spec_topk_warp(const float *tot, float inv, int k, int lane) {
+    uint32_t kh[M], kl[M];
+    float pd[M];
+#pragma unroll
+    for (int i = 0; i < M; ++i) {
+        const uint32_t u = __float_as_uint(__fmul_rn(tot[lane + 32 * i], inv));
+        kh[i] = (u & 0x80000000u) ? ~u : (u | 0x80000000u);   // orders like the floats
+        kl[i] = ~(uint32_t)(lane + 32 * i);
+        pd[i] = 0.0f;
+    }
+    if (M == 2) {
+        sel_cx(kh[0], kl[0], pd[0], kh[1], kl[1], pd[1]);
+    } else if (M == 4) {
+        sel_cx(kh[0], kl[0], pd[0], kh[1], kl[1], pd[1]);
+        sel_cx(kh[2], kl[2], pd[2], kh[3], kl[3], pd[3]);
+        sel_cx(kh[0], kl[0], pd[0], kh[2], kl[2], pd[2]);
+        sel_cx(kh[1], kl[1], pd[1], kh[3], kl[3], pd[3]);
+        sel_cx(kh[1], kl[1], pd[1], kh[2], kl[2], pd[2]);
+    } else if (M == 8) {
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) sel_cx(kh[i], kl[i], pd[i], kh[i + 1], kl[i + 1], pd[i + 1]);
+#pragma unroll
+        for (int i = 0; i < 8; i += 4) {
+            sel_cx(kh[i], kl[i], pd[i], kh[i + 2], kl[i + 2], pd[i + 2]);
+            sel_cx(kh[i + 1], kl[i + 1], pd[i + 1], kh[i + 3], kl[i + 3], pd[i + 3]);
+            sel_cx(kh[i + 1], kl[i + 1], pd[i + 1], kh[i + 2], kl[i + 2], pd[i + 2]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sel_cx(kh[i], kl[i], pd[i], kh[i + 4], kl[i + 4], pd[i + 4]);
+        sel_cx(kh[2], kl[2], pd[2], kh[4], kl[4], pd[4]);
+        sel_cx(kh[3], kl[3], pd[3], kh[5], kl[5], pd[5]);
+        sel_cx(kh[1], kl[1], pd[1], kh[2], kl[2], pd[2]);
+        sel_cx(kh[3], kl[3], pd[3], kh[4], kl[4], pd[4]);
+        sel_cx(kh[5], kl[5], pd[5], kh[6], kl[6], pd[6]);
+    }
+    int out = -1;
+    for (int r = 0; r < k; ++r) {
+        const uint32_t mh = __reduce_max_sync(MOE_FULL, kh[0]);
+        const uint32_t ml = __reduce_max_sync(MOE_FULL, kh[0] == mh ? kl[0] : 0u);
+        if (lane == r) out = (int)(~ml);
+        if (kh[0] == mh && kl[0] == ml) {
+#pragma unroll
+            for (int i = 0; i + 1 < M; ++i) {
+                kh[i] = kh[i + 1];
+                kl[i] = kl[i + 1];
+            }
+            kh[M - 1] = 0u;
+            kl[M - 1] = 0u;
+        }
+    }
+    return out;
+}
+
+// select_warp for the cache prior off, given a prediction of its ids (sp_id of
+// rank `lane` for lane < k, distinct, in [0, 32 M)): the same logits, softmax
+// and probabilities, bit for bit, but instead of the sort and the k rounds of
+// arg-max, a check that the predicted order is the selection order.  It is
+// when the predicted probabilities are strictly decreasing by rank and the
+// last is strictly above every other expert's: then the k largest in the
+// order (probability descending, id ascending) are the predicted ids, in the
+// predicted order, whatever the ties elsewhere.  On success the outputs are
+// select_warp's (s_id / s_p, id_r / w_r with the same rank-order sum) and
+// true is returned; otherwise false and nothing is written, and the caller
+// runs select_warp.
+template <int M>
+__device__ __forceinline__ bool select_warp_check(const float *tot, float inv, int k, int lane, int sp_id,
+                                                  int &id_r, float &w_r, int32_t *s_id, float *s_p) {
+    float lg[M], ex[M], pr[M];
+#pragma unroll
+    for (int i = 0; i < M; ++i) lg[i] = __fmul_rn(tot[lane + 32 * i], inv);
+    float mx = lg[0];
+#pragma unroll
+    for (int i = 1; i < M; ++i) mx = fmaxf(mx, lg[i]);
+    int oi = __float_as_int(mx);
+    oi = oi >= 0 ? oi : oi ^ 0x7FFFFFFF;
+    oi = __reduce_max_sync(MOE_FULL, oi);
+    mx = __int_as_float(oi >= 0 ? oi : oi ^ 0x7FFFFFFF);
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < M; ++i) {
+        ex[i] = expf_exact(__fsub_rn(lg[i], mx));
+        s = i == 0 ? ex[0] : __fadd_rn(s, ex[i]);
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) s = __fadd_rn(s, __shfl_xor_sync(MOE_FULL, s, off));
+#pragma unroll
+    for (int i = 0; i < M; ++i) pr[i] = __fdiv_rn(ex[i], s);
+    // the predicted experts among this lane's (id lane + 32 i), and the
+    // probability of predicted rank `lane`
+    const int src = sp_id & 31, idx = sp_id >> 5;
+    bool mine[M];
+    float p_r = 0.0f;
+#pragma unroll
+    for (int i = 0; i < M; ++i) {
+        mine[i] = false;
+        const float v = __shfl_sync(MOE_FULL, pr[i], src);
+        if (idx == i) p_r = v;
+    }
+    for (int r = 0; r < k; ++r) {
+        const int id = __shfl_sync(MOE_FULL, sp_id, r);
+#pragma unroll
+        for (int i = 0; i < M; ++i) mine[i] |= id == lane + 32 * i;
+    }
+    // probabilities are >= 0: their bits order like unsigned integers
+    uint32_t rest = 0u;
+#pragma unroll
+    for (int i = 0; i < M; ++i) rest = mine[i] ? rest : max(rest, __float_as_uint(pr[i]));
+    rest = __reduce_max_sync(MOE_FULL, rest);
+    const float p_next = __shfl_down_sync(MOE_FULL, p_r, 1);
+    const bool ok = lane >= k || (lane + 1 < k ? p_r > p_next : __float_as_uint(p_r) > rest);
+    if (!__all_sync(MOE_FULL, ok)) return false;
+    if (lane < k) {
+        s_id[lane] = sp_id;
+        s_p[lane] = p_r;
+    }
+    __syncwarp();
+    float ws = s_p[0];
+    for (int r = 1; r < k; ++r) ws = __fadd_rn(ws, s_p[r]);
+    id_r = lane < k ? sp_id : -1;
+    w_r = lane < k ? __fdiv_rn(p_r, ws) : 0.0f;
+    __syncwarp();
+    return true;
+}
+
 // Top-k by rank, all threads of the CTA: rank(e) = #experts before e in the
 // order (selection value descending, id ascending); the k experts with rank < k
 // land at position rank.  The same total order as k rounds of arg-max with

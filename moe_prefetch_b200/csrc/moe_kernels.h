@@ -206,6 +206,9 @@ struct DecodeParams {
     uint64_t *prof;                        // [n_tok][L][DEC_PHASES][grid] or null
     uint64_t wait_ns;                      // limit of every device wait (grid, rank, copies)
     int starve;                            // test hook: r + 1 starves rank r's first wait; 0 off
+    int spec;                              // gate/up copies issued from the logits' top-k before the
+                                           // exact selection (prior off): 1 on, 0 off, 2 on with a
+                                           // wrong prediction every other (token, layer) (tests)
     // shared-memory layout (bytes from the start of dynamic smem)
     int off_xf, off_xq, off_xd, off_xs, off_aq, off_ad, off_as, off_ac, off_rt, off_tbl, off_rown,
         off_gu, off_dn, off_ys, off_prev, smem_bytes;

@@ -311,12 +311,15 @@ class MoeStack:
                  "moe_layer_forward_noalloc")
         return y
 
-    def decode(self, h, out=None, debug=False, stream=None, profile=False, starve=0):
+    def decode(self, h, out=None, debug=False, stream=None, profile=False, starve=0, spec=0):
         """Batch-1 decode of h [n_tok, n_embd] (device) through every layer,
         one token after another; returns out (and the per-layer dumps when
         debug; with profile, dumps["prof"] holds the per-CTA phase timestamps
         [n_tok, n_layers, 12, grid] in ns).  starve = r + 1 is for tests of
-        the watchdog: rank r's first activation wait can then only run out."""
+        the watchdog: rank r's first activation wait can then only run out.
+        spec: the early gate/up copies, 0 on (default), 1 off, 2 on with a
+        wrong prediction in every other (token, layer) (tests of the
+        re-issue); the results are the same bits in every mode."""
         self.start()
         h = h.contiguous()
         n_tok = h.shape[0]
@@ -341,9 +344,9 @@ class MoeStack:
                 dumps["prof"] = torch.zeros(n_tok, L, 12, grid, dtype=torch.int64, device=h.device)
                 prof_ptr = dumps["prof"].data_ptr()
             dbg = MoeDecodeDbg(dumps["x"].data_ptr(), dumps["ids"].data_ptr(),
-                               dumps["w"].data_ptr(), dumps["y"].data_ptr(), prof_ptr, starve)
-        elif starve:
-            dbg = MoeDecodeDbg(None, None, None, None, None, starve)
+                               dumps["w"].data_ptr(), dumps["y"].data_ptr(), prof_ptr, starve, spec)
+        elif starve or spec:
+            dbg = MoeDecodeDbg(None, None, None, None, None, starve, spec)
         self._ck(self.lib.moe_decode(self.ctx, _ptr(h), _ptr(out), n_tok,
                                      C.byref(dbg) if dbg is not None else None, _stream(stream)),
                  "moe_decode")

@@ -271,6 +271,35 @@ def test_decode_prefetch_invariant(stack4):
     st.sync()
 
 
+def test_decode_early_copies_invariant(stack4, oracle_lib):
+    """With the cache prior off, the persistent kernel requests the gate/up
+    rows of the logits' top-k before the exact selection is known, and
+    requests them again for any rank whose exact id differs.  That changes
+    when bytes move, never the result: early copies (default), no early
+    copies, and early copies with a wrong rank-0 prediction in every other
+    (token, layer), so that half of the layers take the re-issue path, give
+    the same outputs and dumps bit for bit, and match the oracle."""
+    st = stack4
+    n_tok = 5
+    h = ar1_states(n_tok, H, seed=31)
+    hd = torch.from_numpy(h).cuda()
+    runs = [st.decode(hd, debug=True, spec=m) for m in (0, 1, 2)]
+    st.sync()
+    out0, dm0 = runs[0]
+    for out, dm in runs[1:]:
+        assert torch.equal(out, out0)
+        for key in ("x", "ids", "w", "y"):
+            assert torch.equal(dm[key], dm0[key]), key
+    dumps = {k: v.cpu().numpy() for k, v in runs[2][1].items()}
+    grid = st.decode_info()["grid"]
+    for L in range(st.n_layers):
+        g, u, d = st.slot_views(L)
+        gate, up, down = (v[:E].cpu().numpy() for v in (g, u, d))
+        W = st.routers[L].cpu().numpy()
+        for t in range(n_tok):
+            check_decode_layer(oracle_lib, h[t], dumps, t, L, W, gate, up, down, grid)
+
+
 def test_decode_matches_layer_forward(stack4):
     """Same x and same routed experts -> the persistent kernel and the
     stand-alone kernels give the same output bits (same unit mapping, same
@@ -333,10 +362,13 @@ def test_layer_forward_with_misses(miss_stack, oracle_lib):
     _check_layer(y.cpu().numpy(), ids.cpu().numpy(), w.cpu().numpy(), ry, rids, rw)
 
 
-def test_decode_with_misses(miss_stack, oracle_lib):
+@pytest.mark.parametrize("spec", [0, 2])
+def test_decode_with_misses(miss_stack, oracle_lib, spec):
+    """spec 2: every other (token, layer) re-issues its gate/up copies after
+    a wrong prediction, with missed experts among the ranks."""
     st, W, gate, up, down = miss_stack
     h = ar1_states(4, H, seed=10)
-    out, dm = st.decode(torch.from_numpy(h).cuda(), debug=True)
+    out, dm = st.decode(torch.from_numpy(h).cuda(), debug=True, spec=spec)
     st.sync()
     dumps = {k: v.cpu().numpy() for k, v in dm.items()}
     ids = dumps["ids"]

@@ -67,11 +67,14 @@ def test_shared_gemm_path(oracle_lib, c4):
     _check(oracle_lib, layers[0], X, y.cpu().numpy(), ids.cpu().numpy(), w.cpu().numpy(), path="f32")
 
 
-def test_shared_decode(oracle_lib, c4):
+@pytest.mark.parametrize("spec", [0, 2])
+def test_shared_decode(oracle_lib, c4, spec):
+    """spec 2: a wrong prediction in every other (token, layer), so that the
+    shared expert's pieces are re-issued too."""
     st, layers = c4
     n_tok = 3
     h = ar1_states(n_tok, H, seed=9)
-    out, dm = st.decode(torch.from_numpy(h).cuda(), debug=True)
+    out, dm = st.decode(torch.from_numpy(h).cuda(), debug=True, spec=spec)
     st.sync()
     dumps = {k: v.cpu().numpy() for k, v in dm.items()}
     grid = st.decode_info()["grid"]
