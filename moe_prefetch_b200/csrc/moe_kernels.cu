@@ -198,9 +198,9 @@ __global__ void __launch_bounds__(512) k_router(const float *__restrict__ W,
     }
 }
 
-// Router for any number of tokens, one cluster of RB_CL CTAs per RB_TOK
-// tokens (the cache prior and the observation apply to single tokens only,
-// and the caller passes them only then).  CTA r of a cluster
+// Router for any number of tokens, one cluster of RB_CL CTAs per TOK tokens
+// (the cache prior and the observation apply to single tokens only, and the
+// caller passes them only then).  CTA r of a cluster
 // computes the logits of experts [r E / RB_CL, (r + 1) E / RB_CL) for the
 // cluster's tokens: warp w takes two of them at a time, holds its lanes'
 // slice of both router rows in registers (n_embd == 2048: 16 float4 per lane
@@ -209,7 +209,13 @@ __global__ void __launch_bounds__(512) k_router(const float *__restrict__ W,
 // k_router.  After a cluster barrier, CTA r gathers token r's E logits from
 // the cluster's shared memory and selects for it (router_select_warp).  Each
 // CTA reads only its 1/RB_CL of the router, instead of all of it.
+// Two shapes: TOK = 8 tokens per cluster with 8 warps per CTA for large
+// batches (the router rows are reused over more tokens), and TOK = 4 with
+// 16 warps, one router row each, for small ones (twice the clusters, and a
+// warp's serial chain of row load and dots is a quarter as long).
 #define RB_TOK 8
+#define RB_TOK_SMALL 4
+#define RB_SMALL_MAX 64   // batches up to this many tokens take TOK = 4
 #define RB_CL 8
 
 __device__ __forceinline__ float router_chain_dot(const float4 (&wv)[16], const float *xt, int lane) {
@@ -228,36 +234,38 @@ __device__ __forceinline__ float router_chain_dot(const float4 (&wv)[16], const 
     return v;
 }
 
-// grid RB_CL x ceil(n_tok / RB_TOK) (cluster dims RB_CL); block 256;
-// dynamic shared memory: the cluster's token rows [RB_TOK][2048].
-__global__ void __cluster_dims__(RB_CL, 1, 1) __launch_bounds__(256)
+// grid RB_CL x ceil(n_tok / TOK) (cluster dims RB_CL); block NT;
+// dynamic shared memory: the cluster's token rows [TOK][2048].
+template <int TOK, int NT>
+__global__ void __cluster_dims__(RB_CL, 1, 1) __launch_bounds__(NT)
     k_router_batch(const float *__restrict__ W, const float *__restrict__ x, int n_tok,
                    int n_expert, int k, int32_t *__restrict__ ids, float *__restrict__ w,
                    const int32_t *__restrict__ table, int ns, float delta, int use_prior,
                    SlotState st, int observe_layer_idx, const int32_t *__restrict__ pub) {
     namespace cg = cooperative_groups;
-    extern __shared__ __align__(16) float xs[];          // [RB_TOK][2048]
-    __shared__ float lg[RB_TOK][256 / RB_CL];            // this CTA's experts' logits
+    static_assert(TOK % 2 == 0 && (TOK * 512) % NT == 0, "k_router_batch shape");
+    extern __shared__ __align__(16) float xs[];          // [TOK][2048]
+    __shared__ float lg[TOK][256 / RB_CL];               // this CTA's experts' logits
     __shared__ float lgf[256];                           // one token's logits, all experts
     __shared__ int32_t sids[MOE_KMAX];
     __shared__ float sw[MOE_KMAX];
     cg::cluster_group cl = cg::this_cluster();
     const int r = (int)cl.block_rank();
-    const int t0 = (blockIdx.x / RB_CL) * RB_TOK;
-    const int nt = min(RB_TOK, n_tok - t0);
+    const int t0 = (blockIdx.x / RB_CL) * TOK;
+    const int nt = min(TOK, n_tok - t0);
     const int epc = n_expert / RB_CL, e0 = r * epc;     // this CTA's experts
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     {   // the token rows: every load issued before the first store
-        constexpr int PER = RB_TOK * 512 / 256;
+        constexpr int PER = TOK * 512 / NT;
         const float4 *xg = reinterpret_cast<const float4 *>(x + (size_t)t0 * 2048);
         float4 v[PER];
 #pragma unroll
         for (int j = 0; j < PER; ++j) {
-            const int i = threadIdx.x + 256 * j;
+            const int i = threadIdx.x + NT * j;
             v[j] = i < nt * 512 ? __ldg(xg + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         }
 #pragma unroll
-        for (int j = 0; j < PER; ++j) reinterpret_cast<float4 *>(xs)[threadIdx.x + 256 * j] = v[j];
+        for (int j = 0; j < PER; ++j) reinterpret_cast<float4 *>(xs)[threadIdx.x + NT * j] = v[j];
     }
     __syncthreads();
     for (int j = warp; j < epc; j += nw) {
@@ -763,16 +771,24 @@ cudaError_t launch_router(const float *W, const float *x, int n_tok, int n_exper
                           int32_t *ids, float *w, float *logits, const SlotState *st,
                           int observe_layer_idx, const int32_t *pub, cudaStream_t s) {
     if (n_embd == 2048 && !logits && (n_tok == 1 || (!use_prior && observe_layer_idx < 0))) {
-        // one cluster of RB_CL CTAs per RB_TOK tokens
-        const size_t sm = sizeof(float) * (size_t)RB_TOK * 2048;
-        cudaError_t e = cudaFuncSetAttribute(k_router_batch, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)sm);
+        // one cluster of RB_CL CTAs per TOK tokens
+        const bool small = n_tok <= RB_SMALL_MAX;
+        const int tok = small ? RB_TOK_SMALL : RB_TOK;
+        const size_t sm = sizeof(float) * (size_t)tok * 2048;
+        const void *fn = small ? (const void *)k_router_batch<RB_TOK_SMALL, 512>
+                               : (const void *)k_router_batch<RB_TOK, 256>;
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
         if (e != cudaSuccess) return e;
-        const int groups = (n_tok + RB_TOK - 1) / RB_TOK;
+        const int groups = (n_tok + tok - 1) / tok;
         SlotState dummy_st{};
-        k_router_batch<<<groups * RB_CL, 256, sm, s>>>(W, x, n_tok, n_expert, k, ids, w, table, ns, delta,
-                                                        use_prior, st ? *st : dummy_st,
-                                                        st ? observe_layer_idx : -1, pub);
+        const SlotState sst = st ? *st : dummy_st;
+        const int obs = st ? observe_layer_idx : -1;
+        if (small)
+            k_router_batch<RB_TOK_SMALL, 512><<<groups * RB_CL, 512, sm, s>>>(
+                W, x, n_tok, n_expert, k, ids, w, table, ns, delta, use_prior, sst, obs, pub);
+        else
+            k_router_batch<RB_TOK, 256><<<groups * RB_CL, 256, sm, s>>>(
+                W, x, n_tok, n_expert, k, ids, w, table, ns, delta, use_prior, sst, obs, pub);
         return cudaGetLastError();
     }
     const size_t smem = sizeof(float) * ((size_t)n_embd + n_expert);

@@ -97,6 +97,29 @@ def test_router_bit_exact(lib, oracle_lib, n_exp):
     _router_case(lib, oracle_lib, W, X, K)
 
 
+@pytest.mark.parametrize("n_exp", [128, 256])
+@pytest.mark.parametrize("n_tok", [1, 3, 4, 5, 32, 63, 64, 65, 200])
+def test_batch_router_bit_exact(lib, oracle_lib, n_exp, n_tok):
+    """Without a logits output the router runs as clusters of 8 CTAs: 4
+    tokens per cluster up to 64 tokens, 8 above.  Ids and weights must equal
+    the oracle's bit for bit for every shape, ragged last clusters included."""
+    rng = np.random.default_rng(100 + n_tok)
+    W = (rng.standard_normal((n_exp, H)) * 0.02).astype(np.float32)
+    X = rms_norm(rng.standard_normal((n_tok, H)))
+    Wd = torch.from_numpy(W).cuda()
+    Xd = torch.from_numpy(X).cuda()
+    ids = torch.empty(n_tok, K, dtype=torch.int32, device="cuda")
+    w = torch.empty(n_tok, K, device="cuda")
+    rc = lib.moe_router_run(_p(Wd), _p(Xd), n_tok, n_exp, H, None, 0, 0.0, K, _p(ids), _p(w), None, _s())
+    assert rc == 0
+    torch.cuda.synchronize()
+    ids, w = ids.cpu().numpy(), w.cpu().numpy()
+    for t in range(n_tok):
+        rid, rw, _, _ = oracle_lib.router(W, X[t], K, None)
+        assert np.array_equal(ids[t], rid), f"ids token {t}: {ids[t]} vs {rid}"
+        assert np.array_equal(w[t].view(np.uint32), rw.view(np.uint32)), f"weights token {t}"
+
+
 def test_router_ties_go_to_lower_id(lib, oracle_lib):
     rng = np.random.default_rng(5)
     W = (rng.standard_normal((E, H)) * 0.02).astype(np.float32)
