@@ -361,7 +361,7 @@ __global__ void __launch_bounds__(256, 2) k_gate_up_grouped(
 // Each lane decodes its half block (Q6_K; 8-lane row groups) or unit (Q4_K)
 // once per row and dots it with every pair's activations: the per-pair
 // kernel's arithmetic and reduction, bit for bit.
-__global__ void __launch_bounds__(256, 2) k_down_grouped(
+__global__ void __launch_bounds__(256, 3) k_down_grouped(
     ExpertSrc src, const int8_t *__restrict__ aq, const float *__restrict__ ad,
     const float *__restrict__ as, const int32_t *__restrict__ off, const int32_t *__restrict__ cnt,
     const int32_t *__restrict__ tiles, const int32_t *__restrict__ n_tiles, int n_embd, int n_ff,
